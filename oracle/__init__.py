@@ -1,0 +1,288 @@
+"""CPU oracle for Pion's FT.SEARCH KNN hot path — TEST INFRASTRUCTURE ONLY.
+
+numpy-facing ctypes bindings over ``oracle/liboracle.so`` (built from
+``oracle/pion_oracle.c`` by ``oracle/Makefile``).  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import this
+package, and only as the checker; the product library ``pion_b200`` never
+imports it and has no CPU fallback.
+
+Parity status: UNPINNED — the reference path is Mojo (no toolchain here) and the
+reference stores no golden vectors.  Each wrapped function names the reference
+``file:line`` it restates (paths inside the pavelhorak/pion repository).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lock = threading.Lock()
+_lib = None
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_p = ctypes.c_void_p
+_f32 = ctypes.c_float
+
+
+def build(force: bool = False) -> str:
+    """Compile the C restatement with its Makefile (gcc, no GPU needed)."""
+    if force or not os.path.exists(_LIB_PATH) or _stale():
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def _stale() -> bool:
+    lib_t = os.path.getmtime(_LIB_PATH)
+    for f in os.listdir(_HERE):
+        if f.endswith((".c", ".h")) and os.path.getmtime(os.path.join(_HERE, f)) > lib_t:
+            return True
+    return False
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                build()
+            L = ctypes.CDLL(_LIB_PATH)
+            L.orc_pkm_quantize_rows_i8.argtypes = [_p, _i64, _i64, _i64, _p, _p]
+            L.orc_pkm_scores_i8.argtypes = [_p, _i64, _i64, _p, _p, _p, _i64, _p]
+            L.orc_pkm_scores_f32.argtypes = [_p, _i64, _i64, _p, _i64, _p]
+            L.orc_pkm_rescore_f32.argtypes = [_p, _i64, _p, _p, _i64, _p]
+            L.orc_pkm_sort_desc.argtypes = [_p, _p, _i64]
+            L.orc_pkm_topk_max.argtypes = [_p, _i64, _i64, _p, _p]
+            L.orc_pkm_topk_max.restype = _i64
+            L.orc_pkm_combine_topk.argtypes = [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p]
+            L.orc_pkm_combine_topk.restype = _i64
+            L.orc_flat_i8_knn.argtypes = [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i32]
+            L.orc_dot_f32_4chain.argtypes = [_p, _p, _i64]
+            L.orc_dot_f32_4chain.restype = _f32
+            L.orc_l2sq_f32_4chain.argtypes = [_p, _p, _i64]
+            L.orc_l2sq_f32_4chain.restype = _f32
+            L.orc_l2_normalize_fp32.argtypes = [_p, _p, _i64]
+            L.orc_exact_query_normalize.argtypes = [_p, _p, _i64, _i32]
+            L.orc_exact_knn.argtypes = [_p, _i64, _i64, _p, _i64, _i32, _p, _p]
+            L.orc_exact_knn.restype = _i64
+            L.orc_exact_knn_batch.argtypes = [_p, _i64, _i64, _p, _i64, _i64, _i32, _p, _p, _i32]
+            L.orc_bq_pack_signs.argtypes = [_p, _i64, _i64, _p]
+            L.orc_hamming.argtypes = [_p, _p, _i64]
+            L.orc_hamming.restype = _i64
+            L.orc_bq_knn_batch.argtypes = [_p, _p, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p,
+                                           _p, _i32]
+            L.orc_shard_merge_asc.argtypes = [_p, _p, _i64, _i64, _p, _p]
+            L.orc_shard_merge_asc.restype = _i64
+            _bind_hnsw(L)
+            _lib = L
+    return _lib
+
+
+def _bind_hnsw(L):
+    if not hasattr(L, "orc_hnsw_build"):
+        return
+    from . import hnsw as _h  # noqa: F401  (binds its own symbols lazily)
+
+
+def _c(a, dtype):
+    a = np.ascontiguousarray(a, dtype=dtype)
+    return a, a.ctypes.data_as(_p)
+
+
+def default_threads() -> int:
+    return max(1, os.cpu_count() or 1)
+
+
+# --------------------------------------------------------------------------
+# PKM routines (src/vector/pkm_kernels.mojo, src/vector/reference/pkm_ref.mojo)
+# --------------------------------------------------------------------------
+
+def pkm_quantize_rows_i8(src: np.ndarray, d: int | None = None):
+    """src/vector/pkm_kernels.mojo:152-191.  src: [n, d_pad] float32 -> (int8, scale)."""
+    src, ps = _c(src, np.float32)
+    n, d_pad = src.shape
+    d = d_pad if d is None else d
+    out = np.empty((n, d_pad), np.int8)
+    sc = np.empty(n, np.float32)
+    lib().orc_pkm_quantize_rows_i8(ps, n, d, d_pad, out.ctypes.data_as(_p), sc.ctypes.data_as(_p))
+    return out, sc
+
+
+def pkm_scores_i8(keys, row_scale, q, q_scale) -> np.ndarray:
+    """src/vector/reference/pkm_ref.mojo:47-61.  -> [nq, S] float32."""
+    keys, pk = _c(keys, np.int8)
+    row_scale, pr = _c(row_scale, np.float32)
+    q, pq = _c(q, np.int8)
+    q_scale, pqs = _c(q_scale, np.float32)
+    s, d_pad = keys.shape
+    nq = q.shape[0]
+    dst = np.empty((nq, s), np.float32)
+    lib().orc_pkm_scores_i8(pk, s, d_pad, pr, pq, pqs, nq, dst.ctypes.data_as(_p))
+    return dst
+
+
+def pkm_scores_f32(keys, q) -> np.ndarray:
+    """src/vector/reference/pkm_ref.mojo:22-31."""
+    keys, pk = _c(keys, np.float32)
+    q, pq = _c(q, np.float32)
+    s, d_pad = keys.shape
+    nq = q.shape[0]
+    dst = np.empty((nq, s), np.float32)
+    lib().orc_pkm_scores_f32(pk, s, d_pad, pq, nq, dst.ctypes.data_as(_p))
+    return dst
+
+
+def pkm_rescore_f32(keys, q, idx) -> np.ndarray:
+    """src/vector/reference/pkm_ref.mojo:34-44."""
+    keys, pk = _c(keys, np.float32)
+    q, pq = _c(q, np.float32)
+    idx, pi = _c(idx, np.int32)
+    dst = np.empty(idx.shape[0], np.float32)
+    lib().orc_pkm_rescore_f32(pk, keys.shape[1], pq, pi, idx.shape[0], dst.ctypes.data_as(_p))
+    return dst
+
+
+def pkm_sort_desc(val, idx):
+    """src/vector/reference/pkm_ref.mojo:92-107 (in place on copies)."""
+    val = np.array(val, np.float32, copy=True)
+    idx = np.array(idx, np.int32, copy=True)
+    lib().orc_pkm_sort_desc(val.ctypes.data_as(_p), idx.ctypes.data_as(_p), val.shape[0])
+    return val, idx
+
+
+def pkm_topk_max(scores, k: int):
+    """src/vector/reference/pkm_ref.mojo:110-130.  -> (idx int32[kk], val float32[kk])."""
+    scores, ps = _c(scores, np.float32)
+    kk = max(0, min(k, scores.shape[0]))
+    oi = np.empty(max(kk, 1), np.int32)
+    ov = np.empty(max(kk, 1), np.float32)
+    got = lib().orc_pkm_topk_max(ps, scores.shape[0], k, oi.ctypes.data_as(_p),
+                                 ov.ctypes.data_as(_p))
+    return oi[:got], ov[:got]
+
+
+def pkm_combine_topk(s0, i0, s1, i1, s_cols: int, k: int):
+    """src/vector/reference/pkm_ref.mojo:133-160."""
+    s0, p0 = _c(s0, np.float32)
+    i0, q0 = _c(i0, np.int32)
+    s1, p1 = _c(s1, np.float32)
+    i1, q1 = _c(i1, np.int32)
+    cap = max(1, min(k, s0.shape[0] * s1.shape[0]))
+    oi = np.empty(cap, np.int32)
+    ov = np.empty(cap, np.float32)
+    got = lib().orc_pkm_combine_topk(p0, q0, s0.shape[0], p1, q1, s1.shape[0], s_cols, k,
+                                     oi.ctypes.data_as(_p), ov.ctypes.data_as(_p))
+    return oi[:got], ov[:got]
+
+
+def flat_i8_knn(keys, row_scale, q, q_scale, k: int, nthreads: int | None = None):
+    """pkm_scores_i8 + pkm_topk_max per query, streamed.  -> (idx [nq,k], val [nq,k])."""
+    keys, pk = _c(keys, np.int8)
+    row_scale, pr = _c(row_scale, np.float32)
+    q, pq = _c(q, np.int8)
+    q_scale, pqs = _c(q_scale, np.float32)
+    n, d_pad = keys.shape
+    nq = q.shape[0]
+    oi = np.empty((nq, k), np.int32)
+    ov = np.empty((nq, k), np.float32)
+    lib().orc_flat_i8_knn(pk, n, d_pad, pr, pq, pqs, nq, k, oi.ctypes.data_as(_p),
+                          ov.ctypes.data_as(_p), nthreads or default_threads())
+    return oi, ov
+
+
+# --------------------------------------------------------------------------
+# Exact FP32 rows (src/vector/fp32_scan.mojo, src/commands/vector.mojo)
+# --------------------------------------------------------------------------
+
+def dot_f32_4chain(q, v) -> float:
+    q, pq = _c(q, np.float32)
+    v, pv = _c(v, np.float32)
+    return lib().orc_dot_f32_4chain(pq, pv, q.shape[0])
+
+
+def l2sq_f32_4chain(a, b) -> float:
+    a, pa = _c(a, np.float32)
+    b, pb = _c(b, np.float32)
+    return lib().orc_l2sq_f32_4chain(pa, pb, a.shape[0])
+
+
+def l2_normalize_rows(x) -> np.ndarray:
+    """src/vector/kernels.mojo:318-357 applied to every row."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    L = lib()
+    dim = x.shape[1]
+    for r in range(x.shape[0]):
+        L.orc_l2_normalize_fp32(x[r].ctypes.data_as(_p), out[r].ctypes.data_as(_p), dim)
+    return out
+
+
+def exact_query_normalize(query, cosine: bool = True) -> np.ndarray:
+    query, pq = _c(query, np.float32)
+    out = np.empty_like(query)
+    lib().orc_exact_query_normalize(pq, out.ctypes.data_as(_p), query.shape[0], int(cosine))
+    return out
+
+
+def exact_knn(rows, queries, k: int, cosine: bool = True, nthreads: int | None = None):
+    """src/commands/vector.mojo:1228-1365 per query.  -> (ids int64 [nq,k], scores [nq,k])."""
+    rows, pr = _c(rows, np.float32)
+    queries, pq = _c(np.atleast_2d(queries), np.float32)
+    n, dim = rows.shape
+    nq = queries.shape[0]
+    ids = np.empty((nq, k), np.int64)
+    sc = np.empty((nq, k), np.float32)
+    lib().orc_exact_knn_batch(pr, n, dim, pq, nq, k, int(cosine), ids.ctypes.data_as(_p),
+                              sc.ctypes.data_as(_p), nthreads or default_threads())
+    return ids, sc
+
+
+# --------------------------------------------------------------------------
+# Binary quantisation + rerank (composed)
+# --------------------------------------------------------------------------
+
+def bq_pack_signs(rows) -> np.ndarray:
+    rows, pr = _c(np.atleast_2d(rows), np.float32)
+    n, dim = rows.shape
+    codes = np.empty((n, dim // 64), np.uint64)
+    lib().orc_bq_pack_signs(pr, n, dim, codes.ctypes.data_as(_p))
+    return codes
+
+
+def hamming(a, b) -> int:
+    a, pa = _c(a, np.uint64)
+    b, pb = _c(b, np.uint64)
+    return lib().orc_hamming(pa, pb, a.shape[0])
+
+
+def bq_knn(codes, rows, queries, shortlist: int, k: int, nthreads: int | None = None):
+    """Hamming shortlist (distance, id) then exact COSINE rerank (stable by score)."""
+    codes, pc = _c(codes, np.uint64)
+    rows, pr = _c(rows, np.float32)
+    queries, pq = _c(np.atleast_2d(queries), np.float32)
+    n, dim = rows.shape
+    nq = queries.shape[0]
+    ids = np.empty((nq, k), np.int64)
+    sc = np.empty((nq, k), np.float32)
+    sid = np.empty((nq, shortlist), np.int32)
+    sd = np.empty((nq, shortlist), np.int32)
+    lib().orc_bq_knn_batch(pc, pr, n, dim, pq, nq, shortlist, k, ids.ctypes.data_as(_p),
+                           sc.ctypes.data_as(_p), sid.ctypes.data_as(_p), sd.ctypes.data_as(_p),
+                           nthreads or default_threads())
+    return ids, sc, sid, sd
+
+
+def shard_merge_asc(ids, scores, k: int):
+    """src/commands/vector.mojo:4394-4429 (selection sort over concatenated shards)."""
+    ids, pi = _c(ids, np.int64)
+    scores, ps = _c(scores, np.float32)
+    n = ids.shape[0]
+    oi = np.empty(max(1, k), np.int64)
+    os_ = np.empty(max(1, k), np.float32)
+    got = lib().orc_shard_merge_asc(pi, ps, n, k, oi.ctypes.data_as(_p), os_.ctypes.data_as(_p))
+    return oi[:got], os_[:got]

@@ -1,0 +1,77 @@
+/*
+ * CPU oracle for the FT.SEARCH KNN hot path of Pion — TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of Pion's open vector reference (Mojo), used by tests/,
+ * __graft_entry__.smoke() and bench.py's CPU-baseline leg as the checker.  It is
+ * never linked into, loaded by, or called from the product library
+ * (pion_b200/libpion_vector_b200.so), which has no CPU fallback.
+ *
+ * Parity status: UNPINNED against the reference's own outputs.  The reference
+ * path is Mojo (the .mojo files under src/vector/reference/) and no Mojo toolchain exists here, and
+ * the reference stores no golden vectors (its differential tests generate data
+ * with Mojo's RNG).  Each function below cites the reference file:line it restates;
+ * the restatement is cross-checked against an independent numpy restatement and
+ * against the reference tests' invariants (tests/test_oracle.py).
+ *
+ * Floating-point conventions followed (x86-64-v2, the `pixi run build-open`
+ * target, pixi.toml:93): no FMA contraction (src/vector/fma_mad.mojo:21-22 lowers
+ * fma_mad to a*b+c there), SSE float width 4, SIMD reduce_add as a halving tree
+ * (lanes [0..w/2) + [w/2..w), recursively).
+ */
+#ifndef PION_ORACLE_H
+#define PION_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- product-key-memory routines used as FLAT INT8 inner product ---------- */
+void orc_pkm_quantize_rows_i8(const float *src, int64_t n_rows, int64_t d, int64_t d_pad,
+                              int8_t *dst, float *dst_scale);
+void orc_pkm_scores_i8(const int8_t *keys, int64_t s_rows, int64_t d_pad, const float *row_scale,
+                       const int8_t *q, const float *q_scale, int64_t nq, float *dst);
+void orc_pkm_scores_f32(const float *keys, int64_t s_rows, int64_t d_pad, const float *q,
+                        int64_t nq, float *dst);
+void orc_pkm_rescore_f32(const float *keys, int64_t d_pad, const float *q, const int32_t *idx,
+                         int64_t cnt, float *dst);
+void orc_pkm_sort_desc(float *val, int32_t *idx, int64_t n);
+int64_t orc_pkm_topk_max(const float *scores, int64_t n, int64_t k, int32_t *out_idx,
+                         float *out_val);
+int64_t orc_pkm_combine_topk(const float *s0, const int32_t *i0, int64_t k0, const float *s1,
+                             const int32_t *i1, int64_t k1, int64_t s_cols, int64_t k,
+                             int32_t *out_id, float *out_score);
+
+/* Batched FLAT INT8 IP KNN = pkm_scores_i8 + pkm_topk_max per query, streamed
+ * (identical results, no score matrix).  Output per query: k (idx, val), descending. */
+void orc_flat_i8_knn(const int8_t *keys, int64_t n, int64_t d_pad, const float *row_scale,
+                     const int8_t *q, const float *q_scale, int64_t nq, int64_t k,
+                     int32_t *out_idx, float *out_val, int nthreads);
+
+/* ---- exact FP32 rows (FLAT FP32 path) ------------------------------------ */
+float orc_dot_f32_4chain(const float *q, const float *v, int64_t dim);
+float orc_l2sq_f32_4chain(const float *a, const float *b, int64_t dim);
+void orc_l2_normalize_fp32(const float *src, float *dst, int64_t dim);
+void orc_exact_query_normalize(const float *query, float *q, int64_t dim, int cosine);
+int64_t orc_exact_knn(const float *rows, int64_t n, int64_t dim, const float *query, int64_t k,
+                      int cosine, int64_t *ids, float *scores);
+void orc_exact_knn_batch(const float *rows, int64_t n, int64_t dim, const float *queries,
+                         int64_t nq, int64_t k, int cosine, int64_t *ids, float *scores,
+                         int nthreads);
+
+/* ---- binary quantisation + FP32 rerank ---------------------------------- */
+void orc_bq_pack_signs(const float *rows, int64_t n, int64_t dim, uint64_t *codes);
+int64_t orc_hamming(const uint64_t *a, const uint64_t *b, int64_t words);
+void orc_bq_knn_batch(const uint64_t *codes, const float *rows, int64_t n, int64_t dim,
+                      const float *queries, int64_t nq, int64_t shortlist, int64_t k,
+                      int64_t *ids, float *scores, int32_t *short_ids, int32_t *short_dist,
+                      int nthreads);
+
+/* ---- sharded merge ------------------------------------------------------- */
+int64_t orc_shard_merge_asc(const int64_t *ids, const float *scores, int64_t n_all, int64_t k,
+                            int64_t *out_ids, float *out_scores);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,106 @@
+"""ctypes binding of libpion_vector_b200.so (the C ABI in include/pion_vector_b200.h).
+
+The library is the product: there is no Python or CPU fallback.  Loading fails
+loudly when the shared library is missing or was built without a symbol.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpion_vector_b200.so")
+
+OK = 0
+EINVAL = -1
+ENOMEM = -2
+ESHAPE = -3
+ENODEV = -4
+ECUDA = -10
+ETIMEOUT = -11
+EABI = -12
+
+MEM_HOST = 0
+MEM_DEVICE = 1
+MEM_DEVICE_BORROW = 2
+
+MERGE_DESC = 1
+MERGE_LISTS_MAJOR = 2
+
+ABI_VERSION = 1
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_PP = ctypes.POINTER(ctypes.c_void_p)
+
+# name -> (restype, argtypes); every symbol include/pion_vector_b200.h declares.
+SIGNATURES = {
+    "pion_v_abi_version": (_I64, []),
+    "pion_v_isa": (_I64, []),
+    "pion_v_pkm_scores_f32": (None, [_P, _I64, _I64, _P, _I64, _P]),
+    "pion_v_pkm_rescore_f32": (None, [_P, _I64, _P, _P, _I64, _P]),
+    "pion_v_pkm_scores_i8": (None, [_P, _I64, _I64, _P, _P, _P, _I64, _P]),
+    "pion_v_pkm_topk_max": (_I64, [_P, _I64, _I64, _P, _P]),
+    "pion_v_pkm_sort_desc": (None, [_P, _P, _I64]),
+    "pion_v_pkm_combine_topk": (_I64, [_P, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "pion_v_b200_init": (_I, [_I, _I, _PP]),
+    "pion_v_b200_shutdown": (_I, [_P]),
+    "pion_v_b200_set_stream": (_I, [_P, _P]),
+    "pion_v_b200_sync": (_I, [_P]),
+    "pion_v_b200_last_error": (ctypes.c_char_p, [_P]),
+    "pion_v_b200_reserve": (_I, [_P, _I64, _I64]),
+    "pion_v_b200_launch_count": (_I64, [_P]),
+    "pion_v_b200_timing_enable": (_I, [_P, _I]),
+    "pion_v_b200_timing_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
+                                     ctypes.POINTER(ctypes.c_int64)]),
+    "pion_v_b200_register_flat_i8": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _PP]),
+    "pion_v_b200_flat_i8_knn": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_register_flat_f32": (_I, [_P, _P, _I64, _I64, _I64, _I, _I, _PP]),
+    "pion_v_b200_flat_f32_knn": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_register_bq": (_I, [_P, _P, _I64, _I64, _I64, _I, _I, _PP]),
+    "pion_v_b200_bq_rerank_knn": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_index_free": (_I, [_P]),
+    "pion_v_b200_index_rows": (_I64, [_P]),
+    "pion_v_b200_quantize_rows_i8": (_I, [_P, _P, _I64, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_l2_normalize_rows": (_I, [_P, _P, _I64, _I64, _P, _I]),
+    "pion_v_b200_merge_topk": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _I]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class PionError(RuntimeError):
+    """A negative status from the library, with its message."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"pion_vector_b200 error {code}: {msg}")
+        self.code = code
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the shared library and bind every declared symbol (raises if absent)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise ImportError(
+                f"{path} is missing: build it with `python -m pion_b200.build` "
+                "(the CUDA library is required; there is no CPU fallback)")
+        lib = ctypes.CDLL(path)
+        missing = []
+        for name, (res, args) in SIGNATURES.items():
+            try:
+                fn = getattr(lib, name)
+            except AttributeError:
+                missing.append(name)
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        if missing:
+            raise ImportError(f"{path} lacks symbols: {', '.join(missing)}")
+        _lib = lib
+        return lib

@@ -1,0 +1,557 @@
+// C-ABI layer of libpion_vector_b200: contexts, device-resident index registration
+// and the batched query entry points declared in include/pion_vector_b200.h.
+//
+// Conventions follow the reference's CUDA shim (src/ffi/cuda_wrap.c:153-437,
+// src/ffi/cuda_kernels.cu:1330-1346): int status, 0 ok, negative error, message kept
+// per context (and printed to stderr for the pion_v_* group, which has no status).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "internal.h"
+
+namespace pion {
+
+int set_error(pion_b200_ctx* ctx, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->last_error = buf;
+    return code;
+}
+
+int ensure(DevBuf& b, size_t bytes) {
+    if (bytes <= b.bytes) return 0;
+    size_t want = bytes + bytes / 4 + 4096;
+    void* p = nullptr;
+    if (cudaMalloc(&p, want) != cudaSuccess) {
+        cudaGetLastError();
+        return PION_B200_ENOMEM;
+    }
+    if (b.ptr) cudaFree(b.ptr);
+    b.ptr = p;
+    b.bytes = want;
+    return 0;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D tensor map, row-major: `inner` elements per row (contiguous), `outer` rows.
+// Out-of-range boxes read as zero.
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+    (void)elem_bytes;
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return PION_B200_ECUDA;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_bytes & 15u) != 0)
+        return PION_B200_EINVAL;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : PION_B200_ECUDA;
+}
+
+// Queues a copy of the status word into pinned host memory.
+static int queue_status_readback(pion_b200_ctx* ctx) {
+    return cudaMemcpyAsync(ctx->h_status, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost,
+                           ctx->stream) == cudaSuccess
+               ? 0
+               : PION_B200_ECUDA;
+}
+
+// Synchronises the stream, then turns a recorded device-side status into a code.
+static int finish_sync(pion_b200_ctx* ctx) {
+    if (queue_status_readback(ctx) != 0)
+        return set_error(ctx, PION_B200_ECUDA, "status copy failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess)
+        return set_error(ctx, PION_B200_ECUDA, "stream failed: %s", cudaGetErrorString(e));
+    int st = *ctx->h_status;
+    if (st != 0) {
+        *ctx->h_status = 0;
+        cudaMemsetAsync(ctx->d_status, 0, sizeof(int), ctx->stream);
+        cudaStreamSynchronize(ctx->stream);
+        return set_error(ctx, st, "device-side wait gave up (status %d)", st);
+    }
+    return 0;
+}
+
+static bool valid_ctx(const pion_b200_ctx* ctx) { return ctx != nullptr && ctx->d_status; }
+
+static int use_device(pion_b200_ctx* ctx) {
+    if (cudaSetDevice(ctx->device) != cudaSuccess)
+        return set_error(ctx, PION_B200_ENODEV, "cudaSetDevice(%d) failed", ctx->device);
+    return 0;
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+void timing_begin(pion_b200_ctx* ctx) {
+    if (!ctx->timing) return;
+    if (ctx->ev_used == ctx->ev_start.size()) {
+        if (ctx->ev_used >= 65536) return;
+        cudaEvent_t a, b;
+        if (cudaEventCreate(&a) != cudaSuccess) return;
+        if (cudaEventCreate(&b) != cudaSuccess) {
+            cudaEventDestroy(a);
+            return;
+        }
+        ctx->ev_start.push_back(a);
+        ctx->ev_end.push_back(b);
+    }
+    cudaEventRecord(ctx->ev_start[ctx->ev_used], ctx->stream);
+}
+
+void timing_end(pion_b200_ctx* ctx) {
+    if (!ctx->timing || ctx->ev_used >= ctx->ev_start.size()) return;
+    cudaEventRecord(ctx->ev_end[ctx->ev_used], ctx->stream);
+    ctx->ev_used++;
+}
+
+}  // namespace pion
+
+using namespace pion;
+
+extern "C" {
+
+int pion_v_b200_init(int device, int worker_id, pion_b200_ctx** out_ctx) {
+    if (!out_ctx) return PION_B200_EINVAL;
+    *out_ctx = nullptr;
+    if (device < 0) {
+        const char* env = getenv("PION_B200_DEVICE");
+        device = env ? atoi(env) : 0;
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device >= n) {
+        cudaGetLastError();
+        fprintf(stderr, "pion_vector_b200: no CUDA device %d\n", device);
+        return PION_B200_ENODEV;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PION_B200_ENODEV;
+    if (prop.major != 10) {
+        fprintf(stderr, "pion_vector_b200: device %d is sm_%d%d, need sm_100\n", device,
+                prop.major, prop.minor);
+        return PION_B200_ENODEV;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) return PION_B200_ENODEV;
+    pion_b200_ctx* ctx = new (std::nothrow) pion_b200_ctx();
+    if (!ctx) return PION_B200_ENOMEM;
+    ctx->device = device;
+    ctx->worker_id = worker_id;
+    ctx->num_sms = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&ctx->h_status, sizeof(int)) != cudaSuccess) {
+        pion_v_b200_shutdown(ctx);
+        return PION_B200_ENOMEM;
+    }
+    ctx->stream = ctx->own_stream;
+    *ctx->h_status = 0;
+    cudaMemset(ctx->d_status, 0, sizeof(int));
+    cudaDeviceSynchronize();
+    *out_ctx = ctx;
+    return 0;
+}
+
+int pion_v_b200_shutdown(pion_b200_ctx* ctx) {
+    if (!ctx) return PION_B200_EINVAL;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    DevBuf* bufs[] = {&ctx->scratch, &ctx->scratch2, &ctx->stage_in, &ctx->stage_out};
+    for (DevBuf* b : bufs)
+        if (b->ptr) cudaFree(b->ptr);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->h_status) cudaFreeHost(ctx->h_status);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    for (cudaEvent_t e : ctx->ev_start) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->ev_end) cudaEventDestroy(e);
+    delete ctx;
+    return 0;
+}
+
+int pion_v_b200_set_stream(pion_b200_ctx* ctx, void* cuda_stream) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    ctx->stream = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : ctx->own_stream;
+    return 0;
+}
+
+int pion_v_b200_sync(pion_b200_ctx* ctx) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (int rc = use_device(ctx)) return rc;
+    return finish_sync(ctx);
+}
+
+const char* pion_v_b200_last_error(const pion_b200_ctx* ctx) {
+    return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+int64_t pion_v_b200_launch_count(const pion_b200_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int pion_v_b200_timing_enable(pion_b200_ctx* ctx, int enable) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStreamSynchronize(ctx->stream);
+    ctx->timing = enable != 0;
+    ctx->ev_used = 0;
+    return 0;
+}
+
+int pion_v_b200_timing_read(pion_b200_ctx* ctx, double* total_ms, int64_t* count) {
+    if (!valid_ctx(ctx) || !total_ms || !count) return PION_B200_EINVAL;
+    if (int rc = use_device(ctx)) return rc;
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        return set_error(ctx, PION_B200_ECUDA, "timing_read: stream failed");
+    double sum = 0.0;
+    for (size_t i = 0; i < ctx->ev_used; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, ctx->ev_start[i], ctx->ev_end[i]) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "timing_read: event %zu", i);
+        sum += ms;
+    }
+    *total_ms = sum;
+    *count = (int64_t)ctx->ev_used;
+    return 0;
+}
+
+int pion_v_b200_reserve(pion_b200_ctx* ctx, int64_t max_nq, int64_t max_k) {
+    if (!valid_ctx(ctx) || max_nq < 0 || max_k < 0) return PION_B200_EINVAL;
+    if (int rc = use_device(ctx)) return rc;
+    const size_t lists = 64;  // upper bound on splits per query tile
+    size_t cand = (size_t)max_nq * lists * (size_t)max_k * 8 + (size_t)ctx->num_sms * 8 * max_k * 8;
+    if (ensure(ctx->scratch, cand) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "reserve: %zu bytes", cand);
+    return 0;
+}
+
+int64_t pion_v_b200_index_rows(const pion_b200_index* index) { return index ? index->n_rows : -1; }
+
+int pion_v_b200_index_free(pion_b200_index* index) {
+    if (!index) return PION_B200_EINVAL;
+    cudaSetDevice(index->device);
+    cudaDeviceSynchronize();
+    if (index->owns) {
+        if (index->rows_i8) cudaFree(index->rows_i8);
+        if (index->row_scale) cudaFree(index->row_scale);
+        if (index->rows_f32) cudaFree(index->rows_f32);
+    }
+    if (index->tile_rs_max) cudaFree(index->tile_rs_max);
+    if (index->codes) cudaFree(index->codes);
+    delete index;
+    return 0;
+}
+
+// ------------------------------------------------------------------ FLAT INT8
+
+int pion_v_b200_register_flat_i8(pion_b200_ctx* ctx, const int8_t* rows, const float* row_scale,
+                                 int64_t n_rows, int64_t dim, int64_t id_base, int mem,
+                                 pion_b200_index** out_index) {
+    if (!valid_ctx(ctx) || !out_index) return PION_B200_EINVAL;
+    *out_index = nullptr;
+    if (n_rows < 0 || (n_rows > 0 && (!rows || !row_scale)))
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_i8: null rows");
+    if (dim <= 0 || dim % 16 != 0 || dim > 16384)
+        return set_error(ctx, PION_B200_ESHAPE, "register_flat_i8: dim %lld must be a multiple "
+                         "of 16 in [16, 16384]", (long long)dim);
+    if (n_rows > INT32_MAX - 1 || id_base < 0 || id_base + n_rows > INT32_MAX)
+        return set_error(ctx, PION_B200_ESHAPE, "register_flat_i8: ids must fit int32");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE && mem != PION_B200_MEM_DEVICE_BORROW)
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_i8: bad mem %d", mem);
+    if (int rc = use_device(ctx)) return rc;
+    pion_b200_index* ix = new (std::nothrow) pion_b200_index();
+    if (!ix) return PION_B200_ENOMEM;
+    ix->kind = kFlatI8;
+    ix->device = ctx->device;
+    ix->n_rows = n_rows;
+    ix->dim = dim;
+    ix->id_base = id_base;
+    const size_t rbytes = (size_t)n_rows * (size_t)dim;
+    const int n_tiles = (int)((n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
+    if (mem == PION_B200_MEM_DEVICE_BORROW) {
+        ix->owns = false;
+        ix->rows_i8 = const_cast<int8_t*>(rows);
+        ix->row_scale = const_cast<float*>(row_scale);
+    } else {
+        if (cudaMalloc(&ix->rows_i8, rbytes ? rbytes : 16) != cudaSuccess ||
+            cudaMalloc(&ix->row_scale, (size_t)(n_rows ? n_rows : 1) * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, PION_B200_ENOMEM, "register_flat_i8: %zu bytes", rbytes);
+        }
+        const cudaMemcpyKind kind =
+            mem == PION_B200_MEM_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+        if (n_rows > 0 &&
+            (cudaMemcpyAsync(ix->rows_i8, rows, rbytes, kind, ctx->stream) != cudaSuccess ||
+             cudaMemcpyAsync(ix->row_scale, row_scale, (size_t)n_rows * 4, kind, ctx->stream) !=
+                 cudaSuccess)) {
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, PION_B200_ECUDA, "register_flat_i8: copy failed");
+        }
+    }
+    if ((reinterpret_cast<uintptr_t>(ix->rows_i8) & 15u) != 0) {
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_i8: rows not 16-byte aligned");
+    }
+    if (cudaMalloc(&ix->tile_rs_max, (size_t)(n_tiles > 0 ? n_tiles : 1) * sizeof(float)) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, PION_B200_ENOMEM, "register_flat_i8: tile maxima");
+    }
+    if (n_rows > 0) {
+        if (launch_tile_max(ix->row_scale, n_rows, ix->tile_rs_max, ctx->stream) != 0) {
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, PION_B200_ECUDA, "register_flat_i8: tile max launch");
+        }
+        ctx->launches++;
+        if (make_tmap_2d(&ix->tmap_rows, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ix->rows_i8,
+                         (uint64_t)dim, (uint64_t)n_rows, (uint64_t)dim, (uint32_t)fi8_k_block(),
+                         (uint32_t)fi8_tile_rows(), CU_TENSOR_MAP_SWIZZLE_128B) != 0) {
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, PION_B200_ECUDA, "register_flat_i8: tensor map");
+        }
+        ix->has_tmap = true;
+    }
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, PION_B200_ECUDA, "register_flat_i8: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    }
+    *out_index = ix;
+    return 0;
+}
+
+// Forced path selection for tests: 0 auto, 1 one-query scan, 2 tensor-core kernel.
+static int forced_i8_path() {
+    const char* e = getenv("PION_B200_I8_PATH");
+    return e ? atoi(e) : 0;
+}
+
+int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* q,
+                            const float* q_scale, int64_t nq, int64_t k, int32_t* out_ids,
+                            float* out_scores, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kFlatI8)
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn: not a FLAT INT8 index");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn: index on device %d, context on %d",
+                         ix->device, ctx->device);
+    if (nq < 0 || k < 1 || (nq > 0 && (!q || !q_scale || !out_ids || !out_scores)))
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn: bad arguments");
+    if (k > 64) return set_error(ctx, PION_B200_ESHAPE, "flat_i8_knn: k %lld > 64", (long long)k);
+    if (nq > (1 << 24)) return set_error(ctx, PION_B200_ESHAPE, "flat_i8_knn: batch too large");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn: bad mem %d", mem);
+    if (nq == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const int dim = (int)ix->dim;
+    const int kk = (int)k;
+    const int nqi = (int)nq;
+
+    const int8_t* dq = q;
+    const float* dqs = q_scale;
+    int32_t* di = out_ids;
+    float* dv = out_scores;
+    const size_t q_bytes = align_up((size_t)nq * dim, 256);
+    const size_t out_bytes = (size_t)nq * kk * 4;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, q_bytes + (size_t)nq * 4) != 0 ||
+            ensure(ctx->stage_out, 2 * align_up(out_bytes, 256)) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn: staging");
+        int8_t* sq = static_cast<int8_t*>(ctx->stage_in.ptr);
+        float* sqs = reinterpret_cast<float*>(sq + q_bytes);
+        if (cudaMemcpyAsync(sq, q, (size_t)nq * dim, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(sqs, q_scale, (size_t)nq * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "flat_i8_knn: query copy failed");
+        dq = sq;
+        dqs = sqs;
+        di = static_cast<int32_t*>(ctx->stage_out.ptr);
+        dv = reinterpret_cast<float*>(static_cast<char*>(ctx->stage_out.ptr) + align_up(out_bytes, 256));
+    } else if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0) {
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn: queries not 16-byte aligned");
+    }
+
+    int rc = 0;
+    if (ix->n_rows == 0) {
+        // Empty index: every result slot is padding (id -1, score -inf).
+        rc = launch_fill_results(dv, di, (size_t)nq * kk, -INFINITY, st);
+        ctx->launches++;
+    }
+    const int path = forced_i8_path();
+    const bool use_scan = ix->n_rows > 0 && (path == 1 || (path == 0 && nq == 1));
+    if (ix->n_rows > 0 && use_scan) {
+        const int ctas = fi8_scan1_ctas(ix->n_rows, ctx->num_sms);
+        const size_t cbytes = (size_t)ctas * kk * 8;
+        if (ensure(ctx->scratch, cbytes * (size_t)nq) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn: scratch");
+        float* cv = static_cast<float*>(ctx->scratch.ptr);
+        int32_t* ci = reinterpret_cast<int32_t*>(cv + (size_t)nq * ctas * kk);
+        for (int64_t t = 0; t < nq && rc == 0; ++t) {
+            timing_begin(ctx);
+            rc = launch_flat_i8_scan1(ix->rows_i8, ix->row_scale, ix->n_rows, dim,
+                                      dq + (size_t)t * dim, dqs + t, kk, ctas,
+                                      cv + (size_t)t * ctas * kk, ci + (size_t)t * ctas * kk, st);
+            timing_end(ctx);
+            ctx->launches++;
+        }
+        if (rc == 0) {
+            rc = launch_merge_lists(cv, ci, nqi, ctas, kk, ix->id_base, true, dv, di, st);
+            ctx->launches++;
+        }
+    } else if (ix->n_rows > 0) {
+        const int n_qt = (nqi + fi8_query_tile() - 1) / fi8_query_tile();
+        const int n_tiles = (int)((ix->n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
+        const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
+        const size_t ncand = (size_t)nq * splits * kk;
+        if (ensure(ctx->scratch, ncand * 8) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn: scratch");
+        float* cv = static_cast<float*>(ctx->scratch.ptr);
+        int32_t* ci = reinterpret_cast<int32_t*>(cv + ncand);
+        CUtensorMap tmap_q;
+        if (make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dq, (uint64_t)dim,
+                         (uint64_t)nq, (uint64_t)dim, (uint32_t)fi8_k_block(),
+                         (uint32_t)fi8_query_tile(), CU_TENSOR_MAP_SWIZZLE_128B) != 0)
+            return set_error(ctx, PION_B200_ECUDA, "flat_i8_knn: query tensor map");
+        timing_begin(ctx);
+        rc = launch_flat_i8_tc(tmap_q, ix->tmap_rows, ix->row_scale, ix->tile_rs_max, dqs,
+                               ix->n_rows, nqi, dim, kk, splits, cv, ci, ctx->d_status, st);
+        timing_end(ctx);
+        ctx->launches++;
+        if (rc == 0) {
+            rc = launch_merge_lists(cv, ci, nqi, splits, kk, ix->id_base, true, dv, di, st);
+            ctx->launches++;
+        }
+    }
+    if (rc != 0)
+        return set_error(ctx, rc, "flat_i8_knn: launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(out_ids, di, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_scores, dv, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "flat_i8_knn: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+// --------------------------------------------------------------- utilities
+
+int pion_v_b200_quantize_rows_i8(pion_b200_ctx* ctx, const float* src, int64_t n_rows, int64_t d,
+                                 int64_t d_pad, int8_t* dst, float* dst_scale, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (n_rows < 0 || d < 0 || d_pad < d || d_pad > (1 << 20) ||
+        (n_rows > 0 && (!src || !dst || !dst_scale)))
+        return set_error(ctx, PION_B200_EINVAL, "quantize_rows_i8: bad arguments");
+    if (n_rows == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const float* ds = src;
+    int8_t* dd = dst;
+    float* dsc = dst_scale;
+    const size_t in_bytes = (size_t)n_rows * d_pad * 4;
+    const size_t out_bytes = align_up((size_t)n_rows * d_pad, 256);
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, in_bytes) != 0 ||
+            ensure(ctx->stage_out, out_bytes + (size_t)n_rows * 4) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "quantize_rows_i8: staging");
+        if (cudaMemcpyAsync(ctx->stage_in.ptr, src, in_bytes, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "quantize_rows_i8: copy failed");
+        ds = static_cast<const float*>(ctx->stage_in.ptr);
+        dd = static_cast<int8_t*>(ctx->stage_out.ptr);
+        dsc = reinterpret_cast<float*>(static_cast<char*>(ctx->stage_out.ptr) + out_bytes);
+    } else if (mem != PION_B200_MEM_DEVICE) {
+        return set_error(ctx, PION_B200_EINVAL, "quantize_rows_i8: bad mem %d", mem);
+    }
+    int rc = launch_quantize_rows_i8(ds, n_rows, (int)d, (int)d_pad, dd, dsc, st);
+    ctx->launches++;
+    if (rc != 0) return set_error(ctx, rc, "quantize_rows_i8: launch failed");
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(dst, dd, (size_t)n_rows * d_pad, cudaMemcpyDeviceToHost, st) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(dst_scale, dsc, (size_t)n_rows * 4, cudaMemcpyDeviceToHost, st) !=
+                cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "quantize_rows_i8: copy back failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+int pion_v_b200_merge_topk(pion_b200_ctx* ctx, const float* cand_scores, const int32_t* cand_ids,
+                           int64_t nq, int64_t n_lists, int64_t k, int flags,
+                           float* out_scores, int32_t* out_ids, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (nq < 0 || n_lists < 1 || k < 1 ||
+        (nq > 0 && (!cand_scores || !cand_ids || !out_scores || !out_ids)))
+        return set_error(ctx, PION_B200_EINVAL, "merge_topk: bad arguments");
+    if (n_lists > 2048 || k > 4096)
+        return set_error(ctx, PION_B200_ESHAPE, "merge_topk: n_lists <= 2048, k <= 4096");
+    if (nq == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const size_t cand = (size_t)nq * n_lists * k;
+    const size_t outn = (size_t)nq * k;
+    const float* cv = cand_scores;
+    const int32_t* ci = cand_ids;
+    float* ov = out_scores;
+    int32_t* oi = out_ids;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, cand * 8) != 0 || ensure(ctx->stage_out, outn * 8) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "merge_topk: staging");
+        float* sv = static_cast<float*>(ctx->stage_in.ptr);
+        int32_t* si = reinterpret_cast<int32_t*>(sv + cand);
+        if (cudaMemcpyAsync(sv, cand_scores, cand * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(si, cand_ids, cand * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "merge_topk: copy failed");
+        cv = sv;
+        ci = si;
+        ov = static_cast<float*>(ctx->stage_out.ptr);
+        oi = reinterpret_cast<int32_t*>(ov + outn);
+    } else if (mem != PION_B200_MEM_DEVICE) {
+        return set_error(ctx, PION_B200_EINVAL, "merge_topk: bad mem %d", mem);
+    }
+    int rc = launch_merge_lists(cv, ci, (int)nq, (int)n_lists, (int)k, 0,
+                                (flags & PION_B200_MERGE_DESC) != 0, ov, oi, st,
+                                (flags & PION_B200_MERGE_LISTS_MAJOR) != 0);
+    ctx->launches++;
+    if (rc != 0) return set_error(ctx, rc, "merge_topk: launch failed");
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(out_scores, ov, outn * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_ids, oi, outn * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "merge_topk: copy back failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,659 @@
+// FLAT INT8 inner-product KNN on B200 (sm_100a).
+//
+// Reference semantics (pavelhorak/pion):
+//   score(t, r) = (f32(dot_i32(q[t], keys[r])) * row_scale[r]) * q_scale[t]
+//     src/vector/reference/pkm_ref.mojo:47-61 (ref_pkm_scores_i8)
+//   top-k largest per query, seeded in index order, strict `>` admission
+//     src/vector/reference/pkm_ref.mojo:110-130 (ref_pkm_topk_max)
+//   rows quantised per row, scale = max|x|/127
+//     src/vector/pkm_kernels.mojo:152-191 (pkm_quantize_rows_i8)
+//
+// Kernels:
+//   flat_i8_tc_kernel     batched scoring on tcgen05 (kind::i8, TMEM accumulators,
+//                         TMA-staged 128B-swizzled tiles) with the top-k fused into
+//                         the TMEM epilogue: no score matrix reaches HBM.
+//   flat_i8_scan1_kernel  one query: an HBM stream of 128-bit loads with dp4a and a
+//                         fused top-k.
+//   merge_lists_kernel    per-query merge of sorted candidate lists.
+//   quantize_rows_i8_kernel, tile_max_kernel  index preparation.
+#include <cstdint>
+#include <cstdio>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace pion {
+namespace fi8 {
+
+constexpr int BM = 128;             // queries per CTA tile (UMMA M, TMEM lanes)
+constexpr int BN = 256;             // index rows per tile (UMMA N, TMEM columns)
+constexpr int BK = 128;             // bytes of K per pipeline stage (one swizzle row)
+constexpr int STAGES = 4;
+constexpr int UMMA_K = 32;          // int8 K consumed by one tcgen05.mma
+constexpr int A_BYTES = BM * BK;    // 16 KB
+constexpr int B_BYTES = BN * BK;    // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int EPI_THREADS = 128;
+constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
+constexpr uint32_t IDESC = make_idesc_i8(BM, BN);
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+
+static_assert(BN <= 256 && BN % 16 == 0, "UMMA N");
+static_assert(BK % UMMA_K == 0, "K step");
+
+struct TcParams {
+    const float* row_scale;    // [n_rows]
+    const float* tile_rs_max;  // [n_tiles] max row_scale over each BN-row tile
+    const float* q_scale;      // [nq]
+    int64_t n_rows;
+    int nq;
+    int k;
+    int n_tiles;
+    int n_splits;
+    int kblocks;
+    float* cand_val;           // [nq][n_splits][k]
+    int32_t* cand_idx;
+    int* status;
+};
+
+// score(d) = fl(fl(fl(d) * rs) * qs), the reference epilogue for one dot product.
+__device__ __forceinline__ float i8_score(int32_t d, float rs, float qs) {
+    return __fmul_rn(__fmul_rn(__int2float_rn(d), rs), qs);
+}
+
+// Largest integer d such that every dot <= d scores <= thr in a tile whose row
+// scales are all <= rs_max (fl(x*y) is monotone in each non-negative factor).
+// Returns INT32_MIN when no such integer bound applies (thr < 0 or -inf), so the
+// caller scores every element exactly.
+__device__ __forceinline__ int32_t dot_bound(float thr, float rs_max, float qs) {
+    if (!(thr >= 0.0f)) return INT32_MIN;
+    const double prod = (double)rs_max * (double)qs;
+    if (!(prod > 0.0)) return INT32_MAX;
+    double est = (double)thr / prod;
+    if (est > 2.0e9) return INT32_MAX;
+    // Start below the real-arithmetic solution by more than the rounding of the
+    // three float operations, then tighten upward with the exact formula.
+    int64_t d = (int64_t)floor(est * (1.0 - 1.0e-6)) - 2;
+    if (d < 0) d = 0;
+#pragma unroll 1
+    for (int it = 0; it < 64 && d < INT32_MAX; ++it) {
+        if (i8_score((int32_t)(d + 1), rs_max, qs) <= thr) ++d;
+        else break;
+    }
+    return (int32_t)d;
+}
+
+template <int KCAP>
+__global__ void __launch_bounds__(THREADS, 1)
+    flat_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                      const __grid_constant__ CUtensorMap tmap_rows, TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int qt = blockIdx.x;
+    const int split = blockIdx.y;
+    const int t_begin = (int)((int64_t)p.n_tiles * split / p.n_splits);
+    const int t_end = (int)((int64_t)p.n_tiles * (split + 1) / p.n_splits);
+    const int my_tiles = t_end - t_begin;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_THREADS);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmap_q);
+            tma_prefetch_desc(&tmap_rows);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_parity[STAGES];
+            bool issued[STAGES];
+            for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+            bool ok = true;
+            for (int t = 0; t < my_tiles && ok; ++t) {
+                const int row0 = (t_begin + t) * BN;
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                    tma_load_2d(sA + stage * A_BYTES, &tmap_q, &full[stage], kb * BK, qt * BM);
+                    tma_load_2d(sB + stage * B_BYTES, &tmap_rows, &full[stage], kb * BK, row0);
+                    issued[stage] = true;
+                    issued_parity[stage] = phase;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Every copy this thread issued lands before the CTA may exit.
+            for (int s = 0; s < STAGES; ++s)
+                if (issued[s]) mbar_wait(&full[s], issued_parity[s], p.status, nullptr);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int t = 0; t < my_tiles; ++t) {
+                const int buf = t & 1;
+                const uint32_t use = (uint32_t)(t >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, p.status, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, p.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                        mma_i8(d_tmem, make_sw128_kmajor_desc(a0 + kk * UMMA_K),
+                               make_sw128_kmajor_desc(b0 + kk * UMMA_K), IDESC,
+                               (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[buf]);
+            }
+            // All MMAs issued above complete before TMEM is released.
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.status, nullptr);
+        }
+    } else {
+        // --------------------------------------------- epilogue: score + top-k
+        const int lg = warp & 3;  // TMEM lane quarter this warp may read
+        const int row = lg * 32 + lane;
+        const int q = qt * BM + row;
+        const bool q_ok = q < p.nq;
+        const float qs = q_ok ? p.q_scale[q] : 0.0f;
+        TopKDesc<KCAP> top;
+        top.init();
+        float thr = -INFINITY;
+        for (int t = 0; t < my_tiles; ++t) {
+            const int buf = t & 1;
+            const uint32_t use = (uint32_t)(t >> 1);
+            // Every lane waits; the warp proceeds only if all of them saw the phase,
+            // so the warp-collective TMEM loads below stay convergent.
+            const bool got = mbar_wait(&tfull[buf], use & 1u, p.status, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const int tile = t_begin + t;
+            const int64_t col0 = (int64_t)tile * BN;
+            const float rs_max = p.tile_rs_max[tile];
+            const int64_t valid = p.n_rows - col0;  // columns of this tile inside the index
+            int32_t dmin = q_ok ? dot_bound(thr, rs_max, qs) : INT32_MAX;
+            const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(buf * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+                tmem_ld_wait();
+                // Cheap pass: one integer compare per column builds the candidate mask.
+                uint32_t mask = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] > dmin ? 1u : 0u) << j;
+                if (valid < (int64_t)(c + 1) * 32) {
+                    const int64_t keep = valid - (int64_t)c * 32;
+                    mask &= keep <= 0 ? 0u : (keep >= 32 ? 0xffffffffu : ((1u << keep) - 1u));
+                }
+                // Exact pass over the (rare) candidates, in ascending column order.
+#pragma unroll 1
+                while (mask) {
+                    const int j = __ffs(mask) - 1;
+                    mask &= mask - 1u;
+                    // Register select (kept as PTX so the compiler cannot turn it
+                    // into an indexed local-memory access to r[]).
+                    uint32_t sel = r[0];
+#pragma unroll
+                    for (int jj = 1; jj < 32; ++jj)
+                        asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\t"
+                            "selp.b32 %0, %1, %0, p;\n\t}"
+                            : "+r"(sel)
+                            : "r"(r[jj]), "r"(j), "r"(jj));
+                    const int32_t dv = (int32_t)sel;
+                    if (dv <= dmin) continue;
+                    const int64_t col = col0 + c * 32 + j;
+                    const float s = i8_score(dv, __ldg(&p.row_scale[col]), qs);
+                    if (s > thr) {
+                        top.insert(s, (int32_t)col);
+                        thr = top.kth(p.k);
+                        dmin = dot_bound(thr, rs_max, qs);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[buf]);
+        }
+        if (q_ok) {
+            const size_t base = ((size_t)q * p.n_splits + split) * p.k;
+#pragma unroll
+            for (int j = 0; j < KCAP; ++j)
+                if (j < p.k) {
+                    p.cand_val[base + j] = top.v[j];
+                    p.cand_idx[base + j] = top.i[j];
+                }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// Max row scale per BN-row tile, for the integer admission bound above.
+__global__ void tile_max_kernel(const float* rs, int64_t n_rows, int tile, float* out,
+                                int n_tiles) {
+    const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= n_tiles) return;
+    const int lane = threadIdx.x & 31;
+    float m = 0.0f;
+    for (int64_t r = (int64_t)t * tile + lane; r < (int64_t)(t + 1) * tile && r < n_rows; r += 32)
+        m = fmaxf(m, rs[r]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) out[t] = m;
+}
+
+// ------------------------------------------------------------- one query scan
+constexpr int SCAN_THREADS = 256;
+constexpr int SCAN_GROUP = 8;                      // lanes per row: 8 x 16 B = 128 B
+constexpr int SCAN_GROUPS = SCAN_THREADS / SCAN_GROUP;
+constexpr int SCAN_MAX_CHUNKS = 1024;              // dim <= 16384
+
+__device__ __forceinline__ int4 ld_stream(const int4* p) {
+    int4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+template <int KCAP>
+__global__ void __launch_bounds__(SCAN_THREADS)
+    flat_i8_scan1_kernel(const int8_t* __restrict__ rows, const float* __restrict__ row_scale,
+                         int64_t n_rows, int dim, const int8_t* __restrict__ q,
+                         const float* __restrict__ q_scale, int k, int64_t rows_per_cta,
+                         float* cand_val, int32_t* cand_idx) {
+    __shared__ int4 qv[SCAN_MAX_CHUNKS];
+    __shared__ float lv[SCAN_GROUPS * KCAP];
+    __shared__ int32_t li[SCAN_GROUPS * KCAP];
+    const int chunks = dim >> 4;
+    for (int c = threadIdx.x; c < chunks; c += SCAN_THREADS)
+        qv[c] = reinterpret_cast<const int4*>(q)[c];
+    __syncthreads();
+    const float qsc = q_scale[0];
+    const int g = threadIdx.x / SCAN_GROUP;
+    const int gl = threadIdx.x % SCAN_GROUP;
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > n_rows) r1 = n_rows;
+    TopKDesc<KCAP> top;
+    top.init();
+    float thr = -INFINITY;
+    // The trip count is the same for every lane of the CTA (rows past r1 are masked),
+    // so the full-warp shuffles below always see all 32 lanes.
+    for (int64_t base = r0; base < r1; base += SCAN_GROUPS) {
+        const int64_t r = base + g;
+        const bool valid = r < r1;
+        int acc = 0;
+        if (valid) {
+            const int4* rp = reinterpret_cast<const int4*>(rows + r * dim);
+#pragma unroll 4
+            for (int c = gl; c < chunks; c += SCAN_GROUP) {
+                const int4 a = ld_stream(rp + c);
+                const int4 b = qv[c];
+                acc = __dp4a(a.x, b.x, acc);
+                acc = __dp4a(a.y, b.y, acc);
+                acc = __dp4a(a.z, b.z, acc);
+                acc = __dp4a(a.w, b.w, acc);
+            }
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        if (valid) {
+            const float s = __fmul_rn(__fmul_rn(__int2float_rn(acc), __ldg(&row_scale[r])), qsc);
+            if (s > thr) {
+                top.insert(s, (int32_t)r);
+                thr = top.kth(k);
+            }
+        }
+    }
+    if (gl == 0) {
+#pragma unroll
+        for (int j = 0; j < KCAP; ++j) {
+            lv[g * KCAP + j] = top.v[j];
+            li[g * KCAP + j] = top.i[j];
+        }
+    }
+    __syncthreads();
+    // Warp 0 merges the CTA's SCAN_GROUPS sorted lists (one per lane) into k.
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int cur = 0;
+        for (int j = 0; j < k; ++j) {
+            float hv = cur < KCAP ? lv[lane * KCAP + cur] : -INFINITY;
+            int32_t hi = cur < KCAP ? li[lane * KCAP + cur] : -1;
+            float bv = hv;
+            int32_t bi = hi;
+            int bl = lane;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+                if (better_desc(ov, oi, bv, bi) || (ov == bv && oi == bi && ol < bl)) {
+                    bv = ov;
+                    bi = oi;
+                    bl = ol;
+                }
+            }
+            if (lane == bl) ++cur;
+            if (lane == 0) {
+                cand_val[(size_t)blockIdx.x * k + j] = bv;
+                cand_idx[(size_t)blockIdx.x * k + j] = bi;
+            }
+        }
+    }
+}
+
+}  // namespace fi8
+
+// ------------------------------------------------------------------ merging --
+// One warp per query merges n_lists sorted lists of k (score, id) pairs laid out
+// [nq][n_lists][k] (list stride `k`) into the k best, adding id_offset to valid ids.
+constexpr int MERGE_WARPS = 4;
+constexpr int MERGE_MAX_LISTS = 2048;
+
+template <bool DESC>
+__device__ __forceinline__ bool merge_better(float sa, int32_t ia, float sb, int32_t ib) {
+    if (DESC) return better_desc(sa, ia, sb, ib);
+    if (sa != sb) return sa < sb;
+    if (ia < 0) return false;
+    if (ib < 0) return true;
+    return ia < ib;
+}
+
+template <bool DESC>
+__global__ void __launch_bounds__(MERGE_WARPS * 32)
+    merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int nq,
+                       int n_lists, int k, int64_t id_offset, float* out_v, int32_t* out_i,
+                       int lists_major) {
+    __shared__ uint16_t cursor[MERGE_WARPS][MERGE_MAX_LISTS];
+    const int w = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = blockIdx.x * MERGE_WARPS + w;
+    if (q >= nq) return;
+    for (int l = lane; l < n_lists; l += 32) cursor[w][l] = 0;
+    __syncwarp();
+    const float pad = DESC ? -INFINITY : INFINITY;
+    // list l of query q starts at base + l * lstride
+    const size_t base = lists_major ? (size_t)q * k : (size_t)q * n_lists * k;
+    const size_t lstride = lists_major ? (size_t)nq * k : (size_t)k;
+    const float* qv = cv + base;
+    const int32_t* qi = ci + base;
+    for (int j = 0; j < k; ++j) {
+        float bv = pad;
+        int32_t bi = -1;
+        int bl = -1;
+        for (int l = lane; l < n_lists; l += 32) {
+            const int c = cursor[w][l];
+            if (c >= k) continue;
+            const float v = qv[(size_t)l * lstride + c];
+            const int32_t id = qi[(size_t)l * lstride + c];
+            if (bl < 0 || merge_better<DESC>(v, id, bv, bi)) {
+                bv = v;
+                bi = id;
+                bl = l;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            const bool take = (ol >= 0) && (bl < 0 || merge_better<DESC>(ov, oi, bv, bi) ||
+                                            (ov == bv && oi == bi && ol < bl));
+            if (take) {
+                bv = ov;
+                bi = oi;
+                bl = ol;
+            }
+        }
+        if (bl >= 0 && (bl % 32) == lane) cursor[w][bl] += 1;
+        __syncwarp();
+        if (lane == 0) {
+            out_v[(size_t)q * k + j] = bv;
+            out_i[(size_t)q * k + j] = bi >= 0 ? (int32_t)(bi + id_offset) : -1;
+        }
+    }
+}
+
+__global__ void fill_results_kernel(float* v, int32_t* i, size_t n, float value) {
+    for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < n;
+         t += (size_t)gridDim.x * blockDim.x) {
+        v[t] = value;
+        i[t] = -1;
+    }
+}
+
+// ------------------------------------------------------------- quantisation --
+// pkm_quantize_rows_i8 (src/vector/pkm_kernels.mojo:152-191), one warp per row.
+// max|x| is order-independent; the divides and the +-0.5 rounding use the same
+// IEEE round-to-nearest operations as the reference, then truncate toward zero.
+__global__ void quantize_rows_i8_kernel(const float* __restrict__ src, int64_t n_rows, int d,
+                                        int d_pad, int8_t* __restrict__ dst,
+                                        float* __restrict__ dst_scale) {
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (r >= n_rows) return;
+    const int lane = threadIdx.x & 31;
+    const float* sp = src + r * d_pad;
+    float m = 0.0f;
+    for (int c = lane; c < d; c += 32) m = fmaxf(m, fabsf(sp[c]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float scale = __fdiv_rn(m, 127.0f);
+    if (m == 0.0f) scale = 1.0f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* dp = dst + r * d_pad;
+    for (int c = lane; c < d_pad; c += 32) {
+        int qi = 0;
+        if (c < d) {
+            const float qv = __fmul_rn(sp[c], inv);
+            qi = qv >= 0.0f ? __float2int_rz(__fadd_rn(qv, 0.5f))
+                            : __float2int_rz(__fsub_rn(qv, 0.5f));
+            qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+        }
+        dp[c] = (int8_t)qi;
+    }
+    if (lane == 0) dst_scale[r] = scale;
+}
+
+// =========================================================== host launchers ==
+
+int fi8_tile_rows() { return fi8::BN; }
+
+int launch_tile_max(const float* rs, int64_t n_rows, float* out, cudaStream_t st) {
+    const int n_tiles = (int)((n_rows + fi8::BN - 1) / fi8::BN);
+    if (n_tiles <= 0) return 0;
+    const int warps = 8;
+    fi8::tile_max_kernel<<<(n_tiles + warps - 1) / warps, warps * 32, 0, st>>>(rs, n_rows, fi8::BN, out,
+                                                                          n_tiles);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_quantize_rows_i8(const float* src, int64_t n_rows, int d, int d_pad, int8_t* dst,
+                            float* dst_scale, cudaStream_t st) {
+    if (n_rows <= 0) return 0;
+    const int warps = 8;
+    const int64_t blocks = (n_rows + warps - 1) / warps;
+    quantize_rows_i8_kernel<<<(unsigned)blocks, warps * 32, 0, st>>>(src, n_rows, d, d_pad, dst,
+                                                                     dst_scale);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st) {
+    if (n == 0) return 0;
+    const unsigned blocks = (unsigned)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+    fill_results_kernel<<<blocks, 256, 0, st>>>(v, i, n, value);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
+                       int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
+                       cudaStream_t st, bool lists_major) {
+    if (nq <= 0) return 0;
+    if (n_lists > MERGE_MAX_LISTS || k > 65535) return PION_B200_ESHAPE;
+    const int blocks = (nq + MERGE_WARPS - 1) / MERGE_WARPS;
+    if (descending)
+        merge_lists_kernel<true><<<blocks, MERGE_WARPS * 32, 0, st>>>(
+            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0);
+    else
+        merge_lists_kernel<false><<<blocks, MERGE_WARPS * 32, 0, st>>>(
+            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+// Splits of the index across CTAs for a batch of n_qt query tiles: the count whose
+// total CTA number fills whole waves of the SMs best, preferring fewer splits.
+int fi8_choose_splits(int n_qt, int n_tiles, int num_sms) {
+    int best = 1;
+    double best_eff = -1.0;
+    for (int s = 1; s <= 64; ++s) {
+        if (s > 1 && n_tiles / s < 4) break;
+        const long total = (long)n_qt * s;
+        const long waves = (total + num_sms - 1) / num_sms;
+        const double eff = (double)total / (double)(waves * num_sms);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = s;
+        }
+    }
+    return best;
+}
+
+int fi8_kcap(int k) { return k <= 16 ? 16 : (k <= 32 ? 32 : (k <= 64 ? 64 : 0)); }
+
+template <int KCAP>
+static int launch_tc_k(const CUtensorMap& tq, const CUtensorMap& tr, const fi8::TcParams& p,
+                       int n_qt, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(fi8::flat_i8_tc_kernel<KCAP>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)fi8::SMEM_BYTES) != cudaSuccess)
+            return PION_B200_ECUDA;
+        configured = true;
+    }
+    dim3 grid(n_qt, p.n_splits);
+    fi8::flat_i8_tc_kernel<KCAP><<<grid, fi8::THREADS, fi8::SMEM_BYTES, st>>>(tq, tr, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_flat_i8_tc(const CUtensorMap& tmap_q, const CUtensorMap& tmap_rows,
+                      const float* row_scale, const float* tile_rs_max, const float* q_scale,
+                      int64_t n_rows, int nq, int dim, int k, int n_splits, float* cand_val,
+                      int32_t* cand_idx, int* status, cudaStream_t st) {
+    fi8::TcParams p;
+    p.row_scale = row_scale;
+    p.tile_rs_max = tile_rs_max;
+    p.q_scale = q_scale;
+    p.n_rows = n_rows;
+    p.nq = nq;
+    p.k = k;
+    p.n_tiles = (int)((n_rows + fi8::BN - 1) / fi8::BN);
+    p.n_splits = n_splits;
+    p.kblocks = (dim + fi8::BK - 1) / fi8::BK;
+    p.cand_val = cand_val;
+    p.cand_idx = cand_idx;
+    p.status = status;
+    const int n_qt = (nq + fi8::BM - 1) / fi8::BM;
+    switch (fi8_kcap(k)) {
+        case 16: return launch_tc_k<16>(tmap_q, tmap_rows, p, n_qt, st);
+        case 32: return launch_tc_k<32>(tmap_q, tmap_rows, p, n_qt, st);
+        case 64: return launch_tc_k<64>(tmap_q, tmap_rows, p, n_qt, st);
+        default: return PION_B200_ESHAPE;
+    }
+}
+
+int fi8_query_tile() { return fi8::BM; }
+int fi8_k_block() { return fi8::BK; }
+
+int fi8_scan1_ctas(int64_t n_rows, int num_sms) {
+    int64_t ctas = (int64_t)num_sms * 4;
+    const int64_t min_rows = 256;
+    if (ctas * min_rows > n_rows) ctas = (n_rows + min_rows - 1) / min_rows;
+    return (int)(ctas < 1 ? 1 : ctas);
+}
+
+int launch_flat_i8_scan1(const int8_t* rows, const float* row_scale, int64_t n_rows, int dim,
+                         const int8_t* q, const float* q_scale, int k, int ctas, float* cand_val,
+                         int32_t* cand_idx, cudaStream_t st) {
+    if (dim % 16 != 0 || dim / 16 > fi8::SCAN_MAX_CHUNKS) return PION_B200_ESHAPE;
+    const int64_t rows_per_cta = (n_rows + ctas - 1) / ctas;
+    switch (fi8_kcap(k)) {
+        case 16:
+            fi8::flat_i8_scan1_kernel<16><<<ctas, fi8::SCAN_THREADS, 0, st>>>(
+                rows, row_scale, n_rows, dim, q, q_scale, k, rows_per_cta, cand_val, cand_idx);
+            break;
+        case 32:
+            fi8::flat_i8_scan1_kernel<32><<<ctas, fi8::SCAN_THREADS, 0, st>>>(
+                rows, row_scale, n_rows, dim, q, q_scale, k, rows_per_cta, cand_val, cand_idx);
+            break;
+        case 64:
+            fi8::flat_i8_scan1_kernel<64><<<ctas, fi8::SCAN_THREADS, 0, st>>>(
+                rows, row_scale, n_rows, dim, q, q_scale, k, rows_per_cta, cand_val, cand_idx);
+            break;
+        default:
+            return PION_B200_ESHAPE;
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+}  // namespace pion

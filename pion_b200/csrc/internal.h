@@ -1,0 +1,100 @@
+// Host-side declarations shared by the .cu files of libpion_vector_b200: the
+// context and index objects behind the opaque C handles, and the kernel launchers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/pion_vector_b200.h"
+
+namespace pion {
+
+// A grow-only device buffer.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+enum IndexKind { kFlatI8 = 1, kFlatF32 = 2, kBQ = 3 };
+
+}  // namespace pion
+
+struct pion_b200_ctx {
+    int device = 0;
+    int worker_id = 0;
+    int num_sms = 148;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int* d_status = nullptr;       // device status word, written by bounded waits
+    int* h_status = nullptr;       // pinned mirror of d_status
+    pion::DevBuf scratch;          // per-call candidate lists
+    pion::DevBuf scratch2;         // second-level scratch (merges, shortlists)
+    pion::DevBuf stage_in;         // device copies of host inputs
+    pion::DevBuf stage_out;        // device outputs copied back to host
+    std::string last_error;
+    int64_t launches = 0;
+    // scoring-kernel timing (pion_v_b200_timing_*)
+    bool timing = false;
+    std::vector<cudaEvent_t> ev_start, ev_end;
+    size_t ev_used = 0;
+};
+
+struct pion_b200_index {
+    int kind = 0;
+    int device = 0;
+    int64_t n_rows = 0;
+    int64_t dim = 0;
+    int64_t id_base = 0;
+    bool owns = true;
+    // FLAT INT8
+    int8_t* rows_i8 = nullptr;
+    float* row_scale = nullptr;
+    float* tile_rs_max = nullptr;
+    // FLAT FP32 and BQ rerank rows
+    float* rows_f32 = nullptr;
+    // BQ sign codes, uint64 words per row
+    uint64_t* codes = nullptr;
+    int64_t words = 0;
+    CUtensorMap tmap_rows;
+    bool has_tmap = false;
+};
+
+namespace pion {
+
+// ---- error helpers (abi.cu)
+int set_error(pion_b200_ctx* ctx, int code, const char* fmt, ...);
+int ensure(DevBuf& b, size_t bytes);
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle);
+
+// ---- flat_i8.cu
+int fi8_tile_rows();
+int fi8_query_tile();
+int fi8_k_block();
+int fi8_kcap(int k);
+int fi8_choose_splits(int n_qt, int n_tiles, int num_sms);
+int fi8_scan1_ctas(int64_t n_rows, int num_sms);
+int launch_tile_max(const float* rs, int64_t n_rows, float* out, cudaStream_t st);
+int launch_quantize_rows_i8(const float* src, int64_t n_rows, int d, int d_pad, int8_t* dst,
+                            float* dst_scale, cudaStream_t st);
+int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st);
+int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
+                       int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
+                       cudaStream_t st, bool lists_major = false);
+// Event pair around one scoring-kernel launch when timing is enabled.
+void timing_begin(pion_b200_ctx* ctx);
+void timing_end(pion_b200_ctx* ctx);
+int launch_flat_i8_tc(const CUtensorMap& tmap_q, const CUtensorMap& tmap_rows,
+                      const float* row_scale, const float* tile_rs_max, const float* q_scale,
+                      int64_t n_rows, int nq, int dim, int k, int n_splits, float* cand_val,
+                      int32_t* cand_idx, int* status, cudaStream_t st);
+int launch_flat_i8_scan1(const int8_t* rows, const float* row_scale, int64_t n_rows, int dim,
+                         const int8_t* q, const float* q_scale, int k, int ctas, float* cand_val,
+                         int32_t* cand_idx, cudaStream_t st);
+
+}  // namespace pion

@@ -1,0 +1,324 @@
+"""Python host API over libpion_vector_b200 — the FT.SEARCH KNN operators.
+
+Mirrors the operator surface of Pion's vector path (pavelhorak/pion):
+
+* ``pkm_quantize_rows_i8`` / ``pkm_scores_i8`` / ``pkm_topk_max`` /
+  ``pkm_sort_desc`` / ``pkm_combine_topk`` / ``pkm_scores_f32`` /
+  ``pkm_rescore_f32`` — same names and argument meaning as
+  src/vector/pkm_kernels.mojo:88-266 (the C symbols the engine binds);
+* ``FlatI8Index.search`` — batched FLAT INT8 inner-product KNN
+  (ref_pkm_scores_i8 + ref_pkm_topk_max per query);
+* ``FlatF32Index.search`` — batched ``exact_knn`` under COSINE
+  (src/commands/vector.mojo:1228-1365);
+* ``BQIndex.search`` — sign-bit Hamming shortlist + exact cosine rerank.
+
+Arrays may be numpy (host memory: the call copies to and from the GPU) or CUDA
+torch tensors (device memory: used in place on the context's stream).  Errors
+raise ``PionError`` with the library's message; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import MEM_DEVICE, MEM_DEVICE_BORROW, MEM_HOST, PionError
+
+try:  # torch is plumbing for device memory and streams; optional for host-only use
+    import torch
+except Exception:  # pragma: no cover
+    torch = None
+
+
+def _is_torch(x) -> bool:
+    return torch is not None and isinstance(x, torch.Tensor)
+
+
+def _ptr(x, dtype_np, name: str):
+    """(pointer, mem kind, keep-alive object) for a numpy array or torch tensor."""
+    if _is_torch(x):
+        if not x.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        want = {np.int8: torch.int8, np.float32: torch.float32, np.int32: torch.int32,
+                np.uint64: torch.uint64 if hasattr(torch, "uint64") else torch.int64}[dtype_np]
+        if x.dtype != want:
+            raise TypeError(f"{name} must be {want}, got {x.dtype}")
+        return x.data_ptr(), (MEM_DEVICE if x.is_cuda else MEM_HOST), x
+    a = np.ascontiguousarray(x, dtype=dtype_np)
+    return a.ctypes.data, MEM_HOST, a
+
+
+def _torch_stream() -> int:
+    """torch's current stream as a cudaStream_t; its legacy default stream has handle 0,
+    which the C API reads as "the context's own stream", so it is passed as
+    cudaStreamLegacy (0x1) instead."""
+    return torch.cuda.current_stream().cuda_stream or 1
+
+
+class _TorchStream:
+    """For device-memory calls: run the library on torch's current CUDA stream so
+    that tensors torch produced (or will consume) are ordered with our kernels."""
+
+    def __init__(self, ctx, mem):
+        self.ctx = ctx
+        self.active = mem in (MEM_DEVICE, MEM_DEVICE_BORROW) and torch is not None
+
+    def __enter__(self):
+        if self.active:
+            self.ctx.lib.pion_v_b200_set_stream(self.ctx.h, ctypes.c_void_p(_torch_stream()))
+        return self
+
+    def __exit__(self, *exc):
+        if self.active:
+            self.ctx.lib.pion_v_b200_set_stream(self.ctx.h, ctypes.c_void_p(self.ctx._stream))
+
+
+def _same_mem(*mems):
+    m = set(mems)
+    if len(m) != 1:
+        raise ValueError("all arrays of one call must live in the same memory (host or device)")
+    return m.pop()
+
+
+class Context:
+    """One worker's CUDA stream, scratch buffers and error slot (pion_v_b200_init)."""
+
+    def __init__(self, device: int = -1, worker_id: int = 0):
+        self.lib = _lib.load()
+        h = ctypes.c_void_p()
+        rc = self.lib.pion_v_b200_init(device, worker_id, ctypes.byref(h))
+        if rc != 0:
+            raise PionError(rc, f"pion_v_b200_init(device={device}) failed")
+        self.h = h
+        self.device = device
+        self._stream = 0  # 0: the context's own stream
+
+    def check(self, rc: int):
+        if rc != 0:
+            msg = self.lib.pion_v_b200_last_error(self.h)
+            raise PionError(rc, msg.decode() if msg else "")
+
+    def use_stream(self, stream_handle: int | None):
+        self._stream = stream_handle or 0
+        self.check(self.lib.pion_v_b200_set_stream(self.h, ctypes.c_void_p(self._stream)))
+
+    def use_torch_stream(self):
+        """Run on torch's current CUDA stream (so torch ops and ours are ordered)."""
+        self.use_stream(_torch_stream())
+
+    def sync(self):
+        self.check(self.lib.pion_v_b200_sync(self.h))
+
+    def reserve(self, max_nq: int, max_k: int):
+        self.check(self.lib.pion_v_b200_reserve(self.h, max_nq, max_k))
+
+    @property
+    def launches(self) -> int:
+        return int(self.lib.pion_v_b200_launch_count(self.h))
+
+    def timing(self, enable: bool):
+        """Record CUDA events around every scoring-kernel launch (benchmarks)."""
+        self.check(self.lib.pion_v_b200_timing_enable(self.h, int(enable)))
+
+    def timing_read(self):
+        """(total ms, launches) of the scoring kernels recorded since timing(True)."""
+        ms = ctypes.c_double()
+        n = ctypes.c_int64()
+        self.check(self.lib.pion_v_b200_timing_read(self.h, ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.pion_v_b200_shutdown(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _outputs(like_device: bool, nq: int, k: int, device=None):
+    if like_device:
+        ids = torch.empty((nq, k), dtype=torch.int32, device=device)
+        sc = torch.empty((nq, k), dtype=torch.float32, device=device)
+        return ids, sc, ids.data_ptr(), sc.data_ptr()
+    ids = np.empty((nq, k), np.int32)
+    sc = np.empty((nq, k), np.float32)
+    return ids, sc, ids.ctypes.data, sc.ctypes.data
+
+
+class _Index:
+    def __init__(self, ctx: Context, handle: ctypes.c_void_p, keep=None):
+        self.ctx = ctx
+        self.h = handle
+        self._keep = keep
+
+    @property
+    def n_rows(self) -> int:
+        return int(self.ctx.lib.pion_v_b200_index_rows(self.h))
+
+    def free(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.pion_v_b200_index_free(self.h)
+            self.h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class FlatI8Index(_Index):
+    """Device-resident FLAT INT8 index (rows int8[n, dim] + per-row fp32 scale)."""
+
+    def __init__(self, ctx: Context, rows, row_scale, id_base: int = 0, borrow: bool = False):
+        pr, mr, kr = _ptr(rows, np.int8, "rows")
+        ps, ms, ks = _ptr(row_scale, np.float32, "row_scale")
+        mem = _same_mem(mr, ms)
+        if borrow:
+            if mem != MEM_DEVICE:
+                raise ValueError("borrow needs device tensors")
+            mem = MEM_DEVICE_BORROW
+        n, dim = (rows.shape[0], rows.shape[1])
+        h = ctypes.c_void_p()
+        with _TorchStream(ctx, mem):
+            ctx.check(ctx.lib.pion_v_b200_register_flat_i8(ctx.h, pr, ps, n, dim, id_base, mem,
+                                                           ctypes.byref(h)))
+        super().__init__(ctx, h, (kr, ks) if borrow else None)
+        self.dim = dim
+
+    def search(self, q, q_scale, k: int):
+        """Top-k by (score desc, id asc) per query -> (ids int32[nq,k], scores f32[nq,k])."""
+        pq, mq, kq = _ptr(q, np.int8, "q")
+        ps, ms, ks = _ptr(q_scale, np.float32, "q_scale")
+        mem = _same_mem(mq, ms)
+        nq = q.shape[0]
+        ids, sc, pi, pv = _outputs(mem == MEM_DEVICE, nq, k,
+                                   q.device if mem == MEM_DEVICE else None)
+        with _TorchStream(self.ctx, mem):
+            self.ctx.check(self.ctx.lib.pion_v_b200_flat_i8_knn(self.ctx.h, self.h, pq, ps, nq,
+                                                                k, pi, pv, mem))
+        return ids, sc
+
+
+class FlatF32Index(_Index):
+    """Device-resident FLAT FP32 index for COSINE exact_knn."""
+
+    def __init__(self, ctx: Context, rows, id_base: int = 0, normalize: bool = True,
+                 borrow: bool = False):
+        pr, mem, kr = _ptr(rows, np.float32, "rows")
+        if borrow:
+            if mem != MEM_DEVICE or normalize:
+                raise ValueError("borrow needs device tensors that are already normalised")
+            mem = MEM_DEVICE_BORROW
+        h = ctypes.c_void_p()
+        with _TorchStream(ctx, mem):
+            ctx.check(ctx.lib.pion_v_b200_register_flat_f32(ctx.h, pr, rows.shape[0],
+                                                            rows.shape[1], id_base,
+                                                            int(normalize), mem,
+                                                            ctypes.byref(h)))
+        super().__init__(ctx, h, kr if borrow else None)
+        self.dim = rows.shape[1]
+
+    def search(self, q, k: int):
+        """k smallest `1 - cos` by (score asc, id asc) -> (ids, scores)."""
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        nq = q.shape[0]
+        ids, sc, pi, pv = _outputs(mem == MEM_DEVICE, nq, k,
+                                   q.device if mem == MEM_DEVICE else None)
+        with _TorchStream(self.ctx, mem):
+            self.ctx.check(self.ctx.lib.pion_v_b200_flat_f32_knn(self.ctx.h, self.h, pq, nq, k,
+                                                                 pi, pv, mem))
+        return ids, sc
+
+
+class BQIndex(_Index):
+    """Sign-bit codes + fp32 rows: Hamming shortlist, exact cosine rerank."""
+
+    def __init__(self, ctx: Context, rows, id_base: int = 0, normalize: bool = True):
+        pr, mem, kr = _ptr(rows, np.float32, "rows")
+        h = ctypes.c_void_p()
+        with _TorchStream(ctx, mem):
+            ctx.check(ctx.lib.pion_v_b200_register_bq(ctx.h, pr, rows.shape[0], rows.shape[1],
+                                                      id_base, int(normalize), mem,
+                                                      ctypes.byref(h)))
+        super().__init__(ctx, h)
+        self.dim = rows.shape[1]
+
+    def search(self, q, k: int, shortlist: int = 100):
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        nq = q.shape[0]
+        ids, sc, pi, pv = _outputs(mem == MEM_DEVICE, nq, k,
+                                   q.device if mem == MEM_DEVICE else None)
+        with _TorchStream(self.ctx, mem):
+            self.ctx.check(self.ctx.lib.pion_v_b200_bq_rerank_knn(self.ctx.h, self.h, pq, nq,
+                                                                  shortlist, k, pi, pv, mem))
+        return ids, sc
+
+
+# --------------------------------------------------------------- functions --
+
+def quantize_rows_i8(ctx: Context, src, d: int | None = None):
+    """pkm_quantize_rows_i8 on the GPU (src/vector/pkm_kernels.mojo:152-191)."""
+    ps, mem, ks = _ptr(src, np.float32, "src")
+    n, d_pad = src.shape
+    d = d_pad if d is None else d
+    if mem == MEM_DEVICE:
+        out = torch.empty((n, d_pad), dtype=torch.int8, device=src.device)
+        sc = torch.empty(n, dtype=torch.float32, device=src.device)
+        po, psc = out.data_ptr(), sc.data_ptr()
+    else:
+        out = np.empty((n, d_pad), np.int8)
+        sc = np.empty(n, np.float32)
+        po, psc = out.ctypes.data, sc.ctypes.data
+    with _TorchStream(ctx, mem):
+        ctx.check(ctx.lib.pion_v_b200_quantize_rows_i8(ctx.h, ps, n, d, d_pad, po, psc, mem))
+    return out, sc
+
+
+def l2_normalize_rows(ctx: Context, src):
+    """l2_normalize_fp32 of every row on the GPU (src/vector/kernels.mojo:318-357)."""
+    ps, mem, ks = _ptr(src, np.float32, "src")
+    n, dim = src.shape
+    if mem == MEM_DEVICE:
+        out = torch.empty_like(src)
+        po = out.data_ptr()
+    else:
+        out = np.empty((n, dim), np.float32)
+        po = out.ctypes.data
+    with _TorchStream(ctx, mem):
+        ctx.check(ctx.lib.pion_v_b200_l2_normalize_rows(ctx.h, ps, n, dim, po, mem))
+    return out
+
+
+def merge_topk(ctx: Context, cand_scores, cand_ids, k: int, descending: bool = True,
+               lists_major: bool = False):
+    """Merge sorted candidate lists into the k best per query: input [nq, n_lists, k],
+    or [n_lists, nq, k] with lists_major (an all-gather of per-shard results)."""
+    pv, mv, kv = _ptr(cand_scores, np.float32, "cand_scores")
+    pi, mi, ki = _ptr(cand_ids, np.int32, "cand_ids")
+    mem = _same_mem(mv, mi)
+    if lists_major:
+        n_lists, nq, kk = cand_scores.shape
+    else:
+        nq, n_lists, kk = cand_scores.shape
+    if kk != k:
+        raise ValueError("candidate lists must hold exactly k entries")
+    ids, sc, po_i, po_v = _outputs(mem == MEM_DEVICE, nq, k,
+                                   cand_scores.device if mem == MEM_DEVICE else None)
+    with _TorchStream(ctx, mem):
+        flags = (_lib.MERGE_DESC if descending else 0) | (_lib.MERGE_LISTS_MAJOR if lists_major
+                                                           else 0)
+        ctx.check(ctx.lib.pion_v_b200_merge_topk(ctx.h, pv, pi, nq, n_lists, k, flags, po_v,
+                                                 po_i, mem))
+    return ids, sc

@@ -1,0 +1,183 @@
+"""FLAT INT8 inner product on the GPU against the CPU oracle.
+
+Scores must be bit-identical to ref_pkm_scores_i8 (src/vector/reference/pkm_ref.mojo:
+47-61) and ids identical to the (score desc, id asc) order; the reference's own
+heap selection (ref_pkm_topk_max) may differ only among scores tied at the k-th
+place, which is checked too."""
+import os
+
+import numpy as np
+import pytest
+
+from pion_b200.workloads import mixture_np
+
+pytestmark = pytest.mark.gpu
+
+
+def quantized_case(oracle, n, dim, nq, seed, centres=64):
+    rows, qs = mixture_np(n, dim, centres, seed, nq)
+    keys, ks = oracle.pkm_quantize_rows_i8(rows)
+    q, qsc = oracle.pkm_quantize_rows_i8(qs)
+    return keys, ks, q, qsc
+
+
+def assert_matches_oracle(oracle, keys, ks, q, qsc, k, ids, sc):
+    n = keys.shape[0]
+    kk = min(k, n)
+    full = oracle.pkm_scores_i8(keys, ks, q, qsc)
+    ref_i, ref_v = oracle.flat_i8_knn(keys, ks, q, qsc, k)
+    for t in range(q.shape[0]):
+        order = np.lexsort((np.arange(n), -full[t]))[:kk]
+        assert ids[t, :kk].tolist() == order.tolist(), f"query {t}"
+        assert np.array_equal(sc[t, :kk].view(np.uint32), full[t][order].view(np.uint32))
+        assert (ids[t, kk:] == -1).all() and np.isneginf(sc[t, kk:]).all()
+        # the reference heap selects the same set unless scores tie at the k-th place
+        a, b = set(order.tolist()), set(ref_i[t, :kk].tolist())
+        if a != b:
+            kth = full[t][order[-1]]
+            assert all(full[t][i] == kth for i in a ^ b)
+        assert np.array_equal(np.sort(ref_v[t, :kk]), np.sort(sc[t, :kk]))
+
+
+@pytest.fixture
+def path_env():
+    old = os.environ.get("PION_B200_I8_PATH")
+    yield
+    if old is None:
+        os.environ.pop("PION_B200_I8_PATH", None)
+    else:
+        os.environ["PION_B200_I8_PATH"] = old
+
+
+def test_quantize_rows_bit_exact(ctx, oracle, rng):
+    import pion_b200
+    x = rng.standard_normal((3000, 1536)).astype(np.float32)
+    x[0] = 0.0
+    x[1, :4] = [1.0, -0.5, 0.25, 0.0]
+    x[1, 4:] = 0.0
+    x[2] *= 1e-30
+    x[3] *= 1e30
+    x[4] = np.float32(0.5) * np.sign(x[4])  # every element on a rounding boundary
+    for d in (1536, 1000):
+        a, s = pion_b200.quantize_rows_i8(ctx, x, d=d)
+        b, t = oracle.pkm_quantize_rows_i8(x, d=d)
+        assert np.array_equal(a, b)
+        assert np.array_equal(s.view(np.uint32), t.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,dim,nq,k,path", [
+    (20000, 1536, 1, 10, 0),
+    (20000, 1536, 1, 10, 2),
+    (20000, 1536, 3, 10, 1),
+    (20000, 1536, 128, 10, 0),
+    (20000, 1536, 300, 32, 0),
+    (5000, 448, 77, 64, 0),
+    (3000, 64, 5, 1, 0),
+    (777, 1536, 130, 16, 0),
+    (50, 1536, 2, 64, 0),
+    (50, 1536, 2, 64, 1),
+])
+def test_flat_i8_knn_matches_oracle(ctx, oracle, path_env, n, dim, nq, k, path):
+    import pion_b200
+    os.environ["PION_B200_I8_PATH"] = str(path)
+    keys, ks, q, qsc = quantized_case(oracle, n, dim, nq, seed=n + nq)
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    ids, sc = ix.search(q, qsc, k)
+    assert_matches_oracle(oracle, keys, ks, q, qsc, k, ids, sc)
+
+
+@pytest.mark.parametrize("path", [1, 2])
+def test_ties_break_by_ascending_id(ctx, oracle, path_env, path):
+    import pion_b200
+    os.environ["PION_B200_I8_PATH"] = str(path)
+    keys, ks, q, qsc = quantized_case(oracle, 4096, 256, 4, seed=5)
+    # plant duplicates of the rows nearest to each query at later ids
+    full = oracle.pkm_scores_i8(keys, ks, q, qsc)
+    for t in range(4):
+        best = int(np.argmax(full[t]))
+        for j in range(3):
+            keys[1000 + 700 * j + t] = keys[best]
+            ks[1000 + 700 * j + t] = ks[best]
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    ids, sc = ix.search(q, qsc, 8)
+    assert_matches_oracle(oracle, keys, ks, q, qsc, 8, ids, sc)
+
+
+def test_device_memory_path_equals_host(ctx, oracle):
+    import torch
+    import pion_b200
+    keys, ks, q, qsc = quantized_case(oracle, 10000, 1536, 200, seed=3)
+    ix_h = pion_b200.FlatI8Index(ctx, keys, ks)
+    ids_h, sc_h = ix_h.search(q, qsc, 10)
+    dk, dks = torch.from_numpy(keys).cuda(), torch.from_numpy(ks).cuda()
+    ix_d = pion_b200.FlatI8Index(ctx, dk, dks, id_base=5, borrow=True)
+    ids_d, sc_d = ix_d.search(torch.from_numpy(q).cuda(), torch.from_numpy(qsc).cuda(), 10)
+    torch.cuda.synchronize()
+    ctx.sync()
+    assert np.array_equal(ids_d.cpu().numpy(), ids_h + 5)
+    assert np.array_equal(sc_d.cpu().numpy(), sc_h)
+
+
+def test_empty_index_and_bad_shapes(ctx, oracle):
+    import pion_b200
+    keys = np.zeros((0, 1536), np.int8)
+    ix = pion_b200.FlatI8Index(ctx, keys, np.zeros(0, np.float32))
+    ids, sc = ix.search(np.zeros((2, 1536), np.int8), np.ones(2, np.float32), 4)
+    assert (ids == -1).all() and np.isneginf(sc).all()
+    keys, ks, q, qsc = quantized_case(oracle, 100, 64, 2, seed=9)
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    with pytest.raises(pion_b200.PionError) as e:
+        ix.search(q, qsc, 65)
+    assert e.value.code == -3
+    with pytest.raises(pion_b200.PionError):
+        pion_b200.FlatI8Index(ctx, np.zeros((10, 24), np.int8), np.ones(10, np.float32))
+
+
+def test_merge_topk_matches_numpy(ctx, rng):
+    import pion_b200
+    nq, L, k = 37, 19, 10
+    v = np.sort(rng.integers(0, 50, (nq, L, k)).astype(np.float32), axis=2)[:, :, ::-1].copy()
+    i = rng.integers(0, 10000, (nq, L, k)).astype(np.int32)
+    # lists must be ordered (score desc, id asc)
+    for a in range(nq):
+        for b in range(L):
+            o = np.lexsort((i[a, b], -v[a, b]))
+            v[a, b], i[a, b] = v[a, b][o], i[a, b][o]
+    ids, sc = pion_b200.merge_topk(ctx, v, i, k, descending=True)
+    for a in range(nq):
+        fv, fi = v[a].ravel(), i[a].ravel()
+        o = np.lexsort((fi, -fv))[:k]
+        assert ids[a].tolist() == fi[o].tolist() and sc[a].tolist() == fv[o].tolist()
+
+
+def test_full_size_one_million_rows(ctx, oracle):
+    """1M x 1536 (1024 centres), 1024 queries, k=10: tensor-core path vs the one-query
+    scan on 16 queries, and vs the oracle on 3 queries."""
+    import torch
+    import pion_b200
+    from pion_b200.workloads import mixture_torch
+    rows, qf = mixture_torch(1_000_000, 1536, 1024, seed=1, n_queries=1024)
+    keys, ks = pion_b200.quantize_rows_i8(ctx, rows)
+    q, qsc = pion_b200.quantize_rows_i8(ctx, qf)
+    del rows
+    ix = pion_b200.FlatI8Index(ctx, keys, ks, borrow=True)
+    try:
+        ids, sc = ix.search(q, qsc, 10)
+        os.environ["PION_B200_I8_PATH"] = "1"
+        ids1, sc1 = ix.search(q[:16].contiguous(), qsc[:16].contiguous(), 10)
+        torch.cuda.synchronize()
+        ctx.sync()
+    finally:
+        os.environ.pop("PION_B200_I8_PATH", None)
+    assert torch.equal(ids[:16], ids1) and torch.equal(sc[:16], sc1)
+    hk, hks = keys.cpu().numpy(), ks.cpu().numpy()
+    hq, hqs = q[:3].cpu().numpy(), qsc[:3].cpu().numpy()
+    oi, ov = oracle.flat_i8_knn(hk, hks, hq, hqs, 10)
+    got_i, got_v = ids[:3].cpu().numpy(), sc[:3].cpu().numpy()
+    for t in range(3):
+        assert np.array_equal(np.sort(ov[t]), np.sort(got_v[t]))
+        assert set(oi[t].tolist()) == set(got_i[t].tolist())
+    # sortedness and id validity over the whole batch
+    s = sc.cpu().numpy()
+    assert (np.diff(s, axis=1) <= 0).all()
+    assert ((ids >= 0) & (ids < 1_000_000)).all()
