@@ -153,6 +153,27 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx *ctx, const pion_b200_index *index, co
                             const float *q_scale, int64_t nq, int64_t k, int32_t *out_ids,
                             float *out_scores, int mem);
 
+/* FLAT INT8 inner-product KNN that allocates no device memory.  It has no
+ * counterpart in the reference.  It is for callers that cannot call cudaMalloc
+ * while serving a query: an engine whose device memory is all reserved by its own
+ * allocator, or a query thread that must not take cudaMalloc's device-wide
+ * synchronisation.  Same selection and ordering as pion_v_b200_flat_i8_knn, but
+ * every pointer is DEVICE memory and no index is registered (rows and row_scale are
+ * read in place).  Its scratch is one static 8 MiB device array per GPU that loads
+ * the library, held until the process exits; a call whose scratch (a 256-byte status
+ * word, 4 * ceil(n_rows / 256) bytes of tile maxima and 8 * nq * lists * k bytes of
+ * candidate lists, each part rounded up to 256; lists <= 64 for a batch, <= 4 * SMs
+ * for one query) exceeds it returns PION_B200_ESHAPE.  The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  All calls on a device share the array and
+ * it keeps the last call's contents, so calls that overlap on the GPU race.  Runs on
+ * `cuda_stream` (NULL: the legacy default stream) and returns once the results are
+ * written: 0, or the device-side status (PION_B200_ETIMEOUT). */
+int pion_v_b200_flat_i8_knn_static(const int8_t *rows, const float *row_scale, int64_t n_rows,
+                                   int64_t dim, const int8_t *q, const float *q_scale, int64_t nq,
+                                   int64_t k, int32_t *out_ids, float *out_scores,
+                                   void *cuda_stream);
+
 /* FLAT FP32 cosine: rows fp32[n_rows x dim].  With
  * `normalize` != 0 every row is unit-normalised on the GPU as
  * l2_normalize_fp32 does at COSINE ingest (src/vector/kernels.mojo:318-357). */

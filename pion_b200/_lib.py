@@ -57,6 +57,8 @@ SIGNATURES = {
                                      ctypes.POINTER(ctypes.c_int64)]),
     "pion_v_b200_register_flat_i8": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _PP]),
     "pion_v_b200_flat_i8_knn": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_flat_i8_knn_static": (_I, [_P, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P,
+                                            _P]),
     "pion_v_b200_register_flat_f32": (_I, [_P, _P, _I64, _I64, _I64, _I, _I, _PP]),
     "pion_v_b200_flat_f32_knn": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_register_bq": (_I, [_P, _P, _I64, _I64, _I64, _I, _I, _PP]),
