@@ -162,7 +162,7 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx *ctx, const pion_b200_index *index, co
  * read in place).  Its scratch is one static 8 MiB device array per GPU that loads
  * the library, held until the process exits; a call whose scratch (a 256-byte status
  * word, 4 * ceil(n_rows / 256) bytes of tile maxima and 8 * nq * lists * k bytes of
- * candidate lists, each part rounded up to 256; lists <= 64 for a batch, <= 4 * SMs
+ * candidate lists, each part rounded up to 256; lists <= 128 for a batch, <= 4 * SMs
  * for one query) exceeds it returns PION_B200_ESHAPE.  The first call on
  * a device looks up the array's device address (cudaGetSymbolAddress); make that
  * first call before any stream capture.  All calls on a device share the array and

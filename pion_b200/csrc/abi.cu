@@ -233,6 +233,9 @@ int pion_v_b200_timing_read(pion_b200_ctx* ctx, double* total_ms, int64_t* count
         return set_error(ctx, PION_B200_ECUDA, "timing_read: stream failed");
     double sum = 0.0;
     for (size_t i = 0; i < ctx->ev_used; ++i) {
+        // the events may sit on a stream other than the current one
+        if (cudaEventSynchronize(ctx->ev_end[i]) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "timing_read: event %zu", i);
         float ms = 0.0f;
         if (cudaEventElapsedTime(&ms, ctx->ev_start[i], ctx->ev_end[i]) != cudaSuccess)
             return set_error(ctx, PION_B200_ECUDA, "timing_read: event %zu", i);
@@ -356,6 +359,19 @@ static int forced_i8_path() {
     return e ? atoi(e) : 0;
 }
 
+// Index tiles scored by the threshold pre-pass (64 x 256 = 16384 rows).
+static constexpr int kPrepassTiles = 64;
+
+// The pre-pass runs for indexes of at least 8 x its sample; PION_B200_I8_PREPASS=0
+// turns it off and =1 forces it whenever the index is larger than the sample.
+static bool use_prepass(int n_tiles) {
+    const char* e = getenv("PION_B200_I8_PREPASS");
+    const int mode = e ? atoi(e) : -1;
+    if (mode == 0) return false;
+    if (mode == 1) return n_tiles > kPrepassTiles;
+    return n_tiles >= 8 * kPrepassTiles;
+}
+
 int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* q,
                             const float* q_scale, int64_t nq, int64_t k, int32_t* out_ids,
                             float* out_scores, int mem) {
@@ -431,24 +447,75 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
     } else if (ix->n_rows > 0) {
         const int n_qt = (nqi + fi8_query_tile() - 1) / fi8_query_tile();
         const int n_tiles = (int)((ix->n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
-        const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
-        const size_t ncand = (size_t)nq * splits * kk;
-        if (ensure(ctx->scratch, ncand * 8) != 0)
+        const int lps = fi8_lists_per_split(kk);
+        // Pre-pass over the first kPrepassTiles tiles: its k-th score per query is an
+        // exact lower bound of the final k-th score, handed to the main pass so that
+        // its integer pre-filter rejects almost every row from the start.
+        const bool pre = use_prepass(n_tiles);
+        const int main_begin = pre ? kPrepassTiles : 0;
+        const int splits = fi8_choose_splits(n_qt, n_tiles - main_begin, ctx->num_sms);
+        const int n_lists = splits * lps + (pre ? 1 : 0);
+        int pre_splits = pre ? ctx->num_sms / n_qt : 0;
+        if (pre) pre_splits = pre_splits < 1 ? 1 : (pre_splits > 16 ? 16 : pre_splits);
+        const int pre_lists = pre_splits * lps;
+        const size_t ncand = (size_t)nq * n_lists * kk;
+        const size_t npre = (size_t)nq * pre_lists * kk;
+        if (ensure(ctx->scratch, (ncand + npre) * 8) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn: scratch");
         float* cv = static_cast<float*>(ctx->scratch.ptr);
         int32_t* ci = reinterpret_cast<int32_t*>(cv + ncand);
+        float* pv = reinterpret_cast<float*>(ci + ncand);
+        int32_t* pi = reinterpret_cast<int32_t*>(pv + npre);
         CUtensorMap tmap_q;
         if (make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dq, (uint64_t)dim,
                          (uint64_t)nq, (uint64_t)dim, (uint32_t)fi8_k_block(),
                          (uint32_t)fi8_query_tile(), CU_TENSOR_MAP_SWIZZLE_128B) != 0)
             return set_error(ctx, PION_B200_ECUDA, "flat_i8_knn: query tensor map");
+        Fi8TcLaunch L;
+        L.tmap_q = &tmap_q;
+        L.tmap_rows = &ix->tmap_rows;
+        L.row_scale = ix->row_scale;
+        L.tile_rs_max = ix->tile_rs_max;
+        L.q_scale = dqs;
+        L.n_rows = ix->n_rows;
+        L.nq = nqi;
+        L.dim = dim;
+        L.k = kk;
+        L.status = ctx->d_status;
         timing_begin(ctx);
-        rc = launch_flat_i8_tc(tmap_q, ix->tmap_rows, ix->row_scale, ix->tile_rs_max, dqs,
-                               ix->n_rows, nqi, dim, kk, splits, cv, ci, ctx->d_status, st);
-        timing_end(ctx);
-        ctx->launches++;
+        if (pre) {
+            L.tile_begin = 0;
+            L.tile_end = kPrepassTiles;
+            L.n_splits = pre_splits;
+            L.n_lists = pre_lists;
+            L.cand_val = pv;
+            L.cand_idx = pi;
+            rc = launch_flat_i8_tc(L, st);
+            ctx->launches++;
+            if (rc == 0) {
+                // the sample's top-k becomes the last candidate list of every query
+                rc = launch_merge_lists(pv, pi, nqi, pre_lists, kk, 0, true,
+                                        cv + (size_t)(n_lists - 1) * kk,
+                                        ci + (size_t)(n_lists - 1) * kk, st, false,
+                                        n_lists * kk);
+                ctx->launches++;
+            }
+        }
         if (rc == 0) {
-            rc = launch_merge_lists(cv, ci, nqi, splits, kk, ix->id_base, true, dv, di, st);
+            L.tile_begin = main_begin;
+            L.tile_end = n_tiles;
+            L.n_splits = splits;
+            L.n_lists = n_lists;
+            L.cand_val = cv;
+            L.cand_idx = ci;
+            L.thr0 = pre ? cv + (size_t)(n_lists - 1) * kk + (kk - 1) : nullptr;
+            L.thr0_stride = n_lists * kk;
+            rc = launch_flat_i8_tc(L, st);
+            ctx->launches++;
+        }
+        timing_end(ctx);
+        if (rc == 0) {
+            rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, dv, di, st);
             ctx->launches++;
         }
     }

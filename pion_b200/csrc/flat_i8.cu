@@ -33,8 +33,7 @@ constexpr int UMMA_K = 32;          // int8 K consumed by one tcgen05.mma
 constexpr int A_BYTES = BM * BK;    // 16 KB
 constexpr int B_BYTES = BN * BK;    // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int EPI_THREADS = 128;
+// Threads: warp 0 TMA producer, warp 1 MMA issuer, then 4 or 8 epilogue warps.
 constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
 constexpr uint32_t IDESC = make_idesc_i8(BM, BN);
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
@@ -46,13 +45,18 @@ struct TcParams {
     const float* row_scale;    // [n_rows]
     const float* tile_rs_max;  // [n_tiles] max row_scale over each BN-row tile
     const float* q_scale;      // [nq]
+    const float* thr0;         // optional per-query lower bound on the final k-th score
+    int thr0_stride;           // elements between consecutive queries' bounds
     int64_t n_rows;
     int nq;
     int k;
-    int n_tiles;
+    int tile_begin;            // index tiles [tile_begin, tile_end) are scored
+    int tile_end;
     int n_splits;
     int kblocks;
-    float* cand_val;           // [nq][n_splits][k]
+    int n_lists;               // candidate lists per query in cand_* (layout [nq][n_lists][k])
+    int list_base;             // first list this launch writes
+    float* cand_val;
     int32_t* cand_idx;
     int* status;
 };
@@ -84,10 +88,58 @@ __device__ __forceinline__ int32_t dot_bound(float thr, float rs_max, float qs) 
     return (int32_t)d;
 }
 
+// Epilogue state of one query (one thread).
 template <int KCAP>
-__global__ void __launch_bounds__(THREADS, 1)
+struct QueryTop {
+    TopKDesc<KCAP> top;
+    float thr;        // admission threshold: max(current k-th score, lower bound - 1 ulp)
+    float floor_thr;  // the lower bound - 1 ulp (or -inf)
+    int32_t dmin;     // integer pre-filter for the current tile
+};
+
+// One 32-column chunk of TMEM accumulators: integer pre-filter into a candidate
+// mask, then the exact reference score for the (rare) candidates, ascending columns.
+template <int KCAP>
+__device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], int64_t col0, int64_t valid,
+                                           const float* __restrict__ row_scale, float qs,
+                                           float rs_max, int k, QueryTop<KCAP>& st) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] > st.dmin ? 1u : 0u) << j;
+    if (valid < 32) mask &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+#pragma unroll 1
+    while (mask) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        // Register select kept as PTX so the compiler cannot turn it into an
+        // indexed local-memory access to r[].
+        uint32_t sel = r[0];
+#pragma unroll
+        for (int jj = 1; jj < 32; ++jj)
+            asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\t"
+                "selp.b32 %0, %1, %0, p;\n\t}"
+                : "+r"(sel)
+                : "r"(r[jj]), "r"(j), "r"(jj));
+        const int32_t dv = (int32_t)sel;
+        if (dv <= st.dmin) continue;
+        const int64_t col = col0 + j;
+        const float s = i8_score(dv, __ldg(&row_scale[col]), qs);
+        if (s > st.thr) {
+            st.top.insert(s, (int32_t)col);
+            st.thr = fmaxf(st.top.kth(k), st.floor_thr);
+            st.dmin = dot_bound(st.thr, rs_max, qs);
+        }
+    }
+}
+
+template <int KCAP, int EPI_WARPS>
+__global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
     flat_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                       const __grid_constant__ CUtensorMap tmap_rows, TcParams p) {
+    constexpr int HALVES = EPI_WARPS / 4;        // column slices of one TMEM lane quarter
+    constexpr int COLS = BN / HALVES;            // columns per epilogue warp per tile
+    constexpr int CHUNKS = COLS / 32;
+    static_assert(CHUNKS % 2 == 0, "chunks are processed in pairs");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -105,8 +157,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int lane = threadIdx.x & 31;
     const int qt = blockIdx.x;
     const int split = blockIdx.y;
-    const int t_begin = (int)((int64_t)p.n_tiles * split / p.n_splits);
-    const int t_end = (int)((int64_t)p.n_tiles * (split + 1) / p.n_splits);
+    const int span = p.tile_end - p.tile_begin;
+    const int t_begin = p.tile_begin + (int)((int64_t)span * split / p.n_splits);
+    const int t_end = p.tile_begin + (int)((int64_t)span * (split + 1) / p.n_splits);
     const int my_tiles = t_end - t_begin;
 
     if (threadIdx.x == 0) {
@@ -116,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], EPI_THREADS);
+            mbar_init(&tempty[b], 32 * EPI_WARPS);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -205,14 +258,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // --------------------------------------------- epilogue: score + top-k
+        const int ew = warp - 2;
         const int lg = warp & 3;  // TMEM lane quarter this warp may read
+        const int half = ew >> 2; // column slice of each tile
         const int row = lg * 32 + lane;
         const int q = qt * BM + row;
         const bool q_ok = q < p.nq;
         const float qs = q_ok ? p.q_scale[q] : 0.0f;
-        TopKDesc<KCAP> top;
-        top.init();
-        float thr = -INFINITY;
+        QueryTop<KCAP> st;
+        st.top.init();
+        st.floor_thr = -INFINITY;
+        if (q_ok && p.thr0) {
+            const float t0 = p.thr0[(size_t)q * p.thr0_stride];
+            // rows scoring exactly the bound may still rank in the top k (ties break by id)
+            if (t0 > -INFINITY) st.floor_thr = nextafterf(t0, -INFINITY);
+        }
+        st.thr = st.floor_thr;
         for (int t = 0; t < my_tiles; ++t) {
             const int buf = t & 1;
             const uint32_t use = (uint32_t)(t >> 1);
@@ -222,59 +283,55 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const int tile = t_begin + t;
-            const int64_t col0 = (int64_t)tile * BN;
+            const int64_t col0 = (int64_t)tile * BN + half * COLS;
             const float rs_max = p.tile_rs_max[tile];
-            const int64_t valid = p.n_rows - col0;  // columns of this tile inside the index
-            int32_t dmin = q_ok ? dot_bound(thr, rs_max, qs) : INT32_MAX;
-            const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(buf * BN);
+            const int64_t valid = p.n_rows - col0;  // columns of this slice inside the index
+            st.dmin = q_ok ? dot_bound(st.thr, rs_max, qs) : INT32_MAX;
+            const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) +
+                                   (uint32_t)(buf * BN + half * COLS);
+            if constexpr (KCAP <= 32) {
+                uint32_t ra[32], rb[32];
+                tmem_ld32(taddr, ra);
+                tmem_ld_wait_regs(ra);
+                // Chunks in pairs: the load of the next chunk is in flight while the
+                // current one is scanned.
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(taddr + (uint32_t)(c * 32), r);
-                tmem_ld_wait();
-                // Cheap pass: one integer compare per column builds the candidate mask.
-                uint32_t mask = 0;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] > dmin ? 1u : 0u) << j;
-                if (valid < (int64_t)(c + 1) * 32) {
-                    const int64_t keep = valid - (int64_t)c * 32;
-                    mask &= keep <= 0 ? 0u : (keep >= 32 ? 0xffffffffu : ((1u << keep) - 1u));
+                for (int c = 0; c < CHUNKS; c += 2) {
+                    __syncwarp();
+                    tmem_ld32(taddr + (uint32_t)((c + 1) * 32), rb);
+                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, p.row_scale, qs, rs_max,
+                                     p.k, st);
+                    __syncwarp();
+                    tmem_ld_wait_regs(rb);
+                    if (c + 2 < CHUNKS) tmem_ld32(taddr + (uint32_t)((c + 2) * 32), ra);
+                    scan_chunk<KCAP>(rb, col0 + (c + 1) * 32, valid - (c + 1) * 32, p.row_scale,
+                                     qs, rs_max, p.k, st);
+                    __syncwarp();
+                    if (c + 2 < CHUNKS) tmem_ld_wait_regs(ra);
                 }
-                // Exact pass over the (rare) candidates, in ascending column order.
+            } else {
+                // a 64-entry list leaves no registers for a second chunk buffer
 #pragma unroll 1
-                while (mask) {
-                    const int j = __ffs(mask) - 1;
-                    mask &= mask - 1u;
-                    // Register select (kept as PTX so the compiler cannot turn it
-                    // into an indexed local-memory access to r[]).
-                    uint32_t sel = r[0];
-#pragma unroll
-                    for (int jj = 1; jj < 32; ++jj)
-                        asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\t"
-                            "selp.b32 %0, %1, %0, p;\n\t}"
-                            : "+r"(sel)
-                            : "r"(r[jj]), "r"(j), "r"(jj));
-                    const int32_t dv = (int32_t)sel;
-                    if (dv <= dmin) continue;
-                    const int64_t col = col0 + c * 32 + j;
-                    const float s = i8_score(dv, __ldg(&p.row_scale[col]), qs);
-                    if (s > thr) {
-                        top.insert(s, (int32_t)col);
-                        thr = top.kth(p.k);
-                        dmin = dot_bound(thr, rs_max, qs);
-                    }
+                for (int c = 0; c < CHUNKS; ++c) {
+                    uint32_t ra[32];
+                    __syncwarp();
+                    tmem_ld32(taddr + (uint32_t)(c * 32), ra);
+                    tmem_ld_wait_regs(ra);
+                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, p.row_scale, qs, rs_max,
+                                     p.k, st);
                 }
             }
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
         }
         if (q_ok) {
-            const size_t base = ((size_t)q * p.n_splits + split) * p.k;
+            const size_t base =
+                ((size_t)q * p.n_lists + p.list_base + (size_t)split * HALVES + half) * p.k;
 #pragma unroll
             for (int j = 0; j < KCAP; ++j)
                 if (j < p.k) {
-                    p.cand_val[base + j] = top.v[j];
-                    p.cand_idx[base + j] = top.i[j];
+                    p.cand_val[base + j] = st.top.v[j];
+                    p.cand_idx[base + j] = st.top.i[j];
                 }
         }
     }
@@ -424,7 +481,7 @@ template <bool DESC>
 __global__ void __launch_bounds__(MERGE_WARPS * 32)
     merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int nq,
                        int n_lists, int k, int64_t id_offset, float* out_v, int32_t* out_i,
-                       int lists_major) {
+                       int lists_major, int out_stride) {
     __shared__ uint16_t cursor[MERGE_WARPS][MERGE_MAX_LISTS];
     const int w = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -469,8 +526,8 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32)
         if (bl >= 0 && (bl % 32) == lane) cursor[w][bl] += 1;
         __syncwarp();
         if (lane == 0) {
-            out_v[(size_t)q * k + j] = bv;
-            out_i[(size_t)q * k + j] = bi >= 0 ? (int32_t)(bi + id_offset) : -1;
+            out_v[(size_t)q * out_stride + j] = bv;
+            out_i[(size_t)q * out_stride + j] = bi >= 0 ? (int32_t)(bi + id_offset) : -1;
         }
     }
 }
@@ -547,16 +604,17 @@ int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_
 
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
-                       cudaStream_t st, bool lists_major) {
+                       cudaStream_t st, bool lists_major, int out_stride) {
     if (nq <= 0) return 0;
     if (n_lists > MERGE_MAX_LISTS || k > 65535) return PION_B200_ESHAPE;
+    if (out_stride <= 0) out_stride = k;
     const int blocks = (nq + MERGE_WARPS - 1) / MERGE_WARPS;
     if (descending)
         merge_lists_kernel<true><<<blocks, MERGE_WARPS * 32, 0, st>>>(
-            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0);
+            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0, out_stride);
     else
         merge_lists_kernel<false><<<blocks, MERGE_WARPS * 32, 0, st>>>(
-            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0);
+            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0, out_stride);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
@@ -580,44 +638,58 @@ int fi8_choose_splits(int n_qt, int n_tiles, int num_sms) {
 
 int fi8_kcap(int k) { return k <= 16 ? 16 : (k <= 32 ? 32 : (k <= 64 ? 64 : 0)); }
 
-template <int KCAP>
+template <int KCAP, int EPI_WARPS>
 static int launch_tc_k(const CUtensorMap& tq, const CUtensorMap& tr, const fi8::TcParams& p,
                        int n_qt, cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
-        if (cudaFuncSetAttribute(fi8::flat_i8_tc_kernel<KCAP>,
+        if (cudaFuncSetAttribute(fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)fi8::SMEM_BYTES) != cudaSuccess)
             return PION_B200_ECUDA;
         configured = true;
     }
     dim3 grid(n_qt, p.n_splits);
-    fi8::flat_i8_tc_kernel<KCAP><<<grid, fi8::THREADS, fi8::SMEM_BYTES, st>>>(tq, tr, p);
+    fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>
+        <<<grid, 64 + 32 * EPI_WARPS, fi8::SMEM_BYTES, st>>>(tq, tr, p);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
-int launch_flat_i8_tc(const CUtensorMap& tmap_q, const CUtensorMap& tmap_rows,
-                      const float* row_scale, const float* tile_rs_max, const float* q_scale,
-                      int64_t n_rows, int nq, int dim, int k, int n_splits, float* cand_val,
-                      int32_t* cand_idx, int* status, cudaStream_t st) {
+// Epilogue warps per CTA: 8 (two per TMEM lane quarter, each taking half of the
+// columns) for a 16-entry register top-k, else 4 (the 320-thread block caps a
+// thread at 168 registers).
+static int fi8_epi_warps(int k) { return k <= 16 ? 8 : 4; }
+
+int fi8_lists_per_split(int k) { return fi8_epi_warps(k) / 4; }
+
+int launch_flat_i8_tc(const Fi8TcLaunch& L, cudaStream_t st) {
     fi8::TcParams p;
-    p.row_scale = row_scale;
-    p.tile_rs_max = tile_rs_max;
-    p.q_scale = q_scale;
-    p.n_rows = n_rows;
-    p.nq = nq;
-    p.k = k;
-    p.n_tiles = (int)((n_rows + fi8::BN - 1) / fi8::BN);
-    p.n_splits = n_splits;
-    p.kblocks = (dim + fi8::BK - 1) / fi8::BK;
-    p.cand_val = cand_val;
-    p.cand_idx = cand_idx;
-    p.status = status;
-    const int n_qt = (nq + fi8::BM - 1) / fi8::BM;
-    switch (fi8_kcap(k)) {
-        case 16: return launch_tc_k<16>(tmap_q, tmap_rows, p, n_qt, st);
-        case 32: return launch_tc_k<32>(tmap_q, tmap_rows, p, n_qt, st);
-        case 64: return launch_tc_k<64>(tmap_q, tmap_rows, p, n_qt, st);
+    p.row_scale = L.row_scale;
+    p.tile_rs_max = L.tile_rs_max;
+    p.q_scale = L.q_scale;
+    p.thr0 = L.thr0;
+    p.thr0_stride = L.thr0_stride;
+    p.n_rows = L.n_rows;
+    p.nq = L.nq;
+    p.k = L.k;
+    p.tile_begin = L.tile_begin;
+    p.tile_end = L.tile_end;
+    p.n_splits = L.n_splits;
+    p.kblocks = (L.dim + fi8::BK - 1) / fi8::BK;
+    p.n_lists = L.n_lists;
+    p.list_base = L.list_base;
+    p.cand_val = L.cand_val;
+    p.cand_idx = L.cand_idx;
+    p.status = L.status;
+    if (p.tile_end <= p.tile_begin || p.n_splits < 1) return PION_B200_ESHAPE;
+    if (p.list_base + p.n_splits * fi8_lists_per_split(p.k) > p.n_lists) return PION_B200_ESHAPE;
+    const int n_qt = (L.nq + fi8::BM - 1) / fi8::BM;
+    const int ew = fi8_epi_warps(L.k);
+    switch (fi8_kcap(L.k)) {
+        case 16: return ew == 8 ? launch_tc_k<16, 8>(*L.tmap_q, *L.tmap_rows, p, n_qt, st)
+                                : PION_B200_ESHAPE;
+        case 32: return launch_tc_k<32, 4>(*L.tmap_q, *L.tmap_rows, p, n_qt, st);
+        case 64: return launch_tc_k<64, 4>(*L.tmap_q, *L.tmap_rows, p, n_qt, st);
         default: return PION_B200_ESHAPE;
     }
 }

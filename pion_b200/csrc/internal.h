@@ -85,14 +85,39 @@ int launch_quantize_rows_i8(const float* src, int64_t n_rows, int d, int d_pad, 
 int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st);
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
-                       cudaStream_t st, bool lists_major = false);
+                       cudaStream_t st, bool lists_major = false, int out_stride = 0);
 // Event pair around one scoring-kernel launch when timing is enabled.
 void timing_begin(pion_b200_ctx* ctx);
 void timing_end(pion_b200_ctx* ctx);
-int launch_flat_i8_tc(const CUtensorMap& tmap_q, const CUtensorMap& tmap_rows,
-                      const float* row_scale, const float* tile_rs_max, const float* q_scale,
-                      int64_t n_rows, int nq, int dim, int k, int n_splits, float* cand_val,
-                      int32_t* cand_idx, int* status, cudaStream_t st);
+// One launch of the tensor-core FLAT INT8 kernel over index tiles [tile_begin,
+// tile_end) (tiles of fi8_tile_rows() rows).  Each (query, split) writes
+// fi8_lists_per_split(k) sorted lists of k (score, id) pairs at list
+// list_base + split * lists_per_split + slice of the [nq][n_lists][k] layout.
+// `thr0` (optional) points at a per-query lower bound of the final k-th score,
+// `thr0_stride` elements apart.
+struct Fi8TcLaunch {
+    const CUtensorMap* tmap_q = nullptr;
+    const CUtensorMap* tmap_rows = nullptr;
+    const float* row_scale = nullptr;
+    const float* tile_rs_max = nullptr;
+    const float* q_scale = nullptr;
+    const float* thr0 = nullptr;
+    int thr0_stride = 0;
+    int64_t n_rows = 0;
+    int nq = 0;
+    int dim = 0;
+    int k = 0;
+    int tile_begin = 0;
+    int tile_end = 0;
+    int n_splits = 1;
+    int n_lists = 1;
+    int list_base = 0;
+    float* cand_val = nullptr;
+    int32_t* cand_idx = nullptr;
+    int* status = nullptr;
+};
+int fi8_lists_per_split(int k);
+int launch_flat_i8_tc(const Fi8TcLaunch& launch, cudaStream_t st);
 int launch_flat_i8_scan1(const int8_t* rows, const float* row_scale, int64_t n_rows, int dim,
                          const int8_t* q, const float* q_scale, int k, int ctas, float* cand_val,
                          int32_t* cand_idx, cudaStream_t st);

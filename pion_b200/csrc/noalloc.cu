@@ -90,11 +90,15 @@ extern "C" int pion_v_b200_flat_i8_knn_static(const int8_t* rows, const float* r
     const int nqi = (int)nq;
     const int n_tiles = (int)((n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
     const bool scan = (nq == 1);
-    int lists = 1;
+    int lists = 1, splits = 1;
     if (n_rows > 0) {
-        lists = scan ? fi8_scan1_ctas(n_rows, num_sms)
-                     : fi8_choose_splits((nqi + fi8_query_tile() - 1) / fi8_query_tile(),
-                                         n_tiles, num_sms);
+        if (scan) {
+            lists = fi8_scan1_ctas(n_rows, num_sms);
+        } else {
+            splits = fi8_choose_splits((nqi + fi8_query_tile() - 1) / fi8_query_tile(), n_tiles,
+                                       num_sms);
+            lists = splits * fi8_lists_per_split(kk);
+        }
     }
     const size_t status_bytes = 256;
     const size_t tiles_bytes = round256((size_t)(n_tiles > 0 ? n_tiles : 1) * sizeof(float));
@@ -132,9 +136,26 @@ extern "C" int pion_v_b200_flat_i8_knn_static(const int8_t* rows, const float* r
                          (uint32_t)fi8_tile_rows(), CU_TENSOR_MAP_SWIZZLE_128B) != 0)
             return PION_B200_ECUDA;
         rc = launch_tile_max(row_scale, n_rows, tile_max, st);
-        if (rc == 0)
-            rc = launch_flat_i8_tc(tmap_q, tmap_rows, row_scale, tile_max, q_scale, n_rows, nqi,
-                                   (int)dim, kk, lists, cv, ci, status, st);
+        if (rc == 0) {
+            Fi8TcLaunch L;
+            L.tmap_q = &tmap_q;
+            L.tmap_rows = &tmap_rows;
+            L.row_scale = row_scale;
+            L.tile_rs_max = tile_max;
+            L.q_scale = q_scale;
+            L.n_rows = n_rows;
+            L.nq = nqi;
+            L.dim = (int)dim;
+            L.k = kk;
+            L.tile_begin = 0;
+            L.tile_end = n_tiles;
+            L.n_splits = splits;
+            L.n_lists = lists;
+            L.cand_val = cv;
+            L.cand_idx = ci;
+            L.status = status;
+            rc = launch_flat_i8_tc(L, st);
+        }
         if (rc == 0)
             rc = launch_merge_lists(cv, ci, nqi, lists, kk, 0, true, out_scores, out_ids, st);
     }

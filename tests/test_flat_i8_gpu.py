@@ -76,6 +76,8 @@ def test_quantize_rows_bit_exact(ctx, oracle, rng):
     (777, 1536, 130, 16, 0),
     (50, 1536, 2, 64, 0),
     (50, 1536, 2, 64, 1),
+    (200000, 1536, 16, 10, 0),   # threshold pre-pass active
+    (200000, 1536, 16, 64, 0),
 ])
 def test_flat_i8_knn_matches_oracle(ctx, oracle, path_env, n, dim, nq, k, path):
     import pion_b200
@@ -83,6 +85,20 @@ def test_flat_i8_knn_matches_oracle(ctx, oracle, path_env, n, dim, nq, k, path):
     keys, ks, q, qsc = quantized_case(oracle, n, dim, nq, seed=n + nq)
     ix = pion_b200.FlatI8Index(ctx, keys, ks)
     ids, sc = ix.search(q, qsc, k)
+    assert_matches_oracle(oracle, keys, ks, q, qsc, k, ids, sc)
+
+
+@pytest.mark.parametrize("k", [1, 10, 32])
+def test_forced_prepass_on_small_index(ctx, oracle, k):
+    """The pre-pass (first 64 tiles) + main pass over the rest, on 79 tiles."""
+    import pion_b200
+    keys, ks, q, qsc = quantized_case(oracle, 20000, 1536, 300, seed=17)
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    os.environ["PION_B200_I8_PREPASS"] = "1"
+    try:
+        ids, sc = ix.search(q, qsc, k)
+    finally:
+        os.environ.pop("PION_B200_I8_PREPASS", None)
     assert_matches_oracle(oracle, keys, ks, q, qsc, k, ids, sc)
 
 
