@@ -373,10 +373,13 @@ def run_ours(a, wl):
         if batch > 1:
             ops = 2.0 * dim * rows_local * batch
             achieved = ops / (kern_avg_ms / 1000.0) / 1e12
-            peak = 2.0 * peaks["bf16_tflops"]
+            # the scoring kernel runs back to back for the whole timed region (hundreds of
+            # ms under the 1 kW power cap), so the sustained figure is the denominator
+            peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
             roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak,
-                    "peak_source": f"2 x {peak_kind} dense bf16 burst (int8 rate = 2 x bf16 "
+                    "frac_of_burst": achieved / (2.0 * peaks["bf16_tflops"]),
+                    "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate = 2 x bf16 "
                                    f"on B200); int8 tera-ops counted as TFLOP",
                     "algorithmic_per_launch": ops,
                     "kernel_ms": kern_avg_ms,

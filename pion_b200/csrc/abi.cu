@@ -359,17 +359,23 @@ static int forced_i8_path() {
     return e ? atoi(e) : 0;
 }
 
-// Index tiles scored by the threshold pre-pass (64 x 256 = 16384 rows).
-static constexpr int kPrepassTiles = 64;
+// Index tiles scored by the threshold pre-pass: 8 tiles (2048 rows) per result
+// slot, at least 64 tiles (16384 rows) -- enough that the sample's k-th score is
+// close to the final one on clustered data, where a query's neighbours are a small
+// fraction of the rows.
+static int prepass_tiles(int k) { return k * 8 > 64 ? k * 8 : 64; }
+
+// Unbounded seed of the pre-pass (tiles of 256 rows).
+static constexpr int kSeedTiles = 8;
 
 // The pre-pass runs for indexes of at least 8 x its sample; PION_B200_I8_PREPASS=0
 // turns it off and =1 forces it whenever the index is larger than the sample.
-static bool use_prepass(int n_tiles) {
+static bool use_prepass(int n_tiles, int k) {
     const char* e = getenv("PION_B200_I8_PREPASS");
     const int mode = e ? atoi(e) : -1;
     if (mode == 0) return false;
-    if (mode == 1) return n_tiles > kPrepassTiles;
-    return n_tiles >= 8 * kPrepassTiles;
+    if (mode == 1) return n_tiles > prepass_tiles(k);
+    return n_tiles >= 8 * prepass_tiles(k);
 }
 
 int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* q,
@@ -448,24 +454,36 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         const int n_qt = (nqi + fi8_query_tile() - 1) / fi8_query_tile();
         const int n_tiles = (int)((ix->n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
         const int lps = fi8_lists_per_split(kk);
-        // Pre-pass over the first kPrepassTiles tiles: its k-th score per query is an
-        // exact lower bound of the final k-th score, handed to the main pass so that
-        // its integer pre-filter rejects almost every row from the start.
-        const bool pre = use_prepass(n_tiles);
-        const int main_begin = pre ? kPrepassTiles : 0;
+        // Threshold pre-pass over a sample of the first tiles, in two stages: a seed
+        // of kSeedTiles scored without a bound, then the rest of the sample with the
+        // seed's k-th score as bound.  The sample's k-th score per query is an exact
+        // lower bound of the final k-th score, handed to the main pass so that its
+        // integer pre-filter rejects almost every row from the start.
+        const bool pre = use_prepass(n_tiles, kk);
+        const int pre_tiles = pre ? prepass_tiles(kk) : 0;
+        const int main_begin = pre_tiles;
         const int splits = fi8_choose_splits(n_qt, n_tiles - main_begin, ctx->num_sms);
         const int n_lists = splits * lps + (pre ? 1 : 0);
-        int pre_splits = pre ? ctx->num_sms / n_qt : 0;
-        if (pre) pre_splits = pre_splits < 1 ? 1 : (pre_splits > 16 ? 16 : pre_splits);
-        const int pre_lists = pre_splits * lps;
+        // seed stage: one tile per CTA; sample stage: about one wave of CTAs
+        const int seed_splits = pre ? kSeedTiles : 0;
+        int samp_splits = pre ? ctx->num_sms / n_qt : 0;
+        if (pre) {
+            const int cap = (pre_tiles - kSeedTiles) / 2;
+            samp_splits = samp_splits < 1 ? 1 : (samp_splits > cap ? cap : samp_splits);
+        }
+        const int seed_lists = seed_splits * lps;
+        const int samp_lists = samp_splits * lps + 1;  // + the seed's merged list
         const size_t ncand = (size_t)nq * n_lists * kk;
-        const size_t npre = (size_t)nq * pre_lists * kk;
-        if (ensure(ctx->scratch, (ncand + npre) * 8) != 0)
+        const size_t nseed = (size_t)nq * seed_lists * kk;
+        const size_t nsamp = (size_t)nq * samp_lists * kk;
+        if (ensure(ctx->scratch, (ncand + nseed + nsamp) * 8) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn: scratch");
         float* cv = static_cast<float*>(ctx->scratch.ptr);
         int32_t* ci = reinterpret_cast<int32_t*>(cv + ncand);
-        float* pv = reinterpret_cast<float*>(ci + ncand);
-        int32_t* pi = reinterpret_cast<int32_t*>(pv + npre);
+        float* sv = reinterpret_cast<float*>(ci + ncand);
+        int32_t* si = reinterpret_cast<int32_t*>(sv + nseed);
+        float* pv = reinterpret_cast<float*>(si + nseed);
+        int32_t* pi = reinterpret_cast<int32_t*>(pv + nsamp);
         CUtensorMap tmap_q;
         if (make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dq, (uint64_t)dim,
                          (uint64_t)nq, (uint64_t)dim, (uint32_t)fi8_k_block(),
@@ -484,17 +502,36 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         L.status = ctx->d_status;
         timing_begin(ctx);
         if (pre) {
+            // seed: tiles [0, kSeedTiles), no bound
             L.tile_begin = 0;
-            L.tile_end = kPrepassTiles;
-            L.n_splits = pre_splits;
-            L.n_lists = pre_lists;
-            L.cand_val = pv;
-            L.cand_idx = pi;
+            L.tile_end = kSeedTiles;
+            L.n_splits = seed_splits;
+            L.n_lists = seed_lists;
+            L.cand_val = sv;
+            L.cand_idx = si;
+            L.thr0 = nullptr;
             rc = launch_flat_i8_tc(L, st);
             ctx->launches++;
-            if (rc == 0) {
-                // the sample's top-k becomes the last candidate list of every query
-                rc = launch_merge_lists(pv, pi, nqi, pre_lists, kk, 0, true,
+            const size_t seed_slot = (size_t)(samp_lists - 1) * kk;
+            if (rc == 0) {  // the seed's top-k becomes the sample stage's last list
+                rc = launch_merge_lists(sv, si, nqi, seed_lists, kk, 0, true, pv + seed_slot,
+                                        pi + seed_slot, st, false, samp_lists * kk);
+                ctx->launches++;
+            }
+            if (rc == 0) {  // rest of the sample, bounded by the seed
+                L.tile_begin = kSeedTiles;
+                L.tile_end = pre_tiles;
+                L.n_splits = samp_splits;
+                L.n_lists = samp_lists;
+                L.cand_val = pv;
+                L.cand_idx = pi;
+                L.thr0 = pv + seed_slot + (kk - 1);
+                L.thr0_stride = samp_lists * kk;
+                rc = launch_flat_i8_tc(L, st);
+                ctx->launches++;
+            }
+            if (rc == 0) {  // the sample's top-k becomes the main pass's last list
+                rc = launch_merge_lists(pv, pi, nqi, samp_lists, kk, 0, true,
                                         cv + (size_t)(n_lists - 1) * kk,
                                         ci + (size_t)(n_lists - 1) * kk, st, false,
                                         n_lists * kk);

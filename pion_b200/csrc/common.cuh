@@ -228,9 +228,21 @@ __host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n) {
 }
 
 // ------------------------------------------------------- top-k in registers --
+// PTX select: the compiler cannot fold a chain of these back into an indexed
+// access, which would move the whole register array to local memory.
+__device__ __forceinline__ uint32_t selp_u32(uint32_t a, uint32_t b, bool take_a) {
+    uint32_t r;
+    asm("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %3, 0;\n\tselp.b32 %0, %1, %2, p;\n\t}"
+        : "=r"(r)
+        : "r"(a), "r"(b), "r"((uint32_t)take_a));
+    return r;
+}
+
 // A sorted (descending) list of KCAP (score, id) pairs kept in registers.  Scans
-// present ids in ascending order, so the strict `>` keeps the earlier id in front
-// of an equal later score: the list is ordered by (score desc, id asc).
+// present ids in ascending order, so the list is ordered by (score desc, id asc).
+// Insertion is low-latency: every entry is compared with the new pair at once
+// (the entries ahead of it form a prefix), then every slot picks its new value
+// independently, instead of a KCAP-long chain of dependent compare-swaps.
 template <int KCAP>
 struct TopKDesc {
     float v[KCAP];
@@ -243,30 +255,40 @@ struct TopKDesc {
         }
     }
     __device__ __forceinline__ void insert(float s, int32_t id) {
+        bool ahead[KCAP];
+#pragma unroll
+        for (int j = 0; j < KCAP; ++j)
+            ahead[j] = v[j] > s || (v[j] == s && i[j] >= 0 && (id < 0 || i[j] < id));
+        float nv[KCAP];
+        int32_t ni[KCAP];
 #pragma unroll
         for (int j = 0; j < KCAP; ++j) {
-            bool take = s > v[j] || (s == v[j] && id >= 0 && (i[j] < 0 || id < i[j]));
-            float tv = take ? v[j] : s;
-            int32_t ti = take ? i[j] : id;
-            v[j] = take ? s : v[j];
-            i[j] = take ? id : i[j];
-            s = tv;
-            id = ti;
+            const bool at = !ahead[j] && (j == 0 || ahead[j - 1]);
+            const float prev_v = j == 0 ? s : v[j - 1];
+            const int32_t prev_i = j == 0 ? id : i[j - 1];
+            nv[j] = ahead[j] ? v[j] : (at ? s : prev_v);
+            ni[j] = ahead[j] ? i[j] : (at ? id : prev_i);
+        }
+#pragma unroll
+        for (int j = 0; j < KCAP; ++j) {
+            v[j] = nv[j];
+            i[j] = ni[j];
         }
     }
-    // The k-th best score (k <= KCAP), without dynamic register indexing.
+    // The k-th best score (1 <= k <= KCAP) by a log-depth select tree over the bits
+    // of k - 1.
     __device__ __forceinline__ float kth(int k) const {
-        // Register selects in PTX: a C++ select chain gets folded back into an
-        // indexed access, which would move the whole list to local memory.
-        uint32_t t = __float_as_uint(v[0]);
-        const int want = k - 1;
+        uint32_t t[KCAP];
 #pragma unroll
-        for (int j = 1; j < KCAP; ++j)
-            asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\t"
-                "selp.b32 %0, %1, %0, p;\n\t}"
-                : "+r"(t)
-                : "r"(__float_as_uint(v[j])), "r"(want), "r"(j));
-        return __uint_as_float(t);
+        for (int j = 0; j < KCAP; ++j) t[j] = __float_as_uint(v[j]);
+        const uint32_t want = (uint32_t)(k - 1);
+#pragma unroll
+        for (int w = KCAP / 2, b = 0; w >= 1; w /= 2, ++b) {
+            const bool hi = (want >> b) & 1u;
+#pragma unroll
+            for (int j = 0; j < w; ++j) t[j] = selp_u32(t[2 * j + 1], t[2 * j], hi);
+        }
+        return __uint_as_float(t[0]);
     }
 };
 

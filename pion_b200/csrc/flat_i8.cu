@@ -36,7 +36,12 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 // Threads: warp 0 TMA producer, warp 1 MMA issuer, then 4 or 8 epilogue warps.
 constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
 constexpr uint32_t IDESC = make_idesc_i8(BM, BN);
-constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+constexpr size_t SMEM_PIPE_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+// per epilogue warp: one 32 x 32 chunk of dots and the 32 row scales of its columns
+constexpr size_t STASH_BYTES = 32 * 32 * 4 + 32 * 4;
+__host__ __device__ constexpr size_t smem_bytes(int epi_warps) {
+    return SMEM_PIPE_BYTES + (size_t)epi_warps * STASH_BYTES;
+}
 
 static_assert(BN <= 256 && BN % 16 == 0, "UMMA N");
 static_assert(BK % UMMA_K == 0, "K step");
@@ -66,26 +71,28 @@ __device__ __forceinline__ float i8_score(int32_t d, float rs, float qs) {
     return __fmul_rn(__fmul_rn(__int2float_rn(d), rs), qs);
 }
 
-// Largest integer d such that every dot <= d scores <= thr in a tile whose row
-// scales are all <= rs_max (fl(x*y) is monotone in each non-negative factor).
-// Returns INT32_MIN when no such integer bound applies (thr < 0 or -inf), so the
-// caller scores every element exactly.
-__device__ __forceinline__ int32_t dot_bound(float thr, float rs_max, float qs) {
+// Integer pre-filter: an integer d such that every dot <= d scores <= thr in a tile
+// whose row scales are all <= rs_max, given inv = fl(1 / fl(rs_max * qs)).
+// fl(x*y) is monotone in each non-negative factor, so score(d) <= fl(fl(fl(d) *
+// rs_max) * qs) <= d * rs_max * qs * (1 + 2^-24)^3.  est = fl(thr * inv) exceeds
+// thr / (rs_max * qs) by at most (1 + 2^-24)^3; shrinking it by 2^-20 and taking two
+// off its floor leaves d < thr / (rs_max * qs) * (1 - 5.9e-7), so score(d) < thr.
+// Returns INT32_MIN (score everything exactly) when thr < 0 or nothing is finite.
+__device__ __forceinline__ int32_t dot_bound(float thr, float inv) {
     if (!(thr >= 0.0f)) return INT32_MIN;
-    const double prod = (double)rs_max * (double)qs;
-    if (!(prod > 0.0)) return INT32_MAX;
-    double est = (double)thr / prod;
-    if (est > 2.0e9) return INT32_MAX;
-    // Start below the real-arithmetic solution by more than the rounding of the
-    // three float operations, then tighten upward with the exact formula.
-    int64_t d = (int64_t)floor(est * (1.0 - 1.0e-6)) - 2;
-    if (d < 0) d = 0;
-#pragma unroll 1
-    for (int it = 0; it < 64 && d < INT32_MAX; ++it) {
-        if (i8_score((int32_t)(d + 1), rs_max, qs) <= thr) ++d;
-        else break;
-    }
-    return (int32_t)d;
+    float est = __fmul_rz(thr, inv);
+    est = __fmul_rz(est, 1.0f - 0x1p-20f);
+    if (!(est < 2.0e9f)) return INT32_MIN;
+    return __float2int_rz(est) - 2;
+}
+
+// rsv[c] for a loop-variant c without indexing the register array dynamically.
+template <int N>
+__device__ __forceinline__ float sel_rs(const float (&rsv)[N], int c) {
+    float v = rsv[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i) v = (c == i) ? rsv[i] : v;
+    return v;
 }
 
 // Epilogue state of one query (one thread).
@@ -99,37 +106,44 @@ struct QueryTop {
 
 // One 32-column chunk of TMEM accumulators: integer pre-filter into a candidate
 // mask, then the exact reference score for the (rare) candidates, ascending columns.
+// When any lane of the warp has a candidate, the warp parks the chunk in its shared
+// `stash` (column-major [32][32], conflict-free) so that candidates are read by index
+// instead of selected out of registers.
 template <int KCAP>
 __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], int64_t col0, int64_t valid,
-                                           const float* __restrict__ row_scale, float qs,
-                                           float rs_max, int k, QueryTop<KCAP>& st) {
-    uint32_t mask = 0;
+                                           float rs_lane, float qs, float inv, int k,
+                                           uint32_t* stash, float* stash_rs, int lane,
+                                           QueryTop<KCAP>& st) {
+    // Common case first: one max-reduction says whether any column can qualify.
+    int32_t mx = (int32_t)r[0];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] > st.dmin ? 1u : 0u) << j;
-    if (valid < 32) mask &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+    for (int j = 1; j < 32; ++j) mx = max(mx, (int32_t)r[j]);
+    uint32_t mask = 0;
+    if (mx > st.dmin) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] > st.dmin ? 1u : 0u) << j;
+        if (valid < 32) mask &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+    }
+    if (!__any_sync(0xffffffffu, mask != 0u)) return;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stash[j * 32 + lane] = r[j];
+    stash_rs[lane] = rs_lane;  // lane j brought the row scale of column j
+    __syncwarp();
 #pragma unroll 1
     while (mask) {
         const int j = __ffs(mask) - 1;
         mask &= mask - 1u;
-        // Register select kept as PTX so the compiler cannot turn it into an
-        // indexed local-memory access to r[].
-        uint32_t sel = r[0];
-#pragma unroll
-        for (int jj = 1; jj < 32; ++jj)
-            asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\t"
-                "selp.b32 %0, %1, %0, p;\n\t}"
-                : "+r"(sel)
-                : "r"(r[jj]), "r"(j), "r"(jj));
-        const int32_t dv = (int32_t)sel;
+        const int32_t dv = (int32_t)stash[j * 32 + lane];
         if (dv <= st.dmin) continue;
         const int64_t col = col0 + j;
-        const float s = i8_score(dv, __ldg(&row_scale[col]), qs);
+        const float s = i8_score(dv, stash_rs[j], qs);
         if (s > st.thr) {
             st.top.insert(s, (int32_t)col);
             st.thr = fmaxf(st.top.kth(k), st.floor_thr);
-            st.dmin = dot_bound(st.thr, rs_max, qs);
+            st.dmin = dot_bound(st.thr, inv);
         }
     }
+    __syncwarp();  // the stash is rewritten by the next chunk
 }
 
 template <int KCAP, int EPI_WARPS>
@@ -152,6 +166,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint32_t* stash_all = reinterpret_cast<uint32_t*>(smem + (SMEM_PIPE_BYTES - 1024));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -259,6 +274,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
     } else {
         // --------------------------------------------- epilogue: score + top-k
         const int ew = warp - 2;
+        uint32_t* stash = stash_all + ew * (STASH_BYTES / 4);
+        float* stash_rs = reinterpret_cast<float*>(stash + 32 * 32);
         const int lg = warp & 3;  // TMEM lane quarter this warp may read
         const int half = ew >> 2; // column slice of each tile
         const int row = lg * 32 + lane;
@@ -277,16 +294,23 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
         for (int t = 0; t < my_tiles; ++t) {
             const int buf = t & 1;
             const uint32_t use = (uint32_t)(t >> 1);
+            const int tile = t_begin + t;
+            const int64_t col0 = (int64_t)tile * BN + half * COLS;
+            const int64_t valid = p.n_rows - col0;  // columns of this slice inside the index
+            // Row scales of this slice (lane j of chunk c: column c*32 + j) and the tile
+            // maximum, loaded before the wait so that their latency hides behind it.
+            float rsv[CHUNKS];
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c)
+                rsv[c] = (c * 32 + lane < valid) ? __ldg(&p.row_scale[col0 + c * 32 + lane]) : 0.f;
+            const float rs_max = __ldg(&p.tile_rs_max[tile]);
             // Every lane waits; the warp proceeds only if all of them saw the phase,
             // so the warp-collective TMEM loads below stay convergent.
             const bool got = mbar_wait(&tfull[buf], use & 1u, p.status, abort_flag);
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
-            const int tile = t_begin + t;
-            const int64_t col0 = (int64_t)tile * BN + half * COLS;
-            const float rs_max = p.tile_rs_max[tile];
-            const int64_t valid = p.n_rows - col0;  // columns of this slice inside the index
-            st.dmin = q_ok ? dot_bound(st.thr, rs_max, qs) : INT32_MAX;
+            const float inv = __frcp_rn(__fmul_rn(rs_max, qs));
+            st.dmin = q_ok ? dot_bound(st.thr, inv) : INT32_MAX;
             const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) +
                                    (uint32_t)(buf * BN + half * COLS);
             if constexpr (KCAP <= 32) {
@@ -299,13 +323,14 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
                 for (int c = 0; c < CHUNKS; c += 2) {
                     __syncwarp();
                     tmem_ld32(taddr + (uint32_t)((c + 1) * 32), rb);
-                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, p.row_scale, qs, rs_max,
-                                     p.k, st);
+                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, sel_rs<CHUNKS>(rsv, c),
+                                     qs, inv, p.k, stash, stash_rs, lane, st);
                     __syncwarp();
                     tmem_ld_wait_regs(rb);
                     if (c + 2 < CHUNKS) tmem_ld32(taddr + (uint32_t)((c + 2) * 32), ra);
-                    scan_chunk<KCAP>(rb, col0 + (c + 1) * 32, valid - (c + 1) * 32, p.row_scale,
-                                     qs, rs_max, p.k, st);
+                    scan_chunk<KCAP>(rb, col0 + (c + 1) * 32, valid - (c + 1) * 32,
+                                     sel_rs<CHUNKS>(rsv, c + 1), qs, inv, p.k, stash,
+                                     stash_rs, lane, st);
                     __syncwarp();
                     if (c + 2 < CHUNKS) tmem_ld_wait_regs(ra);
                 }
@@ -317,8 +342,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
                     __syncwarp();
                     tmem_ld32(taddr + (uint32_t)(c * 32), ra);
                     tmem_ld_wait_regs(ra);
-                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, p.row_scale, qs, rs_max,
-                                     p.k, st);
+                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, sel_rs<CHUNKS>(rsv, c),
+                                     qs, inv, p.k, stash, stash_rs, lane, st);
                 }
             }
             tc_fence_before();
@@ -645,13 +670,13 @@ static int launch_tc_k(const CUtensorMap& tq, const CUtensorMap& tr, const fi8::
     if (!configured) {
         if (cudaFuncSetAttribute(fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)fi8::SMEM_BYTES) != cudaSuccess)
+                                 (int)fi8::smem_bytes(EPI_WARPS)) != cudaSuccess)
             return PION_B200_ECUDA;
         configured = true;
     }
     dim3 grid(n_qt, p.n_splits);
     fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>
-        <<<grid, 64 + 32 * EPI_WARPS, fi8::SMEM_BYTES, st>>>(tq, tr, p);
+        <<<grid, 64 + 32 * EPI_WARPS, fi8::smem_bytes(EPI_WARPS), st>>>(tq, tr, p);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

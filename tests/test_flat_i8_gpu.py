@@ -90,9 +90,9 @@ def test_flat_i8_knn_matches_oracle(ctx, oracle, path_env, n, dim, nq, k, path):
 
 @pytest.mark.parametrize("k", [1, 10, 32])
 def test_forced_prepass_on_small_index(ctx, oracle, k):
-    """The pre-pass (first 64 tiles) + main pass over the rest, on 79 tiles."""
+    """The threshold pre-pass (first max(64, 8k) tiles) + main pass over the rest."""
     import pion_b200
-    keys, ks, q, qsc = quantized_case(oracle, 20000, 1536, 300, seed=17)
+    keys, ks, q, qsc = quantized_case(oracle, 80000, 1536, 130, seed=17)
     ix = pion_b200.FlatI8Index(ctx, keys, ks)
     os.environ["PION_B200_I8_PREPASS"] = "1"
     try:
