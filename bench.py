@@ -1,19 +1,23 @@
 #!/usr/bin/env python
 """Throughput benchmark of the B200 FT.SEARCH KNN path.
 
-Default workload: FLAT INT8 inner-product KNN over 1,000,000 x 1536 rows (1024-centre
-L2-normalised Gaussian mixture, seed 1, per-row symmetric int8 with an fp32 scale),
-1024-query batches, k = 10.  One step = one batch scored against the whole index and
-reduced to the final top-k per query.  On N GPUs the rows are split into N contiguous
-shards (strong scaling: the same total work), each rank scores its shard, an NCCL
-all-gather exchanges the k candidates per query, and every rank merges them.
+Default workload (`--workload flat_i8`): FLAT INT8 inner-product KNN over 1,000,000 x
+1536 rows (1024-centre L2-normalised Gaussian mixture, seed 1, per-row symmetric int8
+with an fp32 scale), 1024-query batches, k = 10.  One step = one batch scored against
+the whole index and reduced to the final top-k per query.  On N GPUs the rows are split
+into N contiguous shards (strong scaling: the same total work), each rank scores its
+shard, an NCCL all-gather exchanges the k candidates per query, and every rank merges.
+
+Other workloads: `flat_i8_b1` (the same index, one query per step), `flat_i8_10m`
+(10M rows, 4096-query batches), `flat_f32` (FLAT FP32 cosine, 100,000 x 1536,
+256 centres, 1000-query batches).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload flat_i8|flat_i8_b1|flat_f32|bq]
+                    [--workload NAME]
 
 Rank 0 prints one JSON line.  `value` is whole-job queries/s timed on the device
 (CUDA events on the launching stream, max over ranks, inputs resident in HBM);
-`e2e` is the same metric through the C-ABI with host buffers (copies inside the
+`e2e` is the same metric through the C ABI with host buffers (copies inside the
 timed region).  `--impl reference` times the CPU oracle (the restatement of Pion's
 open reference routines) on the host cores instead.
 """
@@ -35,18 +39,20 @@ sys.path.insert(0, ROOT)
 METRIC = "KNN queries/sec (1536-d, k=10)"
 
 WORKLOADS = {
-    # name: rows, dim, centres, seed, batch, k, dtype
-    "flat_i8": dict(rows=1_000_000, dim=1536, centres=1024, seed=1, batch=1024, k=10,
-                    dtype="int8", desc="FLAT INT8 inner product, 1M x 1536, 1024-query batches"),
-    "flat_i8_b1": dict(rows=1_000_000, dim=1536, centres=1024, seed=1, batch=1, k=10,
-                       dtype="int8", desc="FLAT INT8 inner product, 1M x 1536, batch 1"),
-    "flat_i8_10m": dict(rows=10_000_000, dim=1536, centres=4096, seed=4, batch=4096, k=10,
-                        dtype="int8", desc="sharded FLAT INT8, 10M x 1536, 4096-query batches"),
+    "flat_i8": dict(kind="i8", rows=1_000_000, dim=1536, centres=1024, seed=1, batch=1024, k=10,
+                    desc="FLAT INT8 inner product, 1M x 1536, 1024-query batches"),
+    "flat_i8_b1": dict(kind="i8", rows=1_000_000, dim=1536, centres=1024, seed=1, batch=1, k=10,
+                       desc="FLAT INT8 inner product, 1M x 1536, batch 1"),
+    "flat_i8_10m": dict(kind="i8", rows=10_000_000, dim=1536, centres=4096, seed=4, batch=4096,
+                        k=10, desc="sharded FLAT INT8, 10M x 1536, 4096-query batches"),
+    "flat_f32": dict(kind="f32", rows=100_000, dim=1536, centres=256, seed=0, batch=1000, k=10,
+                     desc="FLAT FP32 cosine, 100K x 1536, 1000-query batches"),
 }
 
 
 def args_parse(argv=None):
-    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
@@ -68,8 +74,7 @@ def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            d = json.load(f)
-        return d, "measured"
+            return json.load(f), "measured"
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
@@ -148,26 +153,168 @@ def dist_env():
     return world, rank, local
 
 
+def config_of(wl, batch, world):
+    return {"workload": wl["desc"], "rows": wl["rows"], "dim": wl["dim"],
+            "centres": wl["centres"], "batch": batch, "k": wl["k"], "seed": wl["seed"],
+            "parallelism": f"row shards x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+            "l2": "index larger than L2 (no flush needed)"}
+
+
+# ------------------------------------------------------------ workloads --
+
+class I8Workload:
+    """FLAT INT8 inner product: rows quantised per row on the GPU (pkm_quantize_rows_i8)."""
+
+    dtype = "int8"
+    descending = True
+
+    def __init__(self, wl, batch, dev, ctx, lo, hi):
+        import torch
+
+        import pion_b200
+        from pion_b200.workloads import mixture_torch
+
+        self.wl, self.batch, self.k, self.ctx = wl, batch, wl["k"], ctx
+        n, dim = wl["rows"], wl["dim"]
+        self.dim = dim
+        keys = torch.empty((hi - lo, dim), dtype=torch.int8, device=dev)
+        ks = torch.empty(hi - lo, dtype=torch.float32, device=dev)
+        for s in range(lo, hi, 1 << 20):
+            e = min(hi, s + (1 << 20))
+            part, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev,
+                                    row_range=(s, e))
+            kq, sq = pion_b200.quantize_rows_i8(ctx, part)
+            keys[s - lo:e - lo] = kq
+            ks[s - lo:e - lo] = sq
+            del part, kq, sq
+        _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev,
+                              row_range=(0, 0))
+        self.q, self.qs = pion_b200.quantize_rows_i8(ctx, qf)
+        torch.cuda.synchronize()
+        self.keys, self.ks = keys, ks
+        self.ix = pion_b200.FlatI8Index(ctx, keys, ks, id_base=lo, borrow=True)
+
+    def inputs(self):
+        return [self.q, self.qs]
+
+    def search(self, inp):
+        return self.ix.search(inp[0], inp[1], self.k)
+
+    def host_call(self, hin, out_i, out_v):
+        import pion_b200
+        c = self.ctx
+        c.check(c.lib.pion_v_b200_flat_i8_knn(c.h, self.ix.h, hin[0].data_ptr(), hin[1].data_ptr(),
+                                              self.batch, self.k, out_i.data_ptr(),
+                                              out_v.data_ptr(), pion_b200._lib.MEM_HOST))
+
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+        if self.batch > 1:
+            ops = 2.0 * self.dim * rows_local * self.batch
+            achieved = ops / (kern_ms / 1000.0) / 1e12
+            # the scoring kernel runs back to back for the whole timed region (hundreds of
+            # ms under the 1 kW power cap), so the sustained figure is the denominator
+            peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+            return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak,
+                    "frac_of_burst": achieved / (2.0 * peaks["bf16_tflops"]),
+                    "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate = 2 x bf16 "
+                                   f"on B200); int8 tera-ops counted as TFLOP",
+                    "algorithmic_per_launch": ops, "kernel_ms": kern_ms}
+        byts = float(rows_local) * (self.dim + 4)
+        achieved = byts / (kern_ms / 1000.0) / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "algorithmic_per_launch": byts, "kernel_ms": kern_ms}
+
+    def host_data(self):
+        return (self.keys.cpu().numpy(), self.ks.cpu().numpy(), self.q.cpu().numpy(),
+                self.qs.cpu().numpy())
+
+    @staticmethod
+    def cpu_run(data, lo, hi, k, threads):
+        import oracle
+        keys, ks, q, qs = data
+        oracle.flat_i8_knn(keys, ks, q[lo:hi], qs[lo:hi], k, nthreads=threads)
+
+
+class F32Workload:
+    """FLAT FP32 cosine: rows normalised at registration (COSINE ingest)."""
+
+    dtype = "fp32 (3 x bf16 split shortlist on tensor cores + exact fp32 rescore)"
+    descending = False
+
+    def __init__(self, wl, batch, dev, ctx, lo, hi):
+        import torch
+
+        import pion_b200
+        from pion_b200.workloads import mixture_torch
+
+        self.wl, self.batch, self.k, self.ctx = wl, batch, wl["k"], ctx
+        n, dim = wl["rows"], wl["dim"]
+        self.dim = dim
+        rows, self.q = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev,
+                                     row_range=(lo, hi))
+        torch.cuda.synchronize()
+        self.ix = pion_b200.FlatF32Index(ctx, rows, id_base=lo)
+        self.rows_raw = rows
+
+    def inputs(self):
+        return [self.q]
+
+    def search(self, inp):
+        return self.ix.search(inp[0], self.k)
+
+    def host_call(self, hin, out_i, out_v):
+        import pion_b200
+        c = self.ctx
+        c.check(c.lib.pion_v_b200_flat_f32_knn(c.h, self.ix.h, hin[0].data_ptr(), self.batch,
+                                               self.k, out_i.data_ptr(), out_v.data_ptr(),
+                                               pion_b200._lib.MEM_HOST))
+
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+        flops = 2.0 * self.dim * rows_local * self.batch
+        achieved = flops / (kern_ms / 1000.0) / 1e12
+        # three bf16 tensor passes per fp32 product (hi.hi + hi.lo + lo.hi)
+        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) / 3.0
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_source": f"{peak_kind} dense bf16 sustained / 3 (fp32 products as three "
+                               f"bf16 passes); timed: query normalisation + bf16 split + "
+                               f"tensor-core shortlist",
+                "algorithmic_per_launch": flops, "kernel_ms": kern_ms}
+
+    def host_data(self):
+        import oracle
+        return (oracle.l2_normalize_rows(self.rows_raw.cpu().numpy()), self.q.cpu().numpy())
+
+    @staticmethod
+    def cpu_run(data, lo, hi, k, threads):
+        import oracle
+        rows, q = data
+        oracle.exact_knn(rows, q[lo:hi], k, cosine=True, nthreads=threads)
+
+
+ADAPTERS = {"i8": I8Workload, "f32": F32Workload}
+
+
 # --------------------------------------------------------------- reference arm --
 
-def run_reference(a, wl):
-    """CPU oracle timing (the restatement of Pion's open reference routines)."""
-    world, rank, local = dist_env()
-    if rank != 0:
-        return 0
+def reference_data(wl, batch, dev):
+    """The same workload on the host, prepared with plain torch/numpy and the oracle."""
     import numpy as np
     import torch
 
     import oracle
     from pion_b200.workloads import mixture_torch
 
-    oracle.build()
-    batch = a.batch or wl["batch"]
-    dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
-    _, qf = mixture_torch(wl["rows"], wl["dim"], wl["centres"], wl["seed"], batch, device=dev,
-                          row_range=(0, 0))
+    n, dim = wl["rows"], wl["dim"]
+    _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev, row_range=(0, 0))
+    if wl["kind"] == "f32":
+        rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
+        return oracle.l2_normalize_rows(rows.cpu().numpy()), qf.cpu().numpy()
 
-    def q8(x):  # data preparation only: the reference's per-row quantiser in torch ops
+    def q8(x):  # the reference's per-row quantiser in torch ops (data preparation only)
         m = x.abs().amax(dim=1)
         scale = m / 127.0
         scale = torch.where(m == 0, torch.ones_like(scale), scale)
@@ -177,33 +324,47 @@ def run_reference(a, wl):
         return qi.to(torch.int8).cpu().numpy(), scale.cpu().numpy()
 
     keys, ks = [], []
-    for s in range(0, wl["rows"], 1 << 20):
-        part, _ = mixture_torch(wl["rows"], wl["dim"], wl["centres"], wl["seed"], 0, device=dev,
-                                row_range=(s, min(wl["rows"], s + (1 << 20))))
+    for s in range(0, n, 1 << 20):
+        part, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev,
+                                row_range=(s, min(n, s + (1 << 20))))
         a8, s8 = q8(part)
         keys.append(a8)
         ks.append(s8)
         del part
-    keys, ks = np.concatenate(keys), np.concatenate(ks)
     q, qs = q8(qf)
+    return np.concatenate(keys), np.concatenate(ks), q, qs
+
+
+def run_reference(a, wl):
+    """CPU oracle timing (the restatement of Pion's open reference routines)."""
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+
+    import oracle
+
+    oracle.build()
+    batch = a.batch or wl["batch"]
+    dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
+    data = reference_data(wl, batch, dev)
+    run = ADAPTERS[wl["kind"]].cpu_run
     threads = os.cpu_count() or 1
     # size a step: throughput estimate on `threads` queries, then a sample per step so
     # that warmup + steps take about two minutes
     t0 = time.perf_counter()
     est_n = min(batch, threads)
-    oracle.flat_i8_knn(keys, ks, q[:est_n], qs[:est_n], wl["k"], nthreads=threads)
+    run(data, 0, est_n, wl["k"], threads)
     qps_est = est_n / (time.perf_counter() - t0)
     per_step = max(1, min(batch, int(120.0 * qps_est / max(1, a.steps + a.warmup))))
     for i in range(a.warmup):
-        j = (i * per_step) % batch
-        oracle.flat_i8_knn(keys, ks, q[j:j + per_step], qs[j:j + per_step], wl["k"],
-                           nthreads=threads)
+        j = (i * per_step) % max(1, batch - per_step + 1)
+        run(data, j, j + per_step, wl["k"], threads)
     t0 = time.perf_counter()
     done = 0
     for i in range(a.steps):
         j = (i * per_step) % max(1, batch - per_step + 1)
-        oracle.flat_i8_knn(keys, ks, q[j:j + per_step], qs[j:j + per_step], wl["k"],
-                           nthreads=threads)
+        run(data, j, j + per_step, wl["k"], threads)
         done += per_step
     dt = time.perf_counter() - t0
     qps = done / dt
@@ -213,9 +374,8 @@ def run_reference(a, wl):
         "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": 1000.0 * dt / max(1, a.steps), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic",
-        "config": {"workload": wl["desc"], "rows": wl["rows"], "dim": wl["dim"],
-                   "batch": batch, "k": wl["k"], "seed": wl["seed"]},
+        "scaling": "strong", "vs_baseline": None, "dtype": ADAPTERS[wl["kind"]].dtype,
+        "data": "synthetic", "config": config_of(wl, batch, 1),
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
@@ -228,12 +388,10 @@ def run_reference(a, wl):
 # ----------------------------------------------------------------- our arm --
 
 def run_ours(a, wl):
-    import numpy as np
     import torch
     import torch.distributed as dist
 
     import pion_b200
-    from pion_b200.workloads import mixture_torch
 
     world, rank, local = dist_env()
     if world != a.gpus:
@@ -250,44 +408,23 @@ def run_ours(a, wl):
 
     batch = a.batch or wl["batch"]
     k = wl["k"]
-    n, dim = wl["rows"], wl["dim"]
+    n = wl["rows"]
     lo, hi = n * rank // world, n * (rank + 1) // world
     ctx = pion_b200.Context(local)
-
-    # ---- data: each rank draws only its shard (chunk-seeded, identical for any N)
-    keys = torch.empty((hi - lo, dim), dtype=torch.int8, device=dev)
-    ks = torch.empty(hi - lo, dtype=torch.float32, device=dev)
-    piece = 1 << 20
-    qf = None
-    for s in range(lo, hi, piece):
-        e = min(hi, s + piece)
-        part, qq = mixture_torch(n, dim, wl["centres"], wl["seed"],
-                                 batch if qf is None else 0, device=dev, row_range=(s, e))
-        if qf is None:
-            qf = qq
-        kq, sq = pion_b200.quantize_rows_i8(ctx, part)
-        keys[s - lo:e - lo] = kq
-        ks[s - lo:e - lo] = sq
-        del part, kq, sq
-    if qf is None:
-        _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev,
-                              row_range=(0, 0))
-    q, qs = pion_b200.quantize_rows_i8(ctx, qf)
-    torch.cuda.synchronize()
-    ix = pion_b200.FlatI8Index(ctx, keys, ks, id_base=lo, borrow=True)
+    W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi)
     ctx.use_torch_stream()
     stream = torch.cuda.current_stream()
 
     gathered_v = torch.empty((world, batch, k), dtype=torch.float32, device=dev)
     gathered_i = torch.empty((world, batch, k), dtype=torch.int32, device=dev)
 
-    def step(qq, qqs):
-        ids, sc = ix.search(qq, qqs, k)
+    def step(inp):
+        ids, sc = W.search(inp)
         if world == 1:
             return ids, sc
         dist.all_gather_into_tensor(gathered_v, sc)
         dist.all_gather_into_tensor(gathered_i, ids)
-        return pion_b200.merge_topk(ctx, gathered_v, gathered_i, k, descending=True,
+        return pion_b200.merge_topk(ctx, gathered_v, gathered_i, k, descending=W.descending,
                                     lists_major=True)
 
     def barrier():
@@ -296,8 +433,9 @@ def run_ours(a, wl):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
+    inp = W.inputs()
     for _ in range(max(3, a.warmup)):
-        step(q, qs)
+        step(inp)
     barrier()
 
     clocks = ClockMonitor(local)
@@ -308,7 +446,7 @@ def run_ours(a, wl):
     barrier()
     ev0.record(stream)
     for _ in range(a.steps):
-        step(q, qs)
+        step(inp)
     ev1.record(stream)
     barrier()
     elapsed = ev0.elapsed_time(ev1)
@@ -319,25 +457,18 @@ def run_ours(a, wl):
 
     # ---- e2e: host (pinned) queries in, host results out, through the C ABI
     e2e_steps = a.e2e_steps or max(10, min(a.steps, 200))
-    hq = torch.empty((batch, dim), dtype=torch.int8).pin_memory()
-    hqs = torch.empty(batch, dtype=torch.float32).pin_memory()
-    hq.copy_(q.cpu())
-    hqs.copy_(qs.cpu())
+    hin = [t.cpu().pin_memory() for t in inp]
+    dbuf = [torch.empty_like(t) for t in inp]
     out_i = torch.empty((batch, k), dtype=torch.int32).pin_memory()
     out_v = torch.empty((batch, k), dtype=torch.float32).pin_memory()
-    dq = torch.empty_like(q)
-    dqs = torch.empty_like(qs)
 
     def e2e_step():
-        if world == 1:  # the C-ABI host-buffer path (on the context's stream, set to the
-            # dedicated stream above): copies, kernels, copies, sync
-            ctx.check(ctx.lib.pion_v_b200_flat_i8_knn(ctx.h, ix.h, hq.data_ptr(), hqs.data_ptr(),
-                                                      batch, k, out_i.data_ptr(),
-                                                      out_v.data_ptr(), pion_b200._lib.MEM_HOST))
+        if world == 1:  # the C-ABI host-buffer path: copies, kernels, copies, sync
+            W.host_call(hin, out_i, out_v)
             return
-        dq.copy_(hq, non_blocking=True)
-        dqs.copy_(hqs, non_blocking=True)
-        ids, sc = step(dq, dqs)
+        for d, h in zip(dbuf, hin):
+            d.copy_(h, non_blocking=True)
+        ids, sc = step(dbuf)
         out_i.copy_(ids, non_blocking=True)
         out_v.copy_(sc, non_blocking=True)
         stream.synchronize()
@@ -352,7 +483,7 @@ def run_ours(a, wl):
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    h2d = batch * dim + batch * 4
+    h2d = sum(t.numel() * t.element_size() for t in hin)
     d2h = batch * k * 8
 
     # ---- max over ranks
@@ -369,40 +500,14 @@ def run_ours(a, wl):
         qps = batch * a.steps / (elapsed / 1000.0)
         e2e_qps = batch * e2e_steps / (e2e_ms / 1000.0)
         peaks, peak_kind = measured_peaks()
-        rows_local = hi - lo
-        if batch > 1:
-            ops = 2.0 * dim * rows_local * batch
-            achieved = ops / (kern_avg_ms / 1000.0) / 1e12
-            # the scoring kernel runs back to back for the whole timed region (hundreds of
-            # ms under the 1 kW power cap), so the sustained figure is the denominator
-            peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak,
-                    "frac_of_burst": achieved / (2.0 * peaks["bf16_tflops"]),
-                    "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate = 2 x bf16 "
-                                   f"on B200); int8 tera-ops counted as TFLOP",
-                    "algorithmic_per_launch": ops,
-                    "kernel_ms": kern_avg_ms,
-                    "traffic": profiled_traffic(f"{a.workload}_{world}")}
-        else:
-            byts = float(rows_local) * (dim + 4)
-            achieved = byts / (kern_avg_ms / 1000.0) / 1e9
-            peak = peaks["hbm_gbs"]
-            roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                    "algorithmic_per_launch": byts, "kernel_ms": kern_avg_ms,
-                    "traffic": profiled_traffic(f"{a.workload}_{world}")}
+        roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind)
+        roof["traffic"] = profiled_traffic(f"{a.workload}_{world}")
         line = {
             "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed / a.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": wl["dtype"],
-            "data": "synthetic (seeded Gaussian mixture on the device)",
-            "config": {"workload": wl["desc"], "rows": n, "dim": dim, "centres": wl["centres"],
-                       "batch": batch, "k": k, "seed": wl["seed"],
-                       "parallelism": f"row shards x{world}" + (" + NCCL all-gather"
-                                                                if world > 1 else ""),
-                       "l2": "index larger than L2 (no flush needed)"},
+            "dtype": W.dtype, "data": "synthetic (seeded Gaussian mixture on the device)",
+            "config": config_of(wl, batch, world),
             "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches,
@@ -412,12 +517,12 @@ def run_ours(a, wl):
     # ---- CPU baseline on rank 0 at N=1 (bounded sample of the same workload)
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
-            line["cpu_baseline"] = cpu_baseline(keys, ks, q, qs, k, batch, a.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(W, batch, k, a.cpu_seconds)
         except Exception as e:  # pragma: no cover
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    ix.free()
+    W.ix.free()
     ctx.close()
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -425,22 +530,21 @@ def run_ours(a, wl):
     return 0
 
 
-def cpu_baseline(keys, ks, q, qs, k, batch, seconds):
+def cpu_baseline(W, batch, k, seconds):
     import oracle
     oracle.build()
-    hk, hks = keys.cpu().numpy(), ks.cpu().numpy()
-    hq, hqs = q.cpu().numpy(), qs.cpu().numpy()
+    data = W.host_data()
     threads = os.cpu_count() or 1
     t0 = time.perf_counter()
     est = min(batch, threads)
-    oracle.flat_i8_knn(hk, hks, hq[:est], hqs[:est], k, nthreads=threads)
+    W.cpu_run(data, 0, est, k, threads)
     qps_est = est / (time.perf_counter() - t0)
     m = int(max(est, min(batch, qps_est * seconds)))
     t0 = time.perf_counter()
-    oracle.flat_i8_knn(hk, hks, hq[:m], hqs[:m], k, nthreads=threads)
+    W.cpu_run(data, 0, m, k, threads)
     dt = time.perf_counter() - t0
     return {"value": m / dt, "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{m} of the {batch} queries against all {hk.shape[0]:,} rows "
+            "sample": f"{m} of the {batch} queries against all {W.wl['rows']:,} rows "
                       f"({dt:.1f} s, one query per thread)"}
 
 

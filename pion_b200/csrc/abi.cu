@@ -80,7 +80,7 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, co
 }
 
 // Queues a copy of the status word into pinned host memory.
-static int queue_status_readback(pion_b200_ctx* ctx) {
+int queue_status_readback(pion_b200_ctx* ctx) {
     return cudaMemcpyAsync(ctx->h_status, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost,
                            ctx->stream) == cudaSuccess
                ? 0
@@ -88,7 +88,7 @@ static int queue_status_readback(pion_b200_ctx* ctx) {
 }
 
 // Synchronises the stream, then turns a recorded device-side status into a code.
-static int finish_sync(pion_b200_ctx* ctx) {
+int finish_sync(pion_b200_ctx* ctx) {
     if (queue_status_readback(ctx) != 0)
         return set_error(ctx, PION_B200_ECUDA, "status copy failed: %s",
                          cudaGetErrorString(cudaGetLastError()));
@@ -105,15 +105,15 @@ static int finish_sync(pion_b200_ctx* ctx) {
     return 0;
 }
 
-static bool valid_ctx(const pion_b200_ctx* ctx) { return ctx != nullptr && ctx->d_status; }
+bool valid_ctx(const pion_b200_ctx* ctx) { return ctx != nullptr && ctx->d_status; }
 
-static int use_device(pion_b200_ctx* ctx) {
+int use_device(pion_b200_ctx* ctx) {
     if (cudaSetDevice(ctx->device) != cudaSuccess)
         return set_error(ctx, PION_B200_ENODEV, "cudaSetDevice(%d) failed", ctx->device);
     return 0;
 }
 
-static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 void timing_begin(pion_b200_ctx* ctx) {
     if (!ctx->timing) return;
@@ -268,6 +268,8 @@ int pion_v_b200_index_free(pion_b200_index* index) {
         if (index->rows_f32) cudaFree(index->rows_f32);
     }
     if (index->tile_rs_max) cudaFree(index->tile_rs_max);
+    if (index->rows_hi) cudaFree(index->rows_hi);
+    if (index->rows_lo) cudaFree(index->rows_lo);
     if (index->codes) cudaFree(index->codes);
     delete index;
     return 0;
@@ -363,20 +365,22 @@ static int forced_i8_path() {
 // slot, at least 64 tiles (16384 rows) -- enough that the sample's k-th score is
 // close to the final one on clustered data, where a query's neighbours are a small
 // fraction of the rows.
-static int prepass_tiles(int k) { return k * 8 > 64 ? k * 8 : 64; }
+}  // extern "C"
 
-// Unbounded seed of the pre-pass (tiles of 256 rows).
-static constexpr int kSeedTiles = 8;
+int pion::prepass_tiles(int k) { return k * 8 > 64 ? k * 8 : 64; }
 
-// The pre-pass runs for indexes of at least 8 x its sample; PION_B200_I8_PREPASS=0
-// turns it off and =1 forces it whenever the index is larger than the sample.
-static bool use_prepass(int n_tiles, int k) {
-    const char* e = getenv("PION_B200_I8_PREPASS");
+// The pre-pass runs for indexes of at least 8 x its sample; the environment
+// variable `env` (PION_B200_I8_PREPASS / PION_B200_F32_PREPASS) = 0 turns it off
+// and = 1 forces it whenever the index is larger than the sample.
+bool pion::use_prepass(int n_tiles, int k, const char* env) {
+    const char* e = getenv(env);
     const int mode = e ? atoi(e) : -1;
     if (mode == 0) return false;
     if (mode == 1) return n_tiles > prepass_tiles(k);
     return n_tiles >= 8 * prepass_tiles(k);
 }
+
+extern "C" {
 
 int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* q,
                             const float* q_scale, int64_t nq, int64_t k, int32_t* out_ids,
@@ -459,7 +463,7 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         // seed's k-th score as bound.  The sample's k-th score per query is an exact
         // lower bound of the final k-th score, handed to the main pass so that its
         // integer pre-filter rejects almost every row from the start.
-        const bool pre = use_prepass(n_tiles, kk);
+        const bool pre = use_prepass(n_tiles, kk, "PION_B200_I8_PREPASS");
         const int pre_tiles = pre ? prepass_tiles(kk) : 0;
         const int main_begin = pre_tiles;
         const int splits = fi8_choose_splits(n_qt, n_tiles - main_begin, ctx->num_sms);

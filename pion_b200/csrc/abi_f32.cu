@@ -1,0 +1,362 @@
+// C-ABI entry points of the FLAT FP32 cosine path (exact_knn under COSINE,
+// src/commands/vector.mojo:1228-1365) and the row normaliser of COSINE ingest
+// (l2_normalize_fp32, src/vector/kernels.mojo:318-357).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <new>
+
+#include "internal.h"
+
+using namespace pion;
+
+// PION_B200_F32_EXACT=1 sends every query through the exact CUDA-core scan (tests).
+static int force_exact_f32() {
+    const char* e = getenv("PION_B200_F32_EXACT");
+    return e && atoi(e) != 0 ? 1 : 0;
+}
+
+extern "C" {
+
+int pion_v_b200_l2_normalize_rows(pion_b200_ctx* ctx, const float* src, int64_t n_rows,
+                                  int64_t dim, float* dst, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (n_rows < 0 || dim <= 0 || dim > (1 << 20) || (n_rows > 0 && (!src || !dst)))
+        return set_error(ctx, PION_B200_EINVAL, "l2_normalize_rows: bad arguments");
+    if (n_rows == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const size_t bytes = (size_t)n_rows * dim * 4;
+    const float* ds = src;
+    float* dd = dst;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, bytes) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "l2_normalize_rows: staging");
+        if (cudaMemcpyAsync(ctx->stage_in.ptr, src, bytes, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "l2_normalize_rows: copy failed");
+        ds = dd = static_cast<float*>(ctx->stage_in.ptr);
+    } else if (mem != PION_B200_MEM_DEVICE) {
+        return set_error(ctx, PION_B200_EINVAL, "l2_normalize_rows: bad mem %d", mem);
+    }
+    int rc = launch_l2_normalize_rows(ds, n_rows, (int)dim, dd, nullptr, st);
+    ctx->launches++;
+    if (rc != 0) return set_error(ctx, rc, "l2_normalize_rows: launch failed");
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(dst, dd, bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "l2_normalize_rows: copy back failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+int pion_v_b200_register_flat_f32(pion_b200_ctx* ctx, const float* rows, int64_t n_rows,
+                                  int64_t dim, int64_t id_base, int normalize, int mem,
+                                  pion_b200_index** out_index) {
+    if (!valid_ctx(ctx) || !out_index) return PION_B200_EINVAL;
+    *out_index = nullptr;
+    if (n_rows < 0 || (n_rows > 0 && !rows))
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_f32: null rows");
+    if (dim <= 0 || dim % 8 != 0 || dim > 16384)
+        return set_error(ctx, PION_B200_ESHAPE, "register_flat_f32: dim %lld must be a multiple "
+                         "of 8 in [8, 16384]", (long long)dim);
+    if (n_rows > INT32_MAX - 1 || id_base < 0 || id_base + n_rows > INT32_MAX)
+        return set_error(ctx, PION_B200_ESHAPE, "register_flat_f32: ids must fit int32");
+    if (mem == PION_B200_MEM_DEVICE_BORROW && normalize)
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_f32: a borrowed buffer cannot "
+                         "be normalised in place");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE && mem != PION_B200_MEM_DEVICE_BORROW)
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_f32: bad mem %d", mem);
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    pion_b200_index* ix = new (std::nothrow) pion_b200_index();
+    if (!ix) return PION_B200_ENOMEM;
+    ix->kind = kFlatF32;
+    ix->device = ctx->device;
+    ix->n_rows = n_rows;
+    ix->dim = dim;
+    ix->id_base = id_base;
+    const size_t bytes = (size_t)n_rows * dim * 4;
+    if (mem == PION_B200_MEM_DEVICE_BORROW) {
+        ix->owns = false;
+        ix->rows_f32 = const_cast<float*>(rows);
+    } else {
+        if (cudaMalloc(&ix->rows_f32, bytes ? bytes : 16) != cudaSuccess) {
+            cudaGetLastError();
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, PION_B200_ENOMEM, "register_flat_f32: %zu bytes", bytes);
+        }
+        if (n_rows > 0 && cudaMemcpyAsync(ix->rows_f32, rows, bytes,
+                                          mem == PION_B200_MEM_HOST ? cudaMemcpyHostToDevice
+                                                                    : cudaMemcpyDeviceToDevice,
+                                          st) != cudaSuccess) {
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, PION_B200_ECUDA, "register_flat_f32: copy failed");
+        }
+    }
+    if ((reinterpret_cast<uintptr_t>(ix->rows_f32) & 15u) != 0) {
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, PION_B200_EINVAL, "register_flat_f32: rows not 16-byte aligned");
+    }
+    if (n_rows > 0) {
+        int rc = 0;
+        if (normalize) {
+            rc = launch_l2_normalize_rows(ix->rows_f32, n_rows, (int)dim, ix->rows_f32, nullptr,
+                                          st);
+            ctx->launches++;
+        }
+        // largest row norm, for the TF32 error bound of the certificate
+        float* norms = nullptr;
+        if (rc == 0 && cudaMalloc(&norms, (size_t)n_rows * 4 + 256) != cudaSuccess) {
+            cudaGetLastError();
+            rc = PION_B200_ENOMEM;
+        }
+        if (rc == 0) rc = launch_row_norms(ix->rows_f32, n_rows, (int)dim, norms, st);
+        float* dmax = norms ? reinterpret_cast<float*>(reinterpret_cast<char*>(norms) +
+                                                       align_up((size_t)n_rows * 4, 128))
+                            : nullptr;
+        if (rc == 0) rc = launch_max_reduce(norms, n_rows, dmax, st);
+        if (rc == 0 && (cudaMemcpyAsync(&ix->row_norm_max, dmax, 4, cudaMemcpyDeviceToHost, st) !=
+                            cudaSuccess ||
+                        cudaStreamSynchronize(st) != cudaSuccess))
+            rc = PION_B200_ECUDA;
+        ctx->launches += 2;
+        if (norms) cudaFree(norms);
+        // bf16 split of the stored rows for the tensor-core shortlist
+        const size_t half_bytes = (size_t)n_rows * dim * 2;
+        if (rc == 0 && (cudaMalloc(&ix->rows_hi, half_bytes) != cudaSuccess ||
+                        cudaMalloc(&ix->rows_lo, half_bytes) != cudaSuccess)) {
+            cudaGetLastError();
+            rc = PION_B200_ENOMEM;
+        }
+        if (rc == 0) {
+            rc = launch_split_bf16(ix->rows_f32, (size_t)n_rows * dim, ix->rows_hi, ix->rows_lo,
+                                   st);
+            ctx->launches++;
+        }
+        if (rc == 0 && (make_tmap_2d(&ix->tmap_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                     ix->rows_hi, (uint64_t)dim, (uint64_t)n_rows,
+                                     (uint64_t)dim * 2, (uint32_t)ff32_k_elems(),
+                                     (uint32_t)ff32_tile_rows(), CU_TENSOR_MAP_SWIZZLE_128B) != 0 ||
+                        make_tmap_2d(&ix->tmap_rows_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                     ix->rows_lo, (uint64_t)dim, (uint64_t)n_rows,
+                                     (uint64_t)dim * 2, (uint32_t)ff32_k_elems(),
+                                     (uint32_t)ff32_tile_rows(), CU_TENSOR_MAP_SWIZZLE_128B) != 0))
+            rc = PION_B200_ECUDA;
+        if (rc != 0) {
+            pion_v_b200_index_free(ix);
+            return set_error(ctx, rc, "register_flat_f32: preparation failed");
+        }
+        ix->has_tmap = true;
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess) {
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, PION_B200_ECUDA, "register_flat_f32: stream failed");
+    }
+    *out_index = ix;
+    return 0;
+}
+
+int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const float* q,
+                             int64_t nq, int64_t k, int32_t* out_ids, float* out_scores, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kFlatF32)
+        return set_error(ctx, PION_B200_EINVAL, "flat_f32_knn: not a FLAT FP32 index");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "flat_f32_knn: index on another device");
+    if (nq < 0 || k < 1 || (nq > 0 && (!q || !out_ids || !out_scores)))
+        return set_error(ctx, PION_B200_EINVAL, "flat_f32_knn: bad arguments");
+    if (k > 64) return set_error(ctx, PION_B200_ESHAPE, "flat_f32_knn: k %lld > 64", (long long)k);
+    if (nq > (1 << 24)) return set_error(ctx, PION_B200_ESHAPE, "flat_f32_knn: batch too large");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "flat_f32_knn: bad mem %d", mem);
+    if (nq == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const int dim = (int)ix->dim;
+    const int kk = (int)k;
+    const int nqi = (int)nq;
+    const size_t qbytes = align_up((size_t)nq * dim * 4, 256);
+    const size_t out_bytes = (size_t)nq * kk * 4;
+
+    const float* dq = q;
+    int32_t* di = out_ids;
+    float* dv = out_scores;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, qbytes) != 0 ||
+            ensure(ctx->stage_out, 2 * align_up(out_bytes, 256)) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "flat_f32_knn: staging");
+        if (cudaMemcpyAsync(ctx->stage_in.ptr, q, (size_t)nq * dim * 4, cudaMemcpyHostToDevice,
+                            st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "flat_f32_knn: query copy failed");
+        dq = static_cast<const float*>(ctx->stage_in.ptr);
+        di = static_cast<int32_t*>(ctx->stage_out.ptr);
+        dv = reinterpret_cast<float*>(static_cast<char*>(ctx->stage_out.ptr) +
+                                      align_up(out_bytes, 256));
+    }
+    int rc = 0;
+    if (ix->n_rows == 0) {
+        rc = launch_fill_results(dv, di, (size_t)nq * kk, INFINITY, st);
+        ctx->launches++;
+    } else {
+        const int kc = ff32_kc(kk);
+        const int n_qt = (nqi + ff32_query_tile() - 1) / ff32_query_tile();
+        const int n_tiles = (int)((ix->n_rows + ff32_tile_rows() - 1) / ff32_tile_rows());
+        const bool pre = use_prepass(n_tiles, kc, "PION_B200_F32_PREPASS");
+        const int pre_tiles = pre ? prepass_tiles(kc) : 0;
+        const int splits = fi8_choose_splits(n_qt, n_tiles - pre_tiles, ctx->num_sms);
+        const int n_lists = splits + (pre ? 1 : 0);
+        const int seed_splits = pre ? kSeedTiles : 0;
+        int samp_splits = pre ? ctx->num_sms / n_qt : 0;
+        if (pre) {
+            const int cap = (pre_tiles - kSeedTiles) / 2;
+            samp_splits = samp_splits < 1 ? 1 : (samp_splits > cap ? cap : samp_splits);
+        }
+        const int samp_lists = samp_splits + 1;
+        const int chunks = ff32_exact_chunks();
+        // scratch layout (floats / ints)
+        const size_t n_qn = (size_t)nq * dim;
+        const size_t n_cand = (size_t)nq * n_lists * kc;
+        const size_t n_seed = (size_t)nq * seed_splits * kc;
+        const size_t n_samp = (size_t)nq * samp_lists * kc;
+        const size_t n_merged = (size_t)nq * kc;
+        const size_t n_chunk = (size_t)nq * chunks * kk;
+        size_t off = 0;
+        auto take = [&](size_t elems) {
+            size_t o = off;
+            off += align_up(elems * 4, 256);
+            return o;
+        };
+        const size_t o_qn = take(n_qn), o_qh = take(n_qn / 2 + 1), o_ql = take(n_qn / 2 + 1),
+                     o_qnorm = take(nq), o_cv = take(n_cand),
+                     o_ci = take(n_cand), o_sv = take(n_seed), o_si = take(n_seed),
+                     o_pv = take(n_samp), o_pi = take(n_samp), o_mv = take(n_merged),
+                     o_mi = take(n_merged), o_flag = take(nq + 1), o_chd = take(n_chunk),
+                     o_chi = take(n_chunk);
+        if (ensure(ctx->scratch, off) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "flat_f32_knn: scratch");
+        char* base = static_cast<char*>(ctx->scratch.ptr);
+        float* qn = reinterpret_cast<float*>(base + o_qn);
+        float* qnorm = reinterpret_cast<float*>(base + o_qnorm);
+        void* qh = base + o_qh;
+        void* ql = base + o_ql;
+        float* cv = reinterpret_cast<float*>(base + o_cv);
+        int32_t* ci = reinterpret_cast<int32_t*>(base + o_ci);
+        float* sv = reinterpret_cast<float*>(base + o_sv);
+        int32_t* si = reinterpret_cast<int32_t*>(base + o_si);
+        float* pv = reinterpret_cast<float*>(base + o_pv);
+        int32_t* pi = reinterpret_cast<int32_t*>(base + o_pi);
+        float* mv = reinterpret_cast<float*>(base + o_mv);
+        int32_t* mi = reinterpret_cast<int32_t*>(base + o_mi);
+        int* flags = reinterpret_cast<int*>(base + o_flag);  // [0] = count, then query ids
+        float* chd = reinterpret_cast<float*>(base + o_chd);
+        int32_t* chi = reinterpret_cast<int32_t*>(base + o_chi);
+
+        timing_begin(ctx);
+        rc = launch_query_normalize(dq, nqi, dim, qn, qnorm, st);
+        ctx->launches++;
+        if (rc == 0) {
+            rc = launch_split_bf16(qn, (size_t)nq * dim, qh, ql, st);
+            ctx->launches++;
+        }
+        CUtensorMap tmap_qh, tmap_ql;
+        if (rc == 0 && (make_tmap_2d(&tmap_qh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qh,
+                                     (uint64_t)dim, (uint64_t)nq, (uint64_t)dim * 2,
+                                     (uint32_t)ff32_k_elems(), (uint32_t)ff32_query_tile(),
+                                     CU_TENSOR_MAP_SWIZZLE_128B) != 0 ||
+                        make_tmap_2d(&tmap_ql, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ql,
+                                     (uint64_t)dim, (uint64_t)nq, (uint64_t)dim * 2,
+                                     (uint32_t)ff32_k_elems(), (uint32_t)ff32_query_tile(),
+                                     CU_TENSOR_MAP_SWIZZLE_128B) != 0))
+            rc = PION_B200_ECUDA;
+        Ff32TcLaunch L;
+        L.tmap_qh = &tmap_qh;
+        L.tmap_ql = &tmap_ql;
+        L.tmap_rh = &ix->tmap_rows;
+        L.tmap_rl = &ix->tmap_rows_lo;
+        L.n_rows = ix->n_rows;
+        L.nq = nqi;
+        L.dim = dim;
+        L.kc = kc;
+        L.status = ctx->d_status;
+        if (rc == 0 && pre) {
+            L.tile_begin = 0;
+            L.tile_end = kSeedTiles;
+            L.n_splits = seed_splits;
+            L.n_lists = seed_splits;
+            L.cand_val = sv;
+            L.cand_idx = si;
+            rc = launch_flat_bf16x3_tc(L, st);
+            ctx->launches++;
+            const size_t seed_slot = (size_t)(samp_lists - 1) * kc;
+            if (rc == 0) {
+                rc = launch_merge_lists(sv, si, nqi, seed_splits, kc, 0, true, pv + seed_slot,
+                                        pi + seed_slot, st, false, samp_lists * kc);
+                ctx->launches++;
+            }
+            if (rc == 0) {
+                L.tile_begin = kSeedTiles;
+                L.tile_end = pre_tiles;
+                L.n_splits = samp_splits;
+                L.n_lists = samp_lists;
+                L.cand_val = pv;
+                L.cand_idx = pi;
+                L.thr0 = pv + seed_slot + (kc - 1);
+                L.thr0_stride = samp_lists * kc;
+                rc = launch_flat_bf16x3_tc(L, st);
+                ctx->launches++;
+            }
+            if (rc == 0) {
+                rc = launch_merge_lists(pv, pi, nqi, samp_lists, kc, 0, true,
+                                        cv + (size_t)(n_lists - 1) * kc,
+                                        ci + (size_t)(n_lists - 1) * kc, st, false,
+                                        n_lists * kc);
+                ctx->launches++;
+            }
+        }
+        if (rc == 0) {
+            L.tile_begin = pre_tiles;
+            L.tile_end = n_tiles;
+            L.n_splits = splits;
+            L.n_lists = n_lists;
+            L.cand_val = cv;
+            L.cand_idx = ci;
+            L.thr0 = pre ? cv + (size_t)(n_lists - 1) * kc + (kc - 1) : nullptr;
+            L.thr0_stride = n_lists * kc;
+            rc = launch_flat_bf16x3_tc(L, st);
+            ctx->launches++;
+        }
+        timing_end(ctx);
+        if (rc == 0) {
+            rc = launch_merge_lists(cv, ci, nqi, n_lists, kc, 0, true, mv, mi, st);
+            ctx->launches++;
+        }
+        if (rc == 0 && cudaMemsetAsync(flags, 0, sizeof(int), st) != cudaSuccess)
+            rc = PION_B200_ECUDA;
+        if (rc == 0) {
+            rc = launch_rescore_certify(ix->rows_f32, dim, qn, qnorm, ix->row_norm_max, mv, mi,
+                                        nqi, kc, kk, ix->id_base, dv, di, flags + 1, flags,
+                                        force_exact_f32(), st);
+            ctx->launches++;
+        }
+        if (rc == 0) {
+            rc = launch_exact_fallback(ix->rows_f32, ix->n_rows, dim, qn, flags + 1, flags, nqi,
+                                       kk, ix->id_base, chd, chi, dv, di, ctx->num_sms, st);
+            ctx->launches += 2;
+        }
+    }
+    if (rc != 0)
+        return set_error(ctx, rc, "flat_f32_knn: launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(out_ids, di, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_scores, dv, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "flat_f32_knn: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+}  // extern "C"

@@ -159,6 +159,16 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 x bf16 -> f32 (kind::f16).
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives TMEM lane
 // (lane_base + i), columns [col, col + 32).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -223,6 +233,15 @@ __host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n) {
     return (1u << 4)                                   // D format: F32
            | (2u << 7)                                 // A: TF32
            | (2u << 10)                                // B: TF32
+           | (static_cast<uint32_t>(n >> 3) << 17)
+           | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f16 with bf16 operands -> f32, both K-major.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n) {
+    return (1u << 4)                                   // D format: F32
+           | (1u << 7)                                 // A: BF16
+           | (1u << 10)                                // B: BF16
            | (static_cast<uint32_t>(n >> 3) << 17)
            | (static_cast<uint32_t>(m >> 4) << 24);
 }

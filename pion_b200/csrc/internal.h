@@ -21,6 +21,49 @@ struct DevBuf {
 
 enum IndexKind { kFlatI8 = 1, kFlatF32 = 2, kBQ = 3 };
 
+// ---- flat_f32.cu
+int ff32_tile_rows();
+int ff32_query_tile();
+int ff32_k_elems();
+int ff32_kc(int k);
+int ff32_exact_chunks();
+struct Ff32TcLaunch {
+    const CUtensorMap* tmap_qh = nullptr;  // queries, bf16 hi / lo halves
+    const CUtensorMap* tmap_ql = nullptr;
+    const CUtensorMap* tmap_rh = nullptr;  // rows, bf16 hi / lo halves
+    const CUtensorMap* tmap_rl = nullptr;
+    const float* thr0 = nullptr;
+    int thr0_stride = 0;
+    int64_t n_rows = 0;
+    int nq = 0;
+    int dim = 0;
+    int kc = 0;
+    int tile_begin = 0;
+    int tile_end = 0;
+    int n_splits = 1;
+    int n_lists = 1;
+    int list_base = 0;
+    float* cand_val = nullptr;
+    int32_t* cand_idx = nullptr;
+    int* status = nullptr;
+};
+int launch_flat_bf16x3_tc(const Ff32TcLaunch& launch, cudaStream_t st);
+int launch_split_bf16(const float* x, size_t n, void* hi, void* lo, cudaStream_t st);
+int launch_query_normalize(const float* q, int nq, int dim, float* out, float* qnorm,
+                           cudaStream_t st);
+int launch_l2_normalize_rows(const float* src, int64_t n_rows, int dim, float* dst, float* norms,
+                             cudaStream_t st);
+int launch_row_norms(const float* rows, int64_t n_rows, int dim, float* norms, cudaStream_t st);
+int launch_max_reduce(const float* x, int64_t n, float* out, cudaStream_t st);
+int launch_rescore_certify(const float* rows, int dim, const float* qn, const float* qnorm,
+                           float row_norm_max, const float* cand_v, const int32_t* cand_i, int nq,
+                           int kc, int k, int64_t id_base, float* out_d, int32_t* out_i,
+                           int* flagged, int* n_flagged, int force_exact, cudaStream_t st);
+int launch_exact_fallback(const float* rows, int64_t n_rows, int dim, const float* qn,
+                          const int* flagged, const int* n_flagged, int nq, int k,
+                          int64_t id_base, float* chunk_d, int32_t* chunk_i, float* out_d,
+                          int32_t* out_i, int num_sms, cudaStream_t st);
+
 }  // namespace pion
 
 struct pion_b200_ctx {
@@ -56,6 +99,10 @@ struct pion_b200_index {
     float* tile_rs_max = nullptr;
     // FLAT FP32 and BQ rerank rows
     float* rows_f32 = nullptr;
+    float row_norm_max = 0.0f;  // largest row L2 norm (bounds the shortlist error)
+    void* rows_hi = nullptr;    // bf16 split of rows_f32: hi = bf16(x), lo = bf16(x - hi)
+    void* rows_lo = nullptr;
+    CUtensorMap tmap_rows_lo;
     // BQ sign codes, uint64 words per row
     uint64_t* codes = nullptr;
     int64_t words = 0;
@@ -65,8 +112,17 @@ struct pion_b200_index {
 
 namespace pion {
 
-// ---- error helpers (abi.cu)
+// ---- shared ABI helpers (abi.cu)
 int set_error(pion_b200_ctx* ctx, int code, const char* fmt, ...);
+int queue_status_readback(pion_b200_ctx* ctx);
+int finish_sync(pion_b200_ctx* ctx);
+bool valid_ctx(const pion_b200_ctx* ctx);
+int use_device(pion_b200_ctx* ctx);
+size_t align_up(size_t x, size_t a);
+int prepass_tiles(int k);
+bool use_prepass(int n_tiles, int k, const char* env);
+// Unbounded seed of the threshold pre-pass (index tiles).
+constexpr int kSeedTiles = 8;
 int ensure(DevBuf& b, size_t bytes);
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,

@@ -34,14 +34,6 @@ int64_t pion_v_pkm_combine_topk(const float*, const int32_t*, int64_t, const flo
                                 const int32_t*, int64_t, int64_t, int64_t, int32_t*, float*) {
     return pending(nullptr, "pion_v_pkm_combine_topk");
 }
-int pion_v_b200_register_flat_f32(pion_b200_ctx* ctx, const float*, int64_t, int64_t, int64_t,
-                                  int, int, pion_b200_index**) {
-    return pending(ctx, "register_flat_f32");
-}
-int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index*, const float*, int64_t,
-                             int64_t, int32_t*, float*, int) {
-    return pending(ctx, "flat_f32_knn");
-}
 int pion_v_b200_register_bq(pion_b200_ctx* ctx, const float*, int64_t, int64_t, int64_t, int, int,
                             pion_b200_index**) {
     return pending(ctx, "register_bq");
@@ -49,10 +41,6 @@ int pion_v_b200_register_bq(pion_b200_ctx* ctx, const float*, int64_t, int64_t, 
 int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index*, const float*, int64_t,
                               int64_t, int64_t, int32_t*, float*, int) {
     return pending(ctx, "bq_rerank_knn");
-}
-int pion_v_b200_l2_normalize_rows(pion_b200_ctx* ctx, const float*, int64_t, int64_t, float*,
-                                  int) {
-    return pending(ctx, "l2_normalize_rows");
 }
 
 }  // extern "C"
