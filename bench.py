@@ -392,6 +392,7 @@ def run_ours(a, wl):
     import torch.distributed as dist
 
     import pion_b200
+    from pion_b200.sharded import ShardedSearch, shard_bounds
 
     world, rank, local = dist_env()
     if world != a.gpus:
@@ -409,23 +410,17 @@ def run_ours(a, wl):
     batch = a.batch or wl["batch"]
     k = wl["k"]
     n = wl["rows"]
-    lo, hi = n * rank // world, n * (rank + 1) // world
+    lo, hi = shard_bounds(n, world, rank)
     ctx = pion_b200.Context(local)
     W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi)
     ctx.use_torch_stream()
     stream = torch.cuda.current_stream()
 
-    gathered_v = torch.empty((world, batch, k), dtype=torch.float32, device=dev)
-    gathered_i = torch.empty((world, batch, k), dtype=torch.int32, device=dev)
-
-    def step(inp):
-        ids, sc = W.search(inp)
-        if world == 1:
-            return ids, sc
-        dist.all_gather_into_tensor(gathered_v, sc)
-        dist.all_gather_into_tensor(gathered_i, ids)
-        return pion_b200.merge_topk(ctx, gathered_v, gathered_i, k, descending=W.descending,
+    def merge(scores, ids):
+        return pion_b200.merge_topk(ctx, scores, ids, k, descending=W.descending,
                                     lists_major=True)
+
+    step = ShardedSearch(W.search, k, merge)
 
     def barrier():
         torch.cuda.synchronize()

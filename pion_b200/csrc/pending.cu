@@ -14,26 +14,6 @@ static int pending(pion_b200_ctx* ctx, const char* what) {
     return PION_B200_ESHAPE;
 }
 
-int64_t pion_v_abi_version(void) { return PION_B200_ABI_VERSION; }
-int64_t pion_v_isa(void) { return 100; }
-void pion_v_pkm_scores_f32(const float*, int64_t, int64_t, const float*, int64_t, float*) {
-    pending(nullptr, "pion_v_pkm_scores_f32");
-}
-void pion_v_pkm_rescore_f32(const float*, int64_t, const float*, const int32_t*, int64_t, float*) {
-    pending(nullptr, "pion_v_pkm_rescore_f32");
-}
-void pion_v_pkm_scores_i8(const int8_t*, int64_t, int64_t, const float*, const int8_t*,
-                          const float*, int64_t, float*) {
-    pending(nullptr, "pion_v_pkm_scores_i8");
-}
-int64_t pion_v_pkm_topk_max(const float*, int64_t, int64_t, int32_t*, float*) {
-    return pending(nullptr, "pion_v_pkm_topk_max");
-}
-void pion_v_pkm_sort_desc(float*, int32_t*, int64_t) { pending(nullptr, "pion_v_pkm_sort_desc"); }
-int64_t pion_v_pkm_combine_topk(const float*, const int32_t*, int64_t, const float*,
-                                const int32_t*, int64_t, int64_t, int64_t, int32_t*, float*) {
-    return pending(nullptr, "pion_v_pkm_combine_topk");
-}
 int pion_v_b200_register_bq(pion_b200_ctx* ctx, const float*, int64_t, int64_t, int64_t, int, int,
                             pion_b200_index**) {
     return pending(ctx, "register_bq");
