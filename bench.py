@@ -10,7 +10,8 @@ shard, an NCCL all-gather exchanges the k candidates per query, and every rank m
 
 Other workloads: `flat_i8_b1` (the same index, one query per step), `flat_i8_10m`
 (10M rows, 4096-query batches), `flat_f32` (FLAT FP32 cosine, 100,000 x 1536,
-256 centres, 1000-query batches).
+256 centres, 1000-query batches), `bq` (binary-quantised FLAT, 1M x 1536, Hamming
+top-100 then fp32 cosine rerank to 10, 1024-query batches).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME]
@@ -47,6 +48,9 @@ WORKLOADS = {
                         k=10, desc="sharded FLAT INT8, 10M x 1536, 4096-query batches"),
     "flat_f32": dict(kind="f32", rows=100_000, dim=1536, centres=256, seed=0, batch=1000, k=10,
                      desc="FLAT FP32 cosine, 100K x 1536, 1000-query batches"),
+    "bq": dict(kind="bq", rows=1_000_000, dim=1536, centres=1024, seed=2, batch=1024, k=10,
+               desc="binary-quantised FLAT, 1M x 1536 (192-byte codes), Hamming top-100, "
+                    "fp32 cosine rerank to 10, 1024-query batches"),
 }
 
 
@@ -295,7 +299,65 @@ class F32Workload:
         oracle.exact_knn(rows, q[lo:hi], k, cosine=True, nthreads=threads)
 
 
-ADAPTERS = {"i8": I8Workload, "f32": F32Workload}
+class BQWorkload:
+    """Binary-quantised FLAT: sign codes + Hamming shortlist of 100, exact fp32 rerank."""
+
+    dtype = "1-bit codes (int8 tensor-core Hamming) + fp32 rerank"
+    descending = False
+    shortlist = 100
+
+    def __init__(self, wl, batch, dev, ctx, lo, hi):
+        import torch
+
+        import pion_b200
+        from pion_b200.workloads import mixture_torch
+
+        self.wl, self.batch, self.k, self.ctx = wl, batch, wl["k"], ctx
+        n, dim = wl["rows"], wl["dim"]
+        self.dim = dim
+        rows, self.q = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev,
+                                     row_range=(lo, hi))
+        torch.cuda.synchronize()
+        self.ix = pion_b200.BQIndex(ctx, rows, id_base=lo)
+        self.rows_raw = rows
+
+    def inputs(self):
+        return [self.q]
+
+    def search(self, inp):
+        return self.ix.search(inp[0], self.k, shortlist=self.shortlist)
+
+    def host_call(self, hin, out_i, out_v):
+        import pion_b200
+        c = self.ctx
+        c.check(c.lib.pion_v_b200_bq_rerank_knn(c.h, self.ix.h, hin[0].data_ptr(), self.batch,
+                                                self.shortlist, self.k, out_i.data_ptr(),
+                                                out_v.data_ptr(), pion_b200._lib.MEM_HOST))
+
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+        # Hamming of every (query, row) pair as +-1 int8 dot products on the tensor cores
+        ops = 2.0 * self.dim * rows_local * self.batch
+        achieved = ops / (kern_ms / 1000.0) / 1e12
+        peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate); timed: query "
+                               f"normalisation + signs + staged Hamming shortlist",
+                "algorithmic_per_launch": ops, "kernel_ms": kern_ms}
+
+    def host_data(self):
+        import oracle
+        rn = oracle.l2_normalize_rows(self.rows_raw.cpu().numpy())
+        return (oracle.bq_pack_signs(rn), rn, self.q.cpu().numpy())
+
+    @staticmethod
+    def cpu_run(data, lo, hi, k, threads):
+        import oracle
+        codes, rows, q = data
+        oracle.bq_knn(codes, rows, q[lo:hi], BQWorkload.shortlist, k, nthreads=threads)
+
+
+ADAPTERS = {"i8": I8Workload, "f32": F32Workload, "bq": BQWorkload}
 
 
 # --------------------------------------------------------------- reference arm --
@@ -310,9 +372,12 @@ def reference_data(wl, batch, dev):
 
     n, dim = wl["rows"], wl["dim"]
     _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev, row_range=(0, 0))
-    if wl["kind"] == "f32":
+    if wl["kind"] in ("f32", "bq"):
         rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
-        return oracle.l2_normalize_rows(rows.cpu().numpy()), qf.cpu().numpy()
+        rn = oracle.l2_normalize_rows(rows.cpu().numpy())
+        if wl["kind"] == "bq":
+            return oracle.bq_pack_signs(rn), rn, qf.cpu().numpy()
+        return rn, qf.cpu().numpy()
 
     def q8(x):  # the reference's per-row quantiser in torch ops (data preparation only)
         m = x.abs().amax(dim=1)

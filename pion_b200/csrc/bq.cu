@@ -1,0 +1,610 @@
+// Binary-quantised FLAT with FP32 rerank on B200 (sm_100a).
+//
+// Codes: bit b of word w is 1 iff x[64w + b] > 0 (the sign packing of
+// src/vector/kernels.mojo:1711-1720, applied to the normalised vector).  Hamming
+// distance = popcount(a XOR b) over the words (src/vector/reference/quant_dots.mojo:
+// 95-100).  Shortlist: the S smallest Hamming distances by (distance, id).  Rerank:
+// exact_knn's COSINE formula 1 - dot_f32_4chain(q^, row) on the shortlist and the
+// stable insertion sort of _exact_rescore (src/commands/vector.mojo:1413-1456): equal
+// scores keep shortlist order.
+//
+// On ±1 vectors, dot = (bits equal) - (bits differ) = dim - 2 * hamming, so the
+// Hamming distances of a whole query batch come from the INT8 tensor-core pipeline
+// (tcgen05 kind::i8) over a ±1-expanded copy of the codes:
+//   bq_tc_kernel        collects, per (query, split), every row under the query's
+//                       current Hamming bound (no score matrix);
+//   bq_select_kernel    exact S-th smallest distance per query from a histogram of the
+//                       small-integer distances, then the S best by (distance, id);
+//   bq_fallback_kernel  queries whose candidate lists overflowed: exact popcount scan
+//                       of the packed codes;
+//   bq_rerank_kernel    exact fp32 rerank of the shortlist.
+// The bound comes from staged samples: the S-th distance of the first rows bounds the
+// final S-th distance, and later rows (larger ids) must beat it strictly.
+#include <cstdint>
+#include <cstdio>
+
+#include "common.cuh"
+#include "exact_fp32.cuh"
+#include "internal.h"
+
+namespace pion {
+namespace bq {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4, UMMA_K = 32;
+constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = make_idesc_i8(BM, BN);
+constexpr size_t SMEM_PIPE_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+constexpr size_t STASH_BYTES = 32 * 32 * 4;
+constexpr size_t SMEM_BYTES = SMEM_PIPE_BYTES + EPI_WARPS * STASH_BYTES;
+constexpr int CAP = 256;  // candidates kept per (query, list)
+
+struct TcParams {
+    const int* dot_min;   // per query: collect rows with dot >= dot_min (nullptr: all)
+    int64_t n_rows;
+    int nq;
+    int dim;
+    int tile_begin, tile_end, n_splits, kblocks;
+    int n_lists, list_base;
+    int32_t* cand_id;     // [nq][n_lists][CAP]
+    uint16_t* cand_h;     // [nq][n_lists][CAP]
+    int* cand_n;          // [nq][n_lists]
+    int* status;
+};
+
+template <int HALVES>
+__global__ void __launch_bounds__(THREADS, 1)
+    bq_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                 const __grid_constant__ CUtensorMap tmap_rows, TcParams p) {
+    constexpr int COLS = BN / HALVES;
+    constexpr int CHUNKS = COLS / 32;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint32_t* stash_all = reinterpret_cast<uint32_t*>(smem + (SMEM_PIPE_BYTES - 1024));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int qt = blockIdx.x;
+    const int split = blockIdx.y;
+    const int span = p.tile_end - p.tile_begin;
+    const int t_begin = p.tile_begin + (int)((int64_t)span * split / p.n_splits);
+    const int t_end = p.tile_begin + (int)((int64_t)span * (split + 1) / p.n_splits);
+    const int my_tiles = t_end - t_begin;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 32 * EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            tma_prefetch_desc(&tmap_q);
+            tma_prefetch_desc(&tmap_rows);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_parity[STAGES];
+            bool issued[STAGES];
+            for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+            bool ok = true;
+            for (int t = 0; t < my_tiles && ok; ++t) {
+                const int row0 = (t_begin + t) * BN;
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                    tma_load_2d(sA + stage * A_BYTES, &tmap_q, &full[stage], kb * BK, qt * BM);
+                    tma_load_2d(sB + stage * B_BYTES, &tmap_rows, &full[stage], kb * BK, row0);
+                    issued[stage] = true;
+                    issued_parity[stage] = phase;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            for (int s = 0; s < STAGES; ++s)
+                if (issued[s]) mbar_wait(&full[s], issued_parity[s], p.status, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int t = 0; t < my_tiles; ++t) {
+                const int buf = t & 1;
+                const uint32_t use = (uint32_t)(t >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, p.status, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, p.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
+                        mma_i8(d_tmem, make_sw128_kmajor_desc(a0 + kk * UMMA_K),
+                               make_sw128_kmajor_desc(b0 + kk * UMMA_K), IDESC,
+                               (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[buf]);
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.status, nullptr);
+        }
+    } else {
+        // epilogue: collect every column with dot >= dot_min into this thread's list
+        const int ew = warp - 2;
+        uint32_t* stash = stash_all + ew * (STASH_BYTES / 4);
+        const int lg = warp & 3;
+        const int half = ew >> 2;
+        const int q = qt * BM + lg * 32 + lane;
+        const bool q_ok = q < p.nq;
+        const int dmin = !q_ok ? INT32_MAX : (p.dot_min ? p.dot_min[q] : INT32_MIN);
+        const size_t list = (size_t)(q_ok ? q : 0) * p.n_lists + p.list_base +
+                            (size_t)split * HALVES + half;
+        int32_t* out_id = p.cand_id + list * CAP;
+        uint16_t* out_h = p.cand_h + list * CAP;
+        int count = 0;
+        for (int t = 0; t < my_tiles; ++t) {
+            const int buf = t & 1;
+            const uint32_t use = (uint32_t)(t >> 1);
+            const int tile = t_begin + t;
+            const int64_t col0 = (int64_t)tile * BN + half * COLS;
+            const int64_t valid = p.n_rows - col0;
+            const bool got = mbar_wait(&tfull[buf], use & 1u, p.status, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(lg * 32) << 16) +
+                                   (uint32_t)(buf * BN + half * COLS);
+#pragma unroll 1
+            for (int c = 0; c < CHUNKS; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld32(taddr + (uint32_t)(c * 32), r);
+                tmem_ld_wait_regs(r);
+                int32_t mx = (int32_t)r[0];
+#pragma unroll
+                for (int j = 1; j < 32; ++j) mx = max(mx, (int32_t)r[j]);
+                uint32_t mask = 0;
+                if (mx >= dmin) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] >= dmin ? 1u : 0u) << j;
+                    const int64_t vc = valid - c * 32;
+                    if (vc < 32) mask &= vc <= 0 ? 0u : ((1u << vc) - 1u);
+                }
+                if (!__any_sync(0xffffffffu, mask != 0u)) continue;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) stash[j * 32 + lane] = r[j];
+                __syncwarp();
+#pragma unroll 1
+                while (mask) {
+                    const int j = __ffs(mask) - 1;
+                    mask &= mask - 1u;
+                    if (count < CAP) {
+                        const int32_t dv = (int32_t)stash[j * 32 + lane];
+                        out_id[count] = (int32_t)(col0 + c * 32 + j);
+                        out_h[count] = (uint16_t)((p.dim - dv) >> 1);
+                    }
+                    ++count;
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[buf]);
+        }
+        if (q_ok) p.cand_n[list] = count;  // > CAP means the list overflowed
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------ preparation --
+
+// Signs of one row: ±1 int8 (x > 0 -> +1) and the packed code (bit b of word w).
+// One warp per row, 64 elements (one word) per lane step.
+__global__ void signs_kernel(const float* __restrict__ x, int64_t n_rows, int dim,
+                             int8_t* __restrict__ pm, uint64_t* __restrict__ codes) {
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (r >= n_rows) return;
+    const int lane = threadIdx.x & 31;
+    const float* xr = x + r * dim;
+    const int words = dim / 64;
+    for (int w = 0; w < words; ++w) {
+        const float a = xr[w * 64 + lane], b = xr[w * 64 + 32 + lane];
+        const unsigned lo = __ballot_sync(0xffffffffu, a > 0.0f);
+        const unsigned hi = __ballot_sync(0xffffffffu, b > 0.0f);
+        if (pm) {
+            pm[r * dim + w * 64 + lane] = a > 0.0f ? 1 : -1;
+            pm[r * dim + w * 64 + 32 + lane] = b > 0.0f ? 1 : -1;
+        }
+        if (lane == 0) codes[r * words + w] = ((uint64_t)hi << 32) | lo;
+    }
+}
+
+// ------------------------------------------------------------- selection --
+constexpr int SEL_THREADS = 256;
+constexpr int SEL_TIES = 2048;
+
+__device__ __forceinline__ void bitonic_sort_u64(uint64_t* v, int n_pow2) {
+    for (int size = 2; size <= n_pow2; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < n_pow2 / 2; i += blockDim.x) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool asc = ((lo & size) == 0);
+                const uint64_t a = v[lo], b = v[hi];
+                if (asc ? (a > b) : (a < b)) {
+                    v[lo] = b;
+                    v[hi] = a;
+                }
+            }
+            __syncthreads();
+        }
+}
+
+// One CTA per query: the S best candidates by (distance, id) from its lists, sorted.
+// Writes the shortlist, its length, the next stage's bound (dot_min: rows must have a
+// distance strictly below the S-th one) and flags queries whose lists overflowed.
+__global__ void __launch_bounds__(SEL_THREADS)
+    bq_select_kernel(const int32_t* __restrict__ cid, const uint16_t* __restrict__ ch,
+                     const int* __restrict__ cn, int n_lists, int dim, int S,
+                     int32_t* __restrict__ out_id, uint16_t* __restrict__ out_h,
+                     int* __restrict__ out_n, int out_qstride, int n_qstride,
+                     int* __restrict__ next_dot_min, int* __restrict__ flagged,
+                     int* __restrict__ n_flagged, int force_flag) {
+    extern __shared__ int sm_hist[];  // dim + 1 bins
+    __shared__ uint64_t keys[512];
+    __shared__ int32_t ties[SEL_TIES];
+    __shared__ int n_keys, n_ties, overflow, dstar, below, total_s;
+    const int q = blockIdx.x;
+    for (int i = threadIdx.x; i <= dim; i += SEL_THREADS) sm_hist[i] = 0;
+    if (threadIdx.x == 0) {
+        n_keys = n_ties = overflow = 0;
+        total_s = 0;
+    }
+    __syncthreads();
+    const size_t qbase = (size_t)q * n_lists;
+    for (int l = 0; l < n_lists; ++l) {
+        const int c = cn[qbase + l];
+        if (c > CAP && threadIdx.x == 0) overflow = 1;
+        const int m = c < CAP ? c : CAP;
+        for (int j = threadIdx.x; j < m; j += SEL_THREADS)
+            atomicAdd(&sm_hist[ch[(qbase + l) * CAP + j]], 1);
+        if (threadIdx.x == 0) total_s += m;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // smallest d with count(h <= d) >= S (all candidates when fewer than S)
+        int acc = 0, d = 0;
+        const int want = total_s < S ? total_s : S;
+        if (want == 0) {
+            dstar = -1;
+            below = 0;
+        } else {
+            for (d = 0; d <= dim; ++d) {
+                if (acc + sm_hist[d] >= want) break;
+                acc += sm_hist[d];
+            }
+            dstar = d;
+            below = acc;
+        }
+    }
+    __syncthreads();
+    const int D = dstar;
+    const int want = total_s < S ? total_s : S;
+    for (int l = 0; l < n_lists && D >= 0; ++l) {
+        const int c = cn[qbase + l];
+        const int m = c < CAP ? c : CAP;
+        for (int j = threadIdx.x; j < m; j += SEL_THREADS) {
+            const int h = ch[(qbase + l) * CAP + j];
+            const int32_t id = cid[(qbase + l) * CAP + j];
+            if (h < D) {
+                const int pos = atomicAdd(&n_keys, 1);
+                if (pos < 512) keys[pos] = ((uint64_t)h << 32) | (uint32_t)id;
+            } else if (h == D) {
+                const int pos = atomicAdd(&n_ties, 1);
+                if (pos < SEL_TIES) ties[pos] = id;
+            }
+        }
+    }
+    __syncthreads();
+    if (D >= 0 && n_ties > SEL_TIES && threadIdx.x == 0) overflow = 1;
+    // the (want - below) smallest ids among the ties at D
+    const int nt = n_ties < SEL_TIES ? n_ties : SEL_TIES;
+    int p2 = 1;
+    while (p2 < nt) p2 <<= 1;
+    for (int i = nt + threadIdx.x; i < p2; i += SEL_THREADS) ties[i] = INT32_MAX;
+    __syncthreads();
+    if (D >= 0 && nt > 1) {
+        for (int size = 2; size <= p2; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = threadIdx.x; i < p2 / 2; i += SEL_THREADS) {
+                    const int lo = 2 * i - (i & (stride - 1));
+                    const int hi = lo + stride;
+                    const bool asc = ((lo & size) == 0);
+                    const int32_t a = ties[lo], b = ties[hi];
+                    if (asc ? (a > b) : (a < b)) {
+                        ties[lo] = b;
+                        ties[hi] = a;
+                    }
+                }
+                __syncthreads();
+            }
+    }
+    const int take = want - below;
+    for (int i = threadIdx.x; i < take && D >= 0; i += SEL_THREADS)
+        keys[below + i] = ((uint64_t)D << 32) | (uint32_t)ties[i];
+    __syncthreads();
+    // sort the shortlist by (distance, id)
+    int sp2 = 1;
+    while (sp2 < want) sp2 <<= 1;
+    for (int i = want + threadIdx.x; i < sp2; i += SEL_THREADS) keys[i] = ~0ull;
+    __syncthreads();
+    if (want > 1) bitonic_sort_u64(keys, sp2);
+    for (int i = threadIdx.x; i < S; i += SEL_THREADS) {
+        out_id[(size_t)q * out_qstride + i] = i < want ? (int32_t)(uint32_t)keys[i] : -1;
+        out_h[(size_t)q * out_qstride + i] = i < want ? (uint16_t)(keys[i] >> 32) : (uint16_t)0xffff;
+    }
+    if (threadIdx.x == 0) {
+        out_n[(size_t)q * n_qstride] = want;
+        // later rows (larger ids) enter only with a distance below the S-th one
+        next_dot_min[q] = (total_s >= S && D >= 0) ? dim - 2 * (D - 1) : INT32_MIN;
+        if (overflow || force_flag) flagged[atomicAdd(n_flagged, 1)] = q;
+    }
+}
+
+// Flagged queries: the exact shortlist from every packed code (popcount of XOR),
+// one CTA per flagged query: a histogram pass, then an in-order collection.
+__global__ void __launch_bounds__(SEL_THREADS)
+    bq_fallback_kernel(const uint64_t* __restrict__ codes, int64_t n_rows, int words,
+                       const uint64_t* __restrict__ qcodes, const int* __restrict__ flagged,
+                       const int* __restrict__ n_flagged, int S, int32_t* __restrict__ out_id,
+                       uint16_t* __restrict__ out_h, int* __restrict__ out_n) {
+    extern __shared__ int fb_hist[];
+    __shared__ uint64_t keys[512];
+    __shared__ int dstar, below, n_keys, n_tie_taken;
+    const int dim = words * 64;
+    for (int f = blockIdx.x; f < *n_flagged; f += gridDim.x) {
+        const int q = flagged[f];
+        const uint64_t* qc = qcodes + (size_t)q * words;
+        for (int i = threadIdx.x; i <= dim; i += SEL_THREADS) fb_hist[i] = 0;
+        if (threadIdx.x == 0) n_keys = n_tie_taken = 0;
+        __syncthreads();
+        for (int64_t r = threadIdx.x; r < n_rows; r += SEL_THREADS) {
+            int h = 0;
+            for (int w = 0; w < words; ++w) h += __popcll(codes[r * words + w] ^ qc[w]);
+            atomicAdd(&fb_hist[h], 1);
+        }
+        __syncthreads();
+        const int want = n_rows < S ? (int)n_rows : S;
+        if (threadIdx.x == 0) {
+            int acc = 0, d = 0;
+            for (d = 0; d <= dim; ++d) {
+                if (acc + fb_hist[d] >= want) break;
+                acc += fb_hist[d];
+            }
+            dstar = d;
+            below = acc;
+        }
+        __syncthreads();
+        const int D = dstar, need = want - below;
+        // rows in order, block by block: h < D always, h == D while ties are needed
+        for (int64_t base = 0; base < n_rows; base += SEL_THREADS) {
+            const int64_t r = base + threadIdx.x;
+            int h = dim + 1;
+            if (r < n_rows) {
+                h = 0;
+                for (int w = 0; w < words; ++w) h += __popcll(codes[r * words + w] ^ qc[w]);
+            }
+            if (h < D) keys[atomicAdd(&n_keys, 1)] = ((uint64_t)h << 32) | (uint32_t)r;
+            // ties in row order: a block-wide ordered rank
+            const bool tie = (h == D);
+            __shared__ int warp_cnt[SEL_THREADS / 32];
+            const unsigned bal = __ballot_sync(0xffffffffu, tie);
+            const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+            if (lane == 0) warp_cnt[w] = __popc(bal);
+            __syncthreads();
+            int before = n_tie_taken;
+            for (int x = 0; x < w; ++x) before += warp_cnt[x];
+            const int rank = before + __popc(bal & ((1u << lane) - 1u));
+            if (tie && rank < need) keys[below + rank] = ((uint64_t)h << 32) | (uint32_t)r;
+            __syncthreads();
+            if (threadIdx.x == 0)
+                for (int x = 0; x < SEL_THREADS / 32; ++x) n_tie_taken += warp_cnt[x];
+            __syncthreads();
+        }
+        int sp2 = 1;
+        while (sp2 < want) sp2 <<= 1;
+        for (int i = want + threadIdx.x; i < sp2; i += SEL_THREADS) keys[i] = ~0ull;
+        __syncthreads();
+        if (want > 1) bitonic_sort_u64(keys, sp2);
+        for (int i = threadIdx.x; i < S; i += SEL_THREADS) {
+            out_id[(size_t)q * S + i] = i < want ? (int32_t)(uint32_t)keys[i] : -1;
+            out_h[(size_t)q * S + i] = i < want ? (uint16_t)(keys[i] >> 32) : (uint16_t)0xffff;
+        }
+        if (threadIdx.x == 0) out_n[q] = want;
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------- rerank --
+// One warp per query: exact distances of the shortlist (in (distance, id) order),
+// then the k best by (score, shortlist position): the stable insertion sort of
+// _exact_rescore keeps equal scores in shortlist order.
+__global__ void bq_rerank_kernel(const float* __restrict__ rows, int dim,
+                                 const float* __restrict__ qn, const int32_t* __restrict__ sl_id,
+                                 const int* __restrict__ sl_n, int S, int nq, int k,
+                                 int64_t id_base, float* __restrict__ out_d,
+                                 int32_t* __restrict__ out_i) {
+    extern __shared__ float rr[];
+    const int w = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = blockIdx.x * (blockDim.x / 32) + w;
+    if (q >= nq) return;
+    float* dist = rr + (size_t)w * S;
+    const float* qv = qn + (size_t)q * dim;
+    const int n = sl_n[q];
+    const int half = lane >> 4, hl = lane & 15;
+    const unsigned hmask = half ? 0xffff0000u : 0x0000ffffu;
+    for (int j0 = 0; j0 < n; j0 += 2) {
+        const int j = j0 + half;
+        if (j < n) {
+            const int32_t id = sl_id[(size_t)q * S + j];
+            const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
+            if (hl == 0) dist[j] = __fsub_rn(1.0f, s);
+        }
+    }
+    __syncwarp();
+    for (int r = 0; r < k; ++r) {
+        float bd = INFINITY;
+        int bp = -1;
+        for (int j = lane; j < n; j += 32)
+            if (dist[j] == dist[j] && (bp < 0 || dist[j] < bd)) {  // first (lowest j) wins ties
+                bd = dist[j];
+                bp = j;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float od = __shfl_xor_sync(0xffffffffu, bd, o);
+            const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+            if (op >= 0 && (bp < 0 || od < bd || (od == bd && op < bp))) {
+                bd = od;
+                bp = op;
+            }
+        }
+        if (lane == 0) {
+            out_d[(size_t)q * k + r] = bp >= 0 ? bd : INFINITY;
+            out_i[(size_t)q * k + r] =
+                bp >= 0 ? (int32_t)(sl_id[(size_t)q * S + bp] + id_base) : -1;
+        }
+        if (bp >= 0 && lane == (bp & 31)) dist[bp] = __int_as_float(0x7fffffff);  // taken (NaN)
+        __syncwarp();
+    }
+}
+
+}  // namespace bq
+
+// =========================================================== host launchers ==
+
+int bq_tile_rows() { return bq::BN; }
+int bq_query_tile() { return bq::BM; }
+int bq_k_block() { return bq::BK; }
+int bq_cap() { return bq::CAP; }
+int bq_lists_per_split() { return bq::EPI_WARPS / 4; }
+
+int launch_signs(const float* x, int64_t n_rows, int dim, int8_t* pm, uint64_t* codes,
+                 cudaStream_t st) {
+    if (n_rows <= 0) return 0;
+    bq::signs_kernel<<<(unsigned)((n_rows + 7) / 8), 256, 0, st>>>(x, n_rows, dim, pm, codes);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_bq_tc(const BqTcLaunch& L, cudaStream_t st) {
+    bq::TcParams p;
+    p.dot_min = L.dot_min;
+    p.n_rows = L.n_rows;
+    p.nq = L.nq;
+    p.dim = L.dim;
+    p.tile_begin = L.tile_begin;
+    p.tile_end = L.tile_end;
+    p.n_splits = L.n_splits;
+    p.kblocks = (L.dim + bq::BK - 1) / bq::BK;
+    p.n_lists = L.n_lists;
+    p.list_base = L.list_base;
+    p.cand_id = L.cand_id;
+    p.cand_h = L.cand_h;
+    p.cand_n = L.cand_n;
+    p.status = L.status;
+    if (p.tile_end <= p.tile_begin || p.n_splits < 1 ||
+        p.list_base + p.n_splits * bq_lists_per_split() > p.n_lists)
+        return PION_B200_ESHAPE;
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(bq::bq_tc_kernel<bq::EPI_WARPS / 4>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)bq::SMEM_BYTES) != cudaSuccess)
+            return PION_B200_ECUDA;
+        configured = true;
+    }
+    dim3 grid((L.nq + bq::BM - 1) / bq::BM, L.n_splits);
+    bq::bq_tc_kernel<bq::EPI_WARPS / 4><<<grid, bq::THREADS, bq::SMEM_BYTES, st>>>(
+        *L.tmap_q, *L.tmap_rows, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_bq_select(const int32_t* cid, const uint16_t* ch, const int* cn, int nq, int n_lists,
+                     int dim, int S, int32_t* out_id, uint16_t* out_h, int* out_n,
+                     int out_qstride, int n_qstride, int* next_dot_min, int* flagged,
+                     int* n_flagged, int force_flag, cudaStream_t st) {
+    if (nq <= 0) return 0;
+    if (S > 256) return PION_B200_ESHAPE;
+    bq::bq_select_kernel<<<nq, bq::SEL_THREADS, (size_t)(dim + 1) * 4, st>>>(
+        cid, ch, cn, n_lists, dim, S, out_id, out_h, out_n, out_qstride, n_qstride, next_dot_min,
+        flagged, n_flagged, force_flag);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_bq_fallback(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcodes,
+                       const int* flagged, const int* n_flagged, int S, int32_t* out_id,
+                       uint16_t* out_h, int* out_n, int num_sms, cudaStream_t st) {
+    bq::bq_fallback_kernel<<<num_sms, bq::SEL_THREADS, (size_t)(words * 64 + 1) * 4, st>>>(
+        codes, n_rows, words, qcodes, flagged, n_flagged, S, out_id, out_h, out_n);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t* sl_id,
+                     const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
+                     int32_t* out_i, cudaStream_t st) {
+    if (nq <= 0) return 0;
+    const int warps = 4;
+    bq::bq_rerank_kernel<<<(nq + warps - 1) / warps, warps * 32, (size_t)warps * S * 4, st>>>(
+        rows, dim, qn, sl_id, sl_n, S, nq, k, id_base, out_d, out_i);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+}  // namespace pion

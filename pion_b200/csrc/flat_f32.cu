@@ -33,6 +33,7 @@
 #include <cstdio>
 
 #include "common.cuh"
+#include "exact_fp32.cuh"
 #include "internal.h"
 
 namespace pion {
@@ -291,40 +292,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-// ------------------------------------------------------ exact reference arithmetic
-// dot_f32_4chain over `dim` floats by 16 lanes of a warp: lane L (< 16) owns chain
-// L/4, lane L%4, and sums elements L, L+16, ... in order; the tail chain, the
-// ((a0+a1)+(a2+a3)) combine, the halving-tree lane sum and the scalar tail follow
-// src/vector/fp32_scan.mojo:17-38 exactly.  `half` selects lanes 0-15 or 16-31; the
-// result is returned to every lane of that half.
-__device__ __forceinline__ float dot4chain_half(const float* __restrict__ q,
-                                                const float* __restrict__ v, int dim,
-                                                int hl /* lane within half */, unsigned mask) {
-    const int main_end = dim & ~15;
-    float acc = 0.0f;
-    for (int d = hl; d < main_end; d += 16) acc = __fadd_rn(__fmul_rn(q[d], v[d]), acc);
-    // 4-element tail blocks continue chain 0 (lanes 0..3)
-    int d4 = main_end;
-    for (; d4 + 4 <= dim; d4 += 4)
-        if (hl < 4) acc = __fadd_rn(__fmul_rn(q[d4 + hl], v[d4 + hl]), acc);
-    // t[l] = (a0[l] + a1[l]) + (a2[l] + a3[l]): chains c at lanes 4c + l
-    const int base = (threadIdx.x & 31) & 16;  // 0 or 16
-    const int l = hl & 3;
-    const float a0 = __shfl_sync(mask, acc, base + l);
-    const float a1 = __shfl_sync(mask, acc, base + 4 + l);
-    const float a2 = __shfl_sync(mask, acc, base + 8 + l);
-    const float a3 = __shfl_sync(mask, acc, base + 12 + l);
-    const float t = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-    // reduce_add of the 4 lanes t[0..3]: (t0 + t2) + (t1 + t3)
-    const float t0 = __shfl_sync(mask, t, base + 0);
-    const float t1 = __shfl_sync(mask, t, base + 1);
-    const float t2 = __shfl_sync(mask, t, base + 2);
-    const float t3 = __shfl_sync(mask, t, base + 3);
-    float s = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
-    for (int d = d4; d < dim; ++d) s = __fadd_rn(s, __fmul_rn(q[d], v[d]));
-    return s;
-}
-
 // exact_knn's query normalisation (src/commands/vector.mojo:1254-1260): a sequential
 // scalar sum of squares, one thread per query.
 __global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int dim,
@@ -399,14 +366,6 @@ __global__ void max_reduce_kernel(const float* __restrict__ x, int64_t n, float*
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(out), __float_as_int(m));
-}
-
-// (distance asc, id asc)
-__device__ __forceinline__ bool better_asc(float da, int32_t ia, float db, int32_t ib) {
-    if (da != db) return da < db;
-    if (ia < 0) return false;
-    if (ib < 0) return true;
-    return ia < ib;
 }
 
 // One warp per query: exact distances of the kc candidates (two per warp step, one

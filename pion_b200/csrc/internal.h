@@ -178,4 +178,41 @@ int launch_flat_i8_scan1(const int8_t* rows, const float* row_scale, int64_t n_r
                          const int8_t* q, const float* q_scale, int k, int ctas, float* cand_val,
                          int32_t* cand_idx, cudaStream_t st);
 
+// ---- bq.cu
+int bq_tile_rows();
+int bq_query_tile();
+int bq_k_block();
+int bq_cap();
+int bq_lists_per_split();
+struct BqTcLaunch {
+    const CUtensorMap* tmap_q = nullptr;     // queries as ±1 int8
+    const CUtensorMap* tmap_rows = nullptr;  // rows as ±1 int8
+    const int* dot_min = nullptr;            // per query, or nullptr (collect everything)
+    int64_t n_rows = 0;
+    int nq = 0;
+    int dim = 0;
+    int tile_begin = 0;
+    int tile_end = 0;
+    int n_splits = 1;
+    int n_lists = 1;
+    int list_base = 0;
+    int32_t* cand_id = nullptr;
+    uint16_t* cand_h = nullptr;
+    int* cand_n = nullptr;
+    int* status = nullptr;
+};
+int launch_signs(const float* x, int64_t n_rows, int dim, int8_t* pm, uint64_t* codes,
+                 cudaStream_t st);
+int launch_bq_tc(const BqTcLaunch& launch, cudaStream_t st);
+int launch_bq_select(const int32_t* cid, const uint16_t* ch, const int* cn, int nq, int n_lists,
+                     int dim, int S, int32_t* out_id, uint16_t* out_h, int* out_n,
+                     int out_qstride, int n_qstride, int* next_dot_min, int* flagged,
+                     int* n_flagged, int force_flag, cudaStream_t st);
+int launch_bq_fallback(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcodes,
+                       const int* flagged, const int* n_flagged, int S, int32_t* out_id,
+                       uint16_t* out_h, int* out_n, int num_sms, cudaStream_t st);
+int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t* sl_id,
+                     const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
+                     int32_t* out_i, cudaStream_t st);
+
 }  // namespace pion
