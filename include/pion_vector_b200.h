@@ -117,7 +117,9 @@ int pion_v_b200_init(int device, int worker_id, pion_b200_ctx **out_ctx);
 int pion_v_b200_shutdown(pion_b200_ctx *ctx);
 /* Run this context's work on an existing CUDA stream (cudaStream_t), e.g. a
  * framework's current stream; NULL restores the context's own stream (pass
- * cudaStreamLegacy for the legacy default stream). */
+ * cudaStreamLegacy for the legacy default stream).  Work queued after a switch waits
+ * for the work already queued on the previous stream (the context's scratch is
+ * shared), without blocking the host. */
 int pion_v_b200_set_stream(pion_b200_ctx *ctx, void *cuda_stream);
 /* Waits for the context's stream and returns the first error any device-side wait
  * recorded since the last call (PION_B200_ETIMEOUT), else 0. */
@@ -228,6 +230,87 @@ int pion_v_b200_l2_normalize_rows(pion_b200_ctx *ctx, const float *src, int64_t 
 int pion_v_b200_merge_topk(pion_b200_ctx *ctx, const float *cand_scores, const int32_t *cand_ids,
                            int64_t nq, int64_t n_lists, int64_t k, int flags,
                            float *out_scores, int32_t *out_ids, int mem);
+
+/* ------------------------------------------------------------------- HNSW -- */
+
+/* An HNSW INT8 graph in the reference's compact level-0 layout: the buffers that
+ * compact_vectors and _build_l0_slots produce (src/vector/hnsw.mojo:2761-2990) and
+ * that BeamView1536 hands to the beam (src/vector/beam_view.mojo:11-26), plus the
+ * upper levels the greedy descent walks (src/vector/hnsw.mojo:3789-3848).  Node
+ * indices are the graph's internal indices (0 <= node < num_nodes). */
+typedef struct pion_b200_hnsw_layout {
+    int64_t num_nodes;
+    int64_t dim;             /* 1536 (the beam is the 1536-dim routine)             */
+    int64_t M;               /* level-0 lists hold <= 2M <= 32, upper lists <= M     */
+    int64_t entry_point;     /* node                                                 */
+    int64_t max_level;       /* level of the entry point                             */
+    float global_min;        /* SQ8 calibration range (_calibrate, hnsw.mojo:578)    */
+    float global_max;
+    int32_t metric;          /* 0 = L2, 1 = COSINE (queries are unit-normalised)     */
+    int32_t reserved;
+    const int8_t *compact_buffer;  /* num_nodes x compact_stride: per slot an 8-byte
+                                      header (f32 |code|^2, f32 |code[0:256]|^2) then
+                                      the dim int8 codes                             */
+    int64_t compact_stride;        /* multiple of 16, >= compact_hdr + dim           */
+    int64_t compact_hdr;           /* 8                                              */
+    const uint32_t *l0_compact;    /* num_nodes x 33: count, level-0 neighbour nodes */
+    const uint32_t *l0_slots;      /* num_nodes x 33: count, their compact slots     */
+    const uint32_t *node_slot;     /* num_nodes: compact slot of each node           */
+    const int32_t *node_ids;       /* num_nodes: external id returned for a node     */
+    const uint8_t *deleted;        /* (num_nodes + 7) / 8 bytes, bit i = node i
+                                      deleted; NULL = none                           */
+    const int8_t *node_level;      /* num_nodes: level of each node                  */
+    const int64_t *upper_offset;   /* num_nodes: first upper row of the node (-1 at
+                                      level 0); level l >= 1 is row
+                                      upper_offset[node] + l - 1                      */
+    const uint32_t *upper_links;   /* upper_rows x (1 + M): count, neighbour nodes   */
+    int64_t upper_rows;
+} pion_b200_hnsw_layout;
+
+typedef struct pion_b200_hnsw_graph pion_b200_hnsw_graph;
+
+/* Builds an HNSW INT8 graph on the host CPU the way the reference's FT.OPTIMIZE does
+ * (src/vector/hnsw.mojo:2540-2620: _calibrate, quantize, _level_of, the parallel link
+ * lanes of _insert_to_graph_mt, the relink and _repair_l0 passes, compact_vectors),
+ * from rows fp32[n_rows x dim] in HOST memory (normalised first when metric = 1).
+ * Node i gets external id id_base + i.  n_threads link lanes (<= 0: every online
+ * CPU); as in the reference, more than one lane makes the graph depend on thread
+ * timing.  Needs a CPU with AVX2 and FMA (PION_B200_ESHAPE otherwise). */
+int pion_v_b200_hnsw_build(const float *rows, int64_t n_rows, int64_t dim, int64_t M,
+                           int64_t ef_construction, int metric, int64_t id_base, int n_threads,
+                           pion_b200_hnsw_graph **out_graph);
+/* The graph's buffers (host memory owned by the graph). */
+int pion_v_b200_hnsw_graph_layout(const pion_b200_hnsw_graph *graph,
+                                  pion_b200_hnsw_layout *out_layout);
+/* Build counters: link lanes, contended link drops, relinked under-linked nodes, nodes
+ * re-linked by the exit repair, links added by the reachability repair. */
+int pion_v_b200_hnsw_graph_stats(const pion_b200_hnsw_graph *graph, int64_t *out5);
+int pion_v_b200_hnsw_graph_free(pion_b200_hnsw_graph *graph);
+
+/* Copies a graph (every pointer of `layout` in HOST memory) to the GPU.  Checks the
+ * layout: dim 1536, 2M <= 32, counts within capacity, every neighbour and slot in
+ * range. */
+int pion_v_b200_register_hnsw(pion_b200_ctx *ctx, const pion_b200_hnsw_layout *layout,
+                              pion_b200_index **out_index);
+
+/* Batched HNSW search, one beam per query, the reference's search_fp32_scored at
+ * dim 1536 (src/vector/hnsw.mojo:4136-4521): normalise (COSINE), quantise
+ * (_quantize_query_to_int8, :657-680), greedy descent of the upper levels in exact
+ * INT8 L2 (_upper_greedy_codes, :3789-3848), then the level-0 beam
+ * beam_search_1536_ref (src/vector/reference/beam_1536.mojo:85-135) over a LinearPool
+ * of ef entries (src/common/heap.mojo:133-234), with the same lane formulas, prefix
+ * gate, tie order and pool discipline, so the pool equals the reference's entry for
+ * entry.  q fp32[nq x 1536]; out_ids [nq x k] are node_ids of the first min(k, pool
+ * size) pool entries (nearest first), out_dist their pool distances (squared L2 in
+ * code space); the rest are -1 / +inf.  ef in [1, 1024], k >= 1. */
+int pion_v_b200_hnsw_search(pion_b200_ctx *ctx, const pion_b200_index *index, const float *q,
+                            int64_t nq, int64_t k, int64_t ef, int32_t *out_ids, float *out_dist,
+                            int mem);
+
+/* Work counters of the context's last pion_v_b200_hnsw_search (waits for it):
+ * out3 = {level-0 distance evaluations, level-0 expansions, upper-level distance
+ * evaluations}, summed over the batch. */
+int pion_v_b200_hnsw_last_stats(pion_b200_ctx *ctx, int64_t *out3);
 
 #ifdef __cplusplus
 }

@@ -78,15 +78,47 @@ def lib() -> ctypes.CDLL:
                                            _p, _i32]
             L.orc_shard_merge_asc.argtypes = [_p, _p, _i64, _i64, _p, _p]
             L.orc_shard_merge_asc.restype = _i64
-            _bind_hnsw(L)
+            L.orc_hnsw_search.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p, _p, _i32]
+            L.orc_hnsw_search.restype = _i32
+            L.orc_hnsw_query_codes.argtypes = [_p, _p, _i64, _p]
             _lib = L
     return _lib
 
 
-def _bind_hnsw(L):
-    if not hasattr(L, "orc_hnsw_build"):
-        return
-    from . import hnsw as _h  # noqa: F401  (binds its own symbols lazily)
+class _HnswLayout(ctypes.Structure):
+    """orc_hnsw_layout (oracle/pion_oracle.h)."""
+    _fields_ = [
+        ("num_nodes", _i64), ("dim", _i64), ("M", _i64), ("entry_point", _i64),
+        ("max_level", _i64), ("global_min", _f32), ("global_max", _f32),
+        ("metric", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("compact_buffer", _p), ("compact_stride", _i64), ("compact_hdr", _i64),
+        ("l0_compact", _p), ("l0_slots", _p), ("node_slot", _p), ("node_ids", _p),
+        ("deleted", _p), ("node_level", _p), ("upper_offset", _p), ("upper_links", _p),
+        ("upper_rows", _i64),
+    ]
+
+
+_HNSW_ARRAYS = {"compact_buffer": np.int8, "l0_compact": np.uint32, "l0_slots": np.uint32,
+                "node_slot": np.uint32, "node_ids": np.int32, "node_level": np.int8,
+                "upper_offset": np.int64, "upper_links": np.uint32}
+_HNSW_SCALARS = ("num_nodes", "dim", "M", "entry_point", "max_level", "global_min",
+                 "global_max", "metric", "compact_stride", "compact_hdr", "upper_rows")
+
+
+def _hnsw_layout(g: dict):
+    lay = _HnswLayout()
+    keep = []
+    for name in _HNSW_SCALARS:
+        setattr(lay, name, g[name])
+    for name, dt in _HNSW_ARRAYS.items():
+        a, p = _c(g[name], dt)
+        keep.append(a)
+        setattr(lay, name, p if a.size else None)
+    if g.get("deleted") is not None:
+        a, p = _c(g["deleted"], np.uint8)
+        keep.append(a)
+        lay.deleted = p
+    return lay, keep
 
 
 def _c(a, dtype):
@@ -286,3 +318,37 @@ def shard_merge_asc(ids, scores, k: int):
     os_ = np.empty(max(1, k), np.float32)
     got = lib().orc_shard_merge_asc(pi, ps, n, k, oi.ctypes.data_as(_p), os_.ctypes.data_as(_p))
     return oi[:got], os_[:got]
+
+
+def hnsw_search(graph: dict, queries, k: int, ef: int, nthreads: int | None = None):
+    """search_fp32_scored at dim 1536 (src/vector/hnsw.mojo:4136-4521) over a graph in
+    the compact layout (a dict with the fields of pion_b200_hnsw_layout as numpy arrays
+    and scalars): upper-level greedy in code space (:3789-3848), then
+    beam_search_1536_ref (src/vector/reference/beam_1536.mojo:85-135) over a LinearPool
+    (src/common/heap.mojo:133-234).  Returns (ids int32 [nq, k], dist float32 [nq, k],
+    stats {evals, expansions, upper_evals})."""
+    L = lib()
+    lay, keep = _hnsw_layout(graph)
+    q, qp = _c(queries, np.float32)
+    nq = q.shape[0]
+    ids = np.empty((nq, k), np.int32)
+    dist = np.empty((nq, k), np.float32)
+    st = np.zeros(3, np.int64)
+    rc = L.orc_hnsw_search(ctypes.byref(lay), qp, nq, k, ef, ids.ctypes.data_as(_p),
+                           dist.ctypes.data_as(_p), st.ctypes.data_as(_p),
+                           nthreads or default_threads())
+    if rc != 0:
+        raise ValueError("orc_hnsw_search: layout not supported")
+    del keep
+    return ids, dist, {"evals": int(st[0]), "expansions": int(st[1]), "upper_evals": int(st[2])}
+
+
+def hnsw_query_codes(graph: dict, queries):
+    """The int8 codes _quantize_query_to_int8 gives each query (after the search's
+    normalisation), [nq, 1536]."""
+    L = lib()
+    lay, keep = _hnsw_layout(graph)
+    q, qp = _c(queries, np.float32)
+    out = np.empty(q.shape, np.int8)
+    L.orc_hnsw_query_codes(ctypes.byref(lay), qp, q.shape[0], out.ctypes.data_as(_p))
+    return out

@@ -1,0 +1,358 @@
+/*
+ * CPU oracle for the HNSW INT8 search at dim 1536 — TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of the reference's search over a compact graph, used by
+ * tests/ and bench.py's CPU leg as the checker.  Parity status: UNPINNED (the
+ * reference is Mojo; no golden vectors exist).  Restates, paths inside the
+ * pavelhorak/pion repository:
+ *   src/vector/hnsw.mojo:4136-4521     search_fp32_scored (the dim-1536 path)
+ *   src/vector/hnsw.mojo:657-680       _quantize_query_to_int8
+ *   src/vector/kernels.mojo:52-99      quantize_fp32_to_int8_simd (roundeven, clamp)
+ *   src/vector/kernels.mojo:318-357    l2_normalize_fp32
+ *   src/vector/hnsw.mojo:3789-3848     _upper_greedy_codes
+ *   src/vector/reference/beam_1536.mojo:30-135   beam_search_1536_ref, _gather
+ *   src/common/heap.mojo:133-234       LinearPool
+ */
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "pion_oracle.h"
+
+#define HN_DIM 1536
+#define HN_CHECKED 0x80000000u
+
+typedef struct {
+    float dist;
+    uint32_t id;
+} pool_entry;
+
+/* LinearPool (src/common/heap.mojo:133-234). */
+typedef struct {
+    pool_entry *e;
+    int64_t size, cursor, ef;
+} linear_pool;
+
+static void pool_reset(linear_pool *p, int64_t ef) {
+    p->ef = ef < 1 ? 1 : ef;
+    p->size = 0;
+    p->cursor = 0;
+}
+
+/* Accept-gated sorted insert; upper-bound position keeps equal distances in
+ * insertion order; the worst entry falls off a full pool. */
+static int pool_insert(linear_pool *p, float d, uint32_t id) {
+    if (p->size == p->ef && d >= p->e[p->size - 1].dist) return 0;
+    int64_t lo = 0, hi = p->size;
+    while (lo < hi) {
+        int64_t mid = (lo + hi) >> 1;
+        if (p->e[mid].dist > d)
+            hi = mid;
+        else
+            lo = mid + 1;
+    }
+    int64_t move_n = p->size - lo;
+    if (p->size == p->ef) move_n -= 1;
+    if (move_n > 0) memmove(p->e + lo + 1, p->e + lo, (size_t)move_n * sizeof(pool_entry));
+    p->e[lo].dist = d;
+    p->e[lo].id = id;
+    if (p->size < p->ef) p->size += 1;
+    if (lo < p->cursor) p->cursor = lo;
+    return 1;
+}
+
+static int pool_has_next(const linear_pool *p) { return p->cursor < p->size; }
+
+static uint32_t pool_pop(linear_pool *p) {
+    pool_entry e = p->e[p->cursor];
+    p->e[p->cursor].id = e.id | HN_CHECKED;
+    p->cursor += 1;
+    while (p->cursor < p->size && (p->e[p->cursor].id & HN_CHECKED) != 0) p->cursor += 1;
+    return e.id & ~HN_CHECKED;
+}
+
+static float pool_worst(const linear_pool *p) { return p->e[p->size - 1].dist; }
+
+/* _ref_dot / _ref_l2 (beam_1536.mojo:30-44): exact int32 sums. */
+static int32_t ref_dot(const int8_t *a, const int8_t *b, int n) {
+    int32_t s = 0;
+    for (int i = 0; i < n; ++i) s += (int32_t)a[i] * (int32_t)b[i];
+    return s;
+}
+
+static int32_t ref_l2(const int8_t *a, const int8_t *b, int n) {
+    int32_t s = 0;
+    for (int i = 0; i < n; ++i) {
+        int32_t d = (int32_t)a[i] - (int32_t)b[i];
+        s += d * d;
+    }
+    return s;
+}
+
+static int is_deleted(const orc_hnsw_layout *L, uint32_t i) {
+    return L->deleted && ((L->deleted[i >> 3] >> (i & 7)) & 1u);
+}
+
+static const int8_t *slot_vec(const orc_hnsw_layout *L, uint32_t slot) {
+    return L->compact_buffer + (int64_t)slot * L->compact_stride + L->compact_hdr;
+}
+
+/* Node norm^2 from the slot header (beam_1536.mojo:47-51). */
+static float slot_norm(const int8_t *v) {
+    float f;
+    memcpy(&f, v - 8, 4);
+    return f;
+}
+
+/* Normalise (COSINE, twice: search_fp32_scored, then _quantize_query_to_int8 again
+ * in place) and quantise: clamp(roundeven((x - gmin) * scale), 0, 254) - 127. */
+static void query_codes(const orc_hnsw_layout *L, const float *x, float *tmp, int8_t *q) {
+    const float *src = x;
+    if (L->metric == 1) {
+        orc_l2_normalize_fp32(x, tmp, HN_DIM);
+        orc_l2_normalize_fp32(tmp, tmp, HN_DIM);
+        src = tmp;
+    }
+    float range = L->global_max - L->global_min;
+    if (range <= 0.0f) range = 1.0f;
+    const float scale = 254.0f / range;
+    for (int i = 0; i < HN_DIM; ++i) {
+        const float norm = (src[i] - L->global_min) * scale;
+        long r = lrintf(norm);
+        if (r < 0) r = 0;
+        if (r > 254) r = 254;
+        q[i] = (int8_t)(r - 127);
+    }
+}
+
+void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
+                          int8_t *codes) {
+    float tmp[HN_DIM];
+    for (int64_t t = 0; t < nq; ++t)
+        query_codes(L, queries + t * HN_DIM, tmp, codes + t * HN_DIM);
+}
+
+struct hnsw_job {
+    const orc_hnsw_layout *L;
+    const float *queries;
+    int64_t k, ef;
+    int32_t *out_ids;
+    float *out_dist;
+    _Atomic int64_t evals, expansions, upper, bad;
+};
+
+/* Per-thread scratch: epoch, visited epochs, pool, fp32 and int8 query. */
+struct hnsw_scratch {
+    uint16_t epoch;
+    uint16_t *visited;
+    pool_entry *pool;
+    float *fq;
+    int8_t *q;
+};
+
+static size_t scratch_bytes(int64_t n, int64_t ef) {
+    /* the sizes scratch_bind lays out, each section rounded up to 64 bytes */
+    return 64 + ((size_t)n * 2 + 63) / 64 * 64 + 64 +
+           ((size_t)(ef < 1 ? 1 : ef) * sizeof(pool_entry) + 63) / 64 * 64 + 64 + HN_DIM * 4 +
+           64 + HN_DIM + 64;
+}
+
+static void scratch_bind(void *raw, int64_t n, int64_t ef, struct hnsw_scratch *s) {
+    char *p = (char *)raw;
+    uint16_t *epoch_cell = (uint16_t *)p;
+    p += 64;
+    s->epoch = *epoch_cell;
+    s->visited = (uint16_t *)p;
+    p += ((size_t)n * 2 + 63) / 64 * 64 + 64;
+    s->pool = (pool_entry *)p;
+    p += ((size_t)(ef < 1 ? 1 : ef) * sizeof(pool_entry) + 63) / 64 * 64 + 64;
+    s->fq = (float *)p;
+    p += HN_DIM * 4 + 64;
+    s->q = (int8_t *)p;
+}
+
+/* _gather (beam_1536.mojo:58-81): unvisited, undeleted level-0 neighbours of c in
+ * adjacency order, marked visited.  Returns -1 when a neighbour has no compact slot
+ * (the reference would fall back to the engine's node pointer). */
+static int gather(const orc_hnsw_layout *L, uint32_t c, uint16_t *visited, uint16_t epoch,
+                  uint32_t *idxs, const int8_t **ptrs) {
+    const uint32_t *row = L->l0_compact + (int64_t)c * 33;
+    const uint32_t *slots = L->l0_slots + (int64_t)c * 33;
+    const int count = (int)row[0];
+    int n = 0;
+    for (int i = 0; i < count && i < 32; ++i) {
+        const uint32_t nb = row[1 + i];
+        if (nb >= (uint32_t)L->num_nodes) continue;
+        if (is_deleted(L, nb)) continue;
+        if (visited[nb] == epoch) continue;
+        visited[nb] = epoch;
+        if (slots[1 + i] >= (uint32_t)L->num_nodes) return -1;
+        idxs[n] = nb;
+        ptrs[n] = slot_vec(L, slots[1 + i]);
+        n++;
+    }
+    return n;
+}
+
+static void hnsw_item(void *ctx, int64_t t, void *raw) {
+    struct hnsw_job *job = (struct hnsw_job *)ctx;
+    const orc_hnsw_layout *L = job->L;
+    struct hnsw_scratch s;
+    scratch_bind(raw, L->num_nodes, job->ef, &s);
+    int32_t *oid = job->out_ids + t * job->k;
+    float *od = job->out_dist + t * job->k;
+    for (int64_t i = 0; i < job->k; ++i) {
+        oid[i] = -1;
+        od[i] = INFINITY;
+    }
+    if (L->num_nodes == 0) return;
+    if (++s.epoch == 0) {
+        memset(s.visited, 0, (size_t)L->num_nodes * 2);
+        s.epoch = 1;
+    }
+    *(uint16_t *)raw = s.epoch;
+    query_codes(L, job->queries + t * HN_DIM, s.fq, s.q);
+    const int8_t *q = s.q;
+    int32_t qn_int = 0;
+    for (int i = 0; i < HN_DIM; ++i) qn_int += (int32_t)q[i] * (int32_t)q[i];
+    const float qn = (float)qn_int;
+    int64_t n_upper = 0, n_evals = 0, n_expand = 0;
+
+    /* _upper_greedy_codes: levels max_level..1, exact INT8 L2 on codes. */
+    uint32_t curr = (uint32_t)L->entry_point;
+    float curr_dist = (float)ref_l2(q, slot_vec(L, L->node_slot[curr]), HN_DIM);
+    n_upper++;
+    for (int64_t l = L->max_level; l > 0; --l) {
+        int changed = 1;
+        while (changed) {
+            changed = 0;
+            const uint32_t node = curr;
+            int nc = 0;
+            const uint32_t *lst = NULL;
+            const int64_t off = L->upper_offset[node];
+            if (off >= 0 && l <= L->node_level[node]) {
+                lst = L->upper_links + (off + l - 1) * (1 + L->M);
+                nc = (int)lst[0];
+                if (nc > L->M) nc = (int)L->M;
+            }
+            float best = curr_dist;
+            uint32_t best_idx = curr;
+            for (int i = 0; i < nc; ++i) {
+                const uint32_t nidx = lst[1 + i];
+                if (nidx >= (uint32_t)L->num_nodes) continue;
+                if (is_deleted(L, nidx)) continue;
+                const float d = (float)ref_l2(q, slot_vec(L, L->node_slot[nidx]), HN_DIM);
+                n_upper++;
+                if (d < best) {
+                    best = d;
+                    best_idx = nidx;
+                }
+            }
+            if (best_idx != curr) {
+                curr = best_idx;
+                curr_dist = best;
+                changed = 1;
+            }
+        }
+    }
+
+    /* Base level: mark the start visited, seed the pool with its INT8 distance. */
+    s.visited[curr] = s.epoch;
+    linear_pool pool;
+    pool.e = s.pool;
+    pool_reset(&pool, job->ef);
+    pool_insert(&pool, (float)ref_l2(q, slot_vec(L, L->node_slot[curr]), HN_DIM), curr);
+
+    uint32_t idxs[33];
+    const int8_t *ptrs[33];
+    /* Fill: expand the nearest unexpanded entry until the pool holds ef. */
+    while (pool_has_next(&pool) && pool.size < pool.ef) {
+        const uint32_t c = pool_pop(&pool);
+        n_expand++;
+        const int n = gather(L, c, s.visited, s.epoch, idxs, ptrs);
+        if (n < 0) {
+            job->bad++;
+            return;
+        }
+        n_evals += n;
+        const int batched = n - n % 4;
+        for (int j = 0; j < n; ++j) {
+            float d;
+            if (j < batched)
+                d = (qn + slot_norm(ptrs[j])) - 2.0f * (float)ref_dot(q, ptrs[j], HN_DIM);
+            else
+                d = (float)ref_l2(q, ptrs[j], HN_DIM);
+            pool_insert(&pool, d, idxs[j]);
+        }
+    }
+    /* Prune: expand until every pool entry is expanded. */
+    while (pool_has_next(&pool)) {
+        const uint32_t c = pool_pop(&pool);
+        n_expand++;
+        float worst = pool_worst(&pool);
+        const int n = gather(L, c, s.visited, s.epoch, idxs, ptrs);
+        if (n < 0) {
+            job->bad++;
+            return;
+        }
+        n_evals += n;
+        const int batched = n - n % 4;
+        for (int j = 0; j < n; ++j) {
+            const int8_t *p = ptrs[j];
+            if (j < batched) {
+                const float dot =
+                    (float)ref_dot(q, p, 256) + (float)ref_dot(q + 256, p + 256, 1280);
+                const float d = (qn + slot_norm(p)) - 2.0f * dot;
+                if (pool_insert(&pool, d, idxs[j])) worst = pool_worst(&pool);
+            } else {
+                const float d_prefix = (float)ref_l2(q, p, 256);
+                if (d_prefix < worst * 0.175f) {
+                    float running = d_prefix;
+                    int exited = 0;
+                    for (int b = 0; b < 5; ++b) {
+                        const int off = 256 + b * 256;
+                        running += (float)ref_l2(q + off, p + off, 256);
+                        if (running > worst) {
+                            exited = 1;
+                            break;
+                        }
+                    }
+                    if (!exited && running < worst) pool_insert(&pool, running, idxs[j]);
+                }
+            }
+        }
+    }
+    /* Drain: the first k entries, nearest first. */
+    const int64_t n_out = job->k < pool.size ? job->k : pool.size;
+    for (int64_t i = 0; i < n_out; ++i) {
+        oid[i] = L->node_ids[pool.e[i].id & ~HN_CHECKED];
+        od[i] = pool.e[i].dist;
+    }
+    job->evals += n_evals;
+    job->expansions += n_expand;
+    job->upper += n_upper;
+}
+
+int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, int64_t k,
+                    int64_t ef, int32_t *out_ids, float *out_dist, int64_t *stats3, int nthreads) {
+    if (L->dim != HN_DIM || k < 1 || ef < 1) return -1;
+    if (L->num_nodes > 0 && (L->entry_point < 0 || L->entry_point >= L->num_nodes)) return -1;
+    struct hnsw_job job;
+    job.L = L;
+    job.queries = queries;
+    job.k = k;
+    job.ef = ef;
+    job.out_ids = out_ids;
+    job.out_dist = out_dist;
+    job.evals = 0;
+    job.expansions = 0;
+    job.upper = 0;
+    job.bad = 0;
+    orc_parallel_for(nq, nthreads, scratch_bytes(L->num_nodes, ef), hnsw_item, &job);
+    if (stats3) {
+        stats3[0] += job.evals;
+        stats3[1] += job.expansions;
+        stats3[2] += job.upper;
+    }
+    return job.bad ? -1 : 0;
+}

@@ -23,7 +23,6 @@
 /* Query-level threading for the CPU baseline: a dynamic parallel-for over      */
 /* [0, n) with pthreads (one item at a time from an atomic counter).            */
 /* ------------------------------------------------------------------------- */
-typedef void (*orc_item_fn)(void *ctx, int64_t item, void *scratch);
 struct orc_pool_job {
     orc_item_fn fn;
     void *ctx;
@@ -33,7 +32,7 @@ struct orc_pool_job {
 };
 static void *orc_pool_worker(void *arg) {
     struct orc_pool_job *job = (struct orc_pool_job *)arg;
-    void *scratch = job->scratch_bytes ? malloc(job->scratch_bytes) : NULL;
+    void *scratch = job->scratch_bytes ? calloc(1, job->scratch_bytes) : NULL;
     for (;;) {
         int64_t i = atomic_fetch_add(&job->next, 1);
         if (i >= job->n) break;
@@ -42,8 +41,8 @@ static void *orc_pool_worker(void *arg) {
     free(scratch);
     return NULL;
 }
-static void orc_parallel_for(int64_t n, int nthreads, size_t scratch_bytes, orc_item_fn fn,
-                             void *ctx) {
+void orc_parallel_for(int64_t n, int nthreads, size_t scratch_bytes, orc_item_fn fn,
+                      void *ctx) {
     struct orc_pool_job job;
     job.fn = fn;
     job.ctx = ctx;

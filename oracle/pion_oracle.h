@@ -20,6 +20,7 @@
  */
 #ifndef PION_ORACLE_H
 #define PION_ORACLE_H
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -66,6 +67,39 @@ void orc_bq_knn_batch(const uint64_t *codes, const float *rows, int64_t n, int64
                       const float *queries, int64_t nq, int64_t shortlist, int64_t k,
                       int64_t *ids, float *scores, int32_t *short_ids, int32_t *short_dist,
                       int nthreads);
+
+/* ---- HNSW INT8 search (hnsw_oracle.c) ----------------------------------- */
+/* A graph in the reference's compact level-0 layout plus its upper levels
+ * (src/vector/hnsw.mojo:2761-2990, src/vector/beam_view.mojo:11-26). */
+typedef struct orc_hnsw_layout {
+    int64_t num_nodes, dim, M, entry_point, max_level;
+    float global_min, global_max;
+    int32_t metric, reserved;
+    const int8_t *compact_buffer;
+    int64_t compact_stride, compact_hdr;
+    const uint32_t *l0_compact, *l0_slots, *node_slot;
+    const int32_t *node_ids;
+    const uint8_t *deleted;
+    const int8_t *node_level;
+    const int64_t *upper_offset;
+    const uint32_t *upper_links;
+    int64_t upper_rows;
+} orc_hnsw_layout;
+
+/* search_fp32_scored at dim 1536 (src/vector/hnsw.mojo:4136-4521) per query:
+ * out_ids/out_dist [nq x k] (node_ids, pool distances; -1 / +inf past the pool),
+ * stats3 += {level-0 evaluations, expansions, upper-level evaluations}.
+ * Returns 0, or -1 on a layout the restatement cannot follow. */
+int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, int64_t k,
+                    int64_t ef, int32_t *out_ids, float *out_dist, int64_t *stats3, int nthreads);
+/* The query codes of _quantize_query_to_int8 (hnsw.mojo:657-680) after the search's
+ * normalisation: codes [nq x dim]. */
+void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
+                          int8_t *codes);
+
+/* ---- internal: dynamic parallel-for over [0, n) with per-thread zeroed scratch */
+typedef void (*orc_item_fn)(void *ctx, int64_t item, void *scratch);
+void orc_parallel_for(int64_t n, int nthreads, size_t scratch_bytes, orc_item_fn fn, void *ctx);
 
 /* ---- sharded merge ------------------------------------------------------- */
 int64_t orc_shard_merge_asc(const int64_t *ids, const float *scores, int64_t n_all, int64_t k,

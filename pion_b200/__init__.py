@@ -11,10 +11,13 @@ from .search import (  # noqa: F401
     Context,
     FlatF32Index,
     FlatI8Index,
+    HNSWGraph,
+    HNSWIndex,
     l2_normalize_rows,
     merge_topk,
     quantize_rows_i8,
 )
 
-__all__ = ["Context", "FlatI8Index", "FlatF32Index", "BQIndex", "quantize_rows_i8",
+__all__ = ["Context", "FlatI8Index", "FlatF32Index", "BQIndex", "HNSWGraph", "HNSWIndex",
+           "quantize_rows_i8",
            "l2_normalize_rows", "merge_topk", "PionError", "load"]

@@ -68,7 +68,30 @@ SIGNATURES = {
     "pion_v_b200_quantize_rows_i8": (_I, [_P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_l2_normalize_rows": (_I, [_P, _P, _I64, _I64, _P, _I]),
     "pion_v_b200_merge_topk": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _I]),
+    "pion_v_b200_hnsw_build": (_I, [_P, _I64, _I64, _I64, _I64, _I, _I64, _I, _PP]),
+    "pion_v_b200_hnsw_graph_layout": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_graph_stats": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_graph_free": (_I, [_P]),
+    "pion_v_b200_register_hnsw": (_I, [_P, _P, _PP]),
+    "pion_v_b200_hnsw_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_hnsw_last_stats": (_I, [_P, _P]),
 }
+
+
+class HnswLayout(ctypes.Structure):
+    """pion_b200_hnsw_layout (include/pion_vector_b200.h)."""
+    _fields_ = [
+        ("num_nodes", ctypes.c_int64), ("dim", ctypes.c_int64), ("M", ctypes.c_int64),
+        ("entry_point", ctypes.c_int64), ("max_level", ctypes.c_int64),
+        ("global_min", ctypes.c_float), ("global_max", ctypes.c_float),
+        ("metric", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("compact_buffer", ctypes.c_void_p), ("compact_stride", ctypes.c_int64),
+        ("compact_hdr", ctypes.c_int64), ("l0_compact", ctypes.c_void_p),
+        ("l0_slots", ctypes.c_void_p), ("node_slot", ctypes.c_void_p),
+        ("node_ids", ctypes.c_void_p), ("deleted", ctypes.c_void_p),
+        ("node_level", ctypes.c_void_p), ("upper_offset", ctypes.c_void_p),
+        ("upper_links", ctypes.c_void_p), ("upper_rows", ctypes.c_int64),
+    ]
 
 _lock = threading.Lock()
 _lib = None

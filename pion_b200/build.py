@@ -1,7 +1,9 @@
 """Build recipe for libpion_vector_b200.so (sm_100a only).
 
 Every ``.cu`` file under ``pion_b200/csrc`` is compiled with nvcc for
-``arch=compute_100a,code=sm_100a`` into ``pion_b200/_build/`` and linked into
+``arch=compute_100a,code=sm_100a``, and every ``.cpp`` file (host-only code: the
+HNSW graph builder) with the host C++ compiler, into ``pion_b200/_build/``; both are
+linked into
 ``pion_b200/libpion_vector_b200.so`` (in-tree, so the library ships with the
 repository snapshot).  The CUDA runtime is linked statically; the driver API is
 reached through ``cudaGetDriverEntryPoint`` so no ``-lcuda`` is needed.
@@ -28,6 +30,18 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2,-Wall",
               "-Xptxas", "-warn-spills", "--expt-relaxed-constexpr", "-I", INCLUDE]
 
 
+# Host-only sources: the HNSW builder's distance loops use AVX2 + FMA (the library
+# checks the CPU before calling into them).
+CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-mavx2", "-mfma", "-pthread"]
+
+
+def cxx() -> str:
+    for cand in (os.environ.get("CXX"), shutil.which("g++"), shutil.which("c++")):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("no host C++ compiler found")
+
+
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
         if cand and os.path.exists(cand):
@@ -36,7 +50,7 @@ def nvcc() -> str:
 
 
 def _sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
 
 def _headers():
@@ -54,10 +68,13 @@ def _compile(src: str, force: bool) -> str:
     if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(
             os.path.getmtime(src), _newest(_headers())):
         return obj
-    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", src, "-o", obj]
+    if src.endswith(".cpp"):
+        cmd = [cxx(), *CXX_FLAGS, "-c", src, "-o", obj]
+    else:
+        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
+        raise RuntimeError(f"compile failed on {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
     return obj
 
 

@@ -187,11 +187,13 @@ int pion_v_b200_shutdown(pion_b200_ctx* ctx) {
     if (!ctx) return PION_B200_EINVAL;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    DevBuf* bufs[] = {&ctx->scratch, &ctx->scratch2, &ctx->stage_in, &ctx->stage_out};
+    DevBuf* bufs[] = {&ctx->scratch,   &ctx->scratch2,     &ctx->stage_in,
+                      &ctx->stage_out, &ctx->hnsw_visited, &ctx->hnsw_misc};
     for (DevBuf* b : bufs)
         if (b->ptr) cudaFree(b->ptr);
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->h_status) cudaFreeHost(ctx->h_status);
+    if (ctx->switch_ev) cudaEventDestroy(ctx->switch_ev);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     for (cudaEvent_t e : ctx->ev_start) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->ev_end) cudaEventDestroy(e);
@@ -201,7 +203,19 @@ int pion_v_b200_shutdown(pion_b200_ctx* ctx) {
 
 int pion_v_b200_set_stream(pion_b200_ctx* ctx, void* cuda_stream) {
     if (!valid_ctx(ctx)) return PION_B200_EINVAL;
-    ctx->stream = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : ctx->own_stream;
+    cudaStream_t next = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : ctx->own_stream;
+    if (next != ctx->stream) {
+        // The context's scratch is shared by both streams: work queued from now on waits
+        // for everything already queued on the previous stream.
+        if (int rc = use_device(ctx)) return rc;
+        if (!ctx->switch_ev &&
+            cudaEventCreateWithFlags(&ctx->switch_ev, cudaEventDisableTiming) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "set_stream: event create failed");
+        if (cudaEventRecord(ctx->switch_ev, ctx->stream) != cudaSuccess ||
+            cudaStreamWaitEvent(next, ctx->switch_ev, 0) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "set_stream: stream ordering failed");
+    }
+    ctx->stream = next;
     return 0;
 }
 
@@ -271,6 +285,13 @@ int pion_v_b200_index_free(pion_b200_index* index) {
     if (index->rows_hi) cudaFree(index->rows_hi);
     if (index->rows_lo) cudaFree(index->rows_lo);
     if (index->codes) cudaFree(index->codes);
+    void* hn[] = {index->hnsw.codes,      index->hnsw.norms,        index->hnsw.l0_compact,
+                  index->hnsw.l0_slots,
+                  index->hnsw.node_slot,  index->hnsw.node_ids,     index->hnsw.deleted,
+                  index->hnsw.node_level, index->hnsw.upper_offset, index->hnsw.upper_links,
+                  index->hnsw.upper_slots};
+    for (void* p : hn)
+        if (p) cudaFree(p);
     delete index;
     return 0;
 }

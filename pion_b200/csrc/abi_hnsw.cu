@@ -1,0 +1,370 @@
+// C-ABI for HNSW: the host builder (hnsw_build.cpp), device registration of a graph in
+// the reference's compact layout, and the batched beam search (hnsw.cu).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <new>
+#include <thread>
+#include <vector>
+
+#include "hnsw_host.h"
+#include "internal.h"
+
+struct pion_b200_hnsw_graph {
+    pion::hnsw::Graph g;
+    pion::hnsw::BuildStats stats;
+};
+
+using namespace pion;
+
+namespace {
+
+template <typename T>
+int upload(T** dst, const T* src, size_t count) {
+    *dst = nullptr;
+    if (count == 0) return 0;
+    if (cudaMalloc(reinterpret_cast<void**>(dst), count * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        *dst = nullptr;
+        return PION_B200_ENOMEM;
+    }
+    if (cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess)
+        return PION_B200_ECUDA;
+    return 0;
+}
+
+// Structural checks the beam kernel relies on; returns a message or nullptr.
+const char* check_layout(const pion_b200_hnsw_layout* L) {
+    const int64_t n = L->num_nodes;
+    if (n < 0 || n >= (int64_t)0x7fffffff) return "num_nodes out of range";
+    if (L->dim != hnsw_dim()) return "dim must be 1536";
+    if (L->M < 1 || 2 * L->M > 32) return "M must be in [1, 16]";
+    if (L->compact_hdr != 8) return "compact_hdr must be 8";
+    if (L->compact_stride % 16 != 0 || L->compact_stride < L->compact_hdr + L->dim + 8)
+        return "compact_stride must be a multiple of 16 and >= dim + 16";
+    if (L->metric != 0 && L->metric != 1) return "metric must be 0 (L2) or 1 (COSINE)";
+    if (n == 0) return nullptr;
+    if (!L->compact_buffer || !L->l0_compact || !L->l0_slots || !L->node_slot || !L->node_ids ||
+        !L->node_level || !L->upper_offset)
+        return "null layout buffer";
+    if (L->entry_point < 0 || L->entry_point >= n) return "entry_point out of range";
+    if (L->max_level < 0 || L->max_level > 64) return "max_level out of range";
+    if (L->upper_rows < 0 || (L->upper_rows > 0 && !L->upper_links)) return "bad upper_links";
+    auto deleted = [&](uint32_t i) {
+        return L->deleted && ((L->deleted[i >> 3] >> (i & 7)) & 1u);
+    };
+    for (int64_t i = 0; i < n; ++i) {
+        if (L->node_slot[i] >= (uint64_t)n) return "node_slot out of range";
+        const int64_t off = L->upper_offset[i];
+        const int lv = L->node_level[i];
+        if (lv < 0) return "negative node_level";
+        if (off >= 0 && off + lv > L->upper_rows) return "upper_offset out of range";
+        const uint32_t* row = L->l0_compact + i * 33;
+        const uint32_t* srow = L->l0_slots + i * 33;
+        const uint32_t c = row[0] < 32 ? row[0] : 32;
+        for (uint32_t k = 0; k < c; ++k) {
+            const uint32_t nb = row[1 + k];
+            if (nb < (uint32_t)n && !deleted(nb) && srow[1 + k] >= (uint32_t)n)
+                return "l0_slots entry out of range";
+        }
+    }
+    return nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pion_v_b200_hnsw_build(const float* rows, int64_t n_rows, int64_t dim, int64_t M,
+                           int64_t ef_construction, int metric, int64_t id_base, int n_threads,
+                           pion_b200_hnsw_graph** out_graph) {
+    if (!out_graph) return PION_B200_EINVAL;
+    *out_graph = nullptr;
+    if (n_rows < 0 || (n_rows > 0 && !rows) || dim <= 0 || M < 2 || M > 16 ||
+        ef_construction < 1 || (metric != 0 && metric != 1) || id_base < 0 ||
+        n_rows + id_base > INT32_MAX || n_rows >= 0x7fffffff) {
+        fprintf(stderr, "pion_vector_b200: hnsw_build: bad arguments\n");
+        return PION_B200_EINVAL;
+    }
+    __builtin_cpu_init();
+    if (!__builtin_cpu_supports("avx2") || !__builtin_cpu_supports("fma")) {
+        fprintf(stderr, "pion_vector_b200: hnsw_build needs a CPU with AVX2 and FMA\n");
+        return PION_B200_ESHAPE;
+    }
+    if (n_threads <= 0) n_threads = (int)std::thread::hardware_concurrency();
+    if (n_threads <= 0) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pion_b200_hnsw_graph* g = new (std::nothrow) pion_b200_hnsw_graph();
+    if (!g) return PION_B200_ENOMEM;
+    try {
+        hnsw::build(rows, n_rows, dim, M, ef_construction, metric, id_base, n_threads, g->g,
+                    &g->stats);
+    } catch (const std::bad_alloc&) {
+        delete g;
+        return PION_B200_ENOMEM;
+    }
+    *out_graph = g;
+    return 0;
+}
+
+int pion_v_b200_hnsw_graph_layout(const pion_b200_hnsw_graph* graph, pion_b200_hnsw_layout* out) {
+    if (!graph || !out) return PION_B200_EINVAL;
+    const hnsw::Graph& g = graph->g;
+    *out = pion_b200_hnsw_layout{};
+    out->num_nodes = g.n;
+    out->dim = g.dim;
+    out->M = g.M;
+    out->entry_point = g.entry;
+    out->max_level = g.max_level < 0 ? 0 : g.max_level;
+    out->global_min = g.gmin;
+    out->global_max = g.gmax;
+    out->metric = g.metric;
+    out->compact_buffer = g.compact.data();
+    out->compact_stride = g.stride;
+    out->compact_hdr = g.hdr;
+    out->l0_compact = g.l0_compact.data();
+    out->l0_slots = g.l0_slots.data();
+    out->node_slot = g.node_slot.data();
+    out->node_ids = g.node_ids.data();
+    out->deleted = nullptr;
+    out->node_level = g.level.data();
+    out->upper_offset = g.upper_offset.data();
+    out->upper_links = g.upper_links.data();
+    out->upper_rows = g.upper_rows;
+    return 0;
+}
+
+int pion_v_b200_hnsw_graph_stats(const pion_b200_hnsw_graph* graph, int64_t* out5) {
+    if (!graph || !out5) return PION_B200_EINVAL;
+    out5[0] = graph->stats.lanes;
+    out5[1] = graph->stats.link_drops;
+    out5[2] = graph->stats.relinked;
+    out5[3] = graph->stats.repaired_exits;
+    out5[4] = graph->stats.repaired_links;
+    return 0;
+}
+
+int pion_v_b200_hnsw_graph_free(pion_b200_hnsw_graph* graph) {
+    if (!graph) return PION_B200_EINVAL;
+    delete graph;
+    return 0;
+}
+
+int pion_v_b200_register_hnsw(pion_b200_ctx* ctx, const pion_b200_hnsw_layout* L,
+                              pion_b200_index** out_index) {
+    if (!valid_ctx(ctx) || !out_index || !L) return PION_B200_EINVAL;
+    *out_index = nullptr;
+    if (const char* why = check_layout(L))
+        return set_error(ctx, PION_B200_EINVAL, "register_hnsw: %s", why);
+    if (int rc = use_device(ctx)) return rc;
+    pion_b200_index* ix = new (std::nothrow) pion_b200_index();
+    if (!ix) return set_error(ctx, PION_B200_ENOMEM, "register_hnsw: out of host memory");
+    ix->kind = kHNSW;
+    ix->device = ctx->device;
+    ix->n_rows = L->num_nodes;
+    ix->dim = L->dim;
+    auto& h = ix->hnsw;
+    h.M = (int)L->M;
+    h.max_level = (int)L->max_level;
+    h.entry = L->entry_point;
+    h.metric = L->metric;
+    h.gmin = L->global_min;
+    h.gmax = L->global_max;
+    const size_t n = (size_t)L->num_nodes;
+    int rc = 0;
+    if (n > 0) {
+        // the slot buffer travels once, then is re-laid out on the device as 16-byte
+        // aligned code rows plus a norm array
+        int8_t* slots = nullptr;
+        rc = upload(&slots, L->compact_buffer, n * (size_t)L->compact_stride);
+        if (!rc && (cudaMalloc(&h.codes, n * (size_t)hnsw_dim()) != cudaSuccess ||
+                    cudaMalloc(&h.norms, n * sizeof(float)) != cudaSuccess)) {
+            cudaGetLastError();
+            rc = PION_B200_ENOMEM;
+        }
+        if (!rc)
+            rc = launch_hnsw_relayout(slots, (int64_t)n, L->compact_stride, L->compact_hdr,
+                                      h.codes, h.norms, ctx->stream);
+        if (!rc && cudaStreamSynchronize(ctx->stream) != cudaSuccess) rc = PION_B200_ECUDA;
+        if (slots) cudaFree(slots);
+        if (!rc) rc = upload(&h.l0_compact, L->l0_compact, n * 33);
+        if (!rc) rc = upload(&h.l0_slots, L->l0_slots, n * 33);
+        if (!rc) rc = upload(&h.node_slot, L->node_slot, n);
+        if (!rc) rc = upload(&h.node_ids, L->node_ids, n);
+        if (!rc) rc = upload(&h.node_level, L->node_level, n);
+        if (!rc) rc = upload(&h.upper_offset, L->upper_offset, n);
+        if (!rc && L->upper_rows > 0) {
+            const size_t words = (size_t)L->upper_rows * (1 + L->M);
+            rc = upload(&h.upper_links, L->upper_links, words);
+            // the slots of the upper-level neighbours, so the greedy descent finds a
+            // neighbour's codes without a dependent load
+            std::vector<uint32_t> us(words, 0xffffffffu);
+            for (size_t r = 0; r < (size_t)L->upper_rows; ++r) {
+                const uint32_t* row = L->upper_links + r * (1 + L->M);
+                us[r * (1 + L->M)] = row[0];
+                for (int64_t k = 0; k < L->M; ++k)
+                    if (row[1 + k] < (uint32_t)n) us[r * (1 + L->M) + 1 + k] = L->node_slot[row[1 + k]];
+            }
+            if (!rc) rc = upload(&h.upper_slots, us.data(), words);
+        }
+        if (!rc && L->deleted) rc = upload(&h.deleted, L->deleted, (n + 7) / 8);
+    }
+    if (rc) {
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, rc, "register_hnsw: device copy failed");
+    }
+    *out_index = ix;
+    return 0;
+}
+
+int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const float* q,
+                            int64_t nq, int64_t k, int64_t ef, int32_t* out_ids, float* out_dist,
+                            int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kHNSW) return set_error(ctx, PION_B200_EINVAL, "hnsw_search: not an HNSW index");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_search: index on another device");
+    if (nq < 0 || k < 1 || (nq > 0 && (!q || !out_ids || !out_dist)))
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_search: bad arguments");
+    if (ef < 1 || ef > 1024)
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_search: ef %lld not in [1, 1024]",
+                         (long long)ef);
+    if (nq > (1 << 24) || k > (1 << 16))
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_search: batch or k too large");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_search: bad mem %d", mem);
+    if (nq == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const int dim = hnsw_dim();
+    const auto& h = ix->hnsw;
+    const size_t out_bytes = (size_t)nq * k * 4;
+    const float* dq = q;
+    int32_t* di = out_ids;
+    float* dv = out_dist;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, (size_t)nq * dim * 4) != 0 ||
+            ensure(ctx->stage_out, 2 * align_up(out_bytes, 256)) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_search: staging");
+        if (cudaMemcpyAsync(ctx->stage_in.ptr, q, (size_t)nq * dim * 4, cudaMemcpyHostToDevice,
+                            st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_search: query copy failed");
+        dq = static_cast<const float*>(ctx->stage_in.ptr);
+        di = static_cast<int32_t*>(ctx->stage_out.ptr);
+        dv = reinterpret_cast<float*>(static_cast<char*>(ctx->stage_out.ptr) +
+                                      align_up(out_bytes, 256));
+    }
+    if (ensure(ctx->hnsw_misc, 64) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "hnsw_search: counters");
+    unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
+    unsigned* next_query = reinterpret_cast<unsigned*>(stats + 3);
+    if (cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 32, st) != cudaSuccess)
+        return set_error(ctx, PION_B200_ECUDA, "hnsw_search: memset failed");
+    int rc = 0;
+    if (ix->n_rows == 0) {
+        rc = launch_fill_results(dv, di, (size_t)nq * k, INFINITY, st);
+        ctx->launches++;
+    } else {
+        const int per_sm = hnsw_ctas_per_sm((int)ef);
+        if (per_sm <= 0)
+            return set_error(ctx, PION_B200_ESHAPE, "hnsw_search: ef %lld does not fit",
+                             (long long)ef);
+        const int warps = hnsw_warps_per_cta();
+        int64_t ctas = (int64_t)per_sm * ctx->num_sms;
+        const int64_t need = (nq + warps - 1) / warps;
+        if (ctas > need) ctas = need;
+        const int64_t vis_words = ((ix->n_rows + 31) / 32 + 3) / 4 * 4;
+        if (ensure(ctx->hnsw_visited, (size_t)ctas * warps * vis_words * 4) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_search: visited bitmaps");
+        size_t off = 0;
+        auto take = [&](size_t bytes) {
+            size_t o = off;
+            off += align_up(bytes, 256);
+            return o;
+        };
+        const size_t o_qn = take(h.metric == 1 ? (size_t)nq * dim * 4 : 0),
+                     o_codes = take((size_t)nq * dim), o_blk = take((size_t)nq * 8 * 4);
+        if (ensure(ctx->scratch, off) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_search: scratch");
+        char* base = static_cast<char*>(ctx->scratch.ptr);
+        const float* qsrc = dq;
+        if (h.metric == 1) {
+            // search_fp32_scored normalises the query, then _quantize_query_to_int8
+            // normalises that result again in place (hnsw.mojo:4146-4149, :669-671).
+            float* qn = reinterpret_cast<float*>(base + o_qn);
+            rc = launch_l2_normalize_rows(dq, nq, dim, qn, nullptr, st);
+            if (!rc) rc = launch_l2_normalize_rows(qn, nq, dim, qn, nullptr, st);
+            ctx->launches += 2;
+            qsrc = qn;
+        }
+        float range = h.gmax - h.gmin;
+        if (range <= 0.0f) range = 1.0f;
+        const float scale = 254.0f / range;
+        int8_t* codes = reinterpret_cast<int8_t*>(base + o_codes);
+        int32_t* blk = reinterpret_cast<int32_t*>(base + o_blk);
+        if (!rc) rc = launch_hnsw_quantize(qsrc, (int)nq, h.gmin, scale, codes, blk, st);
+        ctx->launches++;
+        if (!rc) {
+            HnswLaunch Lc;
+            Lc.codes = h.codes;
+            Lc.norms = h.norms;
+            Lc.l0_compact = h.l0_compact;
+            Lc.l0_slots = h.l0_slots;
+            Lc.node_slot = h.node_slot;
+            Lc.node_ids = h.node_ids;
+            Lc.deleted = h.deleted;
+            Lc.node_level = h.node_level;
+            Lc.upper_offset = h.upper_offset;
+            Lc.upper_links = h.upper_links;
+            Lc.upper_slots = h.upper_slots;
+            Lc.M = h.M;
+            Lc.max_level = h.max_level;
+            Lc.num_nodes = ix->n_rows;
+            Lc.entry = h.entry;
+            Lc.qcodes = codes;
+            Lc.qblk = blk;
+            Lc.nq = (int)nq;
+            Lc.k = (int)k;
+            Lc.ef = (int)ef;
+            Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+            Lc.vis_words = vis_words;
+            Lc.out_ids = di;
+            Lc.out_dist = dv;
+            Lc.stats = stats;
+            Lc.next_query = next_query;
+            Lc.status = ctx->d_status;
+            Lc.ctas = (int)ctas;
+            timing_begin(ctx);
+            rc = launch_hnsw_beam(Lc, st);
+            timing_end(ctx);
+            ctx->launches++;
+        }
+    }
+    if (rc != 0)
+        return set_error(ctx, rc, "hnsw_search: launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(out_ids, di, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_dist, dv, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_search: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+int pion_v_b200_hnsw_last_stats(pion_b200_ctx* ctx, int64_t* out3) {
+    if (!valid_ctx(ctx) || !out3) return PION_B200_EINVAL;
+    out3[0] = out3[1] = out3[2] = 0;
+    if (!ctx->hnsw_misc.ptr) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    unsigned long long v[3];
+    if (cudaMemcpyAsync(v, ctx->hnsw_misc.ptr, sizeof(v), cudaMemcpyDeviceToHost, ctx->stream) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        return set_error(ctx, PION_B200_ECUDA, "hnsw_last_stats: copy failed");
+    for (int i = 0; i < 3; ++i) out3[i] = (int64_t)v[i];
+    return 0;
+}
+
+}  // extern "C"

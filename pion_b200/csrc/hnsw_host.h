@@ -1,0 +1,46 @@
+// Host-side HNSW graph in the reference's compact level-0 layout (the buffers that
+// src/vector/hnsw.mojo:2761-2990 builds and src/vector/beam_view.mojo:11-26 hands to
+// the beam), plus the upper levels.  Built by hnsw_build.cpp.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+namespace pion {
+namespace hnsw {
+
+struct Graph {
+    int64_t n = 0, dim = 0, M = 0, efc = 0, id_base = 0;
+    int metric = 0;  // 0 = L2, 1 = COSINE
+    float gmin = 0.0f, gmax = 0.0f;
+    int64_t entry = -1;
+    int max_level = -1;
+    std::vector<int8_t> level;  // per node
+    std::vector<int8_t> codes;  // n x dim in node order (released after compaction)
+    // compact layout
+    int64_t stride = 0, hdr = 8;
+    std::vector<int8_t> compact;          // n x stride, BFS slot order
+    std::vector<uint32_t> l0_compact;     // n x 33: count, <= 32 level-0 neighbour nodes
+    std::vector<uint32_t> l0_slots;       // n x 33: count, their compact slots
+    std::vector<uint32_t> node_slot;      // n
+    std::vector<int32_t> node_ids;        // n: external id of each node
+    std::vector<int64_t> upper_offset;    // n: first upper row of the node, -1 at level 0
+    std::vector<uint32_t> upper_links;    // rows of (1 + M): count, <= M neighbour nodes
+    int64_t upper_rows = 0;
+};
+
+struct BuildStats {
+    int64_t lanes = 0;
+    int64_t link_drops = 0;
+    int64_t relinked = 0;
+    int64_t repaired_exits = 0;
+    int64_t repaired_links = 0;
+};
+
+// Builds the graph of n rows (fp32, n x dim, normalised first under COSINE) with the
+// reference's parameters; node i gets external id id_base + i.  n_threads link lanes.
+int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
+          int64_t id_base, int n_threads, Graph& g, BuildStats* stats);
+
+}  // namespace hnsw
+}  // namespace pion

@@ -19,7 +19,7 @@ struct DevBuf {
     size_t bytes = 0;
 };
 
-enum IndexKind { kFlatI8 = 1, kFlatF32 = 2, kBQ = 3 };
+enum IndexKind { kFlatI8 = 1, kFlatF32 = 2, kBQ = 3, kHNSW = 4 };
 
 // ---- flat_f32.cu
 int ff32_tile_rows();
@@ -78,8 +78,11 @@ struct pion_b200_ctx {
     pion::DevBuf scratch2;         // second-level scratch (merges, shortlists)
     pion::DevBuf stage_in;         // device copies of host inputs
     pion::DevBuf stage_out;        // device outputs copied back to host
+    pion::DevBuf hnsw_visited;     // HNSW visited bitmaps, one per resident warp
+    pion::DevBuf hnsw_misc;        // HNSW work counters and query counter
     std::string last_error;
     int64_t launches = 0;
+    cudaEvent_t switch_ev = nullptr;  // orders scratch use across set_stream switches
     // scoring-kernel timing (pion_v_b200_timing_*)
     bool timing = false;
     std::vector<cudaEvent_t> ev_start, ev_end;
@@ -108,9 +111,67 @@ struct pion_b200_index {
     int64_t words = 0;
     CUtensorMap tmap_rows;
     bool has_tmap = false;
+    // HNSW: the compact level-0 layout and the upper levels, on the device
+    struct {
+        int8_t* codes = nullptr;  // [slot][1536], 16-byte aligned
+        float* norms = nullptr;   // [slot]: the slot header's |code|^2
+        uint32_t* l0_compact = nullptr;
+        uint32_t* l0_slots = nullptr;
+        uint32_t* node_slot = nullptr;
+        int32_t* node_ids = nullptr;
+        uint8_t* deleted = nullptr;
+        int8_t* node_level = nullptr;
+        int64_t* upper_offset = nullptr;
+        uint32_t* upper_links = nullptr;
+        uint32_t* upper_slots = nullptr;
+        int M = 0;
+        int max_level = 0;
+        int64_t entry = -1;
+        int metric = 0;
+        float gmin = 0.0f, gmax = 0.0f;
+    } hnsw;
 };
 
 namespace pion {
+
+// ---- hnsw.cu
+struct HnswLaunch {
+    const int8_t* codes = nullptr;  // [slot][1536]
+    const float* norms = nullptr;   // [slot]
+    const uint32_t* l0_compact = nullptr;
+    const uint32_t* l0_slots = nullptr;
+    const uint32_t* node_slot = nullptr;
+    const int32_t* node_ids = nullptr;
+    const uint8_t* deleted = nullptr;
+    const int8_t* node_level = nullptr;
+    const int64_t* upper_offset = nullptr;
+    const uint32_t* upper_links = nullptr;
+    const uint32_t* upper_slots = nullptr;
+    int M = 0;
+    int max_level = 0;
+    int64_t num_nodes = 0;
+    int64_t entry = 0;
+    const int8_t* qcodes = nullptr;
+    const int32_t* qblk = nullptr;
+    int nq = 0, k = 0, ef = 0;
+    uint32_t* visited = nullptr;
+    int64_t vis_words = 0;
+    int32_t* out_ids = nullptr;
+    float* out_dist = nullptr;
+    unsigned long long* stats = nullptr;
+    unsigned* next_query = nullptr;
+    int* status = nullptr;
+    int ctas = 0;
+};
+int hnsw_dim();
+int hnsw_warps_per_cta();
+size_t hnsw_warp_smem(int ef);
+int hnsw_ctas_per_sm(int ef);
+int launch_hnsw_quantize(const float* q, int nq, float gmin, float scale, int8_t* codes,
+                         int32_t* blk, cudaStream_t st);
+int launch_hnsw_beam(const HnswLaunch& launch, cudaStream_t st);
+int launch_hnsw_relayout(const int8_t* src, int64_t n, int64_t stride, int64_t hdr,
+                         int8_t* codes, float* norms, cudaStream_t st);
 
 // ---- shared ABI helpers (abi.cu)
 int set_error(pion_b200_ctx* ctx, int code, const char* fmt, ...);

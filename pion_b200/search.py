@@ -10,7 +10,11 @@ Mirrors the operator surface of Pion's vector path (pavelhorak/pion):
   (ref_pkm_scores_i8 + ref_pkm_topk_max per query);
 * ``FlatF32Index.search`` — batched ``exact_knn`` under COSINE
   (src/commands/vector.mojo:1228-1365);
-* ``BQIndex.search`` — sign-bit Hamming shortlist + exact cosine rerank.
+* ``BQIndex.search`` — sign-bit Hamming shortlist + exact cosine rerank;
+* ``HNSWGraph`` — the reference's FT.OPTIMIZE graph build on the host CPU
+  (src/vector/hnsw.mojo:2540-2620) into its compact level-0 layout;
+* ``HNSWIndex.search`` — batched ``search_fp32_scored`` at dim 1536: upper-level
+  greedy descent, then ``beam_search_1536_ref`` per query on the GPU.
 
 Arrays may be numpy (host memory: the call copies to and from the GPU) or CUDA
 torch tensors (device memory: used in place on the context's stream).  Errors
@@ -322,3 +326,132 @@ def merge_topk(ctx: Context, cand_scores, cand_ids, k: int, descending: bool = T
         ctx.check(ctx.lib.pion_v_b200_merge_topk(ctx.h, pv, pi, nq, n_lists, k, flags, po_v,
                                                  po_i, mem))
     return ids, sc
+
+
+# -------------------------------------------------------------------- HNSW --
+
+_LAYOUT_ARRAYS = {
+    # name: (dtype, shape from (n, stride, M, upper_rows))
+    "compact_buffer": (np.int8, lambda n, st, m, ur: (n, st)),
+    "l0_compact": (np.uint32, lambda n, st, m, ur: (n, 33)),
+    "l0_slots": (np.uint32, lambda n, st, m, ur: (n, 33)),
+    "node_slot": (np.uint32, lambda n, st, m, ur: (n,)),
+    "node_ids": (np.int32, lambda n, st, m, ur: (n,)),
+    "node_level": (np.int8, lambda n, st, m, ur: (n,)),
+    "upper_offset": (np.int64, lambda n, st, m, ur: (n,)),
+    "upper_links": (np.uint32, lambda n, st, m, ur: (ur, 1 + m)),
+}
+_LAYOUT_SCALARS = ("num_nodes", "dim", "M", "entry_point", "max_level", "global_min",
+                   "global_max", "metric", "compact_stride", "compact_hdr", "upper_rows")
+
+
+def hnsw_layout_struct(arrays: dict):
+    """(pion_b200_hnsw_layout, keep-alive list) from a dict of numpy arrays and scalars
+    (the keys of HNSWGraph.arrays(); "deleted" optional)."""
+    lay = _lib.HnswLayout()
+    keep = []
+    for name in _LAYOUT_SCALARS:
+        setattr(lay, name, arrays[name])
+    for name, (dt, _) in _LAYOUT_ARRAYS.items():
+        a = np.ascontiguousarray(arrays[name], dtype=dt)
+        keep.append(a)
+        setattr(lay, name, a.ctypes.data if a.size else None)
+    dele = arrays.get("deleted")
+    if dele is not None:
+        d = np.ascontiguousarray(dele, dtype=np.uint8)
+        keep.append(d)
+        lay.deleted = d.ctypes.data
+    return lay, keep
+
+
+class HNSWGraph:
+    """An HNSW INT8 graph built on the host CPU as the reference's FT.OPTIMIZE builds
+    it (calibrate, quantize, parallel link lanes, relink and level-0 repair, compact),
+    held by the library in the compact level-0 layout.
+
+    rows: float32 [n, dim] host array.  metric: "cosine" (rows and queries are
+    unit-normalised) or "l2".  threads <= 0 uses every online CPU; one thread builds
+    the same graph every time."""
+
+    def __init__(self, rows, M: int = 16, ef_construction: int = 200, metric: str = "cosine",
+                 id_base: int = 0, threads: int = 0):
+        self.lib = _lib.load()
+        a = np.ascontiguousarray(rows, dtype=np.float32)
+        h = ctypes.c_void_p()
+        rc = self.lib.pion_v_b200_hnsw_build(a.ctypes.data, a.shape[0], a.shape[1], M,
+                                             ef_construction, 1 if metric == "cosine" else 0,
+                                             id_base, threads, ctypes.byref(h))
+        if rc != 0:
+            raise PionError(rc, "hnsw_build failed")
+        self.h = h
+        self.layout = _lib.HnswLayout()
+        self.lib.pion_v_b200_hnsw_graph_layout(self.h, ctypes.byref(self.layout))
+
+    def stats(self) -> dict:
+        """lanes, link_drops, relinked, repaired_exits, repaired_links."""
+        out = (ctypes.c_int64 * 5)()
+        self.lib.pion_v_b200_hnsw_graph_stats(self.h, out)
+        return dict(zip(("lanes", "link_drops", "relinked", "repaired_exits",
+                         "repaired_links"), list(out)))
+
+    def arrays(self) -> dict:
+        """The layout as numpy views of the library's buffers (valid while the graph
+        lives) plus its scalars."""
+        L = self.layout
+        n, st, m, ur = L.num_nodes, L.compact_stride, L.M, L.upper_rows
+        out = {name: getattr(L, name) for name in _LAYOUT_SCALARS}
+        ctype = {np.int8: ctypes.c_int8, np.uint32: ctypes.c_uint32, np.int32: ctypes.c_int32,
+                 np.int64: ctypes.c_int64}
+        for name, (dt, shape_of) in _LAYOUT_ARRAYS.items():
+            shape = shape_of(n, st, m, ur)
+            ptr = getattr(L, name)
+            if not ptr or int(np.prod(shape)) == 0:
+                out[name] = np.zeros(shape, dt)
+                continue
+            cp = ctypes.cast(ptr, ctypes.POINTER(ctype[dt]))
+            out[name] = np.ctypeslib.as_array(cp, shape=shape)
+        out["deleted"] = None
+        return out
+
+    def free(self):
+        if getattr(self, "h", None):
+            self.lib.pion_v_b200_hnsw_graph_free(self.h)
+            self.h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class HNSWIndex(_Index):
+    """An HNSW graph copied to the GPU: batched search_fp32_scored at dim 1536."""
+
+    def __init__(self, ctx: Context, graph):
+        if isinstance(graph, HNSWGraph):
+            lay, keep = graph.layout, [graph]
+        else:
+            lay, keep = hnsw_layout_struct(graph)
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.pion_v_b200_register_hnsw(ctx.h, ctypes.byref(lay), ctypes.byref(h)))
+        super().__init__(ctx, h)
+        self.dim = lay.dim
+
+    def search(self, q, k: int, ef: int):
+        """q float32 [nq, 1536] -> (node ids int32 [nq, k], pool distances float32)."""
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        nq = q.shape[0]
+        ids, dist, pi, pv = _outputs(mem == MEM_DEVICE, nq, k,
+                                     q.device if mem == MEM_DEVICE else None)
+        with _TorchStream(self.ctx, mem):
+            self.ctx.check(self.ctx.lib.pion_v_b200_hnsw_search(self.ctx.h, self.h, pq, nq, k,
+                                                                ef, pi, pv, mem))
+        return ids, dist
+
+    def last_stats(self) -> dict:
+        """Work of the context's last search: level-0 evaluations, expansions, upper-level
+        evaluations."""
+        out = (ctypes.c_int64 * 3)()
+        self.ctx.check(self.ctx.lib.pion_v_b200_hnsw_last_stats(self.ctx.h, out))
+        return dict(zip(("evals", "expansions", "upper_evals"), list(out)))

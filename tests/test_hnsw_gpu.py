@@ -1,0 +1,116 @@
+"""HNSW INT8 search on the GPU against the oracle's restatement of the reference's
+search_fp32_scored at dim 1536 (src/vector/hnsw.mojo:4136-4521): the same
+host-built graph, the same queries.  The beam replays LinearPool
+(src/common/heap.mojo:133-234) and the lane formulas of beam_search_1536_ref
+(src/vector/reference/beam_1536.mojo:85-135) exactly, so the pools, and with them the
+returned ids, distances and work counters, must be identical; recall@10 then matches
+the reference's trivially (the parity bar is 0.5 points)."""
+import numpy as np
+import pytest
+
+from pion_b200.workloads import mixture_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _graph(n, centres, seed, threads=1, metric="cosine", M=16, efc=100, nq=64):
+    import pion_b200
+    rows, qs = mixture_np(n, 1536, centres, seed=seed, n_queries=nq)
+    g = pion_b200.HNSWGraph(rows, M=M, ef_construction=efc, metric=metric, threads=threads)
+    return g, rows, qs
+
+
+def _same(oracle, A, ix, qs, k, ef):
+    ids, dist = ix.search(qs, k, ef)
+    st = ix.last_stats()
+    oi, od, ost = oracle.hnsw_search(A, qs, k, ef)
+    assert np.array_equal(ids, oi), f"ids differ at ef={ef}"
+    assert np.array_equal(dist.view(np.uint32), od.view(np.uint32)), f"dists differ at ef={ef}"
+    assert st == ost, (st, ost)
+    return ids, dist
+
+
+@pytest.fixture(scope="module")
+def small(ctx):
+    import pion_b200
+    g, rows, qs = _graph(6000, 64, seed=3)
+    return g, g.arrays(), pion_b200.HNSWIndex(ctx, g), rows, qs
+
+
+@pytest.mark.parametrize("ef", [1, 4, 10, 16, 64, 128, 256, 1024])
+def test_beam_matches_oracle(oracle, small, ef):
+    g, A, ix, rows, qs = small
+    _same(oracle, A, ix, qs, 10, ef)
+
+
+def test_k_beyond_pool_and_device_memory(oracle, small):
+    import torch
+    g, A, ix, rows, qs = small
+    ids, dist = _same(oracle, A, ix, qs, 40, 12)
+    assert (ids[:, 12:] == -1).all() and np.isinf(dist[:, 12:]).all()
+    qd = torch.from_numpy(qs).cuda()
+    di, dd = ix.search(qd, 10, 64)
+    hi, hd = ix.search(qs, 10, 64)
+    assert np.array_equal(di.cpu().numpy(), hi) and np.array_equal(dd.cpu().numpy(), hd)
+
+
+def test_parallel_build_large_batch(ctx, oracle):
+    """A graph from the parallel link lanes; a batch larger than the resident warps."""
+    import pion_b200
+    g, rows, qs = _graph(40000, 256, seed=11, threads=8, nq=5000)
+    A = g.arrays()
+    ix = pion_b200.HNSWIndex(ctx, g)
+    for ef in (64, 200):
+        _same(oracle, A, ix, qs, 10, ef)
+
+
+def test_l2_metric_and_deleted_nodes(ctx, oracle):
+    import pion_b200
+    g, rows, qs = _graph(5000, 32, seed=5, metric="l2")
+    A = dict(g.arrays())
+    dele = np.zeros((A["num_nodes"] + 7) // 8, np.uint8)
+    gone = np.arange(7, A["num_nodes"], 13)
+    gone = gone[gone != A["entry_point"]]
+    np.bitwise_or.at(dele, gone >> 3, (1 << (gone & 7)).astype(np.uint8))
+    A["deleted"] = dele
+    ix = pion_b200.HNSWIndex(ctx, A)
+    ids, _ = _same(oracle, A, ix, qs * 3.0, 10, 64)
+    assert not np.isin(ids, gone).any()
+
+
+def test_recall_smoke(ctx, oracle):
+    """The reference's recall smoke test at dim 1536 (tests/test_vector_recall_smoke.py):
+    150 planted clusters of 10 vectors, 60 queries near cluster centres, k = 10; recall
+    against exact cosine top-10 >= 0.90."""
+    import pion_b200
+    rng = np.random.Generator(np.random.PCG64(150))
+    centres = rng.standard_normal((150, 1536)).astype(np.float32)
+    rows = (np.repeat(centres, 10, axis=0) +
+            0.05 * rng.standard_normal((1500, 1536)).astype(np.float32))
+    pick = rng.choice(150, 60, replace=False)
+    qs = centres[pick] + 0.05 * rng.standard_normal((60, 1536)).astype(np.float32)
+    g = pion_b200.HNSWGraph(rows, M=16, ef_construction=200, threads=1)
+    ix = pion_b200.HNSWIndex(ctx, g)
+    ids, dist = _same(oracle, g.arrays(), ix, qs, 10, 64)
+    rn = rows / np.linalg.norm(rows, axis=1, keepdims=True)
+    qn = qs / np.linalg.norm(qs, axis=1, keepdims=True)
+    truth = np.argsort(-(qn @ rn.T), axis=1, kind="stable")[:, :10]
+    recall = np.mean([len(set(ids[i]) & set(truth[i])) / 10 for i in range(60)])
+    assert recall >= 0.90
+
+
+def test_register_rejects_bad_layouts(ctx, small):
+    import pion_b200
+    g, A, ix, rows, qs = small
+    bad = dict(A)
+    l0 = A["l0_slots"].copy()
+    l0[5, 1] = A["num_nodes"] + 3
+    bad["l0_slots"] = l0
+    with pytest.raises(pion_b200.PionError):
+        pion_b200.HNSWIndex(ctx, bad)
+    bad = dict(A)
+    bad["dim"] = 768
+    with pytest.raises(pion_b200.PionError):
+        pion_b200.HNSWIndex(ctx, bad)
+    with pytest.raises(pion_b200.PionError):
+        ix.search(qs, 10, 2000)
