@@ -11,7 +11,12 @@ shard, an NCCL all-gather exchanges the k candidates per query, and every rank m
 Other workloads: `flat_i8_b1` (the same index, one query per step), `flat_i8_10m`
 (10M rows, 4096-query batches), `flat_f32` (FLAT FP32 cosine, 100,000 x 1536,
 256 centres, 1000-query batches), `bq` (binary-quantised FLAT, 1M x 1536, Hamming
-top-100 then fp32 cosine rerank to 10, 1024-query batches).
+top-100 then fp32 cosine rerank to 10, 1024-query batches), `hnsw` (HNSW INT8 over 1M x
+1536 rows of a 1024-centre mixture, seed 3, graph built on the host CPU with M = 16,
+efConstruction = 200, GPU beam search at --ef (default 128), k = 10, 4096-query
+batches; the line carries recall@10 against exact FLAT results).  HNSW does not shard
+the graph: on N GPUs every rank holds the whole graph (built once on rank 0 and
+broadcast) and searches its 1/N of the batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME]
@@ -51,6 +56,9 @@ WORKLOADS = {
     "bq": dict(kind="bq", rows=1_000_000, dim=1536, centres=1024, seed=2, batch=1024, k=10,
                desc="binary-quantised FLAT, 1M x 1536 (192-byte codes), Hamming top-100, "
                     "fp32 cosine rerank to 10, 1024-query batches"),
+    "hnsw": dict(kind="hnsw", rows=1_000_000, dim=1536, centres=1024, seed=3, batch=4096, k=10,
+                 M=16, ef_construction=200,
+                 desc="HNSW INT8, 1M x 1536, M=16, efConstruction=200, 4096-query batches"),
 }
 
 
@@ -69,6 +77,7 @@ def args_parse(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU work of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ef", type=int, default=128, help="HNSW efSearch")
     return ap.parse_args(argv)
 
 
@@ -157,11 +166,16 @@ def dist_env():
     return world, rank, local
 
 
-def config_of(wl, batch, world):
-    return {"workload": wl["desc"], "rows": wl["rows"], "dim": wl["dim"],
-            "centres": wl["centres"], "batch": batch, "k": wl["k"], "seed": wl["seed"],
-            "parallelism": f"row shards x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-            "l2": "index larger than L2 (no flush needed)"}
+def config_of(wl, batch, world, a=None):
+    c = {"workload": wl["desc"], "rows": wl["rows"], "dim": wl["dim"],
+         "centres": wl["centres"], "batch": batch, "k": wl["k"], "seed": wl["seed"],
+         "parallelism": f"row shards x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+         "l2": "index larger than L2 (no flush needed)"}
+    if wl["kind"] == "hnsw":
+        c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
+                  "ef": a.ef if a is not None else None,
+                  "parallelism": f"graph replicas x{world}, query batch split"})
+    return c
 
 
 # ------------------------------------------------------------ workloads --
@@ -357,7 +371,155 @@ class BQWorkload:
         oracle.bq_knn(codes, rows, q[lo:hi], BQWorkload.shortlist, k, nthreads=threads)
 
 
-ADAPTERS = {"i8": I8Workload, "f32": F32Workload, "bq": BQWorkload}
+class HNSWWorkload:
+    """HNSW INT8: the graph is built on the host CPU (pion_v_b200_hnsw_build, the
+    reference's FT.OPTIMIZE build) on rank 0, broadcast to the other ranks, registered on
+    every GPU; each rank searches its slice of the query batch (replicas, no merge)."""
+
+    dtype = "int8 codes (exact int32 L2), fp32 pool distances"
+    descending = False
+    replicas = True
+
+    def __init__(self, wl, batch, dev, ctx, lo, hi, ef=128):
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        import pion_b200
+        from pion_b200.workloads import mixture_torch
+
+        self.wl, self.k, self.ctx, self.ef = wl, wl["k"], ctx, ef
+        n, dim = wl["rows"], wl["dim"]
+        self.dim = dim
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        _, qall = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev,
+                                row_range=(0, 0))
+        qlo, qhi = batch * rank // world, batch * (rank + 1) // world
+        self.q = qall[qlo:qhi].contiguous()
+        self.batch = qhi - qlo
+        self.qall = qall
+        self.graph = None
+        self.build_s = None
+        if rank == 0:
+            rows = torch.empty((n, dim), dtype=torch.float32)
+            for s in range(0, n, 1 << 18):
+                e = min(n, s + (1 << 18))
+                part, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev,
+                                        row_range=(s, e))
+                rows[s:e] = part.cpu()
+                del part
+            t0 = time.perf_counter()
+            self.graph = pion_b200.HNSWGraph(rows.numpy(), M=wl["M"],
+                                             ef_construction=wl["ef_construction"])
+            self.build_s = time.perf_counter() - t0
+            self.rows_host = rows
+            arrays = self.graph.arrays()
+        else:
+            arrays = None
+        if world > 1:
+            arrays = self._broadcast(arrays, dev, rank)
+        self.arrays = arrays
+        self.ix = pion_b200.HNSWIndex(ctx, self.graph if rank == 0 else arrays)
+        torch.cuda.synchronize()
+
+    @staticmethod
+    def _broadcast(arrays, dev, rank):
+        """Rank 0's layout to every rank (NCCL broadcast of each buffer)."""
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+        names = ["compact_buffer", "l0_compact", "l0_slots", "node_slot", "node_ids",
+                 "node_level", "upper_offset", "upper_links"]
+        scal = ["num_nodes", "dim", "M", "entry_point", "max_level", "compact_stride",
+                "compact_hdr", "upper_rows", "metric"]
+        meta = torch.zeros(len(scal) + 2, dtype=torch.float64, device=dev)
+        if rank == 0:
+            meta[:len(scal)] = torch.tensor([float(arrays[x]) for x in scal], dtype=torch.float64)
+            meta[len(scal)] = float(arrays["global_min"])
+            meta[len(scal) + 1] = float(arrays["global_max"])
+        dist.broadcast(meta, 0)
+        m = meta.tolist()
+        out = {x: int(m[i]) for i, x in enumerate(scal)}
+        out["global_min"], out["global_max"] = m[len(scal)], m[len(scal) + 1]
+        out["global_min"] = float(np.float32(out["global_min"]))
+        out["global_max"] = float(np.float32(out["global_max"]))
+        for nm in names:
+            if rank == 0:
+                a = np.ascontiguousarray(arrays[nm])
+                t = torch.from_numpy(a.view(np.uint8).reshape(-1)).to(dev)
+                shp = torch.tensor(list(a.shape) + [0] * (2 - a.ndim), device=dev)
+            else:
+                shp = torch.zeros(2, dtype=torch.int64, device=dev)
+            dist.broadcast(shp, 0)
+            dt = {"compact_buffer": np.int8, "node_ids": np.int32, "node_level": np.int8,
+                  "upper_offset": np.int64}.get(nm, np.uint32)
+            shape = [int(x) for x in shp.tolist() if x > 0] if nm not in (
+                "node_slot", "node_ids", "node_level", "upper_offset") else [int(shp[0])]
+            nbytes = int(np.prod(shape)) * np.dtype(dt).itemsize
+            if rank != 0:
+                t = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            dist.broadcast(t, 0)
+            out[nm] = t.cpu().numpy().view(dt).reshape(shape)
+        out["deleted"] = None
+        return out
+
+    def inputs(self):
+        return [self.q]
+
+    def search(self, inp):
+        return self.ix.search(inp[0], self.k, self.ef)
+
+    def host_call(self, hin, out_i, out_v):
+        import pion_b200
+        c = self.ctx
+        c.check(c.lib.pion_v_b200_hnsw_search(c.h, self.ix.h, hin[0].data_ptr(), self.batch,
+                                              self.k, self.ef, out_i.data_ptr(),
+                                              out_v.data_ptr(), pion_b200._lib.MEM_HOST))
+
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+        st = self.ix.last_stats()
+        byts = float(st["evals"] + st["upper_evals"]) * 1544.0 + st["expansions"] * 264.0
+        achieved = byts / (kern_ms / 1000.0) / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "algorithmic_per_launch": byts, "kernel_ms": kern_ms,
+                "work_per_query": {k: v / max(1, self.batch) for k, v in st.items()},
+                "note": "random 1.5 KB gathers, latency-bound: bytes = (level-0 + upper-level "
+                        "distance evaluations) x 1544 + expansions x 264"}
+
+    def extra(self, dev):
+        """recall@10 of this rank's results against exact FLAT FP32 cosine (rank 0)."""
+        import numpy as np
+        import torch
+
+        import pion_b200
+        if self.graph is None:
+            return {}
+        rows = self.rows_host.to(dev)
+        flat = pion_b200.FlatF32Index(self.ctx, rows)
+        truth, _ = flat.search(self.q, self.k)
+        ids, _ = self.ix.search(self.q, self.k, self.ef)
+        t, r = truth.cpu().numpy(), ids.cpu().numpy()
+        recall = float(np.mean([len(set(r[i]) & set(t[i])) / self.k for i in range(len(t))]))
+        flat.free()
+        del rows
+        torch.cuda.empty_cache()
+        return {"recall_at_10": recall, "ef": self.ef, "build_s": self.build_s,
+                "build_threads": os.cpu_count()}
+
+    def host_data(self):
+        return (self.graph.arrays(), self.q.cpu().numpy(), self.ef)
+
+    @staticmethod
+    def cpu_run(data, lo, hi, k, threads):
+        import oracle
+        arrays, q, ef = data
+        oracle.hnsw_search(arrays, q[lo:hi], k, ef, nthreads=threads)
+
+
+ADAPTERS = {"i8": I8Workload, "f32": F32Workload, "bq": BQWorkload, "hnsw": HNSWWorkload}
 
 
 # --------------------------------------------------------------- reference arm --
@@ -372,6 +534,12 @@ def reference_data(wl, batch, dev):
 
     n, dim = wl["rows"], wl["dim"]
     _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev, row_range=(0, 0))
+    if wl["kind"] == "hnsw":  # the host build (a restatement of the reference's builder)
+        import pion_b200
+        rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
+        g = pion_b200.HNSWGraph(rows.cpu().numpy(), M=wl["M"],
+                                ef_construction=wl["ef_construction"])
+        return (g.arrays(), qf.cpu().numpy(), wl["ef"]), g
     if wl["kind"] in ("f32", "bq"):
         rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
         rn = oracle.l2_normalize_rows(rows.cpu().numpy())
@@ -413,6 +581,9 @@ def run_reference(a, wl):
     batch = a.batch or wl["batch"]
     dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
     data = reference_data(wl, batch, dev)
+    keep = None
+    if wl["kind"] == "hnsw":
+        data, keep = data
     run = ADAPTERS[wl["kind"]].cpu_run
     threads = os.cpu_count() or 1
     # size a step: throughput estimate on `threads` queries, then a sample per step so
@@ -440,7 +611,7 @@ def run_reference(a, wl):
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": 1000.0 * dt / max(1, a.steps), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": ADAPTERS[wl["kind"]].dtype,
-        "data": "synthetic", "config": config_of(wl, batch, 1),
+        "data": "synthetic", "config": config_of(wl, batch, 1, a),
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
@@ -477,7 +648,11 @@ def run_ours(a, wl):
     n = wl["rows"]
     lo, hi = shard_bounds(n, world, rank)
     ctx = pion_b200.Context(local)
-    W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi)
+    if wl["kind"] == "hnsw":
+        W = HNSWWorkload(wl, batch, dev, ctx, lo, hi, ef=a.ef)
+    else:
+        W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi)
+    local_batch = W.batch
     ctx.use_torch_stream()
     stream = torch.cuda.current_stream()
 
@@ -485,7 +660,7 @@ def run_ours(a, wl):
         return pion_b200.merge_topk(ctx, scores, ids, k, descending=W.descending,
                                     lists_major=True)
 
-    step = ShardedSearch(W.search, k, merge)
+    step = W.search if getattr(W, "replicas", False) else ShardedSearch(W.search, k, merge)
 
     def barrier():
         torch.cuda.synchronize()
@@ -519,11 +694,12 @@ def run_ours(a, wl):
     e2e_steps = a.e2e_steps or max(10, min(a.steps, 200))
     hin = [t.cpu().pin_memory() for t in inp]
     dbuf = [torch.empty_like(t) for t in inp]
-    out_i = torch.empty((batch, k), dtype=torch.int32).pin_memory()
-    out_v = torch.empty((batch, k), dtype=torch.float32).pin_memory()
+    out_i = torch.empty((local_batch, k), dtype=torch.int32).pin_memory()
+    out_v = torch.empty((local_batch, k), dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        if world == 1:  # the C-ABI host-buffer path: copies, kernels, copies, sync
+        if world == 1 or getattr(W, "replicas", False):
+            # the C-ABI host-buffer path: copies, kernels, copies, sync
             W.host_call(hin, out_i, out_v)
             return
         for d, h in zip(dbuf, hin):
@@ -544,7 +720,7 @@ def run_ours(a, wl):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
     h2d = sum(t.numel() * t.element_size() for t in hin)
-    d2h = batch * k * 8
+    d2h = local_batch * k * 8
 
     # ---- max over ranks
     t = torch.tensor([elapsed, e2e_ms, kern_ms / max(1, kern_n)], device=dev, dtype=torch.float64)
@@ -561,13 +737,16 @@ def run_ours(a, wl):
         e2e_qps = batch * e2e_steps / (e2e_ms / 1000.0)
         peaks, peak_kind = measured_peaks()
         roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind)
+        if getattr(W, "replicas", False):
+            # whole-job value: every rank ran its share of the batch in `elapsed` (max)
+            pass
         roof["traffic"] = profiled_traffic(f"{a.workload}_{world}")
         line = {
             "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed / a.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": W.dtype, "data": "synthetic (seeded Gaussian mixture on the device)",
-            "config": config_of(wl, batch, world),
+            "config": config_of(wl, batch, world, a),
             "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches,
@@ -575,6 +754,8 @@ def run_ours(a, wl):
             "clocks": clk,
         }
     # ---- CPU baseline on rank 0 at N=1 (bounded sample of the same workload)
+    if rank == 0 and hasattr(W, "extra"):
+        line["config"].update(W.extra(dev))
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_baseline(W, batch, k, a.cpu_seconds)
@@ -611,6 +792,7 @@ def cpu_baseline(W, batch, k, seconds):
 def main(argv=None):
     a = args_parse(argv)
     wl = dict(WORKLOADS[a.workload])
+    wl["ef"] = a.ef
     if a.rows:
         wl["rows"] = a.rows
         wl["desc"] += f" (rows overridden: {a.rows:,})"
