@@ -489,6 +489,8 @@ __global__ void bq_rerank_kernel(const float* __restrict__ rows, int dim,
     float* dist = rr + (size_t)w * S;
     const float* qv = qn + (size_t)q * dim;
     const int n = sl_n[q];
+    for (int j = lane; j < n; j += 32)
+        prefetch_row_f32_l2(rows + (size_t)sl_id[(size_t)q * S + j] * dim, dim);
     const int half = lane >> 4, hl = lane & 15;
     const unsigned hmask = half ? 0xffff0000u : 0x0000ffffu;
     for (int j0 = 0; j0 < n; j0 += 2) {

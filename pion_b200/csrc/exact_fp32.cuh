@@ -15,6 +15,8 @@ __device__ __forceinline__ float dot4chain_half(const float* __restrict__ q,
                                                 int hl /* lane within half */, unsigned mask) {
     const int main_end = dim & ~15;
     float acc = 0.0f;
+    // unrolled so that the loads run ahead of the (unchanged) addition chain
+#pragma unroll 8
     for (int d = hl; d < main_end; d += 16) acc = __fadd_rn(__fmul_rn(q[d], v[d]), acc);
     // 4-element tail blocks continue chain 0 (lanes 0..3)
     int d4 = main_end;
@@ -36,6 +38,13 @@ __device__ __forceinline__ float dot4chain_half(const float* __restrict__ q,
     float s = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
     for (int d = d4; d < dim; ++d) s = __fadd_rn(s, __fmul_rn(q[d], v[d]));
     return s;
+}
+
+// Asks L2 for whole rows of `dim` floats ahead of the dot products (one bulk prefetch per
+// row; rows start 16-byte aligned and dim * 4 is a multiple of 16).
+__device__ __forceinline__ void prefetch_row_f32_l2(const float* row, int dim) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row), "r"((uint32_t)dim * 4u)
+                 : "memory");
 }
 
 // (distance asc, id asc)

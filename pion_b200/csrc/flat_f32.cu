@@ -294,55 +294,91 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // exact_knn's query normalisation (src/commands/vector.mojo:1254-1260): a sequential
 // scalar sum of squares, one thread per query.
-__global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int dim,
+// exact_knn's query normalisation (src/commands/vector.mojo:1254-1260): a sequential
+// sum of squares, inv = 1/sqrt(ss) (1 if ss == 0), y = x * inv.  A CTA stages ROWS
+// queries in shared memory with coalesced loads; one thread per query runs the
+// sequential sum; all threads write the result.  qnorm (|y|, which only feeds the
+// certification bound, whose 1 % slack covers its rounding) is a warp reduction.
+__global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int dim, int rows,
                                        float* __restrict__ out, float* __restrict__ qnorm) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= nq) return;
-    const float* x = q + (size_t)t * dim;
-    float ss = 0.0f;
-    for (int d = 0; d < dim; ++d) ss = __fadd_rn(ss, __fmul_rn(x[d], x[d]));
-    const float inv = ss > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
-    float n2 = 0.0f;
-    float* o = out + (size_t)t * dim;
-    for (int d = 0; d < dim; ++d) {
-        const float y = __fmul_rn(x[d], inv);
-        o[d] = y;
-        n2 = fmaf(y, y, n2);
+    extern __shared__ float qsm[];  // [rows][dim + 1]
+    __shared__ float inv_s[32];
+    const int q0 = blockIdx.x * rows;
+    const int nr = min(rows, nq - q0);
+    const int pitch = dim + 1;
+    for (int r = 0; r < nr; ++r)
+        for (int d = threadIdx.x; d < dim; d += blockDim.x)
+            qsm[r * pitch + d] = q[(size_t)(q0 + r) * dim + d];
+    __syncthreads();
+    if (threadIdx.x < nr) {
+        const float* x = qsm + threadIdx.x * pitch;
+        float ss = 0.0f;
+        for (int d = 0; d < dim; ++d) ss = __fadd_rn(ss, __fmul_rn(x[d], x[d]));
+        inv_s[threadIdx.x] = ss > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
     }
-    qnorm[t] = sqrtf(n2);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int r = warp; r < nr; r += nw) {
+        const float inv = inv_s[r];
+        float n2 = 0.0f;
+        for (int d = lane; d < dim; d += 32) {
+            const float y = __fmul_rn(qsm[r * pitch + d], inv);
+            out[(size_t)(q0 + r) * dim + d] = y;
+            n2 = fmaf(y, y, n2);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+        if (lane == 0) qnorm[q0 + r] = sqrtf(n2);
+    }
 }
 
 // l2_normalize_fp32 (src/vector/kernels.mojo:318-357), 4 lanes per row: lane l sums
 // elements l, l+4, ... (the 4-lane SSE accumulator), then (s0 + s2) + (s1 + s3), the
 // scalar tail, inv = 1/sqrt.  Also records each row's resulting L2 norm.
-__global__ void l2_normalize_rows_kernel(const float* __restrict__ src, int64_t n_rows, int dim,
-                                         float* __restrict__ dst, float* __restrict__ norms) {
-    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
-    const int l = threadIdx.x & 3;
-    const unsigned mask = 0xffffffffu;
-    const bool ok = r < n_rows;
-    const float* x = src + (ok ? r : 0) * dim;
+// l2_normalize_fp32 (src/vector/kernels.mojo:318-357) of whole rows: four lanes of
+// sequential sums (lane l takes the elements l, l+4, ...), combined (s0 + s2) + (s1 + s3),
+// the scalar tail added in order, inv = 1/sqrt; a zero row passes through.  A CTA stages
+// ROWS rows in shared memory with coalesced loads (in place is allowed: every element is
+// read before any is written), four threads per row run the lane sums, all threads write.
+__global__ void l2_normalize_rows_kernel(const float* src, int64_t n_rows, int dim, int rows,
+                                         float* dst, float* __restrict__ norms) {
+    extern __shared__ float xs[];  // [rows][dim + 1]
+    __shared__ float lane_s[32 * 4];
+    __shared__ float inv_s[32];
+    const int64_t r0 = (int64_t)blockIdx.x * rows;
+    const int nr = (int)min((int64_t)rows, n_rows - r0);
+    const int pitch = dim + 1;
+    for (int r = 0; r < nr; ++r)
+        for (int d = threadIdx.x; d < dim; d += blockDim.x)
+            xs[r * pitch + d] = src[(size_t)(r0 + r) * dim + d];
+    __syncthreads();
     const int main_end = dim & ~3;
-    float acc = 0.0f;
-    if (ok)
+    if (threadIdx.x < 4 * nr) {
+        const int r = threadIdx.x >> 2, l = threadIdx.x & 3;
+        const float* x = xs + r * pitch;
+        float acc = 0.0f;
         for (int d = l; d < main_end; d += 4) acc = __fadd_rn(acc, __fmul_rn(x[d], x[d]));
-    const int g = (threadIdx.x & 31) & ~3;
-    const float s0 = __shfl_sync(mask, acc, g + 0);
-    const float s1 = __shfl_sync(mask, acc, g + 1);
-    const float s2 = __shfl_sync(mask, acc, g + 2);
-    const float s3 = __shfl_sync(mask, acc, g + 3);
-    if (!ok) return;
-    float ns = __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
-    for (int d = main_end; d < dim; ++d) ns = __fadd_rn(ns, __fmul_rn(x[d], x[d]));
-    float* y = dst + r * dim;
-    if (ns <= 0.0f) {
-        for (int d = l; d < dim; d += 4) y[d] = x[d];
-        if (l == 0 && norms) norms[r] = 0.0f;
-        return;
+        lane_s[threadIdx.x] = acc;
     }
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ns));
-    for (int d = l; d < dim; d += 4) y[d] = __fmul_rn(x[d], inv);
-    if (l == 0 && norms) norms[r] = __fmul_rn(__fsqrt_rn(ns), inv);
+    __syncthreads();
+    if (threadIdx.x < nr) {
+        const int r = threadIdx.x;
+        const float* x = xs + r * pitch;
+        const float* a = lane_s + 4 * r;
+        float ns = __fadd_rn(__fadd_rn(a[0], a[2]), __fadd_rn(a[1], a[3]));
+        for (int d = main_end; d < dim; ++d) ns = __fadd_rn(ns, __fmul_rn(x[d], x[d]));
+        const float inv = ns <= 0.0f ? 0.0f : __fdiv_rn(1.0f, __fsqrt_rn(ns));
+        inv_s[r] = ns <= 0.0f ? -1.0f : inv;  // -1: zero row, copied unchanged
+        if (norms) norms[r0 + r] = ns <= 0.0f ? 0.0f : __fmul_rn(__fsqrt_rn(ns), inv);
+    }
+    __syncthreads();
+    for (int r = 0; r < nr; ++r) {
+        const float inv = inv_s[r];
+        for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+            const float x = xs[r * pitch + d];
+            dst[(size_t)(r0 + r) * dim + d] = inv < 0.0f ? x : __fmul_rn(x, inv);
+        }
+    }
 }
 
 // Row L2 norms (for the certification bound) without normalising.
@@ -390,6 +426,11 @@ __global__ void rescore_certify_kernel(const float* __restrict__ rows, int dim,
     const unsigned hmask = half ? 0xffff0000u : 0x0000ffffu;
     int n_valid = 0;
     for (int j = 0; j < kc; ++j) n_valid += cand_i[(size_t)q * kc + j] >= 0 ? 1 : 0;
+    if ((dim & 3) == 0)
+        for (int j = lane; j < kc; j += 32) {
+            const int32_t id = cand_i[(size_t)q * kc + j];
+            if (id >= 0) prefetch_row_f32_l2(rows + (size_t)id * dim, dim);
+        }
     for (int j0 = 0; j0 < kc; j0 += 2) {
         const int j = j0 + half;
         const int32_t id = j < kc ? cand_i[(size_t)q * kc + j] : -1;
@@ -595,19 +636,39 @@ int ff32_query_tile() { return ff32::BM; }
 int ff32_k_elems() { return ff32::KEL; }
 int ff32_kc(int k) { return k <= 16 ? 32 : 64; }
 
+// Rows staged per CTA by the normalisation kernels: up to 8, within 96 KB of shared
+// memory (one row of the largest supported dim, 16384, takes 64 KB).
+static int staged_rows(int dim) {
+    const int per = (int)((96 * 1024) / ((size_t)(dim + 1) * 4));
+    return per < 1 ? 1 : per > 8 ? 8 : per;
+}
+
+template <typename K>
+static bool allow_big_smem(K kernel) {
+    static bool ok = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          200 * 1024) == cudaSuccess;
+    return ok;
+}
+
 int launch_query_normalize(const float* q, int nq, int dim, float* out, float* qnorm,
                            cudaStream_t st) {
     if (nq <= 0) return 0;
-    ff32::query_normalize_kernel<<<(nq + 127) / 128, 128, 0, st>>>(q, nq, dim, out, qnorm);
+    if (!allow_big_smem(ff32::query_normalize_kernel)) return PION_B200_ECUDA;
+    const int rows = staged_rows(dim);
+    const size_t smem = (size_t)rows * (dim + 1) * 4;
+    ff32::query_normalize_kernel<<<(nq + rows - 1) / rows, 256, smem, st>>>(q, nq, dim, rows,
+                                                                          out, qnorm);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
 int launch_l2_normalize_rows(const float* src, int64_t n_rows, int dim, float* dst, float* norms,
                              cudaStream_t st) {
     if (n_rows <= 0) return 0;
-    const int64_t threads = n_rows * 4;
-    ff32::l2_normalize_rows_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-        src, n_rows, dim, dst, norms);
+    if (!allow_big_smem(ff32::l2_normalize_rows_kernel)) return PION_B200_ECUDA;
+    const int rows = staged_rows(dim);
+    const size_t smem = (size_t)rows * (dim + 1) * 4;
+    ff32::l2_normalize_rows_kernel<<<(unsigned)((n_rows + rows - 1) / rows), 256, smem, st>>>(
+        src, n_rows, dim, rows, dst, norms);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
