@@ -387,6 +387,7 @@ constexpr int SCAN_THREADS = 256;
 constexpr int SCAN_GROUP = 8;                      // lanes per row: 8 x 16 B = 128 B
 constexpr int SCAN_GROUPS = SCAN_THREADS / SCAN_GROUP;
 constexpr int SCAN_MAX_CHUNKS = 1024;              // dim <= 16384
+constexpr int SCAN_PER_LANE = 12;                  // fully unrolled up to dim 1536
 
 __device__ __forceinline__ int4 ld_stream(const int4* p) {
     int4 v;
@@ -426,14 +427,35 @@ __global__ void __launch_bounds__(SCAN_THREADS)
         int acc = 0;
         if (valid) {
             const int4* rp = reinterpret_cast<const int4*>(rows + r * dim);
+            if (KCAP <= 16 && chunks <= SCAN_GROUP * SCAN_PER_LANE) {
+                // every load of the row in flight at once (12 per lane at dim 1536)
+                int4 a[SCAN_PER_LANE];
+#pragma unroll
+                for (int i = 0; i < SCAN_PER_LANE; ++i) {
+                    const int c = gl + i * SCAN_GROUP;
+                    if (c < chunks) a[i] = ld_stream(rp + c);
+                }
+#pragma unroll
+                for (int i = 0; i < SCAN_PER_LANE; ++i) {
+                    const int c = gl + i * SCAN_GROUP;
+                    if (c < chunks) {
+                        const int4 b = qv[c];
+                        acc = __dp4a(a[i].x, b.x, acc);
+                        acc = __dp4a(a[i].y, b.y, acc);
+                        acc = __dp4a(a[i].z, b.z, acc);
+                        acc = __dp4a(a[i].w, b.w, acc);
+                    }
+                }
+            } else {
 #pragma unroll 4
-            for (int c = gl; c < chunks; c += SCAN_GROUP) {
-                const int4 a = ld_stream(rp + c);
-                const int4 b = qv[c];
-                acc = __dp4a(a.x, b.x, acc);
-                acc = __dp4a(a.y, b.y, acc);
-                acc = __dp4a(a.z, b.z, acc);
-                acc = __dp4a(a.w, b.w, acc);
+                for (int c = gl; c < chunks; c += SCAN_GROUP) {
+                    const int4 a = ld_stream(rp + c);
+                    const int4 b = qv[c];
+                    acc = __dp4a(a.x, b.x, acc);
+                    acc = __dp4a(a.y, b.y, acc);
+                    acc = __dp4a(a.z, b.z, acc);
+                    acc = __dp4a(a.w, b.w, acc);
+                }
             }
         }
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
