@@ -17,7 +17,10 @@ efConstruction = 200, GPU beam search at --ef (default 128), k = 10, 4096-query
 batches; the line carries recall@10 against exact FLAT results).  HNSW does not shard
 the graph: on N GPUs every rank holds the whole graph (built once on rank 0 and
 broadcast) and serves its own 4096-query batch (weak scaling, N x 4096 queries per
-step).
+step).  Like the reference's server (one query stream per worker thread), the HNSW bench
+runs --workers contexts (default 3), each on its own CUDA stream, taking the batches in
+turn, so the long tail of one batch (its slowest query does ~2.8x the mean work) overlaps
+the start of the next; every batch is still one 4096-query call.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME]
@@ -79,6 +82,9 @@ def args_parse(argv=None):
                     help="target CPU work of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ef", type=int, default=128, help="HNSW efSearch")
+    ap.add_argument("--workers", type=int, default=None,
+                    help="worker contexts (each its own CUDA stream) taking batches in turn; "
+                         "default 3 for hnsw, 1 otherwise")
     return ap.parse_args(argv)
 
 
@@ -467,12 +473,12 @@ class HNSWWorkload:
     def inputs(self):
         return [self.q]
 
-    def search(self, inp):
-        return self.ix.search(inp[0], self.k, self.ef)
+    def search(self, inp, ctx=None):
+        return self.ix.search(inp[0], self.k, self.ef, ctx=ctx)
 
-    def host_call(self, hin, out_i, out_v):
+    def host_call(self, hin, out_i, out_v, ctx=None):
         import pion_b200
-        c = self.ctx
+        c = ctx or self.ctx
         c.check(c.lib.pion_v_b200_hnsw_search(c.h, self.ix.h, hin[0].data_ptr(), self.batch,
                                               self.k, self.ef, out_i.data_ptr(),
                                               out_v.data_ptr(), pion_b200._lib.MEM_HOST))
@@ -480,6 +486,8 @@ class HNSWWorkload:
     def roofline(self, rows_local, kern_ms, peaks, peak_kind):
         st = self.ix.last_stats()
         byts = float(st["evals"] + st["upper_evals"]) * 1544.0 + st["expansions"] * 264.0
+        # with several workers the batches overlap: kern_ms is then the time per batch
+        # of the whole run (elapsed / steps), not a single launch's duration
         achieved = byts / (kern_ms / 1000.0) / 1e9
         peak = peaks["hbm_gbs"]
         return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -661,6 +669,26 @@ def run_ours(a, wl):
                                     lists_major=True)
 
     step = W.search if getattr(W, "replicas", False) else ShardedSearch(W.search, k, merge)
+    workers = a.workers or (3 if wl["kind"] == "hnsw" else 1)
+    if workers > 1 and wl["kind"] != "hnsw":
+        raise SystemExit("--workers > 1 is for the hnsw workload")
+    ctxs = [ctx] + [pion_b200.Context(local) for _ in range(workers - 1)]
+    streams = [stream] + [torch.cuda.Stream(device=dev) for _ in range(workers - 1)]
+
+    def run_steps(n, inp):
+        """n batches, worker i % workers takes batch i on its own context and stream."""
+        if workers == 1:
+            for _ in range(n):
+                step(inp)
+            return
+        for st_ in streams[1:]:
+            st_.wait_stream(stream)
+        for i in range(n):
+            w = i % workers
+            with torch.cuda.stream(streams[w]):
+                W.search(inp, ctx=ctxs[w])
+        for st_ in streams[1:]:
+            stream.wait_stream(st_)
 
     def barrier():
         torch.cuda.synchronize()
@@ -669,25 +697,29 @@ def run_ours(a, wl):
         torch.cuda.synchronize()
 
     inp = W.inputs()
-    for _ in range(max(3, a.warmup)):
-        step(inp)
+    run_steps(max(3, a.warmup), inp)
     barrier()
 
     clocks = ClockMonitor(local)
     clocks.start()
-    ctx.timing(True)
-    launches0 = ctx.launches
+    for c_ in ctxs:
+        c_.timing(True)
+    launches0 = sum(c_.launches for c_ in ctxs)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     ev0.record(stream)
-    for _ in range(a.steps):
-        step(inp)
+    run_steps(a.steps, inp)
     ev1.record(stream)
     barrier()
     elapsed = ev0.elapsed_time(ev1)
-    launches = ctx.launches - launches0
-    kern_ms, kern_n = ctx.timing_read()
-    ctx.timing(False)
+    launches = sum(c_.launches for c_ in ctxs) - launches0
+    kern_ms, kern_n = 0.0, 0
+    for c_ in ctxs:
+        km, kn = c_.timing_read()
+        c_.timing(False)
+        kern_ms, kern_n = kern_ms + km, kern_n + kn
+    if workers > 1:  # overlapping batches: the time per batch of the whole run
+        kern_ms, kern_n = elapsed, a.steps
     clk = clocks.stop()
 
     # ---- e2e: host (pinned) queries in, host results out, through the C ABI
@@ -709,13 +741,35 @@ def run_ours(a, wl):
         out_v.copy_(sc, non_blocking=True)
         stream.synchronize()
 
-    for _ in range(3):
-        e2e_step()
+    def e2e_threads(n):
+        """n batches through the C ABI with host buffers, one host thread per worker
+        context (each call copies in, searches and copies out, synchronously)."""
+        import threading
+        bufs = [([t.clone().pin_memory() for t in hin],
+                 torch.empty_like(out_i).pin_memory(), torch.empty_like(out_v).pin_memory())
+                for _ in range(workers)]
+        errs = []
+
+        def work(w):
+            try:
+                for i in range(w, n, workers):
+                    W.host_call(bufs[w][0], bufs[w][1], bufs[w][2], ctx=ctxs[w])
+            except Exception as e:  # pragma: no cover
+                errs.append(e)
+        ths = [threading.Thread(target=work, args=(w,)) for w in range(workers)]
+        for t_ in ths:
+            t_.start()
+        for t_ in ths:
+            t_.join()
+        if errs:
+            raise errs[0]
+
+    run_e2e = (lambda n: [e2e_step() for _ in range(n)]) if workers == 1 else e2e_threads
+    run_e2e(3)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    run_e2e(e2e_steps)
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
@@ -750,6 +804,7 @@ def run_ours(a, wl):
             "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches,
+            "workers": workers,
             "roofline": roof,
             "clocks": clk,
         }
@@ -764,6 +819,8 @@ def run_ours(a, wl):
     if rank == 0:
         print(json.dumps(line), flush=True)
     W.ix.free()
+    for c_ in ctxs[1:]:
+        c_.close()
     ctx.close()
     if world > 1:
         dist.barrier(device_ids=[local])

@@ -192,6 +192,14 @@ __device__ __forceinline__ void read_vec(const int4* row, int lane, int4 (&v)[3]
     for (int k = 0; k < 3; ++k) v[k] = row[lane + 32 * k];
 }
 
+// A visited-bitmap word, read at L2 (the bitmap is only written by atomics, which act at
+// L2, so an L1 copy could be stale).
+__device__ __forceinline__ uint32_t ld_l2_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // L2 prefetch of the (at most two) 128-byte lines holding a 132-byte adjacency row;
 // both addresses lie inside the row.
 __device__ __forceinline__ void prefetch_row_l2(const uint32_t* row) {
@@ -342,6 +350,12 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             pool[0].id = curr;
         }
         int size = 1, hint = 0;
+        // Look-ahead: the row of the entry predicted to be popped next (the second
+        // unchecked entry at this pop) and the visited words of its neighbours, read
+        // after this step's marks.  Only this warp writes its bitmap, so the words are
+        // exact when the prediction holds; otherwise the step loads as usual.
+        uint32_t sp_node = 0xffffffffu, sp_cnt = 0, sp_nb = 0xffffffffu, sp_sl = 0xffffffffu;
+        uint32_t sp_word = 0;
         __syncwarp();
         for (int64_t step = 0;; ++step) {
             if (step > p.num_nodes) {
@@ -363,21 +377,25 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             if (pos < 0) break;
             const bool fill = size < ef;
             const uint32_t c = pool[pos].id;
-            if (nxt >= 0 && lane < 2) {
-                const uint32_t cn = pool[nxt].id;
-                prefetch_row_l2((lane ? p.l0_slots : p.l0_compact) + (size_t)cn * 33);
-            }
+            const uint32_t pred = nxt >= 0 ? pool[nxt].id : 0xffffffffu;
             __syncwarp();
             if (lane == 0) pool[pos].id = c | CHECKED;
             hint = pos + 1;
             n_expand += 1;
 
-            // gather: unvisited, undeleted neighbours in adjacency order (one round trip
-            // for the row: every lane loads its entry and the count together)
-            const uint32_t* row = p.l0_compact + (size_t)c * 33;
-            const uint32_t cnt_raw = row[0];
-            const uint32_t nb_raw = row[1 + lane];
-            const uint32_t sl = p.l0_slots[(size_t)c * 33 + 1 + lane];
+            // gather: unvisited, undeleted neighbours in adjacency order
+            const bool hit = c == sp_node;  // warp-uniform
+            uint32_t cnt_raw, nb_raw, sl;
+            if (hit) {
+                cnt_raw = sp_cnt;
+                nb_raw = sp_nb;
+                sl = sp_sl;
+            } else {  // one round trip: every lane loads its entry and the count together
+                const uint32_t* row = p.l0_compact + (size_t)c * 33;
+                cnt_raw = row[0];
+                nb_raw = row[1 + lane];
+                sl = p.l0_slots[(size_t)c * 33 + 1 + lane];
+            }
             const int cnt = min((int)cnt_raw, 32);
             const uint32_t nb = lane < cnt ? nb_raw : 0xffffffffu;
             const bool valid = lane < cnt && nb < nn && !is_deleted(p.deleted, nb);
@@ -386,15 +404,35 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             bool fresh = false;
             if (valid && (__ffs(peers) - 1) == lane) {
                 const uint32_t bit = 1u << (nb & 31);
-                fresh = (atomicOr(&vis[nb >> 5], bit) & bit) == 0;
+                if (hit) {  // the word was read after every earlier mark of this query
+                    fresh = (sp_word & bit) == 0;
+                    if (fresh) atomicOr(&vis[nb >> 5], bit);
+                } else {
+                    fresh = (atomicOr(&vis[nb >> 5], bit) & bit) == 0;
+                }
                 if (fresh && sl >= nn) {
                     record_error(p.status, PION_B200_EINVAL);
                     fresh = false;
                 }
             }
+            // look-ahead row of the predicted next pop, in flight while this step scores
+            sp_node = pred;
+            if (pred != 0xffffffffu) {
+                const uint32_t* prow = p.l0_compact + (size_t)pred * 33;
+                sp_cnt = prow[0];
+                sp_nb = prow[1 + lane];
+                sp_sl = p.l0_slots[(size_t)pred * 33 + 1 + lane];
+            }
             const unsigned fm = __ballot_sync(FULL, fresh);
             const int n = __popc(fm);
-            if (n == 0) continue;
+            if (n == 0) {
+                __syncwarp();  // this step's marks before the look-ahead words
+                if (sp_node != 0xffffffffu) {
+                    const bool sv = (int)lane < min((int)sp_cnt, 32) && sp_nb < nn;
+                    sp_word = sv ? ld_l2_u32(&vis[sp_nb >> 5]) : 0xffffffffu;
+                }
+                continue;
+            }
             const int batched = n - (n & 3);
             n_evals += n;
             float my_norm = 0.0f;  // consumed after the staging round trip
@@ -415,6 +453,12 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
                 for (int e = 0; e < STAGE; ++e)
                     if (e < g) stage_vec(stage + e * 96, p.codes, g_slot[v0 + e], lane);
                 cp_async_wait_all();
+                if (v0 == 0 && sp_node != 0xffffffffu) {
+                    // the look-ahead row has arrived by now: its visited words (after this
+                    // step's marks, ordered by the syncs above)
+                    const bool sv = (int)lane < min((int)sp_cnt, 32) && sp_nb < nn;
+                    sp_word = sv ? ld_l2_u32(&vis[sp_nb >> 5]) : 0xffffffffu;
+                }
 #pragma unroll
                 for (int e = 0; e < STAGE; ++e) {
                     if (e >= g) break;
@@ -437,6 +481,11 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
                 }
                 __syncwarp();
             }
+
+            // codes of the look-ahead neighbours that are still unvisited, towards L2
+            if (sp_node != 0xffffffffu && (int)lane < min((int)sp_cnt, 32) && sp_nb < nn &&
+                sp_sl < nn && (sp_word & (1u << (sp_nb & 31))) == 0)
+                prefetch_l2(p.codes + (size_t)sp_sl * DIM, DIM);
 
             // batched merge (every gathered neighbour while filling): lane j holds
             // candidate j, candidates are lanes [0, ns)

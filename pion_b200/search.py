@@ -438,20 +438,23 @@ class HNSWIndex(_Index):
         super().__init__(ctx, h)
         self.dim = lay.dim
 
-    def search(self, q, k: int, ef: int):
-        """q float32 [nq, 1536] -> (node ids int32 [nq, k], pool distances float32)."""
+    def search(self, q, k: int, ef: int, ctx: Context | None = None):
+        """q float32 [nq, 1536] -> (node ids int32 [nq, k], pool distances float32).
+        `ctx`: another context on the same device (a registered graph is read-only and
+        may serve every worker's context at once); default the registering one."""
+        c = ctx or self.ctx
         pq, mem, kq = _ptr(q, np.float32, "q")
         nq = q.shape[0]
         ids, dist, pi, pv = _outputs(mem == MEM_DEVICE, nq, k,
                                      q.device if mem == MEM_DEVICE else None)
-        with _TorchStream(self.ctx, mem):
-            self.ctx.check(self.ctx.lib.pion_v_b200_hnsw_search(self.ctx.h, self.h, pq, nq, k,
-                                                                ef, pi, pv, mem))
+        with _TorchStream(c, mem):
+            c.check(c.lib.pion_v_b200_hnsw_search(c.h, self.h, pq, nq, k, ef, pi, pv, mem))
         return ids, dist
 
-    def last_stats(self) -> dict:
+    def last_stats(self, ctx: Context | None = None) -> dict:
         """Work of the context's last search: level-0 evaluations, expansions, upper-level
         evaluations."""
+        c = ctx or self.ctx
         out = (ctypes.c_int64 * 3)()
-        self.ctx.check(self.ctx.lib.pion_v_b200_hnsw_last_stats(self.ctx.h, out))
+        c.check(c.lib.pion_v_b200_hnsw_last_stats(c.h, out))
         return dict(zip(("evals", "expansions", "upper_evals"), list(out)))
