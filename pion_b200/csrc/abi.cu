@@ -478,36 +478,28 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         const int n_qt = (nqi + fi8_query_tile() - 1) / fi8_query_tile();
         const int n_tiles = (int)((ix->n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
         const int lps = fi8_lists_per_split(kk);
-        // Threshold pre-pass over a sample of the first tiles, in two stages: a seed
-        // of kSeedTiles scored without a bound, then the rest of the sample with the
-        // seed's k-th score as bound.  The sample's k-th score per query is an exact
-        // lower bound of the final k-th score, handed to the main pass so that its
-        // integer pre-filter rejects almost every row from the start.
+        // Threshold pass over a sample of the first tiles: one exact score per 32-row chunk
+        // (bound_mode), whose k-th best per query is an exact lower bound of the final
+        // k-th score; the main pass starts from it, so its integer pre-filter rejects
+        // almost every row at once.  The main pass then scores every tile.
         const bool pre = use_prepass(n_tiles, kk, "PION_B200_I8_PREPASS");
         const int pre_tiles = pre ? prepass_tiles(kk) : 0;
-        const int main_begin = pre_tiles;
-        const int splits = fi8_choose_splits(n_qt, n_tiles - main_begin, ctx->num_sms);
-        const int n_lists = splits * lps + (pre ? 1 : 0);
-        // seed stage: one tile per CTA; sample stage: about one wave of CTAs
-        const int seed_splits = pre ? kSeedTiles : 0;
-        int samp_splits = pre ? ctx->num_sms / n_qt : 0;
-        if (pre) {
-            const int cap = (pre_tiles - kSeedTiles) / 2;
-            samp_splits = samp_splits < 1 ? 1 : (samp_splits > cap ? cap : samp_splits);
-        }
-        const int seed_lists = seed_splits * lps;
-        const int samp_lists = samp_splits * lps + 1;  // + the seed's merged list
+        const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
+        const int n_lists = splits * lps;
+        int bnd_splits = pre ? ctx->num_sms / n_qt : 0;
+        if (pre) bnd_splits = bnd_splits < 1 ? 1 : (bnd_splits > pre_tiles ? pre_tiles : bnd_splits);
+        const int bnd_lists = bnd_splits * lps;
         const size_t ncand = (size_t)nq * n_lists * kk;
-        const size_t nseed = (size_t)nq * seed_lists * kk;
-        const size_t nsamp = (size_t)nq * samp_lists * kk;
-        if (ensure(ctx->scratch, (ncand + nseed + nsamp) * 8) != 0)
+        const size_t nbnd = (size_t)nq * bnd_lists * kk;
+        const size_t nthr = pre ? (size_t)nq * kk : 0;
+        if (ensure(ctx->scratch, (ncand + nbnd + nthr) * 8) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn: scratch");
         float* cv = static_cast<float*>(ctx->scratch.ptr);
         int32_t* ci = reinterpret_cast<int32_t*>(cv + ncand);
-        float* sv = reinterpret_cast<float*>(ci + ncand);
-        int32_t* si = reinterpret_cast<int32_t*>(sv + nseed);
-        float* pv = reinterpret_cast<float*>(si + nseed);
-        int32_t* pi = reinterpret_cast<int32_t*>(pv + nsamp);
+        float* bv = reinterpret_cast<float*>(ci + ncand);
+        int32_t* bi = reinterpret_cast<int32_t*>(bv + nbnd);
+        float* tv = reinterpret_cast<float*>(bi + nbnd);
+        int32_t* ti = reinterpret_cast<int32_t*>(tv + nthr);
         CUtensorMap tmap_q;
         if (make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, dq, (uint64_t)dim,
                          (uint64_t)nq, (uint64_t)dim, (uint32_t)fi8_k_block(),
@@ -526,51 +518,31 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         L.status = ctx->d_status;
         timing_begin(ctx);
         if (pre) {
-            // seed: tiles [0, kSeedTiles), no bound
             L.tile_begin = 0;
-            L.tile_end = kSeedTiles;
-            L.n_splits = seed_splits;
-            L.n_lists = seed_lists;
-            L.cand_val = sv;
-            L.cand_idx = si;
+            L.tile_end = pre_tiles;
+            L.n_splits = bnd_splits;
+            L.n_lists = bnd_lists;
+            L.cand_val = bv;
+            L.cand_idx = bi;
             L.thr0 = nullptr;
+            L.bound_mode = 1;
             rc = launch_flat_i8_tc(L, st);
             ctx->launches++;
-            const size_t seed_slot = (size_t)(samp_lists - 1) * kk;
-            if (rc == 0) {  // the seed's top-k becomes the sample stage's last list
-                rc = launch_merge_lists(sv, si, nqi, seed_lists, kk, 0, true, pv + seed_slot,
-                                        pi + seed_slot, st, false, samp_lists * kk);
-                ctx->launches++;
-            }
-            if (rc == 0) {  // rest of the sample, bounded by the seed
-                L.tile_begin = kSeedTiles;
-                L.tile_end = pre_tiles;
-                L.n_splits = samp_splits;
-                L.n_lists = samp_lists;
-                L.cand_val = pv;
-                L.cand_idx = pi;
-                L.thr0 = pv + seed_slot + (kk - 1);
-                L.thr0_stride = samp_lists * kk;
-                rc = launch_flat_i8_tc(L, st);
-                ctx->launches++;
-            }
-            if (rc == 0) {  // the sample's top-k becomes the main pass's last list
-                rc = launch_merge_lists(pv, pi, nqi, samp_lists, kk, 0, true,
-                                        cv + (size_t)(n_lists - 1) * kk,
-                                        ci + (size_t)(n_lists - 1) * kk, st, false,
-                                        n_lists * kk);
+            if (rc == 0) {  // per query: the k best chunk scores; the k-th is the bound
+                rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, 0, true, tv, ti, st);
                 ctx->launches++;
             }
         }
         if (rc == 0) {
-            L.tile_begin = main_begin;
+            L.tile_begin = 0;
             L.tile_end = n_tiles;
             L.n_splits = splits;
             L.n_lists = n_lists;
             L.cand_val = cv;
             L.cand_idx = ci;
-            L.thr0 = pre ? cv + (size_t)(n_lists - 1) * kk + (kk - 1) : nullptr;
-            L.thr0_stride = n_lists * kk;
+            L.thr0 = pre ? tv + (kk - 1) : nullptr;
+            L.thr0_stride = kk;
+            L.bound_mode = 0;
             rc = launch_flat_i8_tc(L, st);
             ctx->launches++;
         }

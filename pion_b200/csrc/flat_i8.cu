@@ -61,6 +61,7 @@ struct TcParams {
     int kblocks;
     int n_lists;               // candidate lists per query in cand_* (layout [nq][n_lists][k])
     int list_base;             // first list this launch writes
+    int bound_mode;            // 1: keep one exact score per 32-row chunk (threshold pass)
     float* cand_val;
     int32_t* cand_idx;
     int* status;
@@ -144,6 +145,48 @@ __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], int64_t col0
         }
     }
     __syncwarp();  // the stash is rewritten by the next chunk
+}
+
+// Threshold pass: one exact score per 32-column chunk, that of the chunk's largest dot
+// (first column on ties), offered to the top-k.  The rows offered are distinct, so the
+// k-th best of them is at most the k-th best score of the chunks' rows: a lower bound
+// of the final k-th score that costs one candidate per chunk instead of every column
+// above the running threshold.
+template <int KCAP>
+__device__ __forceinline__ void bound_chunk(const uint32_t (&r)[32], int64_t col0, int64_t valid,
+                                            float rs_lane, float qs, float inv, int k,
+                                            QueryTop<KCAP>& st) {
+    int32_t mx = INT32_MIN;
+    int jm = 0;
+    bool any = false;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int32_t v = (int32_t)r[j];
+        const bool take = j < valid && (!any || v > mx);
+        mx = take ? v : mx;
+        jm = take ? j : jm;
+        any = any || j < valid;
+    }
+    const float rs = __shfl_sync(0xffffffffu, rs_lane, jm);  // lane j holds column j's scale
+    if (any && mx > st.dmin) {
+        const float s = i8_score(mx, rs, qs);
+        if (s > st.thr) {
+            st.top.insert(s, (int32_t)(col0 + jm));
+            st.thr = fmaxf(st.top.kth(k), st.floor_thr);
+            st.dmin = dot_bound(st.thr, inv);
+        }
+    }
+}
+
+template <int KCAP>
+__device__ __forceinline__ void process_chunk(bool bound, const uint32_t (&r)[32], int64_t col0,
+                                              int64_t valid, float rs_lane, float qs, float inv,
+                                              int k, uint32_t* stash, float* stash_rs, int lane,
+                                              QueryTop<KCAP>& st) {
+    if (bound)
+        bound_chunk<KCAP>(r, col0, valid, rs_lane, qs, inv, k, st);
+    else
+        scan_chunk<KCAP>(r, col0, valid, rs_lane, qs, inv, k, stash, stash_rs, lane, st);
 }
 
 template <int KCAP, int EPI_WARPS>
@@ -291,6 +334,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
             if (t0 > -INFINITY) st.floor_thr = nextafterf(t0, -INFINITY);
         }
         st.thr = st.floor_thr;
+        const bool bound = p.bound_mode != 0;
         for (int t = 0; t < my_tiles; ++t) {
             const int buf = t & 1;
             const uint32_t use = (uint32_t)(t >> 1);
@@ -323,14 +367,15 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
                 for (int c = 0; c < CHUNKS; c += 2) {
                     __syncwarp();
                     tmem_ld32(taddr + (uint32_t)((c + 1) * 32), rb);
-                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, sel_rs<CHUNKS>(rsv, c),
-                                     qs, inv, p.k, stash, stash_rs, lane, st);
+                    process_chunk<KCAP>(bound, ra, col0 + c * 32, valid - c * 32,
+                                        sel_rs<CHUNKS>(rsv, c), qs, inv, p.k, stash, stash_rs,
+                                        lane, st);
                     __syncwarp();
                     tmem_ld_wait_regs(rb);
                     if (c + 2 < CHUNKS) tmem_ld32(taddr + (uint32_t)((c + 2) * 32), ra);
-                    scan_chunk<KCAP>(rb, col0 + (c + 1) * 32, valid - (c + 1) * 32,
-                                     sel_rs<CHUNKS>(rsv, c + 1), qs, inv, p.k, stash,
-                                     stash_rs, lane, st);
+                    process_chunk<KCAP>(bound, rb, col0 + (c + 1) * 32, valid - (c + 1) * 32,
+                                        sel_rs<CHUNKS>(rsv, c + 1), qs, inv, p.k, stash,
+                                        stash_rs, lane, st);
                     __syncwarp();
                     if (c + 2 < CHUNKS) tmem_ld_wait_regs(ra);
                 }
@@ -342,8 +387,9 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
                     __syncwarp();
                     tmem_ld32(taddr + (uint32_t)(c * 32), ra);
                     tmem_ld_wait_regs(ra);
-                    scan_chunk<KCAP>(ra, col0 + c * 32, valid - c * 32, sel_rs<CHUNKS>(rsv, c),
-                                     qs, inv, p.k, stash, stash_rs, lane, st);
+                    process_chunk<KCAP>(bound, ra, col0 + c * 32, valid - c * 32,
+                                        sel_rs<CHUNKS>(rsv, c), qs, inv, p.k, stash, stash_rs,
+                                        lane, st);
                 }
             }
             tc_fence_before();
@@ -725,6 +771,7 @@ int launch_flat_i8_tc(const Fi8TcLaunch& L, cudaStream_t st) {
     p.kblocks = (L.dim + fi8::BK - 1) / fi8::BK;
     p.n_lists = L.n_lists;
     p.list_base = L.list_base;
+    p.bound_mode = L.bound_mode;
     p.cand_val = L.cand_val;
     p.cand_idx = L.cand_idx;
     p.status = L.status;

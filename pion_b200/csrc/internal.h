@@ -229,6 +229,7 @@ struct Fi8TcLaunch {
     int n_splits = 1;
     int n_lists = 1;
     int list_base = 0;
+    int bound_mode = 0;  // 1: threshold pass (one exact score per 32-row chunk)
     float* cand_val = nullptr;
     int32_t* cand_idx = nullptr;
     int* status = nullptr;
