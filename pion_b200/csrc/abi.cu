@@ -390,14 +390,25 @@ static int forced_i8_path() {
 
 int pion::prepass_tiles(int k) { return k * 8 > 64 ? k * 8 : 64; }
 
-// The pre-pass runs whenever the index is larger than its sample: without a starting
-// threshold every CTA's first tiles pay the full insertion cost, which measured twice
-// the whole step at 125K and 250K rows as well as at 1M.  The environment variable
+// Tiles sampled by the threshold pass: about 1/6 of the index (the main pass scores
+// every tile again), at least 8 and enough 32-row chunks for k candidates, at most
+// prepass_tiles(k).
+int pion::bound_tiles(int n_tiles, int k) {
+    int t = n_tiles / 6;
+    const int lo = 8 > (k + 3) / 4 ? 8 : (k + 3) / 4;
+    if (t < lo) t = lo;
+    const int hi = prepass_tiles(k);
+    return t > hi ? hi : t;
+}
+
+// The threshold pass runs whenever the index is more than twice its sample: without a
+// starting threshold every CTA's first tiles pay the full insertion cost, which measured
+// twice the whole step at 125K and 250K rows as well as at 1M.  The environment variable
 // `env` (PION_B200_I8_PREPASS / PION_B200_F32_PREPASS) = 0 turns it off.
 bool pion::use_prepass(int n_tiles, int k, const char* env) {
     const char* e = getenv(env);
     if (e && atoi(e) == 0) return false;
-    return n_tiles > prepass_tiles(k);
+    return n_tiles > 2 * bound_tiles(n_tiles, k);
 }
 
 extern "C" {
@@ -483,7 +494,7 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         // k-th score; the main pass starts from it, so its integer pre-filter rejects
         // almost every row at once.  The main pass then scores every tile.
         const bool pre = use_prepass(n_tiles, kk, "PION_B200_I8_PREPASS");
-        const int pre_tiles = pre ? prepass_tiles(kk) : 0;
+        const int pre_tiles = pre ? bound_tiles(n_tiles, kk) : 0;
         const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
         const int n_lists = splits * lps;
         int bnd_splits = pre ? ctx->num_sms / n_qt : 0;

@@ -204,23 +204,21 @@ int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, cons
         const int kc = ff32_kc(kk);
         const int n_qt = (nqi + ff32_query_tile() - 1) / ff32_query_tile();
         const int n_tiles = (int)((ix->n_rows + ff32_tile_rows() - 1) / ff32_tile_rows());
+        // Threshold pass over a sample of the first tiles (one approximate dot per 32-row
+        // chunk): the KC-th best is a lower bound of the final KC-th approximate dot, and
+        // the main pass starts from it and scores every tile.
         const bool pre = use_prepass(n_tiles, kc, "PION_B200_F32_PREPASS");
-        const int pre_tiles = pre ? prepass_tiles(kc) : 0;
-        const int splits = fi8_choose_splits(n_qt, n_tiles - pre_tiles, ctx->num_sms);
-        const int n_lists = splits + (pre ? 1 : 0);
-        const int seed_splits = pre ? kSeedTiles : 0;
-        int samp_splits = pre ? ctx->num_sms / n_qt : 0;
-        if (pre) {
-            const int cap = (pre_tiles - kSeedTiles) / 2;
-            samp_splits = samp_splits < 1 ? 1 : (samp_splits > cap ? cap : samp_splits);
-        }
-        const int samp_lists = samp_splits + 1;
+        const int pre_tiles = pre ? bound_tiles(n_tiles, kc) : 0;
+        const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
+        const int n_lists = splits;
+        int bnd_splits = pre ? ctx->num_sms / n_qt : 0;
+        if (pre) bnd_splits = bnd_splits < 1 ? 1 : (bnd_splits > pre_tiles ? pre_tiles : bnd_splits);
         const int chunks = ff32_exact_chunks();
         // scratch layout (floats / ints)
         const size_t n_qn = (size_t)nq * dim;
         const size_t n_cand = (size_t)nq * n_lists * kc;
-        const size_t n_seed = (size_t)nq * seed_splits * kc;
-        const size_t n_samp = (size_t)nq * samp_lists * kc;
+        const size_t n_bnd = (size_t)nq * bnd_splits * kc;
+        const size_t n_thr = (size_t)nq * kc;
         const size_t n_merged = (size_t)nq * kc;
         const size_t n_chunk = (size_t)nq * chunks * kk;
         size_t off = 0;
@@ -231,8 +229,8 @@ int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, cons
         };
         const size_t o_qn = take(n_qn), o_qh = take(n_qn / 2 + 1), o_ql = take(n_qn / 2 + 1),
                      o_qnorm = take(nq), o_cv = take(n_cand),
-                     o_ci = take(n_cand), o_sv = take(n_seed), o_si = take(n_seed),
-                     o_pv = take(n_samp), o_pi = take(n_samp), o_mv = take(n_merged),
+                     o_ci = take(n_cand), o_sv = take(n_bnd), o_si = take(n_bnd),
+                     o_pv = take(n_thr), o_pi = take(n_thr), o_mv = take(n_merged),
                      o_mi = take(n_merged), o_flag = take(nq + 1), o_chd = take(n_chunk),
                      o_chi = take(n_chunk);
         if (ensure(ctx->scratch, off) != 0)
@@ -283,48 +281,30 @@ int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, cons
         L.status = ctx->d_status;
         if (rc == 0 && pre) {
             L.tile_begin = 0;
-            L.tile_end = kSeedTiles;
-            L.n_splits = seed_splits;
-            L.n_lists = seed_splits;
+            L.tile_end = pre_tiles;
+            L.n_splits = bnd_splits;
+            L.n_lists = bnd_splits;
             L.cand_val = sv;
             L.cand_idx = si;
+            L.thr0 = nullptr;
+            L.bound_mode = 1;
             rc = launch_flat_bf16x3_tc(L, st);
             ctx->launches++;
-            const size_t seed_slot = (size_t)(samp_lists - 1) * kc;
             if (rc == 0) {
-                rc = launch_merge_lists(sv, si, nqi, seed_splits, kc, 0, true, pv + seed_slot,
-                                        pi + seed_slot, st, false, samp_lists * kc);
-                ctx->launches++;
-            }
-            if (rc == 0) {
-                L.tile_begin = kSeedTiles;
-                L.tile_end = pre_tiles;
-                L.n_splits = samp_splits;
-                L.n_lists = samp_lists;
-                L.cand_val = pv;
-                L.cand_idx = pi;
-                L.thr0 = pv + seed_slot + (kc - 1);
-                L.thr0_stride = samp_lists * kc;
-                rc = launch_flat_bf16x3_tc(L, st);
-                ctx->launches++;
-            }
-            if (rc == 0) {
-                rc = launch_merge_lists(pv, pi, nqi, samp_lists, kc, 0, true,
-                                        cv + (size_t)(n_lists - 1) * kc,
-                                        ci + (size_t)(n_lists - 1) * kc, st, false,
-                                        n_lists * kc);
+                rc = launch_merge_lists(sv, si, nqi, bnd_splits, kc, 0, true, pv, pi, st);
                 ctx->launches++;
             }
         }
         if (rc == 0) {
-            L.tile_begin = pre_tiles;
+            L.tile_begin = 0;
             L.tile_end = n_tiles;
             L.n_splits = splits;
             L.n_lists = n_lists;
             L.cand_val = cv;
             L.cand_idx = ci;
-            L.thr0 = pre ? cv + (size_t)(n_lists - 1) * kc + (kc - 1) : nullptr;
-            L.thr0_stride = n_lists * kc;
+            L.thr0 = pre ? pv + (kc - 1) : nullptr;
+            L.thr0_stride = kc;
+            L.bound_mode = 0;
             rc = launch_flat_bf16x3_tc(L, st);
             ctx->launches++;
         }

@@ -68,6 +68,7 @@ struct TcParams {
     int kseg;           // 128-byte K blocks per split term (ceil(dim / 64))
     int n_lists;
     int list_base;
+    int bound_mode;     // 1: keep one approximate dot per 32-row chunk (threshold pass)
     float* cand_val;
     int32_t* cand_idx;
     int* status;
@@ -109,6 +110,27 @@ __device__ __forceinline__ void scan_chunk_f(const uint32_t (&r)[32], int64_t co
         }
     }
     __syncwarp();
+}
+
+// Threshold pass: the largest approximate dot of each 32-column chunk (first column on
+// ties) is offered to the top list.  The rows offered are distinct, so the KC-th best of
+// them is a lower bound of the final KC-th approximate dot.
+template <int KCAP>
+__device__ __forceinline__ void bound_chunk_f(const uint32_t (&r)[32], int64_t col0,
+                                              int64_t valid, int kc, ApproxTop<KCAP>& st) {
+    float mx = -INFINITY;
+    int jm = -1;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float v = __uint_as_float(r[j]);
+        const bool take = j < valid && (jm < 0 || v > mx);
+        mx = take ? v : mx;
+        jm = take ? j : jm;
+    }
+    if (jm >= 0 && mx > st.thr) {
+        st.top.insert(mx, (int32_t)(col0 + jm));
+        st.thr = fmaxf(st.top.kth(kc), st.floor_thr);
+    }
 }
 
 // K runs over three segments of the dimension: (qh, vh), (qh, vl), (ql, vh).
@@ -269,7 +291,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
                 tmem_ld32(taddr + (uint32_t)(c * 32), ra);
                 tmem_ld_wait_regs(ra);
-                scan_chunk_f<KCAP>(ra, col0 + c * 32, valid - c * 32, p.kc, stash, lane, st);
+                if (p.bound_mode)
+                    bound_chunk_f<KCAP>(ra, col0 + c * 32, valid - c * 32, p.kc, st);
+                else
+                    scan_chunk_f<KCAP>(ra, col0 + c * 32, valid - c * 32, p.kc, stash, lane, st);
             }
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
@@ -292,8 +317,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-// exact_knn's query normalisation (src/commands/vector.mojo:1254-1260): a sequential
-// scalar sum of squares, one thread per query.
 // exact_knn's query normalisation (src/commands/vector.mojo:1254-1260): a sequential
 // sum of squares, inv = 1/sqrt(ss) (1 if ss == 0), y = x * inv.  A CTA stages ROWS
 // queries in shared memory with coalesced loads; one thread per query runs the
@@ -736,6 +759,7 @@ int launch_flat_bf16x3_tc(const Ff32TcLaunch& L, cudaStream_t st) {
     p.kseg = (L.dim + ff32::KEL - 1) / ff32::KEL;
     p.n_lists = L.n_lists;
     p.list_base = L.list_base;
+    p.bound_mode = L.bound_mode;
     p.cand_val = L.cand_val;
     p.cand_idx = L.cand_idx;
     p.status = L.status;

@@ -43,6 +43,7 @@ struct Ff32TcLaunch {
     int n_splits = 1;
     int n_lists = 1;
     int list_base = 0;
+    int bound_mode = 0;  // 1: threshold pass (one approximate dot per 32-row chunk)
     float* cand_val = nullptr;
     int32_t* cand_idx = nullptr;
     int* status = nullptr;
@@ -181,9 +182,8 @@ bool valid_ctx(const pion_b200_ctx* ctx);
 int use_device(pion_b200_ctx* ctx);
 size_t align_up(size_t x, size_t a);
 int prepass_tiles(int k);
+int bound_tiles(int n_tiles, int k);
 bool use_prepass(int n_tiles, int k, const char* env);
-// Unbounded seed of the threshold pre-pass (index tiles).
-constexpr int kSeedTiles = 8;
 int ensure(DevBuf& b, size_t bytes);
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
