@@ -473,35 +473,37 @@ __global__ void __launch_bounds__(SEL_THREADS)
 }
 
 // ---------------------------------------------------------------- rerank --
-// One warp per query: exact distances of the shortlist (in (distance, id) order),
-// then the k best by (score, shortlist position): the stable insertion sort of
+// One CTA per query: its 16 half-warps take the shortlist (in (distance, id) order) 16
+// rows at a time, exact 4-chain cosine distances with the rows prefetched into L2; then
+// warp 0 keeps the k best by (score, shortlist position): the stable insertion sort of
 // _exact_rescore keeps equal scores in shortlist order.
-__global__ void bq_rerank_kernel(const float* __restrict__ rows, int dim,
-                                 const float* __restrict__ qn, const int32_t* __restrict__ sl_id,
-                                 const int* __restrict__ sl_n, int S, int nq, int k,
-                                 int64_t id_base, float* __restrict__ out_d,
-                                 int32_t* __restrict__ out_i) {
+__global__ void __launch_bounds__(256) bq_rerank_kernel(
+    const float* __restrict__ rows, int dim, const float* __restrict__ qn,
+    const int32_t* __restrict__ sl_id, const int* __restrict__ sl_n, int S, int nq, int k,
+    int64_t id_base, float* __restrict__ out_d, int32_t* __restrict__ out_i) {
     extern __shared__ float rr[];
-    const int w = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int q = blockIdx.x * (blockDim.x / 32) + w;
+    const int q = blockIdx.x;
     if (q >= nq) return;
-    float* dist = rr + (size_t)w * S;
+    const int lane = threadIdx.x & 31;
+    float* dist = rr;
     const float* qv = qn + (size_t)q * dim;
     const int n = sl_n[q];
-    for (int j = lane; j < n; j += 32)
+    for (int j = threadIdx.x; j < n; j += blockDim.x)
         prefetch_row_f32_l2(rows + (size_t)sl_id[(size_t)q * S + j] * dim, dim);
-    const int half = lane >> 4, hl = lane & 15;
-    const unsigned hmask = half ? 0xffff0000u : 0x0000ffffu;
-    for (int j0 = 0; j0 < n; j0 += 2) {
-        const int j = j0 + half;
+    const int hw = threadIdx.x >> 4;  // 16 half-warps, one shortlisted row each
+    const int hl = lane & 15;
+    const unsigned hmask = (lane >> 4) ? 0xffff0000u : 0x0000ffffu;
+    const int halves = blockDim.x >> 4;
+    for (int j0 = 0; j0 < n; j0 += halves) {
+        const int j = j0 + hw;
         if (j < n) {
             const int32_t id = sl_id[(size_t)q * S + j];
             const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
             if (hl == 0) dist[j] = __fsub_rn(1.0f, s);
         }
     }
-    __syncwarp();
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
     for (int r = 0; r < k; ++r) {
         float bd = INFINITY;
         int bp = -1;
@@ -603,9 +605,8 @@ int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t*
                      const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
                      int32_t* out_i, cudaStream_t st) {
     if (nq <= 0) return 0;
-    const int warps = 4;
-    bq::bq_rerank_kernel<<<(nq + warps - 1) / warps, warps * 32, (size_t)warps * S * 4, st>>>(
-        rows, dim, qn, sl_id, sl_n, S, nq, k, id_base, out_d, out_i);
+    bq::bq_rerank_kernel<<<nq, 256, (size_t)S * 4, st>>>(rows, dim, qn, sl_id, sl_n, S, nq, k,
+                                                         id_base, out_d, out_i);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

@@ -429,46 +429,47 @@ __global__ void max_reduce_kernel(const float* __restrict__ x, int64_t n, float*
 
 // One warp per query: exact distances of the kc candidates (two per warp step, one
 // per half-warp), the k best by (distance, id), and the certificate.
-__global__ void rescore_certify_kernel(const float* __restrict__ rows, int dim,
-                                       const float* __restrict__ qn, const float* __restrict__ qnorm,
-                                       float row_norm_max, const float* __restrict__ cand_v,
-                                       const int32_t* __restrict__ cand_i, int nq, int kc, int k,
-                                       int64_t id_base, float* __restrict__ out_d,
-                                       int32_t* __restrict__ out_i, int* __restrict__ flagged,
-                                       int* __restrict__ n_flagged, int force_exact) {
+// One CTA per query: its 16 half-warps take the candidates 16 at a time (exact 4-chain
+// dots, candidate rows prefetched into L2 first), then warp 0 selects and certifies.
+__global__ void __launch_bounds__(256) rescore_certify_kernel(
+    const float* __restrict__ rows, int dim, const float* __restrict__ qn,
+    const float* __restrict__ qnorm, float row_norm_max, const float* __restrict__ cand_v,
+    const int32_t* __restrict__ cand_i, int nq, int kc, int k, int64_t id_base,
+    float* __restrict__ out_d, int32_t* __restrict__ out_i, int* __restrict__ flagged,
+    int* __restrict__ n_flagged, int force_exact) {
     extern __shared__ float sm[];
-    const int w = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int q = blockIdx.x * (blockDim.x / 32) + w;
+    const int q = blockIdx.x;
     if (q >= nq) return;
-    float* dist = sm + (size_t)w * kc * 2;
+    const int lane = threadIdx.x & 31;
+    float* dist = sm;
     int32_t* ids = reinterpret_cast<int32_t*>(dist + kc);
     const float* qv = qn + (size_t)q * dim;
-    const int half = lane >> 4;
+    const int hw = threadIdx.x >> 4;  // half-warp of the CTA
     const int hl = lane & 15;
-    const unsigned hmask = half ? 0xffff0000u : 0x0000ffffu;
-    int n_valid = 0;
-    for (int j = 0; j < kc; ++j) n_valid += cand_i[(size_t)q * kc + j] >= 0 ? 1 : 0;
+    const unsigned hmask = (lane >> 4) ? 0xffff0000u : 0x0000ffffu;
     if ((dim & 3) == 0)
-        for (int j = lane; j < kc; j += 32) {
+        for (int j = threadIdx.x; j < kc; j += blockDim.x) {
             const int32_t id = cand_i[(size_t)q * kc + j];
             if (id >= 0) prefetch_row_f32_l2(rows + (size_t)id * dim, dim);
         }
-    for (int j0 = 0; j0 < kc; j0 += 2) {
-        const int j = j0 + half;
+    const int halves = blockDim.x >> 4;
+    for (int j0 = 0; j0 < kc; j0 += halves) {
+        const int j = j0 + hw;
         const int32_t id = j < kc ? cand_i[(size_t)q * kc + j] : -1;
         float d = INFINITY;
         if (id >= 0) {
             const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
             d = __fsub_rn(1.0f, s);
-        } else {
-            __syncwarp(hmask);
         }
         if (hl == 0 && j < kc) {
             dist[j] = d;
             ids[j] = id;
         }
     }
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    int n_valid = 0;
+    for (int j = 0; j < kc; ++j) n_valid += ids[j] >= 0 ? 1 : 0;
     __syncwarp();
     // k rounds of warp arg-min over the kc candidates
     float kth_d = INFINITY;
@@ -778,11 +779,10 @@ int launch_rescore_certify(const float* rows, int dim, const float* qn, const fl
                            int kc, int k, int64_t id_base, float* out_d, int32_t* out_i,
                            int* flagged, int* n_flagged, int force_exact, cudaStream_t st) {
     if (nq <= 0) return 0;
-    const int warps = 4;
-    const size_t smem = (size_t)warps * kc * 8;
-    ff32::rescore_certify_kernel<<<(nq + warps - 1) / warps, warps * 32, smem, st>>>(
-        rows, dim, qn, qnorm, row_norm_max, cand_v, cand_i, nq, kc, k, id_base, out_d, out_i,
-        flagged, n_flagged, force_exact);
+    const size_t smem = (size_t)kc * 8;
+    ff32::rescore_certify_kernel<<<nq, 256, smem, st>>>(rows, dim, qn, qnorm, row_norm_max,
+                                                        cand_v, cand_i, nq, kc, k, id_base, out_d,
+                                                        out_i, flagged, n_flagged, force_exact);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
