@@ -109,6 +109,56 @@ int64_t pion_v_pkm_combine_topk(const float *s0, const int32_t *i0, int64_t k0,
                                 const float *s1, const int32_t *i1, int64_t k1, int64_t s_cols,
                                 int64_t k, int32_t *out_id, float *out_score);
 
+/* src/common/heap.mojo:133-160: LinearPool's fields, in order (entries are 8-byte
+ * (f32 dist, u32 id) pairs, bit 31 of id = expanded). */
+typedef struct pion_linear_pool {
+    void *entries;
+    int64_t capacity;
+    int64_t size;
+    int64_t cursor;
+    int64_t ef;
+} pion_linear_pool;
+
+/* src/vector/beam_view.mojo:11-26: BeamView1536's fields, in order. */
+typedef struct pion_beam_view_1536 {
+    pion_linear_pool *pool;
+    int64_t ef;
+    float query_norm_sq;
+    float query_prefix_norm_sq;
+    const int8_t *query_int8;
+    const uint32_t *l0_compact;
+    const uint32_t *l0_slots;
+    int64_t num_nodes;
+    const uint8_t *deleted;
+    uint16_t *visited;
+    uint16_t cur_epoch;
+    const int8_t *compact_buffer;
+    int64_t compact_stride;
+    int64_t compact_hdr;
+    const void *nodes;
+} pion_beam_view_1536;
+
+/* src/vector/vector_abi.mojo:31-36 (beam_search_1536) -> beam_search_1536_ref
+ * (src/vector/reference/beam_1536.mojo:85-135): the level-0 beam of one query, on the GPU.
+ * Reads the view's pool (as search_fp32_scored seeds it: the start node, marked visited),
+ * runs the beam and writes the pool back entry for entry (ids with their expanded bit,
+ * distances, size; cursor = size), exactly as the reference would leave it.  The graph
+ * (l0_compact, l0_slots, compact_buffer) is copied to the GPU on the first call for those
+ * buffers and reused while the same pointers and sizes come back; call
+ * pion_v_b200_beam_forget after changing them in place.  The visited array is not
+ * written (the engine starts a new epoch per query).  Returns 0, or a negative code with
+ * a message on stderr. */
+int64_t pion_v_beam_1536(pion_beam_view_1536 *view);
+
+/* src/vector/vector_abi.mojo:40-46 (quant_beam_search_1536) -> the quantised beams (INT4 / INT3+QJL / INT2,
+ * src/vector/reference/quant_beams_1536.mojo): not implemented on the GPU; returns -1 and
+ * prints a message (the caller's pool is left unchanged). */
+int64_t pion_v_quant_beam_1536(void *view);
+
+/* Drops the GPU copy of a graph registered by pion_v_beam_1536 (all of them when
+ * l0_compact is NULL). */
+int pion_v_b200_beam_forget(const uint32_t *l0_compact);
+
 /* ==================================================================== group 2 */
 
 /* Context lifecycle.  `device` < 0 picks PION_B200_DEVICE or 0.  `worker_id` is

@@ -81,6 +81,8 @@ def lib() -> ctypes.CDLL:
             L.orc_hnsw_search.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p, _p, _i32]
             L.orc_hnsw_search.restype = _i32
             L.orc_hnsw_query_codes.argtypes = [_p, _p, _i64, _p]
+            L.orc_hnsw_beam_pool.argtypes = [_p, _p, _f32, _i64, _p, _p, _i64, _i64, _p, _p]
+            L.orc_hnsw_beam_pool.restype = _i64
             _lib = L
     return _lib
 
@@ -352,3 +354,23 @@ def hnsw_query_codes(graph: dict, queries):
     out = np.empty(q.shape, np.int8)
     L.orc_hnsw_query_codes(ctypes.byref(lay), qp, q.shape[0], out.ctypes.data_as(_p))
     return out
+
+
+def hnsw_beam_pool(graph: dict, q_codes, qn: float, ef: int, init_d, init_id, cursor: int = 0):
+    """beam_search_1536_ref (src/vector/reference/beam_1536.mojo:85-135) from a seeded
+    LinearPool: q_codes int8[1536], qn the query's |code|^2 as a float, the pool's
+    (dist, id) entries (bit 31 of id = expanded) and cursor.  Returns the final pool as
+    (dist float32 [size], id uint32 [size])."""
+    L = lib()
+    lay, keep = _hnsw_layout(graph)
+    q, qp = _c(q_codes, np.int8)
+    d0, dp = _c(init_d, np.float32)
+    i0, ip = _c(init_id, np.uint32)
+    out_d = np.empty(max(1, ef), np.float32)
+    out_i = np.empty(max(1, ef), np.uint32)
+    n = L.orc_hnsw_beam_pool(ctypes.byref(lay), qp, float(qn), ef, dp, ip, len(d0), cursor,
+                             out_d.ctypes.data_as(_p), out_i.ctypes.data_as(_p))
+    if n < 0:
+        raise ValueError("orc_hnsw_beam_pool failed")
+    del keep
+    return out_d[:n].copy(), out_i[:n].copy()

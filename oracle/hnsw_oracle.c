@@ -194,6 +194,73 @@ static int gather(const orc_hnsw_layout *L, uint32_t c, uint16_t *visited, uint1
     return n;
 }
 
+/* beam_search_1536_ref (src/vector/reference/beam_1536.mojo:85-135) on a seeded pool. */
+static int beam_1536(const orc_hnsw_layout *L, const int8_t *q, float qn, uint16_t *visited,
+                     uint16_t epoch, linear_pool *pool_p, int64_t *evals, int64_t *expansions) {
+    linear_pool pool = *pool_p;
+    int64_t n_evals = 0, n_expand = 0;
+    struct hnsw_scratch s;
+    s.visited = visited;
+    s.epoch = epoch;
+    uint32_t idxs[33];
+    const int8_t *ptrs[33];
+    /* Fill: expand the nearest unexpanded entry until the pool holds ef. */
+    while (pool_has_next(&pool) && pool.size < pool.ef) {
+        const uint32_t c = pool_pop(&pool);
+        n_expand++;
+        const int n = gather(L, c, s.visited, s.epoch, idxs, ptrs);
+        if (n < 0) return -1;
+        n_evals += n;
+        const int batched = n - n % 4;
+        for (int j = 0; j < n; ++j) {
+            float d;
+            if (j < batched)
+                d = (qn + slot_norm(ptrs[j])) - 2.0f * (float)ref_dot(q, ptrs[j], HN_DIM);
+            else
+                d = (float)ref_l2(q, ptrs[j], HN_DIM);
+            pool_insert(&pool, d, idxs[j]);
+        }
+    }
+    /* Prune: expand until every pool entry is expanded. */
+    while (pool_has_next(&pool)) {
+        const uint32_t c = pool_pop(&pool);
+        n_expand++;
+        float worst = pool_worst(&pool);
+        const int n = gather(L, c, s.visited, s.epoch, idxs, ptrs);
+        if (n < 0) return -1;
+        n_evals += n;
+        const int batched = n - n % 4;
+        for (int j = 0; j < n; ++j) {
+            const int8_t *p = ptrs[j];
+            if (j < batched) {
+                const float dot =
+                    (float)ref_dot(q, p, 256) + (float)ref_dot(q + 256, p + 256, 1280);
+                const float d = (qn + slot_norm(p)) - 2.0f * dot;
+                if (pool_insert(&pool, d, idxs[j])) worst = pool_worst(&pool);
+            } else {
+                const float d_prefix = (float)ref_l2(q, p, 256);
+                if (d_prefix < worst * 0.175f) {
+                    float running = d_prefix;
+                    int exited = 0;
+                    for (int b = 0; b < 5; ++b) {
+                        const int off = 256 + b * 256;
+                        running += (float)ref_l2(q + off, p + off, 256);
+                        if (running > worst) {
+                            exited = 1;
+                            break;
+                        }
+                    }
+                    if (!exited && running < worst) pool_insert(&pool, running, idxs[j]);
+                }
+            }
+        }
+    }
+    *pool_p = pool;
+    *evals += n_evals;
+    *expansions += n_expand;
+    return 0;
+}
+
 static void hnsw_item(void *ctx, int64_t t, void *raw) {
     struct hnsw_job *job = (struct hnsw_job *)ctx;
     const orc_hnsw_layout *L = job->L;
@@ -263,64 +330,9 @@ static void hnsw_item(void *ctx, int64_t t, void *raw) {
     pool_reset(&pool, job->ef);
     pool_insert(&pool, (float)ref_l2(q, slot_vec(L, L->node_slot[curr]), HN_DIM), curr);
 
-    uint32_t idxs[33];
-    const int8_t *ptrs[33];
-    /* Fill: expand the nearest unexpanded entry until the pool holds ef. */
-    while (pool_has_next(&pool) && pool.size < pool.ef) {
-        const uint32_t c = pool_pop(&pool);
-        n_expand++;
-        const int n = gather(L, c, s.visited, s.epoch, idxs, ptrs);
-        if (n < 0) {
-            job->bad++;
-            return;
-        }
-        n_evals += n;
-        const int batched = n - n % 4;
-        for (int j = 0; j < n; ++j) {
-            float d;
-            if (j < batched)
-                d = (qn + slot_norm(ptrs[j])) - 2.0f * (float)ref_dot(q, ptrs[j], HN_DIM);
-            else
-                d = (float)ref_l2(q, ptrs[j], HN_DIM);
-            pool_insert(&pool, d, idxs[j]);
-        }
-    }
-    /* Prune: expand until every pool entry is expanded. */
-    while (pool_has_next(&pool)) {
-        const uint32_t c = pool_pop(&pool);
-        n_expand++;
-        float worst = pool_worst(&pool);
-        const int n = gather(L, c, s.visited, s.epoch, idxs, ptrs);
-        if (n < 0) {
-            job->bad++;
-            return;
-        }
-        n_evals += n;
-        const int batched = n - n % 4;
-        for (int j = 0; j < n; ++j) {
-            const int8_t *p = ptrs[j];
-            if (j < batched) {
-                const float dot =
-                    (float)ref_dot(q, p, 256) + (float)ref_dot(q + 256, p + 256, 1280);
-                const float d = (qn + slot_norm(p)) - 2.0f * dot;
-                if (pool_insert(&pool, d, idxs[j])) worst = pool_worst(&pool);
-            } else {
-                const float d_prefix = (float)ref_l2(q, p, 256);
-                if (d_prefix < worst * 0.175f) {
-                    float running = d_prefix;
-                    int exited = 0;
-                    for (int b = 0; b < 5; ++b) {
-                        const int off = 256 + b * 256;
-                        running += (float)ref_l2(q + off, p + off, 256);
-                        if (running > worst) {
-                            exited = 1;
-                            break;
-                        }
-                    }
-                    if (!exited && running < worst) pool_insert(&pool, running, idxs[j]);
-                }
-            }
-        }
+    if (beam_1536(L, q, qn, s.visited, s.epoch, &pool, &n_evals, &n_expand) != 0) {
+        job->bad++;
+        return;
     }
     /* Drain: the first k entries, nearest first. */
     const int64_t n_out = job->k < pool.size ? job->k : pool.size;
@@ -355,4 +367,43 @@ int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, 
         stats3[2] += job.upper;
     }
     return job.bad ? -1 : 0;
+}
+
+/* The level-0 beam alone from a caller-seeded pool (the contract of the reference's
+ * pion_v_beam_1536): codes q[1536], qn = the query's |code|^2 as the view holds it, the
+ * pool's n_init entries (dist, id with bit 31 = expanded) and cursor; the nodes of the
+ * pool count as visited.  The final pool goes to out (ef entries at most); returns its
+ * size, or -1. */
+int64_t orc_hnsw_beam_pool(const orc_hnsw_layout *L, const int8_t *q, float qn, int64_t ef,
+                           const float *init_d, const uint32_t *init_id, int64_t n_init,
+                           int64_t cursor, float *out_d, uint32_t *out_id) {
+    if (ef < 1) ef = 1;
+    if (n_init > ef || n_init < 0) return -1;
+    uint16_t *visited = (uint16_t *)calloc((size_t)L->num_nodes, sizeof(uint16_t));
+    pool_entry *e = (pool_entry *)malloc((size_t)ef * sizeof(pool_entry));
+    if (!visited || !e) {
+        free(visited);
+        free(e);
+        return -1;
+    }
+    linear_pool pool;
+    pool.e = e;
+    pool.ef = ef;
+    pool.size = n_init;
+    pool.cursor = cursor < n_init ? cursor : n_init;
+    for (int64_t i = 0; i < n_init; ++i) {
+        e[i].dist = init_d[i];
+        e[i].id = init_id[i];
+        const uint32_t nd = init_id[i] & ~HN_CHECKED;
+        if (nd < (uint32_t)L->num_nodes) visited[nd] = 1;
+    }
+    int64_t evals = 0, expansions = 0;
+    const int rc = beam_1536(L, q, qn, visited, 1, &pool, &evals, &expansions);
+    for (int64_t i = 0; rc == 0 && i < pool.size; ++i) {
+        out_d[i] = e[i].dist;
+        out_id[i] = e[i].id;
+    }
+    free(visited);
+    free(e);
+    return rc == 0 ? pool.size : -1;
 }

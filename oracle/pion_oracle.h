@@ -97,6 +97,11 @@ int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, 
 void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
                           int8_t *codes);
 
+/* beam_search_1536_ref from a caller-seeded pool (pion_v_beam_1536's contract). */
+int64_t orc_hnsw_beam_pool(const orc_hnsw_layout *L, const int8_t *q, float qn, int64_t ef,
+                           const float *init_d, const uint32_t *init_id, int64_t n_init,
+                           int64_t cursor, float *out_d, uint32_t *out_id);
+
 /* ---- internal: dynamic parallel-for over [0, n) with per-thread zeroed scratch */
 typedef void (*orc_item_fn)(void *ctx, int64_t item, void *scratch);
 void orc_parallel_for(int64_t n, int nthreads, size_t scratch_bytes, orc_item_fn fn, void *ctx);

@@ -75,7 +75,28 @@ SIGNATURES = {
     "pion_v_b200_register_hnsw": (_I, [_P, _P, _PP]),
     "pion_v_b200_hnsw_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_hnsw_last_stats": (_I, [_P, _P]),
+    "pion_v_beam_1536": (_I64, [_P]),
+    "pion_v_quant_beam_1536": (_I64, [_P]),
+    "pion_v_b200_beam_forget": (_I, [_P]),
 }
+
+
+class LinearPool(ctypes.Structure):
+    """pion_linear_pool (include/pion_vector_b200.h): LinearPool's fields in order."""
+    _fields_ = [("entries", ctypes.c_void_p), ("capacity", ctypes.c_int64),
+                ("size", ctypes.c_int64), ("cursor", ctypes.c_int64), ("ef", ctypes.c_int64)]
+
+
+class BeamView1536(ctypes.Structure):
+    """pion_beam_view_1536 (include/pion_vector_b200.h): BeamView1536's fields in order."""
+    _fields_ = [("pool", ctypes.POINTER(LinearPool)), ("ef", ctypes.c_int64),
+                ("query_norm_sq", ctypes.c_float), ("query_prefix_norm_sq", ctypes.c_float),
+                ("query_int8", ctypes.c_void_p), ("l0_compact", ctypes.c_void_p),
+                ("l0_slots", ctypes.c_void_p), ("num_nodes", ctypes.c_int64),
+                ("deleted", ctypes.c_void_p), ("visited", ctypes.c_void_p),
+                ("cur_epoch", ctypes.c_uint16), ("compact_buffer", ctypes.c_void_p),
+                ("compact_stride", ctypes.c_int64), ("compact_hdr", ctypes.c_int64),
+                ("nodes", ctypes.c_void_p)]
 
 
 class HnswLayout(ctypes.Structure):

@@ -4,6 +4,8 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstring>
+#include <mutex>
 #include <new>
 #include <thread>
 #include <vector>
@@ -364,6 +366,190 @@ int pion_v_b200_hnsw_last_stats(pion_b200_ctx* ctx, int64_t* out3) {
         cudaStreamSynchronize(ctx->stream) != cudaSuccess)
         return set_error(ctx, PION_B200_ECUDA, "hnsw_last_stats: copy failed");
     for (int i = 0; i < 3; ++i) out3[i] = (int64_t)v[i];
+    return 0;
+}
+
+// ------------------------------------------------- pion_v_beam_1536 (compat)
+
+namespace {
+
+// Level-0 graphs registered by pion_v_beam_1536, keyed by the host buffers of the view.
+struct BeamGraph {
+    const uint32_t* l0c;
+    const uint32_t* l0s;
+    const int8_t* comp;
+    int64_t n, stride, hdr;
+    int device;
+    int8_t* codes = nullptr;
+    float* norms = nullptr;
+    uint32_t* l0_compact = nullptr;
+    uint32_t* l0_slots = nullptr;
+};
+std::mutex g_beam_mu;
+std::vector<BeamGraph*> g_beam_graphs;
+
+void free_beam_graph(BeamGraph* g) {
+    cudaSetDevice(g->device);
+    cudaDeviceSynchronize();
+    void* ps[] = {g->codes, g->norms, g->l0_compact, g->l0_slots};
+    for (void* p : ps)
+        if (p) cudaFree(p);
+    delete g;
+}
+
+int beam_fail(const char* what) {
+    fprintf(stderr, "pion_vector_b200: pion_v_beam_1536: %s\n", what);
+    return -1;
+}
+
+// The registered copy of the view's graph (copied and checked on first use).
+BeamGraph* beam_graph(pion_b200_ctx* ctx, const pion_beam_view_1536* v, const char** why) {
+    std::lock_guard<std::mutex> lock(g_beam_mu);
+    for (BeamGraph* g : g_beam_graphs)
+        if (g->l0c == v->l0_compact && g->l0s == v->l0_slots && g->comp == v->compact_buffer &&
+            g->n == v->num_nodes && g->stride == v->compact_stride && g->hdr == v->compact_hdr &&
+            g->device == ctx->device)
+            return g;
+    const int64_t n = v->num_nodes;
+    if (v->compact_hdr != 8 || v->compact_stride % 16 != 0 ||
+        v->compact_stride < v->compact_hdr + hnsw_dim() + 8) {
+        *why = "compact layout must have an 8-byte header and a 16-byte multiple stride";
+        return nullptr;
+    }
+    for (int64_t i = 0; i < n; ++i) {  // the slots the beam will read stay in bounds
+        const uint32_t* row = v->l0_compact + i * 33;
+        const uint32_t c = row[0] < 32 ? row[0] : 32;
+        for (uint32_t k = 0; k < c; ++k)
+            if (row[1 + k] < (uint32_t)n && v->l0_slots[i * 33 + 1 + k] >= (uint32_t)n) {
+                *why = "an l0_slots entry is out of range";
+                return nullptr;
+            }
+    }
+    BeamGraph* g = new (std::nothrow) BeamGraph{v->l0_compact, v->l0_slots, v->compact_buffer, n,
+                                                v->compact_stride, v->compact_hdr, ctx->device};
+    if (!g) {
+        *why = "out of host memory";
+        return nullptr;
+    }
+    int8_t* slots = nullptr;
+    int rc = upload(&slots, v->compact_buffer, (size_t)n * v->compact_stride);
+    if (!rc && (cudaMalloc(&g->codes, (size_t)n * hnsw_dim()) != cudaSuccess ||
+                cudaMalloc(&g->norms, (size_t)n * sizeof(float)) != cudaSuccess)) {
+        cudaGetLastError();
+        rc = PION_B200_ENOMEM;
+    }
+    if (!rc)
+        rc = launch_hnsw_relayout(slots, n, v->compact_stride, v->compact_hdr, g->codes, g->norms,
+                                  ctx->stream);
+    if (!rc && cudaStreamSynchronize(ctx->stream) != cudaSuccess) rc = PION_B200_ECUDA;
+    if (slots) cudaFree(slots);
+    if (!rc) rc = upload(&g->l0_compact, v->l0_compact, (size_t)n * 33);
+    if (!rc) rc = upload(&g->l0_slots, v->l0_slots, (size_t)n * 33);
+    if (rc) {
+        free_beam_graph(g);
+        *why = "device copy of the graph failed";
+        return nullptr;
+    }
+    g_beam_graphs.push_back(g);
+    return g;
+}
+
+}  // namespace
+
+int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
+    if (!v || !v->pool || !v->pool->entries || !v->query_int8 || !v->l0_compact ||
+        !v->l0_slots || !v->compact_buffer || v->num_nodes <= 0 || v->num_nodes >= 0x7fffffff)
+        return beam_fail("bad view");
+    const int64_t ef = v->ef < 1 ? 1 : v->ef;
+    if (ef > 1024) return beam_fail("ef > 1024");
+    pion_linear_pool* pool = v->pool;
+    if (pool->size < 0 || pool->size > ef || pool->cursor < 0) return beam_fail("bad pool");
+    pion_b200_ctx* ctx = compat_default_ctx("pion_v_beam_1536");
+    if (!ctx) return -1;
+    if (use_device(ctx) != 0) return beam_fail("cannot select the device");
+    const char* why = "";
+    BeamGraph* g = beam_graph(ctx, v, &why);
+    if (!g) return beam_fail(why);
+    cudaStream_t st = ctx->stream;
+    const int dim = hnsw_dim();
+    const size_t del_bytes = v->deleted ? (size_t)(v->num_nodes + 7) / 8 : 0;
+    const size_t o_q = 0, o_pool = align_up(dim, 256), o_size = o_pool + align_up(ef * 8, 256),
+                 o_del = o_size + 256, total = o_del + align_up(del_bytes, 256) + 256;
+    if (ensure(ctx->stage_in, total) != 0 || ensure(ctx->hnsw_misc, 64) != 0)
+        return beam_fail("out of device memory");
+    char* base = static_cast<char*>(ctx->stage_in.ptr);
+    if (cudaMemcpyAsync(base + o_q, v->query_int8, dim, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        (pool->size > 0 && cudaMemcpyAsync(base + o_pool, pool->entries, (size_t)pool->size * 8,
+                                           cudaMemcpyHostToDevice, st) != cudaSuccess) ||
+        (del_bytes && cudaMemcpyAsync(base + o_del, v->deleted, del_bytes, cudaMemcpyHostToDevice,
+                                      st) != cudaSuccess) ||
+        cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 32, st) != cudaSuccess)
+        return beam_fail("copy to the device failed");
+    const int warps = hnsw_warps_per_cta();
+    const int64_t vis_words = ((v->num_nodes + 31) / 32 + 3) / 4 * 4;
+    if (ensure(ctx->hnsw_visited, (size_t)warps * vis_words * 4) != 0)
+        return beam_fail("out of device memory");
+    if (hnsw_ctas_per_sm((int)ef) <= 0) return beam_fail("ef does not fit");
+    unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
+    HnswLaunch Lc;
+    Lc.codes = g->codes;
+    Lc.norms = g->norms;
+    Lc.l0_compact = g->l0_compact;
+    Lc.l0_slots = g->l0_slots;
+    Lc.deleted = del_bytes ? reinterpret_cast<const uint8_t*>(base + o_del) : nullptr;
+    Lc.num_nodes = v->num_nodes;
+    Lc.qcodes = reinterpret_cast<const int8_t*>(base + o_q);
+    Lc.qblk = reinterpret_cast<const int32_t*>(base + o_size);  // unused when starting from a pool
+    Lc.nq = 1;
+    Lc.k = 0;
+    Lc.ef = (int)ef;
+    Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+    Lc.vis_words = vis_words;
+    Lc.stats = stats;
+    Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
+    Lc.status = ctx->d_status;
+    Lc.ctas = 1;
+    Lc.pool_io = base + o_pool;
+    Lc.pool_size = (int)pool->size;
+    Lc.pool_cursor = (int)(pool->cursor < pool->size ? pool->cursor : pool->size);
+    Lc.qn_given = v->query_norm_sq;
+    Lc.pool_size_out = reinterpret_cast<int*>(base + o_size);
+    int rc = launch_hnsw_beam(Lc, st);
+    ctx->launches++;
+    if (rc != 0) return beam_fail("launch failed");
+    int out_size = 0;
+    if (cudaMemcpyAsync(&out_size, base + o_size, sizeof(int), cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return beam_fail("copy from the device failed");
+    if (out_size < 0 || out_size > ef) return beam_fail("bad pool size from the device");
+    if (out_size > 0 && cudaMemcpy(pool->entries, base + o_pool, (size_t)out_size * 8,
+                                   cudaMemcpyDeviceToHost) != cudaSuccess)
+        return beam_fail("copy from the device failed");
+    if (finish_sync(ctx) != 0) return beam_fail(pion_v_b200_last_error(ctx));
+    pool->size = out_size;
+    pool->cursor = out_size;
+    return 0;
+}
+
+int64_t pion_v_quant_beam_1536(void* view) {
+    (void)view;
+    fprintf(stderr,
+            "pion_vector_b200: pion_v_quant_beam_1536: the quantised beams (INT4/INT3/INT2) "
+            "are not implemented on the GPU\n");
+    return -1;
+}
+
+int pion_v_b200_beam_forget(const uint32_t* l0_compact) {
+    std::lock_guard<std::mutex> lock(g_beam_mu);
+    std::vector<BeamGraph*> keep;
+    for (BeamGraph* g : g_beam_graphs) {
+        if (!l0_compact || g->l0c == l0_compact)
+            free_beam_graph(g);
+        else
+            keep.push_back(g);
+    }
+    g_beam_graphs.swap(keep);
     return 0;
 }
 

@@ -303,6 +303,12 @@ pion_b200_ctx* default_ctx(const char* who) {
     return tl_ctx.ctx;
 }
 
+}  // namespace
+
+pion_b200_ctx* compat_default_ctx(const char* who) { return default_ctx(who); }
+
+namespace {
+
 int fail(const char* who, const char* what) {
     fprintf(stderr, "pion_vector_b200: %s: %s\n", who, what);
     return -1;

@@ -88,6 +88,14 @@ struct Params {
     unsigned long long* stats;  // level-0 evaluations, expansions, upper evaluations
     unsigned* next_query;
     int* status;
+    // Single-beam mode of pion_v_beam_1536 (nq = 1): the level-0 beam only, from the
+    // caller's pool (entries with their CHECKED bits, size, cursor) and query norm, the
+    // pool written back in place (cursor = size at the end).
+    int from_pool;
+    Entry* pool_io;
+    int pool_size, pool_cursor;
+    float qn_given;
+    int* pool_size_out;
 };
 
 // Per-warp shared memory: the staging rows of `stage` neighbours (copied per round
@@ -252,10 +260,27 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             for (int k = 0; k < 3; ++k) q[k] = qg[lane + 32 * k];
         }
         int32_t qn_int = 0;
+        if (p.from_pool) {  // block norms from the caller's codes
+            int d[3];
 #pragma unroll
-        for (int b = 0; b < NBLK; ++b) qn_int += p.qblk[(size_t)qi * 8 + b];
-        if (lane < 8) qq[lane] = p.qblk[(size_t)qi * 8 + lane];
-        const float qn = (float)qn_int;
+            for (int k2 = 0; k2 < 3; ++k2) d[k2] = dp4a4(q[k2], q[k2], 0);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+                for (int k2 = 0; k2 < 3; ++k2) d[k2] += __shfl_xor_sync(FULL, d[k2], o);
+            if ((lane & 15) == 0)
+#pragma unroll
+                for (int k2 = 0; k2 < 3; ++k2) qq[2 * k2 + (lane >> 4)] = d[k2];
+            if (lane == 0) qq[6] = qq[7] = 0;
+            __syncwarp();
+#pragma unroll
+            for (int b = 0; b < NBLK; ++b) qn_int += qq[b];
+        } else {
+#pragma unroll
+            for (int b = 0; b < NBLK; ++b) qn_int += p.qblk[(size_t)qi * 8 + b];
+            if (lane < 8) qq[lane] = p.qblk[(size_t)qi * 8 + lane];
+        }
+        const float qn = p.from_pool ? p.qn_given : (float)qn_int;
         {
             int4* v4 = reinterpret_cast<int4*>(vis);
             const int64_t n4 = p.vis_words / 4;
@@ -263,21 +288,24 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
         }
         __syncwarp();
 
-        // ---- upper levels: greedy in code space
-        uint32_t curr = (uint32_t)p.entry;
-        int64_t c_off = p.upper_offset[curr];
-        int c_lvl = p.node_level[curr];
+        // ---- upper levels: greedy in code space (skipped when starting from a pool)
+        uint32_t curr = p.from_pool ? 0u : (uint32_t)p.entry;
+        // (a beam started from the caller's pool has no upper levels to read)
+        int64_t c_off = p.from_pool ? -1 : p.upper_offset[curr];
+        int c_lvl = p.from_pool ? 0 : p.node_level[curr];
         float cd;
-        {
+        if (!p.from_pool) {
             int4 v[3];
             stage_vec(stage, p.codes, p.node_slot[curr], lane);
             cp_async_wait_all();
             read_vec(stage, lane, v);
             const VecSums r = reduce_sums(v, q, lane, qq, nullptr);
             cd = (float)(qn_int + r.vv - 2 * r.dot);
+        } else {
+            cd = 0.0f;
         }
         n_upper += 1;
-        for (int l = p.max_level; l >= 1; --l) {
+        for (int l = p.from_pool ? 0 : p.max_level; l >= 1; --l) {
             bool changed = true;
             for (int64_t guard = 0; changed && guard <= p.num_nodes; ++guard) {
                 changed = false;
@@ -344,12 +372,22 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
         }
 
         // ---- level 0: the beam
-        if (lane == 0) {
+        int size = 1, hint = 0;
+        if (p.from_pool) {
+            // the caller's pool; its nodes are the ones it marked visited
+            size = min(p.pool_size, ef);
+            hint = min(p.pool_cursor, size);
+            for (int i = lane; i < size; i += 32) {
+                const Entry e = p.pool_io[i];
+                pool[i] = e;
+                const uint32_t nd = e.id & ~CHECKED;
+                if (nd < nn) atomicOr(&vis[nd >> 5], 1u << (nd & 31));
+            }
+        } else if (lane == 0) {
             atomicOr(&vis[curr >> 5], 1u << (curr & 31));
             pool[0].d = cd;
             pool[0].id = curr;
         }
-        int size = 1, hint = 0;
         // Look-ahead: the row of the entry predicted to be popped next (the second
         // unchecked entry at this pop) and the visited words of its neighbours, read
         // after this step's marks.  Only this warp writes its bitmap, so the words are
@@ -580,6 +618,10 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             }
         }
 
+        if (p.from_pool) {  // the whole pool back to the caller
+            for (int i = lane; i < size; i += 32) p.pool_io[i] = pool[i];
+            if (lane == 0) *p.pool_size_out = size;
+        }
         // drain: the first k entries, nearest first
         for (int i = lane; i < p.k; i += 32) {
             const size_t o = (size_t)qi * p.k + i;
@@ -721,6 +763,12 @@ int launch_hnsw_beam(const HnswLaunch& L, cudaStream_t st) {
     p.stats = L.stats;
     p.next_query = L.next_query;
     p.status = L.status;
+    p.from_pool = L.pool_io != nullptr;
+    p.pool_io = reinterpret_cast<hb::Entry*>(L.pool_io);
+    p.pool_size = L.pool_size;
+    p.pool_cursor = L.pool_cursor;
+    p.qn_given = L.qn_given;
+    p.pool_size_out = L.pool_size_out;
     const size_t smem = (size_t)hb::WARPS * hnsw_warp_smem(L.ef);
     switch (hb::stage_for(L.ef)) {
         case 4: hb::hnsw_beam_kernel<4><<<L.ctas, hb::WARPS * 32, smem, st>>>(p); break;

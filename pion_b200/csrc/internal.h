@@ -163,6 +163,11 @@ struct HnswLaunch {
     unsigned* next_query = nullptr;
     int* status = nullptr;
     int ctas = 0;
+    // single-beam mode (pion_v_beam_1536): start from this pool of (f32 dist, u32 id)
+    void* pool_io = nullptr;
+    int pool_size = 0, pool_cursor = 0;
+    float qn_given = 0.0f;
+    int* pool_size_out = nullptr;
 };
 int hnsw_dim();
 int hnsw_warps_per_cta();
@@ -173,6 +178,9 @@ int launch_hnsw_quantize(const float* q, int nq, float gmin, float scale, int8_t
 int launch_hnsw_beam(const HnswLaunch& launch, cudaStream_t st);
 int launch_hnsw_relayout(const int8_t* src, int64_t n, int64_t stride, int64_t hdr,
                          int8_t* codes, float* norms, cudaStream_t st);
+
+// ---- compat.cu: the per-thread default context of the reference-compatible symbols
+pion_b200_ctx* compat_default_ctx(const char* who);
 
 // ---- shared ABI helpers (abi.cu)
 int set_error(pion_b200_ctx* ctx, int code, const char* fmt, ...);

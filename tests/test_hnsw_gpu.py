@@ -114,3 +114,44 @@ def test_register_rejects_bad_layouts(ctx, small):
         pion_b200.HNSWIndex(ctx, bad)
     with pytest.raises(pion_b200.PionError):
         ix.search(qs, 10, 2000)
+
+
+def test_reference_beam_symbol(oracle, small):
+    """pion_v_beam_1536 (the engine's own symbol, src/vector/vector_abi.mojo:31-36) with a
+    BeamView1536 seeded the way search_fp32_scored seeds it (src/vector/hnsw.mojo:
+    4351-4367: one pool entry for the start node, marked visited at the current epoch):
+    the pool it leaves equals the restated beam_search_1536_ref's entry for entry."""
+    import ctypes
+
+    import pion_b200
+    from pion_b200 import _lib
+    g, A, ix, rows, qs = small
+    lib = pion_b200.load()
+    codes = oracle.hnsw_query_codes(A, qs[:6])
+    comp = A["compact_buffer"]
+    n = A["num_nodes"]
+    rng = np.random.Generator(np.random.PCG64(4))
+    for t in range(6):
+        for ef in (10, 64, 200):
+            start = int(A["entry_point"]) if t % 2 == 0 else int(rng.integers(n))
+            qc = np.ascontiguousarray(codes[t])
+            v = comp[A["node_slot"][start], 8:8 + 1536].astype(np.int32)
+            d0 = np.float32(((v - qc.astype(np.int32)) ** 2).sum())
+            qn = np.float32((qc.astype(np.int32) ** 2).sum())
+            entries = np.zeros(ef, dtype=[("d", "<f4"), ("id", "<u4")])
+            entries[0] = (d0, start)
+            pool = _lib.LinearPool(entries.ctypes.data, ef, 1, 0, ef)
+            visited = np.zeros(n, np.uint16)
+            visited[start] = 7
+            view = _lib.BeamView1536(ctypes.pointer(pool), ef, float(qn), 0.0, qc.ctypes.data,
+                                     A["l0_compact"].ctypes.data, A["l0_slots"].ctypes.data, n,
+                                     None, visited.ctypes.data, 7, comp.ctypes.data,
+                                     A["compact_stride"], A["compact_hdr"], None)
+            assert lib.pion_v_beam_1536(ctypes.byref(view)) == 0
+            od, oi = oracle.hnsw_beam_pool(A, qc, qn, ef, [d0], [start], 0)
+            assert pool.size == len(od) and pool.cursor == pool.size
+            got = entries[:pool.size]
+            assert np.array_equal(got["id"], oi)
+            assert np.array_equal(got["d"].view(np.uint32), od.view(np.uint32))
+    assert lib.pion_v_quant_beam_1536(None) == -1
+    assert lib.pion_v_b200_beam_forget(None) == 0
