@@ -357,6 +357,16 @@ int pion_v_b200_hnsw_search(pion_b200_ctx *ctx, const pion_b200_index *index, co
                             int64_t nq, int64_t k, int64_t ef, int32_t *out_ids, float *out_dist,
                             int mem);
 
+/* metric_scores (src/vector/hnsw.mojo:4523-4651) for INT8 codes: replaces scores[t][j] by
+ * the index metric's distance between query t (normalised once under COSINE, clamped to
+ * the calibration range) and the result ids[t][j] (external ids, as hnsw_search returns
+ * them) dequantised at the middle of each code step: squared L2 under L2, half of it
+ * (= 1 - cos) under COSINE, summed in the reference's order.  Ids that name no node keep
+ * their score.  q fp32[nq x 1536]; ids, scores [nq x k]. */
+int pion_v_b200_hnsw_metric_scores(pion_b200_ctx *ctx, const pion_b200_index *index,
+                                   const float *q, int64_t nq, int64_t k, const int32_t *ids,
+                                   float *scores, int mem);
+
 /* Work counters of the context's last pion_v_b200_hnsw_search (waits for it):
  * out3 = {level-0 distance evaluations, level-0 expansions, upper-level distance
  * evaluations}, summed over the batch. */

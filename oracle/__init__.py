@@ -83,6 +83,7 @@ def lib() -> ctypes.CDLL:
             L.orc_hnsw_query_codes.argtypes = [_p, _p, _i64, _p]
             L.orc_hnsw_beam_pool.argtypes = [_p, _p, _f32, _i64, _p, _p, _i64, _i64, _p, _p]
             L.orc_hnsw_beam_pool.restype = _i64
+            L.orc_hnsw_metric_scores.argtypes = [_p, _p, _i64, _i64, _p, _p]
             _lib = L
     return _lib
 
@@ -374,3 +375,17 @@ def hnsw_beam_pool(graph: dict, q_codes, qn: float, ef: int, init_d, init_id, cu
         raise ValueError("orc_hnsw_beam_pool failed")
     del keep
     return out_d[:n].copy(), out_i[:n].copy()
+
+
+def hnsw_metric_scores(graph: dict, queries, ids, scores):
+    """metric_scores (src/vector/hnsw.mojo:4523-4651) for INT8 codes: returns a copy of
+    `scores` with every id that names a node replaced by its metric distance."""
+    L = lib()
+    lay, keep = _hnsw_layout(graph)
+    q, qp = _c(queries, np.float32)
+    i, ip = _c(ids, np.int32)
+    out = np.array(scores, dtype=np.float32, copy=True, order="C")
+    L.orc_hnsw_metric_scores(ctypes.byref(lay), qp, i.shape[0], i.shape[1], ip,
+                             out.ctypes.data_as(_p))
+    del keep
+    return out

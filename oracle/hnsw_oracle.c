@@ -12,6 +12,7 @@
  *   src/vector/hnsw.mojo:3789-3848     _upper_greedy_codes
  *   src/vector/reference/beam_1536.mojo:30-135   beam_search_1536_ref, _gather
  *   src/common/heap.mojo:133-234       LinearPool
+ *   src/vector/hnsw.mojo:4523-4651     metric_scores (INT8 codes, global calibration)
  */
 #include <math.h>
 #include <stdlib.h>
@@ -406,4 +407,73 @@ int64_t orc_hnsw_beam_pool(const orc_hnsw_layout *L, const int8_t *q, float qn, 
     free(visited);
     free(e);
     return rc == 0 ? pool.size : -1;
+}
+
+/* metric_scores (src/vector/hnsw.mojo:4523-4651), INT8 codes with one global calibration
+ * and no FP32 copy (the Linux build): the query normalised once under COSINE, clamped to
+ * [gmin, gmax]; each code dequantised at the middle of its step, c * g + (127.5 g + gmin)
+ * with g = range / 254 (mul then add: the x86-64-v2 build has no FMA); 4 chains of 8 SIMD
+ * lanes over 32-element strides; (c0 + c1) + (c2 + c3) lane-wise, then the SIMD reduce_add
+ * (halving tree); COSINE halves the squared L2.  ids are external ids; scores in/out. */
+void orc_hnsw_metric_scores(const orc_hnsw_layout *L, const float *queries, int64_t nq,
+                            int64_t k, const int32_t *ids, float *scores) {
+    const int64_t n = L->num_nodes;
+    if (n <= 0) return;
+    int64_t lo = L->node_ids[0], hi = L->node_ids[0];
+    for (int64_t i = 1; i < n; ++i) {
+        if (L->node_ids[i] < lo) lo = L->node_ids[i];
+        if (L->node_ids[i] > hi) hi = L->node_ids[i];
+    }
+    int32_t *map = (int32_t *)malloc((size_t)(hi - lo + 1) * sizeof(int32_t));
+    float *qc = (float *)malloc(HN_DIM * sizeof(float));
+    if (!map || !qc) {
+        free(map);
+        free(qc);
+        return;
+    }
+    for (int64_t i = 0; i < hi - lo + 1; ++i) map[i] = -1;
+    for (int64_t i = 0; i < n; ++i) map[L->node_ids[i] - lo] = (int32_t)i;
+    float range = L->global_max - L->global_min;
+    if (range <= 0.0f) range = 1.0f;
+    const float g = range / 254.0f;
+    const float b = 127.5f * g + L->global_min;
+    for (int64_t t = 0; t < nq; ++t) {
+        const float *x = queries + t * HN_DIM;
+        if (L->metric == 1)
+            orc_l2_normalize_fp32(x, qc, HN_DIM);
+        else
+            memcpy(qc, x, HN_DIM * sizeof(float));
+        for (int d = 0; d < HN_DIM; ++d) {
+            float v = qc[d];
+            if (v < L->global_min) v = L->global_min;
+            if (v > L->global_max) v = L->global_max;
+            qc[d] = v;
+        }
+        for (int64_t r = 0; r < k; ++r) {
+            const int64_t ext = ids[t * k + r];
+            if (ext < lo || ext > hi) continue;
+            const int32_t node = map[ext - lo];
+            if (node < 0) continue;
+            const int8_t *c = slot_vec(L, L->node_slot[node]);
+            float acc[4][8];
+            memset(acc, 0, sizeof(acc));
+            for (int d0 = 0; d0 + 32 <= HN_DIM; d0 += 32)
+                for (int ch = 0; ch < 4; ++ch)
+                    for (int l = 0; l < 8; ++l) {
+                        const int d = d0 + 8 * ch + l;
+                        const float xv = (float)c[d] * g + b;
+                        const float e = qc[d] - xv;
+                        acc[ch][l] = e * e + acc[ch][l];
+                    }
+            float lanes[8];
+            for (int l = 0; l < 8; ++l) lanes[l] = (acc[0][l] + acc[1][l]) + (acc[2][l] + acc[3][l]);
+            for (int w = 8; w > 1; w /= 2)
+                for (int i = 0; i < w / 2; ++i) lanes[i] = lanes[i] + lanes[i + w / 2];
+            float sc = lanes[0];
+            if (L->metric == 1) sc = sc * 0.5f;
+            scores[t * k + r] = sc;
+        }
+    }
+    free(map);
+    free(qc);
 }

@@ -97,6 +97,10 @@ int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, 
 void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
                           int8_t *codes);
 
+/* metric_scores (src/vector/hnsw.mojo:4523-4651) for INT8 codes: scores in/out. */
+void orc_hnsw_metric_scores(const orc_hnsw_layout *L, const float *queries, int64_t nq,
+                            int64_t k, const int32_t *ids, float *scores);
+
 /* beam_search_1536_ref from a caller-seeded pool (pion_v_beam_1536's contract). */
 int64_t orc_hnsw_beam_pool(const orc_hnsw_layout *L, const int8_t *q, float qn, int64_t ef,
                            const float *init_d, const uint32_t *init_id, int64_t n_init,

@@ -75,6 +75,7 @@ SIGNATURES = {
     "pion_v_b200_register_hnsw": (_I, [_P, _P, _PP]),
     "pion_v_b200_hnsw_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_hnsw_last_stats": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_metric_scores": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _I]),
     "pion_v_beam_1536": (_I64, [_P]),
     "pion_v_quant_beam_1536": (_I64, [_P]),
     "pion_v_b200_beam_forget": (_I, [_P]),

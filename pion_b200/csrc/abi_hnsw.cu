@@ -211,6 +211,21 @@ int pion_v_b200_register_hnsw(pion_b200_ctx* ctx, const pion_b200_hnsw_layout* L
             if (!rc) rc = upload(&h.upper_slots, us.data(), words);
         }
         if (!rc && L->deleted) rc = upload(&h.deleted, L->deleted, (n + 7) / 8);
+        if (!rc) {  // external id -> node, for metric_scores (dense id ranges only)
+            int64_t lo = L->node_ids[0], hi = L->node_ids[0];
+            for (size_t i = 1; i < n; ++i) {
+                lo = L->node_ids[i] < lo ? L->node_ids[i] : lo;
+                hi = L->node_ids[i] > hi ? L->node_ids[i] : hi;
+            }
+            const int64_t span = hi - lo + 1;
+            if (span <= 4 * (int64_t)n + 1024) {
+                std::vector<int32_t> inv((size_t)span, -1);
+                for (size_t i = 0; i < n; ++i) inv[(size_t)(L->node_ids[i] - lo)] = (int32_t)i;
+                rc = upload(&h.ext_to_node, inv.data(), (size_t)span);
+                h.ext_base = lo;
+                h.ext_count = span;
+            }
+        }
     }
     if (rc) {
         pion_v_b200_index_free(ix);
@@ -350,6 +365,70 @@ int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         if (cudaMemcpyAsync(out_ids, di, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
             cudaMemcpyAsync(out_dist, dv, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
             return set_error(ctx, PION_B200_ECUDA, "hnsw_search: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+int pion_v_b200_hnsw_metric_scores(pion_b200_ctx* ctx, const pion_b200_index* ix, const float* q,
+                                   int64_t nq, int64_t k, const int32_t* ids, float* scores,
+                                   int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kHNSW)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: not an HNSW index");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: index on another device");
+    if (nq < 0 || k < 1 || (nq > 0 && (!q || !ids || !scores)))
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: bad arguments");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: bad mem %d", mem);
+    if (nq == 0 || ix->n_rows == 0) return 0;
+    const auto& h = ix->hnsw;
+    if (!h.ext_to_node)
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_metric_scores: external ids too sparse");
+    if (nq > (1 << 24) || k > (1 << 16))
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_metric_scores: batch or k too large");
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const int dim = hnsw_dim();
+    const size_t qb = (size_t)nq * dim * 4, rb = (size_t)nq * k * 4;
+    const float* dq = q;
+    const int32_t* di = ids;
+    float* ds = scores;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, align_up(qb, 256) + align_up(rb, 256)) != 0 ||
+            ensure(ctx->stage_out, rb) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_metric_scores: staging");
+        char* in = static_cast<char*>(ctx->stage_in.ptr);
+        if (cudaMemcpyAsync(in, q, qb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(in + align_up(qb, 256), ids, rb, cudaMemcpyHostToDevice, st) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(ctx->stage_out.ptr, scores, rb, cudaMemcpyHostToDevice, st) !=
+                cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_metric_scores: copy failed");
+        dq = reinterpret_cast<const float*>(in);
+        di = reinterpret_cast<const int32_t*>(in + align_up(qb, 256));
+        ds = static_cast<float*>(ctx->stage_out.ptr);
+    }
+    const float* qsrc = dq;
+    int rc = 0;
+    if (h.metric == 1) {  // metric_scores normalises the query once (hnsw.mojo:4542-4544)
+        if (ensure(ctx->scratch, qb) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_metric_scores: scratch");
+        float* qn = static_cast<float*>(ctx->scratch.ptr);
+        rc = launch_l2_normalize_rows(dq, nq, dim, qn, nullptr, st);
+        ctx->launches++;
+        qsrc = qn;
+    }
+    if (!rc)
+        rc = launch_hnsw_metric(qsrc, (int)nq, (int)k, di, h.ext_to_node, h.ext_base,
+                                h.ext_count, h.node_slot, h.codes, h.gmin, h.gmax,
+                                h.metric == 1, ds, st);
+    ctx->launches++;
+    if (rc) return set_error(ctx, rc, "hnsw_metric_scores: launch failed");
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(scores, ds, rb, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_metric_scores: result copy failed");
         return finish_sync(ctx);
     }
     return 0;

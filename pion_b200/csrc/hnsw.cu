@@ -643,6 +643,50 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
     }
 }
 
+// metric_scores (src/vector/hnsw.mojo:4523-4651) with INT8 codes: the reply score of a
+// result node is the squared L2 between the query (normalised once under COSINE, then
+// clamped to the calibration range) and the codes dequantised at the middle of their step,
+// x = c * (range / 254) + (127.5 * range / 254 + gmin), summed as the reference does: 32
+// chains (4 x 8 SIMD lanes; lane L takes elements 32 i + L in order, mul then add), lanes
+// combined (c0 + c1) + (c2 + c3), then the 8-lane SIMD reduction tree; COSINE halves it.
+// One warp per (query, result); ids without a node keep their score.
+__global__ void hnsw_metric_kernel(const float* __restrict__ qn, int nq, int k,
+                                   const int32_t* __restrict__ ids,
+                                   const int32_t* __restrict__ ext_to_node, int64_t ext_base,
+                                   int64_t ext_count, const uint32_t* __restrict__ node_slot,
+                                   const int8_t* __restrict__ codes, float gmin, float gmax,
+                                   int cosine, float* __restrict__ scores) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (int64_t)nq * k) return;  // warp-uniform
+    const int64_t ext = ids[w];
+    if (ext < ext_base || ext - ext_base >= ext_count) return;
+    const int32_t node = ext_to_node[ext - ext_base];
+    if (node < 0) return;
+    float range = __fsub_rn(gmax, gmin);
+    if (range <= 0.0f) range = 1.0f;
+    const float a = __fdiv_rn(range, 254.0f);
+    const float b = __fadd_rn(__fmul_rn(127.5f, a), gmin);
+    const float* q = qn + (w / k) * DIM;
+    const int8_t* c = codes + (size_t)node_slot[node] * DIM;
+    float acc = 0.0f;
+#pragma unroll 4
+    for (int i = 0; i < DIM / 32; ++i) {
+        const int d = 32 * i + lane;
+        const float qv = fminf(fmaxf(q[d], gmin), gmax);
+        const float x = __fadd_rn(__fmul_rn((float)c[d], a), b);
+        const float t = __fsub_rn(qv, x);
+        acc = __fadd_rn(__fmul_rn(t, t), acc);
+    }
+    const int l = lane & 7;
+    const float c0 = __shfl_sync(FULL, acc, l), c1 = __shfl_sync(FULL, acc, 8 + l);
+    const float c2 = __shfl_sync(FULL, acc, 16 + l), c3 = __shfl_sync(FULL, acc, 24 + l);
+    float v = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));  // lane l of the SIMD8 sum
+#pragma unroll
+    for (int h = 4; h > 0; h >>= 1) v = __fadd_rn(v, __shfl_sync(FULL, v, (l + h) & 7));
+    if (lane == 0) scores[w] = cosine ? __fmul_rn(v, 0.5f) : v;
+}
+
 // Device copy of a slot buffer: codes at 16-byte aligned rows of 1536 bytes and the
 // header's norm^2 in its own array.
 __global__ void hnsw_relayout_kernel(const int8_t* __restrict__ src, int64_t n, int64_t stride,
@@ -724,6 +768,18 @@ int hnsw_ctas_per_sm(int ef) {
         case 2: return beam_ctas_per_sm<2>(smem);
         default: return beam_ctas_per_sm<1>(smem);
     }
+}
+
+int launch_hnsw_metric(const float* qn, int nq, int k, const int32_t* ids,
+                       const int32_t* ext_to_node, int64_t ext_base, int64_t ext_count,
+                       const uint32_t* node_slot, const int8_t* codes, float gmin, float gmax,
+                       int cosine, float* scores, cudaStream_t st) {
+    const int64_t warps = (int64_t)nq * k;
+    if (warps <= 0) return 0;
+    hb::hnsw_metric_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+        qn, nq, k, ids, ext_to_node, ext_base, ext_count, node_slot, codes, gmin, gmax, cosine,
+        scores);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
 int launch_hnsw_relayout(const int8_t* src, int64_t n, int64_t stride, int64_t hdr,

@@ -125,6 +125,8 @@ struct pion_b200_index {
         int64_t* upper_offset = nullptr;
         uint32_t* upper_links = nullptr;
         uint32_t* upper_slots = nullptr;
+        int32_t* ext_to_node = nullptr;  // external id - ext_base -> node (-1: none)
+        int64_t ext_base = 0, ext_count = 0;
         int M = 0;
         int max_level = 0;
         int64_t entry = -1;
@@ -178,6 +180,10 @@ int launch_hnsw_quantize(const float* q, int nq, float gmin, float scale, int8_t
 int launch_hnsw_beam(const HnswLaunch& launch, cudaStream_t st);
 int launch_hnsw_relayout(const int8_t* src, int64_t n, int64_t stride, int64_t hdr,
                          int8_t* codes, float* norms, cudaStream_t st);
+int launch_hnsw_metric(const float* qn, int nq, int k, const int32_t* ids,
+                       const int32_t* ext_to_node, int64_t ext_base, int64_t ext_count,
+                       const uint32_t* node_slot, const int8_t* codes, float gmin, float gmax,
+                       int cosine, float* scores, cudaStream_t st);
 
 // ---- compat.cu: the per-thread default context of the reference-compatible symbols
 pion_b200_ctx* compat_default_ctx(const char* who);

@@ -451,6 +451,27 @@ class HNSWIndex(_Index):
             c.check(c.lib.pion_v_b200_hnsw_search(c.h, self.h, pq, nq, k, ef, pi, pv, mem))
         return ids, dist
 
+    def metric_scores(self, q, ids, scores, ctx: Context | None = None):
+        """metric_scores (src/vector/hnsw.mojo:4523-4651): the reply scores of `ids`
+        (external ids, as search returns them) in the index metric (squared L2, or
+        1 - cos under COSINE) from the INT8 codes; `scores` is updated in place and
+        returned (entries whose id names no node keep their value)."""
+        c = ctx or self.ctx
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        pi, mi, ki = _ptr(ids, np.int32, "ids")
+        if _is_torch(scores):
+            ps, ms = scores.data_ptr(), MEM_DEVICE if scores.is_cuda else MEM_HOST
+        else:
+            if not (isinstance(scores, np.ndarray) and scores.dtype == np.float32 and
+                    scores.flags["C_CONTIGUOUS"]):
+                raise TypeError("scores must be a contiguous float32 array (updated in place)")
+            ps, ms = scores.ctypes.data, MEM_HOST
+        m = _same_mem(mem, mi, ms)
+        nq, k = ids.shape
+        with _TorchStream(c, m):
+            c.check(c.lib.pion_v_b200_hnsw_metric_scores(c.h, self.h, pq, nq, k, pi, ps, m))
+        return scores
+
     def last_stats(self, ctx: Context | None = None) -> dict:
         """Work of the context's last search: level-0 evaluations, expansions, upper-level
         evaluations."""

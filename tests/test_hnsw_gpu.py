@@ -155,3 +155,29 @@ def test_reference_beam_symbol(oracle, small):
             assert np.array_equal(got["d"].view(np.uint32), od.view(np.uint32))
     assert lib.pion_v_quant_beam_1536(None) == -1
     assert lib.pion_v_b200_beam_forget(None) == 0
+
+
+def test_metric_scores(oracle, small, ctx):
+    """metric_scores on the GPU == the restatement, bit for bit (COSINE: 1 - cos from the
+    dequantised codes), and close to the exact fp32 cosine distance of the rows."""
+    import pion_b200
+    g, A, ix, rows, qs = small
+    ids, dist = ix.search(qs, 10, 64)
+    ids[3, 4] = -1                      # no node: keeps its score
+    ids[5, 0] = A["num_nodes"] + 10
+    got = ix.metric_scores(qs, ids, dist.copy())
+    want = oracle.hnsw_metric_scores(A, qs, ids, dist)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert got[3, 4] == dist[3, 4] and got[5, 0] == dist[5, 0]
+    rn = rows / np.linalg.norm(rows, axis=1, keepdims=True)
+    qn = qs / np.linalg.norm(qs, axis=1, keepdims=True)
+    ok = (ids >= 0) & (ids < A["num_nodes"])
+    exact = 1.0 - np.einsum("qd,qkd->qk", qn, rn[np.where(ok, ids, 0)])
+    assert np.abs(got - exact)[ok].max() < 0.02
+    # L2 graph: squared L2 units, no halving
+    g2, rows2, qs2 = _graph(3000, 16, seed=9, metric="l2", nq=16)
+    ix2 = pion_b200.HNSWIndex(ctx, g2)
+    i2, d2 = ix2.search(qs2 * 2.0, 10, 32)
+    got2 = ix2.metric_scores(qs2 * 2.0, i2, d2.copy())
+    want2 = oracle.hnsw_metric_scores(g2.arrays(), qs2 * 2.0, i2, d2)
+    assert np.array_equal(got2.view(np.uint32), want2.view(np.uint32))
