@@ -63,6 +63,11 @@ WORKLOADS = {
     "hnsw": dict(kind="hnsw", rows=1_000_000, dim=1536, centres=1024, seed=3, batch=4096, k=10,
                  M=16, ef_construction=200,
                  desc="HNSW INT8, 1M x 1536, M=16, efConstruction=200, 4096-query batches"),
+    "hnsw_brute": dict(kind="slot", rows=1_000_000, dim=1536, centres=1024, seed=3, batch=1024,
+                       k=10, M=16, ef_construction=200,
+                       desc="GPU brute-force scan of the HNSW slot buffer (INT8 L2 of every "
+                            "slot, worst-replace top-20, FP32 rerank to 10), 1M x 1536, "
+                            "1024-query batches"),
 }
 
 
@@ -181,6 +186,10 @@ def config_of(wl, batch, world, a=None):
     if wl["kind"] == "hnsw":
         c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
                   "ef": a.ef if a is not None else None,
+                  "parallelism": f"graph replicas x{world}, one batch per replica"})
+    if wl["kind"] == "slot":
+        c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
+                  "oversample": 2 * wl["k"], "rerank": "fp32 rows by slot",
                   "parallelism": f"graph replicas x{world}, one batch per replica"})
     return c
 
@@ -527,7 +536,103 @@ class HNSWWorkload:
         oracle.hnsw_search(arrays, q[lo:hi], k, ef, nthreads=threads)
 
 
-ADAPTERS = {"i8": I8Workload, "f32": F32Workload, "bq": BQWorkload, "hnsw": HNSWWorkload}
+class SlotWorkload(HNSWWorkload):
+    """search_gpu_brute_force over the HNSW slot buffer: every slot's INT8 L2 on the
+    tensor cores, the worst-replace top-(2k) loop, FP32 rerank rows by slot, top k.
+    The graph comes from the same host build as the hnsw workload (it fixes the slot
+    order); replicas across GPUs, weak scaling."""
+
+    dtype = "int8 codes (exact int32 dot products), fp32 rerank"
+
+    def __init__(self, wl, batch, dev, ctx, lo, hi, ef=128):
+        import numpy as np
+        import torch
+
+        from pion_b200.workloads import mixture_torch
+        super().__init__(wl, batch, dev, ctx, lo, hi, ef)
+        n, dim = wl["rows"], wl["dim"]
+        slot = torch.from_numpy(np.ascontiguousarray(self.arrays["node_slot"]
+                                                     if self.graph is None
+                                                     else self.graph.arrays()["node_slot"])
+                                .astype(np.int64)).to(dev)
+        rr = torch.empty((n, dim), dtype=torch.float32, device=dev)
+        for s in range(0, n, 1 << 18):
+            e = min(n, s + (1 << 18))
+            part, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev,
+                                    row_range=(s, e))
+            rr[slot[s:e]] = part
+            del part
+        self.ix.set_rerank_rows(rr)
+        del rr
+        torch.cuda.synchronize()
+
+    def search(self, inp, ctx=None):
+        return self.ix.brute_force(inp[0], self.k, ctx=ctx)
+
+    def host_call(self, hin, out_i, out_v, ctx=None):
+        import torch
+
+        import pion_b200
+        c = ctx or self.ctx
+        found = getattr(self, "_found", None)
+        if found is None or found.numel() != self.batch:
+            found = self._found = torch.empty(self.batch, dtype=torch.int32).pin_memory()
+        c.check(c.lib.pion_v_b200_hnsw_brute_force(c.h, self.ix.h, hin[0].data_ptr(), self.batch,
+                                                   self.k, out_i.data_ptr(), out_v.data_ptr(),
+                                                   found.data_ptr(), pion_b200._lib.MEM_HOST))
+
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+        st = self.ix.slot_stats()
+        ops = 2.0 * self.dim * self.wl["rows"] * self.batch
+        achieved = ops / (kern_ms / 1000.0) / 1e12
+        peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate); timed: the "
+                               f"staged tensor-core scan and the top-k replay",
+                "algorithmic_per_launch": ops, "kernel_ms": kern_ms,
+                "replayed_per_query": st["replayed"] / max(1, self.batch),
+                "exact_scan_queries": st["exact_queries"]}
+
+    def extra(self, dev):
+        """recall@10 against exact FLAT FP32 cosine (rank 0)."""
+        import numpy as np
+        import torch
+
+        import pion_b200
+        if self.graph is None:
+            return {}
+        rows = self.rows_host.to(dev)
+        flat = pion_b200.FlatF32Index(self.ctx, rows)
+        truth, _ = flat.search(self.q, self.k)
+        ids, _, _ = self.ix.brute_force(self.q, self.k)
+        t, r = truth.cpu().numpy(), ids.cpu().numpy()
+        recall = float(np.mean([len(set(r[i]) & set(t[i])) / self.k for i in range(len(t))]))
+        flat.free()
+        del rows
+        torch.cuda.empty_cache()
+        return {"recall_at_10": recall, "build_s": self.build_s}
+
+    def host_data(self):
+        import numpy as np
+        A = self.graph.arrays()
+        rr = np.empty_like(self.rows_host.numpy())
+        rr[A["node_slot"]] = self.rows_host.numpy()
+        return (A, self.q.cpu().numpy(), rr)
+
+    @staticmethod
+    def cpu_run(data, lo, hi, k, threads):
+        from concurrent.futures import ThreadPoolExecutor
+
+        import oracle
+        A, q, rr = data
+        chunks = [(s, min(hi, s + 1)) for s in range(lo, hi)]
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(lambda c: oracle.hnsw_brute_force(A, q[c[0]:c[1]], k, rr), chunks))
+
+
+ADAPTERS = {"i8": I8Workload, "f32": F32Workload, "bq": BQWorkload, "hnsw": HNSWWorkload,
+            "slot": SlotWorkload}
 
 
 # --------------------------------------------------------------- reference arm --
@@ -542,11 +647,16 @@ def reference_data(wl, batch, dev):
 
     n, dim = wl["rows"], wl["dim"]
     _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev, row_range=(0, 0))
-    if wl["kind"] == "hnsw":  # the host build (a restatement of the reference's builder)
+    if wl["kind"] in ("hnsw", "slot"):  # the host build (a restatement of the reference's)
         import pion_b200
         rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
-        g = pion_b200.HNSWGraph(rows.cpu().numpy(), M=wl["M"],
-                                ef_construction=wl["ef_construction"])
+        rows = rows.cpu().numpy()
+        g = pion_b200.HNSWGraph(rows, M=wl["M"], ef_construction=wl["ef_construction"])
+        if wl["kind"] == "slot":
+            A = g.arrays()
+            rr = np.empty_like(rows)
+            rr[A["node_slot"]] = rows
+            return (A, qf.cpu().numpy(), rr), g
         return (g.arrays(), qf.cpu().numpy(), wl["ef"]), g
     if wl["kind"] in ("f32", "bq"):
         rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
@@ -590,7 +700,7 @@ def run_reference(a, wl):
     dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
     data = reference_data(wl, batch, dev)
     keep = None
-    if wl["kind"] == "hnsw":
+    if wl["kind"] in ("hnsw", "slot"):
         data, keep = data
     run = ADAPTERS[wl["kind"]].cpu_run
     threads = os.cpu_count() or 1
@@ -656,8 +766,8 @@ def run_ours(a, wl):
     n = wl["rows"]
     lo, hi = shard_bounds(n, world, rank)
     ctx = pion_b200.Context(local)
-    if wl["kind"] == "hnsw":
-        W = HNSWWorkload(wl, batch, dev, ctx, lo, hi, ef=a.ef)
+    if wl["kind"] in ("hnsw", "slot"):
+        W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi, ef=a.ef)
     else:
         W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi)
     local_batch = W.batch
@@ -670,8 +780,8 @@ def run_ours(a, wl):
 
     step = W.search if getattr(W, "replicas", False) else ShardedSearch(W.search, k, merge)
     workers = a.workers or (3 if wl["kind"] == "hnsw" else 1)
-    if workers > 1 and wl["kind"] != "hnsw":
-        raise SystemExit("--workers > 1 is for the hnsw workload")
+    if workers > 1 and wl["kind"] not in ("hnsw", "slot"):
+        raise SystemExit("--workers > 1 is for the hnsw workloads")
     ctxs = [ctx] + [pion_b200.Context(local) for _ in range(workers - 1)]
     streams = [stream] + [torch.cuda.Stream(device=dev) for _ in range(workers - 1)]
 

@@ -367,6 +367,43 @@ int pion_v_b200_hnsw_metric_scores(pion_b200_ctx *ctx, const pion_b200_index *in
                                    const float *q, int64_t nq, int64_t k, const int32_t *ids,
                                    float *scores, int mem);
 
+/* The GPU brute-force scan of a registered graph's slot buffer, batched.  Replaces
+ * pion_metal_search_topk_w (src/ffi/metal_wrap.m:495-580) with the shader
+ * int8_l2_distance_batch (src/ffi/metal_compute.metal:19-78): for each query, every slot s
+ * in [0, min(num_vectors, slots)) gets d = (q_norm + slot |code|^2) - 2 * float(dot) and
+ * goes through the wrapper's worst-replace loop over min(k, num_vectors) entries.
+ * out_slots / out_dists [nq x k] hold the entries in the order the loop leaves them
+ * (unsorted, as the engine receives them); entries past min(k, num_vectors) are -1 / +inf.
+ * q_codes int8 [nq x 1536]; q_norm [nq] or NULL (then |code|^2 of the codes, as
+ * norm_sq_int8_jit computes it).  k in [1, 256]. */
+int pion_v_b200_slot_scan_topk(pion_b200_ctx *ctx, const pion_b200_index *index,
+                               const int8_t *q_codes, const float *q_norm, int64_t nq,
+                               int64_t num_vectors, int64_t k, int32_t *out_slots,
+                               float *out_dists, int mem);
+
+/* Work of the context's last slot scan or brute-force call (waits for it): out2 =
+ * {queries that went through the exact CUDA-core scan, candidate slots replayed through
+ * the loop}. */
+int pion_v_b200_slot_last_stats(pion_b200_ctx *ctx, int64_t *out2);
+
+/* pion_metal_register_rerank_buffer / _unregister_ (src/ffi/metal_wrap.m:674-720): FP32
+ * rows [n x dim] by slot (the compact_vectors rerank buffer, hnsw.mojo:2832-2880) for
+ * pion_v_b200_hnsw_brute_force; n = the graph's slots, dim = 1536; rows NULL drops them.
+ * The rows are copied to the device. */
+int pion_v_b200_hnsw_set_rerank_rows(pion_b200_ctx *ctx, pion_b200_index *index,
+                                     const float *rows, int64_t n, int64_t dim, int mem);
+
+/* search_gpu_brute_force (src/vector/hnsw.mojo:3916-3992) for a batch: the query
+ * normalised once (COSINE) and quantised; the slot scan above with min(2 k', n, 256)
+ * entries when rerank rows are set (k' = min(k, n)), else min(k', 256); with rerank rows
+ * every entry's distance becomes the FP32 squared L2 of the raw query and the slot's row
+ * (the engine's CPU rerank loop: 8 lanes, mul then add, halving reduce); a stable sort by
+ * distance; the first k' as external ids.  out_ids / out_scores [nq x k] (-1 / +inf past
+ * out_found[t]); out_found [nq]. */
+int pion_v_b200_hnsw_brute_force(pion_b200_ctx *ctx, const pion_b200_index *index,
+                                 const float *q, int64_t nq, int64_t k, int32_t *out_ids,
+                                 float *out_scores, int32_t *out_found, int mem);
+
 /* Work counters of the context's last pion_v_b200_hnsw_search (waits for it):
  * out3 = {level-0 distance evaluations, level-0 expansions, upper-level distance
  * evaluations}, summed over the batch. */

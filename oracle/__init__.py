@@ -84,6 +84,9 @@ def lib() -> ctypes.CDLL:
             L.orc_hnsw_beam_pool.argtypes = [_p, _p, _f32, _i64, _p, _p, _i64, _i64, _p, _p]
             L.orc_hnsw_beam_pool.restype = _i64
             L.orc_hnsw_metric_scores.argtypes = [_p, _p, _i64, _i64, _p, _p]
+            L.orc_slot_scan_topk.argtypes = [_p, _p, ctypes.c_float, _i64, _i64, _p, _p]
+            L.orc_slot_scan_topk.restype = _i64
+            L.orc_hnsw_brute_force.argtypes = [_p, _p, _p, _i64, _i64, _p, _p, _p]
             _lib = L
     return _lib
 
@@ -389,3 +392,41 @@ def hnsw_metric_scores(graph: dict, queries, ids, scores):
                              out.ctypes.data_as(_p))
     del keep
     return out
+
+
+def slot_scan_topk(graph: dict, qcodes, qnorm, num_vectors: int, k: int):
+    """The GPU brute-force slot scan (src/ffi/metal_compute.metal:19-78) and its
+    worst-replace top-k (src/ffi/metal_wrap.m:495-580) per query: (slots [nq, k],
+    dists [nq, k]) in the order the loop leaves them; -1 / +inf past min(k, n)."""
+    L = lib()
+    lay, keep = _hnsw_layout(graph)
+    q = np.ascontiguousarray(qcodes, dtype=np.int8)
+    nq = q.shape[0]
+    qn = np.ascontiguousarray(qnorm, dtype=np.float32)
+    slots = np.full((nq, k), -1, np.int32)
+    dists = np.full((nq, k), np.inf, np.float32)
+    for t in range(nq):
+        L.orc_slot_scan_topk(ctypes.byref(lay), q[t].ctypes.data_as(_p), float(qn[t]),
+                             num_vectors, k, slots[t].ctypes.data_as(_p),
+                             dists[t].ctypes.data_as(_p))
+    del keep
+    return slots, dists
+
+
+def hnsw_brute_force(graph: dict, queries, k: int, rerank=None):
+    """search_gpu_brute_force (src/vector/hnsw.mojo:3916-3992): (ids, scores, found)."""
+    L = lib()
+    lay, keep = _hnsw_layout(graph)
+    q, qp = _c(queries, np.float32)
+    nq = q.shape[0]
+    rp = None
+    if rerank is not None:
+        r, rp = _c(rerank, np.float32)
+        keep.append(r)
+    ids = np.empty((nq, k), np.int32)
+    sc = np.empty((nq, k), np.float32)
+    found = np.empty(nq, np.int32)
+    L.orc_hnsw_brute_force(ctypes.byref(lay), rp, qp, nq, k, ids.ctypes.data_as(_p),
+                           sc.ctypes.data_as(_p), found.ctypes.data_as(_p))
+    del keep
+    return ids, sc, found

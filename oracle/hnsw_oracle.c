@@ -13,6 +13,9 @@
  *   src/vector/reference/beam_1536.mojo:30-135   beam_search_1536_ref, _gather
  *   src/common/heap.mojo:133-234       LinearPool
  *   src/vector/hnsw.mojo:4523-4651     metric_scores (INT8 codes, global calibration)
+ *   src/ffi/metal_compute.metal:19-143 INT8 L2 of every slot (the GPU brute-force scan)
+ *   src/ffi/metal_wrap.m:495-580       its worst-replace top-k
+ *   src/vector/hnsw.mojo:3916-3992     search_gpu_brute_force (oversample, FP32 rerank)
  */
 #include <math.h>
 #include <stdlib.h>
@@ -105,13 +108,15 @@ static float slot_norm(const int8_t *v) {
     return f;
 }
 
-/* Normalise (COSINE, twice: search_fp32_scored, then _quantize_query_to_int8 again
- * in place) and quantise: clamp(roundeven((x - gmin) * scale), 0, 254) - 127. */
-static void query_codes(const orc_hnsw_layout *L, const float *x, float *tmp, int8_t *q) {
+/* Normalise (COSINE: `passes` times; search_fp32_scored normalises, then
+ * _quantize_query_to_int8 again, the brute-force scan only once) and quantise:
+ * clamp(roundeven((x - gmin) * scale), 0, 254) - 127. */
+static void query_codes_n(const orc_hnsw_layout *L, const float *x, float *tmp, int8_t *q,
+                          int passes) {
     const float *src = x;
     if (L->metric == 1) {
         orc_l2_normalize_fp32(x, tmp, HN_DIM);
-        orc_l2_normalize_fp32(tmp, tmp, HN_DIM);
+        for (int i = 1; i < passes; ++i) orc_l2_normalize_fp32(tmp, tmp, HN_DIM);
         src = tmp;
     }
     float range = L->global_max - L->global_min;
@@ -124,6 +129,10 @@ static void query_codes(const orc_hnsw_layout *L, const float *x, float *tmp, in
         if (r > 254) r = 254;
         q[i] = (int8_t)(r - 127);
     }
+}
+
+static void query_codes(const orc_hnsw_layout *L, const float *x, float *tmp, int8_t *q) {
+    query_codes_n(L, x, tmp, q, 2);
 }
 
 void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
@@ -476,4 +485,131 @@ void orc_hnsw_metric_scores(const orc_hnsw_layout *L, const float *queries, int6
     }
     free(map);
     free(qc);
+}
+
+/* The GPU brute-force scan of the slot buffer for one query.
+ * int8_l2_distance_batch (src/ffi/metal_compute.metal:19-78):
+ *   d = query_norm + cand_norm - 2 * float(dot), cand_norm = the slot header's |code|^2.
+ * pion_metal_search_topk_w (src/ffi/metal_wrap.m:495-580): num_vectors is clamped to the
+ * registered slots and k to num_vectors; k entries start as (+inf, -1), worst = +inf at
+ * entry 0; for every slot in order, d < worst overwrites entry worst_idx, then worst and
+ * worst_idx become the first maximum of the k entries.  The entries stay in that order
+ * (the caller sorts).  Returns k. */
+int64_t orc_slot_scan_topk(const orc_hnsw_layout *L, const int8_t *q, float qn,
+                           int64_t num_vectors, int64_t k, int32_t *out_slots, float *out_d) {
+    if (num_vectors > L->num_nodes) num_vectors = L->num_nodes;
+    if (num_vectors < 0) num_vectors = 0;
+    if (k > num_vectors) k = num_vectors;
+    if (k < 0) k = 0;
+    for (int64_t i = 0; i < k; ++i) {
+        out_d[i] = INFINITY;
+        out_slots[i] = -1;
+    }
+    float worst = INFINITY;
+    int64_t widx = 0;
+    for (int64_t s = 0; s < num_vectors; ++s) {
+        const int8_t *v = slot_vec(L, (uint32_t)s);
+        int32_t dot = 0;
+        for (int d = 0; d < HN_DIM; ++d) dot += (int32_t)q[d] * (int32_t)v[d];
+        const float sum = qn + slot_norm(v);
+        const float dist = sum - 2.0f * (float)dot;
+        if (dist < worst) {
+            out_d[widx] = dist;
+            out_slots[widx] = (int32_t)s;
+            worst = -INFINITY;
+            for (int64_t j = 0; j < k; ++j)
+                if (out_d[j] > worst) {
+                    worst = out_d[j];
+                    widx = j;
+                }
+        }
+    }
+    return k;
+}
+
+/* Exact FP32 L2^2 of the CPU rerank loop of search_gpu_brute_force (src/vector/hnsw.mojo:
+ * 3954-3965): 8 SIMD lanes, lane l over elements 8i + l, acc = acc + diff * diff, then
+ * the SIMD reduce_add (halving tree). */
+static float rerank_l2(const float *q, const float *v) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < HN_DIM / 8; ++i)
+        for (int l = 0; l < 8; ++l) {
+            const float diff = q[8 * i + l] - v[8 * i + l];
+            acc[l] = acc[l] + diff * diff;
+        }
+    for (int w = 8; w > 1; w /= 2)
+        for (int i = 0; i < w / 2; ++i) acc[i] = acc[i] + acc[i + w / 2];
+    return acc[0];
+}
+
+/* search_gpu_brute_force (src/vector/hnsw.mojo:3916-3992) per query: codes of the query
+ * normalised once (_quantize_query_to_int8), query_norm = the integer |code|^2 as f32
+ * (norm_sq_int8_jit, src/vector/kernels.mojo:362-376); oversample = min(2 k', n, 256)
+ * with rerank rows (k' = min(k, n)), else min(k', 256); the scan above; with rerank rows
+ * every entry's distance becomes the FP32 L2^2 of the raw query and its slot's row; a
+ * stable insertion sort by distance; the first k' entries as (slot's external id,
+ * distance).  out_ids/out_scores [nq x k] (-1 / +inf past out_found[t]). */
+void orc_hnsw_brute_force(const orc_hnsw_layout *L, const float *rerank, const float *queries,
+                          int64_t nq, int64_t k, int32_t *out_ids, float *out_scores,
+                          int32_t *out_found) {
+    const int64_t n = L->num_nodes;
+    for (int64_t i = 0; i < nq * k; ++i) {
+        out_ids[i] = -1;
+        out_scores[i] = INFINITY;
+    }
+    for (int64_t t = 0; t < nq; ++t) out_found[t] = 0;
+    if (n <= 0 || k <= 0) return;
+    int32_t *slot_ext = (int32_t *)malloc((size_t)n * sizeof(int32_t));
+    int32_t *ids = (int32_t *)malloc(256 * sizeof(int32_t));
+    float *dist = (float *)malloc(256 * sizeof(float));
+    float *tmp = (float *)malloc(HN_DIM * sizeof(float));
+    int8_t *codes = (int8_t *)malloc(HN_DIM);
+    if (!slot_ext || !ids || !dist || !tmp || !codes) goto done;
+    for (int64_t i = 0; i < n; ++i) slot_ext[i] = -1;
+    for (int64_t i = 0; i < n; ++i)
+        if (L->node_slot[i] < (uint32_t)n) slot_ext[L->node_slot[i]] = L->node_ids[i];
+    const int64_t final_k = k < n ? k : n;
+    int64_t over;
+    if (rerank) {
+        over = 2 * final_k;
+        if (over > n) over = n;
+        if (over > 256) over = 256;
+    } else {
+        over = final_k < 256 ? final_k : 256;
+    }
+    for (int64_t t = 0; t < nq; ++t) {
+        const float *x = queries + t * HN_DIM;
+        query_codes_n(L, x, tmp, codes, 1);
+        int32_t qn_i = 0;
+        for (int d = 0; d < HN_DIM; ++d) qn_i += (int32_t)codes[d] * (int32_t)codes[d];
+        int64_t found = orc_slot_scan_topk(L, codes, (float)qn_i, n, over, ids, dist);
+        if (rerank)
+            for (int64_t i = 0; i < found; ++i)
+                if (ids[i] >= 0 && ids[i] < n)
+                    dist[i] = rerank_l2(x, rerank + (int64_t)ids[i] * HN_DIM);
+        for (int64_t i = 1; i < found; ++i)
+            for (int64_t j = i; j > 0 && dist[j] < dist[j - 1]; --j) {
+                const float td = dist[j];
+                dist[j] = dist[j - 1];
+                dist[j - 1] = td;
+                const int32_t ti = ids[j];
+                ids[j] = ids[j - 1];
+                ids[j - 1] = ti;
+            }
+        if (found > final_k) found = final_k;
+        int32_t c = 0;
+        for (int64_t i = 0; i < found; ++i)
+            if (ids[i] >= 0 && ids[i] < n) {
+                out_ids[t * k + c] = slot_ext[ids[i]];
+                out_scores[t * k + c] = dist[i];
+                ++c;
+            }
+        out_found[t] = c;
+    }
+done:
+    free(slot_ext);
+    free(ids);
+    free(dist);
+    free(tmp);
+    free(codes);
 }

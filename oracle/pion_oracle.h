@@ -101,6 +101,17 @@ void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_
 void orc_hnsw_metric_scores(const orc_hnsw_layout *L, const float *queries, int64_t nq,
                             int64_t k, const int32_t *ids, float *scores);
 
+/* The GPU brute-force slot scan for one query (src/ffi/metal_compute.metal:19-78 and
+ * pion_metal_search_topk_w, src/ffi/metal_wrap.m:495-580): entries in the order the
+ * worst-replace loop leaves them.  Returns min(k, num_vectors). */
+int64_t orc_slot_scan_topk(const orc_hnsw_layout *L, const int8_t *q, float qn,
+                           int64_t num_vectors, int64_t k, int32_t *out_slots, float *out_d);
+/* search_gpu_brute_force (src/vector/hnsw.mojo:3916-3992); rerank: FP32 rows by slot or
+ * NULL. */
+void orc_hnsw_brute_force(const orc_hnsw_layout *L, const float *rerank, const float *queries,
+                          int64_t nq, int64_t k, int32_t *out_ids, float *out_scores,
+                          int32_t *out_found);
+
 /* beam_search_1536_ref from a caller-seeded pool (pion_v_beam_1536's contract). */
 int64_t orc_hnsw_beam_pool(const orc_hnsw_layout *L, const int8_t *q, float qn, int64_t ef,
                            const float *init_d, const uint32_t *init_id, int64_t n_init,

@@ -76,6 +76,10 @@ SIGNATURES = {
     "pion_v_b200_hnsw_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_hnsw_last_stats": (_I, [_P, _P]),
     "pion_v_b200_hnsw_metric_scores": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_slot_scan_topk": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_hnsw_set_rerank_rows": (_I, [_P, _P, _P, _I64, _I64, _I]),
+    "pion_v_b200_slot_last_stats": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_brute_force": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _P, _I]),
     "pion_v_beam_1536": (_I64, [_P]),
     "pion_v_quant_beam_1536": (_I64, [_P]),
     "pion_v_b200_beam_forget": (_I, [_P]),

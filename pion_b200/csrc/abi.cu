@@ -289,7 +289,8 @@ int pion_v_b200_index_free(pion_b200_index* index) {
                   index->hnsw.l0_slots,
                   index->hnsw.node_slot,  index->hnsw.node_ids,     index->hnsw.deleted,
                   index->hnsw.node_level, index->hnsw.upper_offset, index->hnsw.upper_links,
-                  index->hnsw.upper_slots, index->hnsw.ext_to_node};
+                  index->hnsw.upper_slots, index->hnsw.ext_to_node,
+                  index->hnsw.slot_ext,   index->hnsw.rerank,       index->hnsw.chunk_vmin};
     for (void* p : hn)
         if (p) cudaFree(p);
     delete index;

@@ -211,6 +211,29 @@ int pion_v_b200_register_hnsw(pion_b200_ctx* ctx, const pion_b200_hnsw_layout* L
             if (!rc) rc = upload(&h.upper_slots, us.data(), words);
         }
         if (!rc && L->deleted) rc = upload(&h.deleted, L->deleted, (n + 7) / 8);
+        if (!rc) {  // slot -> external id (gpu_slot_ext_ids, hnsw.mojo:2829-2874)
+            std::vector<int32_t> se(n, -1);
+            for (size_t i = 0; i < n; ++i) se[L->node_slot[i]] = L->node_ids[i];
+            rc = upload(&h.slot_ext, se.data(), n);
+        }
+        if (!rc) {  // per 32 slots the smallest norm, for the brute-force scan's pre-test
+            const size_t chunks = (n + 255) / 256 * 8;
+            if (cudaMalloc(&h.chunk_vmin, chunks * sizeof(int)) != cudaSuccess) {
+                cudaGetLastError();
+                h.chunk_vmin = nullptr;
+                rc = PION_B200_ENOMEM;
+            }
+            if (!rc) rc = launch_slot_chunk_vmin(h.norms, (int64_t)n, h.chunk_vmin, ctx->stream);
+            if (!rc && cudaStreamSynchronize(ctx->stream) != cudaSuccess) rc = PION_B200_ECUDA;
+        }
+        if (!rc) {  // the slot codes as the B operand of the brute-force scan
+            if (make_tmap_2d(&ix->tmap_rows, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, h.codes,
+                             (uint64_t)hnsw_dim(), (uint64_t)n, (uint64_t)hnsw_dim(),
+                             (uint32_t)slot_k_block(), (uint32_t)slot_tile_rows(),
+                             CU_TENSOR_MAP_SWIZZLE_128B) != 0)
+                rc = PION_B200_ECUDA;
+            ix->has_tmap = rc == 0;
+        }
         if (!rc) {  // external id -> node, for metric_scores (dense id ranges only)
             int64_t lo = L->node_ids[0], hi = L->node_ids[0];
             for (size_t i = 1; i < n; ++i) {

@@ -84,6 +84,7 @@ struct pion_b200_ctx {
     std::string last_error;
     int64_t launches = 0;
     cudaEvent_t switch_ev = nullptr;  // orders scratch use across set_stream switches
+    int64_t slot_exact = 0;           // queries of the last slot scan that took the exact path
     // scoring-kernel timing (pion_v_b200_timing_*)
     bool timing = false;
     std::vector<cudaEvent_t> ev_start, ev_end;
@@ -126,6 +127,9 @@ struct pion_b200_index {
         uint32_t* upper_links = nullptr;
         uint32_t* upper_slots = nullptr;
         int32_t* ext_to_node = nullptr;  // external id - ext_base -> node (-1: none)
+        int32_t* slot_ext = nullptr;     // slot -> external id (-1: no node)
+        float* rerank = nullptr;         // FP32 rows by slot for the brute-force rerank
+        int* chunk_vmin = nullptr;       // per 32 slots: min floor(norm) (whole tiles)
         int64_t ext_base = 0, ext_count = 0;
         int M = 0;
         int max_level = 0;
@@ -253,6 +257,59 @@ int launch_flat_i8_tc(const Fi8TcLaunch& launch, cudaStream_t st);
 int launch_flat_i8_scan1(const int8_t* rows, const float* row_scale, int64_t n_rows, int dim,
                          const int8_t* q, const float* q_scale, int k, int ctas, float* cand_val,
                          int32_t* cand_idx, cudaStream_t st);
+
+// ---- slot_scan.cu
+int slot_tile_rows();
+int slot_query_tile();
+int slot_k_block();
+int slot_kmax();
+struct SlotTcLaunch {
+    const CUtensorMap* tmap_q = nullptr;     // query codes [nq x 1536]
+    const CUtensorMap* tmap_rows = nullptr;  // slot codes [n x 1536]
+    int k = 1;                               // loop entries
+    const float* bound = nullptr;            // per query: collect d < bound
+    const float* qnorm = nullptr;
+    const float* vnorm = nullptr;
+    int64_t n_rows = 0;
+    int nq = 0;
+    int tile_begin = 0;
+    int tile_end = 0;
+    int n_splits = 1;
+    int cap = 0;
+    float* cand_d = nullptr;
+    int32_t* cand_i = nullptr;
+    int* cand_n = nullptr;
+    int* status = nullptr;
+    float* dense = nullptr;        // dense mode (exact path): [query][slot - dense_base]
+    int64_t dense_base = 0;
+    int64_t dense_ld = 0;
+    const int* n_dense = nullptr;  // queries in the dense rows (null: nq)
+    float* pub = nullptr;          // [nq][n_splits][2] published list thresholds, or null
+    const int* chunk_vmin = nullptr;  // per 32-slot chunk min floor(norm), whole tiles
+};
+int launch_slot_chunk_vmin(const float* vnorm, int64_t n, int* out, cudaStream_t st);
+int launch_slot_prep(const int8_t* codes, const float* qnorm_in, int nq, int k, float* qnorm,
+                     float* st_d, int32_t* st_i, float* st_worst, int* st_widx, int* qflag,
+                     int* flags, int force_exact, cudaStream_t st);
+int launch_slot_tc(const SlotTcLaunch& launch, cudaStream_t st);
+int launch_slot_replay(const float* cand_d, const int32_t* cand_i, const int* cand_n, int n_lists,
+                       int cap, int nq, int k, float* st_d, int32_t* st_i, float* st_worst,
+                       int* st_widx, int* qflag, int* flags, unsigned long long* counters,
+                       cudaStream_t st);
+int launch_slot_gather(const int8_t* qcodes, const float* qnorm, const int* flags, int first,
+                       int count, int k, int8_t* fcodes, float* fqn, int* n_dense, float* fd,
+                       int32_t* fi, float* fworst, int* fwidx, cudaStream_t st);
+int launch_slot_dense_replay(const float* dense, int64_t ld, int64_t base, int64_t len,
+                             const int* n_dense, int count, int k, float* fd, int32_t* fi,
+                             float* fworst, int* fwidx, int last, const int* flags, int first,
+                             float* st_d, int32_t* st_i, float* st_worst, int* st_widx,
+                             const int* qflag, cudaStream_t st);
+int launch_slot_emit(const float* st_d, const int32_t* st_i, int nq, int k, int k_out,
+                     int32_t* out_slots, float* out_d, cudaStream_t st);
+int launch_slot_finish(const float* st_d, const int32_t* st_i, int nq, int k, const float* q_raw,
+                       const float* rerank, const int32_t* slot_ext, int64_t n, int final_k,
+                       int k_out, int32_t* out_ids, float* out_scores, int32_t* out_found,
+                       cudaStream_t st);
 
 // ---- bq.cu
 int bq_tile_rows();

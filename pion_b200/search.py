@@ -472,6 +472,66 @@ class HNSWIndex(_Index):
             c.check(c.lib.pion_v_b200_hnsw_metric_scores(c.h, self.h, pq, nq, k, pi, ps, m))
         return scores
 
+    def slot_scan_topk(self, q_codes, k: int, q_norm=None, num_vectors: int | None = None,
+                       ctx: Context | None = None):
+        """The GPU brute-force slot scan (pion_metal_search_topk_w, src/ffi/metal_wrap.m:
+        495-580) for a batch: int8 codes [nq, 1536] (and optionally their norms) ->
+        (slots int32 [nq, k], INT8 L2 distances float32) in the order the worst-replace
+        loop leaves them; -1 / +inf past min(k, num_vectors)."""
+        c = ctx or self.ctx
+        pq, mem, kq = _ptr(q_codes, np.int8, "q_codes")
+        pn, kn = None, None
+        if q_norm is not None:
+            pn, mn, kn = _ptr(q_norm, np.float32, "q_norm")
+            mem = _same_mem(mem, mn)
+        nq = q_codes.shape[0]
+        nv = self.n_rows if num_vectors is None else int(num_vectors)
+        slots, dist, ps, pd = _outputs(mem == MEM_DEVICE, nq, k,
+                                       q_codes.device if mem == MEM_DEVICE else None)
+        with _TorchStream(c, mem):
+            c.check(c.lib.pion_v_b200_slot_scan_topk(c.h, self.h, pq, pn, nq, nv, k, ps, pd,
+                                                      mem))
+        return slots, dist
+
+    def slot_stats(self, ctx: Context | None = None) -> dict:
+        """Work of the context's last slot scan or brute-force call: queries that took
+        the exact CUDA-core scan, candidate slots replayed through the top-k loop."""
+        c = ctx or self.ctx
+        out = (ctypes.c_int64 * 2)()
+        c.check(c.lib.pion_v_b200_slot_last_stats(c.h, out))
+        return dict(zip(("exact_queries", "replayed"), list(out)))
+
+    def set_rerank_rows(self, rows):
+        """FP32 rows [slots, 1536] by slot for brute_force's rerank
+        (pion_metal_register_rerank_buffer); None drops them."""
+        if rows is None:
+            self.ctx.check(self.ctx.lib.pion_v_b200_hnsw_set_rerank_rows(
+                self.ctx.h, self.h, None, 0, 0, MEM_HOST))
+            return
+        pr, mem, kr = _ptr(rows, np.float32, "rows")
+        with _TorchStream(self.ctx, mem):
+            self.ctx.check(self.ctx.lib.pion_v_b200_hnsw_set_rerank_rows(
+                self.ctx.h, self.h, pr, rows.shape[0], rows.shape[1], mem))
+
+    def brute_force(self, q, k: int, ctx: Context | None = None):
+        """search_gpu_brute_force (src/vector/hnsw.mojo:3916-3992) for a batch: q float32
+        [nq, 1536] -> (external ids int32 [nq, k], scores float32 [nq, k], found int32
+        [nq]); scores are INT8 L2 distances, or FP32 squared L2 with rerank rows."""
+        c = ctx or self.ctx
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        nq = q.shape[0]
+        dev = mem == MEM_DEVICE
+        ids, sc, pi, pv = _outputs(dev, nq, k, q.device if dev else None)
+        if dev:
+            found = torch.empty(nq, dtype=torch.int32, device=q.device)
+            pf = found.data_ptr()
+        else:
+            found = np.empty(nq, np.int32)
+            pf = found.ctypes.data
+        with _TorchStream(c, mem):
+            c.check(c.lib.pion_v_b200_hnsw_brute_force(c.h, self.h, pq, nq, k, pi, pv, pf, mem))
+        return ids, sc, found
+
     def last_stats(self, ctx: Context | None = None) -> dict:
         """Work of the context's last search: level-0 evaluations, expansions, upper-level
         evaluations."""
