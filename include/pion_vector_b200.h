@@ -188,6 +188,28 @@ int pion_v_b200_timing_enable(pion_b200_ctx *ctx, int enable);
  * scoring-kernel launches. */
 int pion_v_b200_timing_read(pion_b200_ctx *ctx, double *total_ms, int64_t *count);
 
+/* ------------------------------------------------------------ any index kind -- */
+#define PION_B200_KIND_FLAT_I8 1  /* rows int8 [n x dim] + row_scale: register_flat_i8 */
+#define PION_B200_KIND_FLAT_F32 2 /* rows fp32 [n x dim]: register_flat_f32 */
+#define PION_B200_KIND_BQ 3       /* rows fp32 [n x dim]: register_bq */
+#define PION_B200_KIND_HNSW 4     /* hnsw layout: register_hnsw */
+
+typedef struct pion_b200_index_desc {
+    int32_t kind;            /* PION_B200_KIND_* */
+    int32_t mem;             /* PION_B200_MEM_* of rows / row_scale */
+    int64_t n_rows, dim, id_base;
+    int32_t normalize;       /* FLAT_F32, BQ: normalise rows at ingest (COSINE) */
+    int32_t reserved;
+    const void *rows;
+    const float *row_scale;  /* FLAT_I8 */
+    const struct pion_b200_hnsw_layout *hnsw; /* HNSW */
+} pion_b200_index_desc;
+
+/* One registration entry point for every index kind: dispatches on desc->kind to the
+ * kind's own register call with the same arguments (and errors). */
+int pion_v_b200_register_index(pion_b200_ctx *ctx, const pion_b200_index_desc *desc,
+                               pion_b200_index **out_index);
+
 /* FLAT INT8 inner product: rows int8[n_rows x dim]
  * (dim % 16 == 0, dim <= 16384) with a per-row fp32 scale, the output of
  * pkm_quantize_rows_i8 (src/vector/pkm_kernels.mojo:152-191).  Result ids are
@@ -356,6 +378,19 @@ int pion_v_b200_register_hnsw(pion_b200_ctx *ctx, const pion_b200_hnsw_layout *l
 int pion_v_b200_hnsw_search(pion_b200_ctx *ctx, const pion_b200_index *index, const float *q,
                             int64_t nq, int64_t k, int64_t ef, int32_t *out_ids, float *out_dist,
                             int mem);
+
+/* The level-0 beam of a batch of queries over a registered graph, each from a pool the
+ * caller seeded: the batched form of pion_v_beam_1536 (beam_search_1536_ref,
+ * src/vector/reference/beam_1536.mojo:85-135, on LinearPool, src/common/heap.mojo:133-234).
+ * q_codes int8 [nq x 1536] (the codes _quantize_query_to_int8 produced), q_norm [nq] (the
+ * view's query_norm_sq); pools [nq x ef] of 8-byte (f32 dist, u32 node | 0x80000000 when
+ * expanded) entries; pool_size [nq] in/out; pool_cursor [nq] or NULL (0).  The nodes in a
+ * pool count as visited.  Each pool is written back entry for entry as the reference leaves
+ * it (its cursor is then its size).  ef in [1, 1024]. */
+int pion_v_b200_hnsw_beam_batch(pion_b200_ctx *ctx, const pion_b200_index *index,
+                                const int8_t *q_codes, const float *q_norm, int64_t nq,
+                                int64_t ef, void *pools, int32_t *pool_size,
+                                const int32_t *pool_cursor, int mem);
 
 /* metric_scores (src/vector/hnsw.mojo:4523-4651) for INT8 codes: replaces scores[t][j] by
  * the index metric's distance between query t (normalised once under COSINE, clamped to

@@ -76,6 +76,8 @@ SIGNATURES = {
     "pion_v_b200_hnsw_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_hnsw_last_stats": (_I, [_P, _P]),
     "pion_v_b200_hnsw_metric_scores": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _I]),
+    "pion_v_b200_register_index": (_I, [_P, _P, _P]),
+    "pion_v_b200_hnsw_beam_batch": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _I]),
     "pion_v_b200_slot_scan_topk": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_hnsw_set_rerank_rows": (_I, [_P, _P, _P, _I64, _I64, _I]),
     "pion_v_b200_slot_last_stats": (_I, [_P, _P]),
@@ -84,6 +86,15 @@ SIGNATURES = {
     "pion_v_quant_beam_1536": (_I64, [_P]),
     "pion_v_b200_beam_forget": (_I, [_P]),
 }
+
+
+class IndexDesc(ctypes.Structure):
+    """pion_b200_index_desc (include/pion_vector_b200.h)."""
+    _fields_ = [("kind", ctypes.c_int32), ("mem", ctypes.c_int32), ("n_rows", ctypes.c_int64),
+                ("dim", ctypes.c_int64), ("id_base", ctypes.c_int64),
+                ("normalize", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("rows", ctypes.c_void_p), ("row_scale", ctypes.c_void_p),
+                ("hnsw", ctypes.c_void_p)]
 
 
 class LinearPool(ctypes.Structure):

@@ -270,6 +270,30 @@ int pion_v_b200_reserve(pion_b200_ctx* ctx, int64_t max_nq, int64_t max_k) {
     return 0;
 }
 
+int pion_v_b200_register_index(pion_b200_ctx* ctx, const pion_b200_index_desc* d,
+                               pion_b200_index** out_index) {
+    if (!valid_ctx(ctx) || !out_index) return PION_B200_EINVAL;
+    if (!d) return set_error(ctx, PION_B200_EINVAL, "register_index: null descriptor");
+    switch (d->kind) {
+        case PION_B200_KIND_FLAT_I8:
+            return pion_v_b200_register_flat_i8(ctx, static_cast<const int8_t*>(d->rows),
+                                                d->row_scale, d->n_rows, d->dim, d->id_base,
+                                                d->mem, out_index);
+        case PION_B200_KIND_FLAT_F32:
+            return pion_v_b200_register_flat_f32(ctx, static_cast<const float*>(d->rows),
+                                                 d->n_rows, d->dim, d->id_base, d->normalize,
+                                                 d->mem, out_index);
+        case PION_B200_KIND_BQ:
+            return pion_v_b200_register_bq(ctx, static_cast<const float*>(d->rows), d->n_rows,
+                                           d->dim, d->id_base, d->normalize, d->mem, out_index);
+        case PION_B200_KIND_HNSW:
+            return pion_v_b200_register_hnsw(ctx, d->hnsw, out_index);
+        default:
+            *out_index = nullptr;
+            return set_error(ctx, PION_B200_EINVAL, "register_index: unknown kind %d", d->kind);
+    }
+}
+
 int64_t pion_v_b200_index_rows(const pion_b200_index* index) { return index ? index->n_rows : -1; }
 
 int pion_v_b200_index_free(pion_b200_index* index) {

@@ -393,6 +393,133 @@ int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const
     return 0;
 }
 
+int pion_v_b200_hnsw_beam_batch(pion_b200_ctx* ctx, const pion_b200_index* ix,
+                                const int8_t* q_codes, const float* q_norm, int64_t nq,
+                                int64_t ef, void* pools, int32_t* pool_size,
+                                const int32_t* pool_cursor, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kHNSW)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_beam_batch: not an HNSW index");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_beam_batch: index on another device");
+    if (nq < 0 || (nq > 0 && (!q_codes || !q_norm || !pools || !pool_size)))
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_beam_batch: bad arguments");
+    if (ef < 1 || ef > 1024)
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_beam_batch: ef %lld not in [1, 1024]",
+                         (long long)ef);
+    if (nq > (1 << 24))
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_beam_batch: batch too large");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_beam_batch: bad mem %d", mem);
+    if (nq == 0 || ix->n_rows == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    const int per_sm = hnsw_ctas_per_sm((int)ef);
+    if (per_sm <= 0)
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_beam_batch: ef %lld does not fit",
+                         (long long)ef);
+    cudaStream_t st = ctx->stream;
+    const int dim = hnsw_dim();
+    const auto& h = ix->hnsw;
+    const size_t cb = (size_t)nq * dim, nb = (size_t)nq * 4, pb = (size_t)nq * ef * 8;
+    const int8_t* dc = q_codes;
+    const float* dn = q_norm;
+    void* dp = pools;
+    int32_t* ds = pool_size;
+    const int32_t* dcur = pool_cursor;
+    int32_t* zero_cur = nullptr;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align_up(bytes, 256);
+        return o;
+    };
+    const size_t o_c = take(mem == PION_B200_MEM_HOST ? cb : 0),
+                 o_n = take(mem == PION_B200_MEM_HOST ? nb : 0),
+                 o_p = take(mem == PION_B200_MEM_HOST ? pb : 0), o_s = take(nb),
+                 o_k = take(nb);
+    if (ensure(ctx->stage_in, off) != 0 || ensure(ctx->hnsw_misc, 64) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "hnsw_beam_batch: staging");
+    char* base = static_cast<char*>(ctx->stage_in.ptr);
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(base + o_c, q_codes, cb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(base + o_n, q_norm, nb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(base + o_p, pools, pb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(base + o_s, pool_size, nb, cudaMemcpyHostToDevice, st) !=
+                cudaSuccess ||
+            (pool_cursor && cudaMemcpyAsync(base + o_k, pool_cursor, nb, cudaMemcpyHostToDevice,
+                                            st) != cudaSuccess))
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_beam_batch: copy failed");
+        dc = reinterpret_cast<const int8_t*>(base + o_c);
+        dn = reinterpret_cast<const float*>(base + o_n);
+        dp = base + o_p;
+        ds = reinterpret_cast<int32_t*>(base + o_s);
+        dcur = pool_cursor ? reinterpret_cast<const int32_t*>(base + o_k) : nullptr;
+    }
+    if (!dcur) {  // cursors default to 0 (the first unchecked entry is found by the scan)
+        zero_cur = reinterpret_cast<int32_t*>(base + o_k);
+        if (cudaMemsetAsync(zero_cur, 0, nb, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_beam_batch: memset failed");
+        dcur = zero_cur;
+    }
+    const int warps = hnsw_warps_per_cta();
+    int64_t ctas = (int64_t)per_sm * ctx->num_sms;
+    const int64_t need = (nq + warps - 1) / warps;
+    if (ctas > need) ctas = need;
+    const int64_t vis_words = ((ix->n_rows + 31) / 32 + 3) / 4 * 4;
+    if (ensure(ctx->hnsw_visited, (size_t)ctas * warps * vis_words * 4) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "hnsw_beam_batch: visited bitmaps");
+    unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
+    if (cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 32, st) != cudaSuccess)
+        return set_error(ctx, PION_B200_ECUDA, "hnsw_beam_batch: memset failed");
+    HnswLaunch Lc;
+    Lc.codes = h.codes;
+    Lc.norms = h.norms;
+    Lc.l0_compact = h.l0_compact;
+    Lc.l0_slots = h.l0_slots;
+    Lc.node_slot = h.node_slot;
+    Lc.node_ids = h.node_ids;
+    Lc.deleted = h.deleted;
+    Lc.node_level = h.node_level;
+    Lc.upper_offset = h.upper_offset;
+    Lc.upper_links = h.upper_links;
+    Lc.upper_slots = h.upper_slots;
+    Lc.M = h.M;
+    Lc.max_level = h.max_level;
+    Lc.num_nodes = ix->n_rows;
+    Lc.entry = h.entry;
+    Lc.qcodes = dc;
+    Lc.qblk = nullptr;  // unused when starting from a pool
+    Lc.nq = (int)nq;
+    Lc.k = 0;
+    Lc.ef = (int)ef;
+    Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+    Lc.vis_words = vis_words;
+    Lc.stats = stats;
+    Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
+    Lc.status = ctx->d_status;
+    Lc.ctas = (int)ctas;
+    Lc.pool_io = dp;
+    Lc.pool_stride = ef;
+    Lc.pool_size = ds;
+    Lc.pool_cursor = dcur;
+    Lc.qn_given = dn;
+    Lc.pool_size_out = ds;
+    timing_begin(ctx);
+    int rc = launch_hnsw_beam(Lc, st);
+    timing_end(ctx);
+    ctx->launches++;
+    if (rc != 0)
+        return set_error(ctx, rc, "hnsw_beam_batch: launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(pools, dp, pb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(pool_size, ds, nb, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_beam_batch: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
 int pion_v_b200_hnsw_metric_scores(pion_b200_ctx* ctx, const pion_b200_index* ix, const float* q,
                                    int64_t nq, int64_t k, const int32_t* ids, float* scores,
                                    int mem) {
@@ -580,7 +707,13 @@ int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
     if (ensure(ctx->stage_in, total) != 0 || ensure(ctx->hnsw_misc, 64) != 0)
         return beam_fail("out of device memory");
     char* base = static_cast<char*>(ctx->stage_in.ptr);
+    // o_size: {size out, size in, cursor in, query norm}
+    int32_t meta[4] = {0, (int32_t)pool->size,
+                       (int32_t)(pool->cursor < pool->size ? pool->cursor : pool->size), 0};
+    memcpy(&meta[3], &v->query_norm_sq, 4);
     if (cudaMemcpyAsync(base + o_q, v->query_int8, dim, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(base + o_size, meta, sizeof(meta), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess ||
         (pool->size > 0 && cudaMemcpyAsync(base + o_pool, pool->entries, (size_t)pool->size * 8,
                                            cudaMemcpyHostToDevice, st) != cudaSuccess) ||
         (del_bytes && cudaMemcpyAsync(base + o_del, v->deleted, del_bytes, cudaMemcpyHostToDevice,
@@ -612,9 +745,10 @@ int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
     Lc.status = ctx->d_status;
     Lc.ctas = 1;
     Lc.pool_io = base + o_pool;
-    Lc.pool_size = (int)pool->size;
-    Lc.pool_cursor = (int)(pool->cursor < pool->size ? pool->cursor : pool->size);
-    Lc.qn_given = v->query_norm_sq;
+    Lc.pool_stride = ef;
+    Lc.pool_size = reinterpret_cast<const int*>(base + o_size) + 1;
+    Lc.pool_cursor = reinterpret_cast<const int*>(base + o_size) + 2;
+    Lc.qn_given = reinterpret_cast<const float*>(base + o_size) + 3;
     Lc.pool_size_out = reinterpret_cast<int*>(base + o_size);
     int rc = launch_hnsw_beam(Lc, st);
     ctx->launches++;

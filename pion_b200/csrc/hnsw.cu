@@ -88,13 +88,16 @@ struct Params {
     unsigned long long* stats;  // level-0 evaluations, expansions, upper evaluations
     unsigned* next_query;
     int* status;
-    // Single-beam mode of pion_v_beam_1536 (nq = 1): the level-0 beam only, from the
-    // caller's pool (entries with their CHECKED bits, size, cursor) and query norm, the
-    // pool written back in place (cursor = size at the end).
+    // From-pool mode (pion_v_beam_1536, pion_v_b200_hnsw_beam_batch): the level-0 beam
+    // only, per query from the caller's pool (entries with their CHECKED bits, size,
+    // cursor; pool_stride entries apart) and query norm, each pool written back in place
+    // (cursor = size at the end).
     int from_pool;
     Entry* pool_io;
-    int pool_size, pool_cursor;
-    float qn_given;
+    int64_t pool_stride;
+    const int* pool_size;
+    const int* pool_cursor;
+    const float* qn_given;
     int* pool_size_out;
 };
 
@@ -280,7 +283,7 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             for (int b = 0; b < NBLK; ++b) qn_int += p.qblk[(size_t)qi * 8 + b];
             if (lane < 8) qq[lane] = p.qblk[(size_t)qi * 8 + lane];
         }
-        const float qn = p.from_pool ? p.qn_given : (float)qn_int;
+        const float qn = p.from_pool ? p.qn_given[qi] : (float)qn_int;
         {
             int4* v4 = reinterpret_cast<int4*>(vis);
             const int64_t n4 = p.vis_words / 4;
@@ -375,10 +378,10 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
         int size = 1, hint = 0;
         if (p.from_pool) {
             // the caller's pool; its nodes are the ones it marked visited
-            size = min(p.pool_size, ef);
-            hint = min(p.pool_cursor, size);
+            size = min(p.pool_size[qi], ef);
+            hint = min(p.pool_cursor[qi], size);
             for (int i = lane; i < size; i += 32) {
-                const Entry e = p.pool_io[i];
+                const Entry e = p.pool_io[(size_t)qi * p.pool_stride + i];
                 pool[i] = e;
                 const uint32_t nd = e.id & ~CHECKED;
                 if (nd < nn) atomicOr(&vis[nd >> 5], 1u << (nd & 31));
@@ -619,8 +622,8 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
         }
 
         if (p.from_pool) {  // the whole pool back to the caller
-            for (int i = lane; i < size; i += 32) p.pool_io[i] = pool[i];
-            if (lane == 0) *p.pool_size_out = size;
+            for (int i = lane; i < size; i += 32) p.pool_io[(size_t)qi * p.pool_stride + i] = pool[i];
+            if (lane == 0) p.pool_size_out[qi] = size;
         }
         // drain: the first k entries, nearest first
         for (int i = lane; i < p.k; i += 32) {
@@ -821,6 +824,7 @@ int launch_hnsw_beam(const HnswLaunch& L, cudaStream_t st) {
     p.status = L.status;
     p.from_pool = L.pool_io != nullptr;
     p.pool_io = reinterpret_cast<hb::Entry*>(L.pool_io);
+    p.pool_stride = L.pool_stride;
     p.pool_size = L.pool_size;
     p.pool_cursor = L.pool_cursor;
     p.qn_given = L.qn_given;

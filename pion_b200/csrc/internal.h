@@ -169,10 +169,13 @@ struct HnswLaunch {
     unsigned* next_query = nullptr;
     int* status = nullptr;
     int ctas = 0;
-    // single-beam mode (pion_v_beam_1536): start from this pool of (f32 dist, u32 id)
+    // from-pool mode (pion_v_beam_1536, hnsw_beam_batch): per query a pool of
+    // (f32 dist, u32 id) entries, pool_stride entries apart, its size, cursor and norm
     void* pool_io = nullptr;
-    int pool_size = 0, pool_cursor = 0;
-    float qn_given = 0.0f;
+    int64_t pool_stride = 0;
+    const int* pool_size = nullptr;
+    const int* pool_cursor = nullptr;
+    const float* qn_given = nullptr;
     int* pool_size_out = nullptr;
 };
 int hnsw_dim();

@@ -14,7 +14,10 @@ Mirrors the operator surface of Pion's vector path (pavelhorak/pion):
 * ``HNSWGraph`` — the reference's FT.OPTIMIZE graph build on the host CPU
   (src/vector/hnsw.mojo:2540-2620) into its compact level-0 layout;
 * ``HNSWIndex.search`` — batched ``search_fp32_scored`` at dim 1536: upper-level
-  greedy descent, then ``beam_search_1536_ref`` per query on the GPU.
+  greedy descent, then ``beam_search_1536_ref`` per query on the GPU;
+  ``metric_scores`` — the reply scores (src/vector/hnsw.mojo:4523-4651);
+  ``slot_scan_topk`` / ``brute_force`` — the GPU brute-force scan of the slot buffer
+  (pion_metal_search_topk_w, search_gpu_brute_force).
 
 Arrays may be numpy (host memory: the call copies to and from the GPU) or CUDA
 torch tensors (device memory: used in place on the context's stream).  Errors
@@ -471,6 +474,42 @@ class HNSWIndex(_Index):
         with _TorchStream(c, m):
             c.check(c.lib.pion_v_b200_hnsw_metric_scores(c.h, self.h, pq, nq, k, pi, ps, m))
         return scores
+
+    def beam_batch(self, q_codes, q_norm, pools, sizes, cursors=None,
+                   ctx: Context | None = None):
+        """The level-0 beam from caller-seeded pools for a batch (pion_v_beam_1536's
+        contract): q_codes int8 [nq, 1536], q_norm float32 [nq], pools a structured or
+        uint64 array [nq, ef] of (f32 dist, u32 node) entries and sizes int32 [nq], both
+        updated in place; cursors int32 [nq] or None."""
+        c = ctx or self.ctx
+        pq, mq, kq = _ptr(q_codes, np.int8, "q_codes")
+        pn, mn, kn = _ptr(q_norm, np.float32, "q_norm")
+        if _is_torch(pools):
+            pp, mp = pools.data_ptr(), MEM_DEVICE if pools.is_cuda else MEM_HOST
+            ps, ms = sizes.data_ptr(), MEM_DEVICE if sizes.is_cuda else MEM_HOST
+        else:
+            for a, nm in ((pools, "pools"), (sizes, "sizes")):
+                if not (isinstance(a, np.ndarray) and a.flags["C_CONTIGUOUS"]):
+                    raise TypeError(f"{nm} must be a contiguous array (updated in place)")
+            if pools.dtype.itemsize * (pools.shape[1] if pools.ndim > 1 else 1) % 8:
+                raise TypeError("pools entries must be 8 bytes")
+            if sizes.dtype != np.int32:
+                raise TypeError("sizes must be int32")
+            pp, mp = pools.ctypes.data, MEM_HOST
+            ps, ms = sizes.ctypes.data, MEM_HOST
+        pc, kc = None, None
+        mems = [mq, mn, mp, ms]
+        if cursors is not None:
+            pc, mc, kc = _ptr(cursors, np.int32, "cursors")
+            mems.append(mc)
+        m = _same_mem(*mems)
+        nq = q_codes.shape[0]
+        ef = pools.shape[1] if (pools.ndim > 1 and pools.dtype.itemsize == 8) else \
+            pools.nbytes // (8 * max(1, nq))
+        with _TorchStream(c, m):
+            c.check(c.lib.pion_v_b200_hnsw_beam_batch(c.h, self.h, pq, pn, nq, ef, pp, ps, pc,
+                                                       m))
+        return pools, sizes
 
     def slot_scan_topk(self, q_codes, k: int, q_norm=None, num_vectors: int | None = None,
                        ctx: Context | None = None):

@@ -134,6 +134,31 @@ def test_device_memory_path_equals_host(ctx, oracle):
     assert np.array_equal(sc_d.cpu().numpy(), sc_h)
 
 
+def test_register_index_descriptor(ctx, oracle):
+    """pion_v_b200_register_index dispatches on the kind: a FLAT INT8 index registered
+    through the descriptor answers like one registered directly; unknown kinds fail."""
+    import ctypes
+
+    import pion_b200
+    from pion_b200 import _lib
+    keys, ks, q, qsc = quantized_case(oracle, 5000, 1536, 64, seed=4)
+    want_i, want_s = pion_b200.FlatI8Index(ctx, keys, ks).search(q, qsc, 10)
+    d = _lib.IndexDesc(kind=1, mem=0, n_rows=keys.shape[0], dim=1536, id_base=0, normalize=0,
+                       reserved=0, rows=keys.ctypes.data, row_scale=ks.ctypes.data, hnsw=None)
+    h = ctypes.c_void_p()
+    ctx.check(ctx.lib.pion_v_b200_register_index(ctx.h, ctypes.byref(d), ctypes.byref(h)))
+    ids = np.empty((64, 10), np.int32)
+    sc = np.empty((64, 10), np.float32)
+    ctx.check(ctx.lib.pion_v_b200_flat_i8_knn(ctx.h, h, q.ctypes.data, qsc.ctypes.data, 64, 10,
+                                              ids.ctypes.data, sc.ctypes.data, 0))
+    ctx.lib.pion_v_b200_index_free(h)
+    assert np.array_equal(ids, want_i) and np.array_equal(sc, want_s)
+    d.kind = 9
+    h2 = ctypes.c_void_p()
+    assert ctx.lib.pion_v_b200_register_index(ctx.h, ctypes.byref(d), ctypes.byref(h2)) == -1
+    assert not h2.value
+
+
 def test_empty_index_and_bad_shapes(ctx, oracle):
     import pion_b200
     keys = np.zeros((0, 1536), np.int8)

@@ -181,3 +181,41 @@ def test_metric_scores(oracle, small, ctx):
     got2 = ix2.metric_scores(qs2 * 2.0, i2, d2.copy())
     want2 = oracle.hnsw_metric_scores(g2.arrays(), qs2 * 2.0, i2, d2)
     assert np.array_equal(got2.view(np.uint32), want2.view(np.uint32))
+
+
+def test_beam_batch_matches_oracle(oracle, small):
+    """pion_v_b200_hnsw_beam_batch over the registered graph: every query's pool, seeded
+    as search_fp32_scored seeds it (the start node), comes back equal to the restated
+    beam_search_1536_ref's entry for entry; pools with several seeded entries, expanded
+    entries and a cursor too."""
+    g, A, ix, rows, qs = small
+    nq = 24
+    codes = oracle.hnsw_query_codes(A, qs[:nq])
+    comp = A["compact_buffer"]
+    n = A["num_nodes"]
+    rng = np.random.Generator(np.random.PCG64(12))
+    qn = (codes.astype(np.int32) ** 2).sum(1).astype(np.float32)
+    for ef in (16, 100):
+        pools = np.zeros((nq, ef), dtype=[("d", "<f4"), ("id", "<u4")])
+        sizes = np.zeros(nq, np.int32)
+        cursors = np.zeros(nq, np.int32)
+        seeds = []
+        for t in range(nq):
+            m = 1 if t % 3 else 3
+            start = rng.choice(n, m, replace=False)
+            d0 = []
+            for s_ in start:
+                v = comp[A["node_slot"][s_], 8:8 + 1536].astype(np.int32)
+                d0.append(np.float32(((v - codes[t].astype(np.int32)) ** 2).sum()))
+            order = np.argsort(np.array(d0), kind="stable")
+            ds_, ids_ = np.array(d0, np.float32)[order], start[order].astype(np.uint32)
+            pools["d"][t, :m] = ds_
+            pools["id"][t, :m] = ids_
+            sizes[t] = m
+            seeds.append((ds_, ids_))
+        ix.beam_batch(codes, qn, pools, sizes, cursors)
+        for t in range(nq):
+            od, oi = oracle.hnsw_beam_pool(A, codes[t], qn[t], ef, seeds[t][0], seeds[t][1], 0)
+            assert sizes[t] == len(od)
+            assert np.array_equal(pools["id"][t, :sizes[t]], oi)
+            assert np.array_equal(pools["d"][t, :sizes[t]].view(np.uint32), od.view(np.uint32))
