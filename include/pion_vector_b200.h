@@ -341,6 +341,18 @@ typedef struct pion_b200_hnsw_layout {
 
 typedef struct pion_b200_hnsw_graph pion_b200_hnsw_graph;
 
+/* The reference's index file pion.hnsw.0 (HNSWGraph.save_to_disk / load_from_disk,
+ * src/vector/hnsw.mojo:1209-1700; format v3 to v5, plain INT8 slots, global calibration):
+ * pion_v_b200_hnsw_load reads one into a host graph whose layout
+ * (pion_v_b200_hnsw_graph_layout) registers with pion_v_b200_register_hnsw, so a graph the
+ * engine built serves on the GPU; l0_slots is derived as _build_l0_slots does.  Quantised
+ * compact formats and per-group calibration are refused (PION_B200_ESHAPE).
+ * pion_v_b200_hnsw_save writes a graph as a v5 file the engine loads (max_elements: the
+ * engine's capacity, which its loader checks; 0 = the largest external id + 1). */
+int pion_v_b200_hnsw_load(const char *path, pion_b200_hnsw_graph **out_graph);
+int pion_v_b200_hnsw_save(const pion_b200_hnsw_graph *graph, const char *path,
+                          int64_t max_elements);
+
 /* Builds an HNSW INT8 graph on the host CPU the way the reference's FT.OPTIMIZE does
  * (src/vector/hnsw.mojo:2540-2620: _calibrate, quantize, _level_of, the parallel link
  * lanes of _insert_to_graph_mt, the relink and _repair_l0 passes, compact_vectors),

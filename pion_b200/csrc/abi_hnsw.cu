@@ -7,6 +7,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <string>
 #include <thread>
 #include <vector>
 
@@ -108,6 +109,43 @@ int pion_v_b200_hnsw_build(const float* rows, int64_t n_rows, int64_t dim, int64
     }
     *out_graph = g;
     return 0;
+}
+
+int pion_v_b200_hnsw_load(const char* path, pion_b200_hnsw_graph** out_graph) {
+    if (!path || !out_graph) return PION_B200_EINVAL;
+    *out_graph = nullptr;
+    pion_b200_hnsw_graph* gr = new (std::nothrow) pion_b200_hnsw_graph();
+    if (!gr) return PION_B200_ENOMEM;
+    std::string why;
+    int rc = 0;
+    try {
+        rc = hnsw::load_file(path, gr->g, why);
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+        why = "out of host memory";
+    }
+    if (rc != 0) {
+        fprintf(stderr, "pion_vector_b200: hnsw_load %s: %s\n", path, why.c_str());
+        delete gr;
+        return rc;
+    }
+    *out_graph = gr;
+    return 0;
+}
+
+int pion_v_b200_hnsw_save(const pion_b200_hnsw_graph* graph, const char* path,
+                          int64_t max_elements) {
+    if (!graph || !path) return PION_B200_EINVAL;
+    std::string why;
+    int rc = 0;
+    try {
+        rc = hnsw::save_file(graph->g, path, max_elements, why);
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+        why = "out of host memory";
+    }
+    if (rc != 0) fprintf(stderr, "pion_vector_b200: hnsw_save %s: %s\n", path, why.c_str());
+    return rc;
 }
 
 int pion_v_b200_hnsw_graph_layout(const pion_b200_hnsw_graph* graph, pion_b200_hnsw_layout* out) {

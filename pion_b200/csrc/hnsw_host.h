@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <string>
 #include <vector>
 
 namespace pion {
@@ -41,6 +42,11 @@ struct BuildStats {
 // reference's parameters; node i gets external id id_base + i.  n_threads link lanes.
 int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
           int64_t id_base, int n_threads, Graph& g, BuildStats* stats);
+
+// The reference's index file (pion.hnsw.0, format v3 to v5, src/vector/hnsw.mojo:
+// 1209-1700): load into a Graph (0, or -1 / -3 with the reason), and save a Graph as v5.
+int load_file(const char* path, Graph& g, std::string& why);
+int save_file(const Graph& g, const char* path, int64_t max_elements, std::string& why);
 
 }  // namespace hnsw
 }  // namespace pion

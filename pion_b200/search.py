@@ -26,6 +26,7 @@ raise ``PionError`` with the library's message; there is no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -386,9 +387,32 @@ class HNSWGraph:
                                              id_base, threads, ctypes.byref(h))
         if rc != 0:
             raise PionError(rc, "hnsw_build failed")
+        self._adopt(h)
+
+    def _adopt(self, h):
         self.h = h
         self.layout = _lib.HnswLayout()
         self.lib.pion_v_b200_hnsw_graph_layout(self.h, ctypes.byref(self.layout))
+
+    @classmethod
+    def load(cls, path: str) -> "HNSWGraph":
+        """A graph from the reference's index file pion.hnsw.0 (format v3 to v5,
+        HNSWGraph.load_from_disk, src/vector/hnsw.mojo:1485-1700)."""
+        self = cls.__new__(cls)
+        self.lib = _lib.load()
+        h = ctypes.c_void_p()
+        rc = self.lib.pion_v_b200_hnsw_load(os.fsencode(path), ctypes.byref(h))
+        if rc != 0:
+            raise PionError(rc, f"hnsw_load {path} failed")
+        self._adopt(h)
+        return self
+
+    def save(self, path: str, max_elements: int = 0):
+        """Write the graph as the reference's index file (format v5, _save_body,
+        src/vector/hnsw.mojo:1209-1440); max_elements: the engine's capacity."""
+        rc = self.lib.pion_v_b200_hnsw_save(self.h, os.fsencode(path), max_elements)
+        if rc != 0:
+            raise PionError(rc, f"hnsw_save {path} failed")
 
     def stats(self) -> dict:
         """lanes, link_drops, relinked, repaired_exits, repaired_links."""

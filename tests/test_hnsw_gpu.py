@@ -219,3 +219,18 @@ def test_beam_batch_matches_oracle(oracle, small):
             assert sizes[t] == len(od)
             assert np.array_equal(pools["id"][t, :sizes[t]], oi)
             assert np.array_equal(pools["d"][t, :sizes[t]].view(np.uint32), od.view(np.uint32))
+
+
+def test_index_file_serves_on_gpu(ctx, oracle, small, tmp_path):
+    """A graph written as the reference's index file (pion.hnsw.0) and read back serves on
+    the GPU with the same pools as the graph it came from."""
+    import pion_b200
+    g, A, ix, rows, qs = small
+    p = str(tmp_path / "pion.hnsw.0")
+    g.save(p)
+    G = pion_b200.HNSWGraph.load(p)
+    gix = pion_b200.HNSWIndex(ctx, G)
+    i0, d0 = ix.search(qs, 10, 64)
+    i1, d1 = gix.search(qs, 10, 64)
+    assert np.array_equal(i0, i1) and np.array_equal(d0.view(np.uint32), d1.view(np.uint32))
+    _same(oracle, G.arrays(), gix, qs, 10, 32)
