@@ -261,6 +261,20 @@ int pion_v_b200_register_flat_f32(pion_b200_ctx *ctx, const float *rows, int64_t
 int pion_v_b200_flat_f32_knn(pion_b200_ctx *ctx, const pion_b200_index *index, const float *q,
                              int64_t nq, int64_t k, int32_t *out_ids, float *out_scores, int mem);
 
+/* merge_delta (src/commands/vector.mojo:1368-1456) for a batch: `index` is a FLAT FP32
+ * index of the ingest rows [0, rows) registered at slot 0 (normalised at ingest under
+ * COSINE); the graph holds slots [0, built).  ids / scores [nq x kg]: each query's graph
+ * results (a -1 id ends a list), rescored in place as _exact_rescore does (slots below
+ * built: 1 - dot_f32_4chain(q^, row) under COSINE, l2sq_f32_4chain(q, row) under L2;
+ * then the stable insertion sort).  The rows [built, rows) are scanned exactly
+ * (exact_knn, k smallest by (score, slot)) and merged: a graph entry first when its score
+ * <= the delta entry's, k kept.  metric: 1 = COSINE, 0 = L2.  out_ids / out_scores
+ * [nq x k] (-1 / +inf past the lists); kg <= 1024, k <= 64. */
+int pion_v_b200_merge_delta(pion_b200_ctx *ctx, const pion_b200_index *index, int64_t built,
+                            int metric, const float *q, int64_t nq, int64_t kg, int32_t *ids,
+                            float *scores, int64_t k, int32_t *out_ids, float *out_scores,
+                            int mem);
+
 /* Binary-quantised FLAT with FP32 rerank: keeps the
  * fp32 rows (normalised like register_flat_f32) and builds 1 sign bit per dimension,
  * bit b of word w = (x[64w + b] > 0) (src/vector/kernels.mojo:1711-1720). */

@@ -430,3 +430,58 @@ def hnsw_brute_force(graph: dict, queries, k: int, rerank=None):
                            sc.ctypes.data_as(_p), found.ctypes.data_as(_p))
     del keep
     return ids, sc, found
+
+
+def merge_delta(rows, built: int, cosine: bool, queries, ids, scores, k: int):
+    """merge_delta (src/commands/vector.mojo:1368-1410) per query, composed from the
+    restated pieces: _exact_rescore (:1413-1456: graph results below `built` rescored from
+    the FP32 rows, 1 - dot_f32_4chain(q^, row) or l2sq_f32_4chain(q, row), then the stable
+    insertion sort), exact_knn over rows [built, len(rows)), and the merge loop (a graph
+    entry first when its score <= the delta entry's, k kept).  ids/scores [nq, kg] with
+    -1 ending a list.  Returns (rescored ids, rescored scores, merged ids [nq, k], merged
+    scores [nq, k]); merged entries past the lists are -1 / +inf."""
+    rows = np.ascontiguousarray(rows, np.float32)
+    queries = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+    nq, kg = ids.shape
+    r_ids = np.array(ids, np.int32, copy=True)
+    r_sc = np.array(scores, np.float32, copy=True)
+    n_rows = rows.shape[0]
+    b = min(built, n_rows)
+    if n_rows > b:
+        d_ids, d_sc = exact_knn(rows[b:], queries, k, cosine=cosine)
+    out_i = np.full((nq, k), -1, np.int32)
+    out_s = np.full((nq, k), np.inf, np.float32)
+    for t in range(nq):
+        q = exact_query_normalize(queries[t], cosine)
+        n = 0
+        while n < kg and r_ids[t, n] >= 0:
+            n += 1
+        li, ls = list(r_ids[t, :n]), list(r_sc[t, :n])
+        for j in range(n):
+            s = li[j]
+            if 0 <= s < b:
+                ls[j] = (np.float32(1.0) - np.float32(dot_f32_4chain(q, rows[s])) if cosine
+                         else np.float32(l2sq_f32_4chain(q, rows[s])))
+        for a in range(1, n):  # insertion sort, strict <
+            j = a
+            while j > 0 and ls[j] < ls[j - 1]:
+                ls[j], ls[j - 1] = ls[j - 1], ls[j]
+                li[j], li[j - 1] = li[j - 1], li[j]
+                j -= 1
+        r_ids[t, :n], r_sc[t, :n] = li, ls
+        dl_i, dl_s = [], []
+        if n_rows > b:
+            for j in range(k):
+                if d_ids[t, j] >= 0 and np.isfinite(d_sc[t, j]):
+                    dl_i.append(int(d_ids[t, j]) + b)
+                    dl_s.append(np.float32(d_sc[t, j]))
+        a = bb = o = 0
+        while o < k and (a < n or bb < len(dl_i)):
+            if bb >= len(dl_i) or (a < n and ls[a] <= dl_s[bb]):
+                out_i[t, o], out_s[t, o] = li[a], ls[a]
+                a += 1
+            else:
+                out_i[t, o], out_s[t, o] = dl_i[bb], dl_s[bb]
+                bb += 1
+            o += 1
+    return r_ids, r_sc, out_i, out_s

@@ -77,6 +77,7 @@ SIGNATURES = {
     "pion_v_b200_hnsw_last_stats": (_I, [_P, _P]),
     "pion_v_b200_hnsw_metric_scores": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_register_index": (_I, [_P, _P, _P]),
+    "pion_v_b200_merge_delta": (_I, [_P, _P, _I64, _I, _P, _I64, _I64, _P, _P, _I64, _P, _P, _I]),
     "pion_v_b200_hnsw_load": (_I, [ctypes.c_char_p, _P]),
     "pion_v_b200_hnsw_save": (_I, [_P, ctypes.c_char_p, _I64]),
     "pion_v_b200_hnsw_beam_batch": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _I]),

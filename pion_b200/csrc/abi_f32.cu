@@ -339,4 +339,116 @@ int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, cons
     return 0;
 }
 
+int pion_v_b200_merge_delta(pion_b200_ctx* ctx, const pion_b200_index* ix, int64_t built,
+                            int metric, const float* q, int64_t nq, int64_t kg, int32_t* ids,
+                            float* scores, int64_t k, int32_t* out_ids, float* out_scores,
+                            int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kFlatF32)
+        return set_error(ctx, PION_B200_EINVAL, "merge_delta: not a FLAT FP32 index of the rows");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "merge_delta: index on another device");
+    if (ix->id_base != 0)
+        return set_error(ctx, PION_B200_EINVAL, "merge_delta: the rows index must start at slot 0");
+    if (nq < 0 || kg < 1 || k < 1 || built < 0 || (metric != 0 && metric != 1) ||
+        (nq > 0 && (!q || !ids || !scores || !out_ids || !out_scores)))
+        return set_error(ctx, PION_B200_EINVAL, "merge_delta: bad arguments");
+    if (kg > delta_kg_max() || k > 64 || nq > (1 << 22))
+        return set_error(ctx, PION_B200_ESHAPE, "merge_delta: kg %lld or k %lld too large",
+                         (long long)kg, (long long)k);
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "merge_delta: bad mem %d", mem);
+    if (nq == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const int dim = (int)ix->dim;
+    const int64_t n_rows = ix->n_rows;
+    const int64_t b = built < n_rows ? built : n_rows;
+    const size_t qb = (size_t)nq * dim * 4, gb = (size_t)nq * kg * 4, ob = (size_t)nq * k * 4;
+    const float* dq = q;
+    int32_t* dgi = ids;
+    float* dgs = scores;
+    int32_t* doi = out_ids;
+    float* dos = out_scores;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, align_up(qb, 256)) != 0 ||
+            ensure(ctx->stage_out, 2 * align_up(gb, 256) + 2 * align_up(ob, 256)) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "merge_delta: staging");
+        char* o = static_cast<char*>(ctx->stage_out.ptr);
+        dq = static_cast<const float*>(ctx->stage_in.ptr);
+        dgi = reinterpret_cast<int32_t*>(o);
+        dgs = reinterpret_cast<float*>(o + align_up(gb, 256));
+        doi = reinterpret_cast<int32_t*>(o + 2 * align_up(gb, 256));
+        dos = reinterpret_cast<float*>(o + 2 * align_up(gb, 256) + align_up(ob, 256));
+        if (cudaMemcpyAsync(const_cast<float*>(dq), q, qb, cudaMemcpyHostToDevice, st) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(dgi, ids, gb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(dgs, scores, gb, cudaMemcpyHostToDevice, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "merge_delta: copy failed");
+    }
+    const int chunks = ff32_exact_chunks();
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align_up(bytes, 256);
+        return o;
+    };
+    const size_t o_q = take(qb), o_qn = take((size_t)nq * 4), o_ng = take((size_t)nq * 4),
+                 o_fl = take((size_t)(nq + 1) * 4),
+                 o_cd = take((size_t)nq * chunks * k * 4), o_ci = take((size_t)nq * chunks * k * 4),
+                 o_dd = take(ob), o_di = take(ob);
+    if (ensure(ctx->scratch, off) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "merge_delta: scratch");
+    char* base = static_cast<char*>(ctx->scratch.ptr);
+    const float* qx = dq;
+    int rc = 0;
+    if (metric == 1) {  // exact_knn / _exact_rescore normalise the query (vector.mojo:1254)
+        rc = launch_query_normalize(dq, (int)nq, dim, reinterpret_cast<float*>(base + o_q),
+                                    reinterpret_cast<float*>(base + o_qn), st);
+        ctx->launches++;
+        qx = reinterpret_cast<const float*>(base + o_q);
+    }
+    int* n_graph = reinterpret_cast<int*>(base + o_ng);
+    int32_t* ddi = reinterpret_cast<int32_t*>(base + o_di);
+    float* dds = reinterpret_cast<float*>(base + o_dd);
+    timing_begin(ctx);
+    if (rc == 0) {
+        rc = launch_delta_rescore(ix->rows_f32, dim, b, metric == 0, qx, (int)nq, (int)kg, dgi,
+                                  dgs, n_graph, st);
+        ctx->launches++;
+    }
+    if (rc == 0) {
+        if (n_rows > b) {  // exact_knn over the rows ingested since the build
+            rc = launch_exact_scan_all(ix->rows_f32 + (size_t)b * dim, n_rows - b, dim, qx,
+                                       (int)nq, (int)k, b, metric == 0,
+                                       reinterpret_cast<int*>(base + o_fl),
+                                       reinterpret_cast<float*>(base + o_cd),
+                                       reinterpret_cast<int32_t*>(base + o_ci), dds, ddi,
+                                       ctx->num_sms, st);
+            ctx->launches += 3;
+        } else {
+            rc = launch_fill_results(dds, ddi, (size_t)nq * k, INFINITY, st);
+            ctx->launches++;
+        }
+    }
+    if (rc == 0) {
+        rc = launch_delta_merge(dgi, dgs, n_graph, (int)kg, ddi, dds, (int)k, (int)nq, (int)k,
+                                doi, dos, st);
+        ctx->launches++;
+    }
+    timing_end(ctx);
+    if (rc != 0)
+        return set_error(ctx, rc, "merge_delta: launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(ids, dgi, gb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(scores, dgs, gb, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_ids, doi, ob, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_scores, dos, ob, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "merge_delta: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
 }  // extern "C"

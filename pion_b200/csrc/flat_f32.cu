@@ -532,6 +532,7 @@ __global__ void __launch_bounds__(256) rescore_certify_kernel(
 constexpr int EX_THREADS = 256;
 constexpr int EX_KMAX = 64;
 
+template <bool L2>
 __global__ void __launch_bounds__(EX_THREADS)
     exact_scan_kernel(const float* __restrict__ rows, int64_t n_rows, int dim,
                       const float* __restrict__ qn, const int* __restrict__ flagged,
@@ -569,7 +570,9 @@ __global__ void __launch_bounds__(EX_THREADS)
             // every half-warp of the warp iterates the same number of times
             const bool valid = r < r1;
             float dd = INFINITY;
-            if (valid) dd = __fsub_rn(1.0f, dot4chain_half(qv, rows + r * dim, dim, hl, hmask));
+            if (valid)
+                dd = L2 ? l2sq4chain_half(qv, rows + r * dim, dim, hl, hmask)
+                        : __fsub_rn(1.0f, dot4chain_half(qv, rows + r * dim, dim, hl, hmask));
             else __syncwarp(hmask);
             if (valid && hl == 0 && better_asc(dd, (int32_t)r, my_d[k - 1], my_i[k - 1])) {
                 int j = k - 1;
@@ -788,13 +791,46 @@ int launch_rescore_certify(const float* rows, int dim, const float* qn, const fl
 
 int ff32_exact_chunks() { return 32; }
 
+namespace ff32 {
+__global__ void iota_kernel(int* flagged, int* n_flagged, int nq) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += gridDim.x * blockDim.x)
+        flagged[i] = i;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *n_flagged = nq;
+}
+}  // namespace ff32
+
+// exact_knn over every row for every query (the exact scan with all queries queued):
+// COSINE 1 - dot_f32_4chain(q^, row) with q^ given, or L2 l2sq_f32_4chain(q, row);
+// [nq x k] ascending by (distance, row + id_base).  `queue` holds nq + 1 ints.
+int launch_exact_scan_all(const float* rows, int64_t n_rows, int dim, const float* q, int nq,
+                          int k, int64_t id_base, int l2, int* queue, float* chunk_d,
+                          int32_t* chunk_i, float* out_d, int32_t* out_i, int num_sms,
+                          cudaStream_t st) {
+    if (nq <= 0) return 0;
+    if (k < 1 || k > ff32::EX_KMAX) return PION_B200_ESHAPE;
+    const int chunks = ff32_exact_chunks();
+    int* flagged = queue + 1;
+    ff32::iota_kernel<<<(nq + 255) / 256 < 1024 ? (nq + 255) / 256 : 1024, 256, 0, st>>>(
+        flagged, queue, nq);
+    if (l2)
+        ff32::exact_scan_kernel<true><<<num_sms * 2, ff32::EX_THREADS, 0, st>>>(
+            rows, n_rows, dim, q, flagged, queue, chunks, k, chunk_d, chunk_i);
+    else
+        ff32::exact_scan_kernel<false><<<num_sms * 2, ff32::EX_THREADS, 0, st>>>(
+            rows, n_rows, dim, q, flagged, queue, chunks, k, chunk_d, chunk_i);
+    if (cudaGetLastError() != cudaSuccess) return PION_B200_ECUDA;
+    ff32::exact_merge_kernel<<<(nq + 3) / 4, 128, 0, st>>>(chunk_d, chunk_i, flagged, queue,
+                                                           chunks, k, id_base, out_d, out_i);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
 int launch_exact_fallback(const float* rows, int64_t n_rows, int dim, const float* qn,
                           const int* flagged, const int* n_flagged, int nq, int k,
                           int64_t id_base, float* chunk_d, int32_t* chunk_i, float* out_d,
                           int32_t* out_i, int num_sms, cudaStream_t st) {
     if (k > ff32::EX_KMAX) return PION_B200_ESHAPE;
     const int chunks = ff32_exact_chunks();
-    ff32::exact_scan_kernel<<<num_sms * 2, ff32::EX_THREADS, 0, st>>>(
+    ff32::exact_scan_kernel<false><<<num_sms * 2, ff32::EX_THREADS, 0, st>>>(
         rows, n_rows, dim, qn, flagged, n_flagged, chunks, k, chunk_d, chunk_i);
     if (cudaGetLastError() != cudaSuccess) return PION_B200_ECUDA;
     ff32::exact_merge_kernel<<<(nq + 3) / 4, 128, 0, st>>>(chunk_d, chunk_i, flagged, n_flagged,

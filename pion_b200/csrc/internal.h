@@ -261,6 +261,18 @@ int launch_flat_i8_scan1(const int8_t* rows, const float* row_scale, int64_t n_r
                          const int8_t* q, const float* q_scale, int k, int ctas, float* cand_val,
                          int32_t* cand_idx, cudaStream_t st);
 
+// ---- delta.cu, and the exact scan of flat_f32.cu for every query
+int delta_kg_max();
+int launch_delta_rescore(const float* rows, int dim, int64_t built, int l2, const float* q, int nq,
+                         int kg, int32_t* ids, float* scores, int* n_graph, cudaStream_t st);
+int launch_delta_merge(const int32_t* gi, const float* gs, const int* n_graph, int kg,
+                       const int32_t* di, const float* ds, int kd, int nq, int k, int32_t* out_i,
+                       float* out_s, cudaStream_t st);
+int launch_exact_scan_all(const float* rows, int64_t n_rows, int dim, const float* q, int nq,
+                          int k, int64_t id_base, int l2, int* queue, float* chunk_d,
+                          int32_t* chunk_i, float* out_d, int32_t* out_i, int num_sms,
+                          cudaStream_t st);
+
 // ---- slot_scan.cu
 int slot_tile_rows();
 int slot_query_tile();

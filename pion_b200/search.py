@@ -249,6 +249,31 @@ class FlatF32Index(_Index):
                                                                  pi, pv, mem))
         return ids, sc
 
+    def merge_delta(self, q, built: int, ids, scores, k: int, cosine: bool = True,
+                    ctx: Context | None = None):
+        """merge_delta (src/commands/vector.mojo:1368-1456) with this index as the FP32
+        ingest rows: ids / scores [nq, kg] (the graph's results, -1 ends a list) are
+        rescored in place; returns the merge with the exact scan of rows [built, n)
+        as (ids int32 [nq, k], scores float32 [nq, k])."""
+        c = ctx or self.ctx
+        pq, mq, kq = _ptr(q, np.float32, "q")
+        if _is_torch(ids):
+            pi, mi = ids.data_ptr(), MEM_DEVICE if ids.is_cuda else MEM_HOST
+            ps, ms = scores.data_ptr(), MEM_DEVICE if scores.is_cuda else MEM_HOST
+        else:
+            for a, nm, dt in ((ids, "ids", np.int32), (scores, "scores", np.float32)):
+                if not (isinstance(a, np.ndarray) and a.dtype == dt and a.flags["C_CONTIGUOUS"]):
+                    raise TypeError(f"{nm} must be a contiguous {np.dtype(dt)} array "
+                                    "(updated in place)")
+            pi, mi, ps, ms = ids.ctypes.data, MEM_HOST, scores.ctypes.data, MEM_HOST
+        m = _same_mem(mq, mi, ms)
+        nq, kg = ids.shape
+        oi, osc, poi, pos = _outputs(m == MEM_DEVICE, nq, k, q.device if m == MEM_DEVICE else None)
+        with _TorchStream(c, m):
+            c.check(c.lib.pion_v_b200_merge_delta(c.h, self.h, built, 1 if cosine else 0, pq, nq,
+                                                   kg, pi, ps, k, poi, pos, m))
+        return oi, osc
+
 
 class BQIndex(_Index):
     """Sign-bit codes + fp32 rows: Hamming shortlist, exact cosine rerank."""

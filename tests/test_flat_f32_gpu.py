@@ -115,3 +115,35 @@ def test_device_tensors_and_empty_index(ctx, oracle):
     empty = pion_b200.FlatF32Index(ctx, np.zeros((0, 64), np.float32))
     ids, d = empty.search(np.ones((2, 64), np.float32), 3)
     assert (ids == -1).all() and np.isposinf(d).all()
+
+
+@pytest.mark.parametrize("cosine", [True, False])
+def test_merge_delta_matches_oracle(ctx, oracle, cosine):
+    """merge_delta (src/commands/vector.mojo:1368-1456): the graph's results rescored
+    exactly from the FP32 rows and merged with the exact scan of the rows ingested since
+    the build, identical to the restated composition."""
+    import pion_b200
+    n, built, nq, kg, k = 6000, 4500, 40, 16, 10
+    rows, qs = mixture_np(n, 1536, 32, seed=21, n_queries=nq)
+    if not cosine:
+        rows = rows * 3.0
+        qs = qs * 3.0
+    stored = oracle.l2_normalize_rows(rows) if cosine else rows
+    ix = pion_b200.FlatF32Index(ctx, rows, normalize=cosine)
+    rng = np.random.Generator(np.random.PCG64(6))
+    ids = np.full((nq, kg), -1, np.int32)
+    for t in range(nq):  # a graph answer: slots below built, some lists short
+        m = kg if t % 4 else kg // 2
+        ids[t, :m] = rng.choice(built, m, replace=False)
+    scores = rng.random((nq, kg)).astype(np.float32)
+    ids[3, 2] = built + 7                 # a slot past the graph keeps its score
+    want = oracle.merge_delta(stored, built, cosine, qs, ids, scores, k)
+    gi, gs = ids.copy(), scores.copy()
+    oi, osc = ix.merge_delta(qs, built, gi, gs, k, cosine=cosine)
+    assert np.array_equal(gi, want[0]) and np.array_equal(gs.view(np.uint32), want[1].view(np.uint32))
+    assert np.array_equal(oi, want[2])
+    assert np.array_equal(osc.view(np.uint32), want[3].view(np.uint32))
+    # nothing ingested since the build: the rescored graph list alone
+    oi2, os2 = ix.merge_delta(qs, n, ids.copy(), scores.copy(), k, cosine=cosine)
+    w2 = oracle.merge_delta(stored, n, cosine, qs, ids, scores, k)
+    assert np.array_equal(oi2, w2[2]) and np.array_equal(os2, w2[3])
