@@ -485,3 +485,170 @@ def merge_delta(rows, built: int, cosine: bool, queries, ids, scores, k: int):
                 bb += 1
             o += 1
     return r_ids, r_sc, out_i, out_s
+
+
+# --------------------------------------------------------------------------
+# Block-quantised HNSW (oracle/quant_oracle.c)
+# --------------------------------------------------------------------------
+
+QUANT_KINDS = {"polar": 0, "nano": 1, "turbo": 2}
+
+
+class _QuantLayout(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("metric", ctypes.c_int32),
+                ("num_nodes", ctypes.c_int64), ("M", ctypes.c_int64),
+                ("entry_point", ctypes.c_int64), ("max_level", ctypes.c_int64),
+                ("compact", _p), ("stride", ctypes.c_int64),
+                ("l0_compact", _p), ("l0_slots", _p), ("node_slot", _p), ("node_ids", _p),
+                ("deleted", _p), ("node_level", _p), ("upper_offset", _p),
+                ("upper_links", _p), ("qjl", _p), ("qjl_res_norms", _p),
+                ("qjl_random_signs", _p), ("qjl_lambda", ctypes.c_float), ("rerank", _p)]
+
+
+def _qlib():
+    L = lib()
+    if not getattr(L, "_quant_bound", False):
+        L.orc_f32_to_f16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_f16.restype = ctypes.c_uint16
+        L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.orc_f16_to_f32.restype = ctypes.c_float
+        L.orc_quant_stride.argtypes = [ctypes.c_int]
+        L.orc_quant_stride.restype = _i64
+        L.orc_quant_block.argtypes = [ctypes.c_int, _p, _p]
+        L.orc_quant_dot.argtypes = [ctypes.c_int, _p, _p, _p]
+        L.orc_quant_dot.restype = ctypes.c_float
+        L.orc_query_block_int8.argtypes = [_p, _p, _p]
+        L.orc_query_block_int8.restype = ctypes.c_float
+        L.orc_qjl_random_signs.argtypes = [_p]
+        L.orc_qjl_signs.argtypes = [_p, _p, _p]
+        L.orc_qjl_signs.restype = ctypes.c_float
+        L.orc_turbo_qjl_row.argtypes = [_p, _p, _p, _p]
+        L.orc_turbo_qjl_row.restype = ctypes.c_float
+        L.orc_quant_search.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p, _p, ctypes.c_int]
+        L.orc_quant_search.restype = ctypes.c_int
+        L._quant_bound = True
+    return L
+
+
+def f32_to_f16_bits(x):
+    L = _qlib()
+    return np.array([L.orc_f32_to_f16(float(v)) for v in np.ravel(x)], np.uint16)
+
+
+def quant_block(kind: str, x) -> np.ndarray:
+    """One vector's block slot (quantize_fp32_to_block_int4 / _int3 / _int2)."""
+    L = _qlib()
+    k = QUANT_KINDS[kind]
+    x, px = _c(x, np.float32)
+    out = np.zeros(L.orc_quant_stride(k), np.int8)
+    L.orc_quant_block(k, px, out.ctypes.data_as(_p))
+    return out
+
+
+def quant_dot(kind: str, qcodes, qscales, slot) -> float:
+    L = _qlib()
+    a, pa = _c(qcodes, np.int8)
+    b, pb = _c(qscales, np.float32)
+    c, pc = _c(slot, np.int8)
+    return L.orc_quant_dot(QUANT_KINDS[kind], pa, pb, pc)
+
+
+def query_block_int8(q):
+    """quantize_fp32_to_block_int8 -> (codes int8 [1536], scales f32 [48], recon |q|^2)."""
+    L = _qlib()
+    q, pq = _c(q, np.float32)
+    codes = np.empty(1536, np.int8)
+    scales = np.empty(48, np.float32)
+    n = L.orc_query_block_int8(pq, codes.ctypes.data_as(_p), scales.ctypes.data_as(_p))
+    return codes, scales, np.float32(n)
+
+
+def qjl_random_signs() -> np.ndarray:
+    out = np.empty(24, np.uint64)
+    _qlib().orc_qjl_random_signs(out.ctypes.data_as(_p))
+    return out
+
+
+def qjl_signs(residual, signs):
+    L = _qlib()
+    r, pr = _c(residual, np.float32)
+    s, ps = _c(signs, np.uint64)
+    out = np.empty(24, np.uint64)
+    n = L.orc_qjl_signs(pr, ps, out.ctypes.data_as(_p))
+    return out, np.float32(n)
+
+
+def quant_graph(graph: dict, rows, kind: str, rerank: bool = True):
+    """The block-quant compact buffer of `graph` (slot order of its node_slot), the QJL rows
+    by node (TurboQuant) and the FP32 rerank rows by node, from the rows the graph was built
+    from (normalised first under COSINE)."""
+    rows = np.ascontiguousarray(rows, np.float32)
+    if graph["metric"] == 1:
+        rows = l2_normalize_rows(rows)
+    n = graph["num_nodes"]
+    k = QUANT_KINDS[kind]
+    L = _qlib()
+    stride = L.orc_quant_stride(k)
+    comp = np.zeros((n, stride), np.int8)
+    slot = graph["node_slot"].astype(np.int64)
+    for i in range(n):
+        L.orc_quant_block(k, rows[i].ctypes.data_as(_p), comp[slot[i]].ctypes.data_as(_p))
+    out = {"kind": kind, "compact": comp.reshape(-1), "stride": stride,
+           "rerank": rows if rerank else None}
+    if kind == "turbo":
+        rs = qjl_random_signs()
+        qjl = np.zeros((n, 24), np.uint64)
+        norms = np.zeros(n, np.float32)
+        for i in range(n):
+            norms[i] = L.orc_turbo_qjl_row(rows[i].ctypes.data_as(_p),
+                                           comp[slot[i]].ctypes.data_as(_p),
+                                           rs.ctypes.data_as(_p), qjl[i].ctypes.data_as(_p))
+        out.update(qjl=qjl, qjl_res_norms=norms, qjl_random_signs=rs, qjl_lambda=1.0)
+    return out
+
+
+def quant_search(graph: dict, quant: dict, queries, k: int, ef: int, nthreads: int | None = None):
+    """search_fp32_scored's block-quant branch (src/vector/hnsw.mojo:4136-4330) with the
+    shared FP32 rerank tail -> (external ids [nq, k], scores [nq, k], counts [nq])."""
+    L = _qlib()
+    keep = []
+
+    def ptr(a, dt):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dtype=dt)
+        keep.append(a)
+        return a.ctypes.data_as(_p)
+
+    lay = _QuantLayout()
+    lay.kind = QUANT_KINDS[quant["kind"]]
+    lay.metric = graph["metric"]
+    lay.num_nodes, lay.M = graph["num_nodes"], graph["M"]
+    lay.entry_point, lay.max_level = graph["entry_point"], graph["max_level"]
+    lay.compact = ptr(quant["compact"], np.int8)
+    lay.stride = quant["stride"]
+    lay.l0_compact = ptr(graph["l0_compact"], np.uint32)
+    lay.l0_slots = ptr(graph["l0_slots"], np.uint32)
+    lay.node_slot = ptr(graph["node_slot"], np.uint32)
+    lay.node_ids = ptr(graph["node_ids"], np.int32)
+    lay.deleted = ptr(graph.get("deleted"), np.uint8)
+    lay.node_level = ptr(graph["node_level"], np.int8)
+    lay.upper_offset = ptr(graph["upper_offset"], np.int64)
+    lay.upper_links = ptr(graph["upper_links"], np.uint32)
+    lay.qjl = ptr(quant.get("qjl"), np.uint64)
+    lay.qjl_res_norms = ptr(quant.get("qjl_res_norms"), np.float32)
+    lay.qjl_random_signs = ptr(quant.get("qjl_random_signs"), np.uint64)
+    lay.qjl_lambda = quant.get("qjl_lambda", 1.0)
+    lay.rerank = ptr(quant.get("rerank"), np.float32)
+    q, pq = _c(np.atleast_2d(queries), np.float32)
+    nq = q.shape[0]
+    ids = np.empty((nq, k), np.int32)
+    sc = np.empty((nq, k), np.float32)
+    cnt = np.empty(nq, np.int64)
+    rc = L.orc_quant_search(ctypes.byref(lay), pq, nq, k, ef, ids.ctypes.data_as(_p),
+                            sc.ctypes.data_as(_p), cnt.ctypes.data_as(_p),
+                            nthreads or default_threads())
+    if rc != 0:
+        raise RuntimeError("orc_quant_search failed")
+    del keep
+    return ids, sc, cnt

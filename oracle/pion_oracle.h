@@ -125,7 +125,46 @@ void orc_parallel_for(int64_t n, int nthreads, size_t scratch_bytes, orc_item_fn
 int64_t orc_shard_merge_asc(const int64_t *ids, const float *scores, int64_t n_all, int64_t k,
                             int64_t *out_ids, float *out_scores);
 
+/* ----------------------------------------------- block-quantised HNSW (quant_oracle.c) */
+#define ORC_QUANT_POLAR 0 /* INT4, stride 868 */
+#define ORC_QUANT_NANO 1  /* INT2, stride 484 */
+#define ORC_QUANT_TURBO 2 /* INT3 + QJL, stride 676 */
+
+typedef struct orc_quant_layout {
+    int32_t kind, metric;
+    int64_t num_nodes, M, entry_point, max_level;
+    const int8_t *compact; /* num_nodes x stride, slot order, header 0 */
+    int64_t stride;
+    const uint32_t *l0_compact, *l0_slots, *node_slot;
+    const int32_t *node_ids;
+    const uint8_t *deleted;
+    const int8_t *node_level;
+    const int64_t *upper_offset;
+    const uint32_t *upper_links; /* rows of (1 + M) */
+    const uint64_t *qjl;         /* num_nodes x 24, by node (TurboQuant) */
+    const float *qjl_res_norms;  /* by node */
+    const uint64_t *qjl_random_signs; /* 24 words */
+    float qjl_lambda;
+    const float *rerank;         /* num_nodes x 1536 FP32 rows by node, or NULL */
+} orc_quant_layout;
+
+uint16_t orc_f32_to_f16(float f);
+float orc_f16_to_f32(uint16_t h);
+int64_t orc_quant_stride(int kind);
+void orc_quant_block(int kind, const float *src, int8_t *dst);
+float orc_quant_dot(int kind, const int8_t *qc, const float *qs, const int8_t *v);
+float orc_query_block_int8(const float *q, int8_t *codes, float *scales);
+void orc_qjl_random_signs(uint64_t *out24);
+float orc_qjl_signs(const float *residual, const uint64_t *rs, uint64_t *dst24);
+float orc_turbo_qjl_row(const float *src, const int8_t *slot, const uint64_t *rs, uint64_t *dst24);
+/* search_fp32_scored's block-quant branch per query: ids (external) / scores [nq x k],
+ * out_n [nq] results per query.  0, or -1 on allocation failure. */
+int orc_quant_search(const orc_quant_layout *L, const float *queries, int64_t nq, int64_t k,
+                     int64_t ef, int32_t *out_ids, float *out_scores, int64_t *out_n,
+                     int nthreads);
+
 #ifdef __cplusplus
 }
 #endif
+
 #endif
