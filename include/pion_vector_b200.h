@@ -193,6 +193,7 @@ int pion_v_b200_timing_read(pion_b200_ctx *ctx, double *total_ms, int64_t *count
 #define PION_B200_KIND_FLAT_F32 2 /* rows fp32 [n x dim]: register_flat_f32 */
 #define PION_B200_KIND_BQ 3       /* rows fp32 [n x dim]: register_bq */
 #define PION_B200_KIND_HNSW 4     /* hnsw layout: register_hnsw */
+#define PION_B200_KIND_HNSW_QUANT 5 /* hnsw + hnsw_quant layouts: register_hnsw_quant */
 
 typedef struct pion_b200_index_desc {
     int32_t kind;            /* PION_B200_KIND_* */
@@ -202,7 +203,8 @@ typedef struct pion_b200_index_desc {
     int32_t reserved;
     const void *rows;
     const float *row_scale;  /* FLAT_I8 */
-    const struct pion_b200_hnsw_layout *hnsw; /* HNSW */
+    const struct pion_b200_hnsw_layout *hnsw; /* HNSW, HNSW_QUANT */
+    const struct pion_b200_hnsw_quant_layout *quant; /* HNSW_QUANT */
 } pion_b200_index_desc;
 
 /* One registration entry point for every index kind: dispatches on desc->kind to the
@@ -465,9 +467,74 @@ int pion_v_b200_hnsw_brute_force(pion_b200_ctx *ctx, const pion_b200_index *inde
                                  const float *q, int64_t nq, int64_t k, int32_t *out_ids,
                                  float *out_scores, int32_t *out_found, int mem);
 
+/* ------------------------------------------------ block-quantised HNSW -- */
+/* The reference's three block-quantised compact formats of an HNSW graph at dim 1536
+ * (compact_vectors, src/vector/hnsw.mojo:2761-2990 and 3138-3230): per slot an f32
+ * reconstructed |v|^2 then 48 blocks of 32 dims, each an f16 scale and the packed codes.
+ *   POLAR  PolarQuant INT4 (quantize_fp32_to_block_int4, kernels.mojo:1116-1175), stride 868
+ *   NANO   NanoQuant INT2 (quantize_fp32_to_block_int2, kernels.mojo:1776-1842), stride 484
+ *   TURBO  TurboQuant INT3 (quantize_fp32_to_block_int3, kernels.mojo:1589-1651), stride 676,
+ *          plus per node 24 QJL sign words of the residual (qjl_compute_signs,
+ *          kernels.mojo:1685-1714, random signs from an LCG seeded 42, hnsw.mojo:497-509)
+ *          and the residual's squared norm. */
+#define PION_B200_QUANT_POLAR 0
+#define PION_B200_QUANT_NANO 1
+#define PION_B200_QUANT_TURBO 2
+
+typedef struct pion_b200_hnsw_quant_layout {
+    int32_t kind;                      /* PION_B200_QUANT_*                          */
+    int32_t reserved;
+    int64_t num_nodes;
+    const int8_t *compact;             /* num_nodes x stride, by slot (the graph's
+                                          node_slot order)                           */
+    int64_t stride;                    /* 868 / 484 / 676                            */
+    const uint64_t *qjl;               /* TURBO: num_nodes x 24 words by node, or NULL */
+    const float *qjl_res_norms;        /* TURBO: num_nodes by node, or NULL          */
+    const uint64_t *qjl_random_signs;  /* TURBO: 24 words, or NULL                   */
+    float qjl_lambda;                  /* 1.0                                        */
+    int32_t reserved2;
+    const float *rerank;               /* num_nodes x 1536 FP32 rows by node (normalised
+                                          under COSINE), or NULL: no rerank         */
+} pion_b200_hnsw_quant_layout;
+
+typedef struct pion_b200_hnsw_quant pion_b200_hnsw_quant;
+
+/* Quantises the rows a graph was built from (fp32 [n_rows x 1536] in HOST memory, node
+ * order, n_rows = the graph's node count; normalised first under COSINE) into `kind`'s
+ * compact buffer in the graph's slot order, with TurboQuant's QJL rows, and keeps the
+ * (normalised) rows as the rerank buffer.  Float steps in the reference's order, f16
+ * scales rounded to nearest even. */
+int pion_v_b200_hnsw_quantize(const pion_b200_hnsw_graph *graph, const float *rows,
+                              int64_t n_rows, int kind, pion_b200_hnsw_quant **out_quant);
+/* The buffers (host memory owned by the quant object). */
+int pion_v_b200_hnsw_quant_layout(const pion_b200_hnsw_quant *quant,
+                                  pion_b200_hnsw_quant_layout *out_layout);
+int pion_v_b200_hnsw_quant_free(pion_b200_hnsw_quant *quant);
+
+/* Copies a graph (its compact_buffer is not used) and its block-quantised slots (every
+ * pointer in HOST memory) to the GPU.  Checks the graph as register_hnsw does and the
+ * quant layout's kind, stride and sizes. */
+int pion_v_b200_register_hnsw_quant(pion_b200_ctx *ctx, const pion_b200_hnsw_layout *graph,
+                                    const pion_b200_hnsw_quant_layout *quant,
+                                    pion_b200_index **out_index);
+
+/* Batched block-quant HNSW search: search_fp32_scored's block-quant branches
+ * (src/vector/hnsw.mojo:4136-4330) per query: normalise (COSINE), block-quantise to int8,
+ * (TURBO) the query's QJL signs, the upper-level greedy with the block distance, the
+ * level-0 beam quant_beam_search_1536_ref (src/vector/reference/quant_beams_1536.mojo:
+ * 20-81) over MinHeap / MaxHeap (src/common/heap.mojo:48-120, 237-339), then
+ * _rerank_fp32_sorted (hnsw.mojo:4052-4134): the ef results reranked by the FP32 rows
+ * (when registered), stably sorted, the first k.  q fp32[nq x 1536]; out_ids /
+ * out_scores [nq x k] (-1 / +inf past out_found[t]); out_found [nq].  ef in [1, 1024]. */
+int pion_v_b200_hnsw_quant_search(pion_b200_ctx *ctx, const pion_b200_index *index,
+                                  const float *q, int64_t nq, int64_t k, int64_t ef,
+                                  int32_t *out_ids, float *out_scores, int32_t *out_found,
+                                  int mem);
+
 /* Work counters of the context's last pion_v_b200_hnsw_search (waits for it):
  * out3 = {level-0 distance evaluations, level-0 expansions, upper-level distance
- * evaluations}, summed over the batch. */
+ * evaluations}, summed over the batch.  After pion_v_b200_hnsw_quant_search: {distance
+ * evaluations, level-0 expansions, queries re-run with a larger candidate heap}. */
 int pion_v_b200_hnsw_last_stats(pion_b200_ctx *ctx, int64_t *out3);
 
 #ifdef __cplusplus

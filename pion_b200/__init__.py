@@ -13,11 +13,13 @@ from .search import (  # noqa: F401
     FlatI8Index,
     HNSWGraph,
     HNSWIndex,
+    HNSWQuant,
+    HNSWQuantIndex,
     l2_normalize_rows,
     merge_topk,
     quantize_rows_i8,
 )
 
 __all__ = ["Context", "FlatI8Index", "FlatF32Index", "BQIndex", "HNSWGraph", "HNSWIndex",
-           "quantize_rows_i8",
+           "HNSWQuant", "HNSWQuantIndex", "quantize_rows_i8",
            "l2_normalize_rows", "merge_topk", "PionError", "load"]

@@ -87,6 +87,11 @@ SIGNATURES = {
     "pion_v_b200_hnsw_brute_force": (_I, [_P, _P, _P, _I64, _I64, _P, _P, _P, _I]),
     "pion_v_beam_1536": (_I64, [_P]),
     "pion_v_quant_beam_1536": (_I64, [_P]),
+    "pion_v_b200_hnsw_quantize": (_I, [_P, _P, _I64, _I, _PP]),
+    "pion_v_b200_hnsw_quant_layout": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_quant_free": (_I, [_P]),
+    "pion_v_b200_register_hnsw_quant": (_I, [_P, _P, _P, _PP]),
+    "pion_v_b200_hnsw_quant_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I]),
     "pion_v_b200_beam_forget": (_I, [_P]),
 }
 
@@ -97,7 +102,17 @@ class IndexDesc(ctypes.Structure):
                 ("dim", ctypes.c_int64), ("id_base", ctypes.c_int64),
                 ("normalize", ctypes.c_int32), ("reserved", ctypes.c_int32),
                 ("rows", ctypes.c_void_p), ("row_scale", ctypes.c_void_p),
-                ("hnsw", ctypes.c_void_p)]
+                ("hnsw", ctypes.c_void_p), ("quant", ctypes.c_void_p)]
+
+
+class HnswQuantLayout(ctypes.Structure):
+    """pion_b200_hnsw_quant_layout (include/pion_vector_b200.h)."""
+    _fields_ = [("kind", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("num_nodes", ctypes.c_int64), ("compact", ctypes.c_void_p),
+                ("stride", ctypes.c_int64), ("qjl", ctypes.c_void_p),
+                ("qjl_res_norms", ctypes.c_void_p), ("qjl_random_signs", ctypes.c_void_p),
+                ("qjl_lambda", ctypes.c_float), ("reserved2", ctypes.c_int32),
+                ("rerank", ctypes.c_void_p)]
 
 
 class LinearPool(ctypes.Structure):

@@ -288,6 +288,8 @@ int pion_v_b200_register_index(pion_b200_ctx* ctx, const pion_b200_index_desc* d
                                            d->dim, d->id_base, d->normalize, d->mem, out_index);
         case PION_B200_KIND_HNSW:
             return pion_v_b200_register_hnsw(ctx, d->hnsw, out_index);
+        case PION_B200_KIND_HNSW_QUANT:
+            return pion_v_b200_register_hnsw_quant(ctx, d->hnsw, d->quant, out_index);
         default:
             *out_index = nullptr;
             return set_error(ctx, PION_B200_EINVAL, "register_index: unknown kind %d", d->kind);
@@ -314,7 +316,9 @@ int pion_v_b200_index_free(pion_b200_index* index) {
                   index->hnsw.node_slot,  index->hnsw.node_ids,     index->hnsw.deleted,
                   index->hnsw.node_level, index->hnsw.upper_offset, index->hnsw.upper_links,
                   index->hnsw.upper_slots, index->hnsw.ext_to_node,
-                  index->hnsw.slot_ext,   index->hnsw.rerank,       index->hnsw.chunk_vmin};
+                  index->hnsw.slot_ext,   index->hnsw.rerank,       index->hnsw.chunk_vmin,
+                  index->hnsw.qcodes,     index->hnsw.qscales,      index->hnsw.qjl,
+                  index->hnsw.qjl_res,    index->hnsw.qjl_rs,       index->hnsw.rerank_node};
     for (void* p : hn)
         if (p) cudaFree(p);
     delete index;

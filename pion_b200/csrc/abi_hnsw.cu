@@ -14,11 +14,6 @@
 #include "hnsw_host.h"
 #include "internal.h"
 
-struct pion_b200_hnsw_graph {
-    pion::hnsw::Graph g;
-    pion::hnsw::BuildStats stats;
-};
-
 using namespace pion;
 
 namespace {

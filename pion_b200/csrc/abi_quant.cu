@@ -1,0 +1,369 @@
+// C-ABI of the block-quantised HNSW search: the host quantiser (hnsw_quant.cpp), device
+// registration of a graph with its PolarQuant / NanoQuant / TurboQuant slots, and the
+// batched search (quant.cu).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "hnsw_host.h"
+#include "internal.h"
+
+using namespace pion;
+
+namespace {
+
+constexpr int kDim = 1536;
+constexpr int kBlocks = 48;
+
+template <typename T>
+int upload(T** dst, const T* src, size_t count) {
+    *dst = nullptr;
+    if (count == 0) return 0;
+    if (cudaMalloc(reinterpret_cast<void**>(dst), count * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        *dst = nullptr;
+        return PION_B200_ENOMEM;
+    }
+    if (cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess)
+        return PION_B200_ECUDA;
+    return 0;
+}
+
+int64_t stride_of(int kind) { return hnsw::quant_stride(kind); }
+int block_bytes(int kind) { return kind == kQPolar ? 18 : kind == kQNano ? 10 : 14; }
+int code_bytes(int kind) { return kind == kQPolar ? 768 : kind == kQNano ? 384 : 576; }
+
+// The graph checks the search relies on (the INT8 compact buffer is not used).
+const char* check_graph(const pion_b200_hnsw_layout* L) {
+    const int64_t n = L->num_nodes;
+    if (n < 0 || n >= (int64_t)0x7fffffff) return "num_nodes out of range";
+    if (L->dim != kDim) return "dim must be 1536";
+    if (L->M < 1 || 2 * L->M > 32) return "M must be in [1, 16]";
+    if (L->metric != 0 && L->metric != 1) return "metric must be 0 (L2) or 1 (COSINE)";
+    if (n == 0) return nullptr;
+    if (!L->l0_compact || !L->l0_slots || !L->node_slot || !L->node_ids || !L->node_level ||
+        !L->upper_offset)
+        return "null layout buffer";
+    if (L->entry_point < 0 || L->entry_point >= n) return "entry_point out of range";
+    if (L->max_level < 0 || L->max_level > 64) return "max_level out of range";
+    if (L->upper_rows < 0 || (L->upper_rows > 0 && !L->upper_links)) return "bad upper_links";
+    for (int64_t i = 0; i < n; ++i) {
+        if (L->node_slot[i] >= (uint64_t)n) return "node_slot out of range";
+        const int64_t off = L->upper_offset[i];
+        const int lv = L->node_level[i];
+        if (lv < 0) return "negative node_level";
+        if (lv > 0 && (off < 0 || off + lv > L->upper_rows)) return "upper_offset out of range";
+        const uint32_t* row = L->l0_compact + i * 33;
+        const uint32_t* srow = L->l0_slots + i * 33;
+        if (row[0] > (uint32_t)(2 * L->M)) return "level-0 count above 2M";
+        for (uint32_t k = 0; k < row[0]; ++k)
+            if (row[1 + k] < (uint32_t)n && srow[1 + k] != 0xffffffffu &&
+                srow[1 + k] >= (uint32_t)n)
+                return "l0_slots entry out of range";
+    }
+    return nullptr;
+}
+
+const char* check_quant(const pion_b200_hnsw_quant_layout* Q, int64_t n) {
+    if (Q->kind < kQPolar || Q->kind > kQTurbo) return "unknown quant kind";
+    if (Q->num_nodes != n) return "quant num_nodes differs from the graph's";
+    if (Q->stride != stride_of(Q->kind)) return "stride does not match the kind";
+    if (n > 0 && !Q->compact) return "null compact buffer";
+    if (Q->kind == kQTurbo && (!Q->qjl) != (!Q->qjl_res_norms))
+        return "qjl and qjl_res_norms go together";
+    if (!std::isfinite(Q->qjl_lambda)) return "qjl_lambda not finite";
+    return nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pion_v_b200_hnsw_quantize(const pion_b200_hnsw_graph* graph, const float* rows,
+                              int64_t n_rows, int kind, pion_b200_hnsw_quant** out_quant) {
+    if (!graph || !out_quant) return PION_B200_EINVAL;
+    *out_quant = nullptr;
+    if (n_rows != graph->g.n || (n_rows > 0 && !rows)) {
+        fprintf(stderr, "pion_vector_b200: hnsw_quantize: rows must be the graph's %lld rows\n",
+                (long long)graph->g.n);
+        return PION_B200_EINVAL;
+    }
+    pion_b200_hnsw_quant* q = new (std::nothrow) pion_b200_hnsw_quant();
+    if (!q) return PION_B200_ENOMEM;
+    std::string why;
+    int rc = 0;
+    try {
+        rc = hnsw::quantize(graph->g, rows, kind, q->q, why);
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+        why = "out of host memory";
+    }
+    if (rc != 0) {
+        fprintf(stderr, "pion_vector_b200: hnsw_quantize: %s\n", why.c_str());
+        delete q;
+        return rc;
+    }
+    q->n = graph->g.n;
+    *out_quant = q;
+    return 0;
+}
+
+int pion_v_b200_hnsw_quant_layout(const pion_b200_hnsw_quant* quant,
+                                  pion_b200_hnsw_quant_layout* out) {
+    if (!quant || !out) return PION_B200_EINVAL;
+    const hnsw::QuantBuffers& b = quant->q;
+    *out = pion_b200_hnsw_quant_layout{};
+    out->kind = b.kind;
+    out->num_nodes = quant->n;
+    out->compact = b.compact.data();
+    out->stride = b.stride;
+    out->qjl = b.qjl.empty() ? nullptr : b.qjl.data();
+    out->qjl_res_norms = b.qjl_res_norms.empty() ? nullptr : b.qjl_res_norms.data();
+    out->qjl_random_signs = b.random_signs.empty() ? nullptr : b.random_signs.data();
+    out->qjl_lambda = 1.0f;
+    out->rerank = b.rerank.empty() ? nullptr : b.rerank.data();
+    return 0;
+}
+
+int pion_v_b200_hnsw_quant_free(pion_b200_hnsw_quant* quant) {
+    if (!quant) return PION_B200_EINVAL;
+    delete quant;
+    return 0;
+}
+
+int pion_v_b200_register_hnsw_quant(pion_b200_ctx* ctx, const pion_b200_hnsw_layout* L,
+                                    const pion_b200_hnsw_quant_layout* Q,
+                                    pion_b200_index** out_index) {
+    if (!valid_ctx(ctx) || !out_index || !L || !Q) return PION_B200_EINVAL;
+    *out_index = nullptr;
+    if (const char* why = check_graph(L))
+        return set_error(ctx, PION_B200_EINVAL, "register_hnsw_quant: %s", why);
+    if (const char* why = check_quant(Q, L->num_nodes))
+        return set_error(ctx, PION_B200_EINVAL, "register_hnsw_quant: %s", why);
+    if (int rc = use_device(ctx)) return rc;
+    pion_b200_index* ix = new (std::nothrow) pion_b200_index();
+    if (!ix) return set_error(ctx, PION_B200_ENOMEM, "register_hnsw_quant: out of host memory");
+    ix->kind = kHNSWQuant;
+    ix->device = ctx->device;
+    ix->n_rows = L->num_nodes;
+    ix->dim = L->dim;
+    auto& h = ix->hnsw;
+    h.M = (int)L->M;
+    h.max_level = (int)L->max_level;
+    h.entry = L->entry_point;
+    h.metric = L->metric;
+    h.quant_kind = Q->kind;
+    h.code_bytes = code_bytes(Q->kind);
+    h.qjl_lambda = Q->qjl_lambda;
+    const size_t n = (size_t)L->num_nodes;
+    int rc = 0;
+    try {
+        if (n > 0) {
+            // slots re-laid out as |v|^2, the 48 f16 scales and the packed codes, each
+            // array 16-byte aligned per slot
+            const int bb = block_bytes(Q->kind), cb = bb - 2;
+            std::vector<float> norms(n);
+            std::vector<uint16_t> scales(n * kBlocks);
+            std::vector<uint8_t> codes(n * (size_t)h.code_bytes);
+            for (size_t s = 0; s < n; ++s) {
+                const int8_t* src = Q->compact + s * (size_t)Q->stride;
+                std::memcpy(&norms[s], src, 4);
+                for (int b = 0; b < kBlocks; ++b) {
+                    std::memcpy(&scales[s * kBlocks + b], src + 4 + b * bb, 2);
+                    std::memcpy(&codes[s * h.code_bytes + (size_t)b * cb], src + 4 + b * bb + 2,
+                                (size_t)cb);
+                }
+            }
+            rc = upload(&h.norms, norms.data(), n);
+            if (!rc) rc = upload(&h.qscales, scales.data(), scales.size());
+            if (!rc) rc = upload(&h.qcodes, codes.data(), codes.size());
+            if (!rc) rc = upload(&h.l0_compact, L->l0_compact, n * 33);
+            if (!rc) rc = upload(&h.l0_slots, L->l0_slots, n * 33);
+            if (!rc) rc = upload(&h.node_slot, L->node_slot, n);
+            if (!rc) rc = upload(&h.node_ids, L->node_ids, n);
+            if (!rc) rc = upload(&h.node_level, L->node_level, n);
+            if (!rc) rc = upload(&h.upper_offset, L->upper_offset, n);
+            if (!rc && L->upper_rows > 0)
+                rc = upload(&h.upper_links, L->upper_links, (size_t)L->upper_rows * (1 + L->M));
+            if (!rc && L->deleted) rc = upload(&h.deleted, L->deleted, (n + 7) / 8);
+            if (!rc && Q->kind == kQTurbo && Q->qjl) {
+                rc = upload(&h.qjl, Q->qjl, n * 24);
+                if (!rc) rc = upload(&h.qjl_res, Q->qjl_res_norms, n);
+            }
+            if (!rc && Q->kind == kQTurbo && Q->qjl_random_signs)
+                rc = upload(&h.qjl_rs, Q->qjl_random_signs, 24);
+            if (!rc && Q->rerank) rc = upload(&h.rerank_node, Q->rerank, n * kDim);
+        }
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+    }
+    if (rc) {
+        pion_v_b200_index_free(ix);
+        return set_error(ctx, rc, "register_hnsw_quant: device copy failed");
+    }
+    *out_index = ix;
+    return 0;
+}
+
+int pion_v_b200_hnsw_quant_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const float* q,
+                                  int64_t nq, int64_t k, int64_t ef, int32_t* out_ids,
+                                  float* out_scores, int32_t* out_found, int mem) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kHNSWQuant)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_quant_search: not a quantised HNSW index");
+    if (ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_quant_search: index on another device");
+    if (nq < 0 || k < 1 || (nq > 0 && (!q || !out_ids || !out_scores || !out_found)))
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_quant_search: bad arguments");
+    if (ef < 1 || ef > quant_top_entries())
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_quant_search: ef %lld not in [1, %d]",
+                         (long long)ef, quant_top_entries());
+    if (nq > (1 << 24) || k > (1 << 16))
+        return set_error(ctx, PION_B200_ESHAPE, "hnsw_quant_search: batch or k too large");
+    if (mem != PION_B200_MEM_HOST && mem != PION_B200_MEM_DEVICE)
+        return set_error(ctx, PION_B200_EINVAL, "hnsw_quant_search: bad mem %d", mem);
+    if (nq == 0) return 0;
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const auto& h = ix->hnsw;
+    const size_t out_bytes = (size_t)nq * k * 4, found_bytes = (size_t)nq * 4;
+    const float* dq = q;
+    int32_t* di = out_ids;
+    float* dv = out_scores;
+    int32_t* df = out_found;
+    if (mem == PION_B200_MEM_HOST) {
+        if (ensure(ctx->stage_in, (size_t)nq * kDim * 4) != 0 ||
+            ensure(ctx->stage_out, 2 * align_up(out_bytes, 256) + align_up(found_bytes, 256)) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_quant_search: staging");
+        if (cudaMemcpyAsync(ctx->stage_in.ptr, q, (size_t)nq * kDim * 4, cudaMemcpyHostToDevice,
+                            st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_quant_search: query copy failed");
+        dq = static_cast<const float*>(ctx->stage_in.ptr);
+        char* o = static_cast<char*>(ctx->stage_out.ptr);
+        di = reinterpret_cast<int32_t*>(o);
+        dv = reinterpret_cast<float*>(o + align_up(out_bytes, 256));
+        df = reinterpret_cast<int32_t*>(o + 2 * align_up(out_bytes, 256));
+    }
+    // counters: 3 x u64 stats, then the two passes' query counters and the re-run count
+    if (ensure(ctx->hnsw_misc, 64) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "hnsw_quant_search: counters");
+    unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
+    unsigned* next1 = reinterpret_cast<unsigned*>(stats + 3);
+    unsigned* next2 = next1 + 1;
+    int* over_n = reinterpret_cast<int*>(next1 + 2);
+    if (cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 64, st) != cudaSuccess)
+        return set_error(ctx, PION_B200_ECUDA, "hnsw_quant_search: memset failed");
+    int rc = 0;
+    const int64_t n = ix->n_rows;
+    if (n == 0) {
+        rc = launch_fill_results(dv, di, (size_t)nq * k, INFINITY, st);
+        if (!rc && cudaMemsetAsync(df, 0, found_bytes, st) != cudaSuccess) rc = PION_B200_ECUDA;
+        ctx->launches++;
+    } else {
+        const int per_sm = quant_ctas_per_sm((int)ef);
+        if (per_sm <= 0)
+            return set_error(ctx, PION_B200_ESHAPE, "hnsw_quant_search: ef %lld does not fit",
+                             (long long)ef);
+        const int warps = quant_warps_per_cta(), top = quant_top_entries();
+        int64_t ctas = (int64_t)per_sm * ctx->num_sms;
+        const int64_t need = (nq + warps - 1) / warps;
+        if (ctas > need) ctas = need;
+        const int64_t vis_words = ((n + 31) / 32 + 3) / 4 * 4;
+        // candidate heap: every node at most once, plus the start
+        const int64_t cap_all = n + 1;
+        int64_t cap1 = cap_all <= top ? top : (cap_all < 16384 ? cap_all : 16384);
+        if (const char* e = getenv("PION_B200_QUANT_HEAP_CAP")) {  // tests: force re-runs
+            const long long v = atoll(e);
+            if (v >= 1 && v < cap1) cap1 = v;
+        }
+        const bool rerun = cap1 < cap_all;
+        int64_t ctas2 = 0;
+        if (rerun) {
+            int64_t w2 = ((int64_t)1 << 30) / (std::max<int64_t>(cap_all - top, 1) * 8);
+            if (w2 > ctas * warps) w2 = ctas * warps;
+            ctas2 = w2 / warps < 1 ? 1 : w2 / warps;
+        }
+        const size_t tails = (size_t)std::max(ctas * warps * std::max<int64_t>(cap1 - top, 0),
+                                              ctas2 * warps * std::max<int64_t>(cap_all - top, 0)) *
+                             8;
+        if (ensure(ctx->hnsw_visited, (size_t)ctas * warps * vis_words * 4) != 0 ||
+            ensure(ctx->scratch2, tails > 0 ? tails : 16) != 0 ||
+            ensure(ctx->scratch, found_bytes) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "hnsw_quant_search: scratch");
+        QuantLaunch Lc;
+        Lc.kind = h.quant_kind;
+        Lc.metric = h.metric;
+        Lc.codes = h.qcodes;
+        Lc.code_bytes = h.code_bytes;
+        Lc.scales = h.qscales;
+        Lc.norms = h.norms;
+        Lc.qjl = h.qjl;
+        Lc.res_norms = h.qjl_res;
+        Lc.rsigns = h.qjl_rs;
+        Lc.lambda = h.qjl_lambda;
+        Lc.rerank = h.rerank_node;
+        Lc.l0_compact = h.l0_compact;
+        Lc.l0_slots = h.l0_slots;
+        Lc.node_slot = h.node_slot;
+        Lc.node_ids = h.node_ids;
+        Lc.deleted = h.deleted;
+        Lc.node_level = h.node_level;
+        Lc.upper_offset = h.upper_offset;
+        Lc.upper_links = h.upper_links;
+        Lc.M = h.M;
+        Lc.max_level = h.max_level;
+        Lc.num_nodes = n;
+        Lc.entry = h.entry;
+        Lc.queries = dq;
+        Lc.nq = (int)nq;
+        Lc.k = (int)k;
+        Lc.ef = (int)ef;
+        Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+        Lc.vis_words = vis_words;
+        Lc.cand_tail = ctx->scratch2.ptr;
+        Lc.cand_cap = cap1;
+        Lc.out_ids = di;
+        Lc.out_scores = dv;
+        Lc.out_found = df;
+        Lc.overflow = rerun ? static_cast<int*>(ctx->scratch.ptr) : nullptr;
+        Lc.overflow_n = over_n;
+        Lc.next_query = next1;
+        Lc.stats = stats;
+        Lc.status = ctx->d_status;
+        Lc.ctas = (int)ctas;
+        timing_begin(ctx);
+        rc = launch_quant_search(Lc, st);
+        ctx->launches++;
+        if (!rc && rerun) {  // the queries whose heap outgrew cap1, with room for all
+            Lc.qlist = static_cast<int*>(ctx->scratch.ptr);
+            Lc.qlist_n = over_n;
+            Lc.overflow = nullptr;
+            Lc.cand_cap = cap_all;
+            Lc.next_query = next2;
+            Lc.ctas = (int)ctas2;
+            rc = launch_quant_search(Lc, st);
+            ctx->launches++;
+        }
+        timing_end(ctx);
+    }
+    if (rc != 0)
+        return set_error(ctx, rc, "hnsw_quant_search: launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    if (mem == PION_B200_MEM_HOST) {
+        if (cudaMemcpyAsync(out_ids, di, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_scores, dv, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(out_found, df, found_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return set_error(ctx, PION_B200_ECUDA, "hnsw_quant_search: result copy failed");
+        return finish_sync(ctx);
+    }
+    return 0;
+}
+
+}  // extern "C"

@@ -43,6 +43,27 @@ struct BuildStats {
 int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
           int64_t id_base, int n_threads, Graph& g, BuildStats* stats);
 
+// Block-quantised slot formats (the reference's PolarQuant / NanoQuant / TurboQuant
+// compact_vectors): kinds, and the buffers quantize() fills from the rows the graph was
+// built from (normalised first under COSINE).
+constexpr int kQuantPolar = 0;  // INT4, stride 868
+constexpr int kQuantNano = 1;   // INT2, stride 484
+constexpr int kQuantTurbo = 2;  // INT3 + QJL, stride 676
+
+struct QuantBuffers {
+    int kind = 0;
+    int64_t stride = 0;
+    std::vector<int8_t> compact;        // n x stride, the graph's slot order
+    std::vector<uint64_t> qjl;          // TurboQuant: n x 24 sign words, by node
+    std::vector<float> qjl_res_norms;   // by node
+    std::vector<uint64_t> random_signs; // 24 words
+    std::vector<float> rerank;          // n x 1536 FP32 rows by node
+};
+
+int64_t quant_stride(int kind);
+void qjl_random_signs(uint64_t* out24);
+int quantize(const Graph& g, const float* rows, int kind, QuantBuffers& out, std::string& why);
+
 // The reference's index file (pion.hnsw.0, format v3 to v5, src/vector/hnsw.mojo:
 // 1209-1700): load into a Graph (0, or -1 / -3 with the reason), and save a Graph as v5.
 int load_file(const char* path, Graph& g, std::string& why);
@@ -50,3 +71,14 @@ int save_file(const Graph& g, const char* path, int64_t max_elements, std::strin
 
 }  // namespace hnsw
 }  // namespace pion
+
+// The objects behind the C handles pion_b200_hnsw_graph and pion_b200_hnsw_quant.
+struct pion_b200_hnsw_graph {
+    pion::hnsw::Graph g;
+    pion::hnsw::BuildStats stats;
+};
+
+struct pion_b200_hnsw_quant {
+    pion::hnsw::QuantBuffers q;
+    int64_t n = 0;
+};

@@ -19,7 +19,12 @@ struct DevBuf {
     size_t bytes = 0;
 };
 
-enum IndexKind { kFlatI8 = 1, kFlatF32 = 2, kBQ = 3, kHNSW = 4 };
+enum IndexKind { kFlatI8 = 1, kFlatF32 = 2, kBQ = 3, kHNSW = 4, kHNSWQuant = 5 };
+
+// Block-quantised slot formats of an HNSW graph (PION_B200_QUANT_*).
+constexpr int kQPolar = 0;  // INT4
+constexpr int kQNano = 1;   // INT2
+constexpr int kQTurbo = 2;  // INT3 + QJL
 
 // ---- flat_f32.cu
 int ff32_tile_rows();
@@ -130,6 +135,18 @@ struct pion_b200_index {
         int32_t* slot_ext = nullptr;     // slot -> external id (-1: no node)
         float* rerank = nullptr;         // FP32 rows by slot for the brute-force rerank
         int* chunk_vmin = nullptr;       // per 32 slots: min floor(norm) (whole tiles)
+        // block-quantised graphs (kHNSWQuant): per slot |v|^2 in `norms`, 48 f16 scales
+        // and the packed block codes; QJL signs and residual norms by node; FP32 rerank
+        // rows by node
+        int quant_kind = -1;
+        int code_bytes = 0;
+        uint8_t* qcodes = nullptr;
+        uint16_t* qscales = nullptr;
+        uint64_t* qjl = nullptr;
+        float* qjl_res = nullptr;
+        uint64_t* qjl_rs = nullptr;
+        float qjl_lambda = 1.0f;
+        float* rerank_node = nullptr;
         int64_t ext_base = 0, ext_count = 0;
         int M = 0;
         int max_level = 0;
@@ -191,6 +208,52 @@ int launch_hnsw_metric(const float* qn, int nq, int k, const int32_t* ids,
                        const int32_t* ext_to_node, int64_t ext_base, int64_t ext_count,
                        const uint32_t* node_slot, const int8_t* codes, float gmin, float gmax,
                        int cosine, float* scores, cudaStream_t st);
+
+// ---- quant.cu
+struct QuantLaunch {
+    int kind = 0, metric = 0;
+    const uint8_t* codes = nullptr;
+    int code_bytes = 0;
+    const uint16_t* scales = nullptr;
+    const float* norms = nullptr;
+    const uint64_t* qjl = nullptr;
+    const float* res_norms = nullptr;
+    const uint64_t* rsigns = nullptr;
+    float lambda = 1.0f;
+    const float* rerank = nullptr;
+    const uint32_t* l0_compact = nullptr;
+    const uint32_t* l0_slots = nullptr;
+    const uint32_t* node_slot = nullptr;
+    const int32_t* node_ids = nullptr;
+    const uint8_t* deleted = nullptr;
+    const int8_t* node_level = nullptr;
+    const int64_t* upper_offset = nullptr;
+    const uint32_t* upper_links = nullptr;
+    int M = 0, max_level = 0;
+    int64_t num_nodes = 0, entry = 0;
+    const float* queries = nullptr;
+    int nq = 0, k = 0, ef = 0;
+    const int* qlist = nullptr;    // queries to run (null: all)
+    const int* qlist_n = nullptr;  // their count, in device memory
+    uint32_t* visited = nullptr;
+    int64_t vis_words = 0;
+    void* cand_tail = nullptr;  // per warp (cand_cap - top entries) x 8 bytes
+    int64_t cand_cap = 0;
+    int32_t* out_ids = nullptr;
+    float* out_scores = nullptr;
+    int32_t* out_found = nullptr;
+    int* overflow = nullptr;  // null: an outgrown heap is an error
+    int* overflow_n = nullptr;
+    unsigned* next_query = nullptr;
+    unsigned long long* stats = nullptr;
+    int* status = nullptr;
+    int ctas = 0;
+};
+size_t quant_warp_smem(int ef);
+int quant_warps_per_cta();
+int quant_top_entries();
+int quant_ctas_per_sm(int ef);
+int launch_quant_search(const QuantLaunch& launch, cudaStream_t st);
 
 // ---- compat.cu: the per-thread default context of the reference-compatible symbols
 pion_b200_ctx* compat_default_ctx(const char* who);

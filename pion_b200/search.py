@@ -627,3 +627,146 @@ class HNSWIndex(_Index):
         out = (ctypes.c_int64 * 3)()
         c.check(c.lib.pion_v_b200_hnsw_last_stats(c.h, out))
         return dict(zip(("evals", "expansions", "upper_evals"), list(out)))
+
+
+# ------------------------------------------------------ block-quantised HNSW --
+
+QUANT_KINDS = {"polar": 0, "nano": 1, "turbo": 2}
+
+
+def _view(ptr, ctype, shape, dtype):
+    if not ptr or int(np.prod(shape)) == 0:
+        return np.zeros(shape, dtype)
+    return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctype)), shape=shape)
+
+
+class HNSWQuant:
+    """A graph's block-quantised slots in one of the reference's compact formats
+    ("polar": PolarQuant INT4, "nano": NanoQuant INT2, "turbo": TurboQuant INT3 + QJL),
+    quantised on the host from the rows the graph was built from (node order; normalised
+    first under COSINE), with those rows kept as the FP32 rerank buffer."""
+
+    def __init__(self, graph: HNSWGraph, rows, kind: str):
+        if kind not in QUANT_KINDS:
+            raise ValueError(f"kind must be one of {sorted(QUANT_KINDS)}")
+        self.lib = _lib.load()
+        a = np.ascontiguousarray(rows, dtype=np.float32)
+        h = ctypes.c_void_p()
+        rc = self.lib.pion_v_b200_hnsw_quantize(graph.h, a.ctypes.data, a.shape[0],
+                                                QUANT_KINDS[kind], ctypes.byref(h))
+        if rc != 0:
+            raise PionError(rc, "hnsw_quantize failed")
+        self.h = h
+        self.kind = kind
+        self.layout = _lib.HnswQuantLayout()
+        self.lib.pion_v_b200_hnsw_quant_layout(self.h, ctypes.byref(self.layout))
+
+    def arrays(self) -> dict:
+        """numpy views of the buffers (valid while this object lives): kind, stride,
+        compact [n * stride] int8 by slot, rerank [n, 1536] by node, and for "turbo" qjl
+        [n, 24] uint64, qjl_res_norms [n], qjl_random_signs [24], qjl_lambda."""
+        L = self.layout
+        n = L.num_nodes
+        out = {"kind": self.kind, "stride": L.stride,
+               "compact": _view(L.compact, ctypes.c_int8, (n * L.stride,), np.int8),
+               "rerank": _view(L.rerank, ctypes.c_float, (n, 1536), np.float32)
+               if L.rerank else None}
+        if L.qjl:
+            out.update(qjl=_view(L.qjl, ctypes.c_uint64, (n, 24), np.uint64),
+                       qjl_res_norms=_view(L.qjl_res_norms, ctypes.c_float, (n,), np.float32),
+                       qjl_random_signs=_view(L.qjl_random_signs, ctypes.c_uint64, (24,),
+                                              np.uint64),
+                       qjl_lambda=L.qjl_lambda)
+        return out
+
+    def free(self):
+        if getattr(self, "h", None):
+            self.lib.pion_v_b200_hnsw_quant_free(self.h)
+            self.h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def hnsw_quant_layout_struct(arrays: dict, num_nodes: int):
+    """(pion_b200_hnsw_quant_layout, keep-alive list) from a dict with HNSWQuant.arrays()'
+    keys (kind as a name or number; qjl keys and rerank optional)."""
+    lay = _lib.HnswQuantLayout()
+    keep = []
+
+    def ptr(name, dt):
+        a = arrays.get(name)
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dtype=dt)
+        keep.append(a)
+        return a.ctypes.data if a.size else None
+
+    kind = arrays["kind"]
+    lay.kind = QUANT_KINDS[kind] if isinstance(kind, str) else int(kind)
+    lay.num_nodes = num_nodes
+    lay.stride = arrays["stride"]
+    lay.compact = ptr("compact", np.int8)
+    lay.qjl = ptr("qjl", np.uint64)
+    lay.qjl_res_norms = ptr("qjl_res_norms", np.float32)
+    lay.qjl_random_signs = ptr("qjl_random_signs", np.uint64)
+    lay.qjl_lambda = float(arrays.get("qjl_lambda", 1.0))
+    lay.rerank = ptr("rerank", np.float32)
+    return lay, keep
+
+
+class HNSWQuantIndex(_Index):
+    """An HNSW graph with block-quantised slots copied to the GPU: the block-quant
+    branches of search_fp32_scored (src/vector/hnsw.mojo:4136-4330) with the FP32 rerank
+    tail, batched.  graph: HNSWGraph or a layout dict; quant: HNSWQuant or a dict of its
+    arrays; rerank=False registers no rerank rows (results keep their block distances)."""
+
+    def __init__(self, ctx: Context, graph, quant, rerank: bool = True):
+        if isinstance(graph, HNSWGraph):
+            glay, keep = graph.layout, [graph]
+        else:
+            glay, keep = hnsw_layout_struct(graph)
+        if isinstance(quant, HNSWQuant):
+            qlay = _lib.HnswQuantLayout.from_buffer_copy(quant.layout)
+            keep.append(quant)
+        else:
+            qlay, k2 = hnsw_quant_layout_struct(quant, glay.num_nodes)
+            keep += k2
+        if not rerank:
+            qlay.rerank = None
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.pion_v_b200_register_hnsw_quant(ctx.h, ctypes.byref(glay),
+                                                          ctypes.byref(qlay), ctypes.byref(h)))
+        super().__init__(ctx, h)
+        self.dim = glay.dim
+
+    def search(self, q, k: int, ef: int, ctx: Context | None = None):
+        """q float32 [nq, 1536] -> (external ids int32 [nq, k], scores float32 [nq, k],
+        found int32 [nq]); scores are FP32 squared L2 after the rerank, else the block
+        distances; -1 / +inf past found."""
+        c = ctx or self.ctx
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        nq = q.shape[0]
+        dev = mem == MEM_DEVICE
+        ids, sc, pi, pv = _outputs(dev, nq, k, q.device if dev else None)
+        if dev:
+            found = torch.empty(nq, dtype=torch.int32, device=q.device)
+            pf = found.data_ptr()
+        else:
+            found = np.empty(nq, np.int32)
+            pf = found.ctypes.data
+        with _TorchStream(c, mem):
+            c.check(c.lib.pion_v_b200_hnsw_quant_search(c.h, self.h, pq, nq, k, ef, pi, pv, pf,
+                                                         mem))
+        return ids, sc, found
+
+    def last_stats(self, ctx: Context | None = None) -> dict:
+        """Work of the context's last search: distance evaluations, level-0 expansions,
+        queries re-run with room for every node in the candidate heap."""
+        c = ctx or self.ctx
+        out = (ctypes.c_int64 * 3)()
+        c.check(c.lib.pion_v_b200_hnsw_last_stats(c.h, out))
+        return dict(zip(("evals", "expansions", "reruns"), list(out)))

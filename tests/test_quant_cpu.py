@@ -396,3 +396,38 @@ def test_quant_search_matches_python(oracle, qgraph, kind):
         assert cnt[t] == len(pi)
         assert list(ids[t, :cnt[t]]) == pi
         assert np.array_equal(sc[t, :cnt[t]].view(np.uint32), np.array(ps, F).view(np.uint32))
+
+
+@pytest.mark.parametrize("metric", ["cosine", "l2"])
+@pytest.mark.parametrize("kind", ["polar", "nano", "turbo"])
+def test_library_quantizer_matches_oracle(oracle, kind, metric):
+    """pion_v_b200_hnsw_quantize (host C++) writes the oracle's compact buffer, QJL rows,
+    residual norms and rerank rows bit for bit."""
+    import pion_b200
+    rows, _ = mixture_np(700, 1536, 9, seed=43 if metric == "cosine" else 47, n_queries=1)
+    rows[5] = 0.0  # a zero row passes through the normalisation
+    rows[6, :32] = 0.0  # an all-zero block takes scale 1
+    g = pion_b200.HNSWGraph(rows, M=6, ef_construction=32, metric=metric, threads=1)
+    A = g.arrays()
+    want = oracle.quant_graph(A, rows, kind)
+    qz = pion_b200.HNSWQuant(g, rows, kind)
+    got = qz.arrays()
+    assert got["stride"] == want["stride"]
+    assert np.array_equal(got["compact"], want["compact"])
+    assert np.array_equal(got["rerank"].view(np.uint32), want["rerank"].view(np.uint32))
+    if kind == "turbo":
+        assert np.array_equal(got["qjl"], want["qjl"])
+        assert np.array_equal(got["qjl_res_norms"].view(np.uint32),
+                              want["qjl_res_norms"].view(np.uint32))
+        assert np.array_equal(got["qjl_random_signs"], want["qjl_random_signs"])
+    else:
+        assert "qjl" not in got
+
+
+def test_library_quantizer_refuses(qgraph):
+    import pion_b200
+    g, A, rows, qs = qgraph
+    with pytest.raises(ValueError):
+        pion_b200.HNSWQuant(g, rows, "int5")
+    with pytest.raises(pion_b200.PionError):
+        pion_b200.HNSWQuant(g, rows[:-1], "polar")
