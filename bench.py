@@ -63,6 +63,12 @@ WORKLOADS = {
     "hnsw": dict(kind="hnsw", rows=1_000_000, dim=1536, centres=1024, seed=3, batch=4096, k=10,
                  M=16, ef_construction=200,
                  desc="HNSW INT8, 1M x 1536, M=16, efConstruction=200, 4096-query batches"),
+    **{f"hnsw_{q}": dict(kind="quant", quant=q, rows=1_000_000, dim=1536, centres=1024, seed=3,
+                          batch=4096, k=10, M=16, ef_construction=200,
+                          desc=f"HNSW {name}, 1M x 1536, M=16, efConstruction=200, FP32 rerank, "
+                               f"4096-query batches")
+       for q, name in (("polar", "PolarQuant INT4"), ("nano", "NanoQuant INT2"),
+                       ("turbo", "TurboQuant INT3 + QJL"))},
     "hnsw_brute": dict(kind="slot", rows=1_000_000, dim=1536, centres=1024, seed=3, batch=1024,
                        k=10, M=16, ef_construction=200,
                        desc="GPU brute-force scan of the HNSW slot buffer (INT8 L2 of every "
@@ -87,6 +93,9 @@ def args_parse(argv=None):
                     help="target CPU work of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ef", type=int, default=128, help="HNSW efSearch")
+    ap.add_argument("--graph-cache", default=None,
+                    help="HNSW workloads: load the graph from this index file (pion.hnsw.0 "
+                         "format) when it exists, else build it and save it there")
     ap.add_argument("--workers", type=int, default=None,
                     help="worker contexts (each its own CUDA stream) taking batches in turn; "
                          "default 3 for hnsw, 1 otherwise")
@@ -186,6 +195,10 @@ def config_of(wl, batch, world, a=None):
     if wl["kind"] == "hnsw":
         c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
                   "ef": a.ef if a is not None else None,
+                  "parallelism": f"graph replicas x{world}, one batch per replica"})
+    if wl["kind"] == "quant":
+        c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
+                  "ef": a.ef if a is not None else None, "quant": wl["quant"],
                   "parallelism": f"graph replicas x{world}, one batch per replica"})
     if wl["kind"] == "slot":
         c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
@@ -424,10 +437,18 @@ class HNSWWorkload:
                                         row_range=(s, e))
                 rows[s:e] = part.cpu()
                 del part
-            t0 = time.perf_counter()
-            self.graph = pion_b200.HNSWGraph(rows.numpy(), M=wl["M"],
-                                             ef_construction=wl["ef_construction"])
-            self.build_s = time.perf_counter() - t0
+            cache = wl.get("graph_cache")
+            if cache and os.path.exists(cache):
+                self.graph = pion_b200.HNSWGraph.load(cache)
+                if self.graph.layout.num_nodes != n:
+                    raise SystemExit(f"{cache} holds {self.graph.layout.num_nodes} nodes, not {n}")
+            else:
+                t0 = time.perf_counter()
+                self.graph = pion_b200.HNSWGraph(rows.numpy(), M=wl["M"],
+                                                 ef_construction=wl["ef_construction"])
+                self.build_s = time.perf_counter() - t0
+                if cache:
+                    self.graph.save(cache)
             self.rows_host = rows
             arrays = self.graph.arrays()
         else:
@@ -631,8 +652,140 @@ class SlotWorkload(HNSWWorkload):
             list(ex.map(lambda c: oracle.hnsw_brute_force(A, q[c[0]:c[1]], k, rr), chunks))
 
 
+class QuantWorkload(HNSWWorkload):
+    """The block-quantised HNSW search (PolarQuant / NanoQuant / TurboQuant): the graph of
+    the hnsw workload, its slots quantised on the host (pion_v_b200_hnsw_quantize) with the
+    FP32 rows kept for the rerank; replicas across GPUs, weak scaling."""
+
+    dtype = "int4 / int2 / int3 + QJL block codes (exact int32 block dots), fp32 rerank"
+
+    def __init__(self, wl, batch, dev, ctx, lo, hi, ef=128):
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        import pion_b200
+        super().__init__(wl, batch, dev, ctx, lo, hi, ef)
+        self.ix.free()  # the INT8 registration is not used
+        kind = wl["quant"]
+        self.dtype = {"polar": "int4", "nano": "int2", "turbo": "int3 + 1-bit QJL"}[kind] + \
+            " block codes (exact int32 block dots), fp32 block sums and rerank"
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        self.quant_s = None
+        if self.graph is not None:
+            t0 = time.perf_counter()
+            self.quant = pion_b200.HNSWQuant(self.graph, self.rows_host.numpy(), kind)
+            self.quant_s = time.perf_counter() - t0
+            qa = self.quant.arrays()
+        else:
+            self.quant, qa = None, None
+        if world > 1:
+            qa = self._broadcast_quant(qa, kind, dev)
+        self.qarrays = qa
+        self.ix = pion_b200.HNSWQuantIndex(ctx, self.graph if self.graph is not None
+                                           else self.arrays, self.quant or qa)
+        self._found = {}
+        torch.cuda.synchronize()
+
+    @staticmethod
+    def _broadcast_quant(qa, kind, dev):
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+        rank = dist.get_rank()
+        names = ["compact", "rerank"] + (["qjl", "qjl_res_norms", "qjl_random_signs"]
+                                         if kind == "turbo" else [])
+        dts = {"compact": np.int8, "rerank": np.float32, "qjl": np.uint64,
+               "qjl_res_norms": np.float32, "qjl_random_signs": np.uint64}
+        out = {"kind": kind, "qjl_lambda": 1.0}
+        meta = torch.zeros(1, dtype=torch.int64, device=dev)
+        if rank == 0:
+            meta[0] = int(qa["stride"])
+        dist.broadcast(meta, 0)
+        out["stride"] = int(meta[0])
+        for nm in names:
+            if rank == 0:
+                a = np.ascontiguousarray(qa[nm])
+                shp = torch.tensor(list(a.shape) + [0] * (2 - a.ndim), device=dev)
+                t = torch.from_numpy(a.view(np.uint8).reshape(-1)).to(dev)
+            else:
+                shp = torch.zeros(2, dtype=torch.int64, device=dev)
+            dist.broadcast(shp, 0)
+            shape = [int(x) for x in shp.tolist() if x > 0]
+            nbytes = int(np.prod(shape)) * np.dtype(dts[nm]).itemsize
+            if rank != 0:
+                t = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            dist.broadcast(t, 0)
+            out[nm] = t.cpu().numpy().view(dts[nm]).reshape(shape)
+            del t
+        return out
+
+    def search(self, inp, ctx=None):
+        ids, sc, _ = self.ix.search(inp[0], self.k, self.ef, ctx=ctx)
+        return ids, sc
+
+    def host_call(self, hin, out_i, out_v, ctx=None):
+        import torch
+
+        import pion_b200
+        c = ctx or self.ctx
+        found = self._found.get(id(c))
+        if found is None:  # one pinned buffer per worker context
+            found = self._found[id(c)] = torch.empty(self.batch, dtype=torch.int32).pin_memory()
+        c.check(c.lib.pion_v_b200_hnsw_quant_search(c.h, self.ix.h, hin[0].data_ptr(),
+                                                    self.batch, self.k, self.ef,
+                                                    out_i.data_ptr(), out_v.data_ptr(),
+                                                    found.data_ptr(), pion_b200._lib.MEM_HOST))
+
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+        st = self.ix.last_stats()
+        kind = self.wl["quant"]
+        slot = 4 + 96 + {"polar": 768, "nano": 384, "turbo": 576}[kind] + \
+            (196 if kind == "turbo" else 0)
+        byts = float(st["evals"]) * slot + st["expansions"] * 264.0 + \
+            self.batch * self.ef * 1536 * 4.0
+        achieved = byts / (kern_ms / 1000.0) / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "algorithmic_per_launch": byts, "kernel_ms": kern_ms,
+                "work_per_query": {k: v / max(1, self.batch) for k, v in st.items()},
+                "note": f"random gathers, latency-bound: bytes = distance evaluations x {slot} "
+                        f"(|v|^2, f16 scales, codes" + (", QJL row" if kind == "turbo" else "") +
+                        ") + expansions x 264 + ef x 6144 (the FP32 rerank rows)"}
+
+    def extra(self, dev):
+        import numpy as np
+        import torch
+
+        import pion_b200
+        if self.graph is None:
+            return {}
+        rows = self.rows_host.to(dev)
+        flat = pion_b200.FlatF32Index(self.ctx, rows)
+        truth, _ = flat.search(self.q, self.k)
+        ids, _, _ = self.ix.search(self.q, self.k, self.ef)
+        t, r = truth.cpu().numpy(), ids.cpu().numpy()
+        recall = float(np.mean([len(set(r[i]) & set(t[i])) / self.k for i in range(len(t))]))
+        flat.free()
+        del rows
+        torch.cuda.empty_cache()
+        return {"recall_at_10": recall, "ef": self.ef, "quant": self.wl["quant"],
+                "build_s": self.build_s, "quantize_s": self.quant_s,
+                "rerank": "fp32 rows by node"}
+
+    def host_data(self):
+        return (self.graph.arrays(), self.quant.arrays(), self.q.cpu().numpy(), self.ef)
+
+    @staticmethod
+    def cpu_run(data, lo, hi, k, threads):
+        import oracle
+        A, Q, q, ef = data
+        oracle.quant_search(A, Q, q[lo:hi], k, ef, nthreads=threads)
+
+
 ADAPTERS = {"i8": I8Workload, "f32": F32Workload, "bq": BQWorkload, "hnsw": HNSWWorkload,
-            "slot": SlotWorkload}
+            "slot": SlotWorkload, "quant": QuantWorkload}
 
 
 # --------------------------------------------------------------- reference arm --
@@ -647,11 +800,18 @@ def reference_data(wl, batch, dev):
 
     n, dim = wl["rows"], wl["dim"]
     _, qf = mixture_torch(n, dim, wl["centres"], wl["seed"], batch, device=dev, row_range=(0, 0))
-    if wl["kind"] in ("hnsw", "slot"):  # the host build (a restatement of the reference's)
+    if wl["kind"] in ("hnsw", "slot", "quant"):  # the host build (restating the reference's)
         import pion_b200
         rows, _ = mixture_torch(n, dim, wl["centres"], wl["seed"], 0, device=dev)
         rows = rows.cpu().numpy()
-        g = pion_b200.HNSWGraph(rows, M=wl["M"], ef_construction=wl["ef_construction"])
+        cache = wl.get("graph_cache")
+        if cache and os.path.exists(cache):
+            g = pion_b200.HNSWGraph.load(cache)
+        else:
+            g = pion_b200.HNSWGraph(rows, M=wl["M"], ef_construction=wl["ef_construction"])
+        if wl["kind"] == "quant":
+            qz = pion_b200.HNSWQuant(g, rows, wl["quant"])
+            return (g.arrays(), qz.arrays(), qf.cpu().numpy(), wl["ef"]), (g, qz)
         if wl["kind"] == "slot":
             A = g.arrays()
             rr = np.empty_like(rows)
@@ -700,7 +860,7 @@ def run_reference(a, wl):
     dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
     data = reference_data(wl, batch, dev)
     keep = None
-    if wl["kind"] in ("hnsw", "slot"):
+    if wl["kind"] in ("hnsw", "slot", "quant"):
         data, keep = data
     run = ADAPTERS[wl["kind"]].cpu_run
     threads = os.cpu_count() or 1
@@ -766,7 +926,7 @@ def run_ours(a, wl):
     n = wl["rows"]
     lo, hi = shard_bounds(n, world, rank)
     ctx = pion_b200.Context(local)
-    if wl["kind"] in ("hnsw", "slot"):
+    if wl["kind"] in ("hnsw", "slot", "quant"):
         W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi, ef=a.ef)
     else:
         W = ADAPTERS[wl["kind"]](wl, batch, dev, ctx, lo, hi)
@@ -779,8 +939,8 @@ def run_ours(a, wl):
                                     lists_major=True)
 
     step = W.search if getattr(W, "replicas", False) else ShardedSearch(W.search, k, merge)
-    workers = a.workers or (3 if wl["kind"] == "hnsw" else 1)
-    if workers > 1 and wl["kind"] not in ("hnsw", "slot"):
+    workers = a.workers or (3 if wl["kind"] in ("hnsw", "quant") else 1)
+    if workers > 1 and wl["kind"] not in ("hnsw", "slot", "quant"):
         raise SystemExit("--workers > 1 is for the hnsw workloads")
     ctxs = [ctx] + [pion_b200.Context(local) for _ in range(workers - 1)]
     streams = [stream] + [torch.cuda.Stream(device=dev) for _ in range(workers - 1)]
@@ -960,6 +1120,7 @@ def main(argv=None):
     a = args_parse(argv)
     wl = dict(WORKLOADS[a.workload])
     wl["ef"] = a.ef
+    wl["graph_cache"] = a.graph_cache
     if a.rows:
         wl["rows"] = a.rows
         wl["desc"] += f" (rows overridden: {a.rows:,})"

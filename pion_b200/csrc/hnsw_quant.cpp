@@ -9,6 +9,8 @@
 // x86-64-v2 has no FMA); f16 scales rounded to nearest even.
 #include <cmath>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 #include "hnsw_host.h"
 
@@ -239,27 +241,44 @@ int quantize(const Graph& g, const float* rows, int kind, QuantBuffers& out, std
     out.stride = stride;
     out.compact.assign((size_t)(n * stride), 0);
     out.rerank.resize((size_t)n * kDim);
-    std::vector<float> x(kDim);
     if (kind == kQuantTurbo) {
         out.qjl.assign((size_t)n * 24, 0ull);
         out.qjl_res_norms.assign((size_t)n, 0.0f);
         out.random_signs.resize(24);
         qjl_random_signs(out.random_signs.data());
     }
-    for (int64_t i = 0; i < n; ++i) {
-        const float* r = rows + i * kDim;
-        if (g.metric == 1) {  // the stored rows of a COSINE index are normalised
-            l2_normalize(r, x.data());
-        } else {
-            std::memcpy(x.data(), r, kDim * sizeof(float));
+    for (int64_t i = 0; i < n; ++i)
+        if (g.node_slot[i] >= (uint64_t)n) {
+            why = "node_slot out of range";
+            return -3;
         }
-        std::memcpy(out.rerank.data() + (size_t)i * kDim, x.data(), kDim * sizeof(float));
-        int8_t* slot = out.compact.data() + (size_t)g.node_slot[i] * stride;
-        block_slot(kind, x.data(), slot);
-        if (kind == kQuantTurbo)
-            out.qjl_res_norms[i] =
-                qjl_row(x.data(), slot, out.random_signs.data(), out.qjl.data() + (size_t)i * 24);
-    }
+    // every node is independent: contiguous node ranges on the host threads
+    auto work = [&](int64_t lo, int64_t hi) {
+        std::vector<float> x(kDim);
+        for (int64_t i = lo; i < hi; ++i) {
+            const float* r = rows + i * kDim;
+            if (g.metric == 1) {  // the stored rows of a COSINE index are normalised
+                l2_normalize(r, x.data());
+            } else {
+                std::memcpy(x.data(), r, kDim * sizeof(float));
+            }
+            std::memcpy(out.rerank.data() + (size_t)i * kDim, x.data(), kDim * sizeof(float));
+            int8_t* slot = out.compact.data() + (size_t)g.node_slot[i] * stride;
+            block_slot(kind, x.data(), slot);
+            if (kind == kQuantTurbo)
+                out.qjl_res_norms[i] = qjl_row(x.data(), slot, out.random_signs.data(),
+                                               out.qjl.data() + (size_t)i * 24);
+        }
+    };
+    int64_t threads = (int64_t)std::thread::hardware_concurrency();
+    if (threads < 1) threads = 1;
+    if (threads > 64) threads = 64;
+    if (threads > n / 256 + 1) threads = n / 256 + 1;
+    std::vector<std::thread> pool;
+    for (int64_t t = 1; t < threads; ++t)
+        pool.emplace_back(work, n * t / threads, n * (t + 1) / threads);
+    work(0, n / threads);
+    for (auto& th : pool) th.join();
     return 0;
 }
 
