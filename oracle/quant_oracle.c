@@ -450,10 +450,14 @@ typedef struct {
     int has_qjl;
 } qctx;
 
-static float qdist(const orc_quant_layout *L, const qctx *Q, const int8_t *v, int64_t nidx) {
+/* The block distance; TurboQuant's QJL correction only where `qjl` is set (the beam:
+ * quant_beams_1536.mojo:62-71), not in the upper-level greedy, which scores plain
+ * int3_dot_single_simd distances (hnsw.mojo:4224-4246). */
+static float qdist(const orc_quant_layout *L, const qctx *Q, const int8_t *v, int64_t nidx,
+                   int qjl) {
     const float norm_v = load_f32(v);
     const float dot = orc_quant_dot(L->kind, Q->qc, Q->qs, v);
-    if (L->kind != ORC_QUANT_TURBO) return (Q->qn + norm_v) - 2.0f * dot;
+    if (L->kind != ORC_QUANT_TURBO || !qjl) return (Q->qn + norm_v) - 2.0f * dot;
     float qjl_c = 0.0f;
     if (Q->has_qjl) {
         int ham = 0;
@@ -490,19 +494,20 @@ static int quant_beam(const orc_quant_layout *L, const qctx *Q, int64_t start, f
             visited[nidx] = 1;
             const uint32_t ns = srow[1 + i];
             const int8_t *v = ns != 0xffffffffu ? L->compact + (int64_t)ns * L->stride : qslot(L, nidx);
-            const float d = qdist(L, Q, v, nidx);
+            const float d = qdist(L, Q, v, nidx, 1);
             if (min_push(cand, d, nidx) || max_push_bounded(res, d, nidx, ef)) return -1;
         }
     }
     return 0;
 }
 
-/* The upper-level greedy of the block-quant branches: the loop bound is the count of the
- * node the pass started from while neighbours are read from the current best node, as
- * the reference's loop does; NanoQuant also skips deleted nodes. */
+/* The upper-level greedy of the block-quant branches (hnsw.mojo:4158-4188, 4220-4246,
+ * 4266-4290): the loop bound is the count of the node the pass started from while
+ * neighbours are read from the current best node, as the reference's loop does; NanoQuant
+ * also skips deleted nodes; distances without the QJL term. */
 static void quant_greedy(const orc_quant_layout *L, const qctx *Q, int64_t *node, float *dist) {
     int64_t cur = L->entry_point;
-    float cd = qdist(L, Q, qslot(L, cur), cur);
+    float cd = qdist(L, Q, qslot(L, cur), cur, 0);
     const int64_t M = L->M;
     for (int64_t l = L->max_level; l >= 1; --l) {
         int changed = 1;
@@ -516,7 +521,7 @@ static void quant_greedy(const orc_quant_layout *L, const qctx *Q, int64_t *node
                 const int64_t nidx = i < M ? (int64_t)urow[1 + i] : -1;
                 if (nidx < 0 || nidx >= L->num_nodes) continue;
                 if (L->kind == ORC_QUANT_NANO && is_del(L, nidx)) continue;
-                const float d = qdist(L, Q, qslot(L, nidx), nidx);
+                const float d = qdist(L, Q, qslot(L, nidx), nidx, 0);
                 if (d < cd) {
                     cd = d;
                     cur = nidx;

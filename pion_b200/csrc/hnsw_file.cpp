@@ -218,7 +218,10 @@ int load_file(const char* path, Graph& g, std::string& why) {
             if (cnt > (uint32_t)M) cnt = (uint32_t)M;
             uint32_t* row = g.upper_links.data() + (size_t)r * (1 + M);
             row[0] = cnt;
-            for (uint32_t j = 0; j < cnt; ++j) row[1 + j] = blk[2 * M + (l - 1) * M + j];
+            // the whole level segment: the block-quant greedy reads positions past the
+            // count of a node it moved to (bounded by the first node's count), as the
+            // reference's loop reads the node's neighbour block
+            for (int64_t j = 0; j < M; ++j) row[1 + j] = blk[2 * M + (l - 1) * M + j];
         }
     }
     // _build_l0_slots: the slot of every level-0 neighbour, 0xFFFFFFFF for none

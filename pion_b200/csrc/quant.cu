@@ -6,10 +6,11 @@
 //             block-quantised to int8 (quantize_fp32_to_block_int8, kernels.mojo:1422-1455)
 //             and, for TurboQuant, its QJL signs (qjl_compute_signs, kernels.mojo:1685-1714:
 //             residual x random signs, three 512-point Walsh-Hadamard transforms);
-//   greedy    the upper levels with the block distance, the reference's loop: the bound is
-//             the count of the node the pass started from while neighbours are read from
-//             the current best node; NanoQuant skips deleted nodes.  The lanes score the
-//             row's remaining positions at once and the first strictly closer one moves;
+//   greedy    the upper levels with the block distance (TurboQuant without its QJL term),
+//             the reference's loop (hnsw.mojo:4158-4290): the bound is the count of the
+//             node the pass started from while neighbours are read from the current best
+//             node; NanoQuant skips deleted nodes.  The lanes score the row's remaining
+//             positions at once and the first strictly closer one moves;
 //   beam      quant_beam_search_1536_ref (src/vector/reference/quant_beams_1536.mojo:20-81)
 //             over the reference's binary heaps (src/common/heap.mojo:48-120, 237-339):
 //             candidates in a MinHeap, results in a MaxHeap bounded at ef with its cached
@@ -238,11 +239,12 @@ __device__ float slot_dot(const Params& p, const Fixed& S, uint32_t slot) {
     return total;
 }
 
-// The block-quant distance of node `node` stored at `slot`.  One lane.
-__device__ float lane_dist(const Params& p, const Fixed& S, uint32_t slot, uint32_t node) {
+// The block-quant distance of node `node` stored at `slot`; TurboQuant's QJL term only
+// when `qjl` (the beam; the greedy scores plain block distances).  One lane.
+__device__ float lane_dist(const Params& p, const Fixed& S, uint32_t slot, uint32_t node, bool qjl) {
     const float dot = slot_dot(p, S, slot);
     const float d = __fsub_rn(__fadd_rn(S.qn, __ldg(p.norms + slot)), __fmul_rn(2.0f, dot));
-    if (p.kind != kQTurbo) return d;
+    if (p.kind != kQTurbo || !qjl) return d;
     float qjl_c = 0.0f;
     if (p.qjl && p.res_norms) {
         const ulonglong2* sg = reinterpret_cast<const ulonglong2*>(p.qjl + (size_t)node * QW);
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
         // upper levels
         uint32_t cur = (uint32_t)p.entry;
         float cd = 0.0f;
-        if (lane == 0) cd = lane_dist(p, S, __ldg(p.node_slot + cur), cur);
+        if (lane == 0) cd = lane_dist(p, S, __ldg(p.node_slot + cur), cur, false);
         cd = __shfl_sync(FULL, cd, 0);
         ++evals;
         for (int l = p.max_level; l >= 1; --l) {
@@ -547,7 +549,7 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
                     bool ok = nidx < (uint64_t)n;
                     if (ok && p.kind == kQNano && is_deleted(p.deleted, nidx)) ok = false;
                     float d = 0.0f;
-                    if (ok) d = lane_dist(p, S, __ldg(p.node_slot + nidx), nidx);
+                    if (ok) d = lane_dist(p, S, __ldg(p.node_slot + nidx), nidx, false);
                     evals += __popc(__ballot_sync(FULL, ok)) * (lane == 0);
                     const unsigned better = __ballot_sync(FULL, ok && d < cd);
                     if (better == 0) break;  // positions past M are never scored
@@ -604,7 +606,7 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
                 uint32_t slot = __ldg(p.l0_slots + (size_t)cid * 33 + 1 + lane);
                 if (slot == 0xffffffffu) slot = __ldg(p.node_slot + nidx);
                 const int at = __popc(keep & ((1u << lane) - 1u));
-                S.nd[at] = lane_dist(p, S, slot, nidx);
+                S.nd[at] = lane_dist(p, S, slot, nidx, true);
                 S.ni[at] = nidx;
             }
             evals += __popc(keep) * (lane == 0);

@@ -306,11 +306,12 @@ def py_search(A, Q, kind, q, k, ef):
         res = np.array([q[i] - F(qc[i]) * qs[i // 32] for i in range(1536)], F)
         qsig, qres = py_qjl(res, Q["qjl_random_signs"])
 
-    def dist(node, slot_row=None):
+    def dist(node, slot_row=None, qjl=True):
+        # the greedy scores without the QJL term (hnsw.mojo:4224-4246), the beam with it
         v = comp[slot_of[node]] if slot_row is None else comp[slot_row]
         norm_v = np.frombuffer(v[:4].tobytes(), F)[0]
         dot = py_dot(kind, qc, qs, v)
-        if kind != "turbo":
+        if kind != "turbo" or not qjl:
             return (qn + norm_v) - F(2.0) * dot
         ham = sum(bin(int(a) ^ int(b)).count("1") for a, b in zip(qsig, Q["qjl"][node]))
         cos_est = (F(1536) - F(2) * F(ham)) * (F(1.0) / F(1536))
@@ -319,7 +320,7 @@ def py_search(A, Q, kind, q, k, ef):
 
     M = A["M"]
     cur = A["entry_point"]
-    cd = dist(cur)
+    cd = dist(cur, qjl=False)
     for lv in range(A["max_level"], 0, -1):
         changed = True
         while changed:
@@ -330,7 +331,7 @@ def py_search(A, Q, kind, q, k, ef):
                 nidx = int(row[1 + i])
                 if nidx >= A["num_nodes"]:
                     continue
-                d = dist(nidx)
+                d = dist(nidx, qjl=False)
                 if d < cd:
                     cd, cur, changed = d, nidx, True
     cand, res, seen = PyMin(), PyMax(), {cur}
