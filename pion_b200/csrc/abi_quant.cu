@@ -190,8 +190,21 @@ int pion_v_b200_register_hnsw_quant(pion_b200_ctx* ctx, const pion_b200_hnsw_lay
             if (!rc) rc = upload(&h.node_ids, L->node_ids, n);
             if (!rc) rc = upload(&h.node_level, L->node_level, n);
             if (!rc) rc = upload(&h.upper_offset, L->upper_offset, n);
-            if (!rc && L->upper_rows > 0)
-                rc = upload(&h.upper_links, L->upper_links, (size_t)L->upper_rows * (1 + L->M));
+            if (!rc && L->upper_rows > 0) {
+                const size_t words = (size_t)L->upper_rows * (1 + L->M);
+                rc = upload(&h.upper_links, L->upper_links, words);
+                // the slots of the upper-level neighbours (every position of a row, as the
+                // greedy may read past a row's count), so a step needs no dependent load
+                std::vector<uint32_t> us(words, 0xffffffffu);
+                for (size_t r = 0; r < (size_t)L->upper_rows; ++r) {
+                    const uint32_t* row = L->upper_links + r * (1 + L->M);
+                    us[r * (1 + L->M)] = row[0];
+                    for (int64_t k = 0; k < L->M; ++k)
+                        if (row[1 + k] < (uint32_t)n)
+                            us[r * (1 + L->M) + 1 + k] = L->node_slot[row[1 + k]];
+                }
+                if (!rc) rc = upload(&h.upper_slots, us.data(), words);
+            }
             if (!rc && L->deleted) rc = upload(&h.deleted, L->deleted, (n + 7) / 8);
             if (!rc && Q->kind == kQTurbo && Q->qjl) {
                 rc = upload(&h.qjl, Q->qjl, n * 24);
@@ -317,6 +330,7 @@ int pion_v_b200_hnsw_quant_search(pion_b200_ctx* ctx, const pion_b200_index* ix,
         Lc.node_level = h.node_level;
         Lc.upper_offset = h.upper_offset;
         Lc.upper_links = h.upper_links;
+        Lc.upper_slots = h.upper_slots;
         Lc.M = h.M;
         Lc.max_level = h.max_level;
         Lc.num_nodes = n;

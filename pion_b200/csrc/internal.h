@@ -229,6 +229,7 @@ struct QuantLaunch {
     const int8_t* node_level = nullptr;
     const int64_t* upper_offset = nullptr;
     const uint32_t* upper_links = nullptr;
+    const uint32_t* upper_slots = nullptr;
     int M = 0, max_level = 0;
     int64_t num_nodes = 0, entry = 0;
     const float* queries = nullptr;

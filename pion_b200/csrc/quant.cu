@@ -14,14 +14,17 @@
 //   beam      quant_beam_search_1536_ref (src/vector/reference/quant_beams_1536.mojo:20-81)
 //             over the reference's binary heaps (src/common/heap.mojo:48-120, 237-339):
 //             candidates in a MinHeap, results in a MaxHeap bounded at ef with its cached
-//             worst.  Each expansion reads the adjacency row once, the lanes take one
-//             neighbour each (adjacency order), drop deleted, visited and repeated nodes and
-//             score their neighbour alone, block by block in the reference's order; lane 0
-//             then pushes the scored neighbours in adjacency order.  The heaps are kept
-//             array for array as the reference keeps them (ties pop in the same order).
+//             worst.  Each expansion reads the adjacency row and its slots in one round
+//             trip, the lanes take one neighbour each (adjacency order) and drop deleted,
+//             visited and repeated nodes; the new neighbours are then scored four lanes to a
+//             neighbour (each lane 12 consecutive blocks with all its loads in flight, the
+//             block terms folded lane to lane in the reference's order) and their rows sent
+//             towards L2; lane 0 pushes them in adjacency order.  The heaps are kept array
+//             for array as the reference keeps them (ties pop in the same order).
 //   tail      the results drained farthest first and reversed, reranked by the FP32 rows
-//             (two 8-lane accumulators over 16-element steps, halving reduce), a stable
-//             sort by distance, the first k as external ids.
+//             (two 8-lane accumulators over 16-element steps, halving reduce; two rows per
+//             warp, 32 loads per lane in flight, the next pair's rows sent towards L2), a
+//             stable sort by distance, the first k as external ids.
 //
 // Distances: (|q|^2 + |v|^2) - 2 dot, dot = sum over blocks of f32(int32 block dot) *
 // (q scale * v scale); TurboQuant subtracts 2 (lambda cos_est)(|q res| |v res|) with
@@ -82,6 +85,7 @@ struct Params {
     const int8_t* node_level;
     const int64_t* upper_offset;
     const uint32_t* upper_links;
+    const uint32_t* upper_slots;  // upper_links with each neighbour replaced by its slot
     int M, max_level;
     int64_t num_nodes, entry;
     const float* queries;
@@ -109,8 +113,9 @@ struct Fixed {
     float qs[NB];         // query block scales
     int32_t qsum[NB];     // sums of the query block codes
     uint64_t qsig[QW];    // query QJL signs
-    float nd[32];         // one expansion's scored neighbours, adjacency order
-    uint32_t ni[32];
+    float nd[32];         // one batch of gathered neighbours, adjacency order: distances,
+    uint32_t ni[32];      // nodes,
+    uint32_t ns[32];      // slots
     float qn, qres, qinv;
     int scaled;
     int cand_n, res_n;
@@ -180,85 +185,130 @@ __device__ __forceinline__ int dot_i3(uint32_t w0, uint32_t w1, uint32_t w2, con
     return a - 4 * qsum;
 }
 
-__device__ __forceinline__ float block_term(float total, int acc, float qs, uint16_t hs) {
-    const float combined = __fmul_rn(qs, __half2float(__ushort_as_half(hs)));
-    return __fadd_rn(total, __fmul_rn((float)acc, combined));
-}
-
-// The block dot of the query with slot `slot`, blocks in order (ref_int4/3/2_dot,
-// src/vector/reference/quant_dots.mojo:45-102).  One lane.
-__device__ float slot_dot(const Params& p, const Fixed& S, uint32_t slot) {
-    const uint4* sc4 = reinterpret_cast<const uint4*>(p.scales + (size_t)slot * NB);
+// The terms f32(acc_b) * (q scale * v scale) of blocks [12 sub, 12 sub + 12) of slot
+// `slot` (ref_int4/3/2_dot, src/vector/reference/quant_dots.mojo:45-102): every load of
+// the lane's share of the slot is issued before the first dot.
+__device__ __forceinline__ void block_terms(const Params& p, const Fixed& S, uint32_t slot,
+                                            int sub, float* t) {
+    const int b0 = 12 * sub;
+    const uint2* sc = reinterpret_cast<const uint2*>(p.scales + (size_t)slot * NB + b0);
+    uint2 sv[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) sv[j] = __ldg(sc + j);
+    uint16_t hs[12];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        hs[4 * j] = (uint16_t)(sv[j].x & 0xffffu);
+        hs[4 * j + 1] = (uint16_t)(sv[j].x >> 16);
+        hs[4 * j + 2] = (uint16_t)(sv[j].y & 0xffffu);
+        hs[4 * j + 3] = (uint16_t)(sv[j].y >> 16);
+    }
     const uint4* cw = reinterpret_cast<const uint4*>(p.codes + (size_t)slot * p.code_bytes);
-    float total = 0.0f;
-    for (int g = 0; g < 6; ++g) {  // 8 blocks per group
-        const uint4 s4 = __ldg(sc4 + g);
-        const uint16_t hs[8] = {(uint16_t)(s4.x & 0xffffu), (uint16_t)(s4.x >> 16),
-                                (uint16_t)(s4.y & 0xffffu), (uint16_t)(s4.y >> 16),
-                                (uint16_t)(s4.z & 0xffffu), (uint16_t)(s4.z >> 16),
-                                (uint16_t)(s4.w & 0xffffu), (uint16_t)(s4.w >> 16)};
-        if (p.kind == kQPolar) {
-            uint4 w[8];
+    int acc[12];
+    if (p.kind == kQPolar) {  // 16 bytes a block
+        uint4 w[12];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) w[j] = __ldg(cw + g * 8 + j);
+        for (int j = 0; j < 12; ++j) w[j] = __ldg(cw + b0 + j);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int b = g * 8 + j;
-                total = block_term(total, dot_i4(w[j], S.qw + b * 8, S.qsum[b]), S.qs[b], hs[j]);
-            }
-        } else if (p.kind == kQNano) {
-            uint4 w[4];
+        for (int j = 0; j < 12; ++j) acc[j] = dot_i4(w[j], S.qw + (b0 + j) * 8, S.qsum[b0 + j]);
+    } else if (p.kind == kQNano) {  // 8 bytes a block
+        uint4 w[6];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) w[j] = __ldg(cw + g * 4 + j);
+        for (int j = 0; j < 6; ++j) w[j] = __ldg(cw + b0 / 2 + j);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int b = g * 8 + j;
-                const uint4 v = w[j >> 1];
-                const uint32_t p0 = (j & 1) ? v.z : v.x, p1 = (j & 1) ? v.w : v.y;
-                total = block_term(total, dot_i2(p0, p1, S.qw + b * 8, S.qsum[b]), S.qs[b], hs[j]);
-            }
-        } else {
-            uint32_t w[24];
-#pragma unroll
-            for (int j = 0; j < 6; ++j) {
-                const uint4 v = __ldg(cw + g * 6 + j);
-                w[4 * j] = v.x;
-                w[4 * j + 1] = v.y;
-                w[4 * j + 2] = v.z;
-                w[4 * j + 3] = v.w;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int b = g * 8 + j;
-                total = block_term(total, dot_i3(w[3 * j], w[3 * j + 1], w[3 * j + 2], S.qw + b * 8,
-                                                 S.qsum[b]),
-                                   S.qs[b], hs[j]);
-            }
+        for (int j = 0; j < 12; ++j) {
+            const uint4 v = w[j >> 1];
+            acc[j] = dot_i2((j & 1) ? v.z : v.x, (j & 1) ? v.w : v.y, S.qw + (b0 + j) * 8,
+                            S.qsum[b0 + j]);
         }
+    } else {  // 12 bytes a block
+        uint32_t w[36];
+#pragma unroll
+        for (int j = 0; j < 9; ++j) {
+            const uint4 v = __ldg(cw + (b0 * 12) / 16 + j);
+            w[4 * j] = v.x;
+            w[4 * j + 1] = v.y;
+            w[4 * j + 2] = v.z;
+            w[4 * j + 3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 12; ++j)
+            acc[j] = dot_i3(w[3 * j], w[3 * j + 1], w[3 * j + 2], S.qw + (b0 + j) * 8,
+                            S.qsum[b0 + j]);
     }
-    return total;
+#pragma unroll
+    for (int j = 0; j < 12; ++j) {
+        const float combined = __fmul_rn(S.qs[b0 + j], __half2float(__ushort_as_half(hs[j])));
+        t[j] = __fmul_rn((float)acc[j], combined);
+    }
 }
 
-// The block-quant distance of node `node` stored at `slot`; TurboQuant's QJL term only
-// when `qjl` (the beam; the greedy scores plain block distances).  One lane.
-__device__ float lane_dist(const Params& p, const Fixed& S, uint32_t slot, uint32_t node, bool qjl) {
-    const float dot = slot_dot(p, S, slot);
-    const float d = __fsub_rn(__fadd_rn(S.qn, __ldg(p.norms + slot)), __fmul_rn(2.0f, dot));
-    if (p.kind != kQTurbo || !qjl) return d;
-    float qjl_c = 0.0f;
-    if (p.qjl && p.res_norms) {
-        const ulonglong2* sg = reinterpret_cast<const ulonglong2*>(p.qjl + (size_t)node * QW);
+// Scores the m (<= 32) gathered neighbours (S.ni nodes at S.ns slots) into S.nd: four
+// lanes per neighbour, eight neighbours at a time, each lane dotting 12 consecutive blocks
+// and folding its terms onto the running sum handed over by the lane before it, so the 48
+// block terms add in the reference's order.  Distance (|q|^2 + |v|^2) - 2 dot, and for
+// TurboQuant with `qjl` set the QJL term (quant_beams_1536.mojo:62-71): the greedy scores
+// plain block distances.  Called by the whole warp.
+__device__ void score_batch(const Params& p, Fixed& S, int m, bool qjl, int lane) {
+    const int sub = lane & 3, grp = lane >> 2;
+    const bool with_qjl = qjl && p.kind == kQTurbo && p.qjl && p.res_norms;
+    for (int base = 0; base < m; base += 8) {
+        const int j = base + grp;
+        const bool act = j < m;
+        const uint32_t slot = act ? S.ns[j] : 0u, node = act ? S.ni[j] : 0u;
+        float nv = 0.0f, rn = 0.0f;
         int ham = 0;
+        if (act) {
+            if (sub == 0) {
+                nv = __ldg(p.norms + slot);
+                if (with_qjl) rn = __ldg(p.res_norms + node);
+            }
+            if (with_qjl) {  // six sign words per lane
+                const ulonglong2* sg =
+                    reinterpret_cast<const ulonglong2*>(p.qjl + (size_t)node * QW + 6 * sub);
 #pragma unroll
-        for (int w = 0; w < QW / 2; ++w) {
-            const ulonglong2 v = __ldg(sg + w);
-            ham += __popcll(S.qsig[2 * w] ^ v.x) + __popcll(S.qsig[2 * w + 1] ^ v.y);
+                for (int w = 0; w < 3; ++w) {
+                    const ulonglong2 v = __ldg(sg + w);
+                    ham += __popcll(S.qsig[6 * sub + 2 * w] ^ v.x) +
+                           __popcll(S.qsig[6 * sub + 2 * w + 1] ^ v.y);
+                }
+            }
         }
-        const float inv_m = __fdiv_rn(1.0f, 1536.0f);
-        const float cos_est = __fmul_rn(__fsub_rn(1536.0f, __fmul_rn(2.0f, (float)ham)), inv_m);
-        qjl_c = __fmul_rn(__fmul_rn(p.lambda, cos_est), __fmul_rn(S.qres, __ldg(p.res_norms + node)));
+        float t[12];
+        if (act) {
+            block_terms(p, S, slot, sub, t);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 12; ++i) t[i] = 0.0f;
+        }
+        float run = 0.0f;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            if (sub == s) {
+#pragma unroll
+                for (int i = 0; i < 12; ++i) run = __fadd_rn(run, t[i]);
+            }
+            run = __shfl_sync(FULL, run, (lane & ~3) | s);
+        }
+        ham += __shfl_xor_sync(FULL, ham, 1);
+        ham += __shfl_xor_sync(FULL, ham, 2);
+        if (act && sub == 0) {
+            float d = __fsub_rn(__fadd_rn(S.qn, nv), __fmul_rn(2.0f, run));
+            if (with_qjl) {
+                const float inv_m = __fdiv_rn(1.0f, 1536.0f);
+                const float cos_est =
+                    __fmul_rn(__fsub_rn(1536.0f, __fmul_rn(2.0f, (float)ham)), inv_m);
+                const float qjl_c = __fmul_rn(__fmul_rn(p.lambda, cos_est), __fmul_rn(S.qres, rn));
+                d = __fsub_rn(d, __fmul_rn(2.0f, qjl_c));
+            }
+            S.nd[j] = d;
+        }
     }
-    return __fsub_rn(d, __fmul_rn(2.0f, qjl_c));
+    __syncwarp();
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
 // --------------------------------------------------------------------- heaps --
@@ -502,7 +552,7 @@ __device__ void prologue(const Params& p, Fixed& S, const float* x, float* tmp, 
 
 // -------------------------------------------------------------------- search --
 
-__global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
+__global__ void __launch_bounds__(WARPS * 32, 4) quant_search_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t wb = warp_bytes(p.ef);
@@ -529,9 +579,13 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
 
         // upper levels
         uint32_t cur = (uint32_t)p.entry;
-        float cd = 0.0f;
-        if (lane == 0) cd = lane_dist(p, S, __ldg(p.node_slot + cur), cur, false);
-        cd = __shfl_sync(FULL, cd, 0);
+        if (lane == 0) {
+            S.ni[0] = cur;
+            S.ns[0] = __ldg(p.node_slot + cur);
+        }
+        __syncwarp();
+        score_batch(p, S, 1, false, lane);
+        float cd = S.nd[0];
         ++evals;
         for (int l = p.max_level; l >= 1; --l) {
             for (int64_t pass = 0; pass <= n; ++pass) {  // `changed` loop
@@ -542,16 +596,27 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
                 int64_t i = 0;
                 while (i < nc) {
                     if (__ldg(p.node_level + cur) < l) break;
-                    const uint32_t* urow = p.upper_links + (__ldg(p.upper_offset + cur) + l - 1) * (1 + p.M);
+                    const size_t r = (size_t)(__ldg(p.upper_offset + cur) + l - 1) * (1 + p.M);
                     const int64_t pos = i + lane;
-                    uint32_t nidx = 0xffffffffu;
-                    if (pos < nc && pos < p.M) nidx = __ldg(urow + 1 + pos);
+                    uint32_t nidx = 0xffffffffu, nslot = 0;
+                    if (pos < nc && pos < p.M) {
+                        nidx = __ldg(p.upper_links + r + 1 + pos);
+                        nslot = __ldg(p.upper_slots + r + 1 + pos);
+                    }
                     bool ok = nidx < (uint64_t)n;
                     if (ok && p.kind == kQNano && is_deleted(p.deleted, nidx)) ok = false;
-                    float d = 0.0f;
-                    if (ok) d = lane_dist(p, S, __ldg(p.node_slot + nidx), nidx, false);
-                    evals += __popc(__ballot_sync(FULL, ok)) * (lane == 0);
+                    const unsigned okm = __ballot_sync(FULL, ok);
+                    const int at = __popc(okm & ((1u << lane) - 1u));
+                    if (ok) {
+                        S.ni[at] = nidx;
+                        S.ns[at] = nslot;
+                    }
+                    __syncwarp();
+                    score_batch(p, S, __popc(okm), false, lane);
+                    const float d = ok ? S.nd[at] : 0.0f;
+                    evals += __popc(okm) * (lane == 0);
                     const unsigned better = __ballot_sync(FULL, ok && d < cd);
+                    __syncwarp();  // every lane has read its distance before the next batch
                     if (better == 0) break;  // positions past M are never scored
                     const int f = __ffs(better) - 1;
                     cd = __shfl_sync(FULL, d, f);
@@ -588,14 +653,19 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
             if (!go) break;
             cid = __shfl_sync(FULL, cid, 0);
             ++expansions;
+            // the row, its slots and the count in one round trip (a row holds 33 words)
             const uint32_t* row = p.l0_compact + (size_t)cid * 33;
             const uint32_t cnt = __ldg(row);
+            const uint32_t rn = __ldg(row + 1 + lane);
+            const uint32_t rs = __ldg(p.l0_slots + (size_t)cid * 33 + 1 + lane);
             uint32_t nidx = 0xffffffffu;
             bool ok = false;
             if ((uint32_t)lane < cnt) {
-                nidx = __ldg(row + 1 + lane);
-                ok = nidx < (uint64_t)n && !is_deleted(p.deleted, nidx) &&
-                     !((__ldcg(vis + (nidx >> 5)) >> (nidx & 31)) & 1u);
+                nidx = rn;
+                if (nidx < (uint64_t)n) {
+                    const uint32_t vw = __ldcg(vis + (nidx >> 5));
+                    ok = !is_deleted(p.deleted, nidx) && !((vw >> (nidx & 31)) & 1u);
+                }
             }
             // a node listed twice counts at its first position only
             const unsigned same = __match_any_sync(FULL, ok ? nidx : (0x80000000u | (unsigned)lane));
@@ -603,14 +673,16 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
             const unsigned keep = __ballot_sync(FULL, ok);
             if (ok) {
                 atomicOr(vis + (nidx >> 5), 1u << (nidx & 31));
-                uint32_t slot = __ldg(p.l0_slots + (size_t)cid * 33 + 1 + lane);
-                if (slot == 0xffffffffu) slot = __ldg(p.node_slot + nidx);
+                // the new neighbours are the likely next candidates: their rows towards L2
+                prefetch_l2(p.l0_compact + (size_t)nidx * 33);
+                prefetch_l2(p.l0_slots + (size_t)nidx * 33);
                 const int at = __popc(keep & ((1u << lane) - 1u));
-                S.nd[at] = lane_dist(p, S, slot, nidx, true);
                 S.ni[at] = nidx;
+                S.ns[at] = rs != 0xffffffffu ? rs : __ldg(p.node_slot + nidx);
             }
-            evals += __popc(keep) * (lane == 0);
             __syncwarp();
+            score_batch(p, S, __popc(keep), true, lane);
+            evals += __popc(keep) * (lane == 0);
             if (lane == 0) {
                 const int m = __popc(keep);
                 for (int j = 0; j < m; ++j) {
@@ -657,13 +729,24 @@ __global__ void __launch_bounds__(WARPS * 32) quant_search_kernel(Params p) {
             const int half = lane >> 4, hl = lane & 15;
             for (int b0 = 0; b0 < m; b0 += 2) {
                 const int i = b0 + half;
+                if (b0 + 2 + half < m) {  // the next pair's rows towards L2 (48 lines each)
+                    const float* nx = p.rerank + (size_t)ids[b0 + 2 + half] * DIM;
+                    for (int c = hl; c < DIM / 32; c += 16) prefetch_l2(nx + 32 * c);
+                }
                 float acc = 0.0f;
                 if (i < m) {
+                    // a lane's accumulator takes dims hl, hl + 16, ...: 32 loads in flight
                     const float* v = p.rerank + (size_t)ids[i] * DIM;
-                    for (int s = 0; s < DIM / 16; ++s) {
-                        const int d = 16 * s + hl;
-                        const float df = __fsub_rn(qv_at(x, S, d), __ldg(v + d));
-                        acc = __fadd_rn(acc, __fmul_rn(df, df));
+                    for (int g = 0; g < 3; ++g) {
+                        float vv[32];
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) vv[u] = __ldg(v + 16 * (32 * g + u) + hl);
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) {
+                            const int d = 16 * (32 * g + u) + hl;
+                            const float df = __fsub_rn(qv_at(x, S, d), vv[u]);
+                            acc = __fadd_rn(acc, __fmul_rn(df, df));
+                        }
                     }
                 }
                 float s8 = __fadd_rn(acc, __shfl_down_sync(FULL, acc, 8, 16));
@@ -745,6 +828,7 @@ int launch_quant_search(const QuantLaunch& L, cudaStream_t st) {
     p.node_level = L.node_level;
     p.upper_offset = L.upper_offset;
     p.upper_links = L.upper_links;
+    p.upper_slots = L.upper_slots;
     p.M = L.M;
     p.max_level = L.max_level;
     p.num_nodes = L.num_nodes;
