@@ -361,8 +361,9 @@ typedef struct pion_b200_hnsw_graph pion_b200_hnsw_graph;
  * src/vector/hnsw.mojo:1209-1700; format v3 to v5, plain INT8 slots, global calibration):
  * pion_v_b200_hnsw_load reads one into a host graph whose layout
  * (pion_v_b200_hnsw_graph_layout) registers with pion_v_b200_register_hnsw, so a graph the
- * engine built serves on the GPU; l0_slots is derived as _build_l0_slots does.  Quantised
- * compact formats and per-group calibration are refused (PION_B200_ESHAPE).
+ * engine built serves on the GPU; l0_slots is derived as _build_l0_slots does.  Block-
+ * quantised files (pion_v_b200_hnsw_load_quant) and per-group calibration are refused
+ * (PION_B200_ESHAPE).
  * pion_v_b200_hnsw_save writes a graph as a v5 file the engine loads (max_elements: the
  * engine's capacity, which its loader checks; 0 = the largest external id + 1). */
 int pion_v_b200_hnsw_load(const char *path, pion_b200_hnsw_graph **out_graph);
@@ -510,6 +511,20 @@ int pion_v_b200_hnsw_quantize(const pion_b200_hnsw_graph *graph, const float *ro
 int pion_v_b200_hnsw_quant_layout(const pion_b200_hnsw_quant *quant,
                                   pion_b200_hnsw_quant_layout *out_layout);
 int pion_v_b200_hnsw_quant_free(pion_b200_hnsw_quant *quant);
+
+/* The reference's index file of a block-quantised graph (pion.hnsw.0 with compact format
+ * 1 INT4, 2 INT3, 4 INT2, HNSWGraph.save_to_disk / load_from_disk,
+ * src/vector/hnsw.mojo:1209-1712): the graph, its slots and the sections the file carries
+ * (FP32 rerank rows; TurboQuant's QJL rows and residual norms; the QJL random signs are
+ * the LCG's, not stored).  *out_quant is NULL after a plain INT8 file (then the graph is
+ * what pion_v_b200_hnsw_load returns).  Per-group calibration is refused.
+ * pion_v_b200_hnsw_save_quant writes a graph with its quant buffers as a v5 file in that
+ * format (zero node norms, as the engine writes them for the block formats). */
+int pion_v_b200_hnsw_load_quant(const char *path, pion_b200_hnsw_graph **out_graph,
+                                pion_b200_hnsw_quant **out_quant);
+int pion_v_b200_hnsw_save_quant(const pion_b200_hnsw_graph *graph,
+                                const pion_b200_hnsw_quant *quant, const char *path,
+                                int64_t max_elements);
 
 /* Copies a graph (its compact_buffer is not used) and its block-quantised slots (every
  * pointer in HOST memory) to the GPU.  Checks the graph as register_hnsw does and the

@@ -91,6 +91,8 @@ SIGNATURES = {
     "pion_v_b200_hnsw_quant_layout": (_I, [_P, _P]),
     "pion_v_b200_hnsw_quant_free": (_I, [_P]),
     "pion_v_b200_register_hnsw_quant": (_I, [_P, _P, _P, _PP]),
+    "pion_v_b200_hnsw_load_quant": (_I, [ctypes.c_char_p, _P, _P]),
+    "pion_v_b200_hnsw_save_quant": (_I, [_P, _P, ctypes.c_char_p, _I64]),
     "pion_v_b200_hnsw_quant_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I]),
     "pion_v_b200_beam_forget": (_I, [_P]),
 }

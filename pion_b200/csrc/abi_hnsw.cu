@@ -114,7 +114,7 @@ int pion_v_b200_hnsw_load(const char* path, pion_b200_hnsw_graph** out_graph) {
     std::string why;
     int rc = 0;
     try {
-        rc = hnsw::load_file(path, gr->g, why);
+        rc = hnsw::load_file(path, gr->g, nullptr, why);
     } catch (const std::bad_alloc&) {
         rc = PION_B200_ENOMEM;
         why = "out of host memory";
@@ -134,7 +134,7 @@ int pion_v_b200_hnsw_save(const pion_b200_hnsw_graph* graph, const char* path,
     std::string why;
     int rc = 0;
     try {
-        rc = hnsw::save_file(graph->g, path, max_elements, why);
+        rc = hnsw::save_file(graph->g, nullptr, path, max_elements, why);
     } catch (const std::bad_alloc&) {
         rc = PION_B200_ENOMEM;
         why = "out of host memory";

@@ -138,6 +138,62 @@ int pion_v_b200_hnsw_quant_free(pion_b200_hnsw_quant* quant) {
     return 0;
 }
 
+int pion_v_b200_hnsw_load_quant(const char* path, pion_b200_hnsw_graph** out_graph,
+                                pion_b200_hnsw_quant** out_quant) {
+    if (!path || !out_graph || !out_quant) return PION_B200_EINVAL;
+    *out_graph = nullptr;
+    *out_quant = nullptr;
+    pion_b200_hnsw_graph* gr = new (std::nothrow) pion_b200_hnsw_graph();
+    pion_b200_hnsw_quant* qz = new (std::nothrow) pion_b200_hnsw_quant();
+    if (!gr || !qz) {
+        delete gr;
+        delete qz;
+        return PION_B200_ENOMEM;
+    }
+    std::string why;
+    int rc = 0;
+    try {
+        rc = hnsw::load_file(path, gr->g, &qz->q, why);
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+        why = "out of host memory";
+    }
+    if (rc != 0) {
+        fprintf(stderr, "pion_vector_b200: hnsw_load_quant %s: %s\n", path, why.c_str());
+        delete gr;
+        delete qz;
+        return rc;
+    }
+    *out_graph = gr;
+    if (qz->q.kind >= kQPolar) {
+        qz->n = gr->g.n;
+        *out_quant = qz;
+    } else {
+        delete qz;
+    }
+    return 0;
+}
+
+int pion_v_b200_hnsw_save_quant(const pion_b200_hnsw_graph* graph,
+                                const pion_b200_hnsw_quant* quant, const char* path,
+                                int64_t max_elements) {
+    if (!graph || !quant || !path) return PION_B200_EINVAL;
+    if (quant->n != graph->g.n) {
+        fprintf(stderr, "pion_vector_b200: hnsw_save_quant: quant buffers of another graph\n");
+        return PION_B200_EINVAL;
+    }
+    std::string why;
+    int rc = 0;
+    try {
+        rc = hnsw::save_file(graph->g, &quant->q, path, max_elements, why);
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+        why = "out of host memory";
+    }
+    if (rc != 0) fprintf(stderr, "pion_vector_b200: hnsw_save_quant %s: %s\n", path, why.c_str());
+    return rc;
+}
+
 int pion_v_b200_register_hnsw_quant(pion_b200_ctx* ctx, const pion_b200_hnsw_layout* L,
                                     const pion_b200_hnsw_quant_layout* Q,
                                     pion_b200_index** out_index) {

@@ -25,11 +25,16 @@
 //   further sections flagged in [25] (FP32 rerank rows of the quantised formats, QJL,
 //   prefixes, schema, long keys)
 //
+// The block-quantised formats ([22] = 1 INT4, 2 INT3, 4 INT2; slot header 0, stride
+// 868 / 676 / 484) keep their slots in the compact buffer, write zero norms, and append
+// after the key records the sections flagged in [25]: bit 0 the FP32 rerank rows
+// (num_nodes x dim f32, by node), bit 1 the QJL sign rows (num_nodes x 24 u64, by node)
+// then the residual norms (num_nodes x f32) (hnsw.mojo:1271-1284, 1421-1430, 1694-1712).
+//
 // The loader keeps what the GPU search needs (the compact slots, level-0 lists, slots,
-// ids, levels and upper-level lists) and derives l0_slots as _build_l0_slots does
-// (hnsw.mojo:2761-2786).  Quantised compact formats and per-group calibration are
-// refused: the GPU beam reads plain INT8 slots and quantises queries with the global
-// range.
+// ids, levels and upper-level lists; for the quantised formats their sections) and
+// derives l0_slots as _build_l0_slots does (hnsw.mojo:2761-2786).  Per-group calibration
+// is refused: the GPU beam quantises queries with the global range.
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -72,7 +77,7 @@ bool write_all(FILE* f, const void* src, size_t bytes) {
 
 }  // namespace
 
-int load_file(const char* path, Graph& g, std::string& why) {
+int load_file(const char* path, Graph& g, QuantBuffers* q, std::string& why) {
     File fh;
     fh.f = fopen(path, "rb");
     if (!fh.f) {
@@ -98,8 +103,19 @@ int load_file(const char* path, Graph& g, std::string& why) {
     const int64_t entry = (int64_t)h[6], max_level = (int64_t)h[7];
     const int64_t pool_per = (int64_t)h[9], max_elem = (int64_t)h[10];
     const int64_t stride = (int64_t)h[20], slot_hdr = (int64_t)h[21];
-    if (h[22] != 0) {
-        why = "quantised compact format (INT4 / INT3 / INT2) is not supported";
+    int qkind = -1;  // the block format of the slots, -1 = plain INT8
+    if (h[22] == 1)
+        qkind = kQuantPolar;
+    else if (h[22] == 2)
+        qkind = kQuantTurbo;
+    else if (h[22] == 4)
+        qkind = kQuantNano;
+    else if (h[22] != 0) {
+        why = "unknown compact format " + std::to_string(h[22]);
+        return -3;
+    }
+    if (qkind >= 0 && !q) {
+        why = "a block-quantised index (INT4 / INT3 / INT2): load it with its quant sections";
         return -3;
     }
     if (h[23] != 0) {
@@ -118,8 +134,12 @@ int load_file(const char* path, Graph& g, std::string& why) {
         why = "bad M or neighbour block size";
         return -3;
     }
-    if (slot_hdr != 8 || stride < slot_hdr + dim || stride % 16 != 0) {
+    if (qkind < 0 && (slot_hdr != 8 || stride < slot_hdr + dim || stride % 16 != 0)) {
         why = "bad slot stride or header";
+        return -3;
+    }
+    if (qkind >= 0 && (slot_hdr != 0 || stride != quant_stride(qkind))) {
+        why = "slot stride or header does not match the block format";
         return -3;
     }
     if (entry < 0 || entry >= n || max_level < 0 || max_level > 6) {
@@ -142,8 +162,10 @@ int load_file(const char* path, Graph& g, std::string& why) {
     g.max_level = (int)max_level;
     g.stride = stride;
     g.hdr = slot_hdr;
-    g.compact.resize((size_t)n * stride);
-    if (!read_all(f, g.compact.data(), g.compact.size())) {
+    if (q) *q = QuantBuffers{};
+    std::vector<int8_t>& slots = qkind >= 0 ? q->compact : g.compact;
+    slots.resize((size_t)n * stride);
+    if (!read_all(f, slots.data(), slots.size())) {
         why = "short compact buffer";
         return -1;
     }
@@ -177,7 +199,38 @@ int load_file(const char* path, Graph& g, std::string& why) {
         why = "short slot section";
         return -1;
     }
-    // the rest (norms, key records, optional sections) is not needed on the GPU
+    if (qkind >= 0) {  // zero norms, key records, then the flagged sections
+        const uint64_t sections = h[25];
+        if (!skip(f, (uint64_t)n * 8 + (uint64_t)n * 32)) {
+            why = "short norm or key sections";
+            return -1;
+        }
+        q->kind = qkind;
+        q->stride = stride;
+        if (sections & 1) {
+            q->rerank.resize((size_t)n * dim);
+            if (!read_all(f, q->rerank.data(), q->rerank.size() * 4)) {
+                why = "short FP32 rerank section";
+                return -1;
+            }
+        }
+        if (sections & 2) {
+            q->qjl.resize((size_t)n * 24);
+            q->qjl_res_norms.resize((size_t)n);
+            if (!read_all(f, q->qjl.data(), q->qjl.size() * 8) ||
+                !read_all(f, q->qjl_res_norms.data(), q->qjl_res_norms.size() * 4)) {
+                why = "short QJL section";
+                return -1;
+            }
+        }
+        if (qkind == kQuantTurbo) {  // not stored: the LCG seeded 42 (hnsw.mojo:497-509)
+            q->random_signs.resize(24);
+            qjl_random_signs(q->random_signs.data());
+        }
+    } else if (q) {
+        q->kind = -1;
+    }
+    // the rest (norms and key records of INT8 files, other sections) is not needed
 
     g.level.resize((size_t)n);
     g.node_ids.resize((size_t)n);
@@ -238,8 +291,18 @@ int load_file(const char* path, Graph& g, std::string& why) {
     return 0;
 }
 
-int save_file(const Graph& g, const char* path, int64_t max_elements, std::string& why) {
-    if (g.n <= 0 || g.compact.size() != (size_t)g.n * g.stride || g.hdr != 8) {
+int save_file(const Graph& g, const QuantBuffers* q, const char* path, int64_t max_elements,
+              std::string& why) {
+    const bool quant = q && q->kind >= kQuantPolar && q->kind <= kQuantTurbo;
+    if (quant && (g.n <= 0 || q->stride != quant_stride(q->kind) ||
+                  q->compact.size() != (size_t)g.n * q->stride ||
+                  (!q->rerank.empty() && q->rerank.size() != (size_t)g.n * g.dim) ||
+                  (!q->qjl.empty() && (q->qjl.size() != (size_t)g.n * 24 ||
+                                       q->qjl_res_norms.size() != (size_t)g.n)))) {
+        why = "quant buffers do not match the graph";
+        return -1;
+    }
+    if (!quant && (g.n <= 0 || g.compact.size() != (size_t)g.n * g.stride || g.hdr != 8)) {
         why = "graph has no compact layout";
         return -1;
     }
@@ -277,10 +340,15 @@ int save_file(const Graph& g, const char* path, int64_t max_elements, std::strin
     memcpy(reinterpret_cast<char*>(h) + 68, &g.gmax, 4);
     h[9] = (uint64_t)pool_per;
     h[10] = (uint64_t)max_elements;
-    h[20] = (uint64_t)g.stride;
-    h[21] = (uint64_t)g.hdr;
+    h[20] = (uint64_t)(quant ? q->stride : g.stride);
+    h[21] = (uint64_t)(quant ? 0 : g.hdr);
+    if (quant) {
+        h[22] = q->kind == kQuantPolar ? 1 : q->kind == kQuantTurbo ? 2 : 4;
+        h[25] = (q->rerank.empty() ? 0 : 1) | (q->qjl.empty() ? 0 : 2);
+    }
     h[24] = (uint64_t)g.metric;
-    bool ok = write_all(f, h, sizeof(h)) && write_all(f, g.compact.data(), g.compact.size());
+    const std::vector<int8_t>& slots = quant ? q->compact : g.compact;
+    bool ok = write_all(f, h, sizeof(h)) && write_all(f, slots.data(), slots.size());
     // node map up to the highest external id
     std::vector<int64_t> map((size_t)map_ids, -1);
     for (int64_t i = 0; i < n; ++i) map[(size_t)g.node_ids[i]] = i;
@@ -298,7 +366,7 @@ int save_file(const Graph& g, const char* path, int64_t max_elements, std::strin
         for (int l = 1; l <= g.level[i]; ++l) {
             const uint32_t* row = g.upper_links.data() + (size_t)(g.upper_offset[i] + l - 1) * (1 + M);
             const uint32_t cnt = row[0] > (uint32_t)M ? (uint32_t)M : row[0];
-            for (uint32_t j = 0; j < cnt; ++j) blk[2 * M + (l - 1) * M + j] = row[1 + j];
+            for (int64_t j = 0; j < M; ++j) blk[2 * M + (l - 1) * M + j] = row[1 + j];
             blk[8 * M + l] = cnt;
         }
         ok = write_all(f, blk.data(), blk.size() * 4);
@@ -308,6 +376,7 @@ int save_file(const Graph& g, const char* path, int64_t max_elements, std::strin
     for (int64_t i = 0; i < n; ++i) {
         id_level[2 * i] = g.node_ids[i];
         id_level[2 * i + 1] = g.level[i];
+        if (quant) continue;  // the block formats keep no node norms: zeros
         const int8_t* s = g.compact.data() + (size_t)g.node_slot[i] * g.stride;
         memcpy(&norms[i], s, 4);
         memcpy(&prefix[i], s + 4, 4);
@@ -317,6 +386,11 @@ int save_file(const Graph& g, const char* path, int64_t max_elements, std::strin
          write_all(f, norms.data(), (size_t)n * 4) && write_all(f, prefix.data(), (size_t)n * 4);
     std::vector<uint8_t> keys((size_t)n * 32, 0);  // no key records: the engine's slot map
     ok = ok && write_all(f, keys.data(), keys.size());
+    if (quant) {
+        ok = ok && write_all(f, q->rerank.data(), q->rerank.size() * 4);
+        ok = ok && write_all(f, q->qjl.data(), q->qjl.size() * 8) &&
+             write_all(f, q->qjl_res_norms.data(), q->qjl.empty() ? 0 : q->qjl_res_norms.size() * 4);
+    }
     if (!ok) {
         why = "write failed";
         return -1;

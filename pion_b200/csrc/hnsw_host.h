@@ -66,8 +66,11 @@ int quantize(const Graph& g, const float* rows, int kind, QuantBuffers& out, std
 
 // The reference's index file (pion.hnsw.0, format v3 to v5, src/vector/hnsw.mojo:
 // 1209-1700): load into a Graph (0, or -1 / -3 with the reason), and save a Graph as v5.
-int load_file(const char* path, Graph& g, std::string& why);
-int save_file(const Graph& g, const char* path, int64_t max_elements, std::string& why);
+// A block-quantised file needs `q` (its slots, rerank rows and QJL sections go there; kind
+// -1 after an INT8 file); save writes the block format of `q` when it has one.
+int load_file(const char* path, Graph& g, QuantBuffers* q, std::string& why);
+int save_file(const Graph& g, const QuantBuffers* q, const char* path, int64_t max_elements,
+              std::string& why);
 
 }  // namespace hnsw
 }  // namespace pion

@@ -432,10 +432,31 @@ class HNSWGraph:
         self._adopt(h)
         return self
 
-    def save(self, path: str, max_elements: int = 0):
+    @classmethod
+    def load_quant(cls, path: str):
+        """A graph and its block-quantised slots from the reference's index file (compact
+        format INT4 / INT3 / INT2 with the FP32 rerank and QJL sections it carries) ->
+        (HNSWGraph, HNSWQuant); the HNSWQuant is None for a plain INT8 file."""
+        self = cls.__new__(cls)
+        self.lib = _lib.load()
+        h, q = ctypes.c_void_p(), ctypes.c_void_p()
+        rc = self.lib.pion_v_b200_hnsw_load_quant(os.fsencode(path), ctypes.byref(h),
+                                                  ctypes.byref(q))
+        if rc != 0:
+            raise PionError(rc, f"hnsw_load_quant {path} failed")
+        self._adopt(h)
+        return self, (HNSWQuant._adopt(self.lib, q) if q.value else None)
+
+    def save(self, path: str, max_elements: int = 0, quant=None):
         """Write the graph as the reference's index file (format v5, _save_body,
-        src/vector/hnsw.mojo:1209-1440); max_elements: the engine's capacity."""
-        rc = self.lib.pion_v_b200_hnsw_save(self.h, os.fsencode(path), max_elements)
+        src/vector/hnsw.mojo:1209-1440); max_elements: the engine's capacity.  With
+        `quant` (an HNSWQuant of this graph) the file holds its block format and
+        sections instead of INT8 slots."""
+        if quant is not None:
+            rc = self.lib.pion_v_b200_hnsw_save_quant(self.h, quant.h, os.fsencode(path),
+                                                      max_elements)
+        else:
+            rc = self.lib.pion_v_b200_hnsw_save(self.h, os.fsencode(path), max_elements)
         if rc != 0:
             raise PionError(rc, f"hnsw_save {path} failed")
 
@@ -660,6 +681,15 @@ class HNSWQuant:
         self.kind = kind
         self.layout = _lib.HnswQuantLayout()
         self.lib.pion_v_b200_hnsw_quant_layout(self.h, ctypes.byref(self.layout))
+
+    @classmethod
+    def _adopt(cls, lib, h):
+        self = cls.__new__(cls)
+        self.lib, self.h = lib, h
+        self.layout = _lib.HnswQuantLayout()
+        lib.pion_v_b200_hnsw_quant_layout(h, ctypes.byref(self.layout))
+        self.kind = {v: k for k, v in QUANT_KINDS.items()}[self.layout.kind]
+        return self
 
     def arrays(self) -> dict:
         """numpy views of the buffers (valid while this object lives): kind, stride,

@@ -1,8 +1,9 @@
 """The reference's index file pion.hnsw.0 (src/vector/hnsw.mojo:1209-1700) read and written
 by the library's host code, on CPU.  A second writer restated here in Python from
 _save_body (hnsw.mojo:1209-1440) produces files the library has not written itself
-(versions 3 and 4, an index name, a larger capacity, key records), so the loader is
-checked against the format rather than against its own writer."""
+(versions 3 and 4, an index name, a larger capacity, key records, the block-quantised
+formats with their rerank and QJL sections), so the loader is checked against the format
+rather than against its own writer."""
 import os
 import struct
 
@@ -41,22 +42,35 @@ def _blocks(A):
     return blk
 
 
+QFMT = {"polar": 1, "turbo": 2, "nano": 4}
+
+
 def write_reference_file(path, A, version=5, max_elements=None, name=b"idx", groups=0,
-                         fmt=0, magic=MAGIC, truncate=None):
-    """_save_body's byte layout (hnsw.mojo:1209-1440), restated."""
-    n, M, stride = A["num_nodes"], A["M"], A["compact_stride"]
+                         fmt=0, magic=MAGIC, truncate=None, quant=None, stride=None):
+    """_save_body's byte layout (hnsw.mojo:1209-1440), restated; with `quant` (arrays of a
+    block format) the slots are the block slots (header 0), the node norms zeros, and the
+    rerank / QJL sections flagged in word 25 follow the key records (:1271-1284,
+    1421-1430)."""
+    n, M = A["num_nodes"], A["M"]
+    stride = stride or (quant["stride"] if quant is not None else A["compact_stride"])
     ids = A["node_ids"].astype(np.int64)
     max_el = max_elements or int(ids.max()) + 1
     h = np.zeros(32, np.uint64)
     h[0], h[1], h[2], h[3], h[4], h[5] = magic, version, n, A["dim"], M, 48
     h[6], h[7] = A["entry_point"], A["max_level"]
     h[9], h[10], h[11] = 8 * M + 7, max_el, len(name)
-    h[20], h[21], h[22], h[23], h[24] = stride, A["compact_hdr"], fmt, groups, A["metric"]
+    if quant is not None:
+        fmt = fmt or QFMT[quant["kind"]]
+        h[25] = (1 if quant.get("rerank") is not None else 0) | \
+            (2 if quant.get("qjl") is not None else 0)
+    h[20], h[21], h[22], h[23], h[24] = stride, 0 if quant is not None else A["compact_hdr"], \
+        fmt, groups, A["metric"]
     hb = bytearray(h.tobytes())
     hb[64:72] = struct.pack("<ff", A["global_min"], A["global_max"])
     hb[96:96 + len(name)] = name
     out = bytearray(hb)
-    out += np.ascontiguousarray(A["compact_buffer"]).tobytes()
+    out += np.ascontiguousarray(quant["compact"] if quant is not None
+                                else A["compact_buffer"]).tobytes()
     node_map = np.full(max_el if version < 4 else int(ids.max()) + 1, -1, np.int64)
     node_map[ids] = np.arange(n)
     if version >= 4:
@@ -70,15 +84,25 @@ def write_reference_file(path, A, version=5, max_elements=None, name=b"idx", gro
     idl = np.stack([ids, A["node_level"].astype(np.int64)], axis=1)
     out += idl.tobytes()
     out += np.ascontiguousarray(A["node_slot"]).tobytes()
-    comp = A["compact_buffer"].reshape(n, stride)
-    norms = comp[A["node_slot"], :8].copy().view(np.float32)
-    out += np.ascontiguousarray(norms[:, 0]).tobytes() + np.ascontiguousarray(norms[:, 1]).tobytes()
+    if quant is not None:
+        out += np.zeros(2 * n, np.float32).tobytes()
+    else:
+        comp = A["compact_buffer"].reshape(n, stride)
+        norms = comp[A["node_slot"], :8].copy().view(np.float32)
+        out += np.ascontiguousarray(norms[:, 0]).tobytes() + \
+            np.ascontiguousarray(norms[:, 1]).tobytes()
     if groups:
         out += np.zeros(2 * groups, np.float32).tobytes()
     keys = np.zeros((n, 32), np.uint8)
     keys[:, 0] = 3
     keys[:, 1:4] = np.frombuffer(b"doc", np.uint8)
     out += keys.tobytes()
+    if quant is not None:
+        if quant.get("rerank") is not None:
+            out += np.ascontiguousarray(quant["rerank"], np.float32).tobytes()
+        if quant.get("qjl") is not None:
+            out += np.ascontiguousarray(quant["qjl"], np.uint64).tobytes()
+            out += np.ascontiguousarray(quant["qjl_res_norms"], np.float32).tobytes()
     if truncate:
         out = out[:truncate]
     with open(path, "wb") as f:
@@ -138,3 +162,98 @@ def test_load_refuses(built, tmp_path, bad):
     with pytest.raises(pion_b200.PionError):
         pion_b200.HNSWGraph.load(str(tmp_path / "missing.hnsw"))
     assert not os.path.exists(str(tmp_path / "missing.hnsw"))
+
+
+# ------------------------------------------------------- block-quantised files --
+
+def _same_quant(G, Q, B, P):
+    """Graph arrays (the INT8 slot keys aside) and quant arrays equal."""
+    for k in ("num_nodes", "dim", "M", "entry_point", "max_level", "metric", "upper_rows"):
+        assert G[k] == B[k], k
+    for k in ("l0_compact", "l0_slots", "node_slot", "node_ids", "node_level", "upper_offset",
+              "upper_links"):
+        assert np.array_equal(G[k], B[k]), k
+    assert Q["kind"] == P["kind"] and Q["stride"] == P["stride"]
+    assert np.array_equal(Q["compact"], P["compact"])
+    assert np.array_equal(Q["rerank"].view(np.uint32), P["rerank"].view(np.uint32))
+    for k in ("qjl", "qjl_random_signs"):
+        assert (k in Q) == (k in P)
+        if k in Q:
+            assert np.array_equal(Q[k], P[k]), k
+    if "qjl_res_norms" in Q:
+        assert np.array_equal(Q["qjl_res_norms"].view(np.uint32),
+                              P["qjl_res_norms"].view(np.uint32))
+
+
+@pytest.mark.parametrize("kind", ["polar", "nano", "turbo"])
+def test_quant_file_round_trip(built, tmp_path, kind, oracle):
+    """A graph saved with its block slots loads back into the same graph and buffers, and
+    the restated quant search answers the same on both."""
+    import pion_b200
+    g, A, rows, qs = built
+    qz = pion_b200.HNSWQuant(g, rows, kind)
+    Q = qz.arrays()
+    p = str(tmp_path / f"{kind}.hnsw")
+    g.save(p, quant=qz)
+    with open(p, "rb") as f:
+        h = np.frombuffer(f.read(256), np.uint64)
+    assert h[22] == QFMT[kind] and h[21] == 0 and h[20] == Q["stride"]
+    assert h[25] == (3 if kind == "turbo" else 1)
+    G2, q2 = pion_b200.HNSWGraph.load_quant(p)
+    B, P = G2.arrays(), q2.arrays()
+    _same_quant(A, Q, B, P)
+    i0, s0, n0 = oracle.quant_search(A, Q, qs, 10, 32)
+    i1, s1, n1 = oracle.quant_search(B, P, qs, 10, 32)
+    assert np.array_equal(i0, i1) and np.array_equal(s0.view(np.uint32), s1.view(np.uint32))
+    with pytest.raises(pion_b200.PionError) as e:  # the INT8 loader refuses it
+        pion_b200.HNSWGraph.load(p)
+    assert e.value.code == -3
+
+
+@pytest.mark.parametrize("kind", ["polar", "turbo"])
+def test_quant_file_reference_layout(built, tmp_path, kind):
+    """Files in the reference's layout with block slots (restated writer) load into the
+    library's graph and buffers; without sections the buffers stay empty."""
+    import pion_b200
+    g, A, rows, qs = built
+    qz = pion_b200.HNSWQuant(g, rows, kind)
+    Q = qz.arrays()
+    p = str(tmp_path / f"ref_{kind}.hnsw")
+    write_reference_file(p, A, quant=Q, max_elements=4000)
+    G2, q2 = pion_b200.HNSWGraph.load_quant(p)
+    _same_quant(A, Q, G2.arrays(), q2.arrays())
+    bare = {"kind": kind, "stride": Q["stride"], "compact": Q["compact"]}
+    write_reference_file(p, A, quant=bare, version=4)
+    G3, q3 = pion_b200.HNSWGraph.load_quant(p)
+    P3 = q3.arrays()
+    assert P3["rerank"] is None and "qjl" not in P3
+    assert np.array_equal(P3["compact"], Q["compact"])
+    # a plain INT8 file through the same call: no quant buffers
+    write_reference_file(p, A)
+    G5, q5 = pion_b200.HNSWGraph.load_quant(p)
+    assert q5 is None
+    _same_graph(A, G5.arrays())
+
+
+@pytest.mark.parametrize("bad", ["two_formats", "stride", "truncated_qjl", "truncated_rerank"])
+def test_quant_file_refuses(built, tmp_path, bad):
+    import pion_b200
+    g, A, rows, qs = built
+    qz = pion_b200.HNSWQuant(g, rows, "turbo")
+    Q = qz.arrays()
+    p = str(tmp_path / "bad.hnsw")
+    n = A["num_nodes"]
+    kw = {"two_formats": dict(fmt=3), "stride": dict(stride=868),
+          "truncated_qjl": dict(truncate=-(n * 4 + 100)),  # inside the QJL rows
+          "truncated_rerank": dict(truncate=-(n * 196 + 100))}[bad]
+    if "truncate" in kw:
+        write_reference_file(p, A, quant=Q)
+        with open(p, "rb") as f:
+            data = f.read()
+        with open(p, "wb") as f:
+            f.write(data[:len(data) + kw["truncate"]])
+    else:
+        write_reference_file(p, A, quant=Q, **kw)
+    with pytest.raises(pion_b200.PionError) as e:
+        pion_b200.HNSWGraph.load_quant(p)
+    assert e.value.code in (-1, -3)

@@ -4,7 +4,8 @@ INT4, NanoQuant INT2 and TurboQuant INT3 + QJL, the beam over MinHeap / MaxHeap
 (src/vector/reference/quant_beams_1536.mojo:20-81, src/common/heap.mojo) and the FP32
 rerank tail (hnsw.mojo:4052-4134).  Covers both metrics, ef below / equal to / above k,
 ef = 1, no rerank rows, deleted nodes, candidate heaps that outgrow their first-pass
-room (the re-run launch), several queries per warp, and device memory."""
+room (the re-run launch), several queries per warp, device memory, and a graph served from
+the reference's index file in a block format."""
 import numpy as np
 import pytest
 
@@ -143,4 +144,19 @@ def test_quant_search_refuses(ctx, graphs):
     with pytest.raises(pion_b200.PionError):
         pion_b200.HNSWQuantIndex(ctx, g, Q)
     hx.free()
+    ix.free()
+
+
+@pytest.mark.parametrize("kind", ["nano", "turbo"])
+def test_quant_search_from_index_file(ctx, oracle, graphs, kind, tmp_path):
+    """A block-quantised index file (pion.hnsw.0 with its rerank and QJL sections) loads
+    and serves on the GPU with the oracle's answers."""
+    import pion_b200
+    g, A, rows, qs = graphs["cosine"]
+    qz = pion_b200.HNSWQuant(g, rows, kind)
+    p = str(tmp_path / "pion.hnsw.0")
+    g.save(p, quant=qz)
+    G2, q2 = pion_b200.HNSWGraph.load_quant(p)
+    ix = pion_b200.HNSWQuantIndex(ctx, G2, q2)
+    _same(ix.search(qs, 10, 64), oracle.quant_search(G2.arrays(), q2.arrays(), qs, 10, 64))
     ix.free()
