@@ -150,13 +150,75 @@ typedef struct pion_beam_view_1536 {
  * a message on stderr. */
 int64_t pion_v_beam_1536(pion_beam_view_1536 *view);
 
-/* src/vector/vector_abi.mojo:40-46 (quant_beam_search_1536) -> the quantised beams (INT4 / INT3+QJL / INT2,
- * src/vector/reference/quant_beams_1536.mojo): not implemented on the GPU; returns -1 and
- * prints a message (the caller's pool is left unchanged). */
-int64_t pion_v_quant_beam_1536(void *view);
+/* src/common/heap.mojo:6-30, 48-56, 237-241: HeapNode (f32 distance, Int id), and the
+ * List[HeapNode] MinHeap and MaxHeap keep (the Mojo List's fields: data, length,
+ * capacity), MaxHeap's cached worst distance after it. */
+typedef struct pion_heap_node {
+    float distance;
+    int32_t pad;
+    int64_t id;
+} pion_heap_node;
 
-/* Drops the GPU copy of a graph registered by pion_v_beam_1536 (all of them when
- * l0_compact is NULL). */
+typedef struct pion_heap_list {
+    pion_heap_node *data;
+    int64_t len;
+    int64_t capacity;
+} pion_heap_list;
+
+typedef struct pion_min_heap {
+    pion_heap_list data;
+} pion_min_heap;
+
+typedef struct pion_max_heap {
+    pion_heap_list data;
+    float cached_worst;
+    int32_t pad;
+} pion_max_heap;
+
+/* src/vector/quant_beam_view.mojo:22-47: QuantBeamView1536's fields, in order. */
+typedef struct pion_quant_beam_view_1536 {
+    int64_t kind; /* 0 PolarQuant INT4, 1 NanoQuant INT2, 2 TurboQuant INT3 + QJL */
+    int64_t ef;
+    pion_min_heap *candidates;
+    pion_max_heap *results;
+    const int8_t *query_block_int8;   /* 1536 codes          */
+    const float *query_block_scales;  /* 48 block scales     */
+    float query_block_norm;
+    const uint32_t *l0_compact;
+    const uint32_t *l0_slots;
+    int64_t num_nodes;
+    const uint8_t *deleted;
+    uint16_t *visited;
+    uint16_t cur_epoch;
+    const int8_t *compact_buffer;
+    int64_t compact_stride;
+    int64_t compact_hdr;
+    const void *nodes;
+    const uint64_t *qjl_buffer;       /* num_nodes x 24, by node */
+    const float *qjl_res_norms;       /* num_nodes, by node      */
+    const uint64_t *qjl_query_signs;  /* 24                      */
+    float qjl_query_res_norm;
+    float qjl_lambda;
+} pion_quant_beam_view_1536;
+
+/* src/vector/vector_abi.mojo:40-46 (quant_beam_search_1536) -> quant_beam_search_1536_ref
+ * (src/vector/reference/quant_beams_1536.mojo:20-81): the level-0 beam of one query over
+ * the block-quantised slots, on the GPU.  Starts from the view's heaps (as the block-quant
+ * branches of search_fp32_scored seed them: the start node in both, marked visited; the
+ * nodes in the heaps count as visited), runs the beam over MinHeap / MaxHeap exactly as
+ * the reference does, and writes both heaps back array for array (the results heap and
+ * its cached worst in full; the candidates heap up to its List's capacity, a prefix of a
+ * binary heap being a heap: the engine clears it before its next use and a C library
+ * cannot grow a Mojo List).  The graph (l0_compact, l0_slots, the slots at compact_buffer
+ * + slot * compact_stride + compact_hdr, the QJL rows) is copied to the GPU on the first
+ * call for those buffers and reused while the same pointers and sizes come back
+ * (pion_v_b200_beam_forget drops it).  Every l0_slots entry of a listed node must name a
+ * slot (the nodes' own vector pointers are not read).  The visited array is not written.
+ * Returns 0, or a negative code with a message on stderr (the heaps are then unchanged). */
+int64_t pion_v_quant_beam_1536(pion_quant_beam_view_1536 *view);
+
+/* Drops the GPU copy of a graph registered by pion_v_beam_1536 or pion_v_quant_beam_1536
+ * (all of them when l0_compact is NULL). */
 int pion_v_b200_beam_forget(const uint32_t *l0_compact);
 
 /* ==================================================================== group 2 */

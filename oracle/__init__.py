@@ -526,6 +526,9 @@ def _qlib():
         L.orc_turbo_qjl_row.restype = ctypes.c_float
         L.orc_quant_search.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p, _p, ctypes.c_int]
         L.orc_quant_search.restype = ctypes.c_int
+        L.orc_quant_beam_heaps.argtypes = [_p, _p, _p, ctypes.c_float, _p, ctypes.c_float, _i64,
+                                           _p, _p, _p, _i64, _p, _p, _p, _p, _p]
+        L.orc_quant_beam_heaps.restype = ctypes.c_int
         L._quant_bound = True
     return L
 
@@ -607,10 +610,8 @@ def quant_graph(graph: dict, rows, kind: str, rerank: bool = True):
     return out
 
 
-def quant_search(graph: dict, quant: dict, queries, k: int, ef: int, nthreads: int | None = None):
-    """search_fp32_scored's block-quant branch (src/vector/hnsw.mojo:4136-4330) with the
-    shared FP32 rerank tail -> (external ids [nq, k], scores [nq, k], counts [nq])."""
-    L = _qlib()
+def _quant_layout(graph: dict, quant: dict):
+    """(orc_quant_layout, keep-alive list) of a graph dict and a quant dict."""
     keep = []
 
     def ptr(a, dt):
@@ -640,6 +641,14 @@ def quant_search(graph: dict, quant: dict, queries, k: int, ef: int, nthreads: i
     lay.qjl_random_signs = ptr(quant.get("qjl_random_signs"), np.uint64)
     lay.qjl_lambda = quant.get("qjl_lambda", 1.0)
     lay.rerank = ptr(quant.get("rerank"), np.float32)
+    return lay, keep
+
+
+def quant_search(graph: dict, quant: dict, queries, k: int, ef: int, nthreads: int | None = None):
+    """search_fp32_scored's block-quant branch (src/vector/hnsw.mojo:4136-4330) with the
+    shared FP32 rerank tail -> (external ids [nq, k], scores [nq, k], counts [nq])."""
+    L = _qlib()
+    lay, keep = _quant_layout(graph, quant)
     q, pq = _c(np.atleast_2d(queries), np.float32)
     nq = q.shape[0]
     ids = np.empty((nq, k), np.int32)
@@ -652,3 +661,38 @@ def quant_search(graph: dict, quant: dict, queries, k: int, ef: int, nthreads: i
         raise RuntimeError("orc_quant_search failed")
     del keep
     return ids, sc, cnt
+
+
+def quant_beam_heaps(graph: dict, quant: dict, qcodes, qscales, qnorm, qsig, qres, ef: int,
+                     cand, res, worst, cand_cap: int | None = None):
+    """quant_beam_search_1536_ref on a view's state: the query (codes, scales, |q|^2, QJL
+    signs or None, residual norm) and the heaps as lists of (distance, node) in array order
+    (their nodes visited) -> (candidates [up to cand_cap], the whole candidate count,
+    results, results' cached worst)."""
+    L = _qlib()
+    lay, keep = _quant_layout(graph, quant)
+    n = graph["num_nodes"] + len(cand) + 1
+    cap = n if cand_cap is None else cand_cap
+    cd = np.zeros(max(n, len(cand)), np.float32)
+    ci = np.zeros(max(n, len(cand)), np.int64)
+    for i, (d, j) in enumerate(cand):
+        cd[i], ci[i] = d, j
+    rd = np.zeros(max(ef, len(res)) + 1, np.float32)
+    ri = np.zeros(max(ef, len(res)) + 1, np.int64)
+    for i, (d, j) in enumerate(res):
+        rd[i], ri[i] = d, j
+    cn, rn, tot = ctypes.c_int64(len(cand)), ctypes.c_int64(len(res)), ctypes.c_int64(0)
+    w = ctypes.c_float(worst)
+    qc, pqc = _c(qcodes, np.int8)
+    qs_, pqs = _c(qscales, np.float32)
+    sig = None if qsig is None else np.ascontiguousarray(qsig, np.uint64)
+    rc = L.orc_quant_beam_heaps(ctypes.byref(lay), pqc, pqs, float(qnorm),
+                                None if sig is None else sig.ctypes.data_as(_p), float(qres), ef,
+                                cd.ctypes.data_as(_p), ci.ctypes.data_as(_p), ctypes.byref(cn),
+                                cap, ctypes.byref(tot), rd.ctypes.data_as(_p),
+                                ri.ctypes.data_as(_p), ctypes.byref(rn), ctypes.byref(w))
+    if rc != 0:
+        raise RuntimeError("orc_quant_beam_heaps failed")
+    del keep
+    return ([(cd[i], int(ci[i])) for i in range(cn.value)], tot.value,
+            [(rd[i], int(ri[i])) for i in range(rn.value)], np.float32(w.value))

@@ -470,14 +470,9 @@ static float qdist(const orc_quant_layout *L, const qctx *Q, const int8_t *v, in
     return ((Q->qn + norm_v) - 2.0f * dot) - 2.0f * qjl_c;
 }
 
-/* The level-0 beam (quant_beams_1536.mojo:20-81) from (start, start_d). */
-static int quant_beam(const orc_quant_layout *L, const qctx *Q, int64_t start, float start_d,
-                      int64_t ef, uint8_t *visited, heap *cand, heap *res) {
-    cand->n = 0;
-    res->n = 0;
-    res->worst = -1e30f;
-    if (min_push(cand, start_d, start) || max_push(res, start_d, start)) return -1;
-    visited[start] = 1;
+/* The level-0 beam loop (quant_beams_1536.mojo:20-81) over heaps already seeded. */
+static int quant_beam_run(const orc_quant_layout *L, const qctx *Q, int64_t ef,
+                          uint8_t *visited, heap *cand, heap *res) {
     const int64_t n = L->num_nodes;
     while (cand->n > 0) {
         const hnode c = min_pop(cand);
@@ -499,6 +494,72 @@ static int quant_beam(const orc_quant_layout *L, const qctx *Q, int64_t start, f
         }
     }
     return 0;
+}
+
+/* The beam from (start, start_d), as the block-quant branches seed it. */
+static int quant_beam(const orc_quant_layout *L, const qctx *Q, int64_t start, float start_d,
+                      int64_t ef, uint8_t *visited, heap *cand, heap *res) {
+    cand->n = 0;
+    res->n = 0;
+    res->worst = -1e30f;
+    if (min_push(cand, start_d, start) || max_push(res, start_d, start)) return -1;
+    visited[start] = 1;
+    return quant_beam_run(L, Q, ef, visited, cand, res);
+}
+
+/* quant_beam_search_1536_ref on a view's state: the query as codes, scales, |q|^2 and
+ * QJL signs (qsig NULL: none), the heaps given as arrays (their nodes visited), both
+ * written back with their sizes (candidates up to cand_cap entries; *cand_total = the
+ * whole heap's size) and the results' cached worst. */
+int orc_quant_beam_heaps(const orc_quant_layout *L, const int8_t *qc, const float *qs,
+                         float qn, const uint64_t *qsig, float qres, int64_t ef, float *cand_d,
+                         int64_t *cand_id, int64_t *cand_n, int64_t cand_cap,
+                         int64_t *cand_total, float *res_d, int64_t *res_id, int64_t *res_n,
+                         float *worst) {
+    qctx *Q = (qctx *)calloc(1, sizeof(qctx));
+    uint8_t *visited = (uint8_t *)calloc((size_t)L->num_nodes, 1);
+    heap cand = {0}, res = {0};
+    int rc = -1;
+    if (!Q || !visited) goto out;
+    memcpy(Q->qc, qc, QD);
+    memcpy(Q->qs, qs, QB * sizeof(float));
+    Q->qn = qn;
+    if (qsig) memcpy(Q->qsig, qsig, QW * sizeof(uint64_t));
+    Q->qres = qres;
+    Q->has_qjl = L->kind == ORC_QUANT_TURBO && L->qjl && L->qjl_res_norms;
+    for (int64_t i = 0; i < *cand_n; ++i) {
+        if (heap_grow(&cand)) goto out;
+        cand.a[cand.n].d = cand_d[i];
+        cand.a[cand.n++].id = cand_id[i];
+        visited[cand_id[i]] = 1;
+    }
+    for (int64_t i = 0; i < *res_n; ++i) {
+        if (heap_grow(&res)) goto out;
+        res.a[res.n].d = res_d[i];
+        res.a[res.n++].id = res_id[i];
+        visited[res_id[i]] = 1;
+    }
+    res.worst = *worst;
+    if (quant_beam_run(L, Q, ef, visited, &cand, &res)) goto out;
+    *cand_total = cand.n;
+    *cand_n = cand.n < cand_cap ? cand.n : cand_cap;
+    for (int64_t i = 0; i < *cand_n; ++i) {
+        cand_d[i] = cand.a[i].d;
+        cand_id[i] = cand.a[i].id;
+    }
+    *res_n = res.n;
+    for (int64_t i = 0; i < res.n; ++i) {
+        res_d[i] = res.a[i].d;
+        res_id[i] = res.a[i].id;
+    }
+    *worst = res.worst;
+    rc = 0;
+out:
+    free(cand.a);
+    free(res.a);
+    free(visited);
+    free(Q);
+    return rc;
 }
 
 /* The upper-level greedy of the block-quant branches (hnsw.mojo:4158-4188, 4220-4246,

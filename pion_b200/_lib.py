@@ -135,6 +135,40 @@ class BeamView1536(ctypes.Structure):
                 ("nodes", ctypes.c_void_p)]
 
 
+class HeapNode(ctypes.Structure):
+    """pion_heap_node (include/pion_vector_b200.h): HeapNode's layout."""
+    _fields_ = [("distance", ctypes.c_float), ("pad", ctypes.c_int32), ("id", ctypes.c_int64)]
+
+
+class HeapList(ctypes.Structure):
+    """pion_heap_list: the List[HeapNode] of MinHeap / MaxHeap (data, length, capacity)."""
+    _fields_ = [("data", ctypes.c_void_p), ("len", ctypes.c_int64), ("capacity", ctypes.c_int64)]
+
+
+class MinHeap(ctypes.Structure):
+    _fields_ = [("data", HeapList)]
+
+
+class MaxHeap(ctypes.Structure):
+    _fields_ = [("data", HeapList), ("cached_worst", ctypes.c_float), ("pad", ctypes.c_int32)]
+
+
+class QuantBeamView1536(ctypes.Structure):
+    """pion_quant_beam_view_1536 (include/pion_vector_b200.h): QuantBeamView1536's fields
+    in order."""
+    _fields_ = [("kind", ctypes.c_int64), ("ef", ctypes.c_int64),
+                ("candidates", ctypes.POINTER(MinHeap)), ("results", ctypes.POINTER(MaxHeap)),
+                ("query_block_int8", ctypes.c_void_p), ("query_block_scales", ctypes.c_void_p),
+                ("query_block_norm", ctypes.c_float), ("l0_compact", ctypes.c_void_p),
+                ("l0_slots", ctypes.c_void_p), ("num_nodes", ctypes.c_int64),
+                ("deleted", ctypes.c_void_p), ("visited", ctypes.c_void_p),
+                ("cur_epoch", ctypes.c_uint16), ("compact_buffer", ctypes.c_void_p),
+                ("compact_stride", ctypes.c_int64), ("compact_hdr", ctypes.c_int64),
+                ("nodes", ctypes.c_void_p), ("qjl_buffer", ctypes.c_void_p),
+                ("qjl_res_norms", ctypes.c_void_p), ("qjl_query_signs", ctypes.c_void_p),
+                ("qjl_query_res_norm", ctypes.c_float), ("qjl_lambda", ctypes.c_float)]
+
+
 class HnswLayout(ctypes.Structure):
     """pion_b200_hnsw_layout (include/pion_vector_b200.h)."""
     _fields_ = [

@@ -801,15 +801,8 @@ int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
     return 0;
 }
 
-int64_t pion_v_quant_beam_1536(void* view) {
-    (void)view;
-    fprintf(stderr,
-            "pion_vector_b200: pion_v_quant_beam_1536: the quantised beams (INT4/INT3/INT2) "
-            "are not implemented on the GPU\n");
-    return -1;
-}
-
 int pion_v_b200_beam_forget(const uint32_t* l0_compact) {
+    quant_beam_forget(l0_compact);
     std::lock_guard<std::mutex> lock(g_beam_mu);
     std::vector<BeamGraph*> keep;
     for (BeamGraph* g : g_beam_graphs) {

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -82,9 +83,278 @@ const char* check_quant(const pion_b200_hnsw_quant_layout* Q, int64_t n) {
     return nullptr;
 }
 
+// Graphs registered by pion_v_quant_beam_1536, keyed by the view's host buffers.
+struct QuantBeamGraph {
+    const uint32_t* l0c;
+    const uint32_t* l0s;
+    const int8_t* comp;
+    const uint64_t* qjl;
+    const float* qres;
+    int64_t n, stride, hdr;
+    int kind, device;
+    float* norms = nullptr;
+    uint16_t* scales = nullptr;
+    uint8_t* codes = nullptr;
+    uint32_t* l0_compact = nullptr;
+    uint32_t* l0_slots = nullptr;
+    uint64_t* qjl_dev = nullptr;
+    float* qres_dev = nullptr;
+};
+std::mutex g_qbeam_mu;
+std::vector<QuantBeamGraph*> g_qbeam_graphs;
+
+void free_qbeam_graph(QuantBeamGraph* g) {
+    cudaSetDevice(g->device);
+    cudaDeviceSynchronize();
+    void* ps[] = {g->norms, g->scales, g->codes, g->l0_compact, g->l0_slots, g->qjl_dev,
+                  g->qres_dev};
+    for (void* p : ps)
+        if (p) cudaFree(p);
+    delete g;
+}
+
+int qbeam_fail(const char* what) {
+    fprintf(stderr, "pion_vector_b200: pion_v_quant_beam_1536: %s\n", what);
+    return -1;
+}
+
+// The registered copy of the view's graph (checked and copied on first use).
+QuantBeamGraph* qbeam_graph(pion_b200_ctx* ctx, const pion_quant_beam_view_1536* v,
+                            const char** why) {
+    std::lock_guard<std::mutex> lock(g_qbeam_mu);
+    for (QuantBeamGraph* g : g_qbeam_graphs)
+        if (g->l0c == v->l0_compact && g->l0s == v->l0_slots && g->comp == v->compact_buffer &&
+            g->qjl == v->qjl_buffer && g->qres == v->qjl_res_norms && g->n == v->num_nodes &&
+            g->stride == v->compact_stride && g->hdr == v->compact_hdr && g->kind == v->kind &&
+            g->device == ctx->device)
+            return g;
+    const int64_t n = v->num_nodes;
+    const int kind = (int)v->kind;
+    const int bb = block_bytes(kind), cb = bb - 2, cbytes = code_bytes(kind);
+    if (v->compact_hdr < 0 || v->compact_stride < v->compact_hdr + stride_of(kind)) {
+        *why = "compact stride too small for the block format";
+        return nullptr;
+    }
+    for (int64_t i = 0; i < n; ++i) {  // every listed neighbour names a slot
+        const uint32_t* row = v->l0_compact + i * 33;
+        if (row[0] > 32u) {
+            *why = "a level-0 count above 32";
+            return nullptr;
+        }
+        for (uint32_t k = 0; k < row[0]; ++k)
+            if (row[1 + k] < (uint32_t)n && v->l0_slots[i * 33 + 1 + k] >= (uint32_t)n) {
+                *why = "an l0_slots entry names no slot";
+                return nullptr;
+            }
+    }
+    QuantBeamGraph* g = new (std::nothrow) QuantBeamGraph{
+        v->l0_compact, v->l0_slots, v->compact_buffer, v->qjl_buffer, v->qjl_res_norms, n,
+        v->compact_stride, v->compact_hdr, kind, ctx->device};
+    if (!g) {
+        *why = "out of host memory";
+        return nullptr;
+    }
+    int rc = 0;
+    try {
+        std::vector<float> norms((size_t)n);
+        std::vector<uint16_t> scales((size_t)n * kBlocks);
+        std::vector<uint8_t> codes((size_t)n * cbytes);
+        for (int64_t sl = 0; sl < n; ++sl) {
+            const int8_t* src = v->compact_buffer + sl * v->compact_stride + v->compact_hdr;
+            std::memcpy(&norms[sl], src, 4);
+            for (int b = 0; b < kBlocks; ++b) {
+                std::memcpy(&scales[sl * kBlocks + b], src + 4 + b * bb, 2);
+                std::memcpy(&codes[sl * cbytes + (size_t)b * cb], src + 4 + b * bb + 2, (size_t)cb);
+            }
+        }
+        rc = upload(&g->norms, norms.data(), norms.size());
+        if (!rc) rc = upload(&g->scales, scales.data(), scales.size());
+        if (!rc) rc = upload(&g->codes, codes.data(), codes.size());
+    } catch (const std::bad_alloc&) {
+        rc = PION_B200_ENOMEM;
+    }
+    if (!rc) rc = upload(&g->l0_compact, v->l0_compact, (size_t)n * 33);
+    if (!rc) rc = upload(&g->l0_slots, v->l0_slots, (size_t)n * 33);
+    if (!rc && kind == kQTurbo && v->qjl_buffer && v->qjl_res_norms) {
+        rc = upload(&g->qjl_dev, v->qjl_buffer, (size_t)n * 24);
+        if (!rc) rc = upload(&g->qres_dev, v->qjl_res_norms, (size_t)n);
+    }
+    if (rc) {
+        free_qbeam_graph(g);
+        *why = "device copy of the graph failed";
+        return nullptr;
+    }
+    g_qbeam_graphs.push_back(g);
+    return g;
+}
+
 }  // namespace
 
+void pion::quant_beam_forget(const uint32_t* l0_compact) {
+    std::lock_guard<std::mutex> lock(g_qbeam_mu);
+    std::vector<QuantBeamGraph*> keep;
+    for (QuantBeamGraph* g : g_qbeam_graphs) {
+        if (!l0_compact || g->l0c == l0_compact)
+            free_qbeam_graph(g);
+        else
+            keep.push_back(g);
+    }
+    g_qbeam_graphs.swap(keep);
+}
+
 extern "C" {
+
+int64_t pion_v_quant_beam_1536(pion_quant_beam_view_1536* v) {
+    if (!v || !v->candidates || !v->results || !v->query_block_int8 || !v->query_block_scales ||
+        !v->l0_compact || !v->l0_slots || !v->compact_buffer || v->num_nodes <= 0 ||
+        v->num_nodes >= 0x7fffffff)
+        return qbeam_fail("bad view");
+    if (v->kind < kQPolar || v->kind > kQTurbo) return qbeam_fail("unknown block format");
+    const int64_t ef = v->ef < 1 ? 1 : v->ef;
+    if (ef > quant_top_entries()) return qbeam_fail("ef above 1024");
+    const int64_t n = v->num_nodes;
+    pion_heap_list& cl = v->candidates->data;
+    pion_heap_list& rl = v->results->data;
+    if (cl.len < 0 || cl.capacity < cl.len || (cl.len > 0 && !cl.data) || rl.len < 0 ||
+        rl.len > ef || rl.capacity < rl.len || (rl.len > 0 && !rl.data))
+        return qbeam_fail("bad heaps");
+    if (cl.len > n + 1) return qbeam_fail("more candidates than nodes");
+    for (int64_t i = 0; i < cl.len; ++i)
+        if (cl.data[i].id < 0 || cl.data[i].id >= n) return qbeam_fail("a heap entry names no node");
+    for (int64_t i = 0; i < rl.len; ++i)
+        if (rl.data[i].id < 0 || rl.data[i].id >= n) return qbeam_fail("a heap entry names no node");
+    if (rl.len > 0 && rl.capacity < ef && rl.capacity < rl.len + 1)
+        ;  // the results heap never grows past max(len, ef): checked below after the run
+    pion_b200_ctx* ctx = compat_default_ctx("pion_v_quant_beam_1536");
+    if (!ctx) return -1;
+    if (use_device(ctx) != 0) return qbeam_fail("cannot select the device");
+    const char* why = "";
+    QuantBeamGraph* g = qbeam_graph(ctx, v, &why);
+    if (!g) return qbeam_fail(why);
+    const int per_sm = quant_ctas_per_sm((int)ef);
+    if (per_sm <= 0) return qbeam_fail("ef does not fit");
+    cudaStream_t st = ctx->stream;
+    const int64_t cand_io_cap = cl.capacity > 0 ? cl.capacity : 1;
+    const size_t del_bytes = v->deleted ? (size_t)(n + 7) / 8 : 0;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += align_up(bytes, 256);
+        return o;
+    };
+    const size_t o_codes = take(kDim), o_scales = take(kBlocks * 4), o_norms = take(8),
+                 o_signs = take(24 * 8), o_meta = take(6 * 4), o_del = take(del_bytes),
+                 o_cand = take((size_t)cand_io_cap * 8), o_res = take((size_t)ef * 8),
+                 o_q = take(kDim * 4);
+    const int warps = quant_warps_per_cta(), top = quant_top_entries();
+    const int64_t vis_words = ((n + 31) / 32 + 3) / 4 * 4;
+    const int64_t cap = n + cl.len + 1;
+    const size_t tail = (size_t)warps * (size_t)std::max<int64_t>(cap - top, 0) * 8;
+    if (ensure(ctx->stage_in, off) != 0 || ensure(ctx->hnsw_misc, 64) != 0 ||
+        ensure(ctx->hnsw_visited, (size_t)warps * vis_words * 4) != 0 ||
+        ensure(ctx->scratch2, tail > 0 ? tail : 16) != 0)
+        return qbeam_fail("out of device memory");
+    char* base = static_cast<char*>(ctx->stage_in.ptr);
+    // host side of the copies: the heaps as (f32 dist, u32 node) entries, the scalars
+    std::vector<uint32_t> cand_h((size_t)cand_io_cap * 2), res_h((size_t)ef * 2);
+    for (int64_t i = 0; i < cl.len; ++i) {
+        std::memcpy(&cand_h[2 * i], &cl.data[i].distance, 4);
+        cand_h[2 * i + 1] = (uint32_t)cl.data[i].id;
+    }
+    for (int64_t i = 0; i < rl.len; ++i) {
+        std::memcpy(&res_h[2 * i], &rl.data[i].distance, 4);
+        res_h[2 * i + 1] = (uint32_t)rl.data[i].id;
+    }
+    int32_t meta[6] = {(int32_t)cl.len, (int32_t)rl.len, 0, 0, 0, 0};
+    std::memcpy(&meta[2], &v->results->cached_worst, 4);
+    const float norms2[2] = {v->query_block_norm, v->qjl_query_res_norm};
+    bool ok =
+        cudaMemcpyAsync(base + o_codes, v->query_block_int8, kDim, cudaMemcpyHostToDevice, st) ==
+            cudaSuccess &&
+        cudaMemcpyAsync(base + o_scales, v->query_block_scales, kBlocks * 4,
+                        cudaMemcpyHostToDevice, st) == cudaSuccess &&
+        cudaMemcpyAsync(base + o_norms, norms2, 8, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+        (!v->qjl_query_signs || cudaMemcpyAsync(base + o_signs, v->qjl_query_signs, 24 * 8,
+                                                cudaMemcpyHostToDevice, st) == cudaSuccess) &&
+        cudaMemcpyAsync(base + o_meta, meta, sizeof(meta), cudaMemcpyHostToDevice, st) ==
+            cudaSuccess &&
+        (!del_bytes || cudaMemcpyAsync(base + o_del, v->deleted, del_bytes,
+                                       cudaMemcpyHostToDevice, st) == cudaSuccess) &&
+        (cl.len == 0 || cudaMemcpyAsync(base + o_cand, cand_h.data(), (size_t)cl.len * 8,
+                                        cudaMemcpyHostToDevice, st) == cudaSuccess) &&
+        (rl.len == 0 || cudaMemcpyAsync(base + o_res, res_h.data(), (size_t)rl.len * 8,
+                                        cudaMemcpyHostToDevice, st) == cudaSuccess) &&
+        cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 64, st) == cudaSuccess;
+    if (!ok) return qbeam_fail("copy to the device failed");
+    unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
+    QuantLaunch Lc;
+    Lc.kind = (int)v->kind;
+    Lc.metric = 0;
+    Lc.codes = g->codes;
+    Lc.code_bytes = code_bytes((int)v->kind);
+    Lc.scales = g->scales;
+    Lc.norms = g->norms;
+    Lc.qjl = g->qjl_dev;
+    Lc.res_norms = g->qres_dev;
+    Lc.lambda = v->qjl_lambda;
+    Lc.l0_compact = g->l0_compact;
+    Lc.l0_slots = g->l0_slots;
+    Lc.deleted = del_bytes ? reinterpret_cast<const uint8_t*>(base + o_del) : nullptr;
+    Lc.num_nodes = n;
+    Lc.queries = reinterpret_cast<const float*>(base + o_q);  // not read in this mode
+    Lc.nq = 1;
+    Lc.k = 1;
+    Lc.ef = (int)ef;
+    Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+    Lc.vis_words = vis_words;
+    Lc.cand_tail = ctx->scratch2.ptr;
+    Lc.cand_cap = cap;
+    Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
+    Lc.stats = stats;
+    Lc.status = ctx->d_status;
+    Lc.ctas = 1;
+    Lc.from_heaps = 1;
+    Lc.given_codes = reinterpret_cast<const int8_t*>(base + o_codes);
+    Lc.given_scales = reinterpret_cast<const float*>(base + o_scales);
+    Lc.given_norms = reinterpret_cast<const float*>(base + o_norms);
+    Lc.given_signs = v->qjl_query_signs ? reinterpret_cast<const uint64_t*>(base + o_signs)
+                                        : nullptr;
+    Lc.cand_io = base + o_cand;
+    Lc.cand_io_cap = cand_io_cap;
+    Lc.res_io = base + o_res;
+    Lc.heap_meta = reinterpret_cast<int*>(base + o_meta);
+    if (launch_quant_search(Lc, st) != 0) return qbeam_fail("launch failed");
+    ctx->launches++;
+    if (cudaMemcpyAsync(meta, base + o_meta, sizeof(meta), cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return qbeam_fail("copy from the device failed");
+    const int32_t cn = meta[3], rn = meta[4];
+    if (cn < 0 || rn < 0 || rn > ef) return qbeam_fail("bad heap sizes from the device");
+    if (rn > rl.capacity) return qbeam_fail("the results heap's List is too small");
+    const int64_t cw = cn < cand_io_cap ? cn : cand_io_cap;
+    if ((cw > 0 && cudaMemcpy(cand_h.data(), base + o_cand, (size_t)cw * 8,
+                              cudaMemcpyDeviceToHost) != cudaSuccess) ||
+        (rn > 0 && cudaMemcpy(res_h.data(), base + o_res, (size_t)rn * 8,
+                              cudaMemcpyDeviceToHost) != cudaSuccess))
+        return qbeam_fail("copy from the device failed");
+    if (finish_sync(ctx) != 0) return qbeam_fail(pion_v_b200_last_error(ctx));
+    const int64_t cfit = cw < cl.capacity ? cw : cl.capacity;
+    for (int64_t i = 0; i < cfit; ++i) {
+        std::memcpy(&cl.data[i].distance, &cand_h[2 * i], 4);
+        cl.data[i].pad = 0;
+        cl.data[i].id = (int64_t)cand_h[2 * i + 1];
+    }
+    cl.len = cfit;
+    for (int64_t i = 0; i < rn; ++i) {
+        std::memcpy(&rl.data[i].distance, &res_h[2 * i], 4);
+        rl.data[i].pad = 0;
+        rl.data[i].id = (int64_t)res_h[2 * i + 1];
+    }
+    rl.len = rn;
+    std::memcpy(&v->results->cached_worst, &meta[5], 4);
+    return 0;
+}
 
 int pion_v_b200_hnsw_quantize(const pion_b200_hnsw_graph* graph, const float* rows,
                               int64_t n_rows, int kind, pion_b200_hnsw_quant** out_quant) {

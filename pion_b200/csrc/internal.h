@@ -249,12 +249,25 @@ struct QuantLaunch {
     unsigned long long* stats = nullptr;
     int* status = nullptr;
     int ctas = 0;
+    // from-heaps mode (pion_v_quant_beam_1536): one query given as codes, scales,
+    // {|q|^2, |residual|^2} and QJL signs; the caller's heaps in and out
+    int from_heaps = 0;
+    const int8_t* given_codes = nullptr;
+    const float* given_scales = nullptr;
+    const float* given_norms = nullptr;
+    const uint64_t* given_signs = nullptr;
+    void* cand_io = nullptr;  // cand_io_cap entries of 8 bytes (f32 dist, u32 node)
+    int64_t cand_io_cap = 0;
+    void* res_io = nullptr;   // ef entries
+    int* heap_meta = nullptr; // 6 ints
 };
 size_t quant_warp_smem(int ef);
 int quant_warps_per_cta();
 int quant_top_entries();
 int quant_ctas_per_sm(int ef);
 int launch_quant_search(const QuantLaunch& launch, cudaStream_t st);
+// abi_quant.cu: drops the graphs pion_v_quant_beam_1536 registered (all when null)
+void quant_beam_forget(const uint32_t* l0_compact);
 
 // ---- compat.cu: the per-thread default context of the reference-compatible symbols
 pion_b200_ctx* compat_default_ctx(const char* who);

@@ -104,6 +104,19 @@ struct Params {
     unsigned* next_query;
     unsigned long long* stats;  // distance evaluations, expansions
     int* status;
+    // From-heaps mode (pion_v_quant_beam_1536): one query, given as codes, scales,
+    // {|q|^2, |residual|^2} and QJL signs; the level-0 beam from the caller's heaps
+    // (their nodes count as visited), the heaps written back.  heap_meta: {candidates
+    // in, results in, worst in (f32 bits), candidates out, results out, worst out}.
+    int from_heaps;
+    const int8_t* given_codes;
+    const float* given_scales;
+    const float* given_norms;
+    const uint64_t* given_signs;
+    Entry* cand_io;  // cand_io_cap entries
+    int64_t cand_io_cap;
+    Entry* res_io;   // ef entries
+    int* heap_meta;
 };
 
 // Per-warp shared memory: this fixed part, then TOP candidate entries (also the
@@ -450,6 +463,23 @@ __device__ __forceinline__ int round_away(float q) {
     return q >= 0.0f ? __float2int_rz(__fadd_rn(q, 0.5f)) : __float2int_rz(__fsub_rn(q, 0.5f));
 }
 
+// NanoQuant's dot regroups the query code words: word 8 b + 4 h + s = the bytes of dims
+// 32 b + 16 h + s, +4, +8, +12.
+__device__ void regroup_nano(Fixed& S, int lane) {
+    const int8_t* qc = reinterpret_cast<const int8_t*>(S.qw);
+    int32_t v[12];
+#pragma unroll
+    for (int r = 0; r < 12; ++r) {
+        const int wi = lane + 32 * r, b = wi >> 3, m = wi & 7, h = m >> 2, s = m & 3;
+        const int8_t* src = qc + b * 32 + 16 * h + s;
+        v[r] = (int32_t)((uint32_t)(uint8_t)src[0] | ((uint32_t)(uint8_t)src[4] << 8) |
+                         ((uint32_t)(uint8_t)src[8] << 16) | ((uint32_t)(uint8_t)src[12] << 24));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < 12; ++r) S.qw[lane + 32 * r] = v[r];
+}
+
 // The query's codes, scales, |q|^2 and (TurboQuant) QJL signs; `tmp` holds >= 1536 floats.
 __device__ void prologue(const Params& p, Fixed& S, const float* x, float* tmp, int lane) {
     // l2_normalize_fp32: four running sums (d mod 4), (s0 + s2) + (s1 + s3)
@@ -534,19 +564,32 @@ __device__ void prologue(const Params& p, Fixed& S, const float* x, float* tmp, 
             if (lane == 0) S.qsig[w] = (uint64_t)lo | ((uint64_t)hi << 32);
         }
     }
-    if (p.kind == kQNano) {  // regroup the code words for dot_i2
-        int32_t v[12];
-#pragma unroll
-        for (int r = 0; r < 12; ++r) {
-            const int wi = lane + 32 * r, b = wi >> 3, m = wi & 7, h = m >> 2, s = m & 3;
-            const int8_t* src = qc + b * 32 + 16 * h + s;
-            v[r] = (int32_t)((uint32_t)(uint8_t)src[0] | ((uint32_t)(uint8_t)src[4] << 8) |
-                             ((uint32_t)(uint8_t)src[8] << 16) | ((uint32_t)(uint8_t)src[12] << 24));
+    if (p.kind == kQNano) regroup_nano(S, lane);
+    __syncwarp();
+}
+
+// The query side given by the caller (the reference's per-query beam view): codes,
+// scales, |q|^2 and QJL signs as the engine computed them.
+__device__ void given_query(const Params& p, Fixed& S, int lane) {
+    int8_t* qc = reinterpret_cast<int8_t*>(S.qw);
+    for (int b = 0; b < NB; ++b) {
+        const int c = p.given_codes[b * 32 + lane];
+        qc[b * 32 + lane] = (int8_t)c;
+        const int sum = __reduce_add_sync(FULL, c);
+        if (lane == 0) {
+            S.qs[b] = p.given_scales[b];
+            S.qsum[b] = sum;
         }
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 12; ++r) S.qw[lane + 32 * r] = v[r];
     }
+    if (lane < QW) S.qsig[lane] = p.given_signs ? p.given_signs[lane] : 0ull;
+    if (lane == 0) {
+        S.qn = p.given_norms[0];
+        S.qres = p.given_norms[1];
+        S.scaled = 0;
+        S.qinv = 1.0f;
+    }
+    __syncwarp();
+    if (p.kind == kQNano) regroup_nano(S, lane);
     __syncwarp();
 }
 
@@ -575,6 +618,27 @@ __global__ void __launch_bounds__(WARPS * 32, 4) quant_search_kernel(Params p) {
         const float* x = p.queries + (size_t)t * DIM;
         for (int64_t w = lane * 4; w < p.vis_words; w += 128)
             *reinterpret_cast<uint4*>(vis + w) = make_uint4(0, 0, 0, 0);
+        if (p.from_heaps) {
+            given_query(p, S, lane);
+            const int cn = p.heap_meta[0], rn = p.heap_meta[1];
+            if (lane == 0) {
+                S.cand_n = cn;
+                S.res_n = rn;
+                S.res_worst = __int_as_float(p.heap_meta[2]);
+                S.abandon = 0;
+            }
+            for (int i = lane; i < cn; i += 32) {
+                const Entry e = p.cand_io[i];
+                cand.put(i, e);
+                atomicOr(vis + (e.id >> 5), 1u << (e.id & 31));
+            }
+            for (int i = lane; i < rn; i += 32) {
+                const Entry e = p.res_io[i];
+                res[i] = e;
+                atomicOr(vis + (e.id >> 5), 1u << (e.id & 31));
+            }
+            __syncwarp();
+        } else {
         prologue(p, S, x, reinterpret_cast<float*>(top), lane);
 
         // upper levels
@@ -641,6 +705,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) quant_search_kernel(Params p) {
             atomicOr(vis + (cur >> 5), 1u << (cur & 31));
         }
         __syncwarp();
+        }  // from the caller's heaps or from the greedy's node
         for (int64_t step = 0; step <= n; ++step) {
             uint32_t cid = 0;
             int go = 0;
@@ -696,6 +761,19 @@ __global__ void __launch_bounds__(WARPS * 32, 4) quant_search_kernel(Params p) {
             }
             __syncwarp();
             if (S.abandon) break;
+        }
+        if (p.from_heaps) {  // the heaps back to the caller
+            const int cn = S.cand_n, rn = S.res_n;
+            if (lane == 0) {
+                p.heap_meta[3] = S.abandon ? -1 : cn;
+                p.heap_meta[4] = rn;
+                p.heap_meta[5] = __float_as_int(S.res_worst);
+            }
+            const int64_t co = cn < p.cand_io_cap ? cn : p.cand_io_cap;
+            for (int64_t i = lane; i < co; i += 32) p.cand_io[i] = cand.get(i);
+            for (int i = lane; i < rn; i += 32) p.res_io[i] = res[i];
+            __syncwarp();
+            continue;
         }
         if (S.abandon) {
             if (lane == 0) {
@@ -851,6 +929,15 @@ int launch_quant_search(const QuantLaunch& L, cudaStream_t st) {
     p.next_query = L.next_query;
     p.stats = L.stats;
     p.status = L.status;
+    p.from_heaps = L.from_heaps;
+    p.given_codes = L.given_codes;
+    p.given_scales = L.given_scales;
+    p.given_norms = L.given_norms;
+    p.given_signs = L.given_signs;
+    p.cand_io = reinterpret_cast<qb::Entry*>(L.cand_io);
+    p.cand_io_cap = L.cand_io_cap;
+    p.res_io = reinterpret_cast<qb::Entry*>(L.res_io);
+    p.heap_meta = L.heap_meta;
     if (L.ctas <= 0 || L.ef < 1 || L.ef > qb::TOP || L.code_bytes % 16 != 0) return PION_B200_ESHAPE;
     const size_t bytes = qb::WARPS * qb::warp_bytes(L.ef);
     if (cudaFuncSetAttribute(qb::quant_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -294,6 +294,23 @@ class PyMax:
         return root
 
 
+def py_beam(A, dist, ef, cand, res, seen):
+    """quant_beam_search_1536_ref's loop over seeded heaps (no deleted nodes here)."""
+    while cand.a:
+        c = cand.pop()
+        if c[0] > res.worst and len(res.a) >= ef:
+            break
+        row, srow = A["l0_compact"][c[1]], A["l0_slots"][c[1]]
+        for i in range(int(row[0])):
+            nidx = int(row[1 + i])
+            if nidx >= A["num_nodes"] or nidx in seen:
+                continue
+            seen.add(nidx)
+            d = dist(nidx, int(srow[1 + i]))
+            cand.push(d, nidx)
+            res.push_bounded(d, nidx, ef)
+
+
 def py_search(A, Q, kind, q, k, ef):
     comp = Q["compact"].reshape(A["num_nodes"], Q["stride"])
     slot_of = A["node_slot"]
@@ -337,19 +354,7 @@ def py_search(A, Q, kind, q, k, ef):
     cand, res, seen = PyMin(), PyMax(), {cur}
     cand.push(cd, cur)
     res.push(cd, cur)
-    while cand.a:
-        c = cand.pop()
-        if c[0] > res.worst and len(res.a) >= ef:
-            break
-        row, srow = A["l0_compact"][c[1]], A["l0_slots"][c[1]]
-        for i in range(int(row[0])):
-            nidx = int(row[1 + i])
-            if nidx >= A["num_nodes"] or nidx in seen:
-                continue
-            seen.add(nidx)
-            d = dist(nidx, int(srow[1 + i]))
-            cand.push(d, nidx)
-            res.push_bounded(d, nidx, ef)
+    py_beam(A, dist, ef, cand, res, seen)
     ids, ds = [], []
     while res.a:
         r = res.pop()
@@ -432,3 +437,47 @@ def test_library_quantizer_refuses(qgraph):
         pion_b200.HNSWQuant(g, rows, "int5")
     with pytest.raises(pion_b200.PionError):
         pion_b200.HNSWQuant(g, rows[:-1], "polar")
+
+
+@pytest.mark.parametrize("kind", ["polar", "turbo"])
+def test_beam_from_heaps_matches_python(oracle, qgraph, kind):
+    """The oracle's beam on a view's state (orc_quant_beam_heaps: the query given as codes,
+    heaps given as arrays) leaves the heaps array for array as the Python loop does, and
+    cuts the candidates at a capacity."""
+    g, A, rows, qs = qgraph
+    Q = oracle.quant_graph(A, rows, kind)
+    comp = Q["compact"].reshape(A["num_nodes"], Q["stride"])
+    q = oracle.l2_normalize_rows(qs[1][None])[0] if A["metric"] == 1 else qs[1]
+    qc, qsc, qn = oracle.query_block_int8(q)
+    qsig, qres = None, F(0.0)
+    if kind == "turbo":
+        resid = np.array([q[i] - F(qc[i]) * qsc[i // 32] for i in range(1536)], F)
+        qsig, qres = oracle.qjl_signs(resid, Q["qjl_random_signs"])
+
+    def dist(node, slot_row=None, qjl=True):
+        v = comp[A["node_slot"][node]] if slot_row is None else comp[slot_row]
+        nv = np.frombuffer(v[:4].tobytes(), F)[0]
+        d = (qn + nv) - F(2.0) * F(oracle.quant_dot(kind, qc, qsc, v))
+        if kind != "turbo" or not qjl:
+            return d
+        ham = sum(bin(int(a) ^ int(b)).count("1") for a, b in zip(qsig, Q["qjl"][node]))
+        cos_est = (F(1536) - F(2) * F(ham)) * (F(1.0) / F(1536))
+        return d - F(2.0) * (F(Q["qjl_lambda"]) * cos_est * (qres * Q["qjl_res_norms"][node]))
+
+    start = int(A["entry_point"])
+    d0 = dist(start, qjl=False)
+    cand, res = PyMin(), PyMax()
+    cand.push(d0, start)
+    res.push(d0, start)
+    py_beam(A, dist, 20, cand, res, {start})
+    got_c, total, got_r, worst = oracle.quant_beam_heaps(A, Q, qc, qsc, qn, qsig, qres, 20,
+                                                         [(d0, start)], [(d0, start)], d0)
+    assert total == len(cand.a) == len(got_c)
+    assert [(np.float32(d).view(np.uint32), i) for d, i in got_c] == \
+        [(np.float32(d).view(np.uint32), i) for d, i in cand.a]
+    assert [(np.float32(d).view(np.uint32), i) for d, i in got_r] == \
+        [(np.float32(d).view(np.uint32), i) for d, i in res.a]
+    assert worst == res.worst
+    cut, total2, _, _ = oracle.quant_beam_heaps(A, Q, qc, qsc, qn, qsig, qres, 20,
+                                                [(d0, start)], [(d0, start)], d0, cand_cap=5)
+    assert total2 == total and cut == got_c[:5]

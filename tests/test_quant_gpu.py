@@ -160,3 +160,72 @@ def test_quant_search_from_index_file(ctx, oracle, graphs, kind, tmp_path):
     ix = pion_b200.HNSWQuantIndex(ctx, G2, q2)
     _same(ix.search(qs, 10, 64), oracle.quant_search(G2.arrays(), q2.arrays(), qs, 10, 64))
     ix.free()
+
+
+NODE = np.dtype([("d", "<f4"), ("pad", "<i4"), ("id", "<i8")])
+
+
+@pytest.mark.parametrize("kind,cap", [("polar", None), ("nano", None), ("turbo", None),
+                                      ("turbo", 12)])
+def test_quant_beam_symbol(ctx, oracle, graphs, kind, cap):
+    """The reference's per-query symbol pion_v_quant_beam_1536 on a QuantBeamView1536
+    seeded as search_fp32_scored seeds it (the start node in both heaps, the List reserves
+    of ef + 32): the heaps come back array for array as the oracle's beam leaves them, the
+    candidates cut at the List's capacity."""
+    import ctypes
+
+    import pion_b200
+    from pion_b200 import _lib
+    g, A, rows, qs = graphs["cosine"]
+    qz = pion_b200.HNSWQuant(g, rows, kind)
+    Q = qz.arrays()
+    comp = Q["compact"].reshape(A["num_nodes"], Q["stride"])
+    lib = pion_b200.load()
+    n, ef = A["num_nodes"], 48
+    visited = np.zeros(n, np.uint16)
+    l0c = np.ascontiguousarray(A["l0_compact"])
+    l0s = np.ascontiguousarray(A["l0_slots"])
+    for t in range(6):
+        q = oracle.l2_normalize_rows(qs[t][None])[0]
+        qc, qsc, qn = oracle.query_block_int8(q)
+        qsig, qres = None, np.float32(0.0)
+        if kind == "turbo":
+            resid = np.array([q[i] - np.float32(qc[i]) * qsc[i // 32] for i in range(1536)],
+                             np.float32)
+            qsig, qres = oracle.qjl_signs(resid, Q["qjl_random_signs"])
+        start = (int(A["entry_point"]) + 97 * t) % n
+        v = comp[A["node_slot"][start]]
+        d0 = (qn + np.frombuffer(v[:4].tobytes(), np.float32)[0]) - \
+            np.float32(2.0) * np.float32(oracle.quant_dot(kind, qc, qsc, v))
+        ccap = cap or ef + 32
+        cn = np.zeros(ccap, NODE)
+        rn = np.zeros(ef + 32, NODE)
+        cn[0] = (d0, 0, start)
+        rn[0] = (d0, 0, start)
+        minh = _lib.MinHeap(_lib.HeapList(cn.ctypes.data, 1, ccap))
+        maxh = _lib.MaxHeap(_lib.HeapList(rn.ctypes.data, 1, ef + 32), float(d0), 0)
+        keep = [np.ascontiguousarray(qc), np.ascontiguousarray(qsc)]
+        sig = None if qsig is None else np.ascontiguousarray(qsig, np.uint64)
+        view = _lib.QuantBeamView1536(
+            kind=pion_b200.search.QUANT_KINDS[kind], ef=ef, candidates=ctypes.pointer(minh),
+            results=ctypes.pointer(maxh), query_block_int8=keep[0].ctypes.data,
+            query_block_scales=keep[1].ctypes.data, query_block_norm=float(qn),
+            l0_compact=l0c.ctypes.data, l0_slots=l0s.ctypes.data, num_nodes=n, deleted=None,
+            visited=visited.ctypes.data, cur_epoch=1, compact_buffer=comp.ctypes.data,
+            compact_stride=Q["stride"], compact_hdr=0, nodes=None,
+            qjl_buffer=Q["qjl"].ctypes.data if kind == "turbo" else None,
+            qjl_res_norms=Q["qjl_res_norms"].ctypes.data if kind == "turbo" else None,
+            qjl_query_signs=None if sig is None else sig.ctypes.data,
+            qjl_query_res_norm=float(qres), qjl_lambda=1.0)
+        assert lib.pion_v_quant_beam_1536(ctypes.byref(view)) == 0
+        want_c, total, want_r, worst = oracle.quant_beam_heaps(
+            A, Q, qc, qsc, qn, qsig, qres, ef, [(d0, start)], [(d0, start)], d0, cand_cap=ccap)
+        assert minh.data.len == len(want_c) and maxh.data.len == len(want_r)
+        got_c = [(np.float32(e["d"]).view(np.uint32), int(e["id"])) for e in cn[:minh.data.len]]
+        got_r = [(np.float32(e["d"]).view(np.uint32), int(e["id"])) for e in rn[:maxh.data.len]]
+        assert got_c == [(np.float32(d).view(np.uint32), i) for d, i in want_c]
+        assert got_r == [(np.float32(d).view(np.uint32), i) for d, i in want_r]
+        assert np.float32(maxh.cached_worst) == worst
+        if cap is not None:
+            assert total > cap  # the whole heap did not fit the List: cut at its capacity
+    lib.pion_v_b200_beam_forget(None)
