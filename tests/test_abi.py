@@ -59,3 +59,48 @@ def test_bad_arguments_are_rejected_without_gpu():
     assert L.pion_v_b200_init(0, 0, None) == _lib.EINVAL
     assert L.pion_v_b200_flat_i8_knn(None, None, None, None, 1, 10, None, None, 0) == _lib.EINVAL
     assert L.pion_v_b200_sync(None) == _lib.EINVAL
+
+
+STRUCTS = {  # C type in include/pion_vector_b200.h -> ctypes mirror in pion_b200._lib
+    "pion_b200_index_desc": "IndexDesc",
+    "pion_linear_pool": "LinearPool",
+    "pion_beam_view_1536": "BeamView1536",
+    "pion_b200_hnsw_layout": "HnswLayout",
+    "pion_b200_hnsw_quant_layout": "HnswQuantLayout",
+    "pion_heap_node": "HeapNode",
+    "pion_heap_list": "HeapList",
+    "pion_min_heap": "MinHeap",
+    "pion_max_heap": "MaxHeap",
+    "pion_quant_beam_view_1536": "QuantBeamView1536",
+}
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """Every struct of the header has the size and field offsets its ctypes mirror has,
+    as the host C compiler lays it out."""
+    import shutil
+    import subprocess
+
+    from pion_b200 import _lib
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "pion_vector_b200.h"',
+             "int main(void) {"]
+    want = []
+    for cname, pyname in STRUCTS.items():
+        cls = getattr(_lib, pyname)
+        lines.append(f'printf("%zu\\n", sizeof({cname}));')
+        want.append(ctypes.sizeof(cls))
+        for fname, _ in cls._fields_:
+            lines.append(f'printf("%zu\\n", offsetof({cname}, {fname}));')
+            want.append(getattr(cls, fname).offset)
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True, capture_output=True)
+    got = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    assert got == want
