@@ -442,11 +442,25 @@ int pion_v_b200_hnsw_save(const pion_b200_hnsw_graph *graph, const char *path,
 int pion_v_b200_hnsw_build(const float *rows, int64_t n_rows, int64_t dim, int64_t M,
                            int64_t ef_construction, int metric, int64_t id_base, int n_threads,
                            pion_b200_hnsw_graph **out_graph);
+/* The same build with batched insertion instead of racing link lanes: the nodes are
+ * inserted in batches (a quarter of the nodes linked so far, at most max_batch >= 1); every
+ * node of a batch does the search half of _insert_to_graph_mt (greedy descent,
+ * _search_layer_mt at efConstruction, _prune_neighbors) against the graph as it stood
+ * before the batch, n_threads at a time, then the batch is linked node by node in order
+ * (own lists and evict-farthest backlinks), followed by the relink and repair passes and
+ * compact_vectors.  The graph does not depend on the thread count; max_batch = 1 is the
+ * one-lane build.  The searches of a batch are independent, which is the shape of the
+ * work a GPU takes over. */
+int pion_v_b200_hnsw_build_batched(const float *rows, int64_t n_rows, int64_t dim, int64_t M,
+                                   int64_t ef_construction, int metric, int64_t id_base,
+                                   int n_threads, int64_t max_batch,
+                                   pion_b200_hnsw_graph **out_graph);
 /* The graph's buffers (host memory owned by the graph). */
 int pion_v_b200_hnsw_graph_layout(const pion_b200_hnsw_graph *graph,
                                   pion_b200_hnsw_layout *out_layout);
-/* Build counters: link lanes, contended link drops, relinked under-linked nodes, nodes
- * re-linked by the exit repair, links added by the reachability repair. */
+/* Build counters: link lanes (minus the batch count after a batched build), contended
+ * link drops, relinked under-linked nodes, nodes re-linked by the exit repair, links added
+ * by the reachability repair. */
 int pion_v_b200_hnsw_graph_stats(const pion_b200_hnsw_graph *graph, int64_t *out5);
 int pion_v_b200_hnsw_graph_free(pion_b200_hnsw_graph *graph);
 

@@ -69,6 +69,8 @@ SIGNATURES = {
     "pion_v_b200_l2_normalize_rows": (_I, [_P, _P, _I64, _I64, _P, _I]),
     "pion_v_b200_merge_topk": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _I]),
     "pion_v_b200_hnsw_build": (_I, [_P, _I64, _I64, _I64, _I64, _I, _I64, _I, _PP]),
+    "pion_v_b200_hnsw_build_batched": (_I, [_P, _I64, _I64, _I64, _I64, _I, _I64, _I, _I64,
+                                            _PP]),
     "pion_v_b200_hnsw_graph_layout": (_I, [_P, _P]),
     "pion_v_b200_hnsw_graph_stats": (_I, [_P, _P]),
     "pion_v_b200_hnsw_graph_free": (_I, [_P]),

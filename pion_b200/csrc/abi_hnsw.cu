@@ -106,6 +106,39 @@ int pion_v_b200_hnsw_build(const float* rows, int64_t n_rows, int64_t dim, int64
     return 0;
 }
 
+int pion_v_b200_hnsw_build_batched(const float* rows, int64_t n_rows, int64_t dim, int64_t M,
+                                   int64_t ef_construction, int metric, int64_t id_base,
+                                   int n_threads, int64_t max_batch,
+                                   pion_b200_hnsw_graph** out_graph) {
+    if (!out_graph) return PION_B200_EINVAL;
+    *out_graph = nullptr;
+    if (max_batch < 1 || n_rows < 0 || (n_rows > 0 && !rows) || dim <= 0 || M < 2 || M > 16 ||
+        ef_construction < 1 || (metric != 0 && metric != 1) || id_base < 0 ||
+        n_rows + id_base > INT32_MAX || n_rows >= 0x7fffffff) {
+        fprintf(stderr, "pion_vector_b200: hnsw_build_batched: bad arguments\n");
+        return PION_B200_EINVAL;
+    }
+    __builtin_cpu_init();
+    if (!__builtin_cpu_supports("avx2") || !__builtin_cpu_supports("fma")) {
+        fprintf(stderr, "pion_vector_b200: hnsw_build_batched needs a CPU with AVX2 and FMA\n");
+        return PION_B200_ESHAPE;
+    }
+    if (n_threads <= 0) n_threads = (int)std::thread::hardware_concurrency();
+    if (n_threads <= 0) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    pion_b200_hnsw_graph* g = new (std::nothrow) pion_b200_hnsw_graph();
+    if (!g) return PION_B200_ENOMEM;
+    try {
+        hnsw::build(rows, n_rows, dim, M, ef_construction, metric, id_base, n_threads, g->g,
+                    &g->stats, max_batch);
+    } catch (const std::bad_alloc&) {
+        delete g;
+        return PION_B200_ENOMEM;
+    }
+    *out_graph = g;
+    return 0;
+}
+
 int pion_v_b200_hnsw_load(const char* path, pion_b200_hnsw_graph** out_graph) {
     if (!path || !out_graph) return PION_B200_EINVAL;
     *out_graph = nullptr;

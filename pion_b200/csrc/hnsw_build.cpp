@@ -350,6 +350,95 @@ struct Builder {
         }
     }
 
+    // The search half of an insertion, against the graph as it stands (read only): the
+    // greedy descent, search_layer and prune of every level the node joins, the pruned
+    // neighbours kept per level (level l's at [offs[l'], offs[l' + 1]) with l' counted
+    // from the top).  link() applies them as insert() would; plan() then link() of one
+    // node is insert() (a level's links never change a lower level's search).
+    struct Plan {
+        std::vector<uint32_t> ids;
+        std::vector<uint32_t> offs;
+        int top = -1;
+    };
+
+    void plan(int64_t id, Scratch& s, Plan& p) {
+        const int lvl = g.level[id];
+        const int8_t* q = code(id);
+        const float* v = row(id, s.fbuf);
+        int64_t ep = g.entry;
+        p.ids.clear();
+        p.offs.assign(1, 0);
+        for (int l = g.max_level; l > lvl; --l) {
+            float best = dist_f32_i8(v, code(ep), g.dim, scale, offset);
+            bool changed = true;
+            while (changed) {
+                changed = false;
+                const int64_t cur = ep;
+                if (l > g.level[cur]) break;
+                const uint32_t nc = count(cur, l).load(std::memory_order_acquire);
+                const uint32_t* lst = list(cur, l);
+                for (uint32_t i = 0; i < nc; ++i) {
+                    const uint32_t nb = lst[i];
+                    if (nb >= (uint32_t)g.n) continue;
+                    const float d = dist_f32_i8(v, code(nb), g.dim, scale, offset);
+                    if (d < best) {
+                        best = d;
+                        ep = nb;
+                        changed = true;
+                    }
+                }
+            }
+        }
+        p.top = std::min(lvl, g.max_level);
+        for (int l = p.top; l >= 0; --l) {
+            search_layer(q, ep, g.efc, l, s);
+            if (s.res.size() > 0) {
+                s.all.clear();
+                while (s.res.size() > 0) s.all.push_back(s.res.pop());
+                ep = s.all.back().id;
+                prune(s.all, cap(l), s);
+                p.ids.insert(p.ids.end(), s.pruned.begin(), s.pruned.end());
+            }
+            p.offs.push_back((uint32_t)p.ids.size());
+        }
+    }
+
+    // The link half: the node's own lists and the evict-farthest backlinks, level by level
+    // from the top, in the order insert() makes them (one thread).
+    void link(int64_t id, const Plan& p) {
+        const int8_t* q = code(id);
+        for (int l = p.top, k = 0; l >= 0; --l, ++k) {
+            const int64_t m_limit = cap(l);
+            for (uint32_t j = p.offs[k]; j < p.offs[k + 1]; ++j) {
+                const uint32_t nb = p.ids[j];
+                int64_t evicted = -1;
+                const uint32_t nc = count(nb, l).load(std::memory_order_relaxed);
+                if ((int64_t)nc < m_limit) {
+                    add_published(nb, l, (uint32_t)id);
+                } else {
+                    float worst;
+                    const int64_t pos = farthest(nb, l, nc, worst);
+                    if (dist_i8(code(nb), q, g.dim) < worst) {
+                        evicted = list(nb, l)[pos];
+                        list(nb, l)[pos] = (uint32_t)id;
+                    }
+                }
+                if (evicted >= 0 && evicted < g.n) remove_link(evicted, l, nb);
+                const uint32_t onc = count(id, l).load(std::memory_order_relaxed);
+                if ((int64_t)onc < m_limit) {
+                    add_published(id, l, nb);
+                } else {
+                    float worst;
+                    const int64_t pos = farthest(id, l, onc, worst);
+                    if (dist_i8(q, code(nb), g.dim) < worst)
+                        list(id, l)[pos] = nb;
+                    else
+                        link_drops.fetch_add(1, std::memory_order_relaxed);
+                }
+            }
+        }
+    }
+
     // _insert_to_graph_mt (hnsw.mojo:2117-2240).
     void insert(int64_t id, Scratch& s) {
         const int lvl = g.level[id];
@@ -689,7 +778,7 @@ int level_of(int64_t i, float ml) {
 }  // namespace
 
 int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
-          int64_t id_base, int n_threads, Graph& g, BuildStats* stats) {
+          int64_t id_base, int n_threads, Graph& g, BuildStats* stats, int64_t max_batch) {
     g = Graph();
     g.n = n;
     g.dim = dim;
@@ -782,8 +871,49 @@ int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int
     b.locks.reset(new std::atomic<uint8_t>[(size_t)std::max<int64_t>(n, 1)]);
     for (int64_t i = 0; i < n; ++i) b.locks[i].store(0, std::memory_order_relaxed);
 
-    int lanes = n >= 4096 ? std::max(1, n_threads) : 1;
-    if (n > 0) {
+    const bool batched = max_batch > 0;
+    int lanes = batched ? 1 : (n >= 4096 ? std::max(1, n_threads) : 1);
+    int64_t batches = 0;
+    if (n > 0 && batched) {
+        // Batched insertion: the nodes of a batch are planned against the graph as it
+        // stood before the batch (in parallel: the graph is read only), then linked one by
+        // one in node order.  The batch grows with the graph (a quarter of the nodes
+        // linked so far, at most max_batch), so the first nodes go in one at a time.
+        // The result does not depend on the thread count.
+        const int nt = std::max(1, n_threads);
+        std::vector<Builder::Scratch> scratch((size_t)nt);
+        for (auto& sc : scratch) b.init_scratch(sc);
+        std::vector<int64_t> order;
+        order.reserve((size_t)n);
+        for (int64_t i = 0; i < n; ++i)
+            if (i != g.entry) order.push_back(i);
+        std::vector<Builder::Plan> plans;
+        int64_t done = 0, linked = 1;
+        while (done < (int64_t)order.size()) {
+            int64_t bsz = std::max<int64_t>(1, linked / 4);
+            bsz = std::min(bsz, max_batch);
+            bsz = std::min(bsz, (int64_t)order.size() - done);
+            if ((int64_t)plans.size() < bsz) plans.resize((size_t)bsz);
+            std::atomic<int64_t> next{0};
+            auto work = [&](int t) {
+                for (int64_t j = next.fetch_add(1); j < bsz; j = next.fetch_add(1))
+                    b.plan(order[(size_t)(done + j)], scratch[(size_t)t], plans[(size_t)j]);
+            };
+            const int use = (int)std::min<int64_t>(nt, bsz);
+            if (use <= 1) {
+                work(0);
+            } else {
+                std::vector<std::thread> th;
+                for (int t = 1; t < use; ++t) th.emplace_back(work, t);
+                work(0);
+                for (auto& x : th) x.join();
+            }
+            for (int64_t j = 0; j < bsz; ++j) b.link(order[(size_t)(done + j)], plans[(size_t)j]);
+            done += bsz;
+            linked += bsz;
+            ++batches;
+        }
+    } else if (n > 0) {
         std::vector<std::thread> th;
         for (int t = 0; t < lanes; ++t)
             th.emplace_back([&, t]() {
@@ -798,7 +928,7 @@ int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int
     b.init_scratch(s);
     int64_t relinked = 0, exits = 0, links = 0;
     if (n > 0) {
-        if (lanes > 1)
+        if (lanes > 1 || (batched && max_batch > 1))
             for (int64_t i = 0; i < n; ++i)
                 if ((int64_t)b.count(i, 0).load() < M / 2) {
                     b.relink_l0(i, s);
@@ -814,7 +944,7 @@ int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int
     }
     b.compact();
     if (stats) {
-        stats->lanes = lanes;
+        stats->lanes = batched ? -batches : lanes;
         stats->link_drops = (int64_t)b.link_drops.load();
         stats->relinked = relinked;
         stats->repaired_exits = exits;

@@ -39,9 +39,10 @@ struct BuildStats {
 };
 
 // Builds the graph of n rows (fp32, n x dim, normalised first under COSINE) with the
-// reference's parameters; node i gets external id id_base + i.  n_threads link lanes.
+// reference's parameters; node i gets external id id_base + i.  n_threads link lanes, or
+// with max_batch > 0 batched insertion (deterministic; n_threads plan each batch).
 int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
-          int64_t id_base, int n_threads, Graph& g, BuildStats* stats);
+          int64_t id_base, int n_threads, Graph& g, BuildStats* stats, int64_t max_batch = 0);
 
 // Block-quantised slot formats (the reference's PolarQuant / NanoQuant / TurboQuant
 // compact_vectors): kinds, and the buffers quantize() fills from the rows the graph was

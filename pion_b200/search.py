@@ -400,16 +400,23 @@ class HNSWGraph:
 
     rows: float32 [n, dim] host array.  metric: "cosine" (rows and queries are
     unit-normalised) or "l2".  threads <= 0 uses every online CPU; one thread builds
-    the same graph every time."""
+    the same graph every time.  batch > 0: batched insertion of up to `batch` nodes at a
+    time (the same graph for any thread count; batch = 1 is the one-lane build)."""
 
     def __init__(self, rows, M: int = 16, ef_construction: int = 200, metric: str = "cosine",
-                 id_base: int = 0, threads: int = 0):
+                 id_base: int = 0, threads: int = 0, batch: int = 0):
         self.lib = _lib.load()
         a = np.ascontiguousarray(rows, dtype=np.float32)
         h = ctypes.c_void_p()
-        rc = self.lib.pion_v_b200_hnsw_build(a.ctypes.data, a.shape[0], a.shape[1], M,
-                                             ef_construction, 1 if metric == "cosine" else 0,
-                                             id_base, threads, ctypes.byref(h))
+        mt = 1 if metric == "cosine" else 0
+        if batch > 0:  # batched insertion (deterministic for any thread count)
+            rc = self.lib.pion_v_b200_hnsw_build_batched(a.ctypes.data, a.shape[0], a.shape[1],
+                                                         M, ef_construction, mt, id_base,
+                                                         threads, batch, ctypes.byref(h))
+        else:
+            rc = self.lib.pion_v_b200_hnsw_build(a.ctypes.data, a.shape[0], a.shape[1], M,
+                                                 ef_construction, mt, id_base, threads,
+                                                 ctypes.byref(h))
         if rc != 0:
             raise PionError(rc, "hnsw_build failed")
         self._adopt(h)
@@ -468,8 +475,8 @@ class HNSWGraph:
                          "repaired_links"), list(out)))
 
     def arrays(self) -> dict:
-        """The layout as numpy views of the library's buffers (valid while the graph
-        lives) plus its scalars."""
+        """The layout as numpy views of the library's buffers (each view keeps the graph
+        alive) plus its scalars."""
         L = self.layout
         n, st, m, ur = L.num_nodes, L.compact_stride, L.M, L.upper_rows
         out = {name: getattr(L, name) for name in _LAYOUT_SCALARS}
@@ -481,8 +488,7 @@ class HNSWGraph:
             if not ptr or int(np.prod(shape)) == 0:
                 out[name] = np.zeros(shape, dt)
                 continue
-            cp = ctypes.cast(ptr, ctypes.POINTER(ctype[dt]))
-            out[name] = np.ctypeslib.as_array(cp, shape=shape)
+            out[name] = _view(ptr, ctype[dt], shape, dt, self)
         out["deleted"] = None
         return out
 
@@ -655,10 +661,15 @@ class HNSWIndex(_Index):
 QUANT_KINDS = {"polar": 0, "nano": 1, "turbo": 2}
 
 
-def _view(ptr, ctype, shape, dtype):
-    if not ptr or int(np.prod(shape)) == 0:
+def _view(ptr, ctype, shape, dtype, owner=None):
+    """A numpy view of library memory that keeps `owner` (the object whose buffers these
+    are) alive as long as the view lives."""
+    count = int(np.prod(shape))
+    if not ptr or count == 0:
         return np.zeros(shape, dtype)
-    return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctype)), shape=shape)
+    buf = (ctype * count).from_address(ptr)
+    buf._owner = owner
+    return np.frombuffer(buf, dtype).reshape(shape)
 
 
 class HNSWQuant:
@@ -692,20 +703,21 @@ class HNSWQuant:
         return self
 
     def arrays(self) -> dict:
-        """numpy views of the buffers (valid while this object lives): kind, stride,
+        """numpy views of the buffers (each keeps this object alive): kind, stride,
         compact [n * stride] int8 by slot, rerank [n, 1536] by node, and for "turbo" qjl
         [n, 24] uint64, qjl_res_norms [n], qjl_random_signs [24], qjl_lambda."""
         L = self.layout
         n = L.num_nodes
         out = {"kind": self.kind, "stride": L.stride,
-               "compact": _view(L.compact, ctypes.c_int8, (n * L.stride,), np.int8),
-               "rerank": _view(L.rerank, ctypes.c_float, (n, 1536), np.float32)
+               "compact": _view(L.compact, ctypes.c_int8, (n * L.stride,), np.int8, self),
+               "rerank": _view(L.rerank, ctypes.c_float, (n, 1536), np.float32, self)
                if L.rerank else None}
         if L.qjl:
-            out.update(qjl=_view(L.qjl, ctypes.c_uint64, (n, 24), np.uint64),
-                       qjl_res_norms=_view(L.qjl_res_norms, ctypes.c_float, (n,), np.float32),
+            out.update(qjl=_view(L.qjl, ctypes.c_uint64, (n, 24), np.uint64, self),
+                       qjl_res_norms=_view(L.qjl_res_norms, ctypes.c_float, (n,), np.float32,
+                                           self),
                        qjl_random_signs=_view(L.qjl_random_signs, ctypes.c_uint64, (24,),
-                                              np.uint64),
+                                              np.uint64, self),
                        qjl_lambda=L.qjl_lambda)
         return out
 

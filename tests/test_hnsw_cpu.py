@@ -131,3 +131,56 @@ def test_build_rejects_bad_arguments():
     import pion_b200
     with pytest.raises(pion_b200.PionError):
         pion_b200.HNSWGraph(np.zeros((10, 1536), np.float32), M=40)
+
+
+KEYS = ("compact_buffer", "l0_compact", "l0_slots", "upper_links", "node_slot", "node_level")
+
+
+def test_batched_build_of_one_is_the_one_lane_build(built):
+    """Batched insertion with batches of one node is the one-lane build, array for array
+    (the search half of an insertion never reads what its own links change)."""
+    import pion_b200
+    g, A, rows, qs = built
+    gb = pion_b200.HNSWGraph(rows, M=8, ef_construction=64, threads=4, batch=1)
+    B = gb.arrays()  # views of gb's buffers: gb stays alive while they are read
+    for key in KEYS:
+        assert np.array_equal(A[key], B[key]), key
+
+
+def test_batched_build_is_deterministic_and_sound(oracle, built):
+    """Batches of up to 128 nodes planned on 1 or 3 threads give the same graph, with the
+    structure the beam needs and the recall of the one-lane build."""
+    import pion_b200
+    g, A, rows, qs = built
+    g1 = pion_b200.HNSWGraph(rows, M=8, ef_construction=64, threads=1, batch=128)
+    g3 = pion_b200.HNSWGraph(rows, M=8, ef_construction=64, threads=3, batch=128)
+    B, C = g1.arrays(), g3.arrays()
+    for key in KEYS:
+        assert np.array_equal(B[key], C[key]), key
+    assert g1.stats()["lanes"] < -1  # the batch count
+    n, M = B["num_nodes"], B["M"]
+    cnt = B["l0_compact"][:, 0]
+    assert cnt.max() <= 2 * M and (cnt > 0).all()
+    for i in range(n):  # no self links, every neighbour a node
+        nb = B["l0_compact"][i, 1:1 + cnt[i]]
+        assert (nb < n).all() and (nb != i).all()
+    seen = np.zeros(n, bool)
+    seen[B["entry_point"]] = True
+    frontier = [B["entry_point"]]
+    while frontier:
+        nxt = []
+        for x in frontier:
+            for nb in B["l0_compact"][x, 1:1 + B["l0_compact"][x, 0]]:
+                if not seen[nb]:
+                    seen[nb] = True
+                    nxt.append(nb)
+        frontier = nxt
+    assert seen.all()
+    rn = rows / np.linalg.norm(rows, axis=1, keepdims=True)
+    qn = qs / np.linalg.norm(qs, axis=1, keepdims=True)
+    truth = np.argsort(-(qn @ rn.T), axis=1)[:, :10]
+
+    def recall(G):
+        ids, _, _ = oracle.hnsw_search(G, qs, 10, 64)
+        return np.mean([len(set(ids[i]) & set(truth[i])) / 10 for i in range(len(qs))])
+    assert recall(B) >= recall(A) - 0.02
