@@ -219,12 +219,10 @@ int64_t pion_v_quant_beam_1536(pion_quant_beam_view_1536* v) {
         rl.len > ef || rl.capacity < rl.len || (rl.len > 0 && !rl.data))
         return qbeam_fail("bad heaps");
     if (cl.len > n + 1) return qbeam_fail("more candidates than nodes");
-    for (int64_t i = 0; i < cl.len; ++i)
-        if (cl.data[i].id < 0 || cl.data[i].id >= n) return qbeam_fail("a heap entry names no node");
-    for (int64_t i = 0; i < rl.len; ++i)
-        if (rl.data[i].id < 0 || rl.data[i].id >= n) return qbeam_fail("a heap entry names no node");
-    if (rl.len > 0 && rl.capacity < ef && rl.capacity < rl.len + 1)
-        ;  // the results heap never grows past max(len, ef): checked below after the run
+    for (int64_t i = 0; i < cl.len + rl.len; ++i) {
+        const int64_t id = i < cl.len ? cl.data[i].id : rl.data[i - cl.len].id;
+        if (id < 0 || id >= n) return qbeam_fail("a heap entry names no node");
+    }
     pion_b200_ctx* ctx = compat_default_ctx("pion_v_quant_beam_1536");
     if (!ctx) return -1;
     if (use_device(ctx) != 0) return qbeam_fail("cannot select the device");

@@ -185,7 +185,8 @@ int load_file(const char* path, Graph& g, QuantBuffers* q, std::string& why) {
     }
     const int64_t blocks = version < 4 ? max_elem : n;
     std::vector<uint32_t> pool((size_t)n * pool_per);
-    if (!read_all(f, pool.data(), pool.size() * 4) || !skip(f, (uint64_t)(blocks - n) * pool_per * 4)) {
+    if (!read_all(f, pool.data(), pool.size() * 4) ||
+        !skip(f, (uint64_t)(blocks - n) * pool_per * 4)) {
         why = "short neighbour blocks";
         return -1;
     }
@@ -364,7 +365,8 @@ int save_file(const Graph& g, const QuantBuffers* q, const char* path, int64_t m
         for (uint32_t j = 0; j < c0; ++j) blk[j] = g.l0_compact[(size_t)i * 33 + 1 + j];
         blk[8 * M] = c0;
         for (int l = 1; l <= g.level[i]; ++l) {
-            const uint32_t* row = g.upper_links.data() + (size_t)(g.upper_offset[i] + l - 1) * (1 + M);
+            const uint32_t* row =
+                g.upper_links.data() + (size_t)(g.upper_offset[i] + l - 1) * (1 + M);
             const uint32_t cnt = row[0] > (uint32_t)M ? (uint32_t)M : row[0];
             for (int64_t j = 0; j < M; ++j) blk[2 * M + (l - 1) * M + j] = row[1 + j];
             blk[8 * M + l] = cnt;
@@ -388,8 +390,9 @@ int save_file(const Graph& g, const QuantBuffers* q, const char* path, int64_t m
     ok = ok && write_all(f, keys.data(), keys.size());
     if (quant) {
         ok = ok && write_all(f, q->rerank.data(), q->rerank.size() * 4);
+        const size_t res_bytes = q->qjl.empty() ? 0 : q->qjl_res_norms.size() * 4;
         ok = ok && write_all(f, q->qjl.data(), q->qjl.size() * 8) &&
-             write_all(f, q->qjl_res_norms.data(), q->qjl.empty() ? 0 : q->qjl_res_norms.size() * 4);
+             write_all(f, q->qjl_res_norms.data(), res_bytes);
     }
     if (!ok) {
         why = "write failed";

@@ -138,7 +138,8 @@ struct Fixed {
 
 __host__ __device__ constexpr size_t fixed_bytes() { return (sizeof(Fixed) + 15) / 16 * 16; }
 __host__ __device__ constexpr size_t warp_bytes(int ef) {
-    return fixed_bytes() + (size_t)TOP * sizeof(Entry) + ((size_t)ef * sizeof(Entry) + 15) / 16 * 16;
+    return fixed_bytes() + (size_t)TOP * sizeof(Entry) +
+           ((size_t)ef * sizeof(Entry) + 15) / 16 * 16;
 }
 
 __device__ __forceinline__ bool is_deleted(const uint8_t* del, uint32_t i) {
@@ -331,7 +332,9 @@ struct Cand {
     Entry* top;   // [0, TOP)
     Entry* tail;  // [TOP, cap)
     int64_t cap;
-    __device__ __forceinline__ Entry get(int64_t i) const { return i < TOP ? top[i] : tail[i - TOP]; }
+    __device__ __forceinline__ Entry get(int64_t i) const {
+        return i < TOP ? top[i] : tail[i - TOP];
+    }
     __device__ __forceinline__ void put(int64_t i, Entry e) const {
         if (i < TOP)
             top[i] = e;
@@ -639,72 +642,72 @@ __global__ void __launch_bounds__(WARPS * 32, 4) quant_search_kernel(Params p) {
             }
             __syncwarp();
         } else {
-        prologue(p, S, x, reinterpret_cast<float*>(top), lane);
+            prologue(p, S, x, reinterpret_cast<float*>(top), lane);
 
-        // upper levels
-        uint32_t cur = (uint32_t)p.entry;
-        if (lane == 0) {
-            S.ni[0] = cur;
-            S.ns[0] = __ldg(p.node_slot + cur);
-        }
-        __syncwarp();
-        score_batch(p, S, 1, false, lane);
-        float cd = S.nd[0];
-        ++evals;
-        for (int l = p.max_level; l >= 1; --l) {
-            for (int64_t pass = 0; pass <= n; ++pass) {  // `changed` loop
-                bool changed = false;
-                if (__ldg(p.node_level + cur) < l) break;
-                const int64_t nc =
-                    __ldg(p.upper_links + (__ldg(p.upper_offset + cur) + l - 1) * (1 + p.M));
-                int64_t i = 0;
-                while (i < nc) {
-                    if (__ldg(p.node_level + cur) < l) break;
-                    const size_t r = (size_t)(__ldg(p.upper_offset + cur) + l - 1) * (1 + p.M);
-                    const int64_t pos = i + lane;
-                    uint32_t nidx = 0xffffffffu, nslot = 0;
-                    if (pos < nc && pos < p.M) {
-                        nidx = __ldg(p.upper_links + r + 1 + pos);
-                        nslot = __ldg(p.upper_slots + r + 1 + pos);
-                    }
-                    bool ok = nidx < (uint64_t)n;
-                    if (ok && p.kind == kQNano && is_deleted(p.deleted, nidx)) ok = false;
-                    const unsigned okm = __ballot_sync(FULL, ok);
-                    const int at = __popc(okm & ((1u << lane) - 1u));
-                    if (ok) {
-                        S.ni[at] = nidx;
-                        S.ns[at] = nslot;
-                    }
-                    __syncwarp();
-                    score_batch(p, S, __popc(okm), false, lane);
-                    const float d = ok ? S.nd[at] : 0.0f;
-                    evals += __popc(okm) * (lane == 0);
-                    const unsigned better = __ballot_sync(FULL, ok && d < cd);
-                    __syncwarp();  // every lane has read its distance before the next batch
-                    if (better == 0) break;  // positions past M are never scored
-                    const int f = __ffs(better) - 1;
-                    cd = __shfl_sync(FULL, d, f);
-                    cur = __shfl_sync(FULL, nidx, f);
-                    changed = true;
-                    i += f + 1;
-                }
-                if (!changed) break;
+            // upper levels
+            uint32_t cur = (uint32_t)p.entry;
+            if (lane == 0) {
+                S.ni[0] = cur;
+                S.ns[0] = __ldg(p.node_slot + cur);
             }
-        }
+            __syncwarp();
+            score_batch(p, S, 1, false, lane);
+            float cd = S.nd[0];
+            ++evals;
+            for (int l = p.max_level; l >= 1; --l) {
+                for (int64_t pass = 0; pass <= n; ++pass) {  // `changed` loop
+                    bool changed = false;
+                    if (__ldg(p.node_level + cur) < l) break;
+                    const int64_t nc =
+                        __ldg(p.upper_links + (__ldg(p.upper_offset + cur) + l - 1) * (1 + p.M));
+                    int64_t i = 0;
+                    while (i < nc) {
+                        if (__ldg(p.node_level + cur) < l) break;
+                        const size_t r = (size_t)(__ldg(p.upper_offset + cur) + l - 1) * (1 + p.M);
+                        const int64_t pos = i + lane;
+                        uint32_t nidx = 0xffffffffu, nslot = 0;
+                        if (pos < nc && pos < p.M) {
+                            nidx = __ldg(p.upper_links + r + 1 + pos);
+                            nslot = __ldg(p.upper_slots + r + 1 + pos);
+                        }
+                        bool ok = nidx < (uint64_t)n;
+                        if (ok && p.kind == kQNano && is_deleted(p.deleted, nidx)) ok = false;
+                        const unsigned okm = __ballot_sync(FULL, ok);
+                        const int at = __popc(okm & ((1u << lane) - 1u));
+                        if (ok) {
+                            S.ni[at] = nidx;
+                            S.ns[at] = nslot;
+                        }
+                        __syncwarp();
+                        score_batch(p, S, __popc(okm), false, lane);
+                        const float d = ok ? S.nd[at] : 0.0f;
+                        evals += __popc(okm) * (lane == 0);
+                        const unsigned better = __ballot_sync(FULL, ok && d < cd);
+                        __syncwarp();  // every lane has read its distance before the next batch
+                        if (better == 0) break;  // positions past M are never scored
+                        const int f = __ffs(better) - 1;
+                        cd = __shfl_sync(FULL, d, f);
+                        cur = __shfl_sync(FULL, nidx, f);
+                        changed = true;
+                        i += f + 1;
+                    }
+                    if (!changed) break;
+                }
+            }
 
-        // level-0 beam from (cur, cd)
-        if (lane == 0) {
-            S.cand_n = 0;
-            S.res_n = 0;
-            S.res_worst = WORST0;
-            S.abandon = 0;
-            min_push(cand, S.cand_n, Entry{cd, cur});
-            // MaxHeap.push: the worst first, then the entry
-            if (cd > S.res_worst) S.res_worst = cd;
-            max_sift_up(res, S.res_n++, Entry{cd, cur});
-            atomicOr(vis + (cur >> 5), 1u << (cur & 31));
-        }
-        __syncwarp();
+            // level-0 beam from (cur, cd)
+            if (lane == 0) {
+                S.cand_n = 0;
+                S.res_n = 0;
+                S.res_worst = WORST0;
+                S.abandon = 0;
+                min_push(cand, S.cand_n, Entry{cd, cur});
+                // MaxHeap.push: the worst first, then the entry
+                if (cd > S.res_worst) S.res_worst = cd;
+                max_sift_up(res, S.res_n++, Entry{cd, cur});
+                atomicOr(vis + (cur >> 5), 1u << (cur & 31));
+            }
+            __syncwarp();
         }  // from the caller's heaps or from the greedy's node
         for (int64_t step = 0; step <= n; ++step) {
             uint32_t cid = 0;
@@ -733,7 +736,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) quant_search_kernel(Params p) {
                 }
             }
             // a node listed twice counts at its first position only
-            const unsigned same = __match_any_sync(FULL, ok ? nidx : (0x80000000u | (unsigned)lane));
+            const unsigned same =
+                __match_any_sync(FULL, ok ? nidx : (0x80000000u | (unsigned)lane));
             ok = ok && (__ffs(same) - 1 == lane);
             const unsigned keep = __ballot_sync(FULL, ok);
             if (ok) {
@@ -938,7 +942,8 @@ int launch_quant_search(const QuantLaunch& L, cudaStream_t st) {
     p.cand_io_cap = L.cand_io_cap;
     p.res_io = reinterpret_cast<qb::Entry*>(L.res_io);
     p.heap_meta = L.heap_meta;
-    if (L.ctas <= 0 || L.ef < 1 || L.ef > qb::TOP || L.code_bytes % 16 != 0) return PION_B200_ESHAPE;
+    if (L.ctas <= 0 || L.ef < 1 || L.ef > qb::TOP || L.code_bytes % 16 != 0)
+        return PION_B200_ESHAPE;
     const size_t bytes = qb::WARPS * qb::warp_bytes(L.ef);
     if (cudaFuncSetAttribute(qb::quant_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)bytes) != cudaSuccess)
