@@ -294,8 +294,14 @@ class PyMax:
         return root
 
 
+def is_del(A, i):
+    d = A.get("deleted")
+    return d is not None and (int(d[i >> 3]) >> (i & 7)) & 1 == 1
+
+
 def py_beam(A, dist, ef, cand, res, seen):
-    """quant_beam_search_1536_ref's loop over seeded heaps (no deleted nodes here)."""
+    """quant_beam_search_1536_ref's loop over seeded heaps: deleted nodes are skipped before
+    the visited test and never marked."""
     while cand.a:
         c = cand.pop()
         if c[0] > res.worst and len(res.a) >= ef:
@@ -303,7 +309,7 @@ def py_beam(A, dist, ef, cand, res, seen):
         row, srow = A["l0_compact"][c[1]], A["l0_slots"][c[1]]
         for i in range(int(row[0])):
             nidx = int(row[1 + i])
-            if nidx >= A["num_nodes"] or nidx in seen:
+            if nidx >= A["num_nodes"] or is_del(A, nidx) or nidx in seen:
                 continue
             seen.add(nidx)
             d = dist(nidx, int(srow[1 + i]))
@@ -347,6 +353,8 @@ def py_search(A, Q, kind, q, k, ef):
                 row = A["upper_links"][A["upper_offset"][cur] + lv - 1]
                 nidx = int(row[1 + i])
                 if nidx >= A["num_nodes"]:
+                    continue
+                if kind == "nano" and is_del(A, nidx):  # NanoQuant's greedy skips them
                     continue
                 d = dist(nidx, qjl=False)
                 if d < cd:
@@ -481,3 +489,25 @@ def test_beam_from_heaps_matches_python(oracle, qgraph, kind):
     cut, total2, _, _ = oracle.quant_beam_heaps(A, Q, qc, qsc, qn, qsig, qres, 20,
                                                 [(d0, start)], [(d0, start)], d0, cand_cap=5)
     assert total2 == total and cut == got_c[:5]
+
+
+@pytest.mark.parametrize("kind", ["polar", "nano"])
+def test_quant_search_deleted_matches_python(oracle, qgraph, kind):
+    """With a deletion bitmap: the beam skips deleted nodes (all kinds), NanoQuant's
+    greedy skips them too (hnsw.mojo:4179), the others' greedy does not."""
+    g, A, rows, qs = qgraph
+    n = A["num_nodes"]
+    gen = np.random.default_rng(5)
+    dead = gen.choice(n, n // 6, replace=False)
+    bits = np.zeros((n + 7) // 8, np.uint8)
+    for i in dead:
+        bits[i >> 3] |= np.uint8(1 << (i & 7))
+    A2 = dict(A)
+    A2["deleted"] = bits
+    Q = oracle.quant_graph(A, rows, kind)
+    ids, sc, cnt = oracle.quant_search(A2, Q, qs, 10, 24)
+    for t in range(len(qs)):
+        pi, ps = py_search(A2, Q, kind, qs[t], 10, 24)
+        assert cnt[t] == len(pi)
+        assert list(ids[t, :cnt[t]]) == pi
+        assert np.array_equal(sc[t, :cnt[t]].view(np.uint32), np.array(ps, F).view(np.uint32))
