@@ -502,7 +502,10 @@ int pion_v_b200_hnsw_beam_batch(pion_b200_ctx *ctx, const pion_b200_index *index
  * the calibration range) and the result ids[t][j] (external ids, as hnsw_search returns
  * them) dequantised at the middle of each code step: squared L2 under L2, half of it
  * (= 1 - cos) under COSINE, summed in the reference's order.  Ids that name no node keep
- * their score.  q fp32[nq x 1536]; ids, scores [nq x k]. */
+ * their score.  q fp32[nq x 1536]; ids, scores [nq x k].  On a block-quantised graph
+ * (pion_v_b200_register_hnsw_quant) the source is its FP32 copy by node, the query
+ * unclamped; without one it has no source: returns 1 and leaves every score (the
+ * reference returns False). */
 int pion_v_b200_hnsw_metric_scores(pion_b200_ctx *ctx, const pion_b200_index *index,
                                    const float *q, int64_t nq, int64_t k, const int32_t *ids,
                                    float *scores, int mem);

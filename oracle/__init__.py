@@ -696,3 +696,18 @@ def quant_beam_heaps(graph: dict, quant: dict, qcodes, qscales, qnorm, qsig, qre
     del keep
     return ([(cd[i], int(ci[i])) for i in range(cn.value)], tot.value,
             [(rd[i], int(ri[i])) for i in range(rn.value)], np.float32(w.value))
+
+
+def metric_scores_f32(graph: dict, rows, queries, ids, scores):
+    """metric_scores' FP32-copy branch (src/vector/hnsw.mojo:4586-4600) with the rows by
+    node -> new scores (ids that name no node keep theirs)."""
+    L = lib()
+    L.orc_metric_scores_f32.argtypes = [_p, _i64, ctypes.c_int, _p, _p, _i64, _i64, _p, _p]
+    nid, pn = _c(graph["node_ids"], np.int32)
+    r, pr = _c(rows, np.float32)
+    q, pq = _c(np.atleast_2d(queries), np.float32)
+    i, pi = _c(ids, np.int32)
+    out = np.array(scores, np.float32, copy=True)
+    L.orc_metric_scores_f32(pn, graph["num_nodes"], graph["metric"], pr, pq, q.shape[0],
+                            i.shape[1], pi, out.ctypes.data_as(_p))
+    return out

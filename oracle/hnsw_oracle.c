@@ -418,6 +418,46 @@ int64_t orc_hnsw_beam_pool(const orc_hnsw_layout *L, const int8_t *q, float qn, 
     return rc == 0 ? pool.size : -1;
 }
 
+/* metric_scores' FP32-copy branch (src/vector/hnsw.mojo:4586-4600, 4643-4647): the
+ * rows by node (the block-quantised formats keep them so), the query normalised once under
+ * COSINE and not clamped; 4 chains of 8 lanes over 32-element strides (mul then add),
+ * (c0 + c1) + (c2 + c3) lane-wise, the halving reduce_add; COSINE halves it.  ids are
+ * external ids (node_ids of the n nodes); scores in/out. */
+void orc_metric_scores_f32(const int32_t *node_ids, int64_t n, int metric, const float *rows,
+                           const float *queries, int64_t nq, int64_t k, const int32_t *ids,
+                           float *scores) {
+    float qc[HN_DIM];
+    for (int64_t t = 0; t < nq; ++t) {
+        const float *x = queries + t * HN_DIM;
+        if (metric == 1)
+            orc_l2_normalize_fp32(x, qc, HN_DIM);
+        else
+            memcpy(qc, x, HN_DIM * sizeof(float));
+        for (int64_t r = 0; r < k; ++r) {
+            const int32_t ext = ids[t * k + r];
+            int64_t node = -1;
+            for (int64_t i = 0; i < n && node < 0; ++i)
+                if (node_ids[i] == ext) node = i;
+            if (node < 0) continue;
+            const float *v = rows + node * HN_DIM;
+            float acc[4][8];
+            memset(acc, 0, sizeof(acc));
+            for (int d0 = 0; d0 + 32 <= HN_DIM; d0 += 32)
+                for (int ch = 0; ch < 4; ++ch)
+                    for (int l = 0; l < 8; ++l) {
+                        const int d = d0 + 8 * ch + l;
+                        const float e = qc[d] - v[d];
+                        acc[ch][l] = e * e + acc[ch][l];
+                    }
+            float lanes[8];
+            for (int l = 0; l < 8; ++l) lanes[l] = (acc[0][l] + acc[1][l]) + (acc[2][l] + acc[3][l]);
+            for (int w = 8; w > 1; w /= 2)
+                for (int i = 0; i < w / 2; ++i) lanes[i] = lanes[i] + lanes[i + w / 2];
+            scores[t * k + r] = metric == 1 ? lanes[0] * 0.5f : lanes[0];
+        }
+    }
+}
+
 /* metric_scores (src/vector/hnsw.mojo:4523-4651), INT8 codes with one global calibration
  * and no FP32 copy (the Linux build): the query normalised once under COSINE, clamped to
  * [gmin, gmax]; each code dequantised at the middle of its step, c * g + (127.5 g + gmin)

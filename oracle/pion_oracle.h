@@ -159,6 +159,9 @@ float orc_qjl_signs(const float *residual, const uint64_t *rs, uint64_t *dst24);
 float orc_turbo_qjl_row(const float *src, const int8_t *slot, const uint64_t *rs, uint64_t *dst24);
 /* search_fp32_scored's block-quant branch per query: ids (external) / scores [nq x k],
  * out_n [nq] results per query.  0, or -1 on allocation failure. */
+void orc_metric_scores_f32(const int32_t *node_ids, int64_t n, int metric, const float *rows,
+                           const float *queries, int64_t nq, int64_t k, const int32_t *ids,
+                           float *scores);
 int orc_quant_beam_heaps(const orc_quant_layout *L, const int8_t *qc, const float *qs,
                          float qn, const uint64_t *qsig, float qres, int64_t ef, float *cand_d,
                          int64_t *cand_id, int64_t *cand_n, int64_t cand_cap,

@@ -590,7 +590,7 @@ int pion_v_b200_hnsw_metric_scores(pion_b200_ctx* ctx, const pion_b200_index* ix
                                    int64_t nq, int64_t k, const int32_t* ids, float* scores,
                                    int mem) {
     if (!valid_ctx(ctx)) return PION_B200_EINVAL;
-    if (!ix || ix->kind != kHNSW)
+    if (!ix || (ix->kind != kHNSW && ix->kind != kHNSWQuant))
         return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: not an HNSW index");
     if (ix->device != ctx->device)
         return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: index on another device");
@@ -600,6 +600,9 @@ int pion_v_b200_hnsw_metric_scores(pion_b200_ctx* ctx, const pion_b200_index* ix
         return set_error(ctx, PION_B200_EINVAL, "hnsw_metric_scores: bad mem %d", mem);
     if (nq == 0 || ix->n_rows == 0) return 0;
     const auto& h = ix->hnsw;
+    // a block-quantised graph scores from its FP32 copy; without one it has neither source
+    // and keeps its scores (the reference's `return False`)
+    if (ix->kind == kHNSWQuant && !h.rerank_node) return 1;
     if (!h.ext_to_node)
         return set_error(ctx, PION_B200_ESHAPE, "hnsw_metric_scores: external ids too sparse");
     if (nq > (1 << 24) || k > (1 << 16))
@@ -639,7 +642,8 @@ int pion_v_b200_hnsw_metric_scores(pion_b200_ctx* ctx, const pion_b200_index* ix
     if (!rc)
         rc = launch_hnsw_metric(qsrc, (int)nq, (int)k, di, h.ext_to_node, h.ext_base,
                                 h.ext_count, h.node_slot, h.codes, h.gmin, h.gmax,
-                                h.metric == 1, ds, st);
+                                h.metric == 1, ix->kind == kHNSWQuant ? h.rerank_node : nullptr,
+                                ds, st);
     ctx->launches++;
     if (rc) return set_error(ctx, rc, "hnsw_metric_scores: launch failed");
     if (mem == PION_B200_MEM_HOST) {

@@ -537,6 +537,21 @@ int pion_v_b200_register_hnsw_quant(pion_b200_ctx* ctx, const pion_b200_hnsw_lay
             if (!rc && Q->kind == kQTurbo && Q->qjl_random_signs)
                 rc = upload(&h.qjl_rs, Q->qjl_random_signs, 24);
             if (!rc && Q->rerank) rc = upload(&h.rerank_node, Q->rerank, n * kDim);
+            if (!rc) {  // external id -> node, for metric_scores (dense id ranges only)
+                int64_t lo = L->node_ids[0], hi = L->node_ids[0];
+                for (size_t i = 1; i < n; ++i) {
+                    lo = L->node_ids[i] < lo ? L->node_ids[i] : lo;
+                    hi = L->node_ids[i] > hi ? L->node_ids[i] : hi;
+                }
+                const int64_t span = hi - lo + 1;
+                if (span <= 4 * (int64_t)n + 1024) {
+                    std::vector<int32_t> inv((size_t)span, -1);
+                    for (size_t i = 0; i < n; ++i) inv[(size_t)(L->node_ids[i] - lo)] = (int32_t)i;
+                    rc = upload(&h.ext_to_node, inv.data(), (size_t)span);
+                    h.ext_base = lo;
+                    h.ext_count = span;
+                }
+            }
         }
     } catch (const std::bad_alloc&) {
         rc = PION_B200_ENOMEM;

@@ -658,7 +658,8 @@ __global__ void hnsw_metric_kernel(const float* __restrict__ qn, int nq, int k,
                                    const int32_t* __restrict__ ext_to_node, int64_t ext_base,
                                    int64_t ext_count, const uint32_t* __restrict__ node_slot,
                                    const int8_t* __restrict__ codes, float gmin, float gmax,
-                                   int cosine, float* __restrict__ scores) {
+                                   int cosine, const float* __restrict__ rows,
+                                   float* __restrict__ scores) {
     const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (w >= (int64_t)nq * k) return;  // warp-uniform
@@ -671,15 +672,25 @@ __global__ void hnsw_metric_kernel(const float* __restrict__ qn, int nq, int k,
     const float a = __fdiv_rn(range, 254.0f);
     const float b = __fadd_rn(__fmul_rn(127.5f, a), gmin);
     const float* q = qn + (w / k) * DIM;
-    const int8_t* c = codes + (size_t)node_slot[node] * DIM;
     float acc = 0.0f;
+    if (rows) {  // the FP32 copy by node: the unclamped query against the row
+        const float* v = rows + (size_t)node * DIM;
 #pragma unroll 4
-    for (int i = 0; i < DIM / 32; ++i) {
-        const int d = 32 * i + lane;
-        const float qv = fminf(fmaxf(q[d], gmin), gmax);
-        const float x = __fadd_rn(__fmul_rn((float)c[d], a), b);
-        const float t = __fsub_rn(qv, x);
-        acc = __fadd_rn(__fmul_rn(t, t), acc);
+        for (int i = 0; i < DIM / 32; ++i) {
+            const int d = 32 * i + lane;
+            const float t = __fsub_rn(q[d], v[d]);
+            acc = __fadd_rn(__fmul_rn(t, t), acc);
+        }
+    } else {
+        const int8_t* c = codes + (size_t)node_slot[node] * DIM;
+#pragma unroll 4
+        for (int i = 0; i < DIM / 32; ++i) {
+            const int d = 32 * i + lane;
+            const float qv = fminf(fmaxf(q[d], gmin), gmax);
+            const float x = __fadd_rn(__fmul_rn((float)c[d], a), b);
+            const float t = __fsub_rn(qv, x);
+            acc = __fadd_rn(__fmul_rn(t, t), acc);
+        }
     }
     const int l = lane & 7;
     const float c0 = __shfl_sync(FULL, acc, l), c1 = __shfl_sync(FULL, acc, 8 + l);
@@ -776,12 +787,12 @@ int hnsw_ctas_per_sm(int ef) {
 int launch_hnsw_metric(const float* qn, int nq, int k, const int32_t* ids,
                        const int32_t* ext_to_node, int64_t ext_base, int64_t ext_count,
                        const uint32_t* node_slot, const int8_t* codes, float gmin, float gmax,
-                       int cosine, float* scores, cudaStream_t st) {
+                       int cosine, const float* rows, float* scores, cudaStream_t st) {
     const int64_t warps = (int64_t)nq * k;
     if (warps <= 0) return 0;
     hb::hnsw_metric_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
         qn, nq, k, ids, ext_to_node, ext_base, ext_count, node_slot, codes, gmin, gmax, cosine,
-        scores);
+        rows, scores);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

@@ -204,10 +204,11 @@ int launch_hnsw_quantize(const float* q, int nq, float gmin, float scale, int8_t
 int launch_hnsw_beam(const HnswLaunch& launch, cudaStream_t st);
 int launch_hnsw_relayout(const int8_t* src, int64_t n, int64_t stride, int64_t hdr,
                          int8_t* codes, float* norms, cudaStream_t st);
+// rows: the FP32 copy by node (the metric then reads it, unclamped), or null (the codes)
 int launch_hnsw_metric(const float* qn, int nq, int k, const int32_t* ids,
                        const int32_t* ext_to_node, int64_t ext_base, int64_t ext_count,
                        const uint32_t* node_slot, const int8_t* codes, float gmin, float gmax,
-                       int cosine, float* scores, cudaStream_t st);
+                       int cosine, const float* rows, float* scores, cudaStream_t st);
 
 // ---- quant.cu
 struct QuantLaunch {

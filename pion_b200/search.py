@@ -805,6 +805,26 @@ class HNSWQuantIndex(_Index):
                                                          mem))
         return ids, sc, found
 
+    def metric_scores(self, q, ids, scores, ctx: Context | None = None):
+        """metric_scores (src/vector/hnsw.mojo:4523-4651) from the FP32 copy: the reply
+        scores of `ids` (external ids) in the index metric (squared L2, or 1 - cos under
+        COSINE); `scores` (contiguous float32, host) is updated in place.  Returns False,
+        leaving the scores, when the graph was registered without FP32 rows."""
+        c = ctx or self.ctx
+        pq, mem, kq = _ptr(q, np.float32, "q")
+        pi, mi, ki = _ptr(ids, np.int32, "ids")
+        if not (isinstance(scores, np.ndarray) and scores.dtype == np.float32 and
+                scores.flags["C_CONTIGUOUS"]):
+            raise TypeError("scores must be a contiguous float32 array (updated in place)")
+        m = _same_mem(mem, mi, MEM_HOST)
+        nq, k = ids.shape
+        rc = c.lib.pion_v_b200_hnsw_metric_scores(c.h, self.h, pq, nq, k, pi,
+                                                  scores.ctypes.data, m)
+        if rc == 1:
+            return False
+        c.check(rc)
+        return True
+
     def last_stats(self, ctx: Context | None = None) -> dict:
         """Work of the context's last search: distance evaluations, level-0 expansions,
         queries re-run with room for every node in the candidate heap."""

@@ -229,3 +229,28 @@ def test_quant_beam_symbol(ctx, oracle, graphs, kind, cap):
         if cap is not None:
             assert total > cap  # the whole heap did not fit the List: cut at its capacity
     lib.pion_v_b200_beam_forget(None)
+
+
+def test_quant_metric_scores(ctx, oracle, graphs):
+    """metric_scores on a block-quantised graph reads its FP32 copy (hnsw.mojo:4586-4600):
+    bit for bit the oracle's; without the copy the scores stay."""
+    import pion_b200
+    for metric in ("cosine", "l2"):
+        g, A, rows, qs = graphs[metric]
+        qz = pion_b200.HNSWQuant(g, rows, "turbo")
+        Q = qz.arrays()
+        ix = pion_b200.HNSWQuantIndex(ctx, g, qz)
+        ids, sc, found = ix.search(qs, 10, 40)
+        ids = np.array(ids)
+        ids[0, 3] = 999999  # names no node: keeps its score
+        got = np.array(sc, np.float32)
+        assert ix.metric_scores(qs, ids, got) is True
+        want = oracle.metric_scores_f32(A, Q["rerank"], qs, ids, sc)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert got[0, 3] == sc[0, 3]
+        ix.free()
+        bare = pion_b200.HNSWQuantIndex(ctx, g, qz, rerank=False)
+        kept = np.array(sc, np.float32)
+        assert bare.metric_scores(qs, ids, kept) is False
+        assert np.array_equal(kept, sc)
+        bare.free()
