@@ -217,14 +217,19 @@ struct Builder {
     std::unique_ptr<std::atomic<uint8_t>[]> locks;
     std::vector<int64_t> link_base, cnt_base;
     std::vector<uint32_t> links;
+    // the distance of every list entry to the list's node (dist_i8, exact), kept beside
+    // it so the evict-farthest choice reads it instead of recomputing the whole list
+    std::vector<float> link_d;
     std::atomic<uint64_t> link_drops{0};
 
     Builder(Graph& graph, const float* r) : g(graph), rows(r) {}
 
     int64_t cap(int l) const { return l == 0 ? 2 * g.M : g.M; }
-    uint32_t* list(int64_t i, int l) {
-        return links.data() + link_base[i] + (l == 0 ? 0 : 2 * g.M + (int64_t)(l - 1) * g.M);
+    int64_t list_at(int64_t i, int l) const {
+        return link_base[i] + (l == 0 ? 0 : 2 * g.M + (int64_t)(l - 1) * g.M);
     }
+    uint32_t* list(int64_t i, int l) { return links.data() + list_at(i, l); }
+    float* dlist(int64_t i, int l) { return link_d.data() + list_at(i, l); }
     std::atomic<uint32_t>& count(int64_t i, int l) { return cnt[cnt_base[i] + l]; }
     const int8_t* code(int64_t i) const { return g.codes.data() + i * g.dim; }
     void lock(int64_t i) {
@@ -248,6 +253,7 @@ struct Builder {
         std::vector<float> fbuf;
         std::vector<HeapNode> all;
         std::vector<uint32_t> pruned, discarded;
+        std::vector<float> pruned_d, discarded_d;  // their distances to the query
     };
 
     void init_scratch(Scratch& s) {
@@ -290,6 +296,8 @@ struct Builder {
     void prune(const std::vector<HeapNode>& all, int64_t m_limit, Scratch& s) {
         s.pruned.clear();
         s.discarded.clear();
+        s.pruned_d.clear();
+        s.discarded_d.clear();
         for (int64_t i = (int64_t)all.size() - 1; i >= 0; --i) {
             if ((int64_t)s.pruned.size() >= m_limit) break;
             const HeapNode c = all[i];
@@ -301,15 +309,19 @@ struct Builder {
                 }
             }
             (good ? s.pruned : s.discarded).push_back(c.id);
+            (good ? s.pruned_d : s.discarded_d).push_back(c.d);
         }
-        for (size_t i = 0; (int64_t)s.pruned.size() < m_limit && i < s.discarded.size(); ++i)
+        for (size_t i = 0; (int64_t)s.pruned.size() < m_limit && i < s.discarded.size(); ++i) {
             s.pruned.push_back(s.discarded[i]);
+            s.pruned_d.push_back(s.discarded_d[i]);
+        }
     }
 
     // Position and distance of the farthest entry of node i's list at `level`
     // (first maximum; an out-of-range id counts as infinitely far).
     int64_t farthest(int64_t i, int level, uint32_t nc, float& worst) {
         const uint32_t* lst = list(i, level);
+        const float* dl = dlist(i, level);
         int64_t pos = 0;
         worst = -1.0f;
         for (uint32_t k = 0; k < nc; ++k) {
@@ -318,7 +330,7 @@ struct Builder {
                 worst = 1e30f;
                 return k;
             }
-            const float d = dist_i8(code(i), code(e), g.dim);
+            const float d = dl[k];
             if (worst < 0.0f || d > worst) {
                 worst = d;
                 pos = k;
@@ -327,23 +339,32 @@ struct Builder {
         return pos;
     }
 
-    void add_published(int64_t i, int level, uint32_t nb) {
+    // Appends nb (at distance d from node i) to i's list when it has room.
+    void add_published(int64_t i, int level, uint32_t nb, float d) {
         if (level > g.level[i]) return;
         const uint32_t c = count(i, level).load(std::memory_order_relaxed);
         if ((int64_t)c < cap(level)) {
             list(i, level)[c] = nb;
+            dlist(i, level)[c] = d;
             count(i, level).store(c + 1, std::memory_order_release);
         }
+    }
+
+    void set_entry(int64_t i, int level, int64_t pos, uint32_t nb, float d) {
+        list(i, level)[pos] = nb;
+        dlist(i, level)[pos] = d;
     }
 
     // Swap-remove `target` from node i's list at `level`.
     void remove_link(int64_t i, int level, uint32_t target) {
         if (level > g.level[i]) return;
         uint32_t* lst = list(i, level);
+        float* dl = dlist(i, level);
         const uint32_t c = count(i, level).load(std::memory_order_relaxed);
         for (uint32_t k = 0; k < c; ++k) {
             if (lst[k] == target) {
                 lst[k] = lst[c - 1];
+                dl[k] = dl[c - 1];
                 count(i, level).store(c - 1, std::memory_order_release);
                 return;
             }
@@ -357,6 +378,7 @@ struct Builder {
     // node is insert() (a level's links never change a lower level's search).
     struct Plan {
         std::vector<uint32_t> ids;
+        std::vector<float> d;  // their distances to the node
         std::vector<uint32_t> offs;
         int top = -1;
     };
@@ -367,6 +389,7 @@ struct Builder {
         const float* v = row(id, s.fbuf);
         int64_t ep = g.entry;
         p.ids.clear();
+        p.d.clear();
         p.offs.assign(1, 0);
         for (int l = g.max_level; l > lvl; --l) {
             float best = dist_f32_i8(v, code(ep), g.dim, scale, offset);
@@ -398,6 +421,7 @@ struct Builder {
                 ep = s.all.back().id;
                 prune(s.all, cap(l), s);
                 p.ids.insert(p.ids.end(), s.pruned.begin(), s.pruned.end());
+                p.d.insert(p.d.end(), s.pruned_d.begin(), s.pruned_d.end());
             }
             p.offs.push_back((uint32_t)p.ids.size());
         }
@@ -411,27 +435,28 @@ struct Builder {
             const int64_t m_limit = cap(l);
             for (uint32_t j = p.offs[k]; j < p.offs[k + 1]; ++j) {
                 const uint32_t nb = p.ids[j];
+                const float dnb = p.d[j];  // dist_i8(q, code(nb)), as the search found it
                 int64_t evicted = -1;
                 const uint32_t nc = count(nb, l).load(std::memory_order_relaxed);
                 if ((int64_t)nc < m_limit) {
-                    add_published(nb, l, (uint32_t)id);
+                    add_published(nb, l, (uint32_t)id, dnb);
                 } else {
                     float worst;
                     const int64_t pos = farthest(nb, l, nc, worst);
-                    if (dist_i8(code(nb), q, g.dim) < worst) {
+                    if (dnb < worst) {
                         evicted = list(nb, l)[pos];
-                        list(nb, l)[pos] = (uint32_t)id;
+                        set_entry(nb, l, pos, (uint32_t)id, dnb);
                     }
                 }
                 if (evicted >= 0 && evicted < g.n) remove_link(evicted, l, nb);
                 const uint32_t onc = count(id, l).load(std::memory_order_relaxed);
                 if ((int64_t)onc < m_limit) {
-                    add_published(id, l, nb);
+                    add_published(id, l, nb, dnb);
                 } else {
                     float worst;
                     const int64_t pos = farthest(id, l, onc, worst);
-                    if (dist_i8(q, code(nb), g.dim) < worst)
-                        list(id, l)[pos] = nb;
+                    if (dnb < worst)
+                        set_entry(id, l, pos, nb, dnb);
                     else
                         link_drops.fetch_add(1, std::memory_order_relaxed);
                 }
@@ -474,19 +499,20 @@ struct Builder {
             const int64_t m_limit = cap(l);
             ep = s.all.back().id;
             prune(s.all, m_limit, s);
-            for (uint32_t nb : s.pruned) {
+            for (size_t j = 0; j < s.pruned.size(); ++j) {
+                const uint32_t nb = s.pruned[j];
+                const float dnb = s.pruned_d[j];  // dist_i8(q, code(nb))
                 int64_t evicted = -1;
                 lock(nb);
                 const uint32_t nc = count(nb, l).load(std::memory_order_relaxed);
                 if ((int64_t)nc < m_limit) {
-                    add_published(nb, l, (uint32_t)id);
+                    add_published(nb, l, (uint32_t)id, dnb);
                 } else {
                     float worst;
                     const int64_t pos = farthest(nb, l, nc, worst);
-                    const float d_new = dist_i8(code(nb), q, g.dim);
-                    if (d_new < worst) {
+                    if (dnb < worst) {
                         evicted = list(nb, l)[pos];
-                        list(nb, l)[pos] = (uint32_t)id;
+                        set_entry(nb, l, pos, (uint32_t)id, dnb);
                     }
                 }
                 unlock(nb);
@@ -498,13 +524,12 @@ struct Builder {
                 lock(id);
                 const uint32_t onc = count(id, l).load(std::memory_order_relaxed);
                 if ((int64_t)onc < m_limit) {
-                    add_published(id, l, nb);
+                    add_published(id, l, nb, dnb);
                 } else {
                     float worst;
                     const int64_t pos = farthest(id, l, onc, worst);
-                    const float d_new = dist_i8(q, code(nb), g.dim);
-                    if (d_new < worst)
-                        list(id, l)[pos] = nb;
+                    if (dnb < worst)
+                        set_entry(id, l, pos, nb, dnb);
                     else
                         link_drops.fetch_add(1, std::memory_order_relaxed);
                 }
@@ -531,21 +556,23 @@ struct Builder {
         while (s.res.size() > 0) s.all.push_back(s.res.pop());
         const int64_t m_limit = 2 * g.M;
         prune(s.all, m_limit, s);
-        for (uint32_t nb : s.pruned) {
+        for (size_t j = 0; j < s.pruned.size(); ++j) {
+            const uint32_t nb = s.pruned[j];
+            const float dnb = s.pruned_d[j];  // dist_i8(q, code(nb))
             if ((int64_t)nb == u) continue;
             if (has_link(u, nb)) continue;
             if ((int64_t)count(u, 0).load() >= m_limit) break;
-            add_published(u, 0, nb);
+            add_published(u, 0, nb, dnb);
             if (has_link(nb, (uint32_t)u)) continue;
             const uint32_t nc = count(nb, 0).load();
             if ((int64_t)nc < m_limit) {
-                add_published(nb, 0, (uint32_t)u);
+                add_published(nb, 0, (uint32_t)u, dnb);
             } else {
                 float worst;
                 const int64_t pos = farthest(nb, 0, nc, worst);
-                if (dist_i8(code(nb), q, g.dim) < worst) {
+                if (dnb < worst) {
                     const uint32_t ev = list(nb, 0)[pos];
-                    list(nb, 0)[pos] = (uint32_t)u;
+                    set_entry(nb, 0, pos, (uint32_t)u, dnb);
                     if (ev < (uint32_t)g.n) remove_link(ev, 0, nb);
                 }
             }
@@ -633,11 +660,13 @@ struct Builder {
                 s.all.clear();
                 while (s.res.size() > 0) s.all.push_back(s.res.pop());  // farthest first
                 int64_t pick = -1;
+                float pick_d = 0.0f;  // dist_i8(code(u), code(pick)), as the search found it
                 for (int64_t fi = (int64_t)s.all.size() - 1; fi >= 0; --fi) {
                     const uint32_t r = s.all[fi].id;
                     if ((int64_t)r != u && reach[r] && (int64_t)count(r, 0).load() < capl) {
-                        add_published(r, 0, (uint32_t)u);
+                        add_published(r, 0, (uint32_t)u, s.all[fi].d);
                         pick = r;
+                        pick_d = s.all[fi].d;
                         break;
                     }
                 }
@@ -645,28 +674,29 @@ struct Builder {
                     const uint32_t r = s.all[fi].id;
                     if ((int64_t)r == u || !reach[r]) continue;
                     const uint32_t nc = count(r, 0).load();
-                    uint32_t* lst = list(r, 0);
+                    const uint32_t* lst = list(r, 0);
+                    const float* dl = dlist(r, 0);
                     int64_t wpos = -1;
                     float wd = -1.0f;
                     for (uint32_t k = 0; k < nc; ++k) {
                         if (lst[k] >= (uint32_t)n) continue;
-                        const float d = dist_i8(code(r), code(lst[k]), g.dim);
-                        if (d > wd) {
-                            wd = d;
+                        if (dl[k] > wd) {
+                            wd = dl[k];
                             wpos = k;
                         }
                     }
                     if (wpos < 0) continue;
                     const uint32_t w = lst[wpos];
                     if (indeg[w] < 2) continue;
-                    lst[wpos] = (uint32_t)u;
+                    set_entry(r, 0, wpos, (uint32_t)u, s.all[fi].d);
                     --indeg[w];
                     pick = r;
+                    pick_d = s.all[fi].d;
                 }
                 if (pick < 0) continue;
                 ++indeg[u];
                 if ((int64_t)count(u, 0).load() < capl && !has_link(u, (uint32_t)pick)) {
-                    add_published(u, 0, (uint32_t)pick);
+                    add_published(u, 0, (uint32_t)pick, pick_d);
                     ++indeg[pick];
                 }
                 ++linked;
@@ -866,6 +896,7 @@ int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int
         ct += 1 + g.level[i];
     }
     b.links.assign((size_t)lt, 0xFFFFFFFFu);
+    b.link_d.assign((size_t)lt, 0.0f);
     b.cnt.reset(new std::atomic<uint32_t>[(size_t)std::max<int64_t>(ct, 1)]);
     for (int64_t i = 0; i < ct; ++i) b.cnt[i].store(0, std::memory_order_relaxed);
     b.locks.reset(new std::atomic<uint8_t>[(size_t)std::max<int64_t>(n, 1)]);
