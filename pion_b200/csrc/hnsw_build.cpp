@@ -281,6 +281,17 @@ struct Builder {
             if (level > g.level[c.id]) continue;
             const uint32_t nc = count(c.id, level).load(std::memory_order_acquire);
             const uint32_t* lst = list(c.id, level);
+            // the codes of the unvisited neighbours towards the cache before the first
+            // distance (the first lines of each; the rest follow as it streams)
+            for (uint32_t i = 0; i < nc; ++i) {
+                const uint32_t nb = lst[i];
+                if (nb >= (uint32_t)g.n || s.visited[nb] == s.epoch) continue;
+                const char* p = reinterpret_cast<const char*>(code(nb));
+                _mm_prefetch(p, _MM_HINT_T0);
+                _mm_prefetch(p + 64, _MM_HINT_T0);
+                _mm_prefetch(p + 128, _MM_HINT_T0);
+                _mm_prefetch(p + 192, _MM_HINT_T0);
+            }
             for (uint32_t i = 0; i < nc; ++i) {
                 const uint32_t nb = lst[i];
                 if (nb >= (uint32_t)g.n) continue;
