@@ -80,6 +80,8 @@ def lib() -> ctypes.CDLL:
             L.orc_shard_merge_asc.restype = _i64
             L.orc_hnsw_search.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p, _p, _i32]
             L.orc_hnsw_search.restype = _i32
+            L.orc_hnsw_search_ft.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p, _p, _i32]
+            L.orc_hnsw_search_ft.restype = _i32
             L.orc_hnsw_query_codes.argtypes = [_p, _p, _i64, _p]
             L.orc_hnsw_beam_pool.argtypes = [_p, _p, _f32, _i64, _p, _p, _i64, _i64, _p, _p]
             L.orc_hnsw_beam_pool.restype = _i64
@@ -326,13 +328,16 @@ def shard_merge_asc(ids, scores, k: int):
     return oi[:got], os_[:got]
 
 
-def hnsw_search(graph: dict, queries, k: int, ef: int, nthreads: int | None = None):
+def hnsw_search(graph: dict, queries, k: int, ef: int, nthreads: int | None = None,
+                ft: bool = False):
     """search_fp32_scored at dim 1536 (src/vector/hnsw.mojo:4136-4521) over a graph in
     the compact layout (a dict with the fields of pion_b200_hnsw_layout as numpy arrays
     and scalars): upper-level greedy in code space (:3789-3848), then
     beam_search_1536_ref (src/vector/reference/beam_1536.mojo:85-135) over a LinearPool
-    (src/common/heap.mojo:133-234).  Returns (ids int32 [nq, k], dist float32 [nq, k],
-    stats {evals, expansions, upper_evals})."""
+    (src/common/heap.mojo:133-234).  ft=True: the FT.SEARCH composition, whose start node
+    comes from _upper_level_greedy on the raw query (greedy codes of the once-normalised
+    query; src/commands/vector.mojo:4514-4518).  Returns (ids int32 [nq, k], dist float32
+    [nq, k], stats {evals, expansions, upper_evals})."""
     L = lib()
     lay, keep = _hnsw_layout(graph)
     q, qp = _c(queries, np.float32)
@@ -340,7 +345,8 @@ def hnsw_search(graph: dict, queries, k: int, ef: int, nthreads: int | None = No
     ids = np.empty((nq, k), np.int32)
     dist = np.empty((nq, k), np.float32)
     st = np.zeros(3, np.int64)
-    rc = L.orc_hnsw_search(ctypes.byref(lay), qp, nq, k, ef, ids.ctypes.data_as(_p),
+    fn = L.orc_hnsw_search_ft if ft else L.orc_hnsw_search
+    rc = fn(ctypes.byref(lay), qp, nq, k, ef, ids.ctypes.data_as(_p),
                            dist.ctypes.data_as(_p), st.ctypes.data_as(_p),
                            nthreads or default_threads())
     if rc != 0:

@@ -146,6 +146,7 @@ struct hnsw_job {
     const orc_hnsw_layout *L;
     const float *queries;
     int64_t k, ef;
+    int greedy_passes;  /* normalisations before the greedy's codes (COSINE): 2, or 1 */
     int32_t *out_ids;
     float *out_dist;
     _Atomic int64_t evals, expansions, upper, bad;
@@ -294,10 +295,20 @@ static void hnsw_item(void *ctx, int64_t t, void *raw) {
     for (int i = 0; i < HN_DIM; ++i) qn_int += (int32_t)q[i] * (int32_t)q[i];
     const float qn = (float)qn_int;
     int64_t n_upper = 0, n_evals = 0, n_expand = 0;
+    /* FT.SEARCH's start node: _upper_level_greedy quantises the raw query (normalised
+     * once, hnsw.mojo:3850-3865) before search_fp32_scored normalises it twice for the
+     * beam (src/commands/vector.mojo:4514-4518, src/network/slow_path.mojo:3310-3314). */
+    int8_t gq_buf[HN_DIM];
+    const int8_t *gq = q;
+    if (job->greedy_passes != 2) {
+        float gtmp[HN_DIM];
+        query_codes_n(L, job->queries + t * HN_DIM, gtmp, gq_buf, job->greedy_passes);
+        gq = gq_buf;
+    }
 
     /* _upper_greedy_codes: levels max_level..1, exact INT8 L2 on codes. */
     uint32_t curr = (uint32_t)L->entry_point;
-    float curr_dist = (float)ref_l2(q, slot_vec(L, L->node_slot[curr]), HN_DIM);
+    float curr_dist = (float)ref_l2(gq, slot_vec(L, L->node_slot[curr]), HN_DIM);
     n_upper++;
     for (int64_t l = L->max_level; l > 0; --l) {
         int changed = 1;
@@ -318,7 +329,7 @@ static void hnsw_item(void *ctx, int64_t t, void *raw) {
                 const uint32_t nidx = lst[1 + i];
                 if (nidx >= (uint32_t)L->num_nodes) continue;
                 if (is_deleted(L, nidx)) continue;
-                const float d = (float)ref_l2(q, slot_vec(L, L->node_slot[nidx]), HN_DIM);
+                const float d = (float)ref_l2(gq, slot_vec(L, L->node_slot[nidx]), HN_DIM);
                 n_upper++;
                 if (d < best) {
                     best = d;
@@ -355,8 +366,26 @@ static void hnsw_item(void *ctx, int64_t t, void *raw) {
     job->upper += n_upper;
 }
 
+static int hnsw_search_passes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
+                              int64_t k, int64_t ef, int32_t *out_ids, float *out_dist,
+                              int64_t *stats3, int nthreads, int greedy_passes);
+
 int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, int64_t k,
                     int64_t ef, int32_t *out_ids, float *out_dist, int64_t *stats3, int nthreads) {
+    return hnsw_search_passes(L, queries, nq, k, ef, out_ids, out_dist, stats3, nthreads, 2);
+}
+
+/* The FT.SEARCH composition: the start node as _upper_level_greedy finds it on the raw
+ * query (codes of the once-normalised query), then search_fp32_scored from that node. */
+int orc_hnsw_search_ft(const orc_hnsw_layout *L, const float *queries, int64_t nq, int64_t k,
+                       int64_t ef, int32_t *out_ids, float *out_dist, int64_t *stats3,
+                       int nthreads) {
+    return hnsw_search_passes(L, queries, nq, k, ef, out_ids, out_dist, stats3, nthreads, 1);
+}
+
+static int hnsw_search_passes(const orc_hnsw_layout *L, const float *queries, int64_t nq,
+                              int64_t k, int64_t ef, int32_t *out_ids, float *out_dist,
+                              int64_t *stats3, int nthreads, int greedy_passes) {
     if (L->dim != HN_DIM || k < 1 || ef < 1) return -1;
     if (L->num_nodes > 0 && (L->entry_point < 0 || L->entry_point >= L->num_nodes)) return -1;
     struct hnsw_job job;
@@ -364,6 +393,7 @@ int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, 
     job.queries = queries;
     job.k = k;
     job.ef = ef;
+    job.greedy_passes = greedy_passes;
     job.out_ids = out_ids;
     job.out_dist = out_dist;
     job.evals = 0;

@@ -92,6 +92,8 @@ typedef struct orc_hnsw_layout {
  * Returns 0, or -1 on a layout the restatement cannot follow. */
 int orc_hnsw_search(const orc_hnsw_layout *L, const float *queries, int64_t nq, int64_t k,
                     int64_t ef, int32_t *out_ids, float *out_dist, int64_t *stats3, int nthreads);
+int orc_hnsw_search_ft(const orc_hnsw_layout *L, const float *queries, int64_t nq, int64_t k,
+                    int64_t ef, int32_t *out_ids, float *out_dist, int64_t *stats3, int nthreads);
 /* The query codes of _quantize_query_to_int8 (hnsw.mojo:657-680) after the search's
  * normalisation: codes [nq x dim]. */
 void orc_hnsw_query_codes(const orc_hnsw_layout *L, const float *queries, int64_t nq,

@@ -184,3 +184,17 @@ def test_batched_build_is_deterministic_and_sound(oracle, built):
         ids, _, _ = oracle.hnsw_search(G, qs, 10, 64)
         return np.mean([len(set(ids[i]) & set(truth[i])) / 10 for i in range(len(qs))])
     assert recall(B) >= recall(A) - 0.02
+
+
+def test_ft_search_start_node_composition(oracle, built):
+    """FT.SEARCH takes its start node from _upper_level_greedy on the raw query (codes of the
+    once-normalised query, src/commands/vector.mojo:4514-4518) and then runs
+    search_fp32_scored from it, whose beam quantises the twice-normalised query.  The two
+    greedy code sets differ only where the second normalisation moves a value across a
+    rounding boundary, so the composition answers as the direct search does here."""
+    g, A, rows, qs = built
+    i0, d0, s0 = oracle.hnsw_search(A, qs, 10, 32)
+    i1, d1, s1 = oracle.hnsw_search(A, qs, 10, 32, ft=True)
+    same = (i0 == i1).all(1) & (d0.view(np.uint32) == d1.view(np.uint32)).all(1)
+    assert same.mean() >= 0.99
+    assert s1["expansions"] > 0
