@@ -511,3 +511,29 @@ def test_quant_search_deleted_matches_python(oracle, qgraph, kind):
         assert cnt[t] == len(pi)
         assert list(ids[t, :cnt[t]]) == pi
         assert np.array_equal(sc[t, :cnt[t]].view(np.uint32), np.array(ps, F).view(np.uint32))
+
+
+@pytest.mark.parametrize("seed", [3, 11])
+def test_quant_search_randomised_against_python(oracle, seed):
+    """Small random graphs (M, ef, k, metric and kind drawn per case) with duplicated rows
+    (ties in every distance): the oracle and the statement-by-statement Python restatement
+    agree on ids and score bits."""
+    import pion_b200
+    gen = np.random.default_rng(seed)
+    n = int(gen.integers(300, 700))
+    rows, qs = mixture_np(n, 1536, int(gen.integers(4, 16)), seed=seed, n_queries=3)
+    rows[n // 2:n // 2 + 20] = rows[:20]  # exact duplicates: equal distances
+    metric = ["cosine", "l2"][seed % 2]
+    g = pion_b200.HNSWGraph(rows, M=int(gen.integers(4, 9)), ef_construction=32,
+                           metric=metric, threads=1)
+    A = g.arrays()
+    for kind in ("polar", "nano", "turbo"):
+        Q = oracle.quant_graph(A, rows, kind)
+        k, ef = int(gen.integers(1, 12)), int(gen.integers(1, 40))
+        ids, sc, cnt = oracle.quant_search(A, Q, qs, k, ef)
+        for t in range(len(qs)):
+            pi, ps = py_search(A, Q, kind, qs[t], k, ef)
+            assert cnt[t] == len(pi)
+            assert list(ids[t, :cnt[t]]) == pi
+            assert np.array_equal(sc[t, :cnt[t]].view(np.uint32),
+                                  np.array(ps, F).view(np.uint32))
