@@ -18,8 +18,9 @@ from .search import (  # noqa: F401
     l2_normalize_rows,
     merge_topk,
     quantize_rows_i8,
+    rescore_knn,
 )
 
 __all__ = ["Context", "FlatI8Index", "FlatF32Index", "BQIndex", "HNSWGraph", "HNSWIndex",
            "HNSWQuant", "HNSWQuantIndex", "quantize_rows_i8",
-           "l2_normalize_rows", "merge_topk", "PionError", "load"]
+           "l2_normalize_rows", "merge_topk", "rescore_knn", "PionError", "load"]

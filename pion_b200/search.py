@@ -832,3 +832,19 @@ class HNSWQuantIndex(_Index):
         out = (ctypes.c_int64 * 3)()
         c.check(c.lib.pion_v_b200_hnsw_last_stats(c.h, out))
         return dict(zip(("evals", "expansions", "reruns"), list(out)))
+
+
+def rescore_knn(index, q, ids, scores, ctx: Context | None = None):
+    """_rescore_knn (src/commands/vector.mojo:1091-1105) for a batch: the reply scores of
+    `ids` in the index metric (metric_scores on the GPU), then each row re-sorted by them,
+    ascending and stable (the reference's insertion sort), ids alongside.  `ids` int32
+    [nq, k] and `scores` float32 [nq, k], host arrays, are updated in place; when the index
+    has no source for metric scores (a block-quantised graph without FP32 rows) both stay
+    as they are.  Returns (ids, scores)."""
+    ok = index.metric_scores(q, ids, scores, ctx=ctx)
+    if ok is False:
+        return ids, scores
+    order = np.argsort(scores, axis=1, kind="stable")
+    ids[...] = np.take_along_axis(ids, order, axis=1)
+    scores[...] = np.take_along_axis(scores, order, axis=1)
+    return ids, scores

@@ -198,3 +198,37 @@ def test_ft_search_start_node_composition(oracle, built):
     same = (i0 == i1).all(1) & (d0.view(np.uint32) == d1.view(np.uint32)).all(1)
     assert same.mean() >= 0.99
     assert s1["expansions"] > 0
+
+
+def test_rescore_knn_sorts_like_the_reference():
+    """rescore_knn's re-sort is _rescore_knn's insertion sort (src/commands/vector.mojo:
+    1100-1105): ascending, equal scores keep their order; an index with no metric source
+    leaves both arrays."""
+    import pion_b200
+
+    class Fake:
+        def __init__(self, new, ok=True):
+            self.new, self.ok = new, ok
+
+        def metric_scores(self, q, ids, scores, ctx=None):
+            if not self.ok:
+                return False
+            scores[...] = self.new
+            return True
+
+    gen = np.random.default_rng(4)
+    ids = np.arange(40, dtype=np.int32).reshape(4, 10)
+    new = gen.integers(0, 5, (4, 10)).astype(np.float32)  # many ties
+    got_i, got_s = pion_b200.rescore_knn(Fake(new), None, ids.copy(), np.zeros((4, 10), np.float32))
+    for t in range(4):
+        si, ss = list(ids[t]), list(new[t])
+        for a in range(1, 10):
+            b = a
+            while b > 0 and ss[b] < ss[b - 1]:
+                ss[b], ss[b - 1] = ss[b - 1], ss[b]
+                si[b], si[b - 1] = si[b - 1], si[b]
+                b -= 1
+        assert list(got_i[t]) == si and list(got_s[t]) == ss
+    keep_i, keep_s = ids.copy(), new.copy()
+    pion_b200.rescore_knn(Fake(None, ok=False), None, keep_i, keep_s)
+    assert np.array_equal(keep_i, ids) and np.array_equal(keep_s, new)
