@@ -129,55 +129,124 @@ def profiled_traffic(key: str):
 
 
 class ClockMonitor:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks, power and throttle reasons sampled DURING the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    A host thread reads them through NVML every `period_s` (read-only queries: clock,
+    max clock, power, clocks-event reasons), so a timed region of a few tens of ms still
+    gets several samples; nvidia-smi is the fallback when NVML is unavailable."""
 
-    def __init__(self, device_index: int):
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("sw_power_cap", 0x4))
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.dev = device_index
+        self.period = period_s
+        self.samples = []
+        self.thread = None
         self.proc = None
         self.path = None
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.dev]) if vis else self.dev
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
 
     def start(self):
+        import threading
         try:
+            nv, h = self._nvml_handle()
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.stop_flag = threading.Event()
+
+            def run():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                             float(smax), int(get_reasons(h)),
+                                             nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                    except Exception:
+                        pass
+                    self.stop_flag.wait(self.period)
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            self.source = f"NVML every {self.period * 1000:.0f} ms"
+            return
+        except Exception:
+            self.thread = None
+        try:  # fallback: nvidia-smi at its shortest loop period
             fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
             os.close(fd)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,"
+                 "clocks_event_reasons.active,power.draw", "--format=csv,noheader,nounits",
                  "-i", str(self.dev), "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi every 100 ms"
         except Exception:
             self.proc = None
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.fh.close()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            p = [x.strip() for x in line.split(",")]
-            if len(p) < 9:
-                continue
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(p[1]))
-                smax.append(float(p[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, p[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(self.path)
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+            for line in open(self.path):
+                p = [x.strip() for x in line.split(",")]
+                try:
+                    self.samples.append((float(p[0]), float(p[1]), int(p[2], 16),
+                                         float(p[3])))
+                except (ValueError, IndexError):
+                    continue
+            os.unlink(self.path)
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"],
+                    "samples": 0}
+        sm = [x[0] for x in self.samples]
+        reasons = sorted({n for x in self.samples for n, bit in self.REASONS if x[2] & bit})
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "sm_min_mhz": min(sm) if sm else None,
+                "sm_max_mhz": max(x[1] for x in self.samples) if sm else None,
+                "power_w_max": max(x[3] for x in self.samples) if sm else None,
+                "reasons": reasons, "samples": len(sm), "source": self.source}
+
+
+def choose_regime(region_s: float, clk: dict) -> tuple:
+    """Which measured peak fits the timed region: the burst figure (a kernel timed alone,
+    clocks at max) when the region is shorter than 2 s or the median SM clock under load
+    stayed within 5 % of max; the sustained figure (seconds under the 1 kW power cap)
+    otherwise.  Returns (regime, reason)."""
+    med, mx = clk.get("sm_mhz"), clk.get("sm_max_mhz")
+    if region_s < 2.0:
+        return "burst", f"timed region {region_s:.3f} s < 2 s"
+    if med and mx and med >= 0.95 * mx:
+        return "burst", f"median SM clock {med:.0f} MHz within 5 % of max {mx:.0f}"
+    return "sustained", (f"timed region {region_s:.1f} s at median SM clock {med} MHz "
+                         f"(max {mx})")
+
+
+def tensor_peak(peaks, regime: str, factor: float):
+    """(peak TFLOP/s, both candidates) for a tensor-bound kernel: `factor` x the measured
+    dense bf16 figure of the regime (2 for int8, 1/3 for the 3 x bf16 split)."""
+    burst = factor * peaks["bf16_tflops"]
+    sus = factor * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    return (burst if regime == "burst" else sus), burst, sus
 
 
 def dist_env():
@@ -254,19 +323,23 @@ class I8Workload:
                                               self.batch, self.k, out_i.data_ptr(),
                                               out_v.data_ptr(), pion_b200._lib.MEM_HOST))
 
-    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
         if self.batch > 1:
             ops = 2.0 * self.dim * rows_local * self.batch
             achieved = ops / (kern_ms / 1000.0) / 1e12
-            # the scoring kernel runs back to back for the whole timed region (hundreds of
-            # ms under the 1 kW power cap), so the sustained figure is the denominator
-            peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-            return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak,
-                    "frac_of_burst": achieved / (2.0 * peaks["bf16_tflops"]),
-                    "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate = 2 x bf16 "
-                                   f"on B200); int8 tera-ops counted as TFLOP",
-                    "algorithmic_per_launch": ops, "kernel_ms": kern_ms}
+            peak, burst, sus = tensor_peak(peaks, regime, 2.0)
+            r = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                 "frac": achieved / peak, "regime": regime,
+                 "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sus,
+                 "peak_source": f"2 x {peak_kind} dense bf16 {regime} (int8 rate = 2 x bf16 "
+                                f"on B200); int8 tera-ops counted as TFLOP",
+                 "algorithmic_per_launch": ops, "kernel_ms": kern_ms,
+                 "kernel_ms_covers": "threshold pass + its merge + main pass, per search"}
+            if phases and phases.get("main_ms"):
+                r["main_pass_ms"] = phases["main_ms"]
+                r["threshold_pass_ms"] = phases.get("threshold_ms")
+                r["frac_main_pass"] = ops / (phases["main_ms"] / 1000.0) / 1e12 / peak
+            return r
         byts = float(rows_local) * (self.dim + 4)
         achieved = byts / (kern_ms / 1000.0) / 1e9
         peak = peaks["hbm_gbs"]
@@ -319,14 +392,15 @@ class F32Workload:
                                                self.k, out_i.data_ptr(), out_v.data_ptr(),
                                                pion_b200._lib.MEM_HOST))
 
-    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
         flops = 2.0 * self.dim * rows_local * self.batch
         achieved = flops / (kern_ms / 1000.0) / 1e12
         # three bf16 tensor passes per fp32 product (hi.hi + hi.lo + lo.hi)
-        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) / 3.0
+        peak, burst, sus = tensor_peak(peaks, regime, 1.0 / 3.0)
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak,
-                "peak_source": f"{peak_kind} dense bf16 sustained / 3 (fp32 products as three "
+                "frac": achieved / peak, "regime": regime,
+                "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sus,
+                "peak_source": f"{peak_kind} dense bf16 {regime} / 3 (fp32 products as three "
                                f"bf16 passes); timed: query normalisation + bf16 split + "
                                f"tensor-core shortlist",
                 "algorithmic_per_launch": flops, "kernel_ms": kern_ms}
@@ -377,14 +451,15 @@ class BQWorkload:
                                                 self.shortlist, self.k, out_i.data_ptr(),
                                                 out_v.data_ptr(), pion_b200._lib.MEM_HOST))
 
-    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
         # Hamming of every (query, row) pair as +-1 int8 dot products on the tensor cores
         ops = 2.0 * self.dim * rows_local * self.batch
         achieved = ops / (kern_ms / 1000.0) / 1e12
-        peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        peak, burst, sus = tensor_peak(peaks, regime, 2.0)
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak,
-                "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate); timed: query "
+                "frac": achieved / peak, "regime": regime,
+                "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sus,
+                "peak_source": f"2 x {peak_kind} dense bf16 {regime} (int8 rate); timed: query "
                                f"normalisation + signs + staged Hamming shortlist",
                 "algorithmic_per_launch": ops, "kernel_ms": kern_ms}
 
@@ -513,7 +588,7 @@ class HNSWWorkload:
                                               self.k, self.ef, out_i.data_ptr(),
                                               out_v.data_ptr(), pion_b200._lib.MEM_HOST))
 
-    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
         st = self.ix.last_stats()
         byts = float(st["evals"] + st["upper_evals"]) * 1544.0 + st["expansions"] * 264.0
         # with several workers the batches overlap: kern_ms is then the time per batch
@@ -602,14 +677,15 @@ class SlotWorkload(HNSWWorkload):
                                                    self.k, out_i.data_ptr(), out_v.data_ptr(),
                                                    found.data_ptr(), pion_b200._lib.MEM_HOST))
 
-    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
         st = self.ix.slot_stats()
         ops = 2.0 * self.dim * self.wl["rows"] * self.batch
         achieved = ops / (kern_ms / 1000.0) / 1e12
-        peak = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        peak, burst, sus = tensor_peak(peaks, regime, 2.0)
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak,
-                "peak_source": f"2 x {peak_kind} dense bf16 sustained (int8 rate); timed: the "
+                "frac": achieved / peak, "regime": regime,
+                "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sus,
+                "peak_source": f"2 x {peak_kind} dense bf16 {regime} (int8 rate); timed: the "
                                f"staged tensor-core scan and the top-k replay",
                 "algorithmic_per_launch": ops, "kernel_ms": kern_ms,
                 "replayed_per_query": st["replayed"] / max(1, self.batch),
@@ -737,7 +813,7 @@ class QuantWorkload(HNSWWorkload):
                                                     out_i.data_ptr(), out_v.data_ptr(),
                                                     found.data_ptr(), pion_b200._lib.MEM_HOST))
 
-    def roofline(self, rows_local, kern_ms, peaks, peak_kind):
+    def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
         st = self.ix.last_stats()
         kind = self.wl["quant"]
         slot = 4 + 96 + {"polar": 768, "nano": 384, "turbo": 576}[kind] + \
@@ -934,9 +1010,9 @@ def run_ours(a, wl):
     ctx.use_torch_stream()
     stream = torch.cuda.current_stream()
 
-    def merge(scores, ids):
-        return pion_b200.merge_topk(ctx, scores, ids, k, descending=W.descending,
-                                    lists_major=True)
+    def merge(pairs):  # [world, batch, k, 2]: the all-gather of every shard's pairs
+        return pion_b200.merge_topk_pairs(ctx, pairs, k, descending=W.descending,
+                                          lists_major=True)
 
     step = W.search if getattr(W, "replicas", False) else ShardedSearch(W.search, k, merge)
     workers = a.workers or (3 if wl["kind"] in ("hnsw", "quant") else 1)
@@ -984,13 +1060,21 @@ def run_ours(a, wl):
     elapsed = ev0.elapsed_time(ev1)
     launches = sum(c_.launches for c_ in ctxs) - launches0
     kern_ms, kern_n = 0.0, 0
+    phase_ms = {"threshold_ms": 0.0, "main_ms": 0.0}
     for c_ in ctxs:
         km, kn = c_.timing_read()
+        for tag, key in ((1, "threshold_ms"), (2, "main_ms")):
+            pm, pn = c_.timing_read(tag)
+            phase_ms[key] += pm / max(1, kn)
         c_.timing(False)
         kern_ms, kern_n = kern_ms + km, kern_n + kn
     if workers > 1:  # overlapping batches: the time per batch of the whole run
         kern_ms, kern_n = elapsed, a.steps
     clk = clocks.stop()
+    # per-phase device time of a few more steps: local scoring, all-gather, merge
+    breakdown = None
+    if isinstance(step, ShardedSearch):
+        breakdown = step.breakdown(inp, max(3, min(a.steps, 20)))
 
     # ---- e2e: host (pinned) queries in, host results out, through the C ABI
     e2e_steps = a.e2e_steps or max(10, min(a.steps, 200))
@@ -1047,12 +1131,14 @@ def run_ours(a, wl):
     d2h = local_batch * k * 8
 
     # ---- max over ranks
-    t = torch.tensor([elapsed, e2e_ms, kern_ms / max(1, kern_n)], device=dev, dtype=torch.float64)
+    bd = [breakdown[x] for x in ("local_ms", "allgather_ms", "merge_ms")] if breakdown else [0.0] * 3
+    t = torch.tensor([elapsed, e2e_ms, kern_ms / max(1, kern_n), phase_ms["threshold_ms"],
+                      phase_ms["main_ms"], *bd], device=dev, dtype=torch.float64)
     lt = torch.tensor([launches], device=dev, dtype=torch.int64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.all_reduce(lt, op=dist.ReduceOp.SUM)
-    elapsed, e2e_ms, kern_avg_ms = t.tolist()
+    elapsed, e2e_ms, kern_avg_ms, thr_ms, main_ms, bd_local, bd_ag, bd_merge = t.tolist()
     launches = int(lt.item())
 
     line = None
@@ -1061,7 +1147,10 @@ def run_ours(a, wl):
         qps = per_step * a.steps / (elapsed / 1000.0)
         e2e_qps = per_step * e2e_steps / (e2e_ms / 1000.0)
         peaks, peak_kind = measured_peaks()
-        roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind)
+        regime, why = choose_regime(elapsed / 1000.0, clk)
+        roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind, regime=regime,
+                          phases={"threshold_ms": thr_ms, "main_ms": main_ms})
+        roof["regime_reason"] = why
         roof["traffic"] = profiled_traffic(f"{a.workload}_{world}")
         line = {
             "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
@@ -1078,6 +1167,11 @@ def run_ours(a, wl):
             "roofline": roof,
             "clocks": clk,
         }
+        if breakdown is not None:
+            line["step_breakdown_ms"] = {
+                "local_search": bd_local, "pack_allgather": bd_ag, "merge": bd_merge,
+                "note": "max over ranks of the per-step device time of each phase, CUDA events "
+                        "over extra steps after the timed region"}
     # ---- CPU baseline on rank 0 at N=1 (bounded sample of the same workload)
     if rank == 0 and hasattr(W, "extra"):
         line["config"].update(W.extra(dev))

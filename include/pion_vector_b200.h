@@ -234,8 +234,18 @@ int pion_v_b200_shutdown(pion_b200_ctx *ctx);
  * shared), without blocking the host. */
 int pion_v_b200_set_stream(pion_b200_ctx *ctx, void *cuda_stream);
 /* Waits for the context's stream and returns the first error any device-side wait
- * recorded since the last call (PION_B200_ETIMEOUT), else 0. */
+ * recorded since the last call (PION_B200_ETIMEOUT), else 0.  A call with host buffers
+ * checks its own kernels' waits before it returns; a call with device buffers returns
+ * once its kernels are queued, so its waits are reported here (they are never reported
+ * as a later host-buffer call's failure). */
 int pion_v_b200_sync(pion_b200_ctx *ctx);
+/* Budget of each device-side wait in this context's FLAT INT8 tensor-core kernels, in
+ * ns (<= 0 restores the default of 2 s).  A wait that runs out records
+ * PION_B200_ETIMEOUT; the kernel then drains its copies and MMAs, frees its tensor
+ * memory and returns, so the context stays usable.  (For tests, the environment
+ * variable PION_B200_TEST_STALL=1 makes one CTA of each main pass wait on a barrier that
+ * nothing arrives on.) */
+int pion_v_b200_set_wait_budget(pion_b200_ctx *ctx, int64_t ns);
 /* Message of the last failing call on this context ("" if none). */
 const char *pion_v_b200_last_error(const pion_b200_ctx *ctx);
 /* Pre-size per-call scratch so that query calls up to these sizes allocate nothing. */
@@ -247,8 +257,15 @@ int64_t pion_v_b200_launch_count(const pion_b200_ctx *ctx);
  * tensor-core or scan kernel that reads the index).  Enabling clears the record. */
 int pion_v_b200_timing_enable(pion_b200_ctx *ctx, int enable);
 /* Waits for the stream; returns the summed duration (ms) and count of the recorded
- * scoring-kernel launches. */
+ * scoring-kernel launches (= pion_v_b200_timing_read_tag(ctx, PION_B200_TIMING_SCORING)). */
 int pion_v_b200_timing_read(pion_b200_ctx *ctx, double *total_ms, int64_t *count);
+/* The same for one phase.  SCORING spans every kernel that reads the index in one call;
+ * inside it the FLAT INT8 tensor-core path also records its threshold pass (the sampled
+ * bound and its merge) and its main pass separately. */
+#define PION_B200_TIMING_SCORING 0
+#define PION_B200_TIMING_THRESHOLD 1
+#define PION_B200_TIMING_MAIN 2
+int pion_v_b200_timing_read_tag(pion_b200_ctx *ctx, int tag, double *total_ms, int64_t *count);
 
 /* ------------------------------------------------------------ any index kind -- */
 #define PION_B200_KIND_FLAT_I8 1  /* rows int8 [n x dim] + row_scale: register_flat_i8 */
@@ -374,9 +391,13 @@ int pion_v_b200_l2_normalize_rows(pion_b200_ctx *ctx, const float *src, int64_t 
  * of src/commands/vector.mojo:4394-4436, with ids breaking ties).  Flags:
  * PION_B200_MERGE_DESC orders by (score desc, id asc), else (score asc, id asc);
  * PION_B200_MERGE_LISTS_MAJOR reads the input as [n_lists][nq][k] (the layout of an
- * all-gather of per-shard results) instead of [nq][n_lists][k]. */
+ * all-gather of per-shard results) instead of [nq][n_lists][k];
+ * PION_B200_MERGE_PAIRS reads cand_scores as interleaved 8-byte (f32 score, i32 id)
+ * pairs (one buffer, so a shard exchanges its results in one collective) and ignores
+ * cand_ids, which may be NULL. */
 #define PION_B200_MERGE_DESC 1
 #define PION_B200_MERGE_LISTS_MAJOR 2
+#define PION_B200_MERGE_PAIRS 4
 int pion_v_b200_merge_topk(pion_b200_ctx *ctx, const float *cand_scores, const int32_t *cand_ids,
                            int64_t nq, int64_t n_lists, int64_t k, int flags,
                            float *out_scores, int32_t *out_ids, int mem);

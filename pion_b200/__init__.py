@@ -17,10 +17,11 @@ from .search import (  # noqa: F401
     HNSWQuantIndex,
     l2_normalize_rows,
     merge_topk,
+    merge_topk_pairs,
     quantize_rows_i8,
     rescore_knn,
 )
 
 __all__ = ["Context", "FlatI8Index", "FlatF32Index", "BQIndex", "HNSWGraph", "HNSWIndex",
            "HNSWQuant", "HNSWQuantIndex", "quantize_rows_i8",
-           "l2_normalize_rows", "merge_topk", "rescore_knn", "PionError", "load"]
+           "l2_normalize_rows", "merge_topk", "merge_topk_pairs", "rescore_knn", "PionError", "load"]

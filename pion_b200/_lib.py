@@ -27,6 +27,7 @@ MEM_DEVICE_BORROW = 2
 
 MERGE_DESC = 1
 MERGE_LISTS_MAJOR = 2
+MERGE_PAIRS = 4
 
 ABI_VERSION = 1
 
@@ -49,12 +50,15 @@ SIGNATURES = {
     "pion_v_b200_shutdown": (_I, [_P]),
     "pion_v_b200_set_stream": (_I, [_P, _P]),
     "pion_v_b200_sync": (_I, [_P]),
+    "pion_v_b200_set_wait_budget": (_I, [_P, _I64]),
     "pion_v_b200_last_error": (ctypes.c_char_p, [_P]),
     "pion_v_b200_reserve": (_I, [_P, _I64, _I64]),
     "pion_v_b200_launch_count": (_I64, [_P]),
     "pion_v_b200_timing_enable": (_I, [_P, _I]),
     "pion_v_b200_timing_read": (_I, [_P, ctypes.POINTER(ctypes.c_double),
                                      ctypes.POINTER(ctypes.c_int64)]),
+    "pion_v_b200_timing_read_tag": (_I, [_P, _I, ctypes.POINTER(ctypes.c_double),
+                                         ctypes.POINTER(ctypes.c_int64)]),
     "pion_v_b200_register_flat_i8": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _PP]),
     "pion_v_b200_flat_i8_knn": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_flat_i8_knn_static": (_I, [_P, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P,

@@ -11,7 +11,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <new>
+#include <utility>
 
 #include "internal.h"
 
@@ -39,6 +42,49 @@ int ensure(DevBuf& b, size_t bytes) {
     b.ptr = p;
     b.bytes = want;
     return 0;
+}
+
+int set_smem_limit(const void* kernel, int bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return PION_B200_ECUDA;
+    }
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes set
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(kernel, dev);
+    const auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return PION_B200_ECUDA;
+    }
+    done[key] = bytes;
+    return 0;
+}
+
+uint64_t sample_rows_hash(uint64_t h, const void* base, int64_t n_rows, int64_t row_bytes,
+                          int64_t take_bytes) {
+    if (!base || n_rows <= 0 || row_bytes <= 0) return h;
+    if (take_bytes > row_bytes) take_bytes = row_bytes;
+    const unsigned char* p = static_cast<const unsigned char*>(base);
+    const int64_t samples = n_rows < 64 ? n_rows : 64;
+    for (int64_t j = 0; j <= samples; ++j) {
+        const int64_t row = j == samples ? n_rows - 1 : j * n_rows / samples;
+        const unsigned char* r = p + row * row_bytes;
+        int64_t b = 0;
+        for (; b + 8 <= take_bytes; b += 8) {
+            uint64_t w;
+            memcpy(&w, r + b, 8);
+            h = (h ^ w) * 0x100000001b3ull;
+            h ^= h >> 29;
+        }
+        for (; b < take_bytes; ++b) h = (h ^ r[b]) * 0x100000001b3ull;
+        h = (h ^ (uint64_t)row) * 0x9e3779b97f4a7c15ull;
+    }
+    return h;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -79,31 +125,43 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, co
     return r == CUDA_SUCCESS ? 0 : PION_B200_ECUDA;
 }
 
-// Queues a copy of the status word into pinned host memory.
+int* call_status(pion_b200_ctx* ctx, int mem) {
+    return ctx->d_status + (mem == PION_B200_MEM_HOST ? 0 : 1);
+}
+
+// Queues a copy of both status words into pinned host memory.
 int queue_status_readback(pion_b200_ctx* ctx) {
-    return cudaMemcpyAsync(ctx->h_status, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost,
+    return cudaMemcpyAsync(ctx->h_status, ctx->d_status, 2 * sizeof(int), cudaMemcpyDeviceToHost,
                            ctx->stream) == cudaSuccess
                ? 0
                : PION_B200_ECUDA;
 }
 
-// Synchronises the stream, then turns a recorded device-side status into a code.
-int finish_sync(pion_b200_ctx* ctx) {
+// Synchronises the stream, then turns a status recorded in words [first, last] into a
+// code (and clears them).  Host-memory calls check word 0 only: a device-memory call's
+// failure stays in word 1 for pion_v_b200_sync and is never reported as a later
+// host-memory call's own.
+static int sync_words(pion_b200_ctx* ctx, int first, int last) {
     if (queue_status_readback(ctx) != 0)
         return set_error(ctx, PION_B200_ECUDA, "status copy failed: %s",
                          cudaGetErrorString(cudaGetLastError()));
     cudaError_t e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess)
         return set_error(ctx, PION_B200_ECUDA, "stream failed: %s", cudaGetErrorString(e));
-    int st = *ctx->h_status;
-    if (st != 0) {
-        *ctx->h_status = 0;
-        cudaMemsetAsync(ctx->d_status, 0, sizeof(int), ctx->stream);
-        cudaStreamSynchronize(ctx->stream);
-        return set_error(ctx, st, "device-side wait gave up (status %d)", st);
+    for (int w = first; w <= last; ++w) {
+        const int st = ctx->h_status[w];
+        if (st != 0) {
+            ctx->h_status[w] = 0;
+            cudaMemsetAsync(ctx->d_status + w, 0, sizeof(int), ctx->stream);
+            cudaStreamSynchronize(ctx->stream);
+            return set_error(ctx, st, "device-side wait gave up (status %d, %s-memory call)",
+                             st, w == 0 ? "host" : "device");
+        }
     }
     return 0;
 }
+
+int finish_sync(pion_b200_ctx* ctx) { return sync_words(ctx, 0, 0); }
 
 bool valid_ctx(const pion_b200_ctx* ctx) { return ctx != nullptr && ctx->d_status; }
 
@@ -115,26 +173,35 @@ int use_device(pion_b200_ctx* ctx) {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-void timing_begin(pion_b200_ctx* ctx) {
-    if (!ctx->timing) return;
+int timing_begin(pion_b200_ctx* ctx, int tag) {
+    if (!ctx->timing) return -1;
     if (ctx->ev_used == ctx->ev_start.size()) {
-        if (ctx->ev_used >= 65536) return;
+        if (ctx->ev_used >= 65536) return -1;
         cudaEvent_t a, b;
-        if (cudaEventCreate(&a) != cudaSuccess) return;
+        if (cudaEventCreate(&a) != cudaSuccess) return -1;
         if (cudaEventCreate(&b) != cudaSuccess) {
             cudaEventDestroy(a);
-            return;
+            return -1;
         }
         ctx->ev_start.push_back(a);
         ctx->ev_end.push_back(b);
+        ctx->ev_tag.push_back(0);
+        ctx->ev_closed.push_back(false);
     }
-    cudaEventRecord(ctx->ev_start[ctx->ev_used], ctx->stream);
+    const int slot = (int)ctx->ev_used++;
+    ctx->ev_tag[slot] = tag;
+    ctx->ev_closed[slot] = false;
+    ctx->ev_open = slot;
+    cudaEventRecord(ctx->ev_start[slot], ctx->stream);
+    return slot;
 }
 
-void timing_end(pion_b200_ctx* ctx) {
-    if (!ctx->timing || ctx->ev_used >= ctx->ev_start.size()) return;
-    cudaEventRecord(ctx->ev_end[ctx->ev_used], ctx->stream);
-    ctx->ev_used++;
+void timing_end(pion_b200_ctx* ctx, int slot) {
+    if (!ctx->timing) return;
+    if (slot < 0) slot = ctx->ev_open;
+    if (slot < 0 || (size_t)slot >= ctx->ev_used || ctx->ev_closed[slot]) return;
+    cudaEventRecord(ctx->ev_end[slot], ctx->stream);
+    ctx->ev_closed[slot] = true;
 }
 
 }  // namespace pion
@@ -170,14 +237,14 @@ int pion_v_b200_init(int device, int worker_id, pion_b200_ctx** out_ctx) {
     ctx->worker_id = worker_id;
     ctx->num_sms = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess ||
-        cudaMallocHost(&ctx->h_status, sizeof(int)) != cudaSuccess) {
+        cudaMalloc(&ctx->d_status, 2 * sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&ctx->h_status, 2 * sizeof(int)) != cudaSuccess) {
         pion_v_b200_shutdown(ctx);
         return PION_B200_ENOMEM;
     }
     ctx->stream = ctx->own_stream;
-    *ctx->h_status = 0;
-    cudaMemset(ctx->d_status, 0, sizeof(int));
+    ctx->h_status[0] = ctx->h_status[1] = 0;
+    cudaMemset(ctx->d_status, 0, 2 * sizeof(int));
     cudaDeviceSynchronize();
     *out_ctx = ctx;
     return 0;
@@ -219,10 +286,16 @@ int pion_v_b200_set_stream(pion_b200_ctx* ctx, void* cuda_stream) {
     return 0;
 }
 
+int pion_v_b200_set_wait_budget(pion_b200_ctx* ctx, int64_t ns) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    ctx->wait_ns = ns > 0 ? (uint64_t)ns : kDefaultWaitNs;
+    return 0;
+}
+
 int pion_v_b200_sync(pion_b200_ctx* ctx) {
     if (!valid_ctx(ctx)) return PION_B200_EINVAL;
     if (int rc = use_device(ctx)) return rc;
-    return finish_sync(ctx);
+    return sync_words(ctx, 0, 1);
 }
 
 const char* pion_v_b200_last_error(const pion_b200_ctx* ctx) {
@@ -237,16 +310,19 @@ int pion_v_b200_timing_enable(pion_b200_ctx* ctx, int enable) {
     cudaStreamSynchronize(ctx->stream);
     ctx->timing = enable != 0;
     ctx->ev_used = 0;
+    ctx->ev_open = -1;
     return 0;
 }
 
-int pion_v_b200_timing_read(pion_b200_ctx* ctx, double* total_ms, int64_t* count) {
+int pion_v_b200_timing_read_tag(pion_b200_ctx* ctx, int tag, double* total_ms, int64_t* count) {
     if (!valid_ctx(ctx) || !total_ms || !count) return PION_B200_EINVAL;
     if (int rc = use_device(ctx)) return rc;
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess)
         return set_error(ctx, PION_B200_ECUDA, "timing_read: stream failed");
     double sum = 0.0;
+    int64_t n = 0;
     for (size_t i = 0; i < ctx->ev_used; ++i) {
+        if (ctx->ev_tag[i] != tag || !ctx->ev_closed[i]) continue;
         // the events may sit on a stream other than the current one
         if (cudaEventSynchronize(ctx->ev_end[i]) != cudaSuccess)
             return set_error(ctx, PION_B200_ECUDA, "timing_read: event %zu", i);
@@ -254,10 +330,15 @@ int pion_v_b200_timing_read(pion_b200_ctx* ctx, double* total_ms, int64_t* count
         if (cudaEventElapsedTime(&ms, ctx->ev_start[i], ctx->ev_end[i]) != cudaSuccess)
             return set_error(ctx, PION_B200_ECUDA, "timing_read: event %zu", i);
         sum += ms;
+        ++n;
     }
     *total_ms = sum;
-    *count = (int64_t)ctx->ev_used;
+    *count = n;
     return 0;
+}
+
+int pion_v_b200_timing_read(pion_b200_ctx* ctx, double* total_ms, int64_t* count) {
+    return pion_v_b200_timing_read_tag(ctx, PION_B200_TIMING_SCORING, total_ms, count);
 }
 
 int pion_v_b200_reserve(pion_b200_ctx* ctx, int64_t max_nq, int64_t max_k) {
@@ -403,6 +484,14 @@ int pion_v_b200_register_flat_i8(pion_b200_ctx* ctx, const int8_t* rows, const f
     }
     *out_index = ix;
     return 0;
+}
+
+// Test hook (PION_B200_TEST_STALL=1): one CTA of the next main passes waits on a
+// barrier nothing arrives on, so the wait runs out after the context's budget and the
+// call reports PION_B200_ETIMEOUT (no fault, the GPU stays usable).
+static int test_stall() {
+    const char* e = getenv("PION_B200_TEST_STALL");
+    return e && atoi(e) == 1 ? 1 : 0;
 }
 
 // Forced path selection for tests: 0 auto, 1 one-query scan, 2 tensor-core kernel.
@@ -555,9 +644,11 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         L.nq = nqi;
         L.dim = dim;
         L.k = kk;
-        L.status = ctx->d_status;
-        timing_begin(ctx);
+        L.status = call_status(ctx, mem);
+        L.wait_ns = ctx->wait_ns;
+        const int t_all = timing_begin(ctx);
         if (pre) {
+            const int t_pre = timing_begin(ctx, PION_B200_TIMING_THRESHOLD);
             L.tile_begin = 0;
             L.tile_end = pre_tiles;
             L.n_splits = bnd_splits;
@@ -572,8 +663,10 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
                 rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, 0, true, tv, ti, st);
                 ctx->launches++;
             }
+            timing_end(ctx, t_pre);
         }
         if (rc == 0) {
+            const int t_main = timing_begin(ctx, PION_B200_TIMING_MAIN);
             L.tile_begin = 0;
             L.tile_end = n_tiles;
             L.n_splits = splits;
@@ -583,10 +676,12 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
             L.thr0 = pre ? tv + (kk - 1) : nullptr;
             L.thr0_stride = kk;
             L.bound_mode = 0;
+            L.test_stall = test_stall();
             rc = launch_flat_i8_tc(L, st);
             ctx->launches++;
+            timing_end(ctx, t_main);
         }
-        timing_end(ctx);
+        timing_end(ctx, t_all);
         if (rc == 0) {
             rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, dv, di, st);
             ctx->launches++;
@@ -651,11 +746,14 @@ int pion_v_b200_merge_topk(pion_b200_ctx* ctx, const float* cand_scores, const i
                            int64_t nq, int64_t n_lists, int64_t k, int flags,
                            float* out_scores, int32_t* out_ids, int mem) {
     if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    const bool pairs = (flags & PION_B200_MERGE_PAIRS) != 0;
     if (nq < 0 || n_lists < 1 || k < 1 ||
-        (nq > 0 && (!cand_scores || !cand_ids || !out_scores || !out_ids)))
+        (nq > 0 && (!cand_scores || (!pairs && !cand_ids) || !out_scores || !out_ids)))
         return set_error(ctx, PION_B200_EINVAL, "merge_topk: bad arguments");
     if (n_lists > 2048 || k > 4096)
         return set_error(ctx, PION_B200_ESHAPE, "merge_topk: n_lists <= 2048, k <= 4096");
+    if (pairs && (reinterpret_cast<uintptr_t>(cand_scores) & 7u) != 0)
+        return set_error(ctx, PION_B200_EINVAL, "merge_topk: pairs not 8-byte aligned");
     if (nq == 0) return 0;
     if (int rc = use_device(ctx)) return rc;
     cudaStream_t st = ctx->stream;
@@ -670,9 +768,16 @@ int pion_v_b200_merge_topk(pion_b200_ctx* ctx, const float* cand_scores, const i
             return set_error(ctx, PION_B200_ENOMEM, "merge_topk: staging");
         float* sv = static_cast<float*>(ctx->stage_in.ptr);
         int32_t* si = reinterpret_cast<int32_t*>(sv + cand);
-        if (cudaMemcpyAsync(sv, cand_scores, cand * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(si, cand_ids, cand * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
-            return set_error(ctx, PION_B200_ECUDA, "merge_topk: copy failed");
+        bool ok;
+        if (pairs)
+            ok = cudaMemcpyAsync(sv, cand_scores, cand * 8, cudaMemcpyHostToDevice, st) ==
+                 cudaSuccess;
+        else
+            ok = cudaMemcpyAsync(sv, cand_scores, cand * 4, cudaMemcpyHostToDevice, st) ==
+                     cudaSuccess &&
+                 cudaMemcpyAsync(si, cand_ids, cand * 4, cudaMemcpyHostToDevice, st) ==
+                     cudaSuccess;
+        if (!ok) return set_error(ctx, PION_B200_ECUDA, "merge_topk: copy failed");
         cv = sv;
         ci = si;
         ov = static_cast<float*>(ctx->stage_out.ptr);
@@ -682,7 +787,7 @@ int pion_v_b200_merge_topk(pion_b200_ctx* ctx, const float* cand_scores, const i
     }
     int rc = launch_merge_lists(cv, ci, (int)nq, (int)n_lists, (int)k, 0,
                                 (flags & PION_B200_MERGE_DESC) != 0, ov, oi, st,
-                                (flags & PION_B200_MERGE_LISTS_MAJOR) != 0);
+                                (flags & PION_B200_MERGE_LISTS_MAJOR) != 0, 0, pairs);
     ctx->launches++;
     if (rc != 0) return set_error(ctx, rc, "merge_topk: launch failed");
     if (mem == PION_B200_MEM_HOST) {

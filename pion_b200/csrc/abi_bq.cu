@@ -223,7 +223,7 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
             L.cand_id = cid[buf];
             L.cand_h = ch[buf];
             L.cand_n = cn[buf];
-            L.status = ctx->d_status;
+            L.status = call_status(ctx, mem);
             rc = launch_bq_tc(L, st);
             ctx->launches++;
             if (rc != 0) break;

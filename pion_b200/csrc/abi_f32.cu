@@ -278,7 +278,7 @@ int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, cons
         L.nq = nqi;
         L.dim = dim;
         L.kc = kc;
-        L.status = ctx->d_status;
+        L.status = call_status(ctx, mem);
         if (rc == 0 && pre) {
             L.tile_begin = 0;
             L.tile_end = pre_tiles;

@@ -439,7 +439,7 @@ int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const
             Lc.out_dist = dv;
             Lc.stats = stats;
             Lc.next_query = next_query;
-            Lc.status = ctx->d_status;
+            Lc.status = call_status(ctx, mem);
             Lc.ctas = (int)ctas;
             timing_begin(ctx);
             rc = launch_hnsw_beam(Lc, st);
@@ -562,7 +562,7 @@ int pion_v_b200_hnsw_beam_batch(pion_b200_ctx* ctx, const pion_b200_index* ix,
     Lc.vis_words = vis_words;
     Lc.stats = stats;
     Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
-    Lc.status = ctx->d_status;
+    Lc.status = call_status(ctx, mem);
     Lc.ctas = (int)ctas;
     Lc.pool_io = dp;
     Lc.pool_stride = ef;
@@ -679,6 +679,7 @@ struct BeamGraph {
     const int8_t* comp;
     int64_t n, stride, hdr;
     int device;
+    uint64_t fp;  // content fingerprint of the three host tables when copied
     int8_t* codes = nullptr;
     float* norms = nullptr;
     uint32_t* l0_compact = nullptr;
@@ -701,14 +702,31 @@ int beam_fail(const char* what) {
     return -1;
 }
 
-// The registered copy of the view's graph (copied and checked on first use).
+uint64_t beam_fingerprint(const pion_beam_view_1536* v) {
+    uint64_t h = 0xcbf29ce484222325ull;
+    h = sample_rows_hash(h, v->l0_compact, v->num_nodes, 33 * 4, 33 * 4);
+    h = sample_rows_hash(h, v->l0_slots, v->num_nodes, 33 * 4, 33 * 4);
+    return sample_rows_hash(h, v->compact_buffer, v->num_nodes, v->compact_stride, 256);
+}
+
+// The registered copy of the view's graph (copied and checked on first use).  The copy
+// is keyed by the view's host pointers and sizes AND a fingerprint of sampled rows of
+// the three tables, so a different graph the engine placed at the same addresses is
+// copied again instead of served from the stale copy.
 BeamGraph* beam_graph(pion_b200_ctx* ctx, const pion_beam_view_1536* v, const char** why) {
     std::lock_guard<std::mutex> lock(g_beam_mu);
-    for (BeamGraph* g : g_beam_graphs)
+    const uint64_t fp = beam_fingerprint(v);
+    for (size_t i = 0; i < g_beam_graphs.size(); ++i) {
+        BeamGraph* g = g_beam_graphs[i];
         if (g->l0c == v->l0_compact && g->l0s == v->l0_slots && g->comp == v->compact_buffer &&
             g->n == v->num_nodes && g->stride == v->compact_stride && g->hdr == v->compact_hdr &&
-            g->device == ctx->device)
-            return g;
+            g->device == ctx->device) {
+            if (g->fp == fp) return g;
+            free_beam_graph(g);  // same addresses, other content: drop the stale copy
+            g_beam_graphs.erase(g_beam_graphs.begin() + (ptrdiff_t)i);
+            break;
+        }
+    }
     const int64_t n = v->num_nodes;
     if (v->compact_hdr != 8 || v->compact_stride % 16 != 0 ||
         v->compact_stride < v->compact_hdr + hnsw_dim() + 8) {
@@ -725,7 +743,8 @@ BeamGraph* beam_graph(pion_b200_ctx* ctx, const pion_beam_view_1536* v, const ch
             }
     }
     BeamGraph* g = new (std::nothrow) BeamGraph{v->l0_compact, v->l0_slots, v->compact_buffer, n,
-                                                v->compact_stride, v->compact_hdr, ctx->device};
+                                                v->compact_stride, v->compact_hdr, ctx->device,
+                                                fp};
     if (!g) {
         *why = "out of host memory";
         return nullptr;
@@ -812,7 +831,7 @@ int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
     Lc.vis_words = vis_words;
     Lc.stats = stats;
     Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
-    Lc.status = ctx->d_status;
+    Lc.status = call_status(ctx, PION_B200_MEM_HOST);
     Lc.ctas = 1;
     Lc.pool_io = base + o_pool;
     Lc.pool_stride = ef;

@@ -92,6 +92,7 @@ struct QuantBeamGraph {
     const float* qres;
     int64_t n, stride, hdr;
     int kind, device;
+    uint64_t fp;  // content fingerprint of the host tables when copied
     float* norms = nullptr;
     uint16_t* scales = nullptr;
     uint8_t* codes = nullptr;
@@ -118,16 +119,34 @@ int qbeam_fail(const char* what) {
     return -1;
 }
 
-// The registered copy of the view's graph (checked and copied on first use).
+uint64_t qbeam_fingerprint(const pion_quant_beam_view_1536* v) {
+    uint64_t h = 0xcbf29ce484222325ull ^ (uint64_t)v->kind;
+    h = sample_rows_hash(h, v->l0_compact, v->num_nodes, 33 * 4, 33 * 4);
+    h = sample_rows_hash(h, v->l0_slots, v->num_nodes, 33 * 4, 33 * 4);
+    h = sample_rows_hash(h, v->compact_buffer, v->num_nodes, v->compact_stride, 256);
+    h = sample_rows_hash(h, v->qjl_buffer, v->num_nodes, 24 * 8, 24 * 8);
+    return sample_rows_hash(h, v->qjl_res_norms, v->num_nodes, 4, 4);
+}
+
+// The registered copy of the view's graph (checked and copied on first use), keyed by
+// the view's host pointers and sizes and a fingerprint of sampled rows of its tables:
+// a different graph placed at the same addresses is copied again, not served stale.
 QuantBeamGraph* qbeam_graph(pion_b200_ctx* ctx, const pion_quant_beam_view_1536* v,
                             const char** why) {
     std::lock_guard<std::mutex> lock(g_qbeam_mu);
-    for (QuantBeamGraph* g : g_qbeam_graphs)
+    const uint64_t fp = qbeam_fingerprint(v);
+    for (size_t i = 0; i < g_qbeam_graphs.size(); ++i) {
+        QuantBeamGraph* g = g_qbeam_graphs[i];
         if (g->l0c == v->l0_compact && g->l0s == v->l0_slots && g->comp == v->compact_buffer &&
             g->qjl == v->qjl_buffer && g->qres == v->qjl_res_norms && g->n == v->num_nodes &&
             g->stride == v->compact_stride && g->hdr == v->compact_hdr && g->kind == v->kind &&
-            g->device == ctx->device)
-            return g;
+            g->device == ctx->device) {
+            if (g->fp == fp) return g;
+            free_qbeam_graph(g);  // same addresses, other content: drop the stale copy
+            g_qbeam_graphs.erase(g_qbeam_graphs.begin() + (ptrdiff_t)i);
+            break;
+        }
+    }
     const int64_t n = v->num_nodes;
     const int kind = (int)v->kind;
     const int bb = block_bytes(kind), cb = bb - 2, cbytes = code_bytes(kind);
@@ -149,7 +168,7 @@ QuantBeamGraph* qbeam_graph(pion_b200_ctx* ctx, const pion_quant_beam_view_1536*
     }
     QuantBeamGraph* g = new (std::nothrow) QuantBeamGraph{
         v->l0_compact, v->l0_slots, v->compact_buffer, v->qjl_buffer, v->qjl_res_norms, n,
-        v->compact_stride, v->compact_hdr, kind, ctx->device};
+        v->compact_stride, v->compact_hdr, kind, ctx->device, fp};
     if (!g) {
         *why = "out of host memory";
         return nullptr;
@@ -309,7 +328,7 @@ int64_t pion_v_quant_beam_1536(pion_quant_beam_view_1536* v) {
     Lc.cand_cap = cap;
     Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
     Lc.stats = stats;
-    Lc.status = ctx->d_status;
+    Lc.status = call_status(ctx, PION_B200_MEM_HOST);
     Lc.ctas = 1;
     Lc.from_heaps = 1;
     Lc.given_codes = reinterpret_cast<const int8_t*>(base + o_codes);
@@ -689,7 +708,7 @@ int pion_v_b200_hnsw_quant_search(pion_b200_ctx* ctx, const pion_b200_index* ix,
         Lc.overflow_n = over_n;
         Lc.next_query = next1;
         Lc.stats = stats;
-        Lc.status = ctx->d_status;
+        Lc.status = call_status(ctx, mem);
         Lc.ctas = (int)ctas;
         timing_begin(ctx);
         rc = launch_quant_search(Lc, st);

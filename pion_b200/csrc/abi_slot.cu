@@ -87,6 +87,7 @@ struct ScanState {
     int32_t* cand_i;
     int* cand_n;
     float* pub;
+    int* status = nullptr;  // the call's status word (call_status)
 };
 
 // Bytes of scratch the scan needs after `off`, and the plan.
@@ -182,7 +183,7 @@ int run_dense(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes
             L.tile_end = (int)((base + len + tr - 1) / tr);
             const int tiles = L.tile_end - L.tile_begin;
             L.n_splits = tiles < ctx->num_sms ? tiles : ctx->num_sms;
-            L.status = ctx->d_status;
+            L.status = S.status;
             L.dense = dense;
             L.dense_base = base;
             L.dense_ld = clen;
@@ -242,7 +243,7 @@ int run_scan(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes,
         const int n_qt = (nq + slot_query_tile() - 1) / slot_query_tile();
         int sp = (ctx->num_sms + n_qt - 1) / n_qt;
         L.n_splits = sp < L.tile_end ? sp : L.tile_end;
-        L.status = ctx->d_status;
+        L.status = S.status;
         L.dense = dense;
         L.dense_base = 0;
         L.dense_ld = pre;
@@ -273,7 +274,7 @@ int run_scan(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes,
         L.cand_d = S.cand_d;
         L.cand_i = S.cand_i;
         L.cand_n = S.cand_n;
-        L.status = ctx->d_status;
+        L.status = S.status;
         if (keff <= kLocalKMax) {  // thresholds start "none" (0x7f7f7f7f = 3.4e38)
             L.pub = S.pub;
             if (cudaMemsetAsync(S.pub, 0x7f, (size_t)nq * stages[s].splits * 2 * 4, st) !=
@@ -373,6 +374,7 @@ int pion_v_b200_slot_scan_topk(pion_b200_ctx* ctx, const pion_b200_index* ix,
         if (ensure(ctx->scratch, need) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "slot_scan_topk: scratch");
         scan_layout(0, nq, keff, ms, &S, static_cast<char*>(ctx->scratch.ptr));
+        S.status = call_status(ctx, mem);
         rc = run_scan(ctx, ix, dc, dn, (int)nq, n_scan, keff, stages, ns, S);
         if (rc == 0) {
             rc = launch_slot_emit(S.st_d, S.st_i, (int)nq, keff, (int)k, ds, dd, st);
@@ -495,6 +497,7 @@ int pion_v_b200_hnsw_brute_force(pion_b200_ctx* ctx, const pion_b200_index* ix, 
             return set_error(ctx, PION_B200_ENOMEM, "hnsw_brute_force: scratch");
         char* base = static_cast<char*>(ctx->scratch.ptr);
         scan_layout(off, nq, keff, ms, &S, base);
+        S.status = call_status(ctx, mem);
         const float* qsrc = dq;
         if (h.metric == 1) {  // _quantize_query_to_int8 normalises once (hnsw.mojo:669-671)
             float* qn = reinterpret_cast<float*>(base + o_qn);

@@ -567,14 +567,8 @@ int launch_bq_tc(const BqTcLaunch& L, cudaStream_t st) {
     if (p.tile_end <= p.tile_begin || p.n_splits < 1 ||
         p.list_base + p.n_splits * bq_lists_per_split() > p.n_lists)
         return PION_B200_ESHAPE;
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(bq::bq_tc_kernel<bq::EPI_WARPS / 4>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)bq::SMEM_BYTES) != cudaSuccess)
-            return PION_B200_ECUDA;
-        configured = true;
-    }
+    if (set_smem_limit((const void*)bq::bq_tc_kernel<bq::EPI_WARPS / 4>, (int)bq::SMEM_BYTES) != 0)
+        return PION_B200_ECUDA;
     dim3 grid((L.nq + bq::BM - 1) / bq::BM, L.n_splits);
     bq::bq_tc_kernel<bq::EPI_WARPS / 4><<<grid, bq::THREADS, bq::SMEM_BYTES, st>>>(
         *L.tmap_q, *L.tmap_rows, p);

@@ -67,7 +67,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete.  Returns false (and
 // records a timeout) if the budget runs out or another thread already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag,
+                                          uint64_t budget_ns = kWaitBudgetNs) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
@@ -75,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
         if (mbar_try_wait(bar, parity)) return true;
         if ((++spins & 63u) == 0) {
             if (abort_flag && *abort_flag) return false;
-            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            if (globaltimer_ns() - t0 > budget_ns) {
                 record_error(status, PION_B200_ETIMEOUT);
                 if (abort_flag) *abort_flag = 1;
                 return false;

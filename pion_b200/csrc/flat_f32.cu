@@ -672,9 +672,7 @@ static int staged_rows(int dim) {
 
 template <typename K>
 static bool allow_big_smem(K kernel) {
-    static bool ok = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          200 * 1024) == cudaSuccess;
-    return ok;
+    return set_smem_limit((const void*)kernel, 200 * 1024) == 0;
 }
 
 int launch_query_normalize(const float* q, int nq, int dim, float* out, float* qnorm,
@@ -715,14 +713,8 @@ int launch_max_reduce(const float* x, int64_t n, float* out, cudaStream_t st) {
 template <int KCAP>
 static int launch_bf16x3_k(const Ff32TcLaunch& L, const ff32::TcParams& p, int n_qt,
                            cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(ff32::flat_bf16x3_tc_kernel<KCAP>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)ff32::SMEM_BYTES) != cudaSuccess)
-            return PION_B200_ECUDA;
-        configured = true;
-    }
+    if (set_smem_limit((const void*)ff32::flat_bf16x3_tc_kernel<KCAP>, (int)ff32::SMEM_BYTES) != 0)
+        return PION_B200_ECUDA;
     dim3 grid(n_qt, p.n_splits);
     ff32::flat_bf16x3_tc_kernel<KCAP><<<grid, ff32::THREADS, ff32::SMEM_BYTES, st>>>(
         *L.tmap_qh, *L.tmap_ql, *L.tmap_rh, *L.tmap_rl, p);

@@ -65,6 +65,9 @@ struct TcParams {
     float* cand_val;
     int32_t* cand_idx;
     int* status;
+    uint64_t wait_ns;          // budget of every mbarrier wait
+    int test_stall;            // 1: CTA (0, 0)'s MMA warp first waits on a barrier that
+                               // nothing arrives on (exercises the timeout path)
 };
 
 // score(d) = fl(fl(fl(d) * rs) * qs), the reference epilogue for one dot product.
@@ -207,7 +210,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* stall = drain + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stall + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint32_t* stash_all = reinterpret_cast<uint32_t*>(smem + (SMEM_PIPE_BYTES - 1024));
 
@@ -230,6 +234,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
             mbar_init(&tempty[b], 32 * EPI_WARPS);
         }
         mbar_init(drain, 1);
+        mbar_init(stall, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
             for (int t = 0; t < my_tiles && ok; ++t) {
                 const int row0 = (t_begin + t) * BN;
                 for (int kb = 0; kb < p.kblocks; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, abort_flag)) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -273,22 +278,27 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
             }
             // Every copy this thread issued lands before the CTA may exit.
             for (int s = 0; s < STAGES; ++s)
-                if (issued[s]) mbar_wait(&full[s], issued_parity[s], p.status, nullptr);
+                if (issued[s]) mbar_wait(&full[s], issued_parity[s], p.status, nullptr, p.wait_ns);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int t = 0; t < my_tiles; ++t) {
+            // Test hook: a wait that runs out (nothing arrives on `stall`), after which the
+            // pipeline drains and the CTA frees its TMEM and returns with ETIMEOUT recorded.
+            const bool stalled = p.test_stall && blockIdx.x == 0 && blockIdx.y == 0 &&
+                                 !mbar_wait(stall, 0, p.status, abort_flag, p.wait_ns);
+            for (int t = 0; t < my_tiles && !stalled; ++t) {
                 const int buf = t & 1;
                 const uint32_t use = (uint32_t)(t >> 1);
-                if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, p.status, abort_flag)) break;
+                if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, p.status, abort_flag, p.wait_ns))
+                    break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
                 bool ok = true;
                 for (int kb = 0; kb < p.kblocks; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, p.status, abort_flag)) {
+                    if (!mbar_wait(&full[stage], phase, p.status, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -312,7 +322,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
             }
             // All MMAs issued above complete before TMEM is released.
             tc_commit(drain);
-            mbar_wait(drain, 0, p.status, nullptr);
+            mbar_wait(drain, 0, p.status, nullptr, p.wait_ns);
         }
     } else {
         // --------------------------------------------- epilogue: score + top-k
@@ -350,7 +360,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
             const float rs_max = __ldg(&p.tile_rs_max[tile]);
             // Every lane waits; the warp proceeds only if all of them saw the phase,
             // so the warp-collective TMEM loads below stay convergent.
-            const bool got = mbar_wait(&tfull[buf], use & 1u, p.status, abort_flag);
+            const bool got = mbar_wait(&tfull[buf], use & 1u, p.status, abort_flag, p.wait_ns);
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const float inv = __frcp_rn(__fmul_rn(rs_max, qs));
@@ -556,10 +566,19 @@ __global__ void __launch_bounds__(SCAN_THREADS)
 }  // namespace fi8
 
 // ------------------------------------------------------------------ merging --
-// One warp per query merges n_lists sorted lists of k (score, id) pairs laid out
-// [nq][n_lists][k] (list stride `k`) into the k best, adding id_offset to valid ids.
+// One warp per query merges n_lists sorted lists of k (score, id) pairs into the k
+// best by (score, id), adding id_offset to valid ids.  Input layouts: [nq][n_lists][k]
+// (list stride k) or lists-major [n_lists][nq][k] (an all-gather of per-shard lists);
+// scores and ids either in two arrays (es = 1) or interleaved as 8-byte (f32 score,
+// i32 id) pairs (es = 2, ci = the ids' view of the same buffer).
+//
+// When a query's lists fit the warp's shared-memory slice they are staged there with
+// coalesced loads first, so the k selection rounds read shared memory only.  Each lane
+// keeps the best head of its own lists (l = lane, lane + 32, ...) across rounds and
+// rescans them only when one of its lists supplied the winner.
 constexpr int MERGE_WARPS = 4;
 constexpr int MERGE_MAX_LISTS = 2048;
+constexpr int MERGE_STAGE_ENTRIES = 1024;  // per warp: 8 KB of staged pairs
 
 template <bool DESC>
 __device__ __forceinline__ bool merge_better(float sa, int32_t ia, float sb, int32_t ib) {
@@ -570,39 +589,69 @@ __device__ __forceinline__ bool merge_better(float sa, int32_t ia, float sb, int
     return ia < ib;
 }
 
-template <bool DESC>
+template <bool DESC, bool STAGED>
 __global__ void __launch_bounds__(MERGE_WARPS * 32)
-    merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int nq,
-                       int n_lists, int k, int64_t id_offset, float* out_v, int32_t* out_i,
-                       int lists_major, int out_stride) {
-    __shared__ uint16_t cursor[MERGE_WARPS][MERGE_MAX_LISTS];
+    merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int es,
+                       int nq, int n_lists, int k, int64_t id_offset, float* out_v,
+                       int32_t* out_i, int lists_major, int out_stride) {
+    __shared__ uint16_t cursor[MERGE_WARPS][STAGED ? MERGE_STAGE_ENTRIES : MERGE_MAX_LISTS];
+    __shared__ float stage_v[STAGED ? MERGE_WARPS : 1][STAGED ? MERGE_STAGE_ENTRIES : 1];
+    __shared__ int32_t stage_i[STAGED ? MERGE_WARPS : 1][STAGED ? MERGE_STAGE_ENTRIES : 1];
     const int w = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int q = blockIdx.x * MERGE_WARPS + w;
     if (q >= nq) return;
     for (int l = lane; l < n_lists; l += 32) cursor[w][l] = 0;
-    __syncwarp();
     const float pad = DESC ? -INFINITY : INFINITY;
-    // list l of query q starts at base + l * lstride
+    // entry c of list l of query q sits at element (base + l * lstride + c) * es
     const size_t base = lists_major ? (size_t)q * k : (size_t)q * n_lists * k;
     const size_t lstride = lists_major ? (size_t)nq * k : (size_t)k;
-    const float* qv = cv + base;
-    const int32_t* qi = ci + base;
-    for (int j = 0; j < k; ++j) {
-        float bv = pad;
-        int32_t bi = -1;
-        int bl = -1;
+    if (STAGED) {
+        const int total = n_lists * k;
+        for (int e = lane; e < total; e += 32) {
+            const int l = e / k, c = e - l * k;
+            const size_t at = (base + (size_t)l * lstride + c) * es;
+            stage_v[w][e] = cv[at];
+            stage_i[w][e] = ci[at];
+        }
+    }
+    __syncwarp();
+    auto head = [&](int l, int c, float& v, int32_t& id) {
+        if (STAGED) {
+            v = stage_v[w][l * k + c];
+            id = stage_i[w][l * k + c];
+        } else {
+            const size_t at = (base + (size_t)l * lstride + c) * es;
+            v = cv[at];
+            id = ci[at];
+        }
+    };
+    // best head among this lane's own lists
+    auto lane_best = [&](float& bv, int32_t& bi, int& bl) {
+        bv = pad;
+        bi = -1;
+        bl = -1;
         for (int l = lane; l < n_lists; l += 32) {
             const int c = cursor[w][l];
             if (c >= k) continue;
-            const float v = qv[(size_t)l * lstride + c];
-            const int32_t id = qi[(size_t)l * lstride + c];
+            float v;
+            int32_t id;
+            head(l, c, v, id);
             if (bl < 0 || merge_better<DESC>(v, id, bv, bi)) {
                 bv = v;
                 bi = id;
                 bl = l;
             }
         }
+    };
+    float mv;
+    int32_t mi;
+    int ml;
+    lane_best(mv, mi, ml);
+    for (int j = 0; j < k; ++j) {
+        float bv = mv;
+        int32_t bi = mi;
+        int bl = ml;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -616,11 +665,13 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32)
                 bl = ol;
             }
         }
-        if (bl >= 0 && (bl % 32) == lane) cursor[w][bl] += 1;
-        __syncwarp();
         if (lane == 0) {
-            out_v[(size_t)q * out_stride + j] = bv;
-            out_i[(size_t)q * out_stride + j] = bi >= 0 ? (int32_t)(bi + id_offset) : -1;
+            out_v[(size_t)q * out_stride + j] = bl >= 0 ? bv : pad;
+            out_i[(size_t)q * out_stride + j] = (bl >= 0 && bi >= 0) ? (int32_t)(bi + id_offset) : -1;
+        }
+        if (bl >= 0 && (bl & 31) == lane) {
+            cursor[w][bl] += 1;
+            lane_best(mv, mi, ml);
         }
     }
 }
@@ -697,17 +748,25 @@ int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_
 
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
-                       cudaStream_t st, bool lists_major, int out_stride) {
+                       cudaStream_t st, bool lists_major, int out_stride, bool pairs) {
     if (nq <= 0) return 0;
-    if (n_lists > MERGE_MAX_LISTS || k > 65535) return PION_B200_ESHAPE;
+    if (n_lists < 1 || n_lists > MERGE_MAX_LISTS || k < 1 || k > 65535) return PION_B200_ESHAPE;
     if (out_stride <= 0) out_stride = k;
+    const int es = pairs ? 2 : 1;
+    if (pairs) ci = reinterpret_cast<const int32_t*>(cv) + 1;
     const int blocks = (nq + MERGE_WARPS - 1) / MERGE_WARPS;
-    if (descending)
-        merge_lists_kernel<true><<<blocks, MERGE_WARPS * 32, 0, st>>>(
-            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0, out_stride);
-    else
-        merge_lists_kernel<false><<<blocks, MERGE_WARPS * 32, 0, st>>>(
-            cv, ci, nq, n_lists, k, id_offset, out_v, out_i, lists_major ? 1 : 0, out_stride);
+    const bool staged = (int64_t)n_lists * k <= MERGE_STAGE_ENTRIES;
+    const int lm = lists_major ? 1 : 0;
+#define PION_MERGE_GO(D, S)                                                              \
+    merge_lists_kernel<D, S><<<blocks, MERGE_WARPS * 32, 0, st>>>(cv, ci, es, nq, n_lists, k, \
+                                                                  id_offset, out_v, out_i, lm, \
+                                                                  out_stride)
+    if (descending) {
+        if (staged) PION_MERGE_GO(true, true); else PION_MERGE_GO(true, false);
+    } else {
+        if (staged) PION_MERGE_GO(false, true); else PION_MERGE_GO(false, false);
+    }
+#undef PION_MERGE_GO
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
@@ -734,14 +793,9 @@ int fi8_kcap(int k) { return k <= 16 ? 16 : (k <= 32 ? 32 : (k <= 64 ? 64 : 0));
 template <int KCAP, int EPI_WARPS>
 static int launch_tc_k(const CUtensorMap& tq, const CUtensorMap& tr, const fi8::TcParams& p,
                        int n_qt, cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)fi8::smem_bytes(EPI_WARPS)) != cudaSuccess)
-            return PION_B200_ECUDA;
-        configured = true;
-    }
+    if (set_smem_limit((const void*)fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>,
+                       (int)fi8::smem_bytes(EPI_WARPS)) != 0)
+        return PION_B200_ECUDA;
     dim3 grid(n_qt, p.n_splits);
     fi8::flat_i8_tc_kernel<KCAP, EPI_WARPS>
         <<<grid, 64 + 32 * EPI_WARPS, fi8::smem_bytes(EPI_WARPS), st>>>(tq, tr, p);
@@ -775,6 +829,8 @@ int launch_flat_i8_tc(const Fi8TcLaunch& L, cudaStream_t st) {
     p.cand_val = L.cand_val;
     p.cand_idx = L.cand_idx;
     p.status = L.status;
+    p.wait_ns = L.wait_ns;
+    p.test_stall = L.test_stall;
     if (p.tile_end <= p.tile_begin || p.n_splits < 1) return PION_B200_ESHAPE;
     if (p.list_base + p.n_splits * fi8_lists_per_split(p.k) > p.n_lists) return PION_B200_ESHAPE;
     const int n_qt = (L.nq + fi8::BM - 1) / fi8::BM;

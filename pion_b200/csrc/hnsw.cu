@@ -758,14 +758,7 @@ int launch_hnsw_quantize(const float* q, int nq, float gmin, float scale, int8_t
 
 template <int STAGE>
 static int beam_ctas_per_sm(size_t smem) {
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(hb::hnsw_beam_kernel<STAGE>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 227 * 1024) != cudaSuccess)
-            return 0;
-        configured = true;
-    }
+    if (set_smem_limit((const void*)hb::hnsw_beam_kernel<STAGE>, 227 * 1024) != 0) return 0;
     int blocks = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, hb::hnsw_beam_kernel<STAGE>,
                                                       hb::WARPS * 32, smem) != cudaSuccess)

@@ -13,6 +13,10 @@
 
 namespace pion {
 
+// Default budget of a device-side wait (ns): kernels finish in milliseconds, so two
+// seconds without progress means a stuck pipeline.
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;
+
 // A grow-only device buffer.
 struct DevBuf {
     void* ptr = nullptr;
@@ -78,8 +82,9 @@ struct pion_b200_ctx {
     int num_sms = 148;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
-    int* d_status = nullptr;       // device status word, written by bounded waits
-    int* h_status = nullptr;       // pinned mirror of d_status
+    int* d_status = nullptr;       // device status words written by bounded waits:
+                                   // [0] host-memory calls, [1] device-memory calls
+    int* h_status = nullptr;       // pinned mirror of both words
     pion::DevBuf scratch;          // per-call candidate lists
     pion::DevBuf scratch2;         // second-level scratch (merges, shortlists)
     pion::DevBuf stage_in;         // device copies of host inputs
@@ -90,10 +95,14 @@ struct pion_b200_ctx {
     int64_t launches = 0;
     cudaEvent_t switch_ev = nullptr;  // orders scratch use across set_stream switches
     int64_t slot_exact = 0;           // queries of the last slot scan that took the exact path
+    uint64_t wait_ns = pion::kDefaultWaitNs;  // budget of the FLAT INT8 kernels' waits
     // scoring-kernel timing (pion_v_b200_timing_*)
     bool timing = false;
     std::vector<cudaEvent_t> ev_start, ev_end;
+    std::vector<int> ev_tag;       // PION_B200_TIMING_* of each event pair
+    std::vector<bool> ev_closed;   // its end event was recorded
     size_t ev_used = 0;
+    int ev_open = -1;              // the pair opened last
 };
 
 struct pion_b200_index {
@@ -276,6 +285,9 @@ pion_b200_ctx* compat_default_ctx(const char* who);
 // ---- shared ABI helpers (abi.cu)
 int set_error(pion_b200_ctx* ctx, int code, const char* fmt, ...);
 int queue_status_readback(pion_b200_ctx* ctx);
+// The status word a call's kernels record into: word 0 for host-memory calls (checked
+// by the call itself), word 1 for device-memory calls (reported by pion_v_b200_sync).
+int* call_status(pion_b200_ctx* ctx, int mem);
 int finish_sync(pion_b200_ctx* ctx);
 bool valid_ctx(const pion_b200_ctx* ctx);
 int use_device(pion_b200_ctx* ctx);
@@ -284,6 +296,15 @@ int prepass_tiles(int k);
 int bound_tiles(int n_tiles, int k);
 bool use_prepass(int n_tiles, int k, const char* env);
 int ensure(DevBuf& b, size_t bytes);
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the CURRENT device
+// (cudaFuncSetAttribute is per device), remembered per (kernel, device) under a lock,
+// so a process that uses several GPUs from several host threads configures each one.
+int set_smem_limit(const void* kernel, int bytes);
+// Content fingerprint of a host table: `h` mixed with the first `take_bytes` bytes of
+// 64 evenly spaced rows and the last one.  Guards caches keyed by host pointers
+// against a different table allocated at the same address.
+uint64_t sample_rows_hash(uint64_t h, const void* base, int64_t n_rows, int64_t row_bytes,
+                          int64_t take_bytes);
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
                  uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                  uint32_t box_outer, CUtensorMapSwizzle swizzle);
@@ -301,10 +322,13 @@ int launch_quantize_rows_i8(const float* src, int64_t n_rows, int d, int d_pad, 
 int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st);
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
-                       cudaStream_t st, bool lists_major = false, int out_stride = 0);
-// Event pair around one scoring-kernel launch when timing is enabled.
-void timing_begin(pion_b200_ctx* ctx);
-void timing_end(pion_b200_ctx* ctx);
+                       cudaStream_t st, bool lists_major = false, int out_stride = 0,
+                       bool pairs = false);
+// Event pair around one scoring-kernel launch (or one phase of it, `tag` =
+// PION_B200_TIMING_*) when timing is enabled.  timing_begin returns the pair's slot
+// (-1 when timing is off); timing_end closes `slot`, or the pair opened last.
+int timing_begin(pion_b200_ctx* ctx, int tag = PION_B200_TIMING_SCORING);
+void timing_end(pion_b200_ctx* ctx, int slot = -1);
 // One launch of the tensor-core FLAT INT8 kernel over index tiles [tile_begin,
 // tile_end) (tiles of fi8_tile_rows() rows).  Each (query, split) writes
 // fi8_lists_per_split(k) sorted lists of k (score, id) pairs at list
@@ -332,6 +356,8 @@ struct Fi8TcLaunch {
     float* cand_val = nullptr;
     int32_t* cand_idx = nullptr;
     int* status = nullptr;
+    uint64_t wait_ns = kDefaultWaitNs;  // budget of every mbarrier wait in the kernel
+    int test_stall = 0;  // 1: one CTA waits on a barrier nothing arrives on (tests)
 };
 int fi8_lists_per_split(int k);
 int launch_flat_i8_tc(const Fi8TcLaunch& launch, cudaStream_t st);

@@ -837,14 +837,8 @@ int launch_slot_prep(const int8_t* codes, const float* qnorm_in, int nq, int k, 
 template <int KCAP, bool DENSE>
 static int slot_tc_go(dim3 grid, const SlotTcLaunch& L, const slot::TcParams& p,
                       cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(slot::slot_tc_kernel<KCAP, DENSE>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)slot::SMEM_BYTES) != cudaSuccess)
-            return PION_B200_ECUDA;
-        configured = true;
-    }
+    if (set_smem_limit((const void*)slot::slot_tc_kernel<KCAP, DENSE>, (int)slot::SMEM_BYTES) != 0)
+        return PION_B200_ECUDA;
     slot::slot_tc_kernel<KCAP, DENSE><<<grid, slot::THREADS, slot::SMEM_BYTES, st>>>(
         *L.tmap_q, *L.tmap_rows, p);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;

@@ -118,6 +118,10 @@ class Context:
     def sync(self):
         self.check(self.lib.pion_v_b200_sync(self.h))
 
+    def set_wait_budget(self, ns: int):
+        """Budget of each device-side wait of the FLAT INT8 kernels (ns; <= 0: 2 s)."""
+        self.check(self.lib.pion_v_b200_set_wait_budget(self.h, int(ns)))
+
     def reserve(self, max_nq: int, max_k: int):
         self.check(self.lib.pion_v_b200_reserve(self.h, max_nq, max_k))
 
@@ -129,11 +133,13 @@ class Context:
         """Record CUDA events around every scoring-kernel launch (benchmarks)."""
         self.check(self.lib.pion_v_b200_timing_enable(self.h, int(enable)))
 
-    def timing_read(self):
-        """(total ms, launches) of the scoring kernels recorded since timing(True)."""
+    def timing_read(self, tag: int = 0):
+        """(total ms, count) of the event pairs recorded since timing(True) for one phase:
+        0 every scoring kernel of a call, 1 the FLAT INT8 threshold pass, 2 its main pass."""
         ms = ctypes.c_double()
         n = ctypes.c_int64()
-        self.check(self.lib.pion_v_b200_timing_read(self.h, ctypes.byref(ms), ctypes.byref(n)))
+        self.check(self.lib.pion_v_b200_timing_read_tag(self.h, int(tag), ctypes.byref(ms),
+                                                        ctypes.byref(n)))
         return ms.value, n.value
 
     def close(self):
@@ -353,6 +359,37 @@ def merge_topk(ctx: Context, cand_scores, cand_ids, k: int, descending: bool = T
         flags = (_lib.MERGE_DESC if descending else 0) | (_lib.MERGE_LISTS_MAJOR if lists_major
                                                            else 0)
         ctx.check(ctx.lib.pion_v_b200_merge_topk(ctx.h, pv, pi, nq, n_lists, k, flags, po_v,
+                                                 po_i, mem))
+    return ids, sc
+
+
+def merge_topk_pairs(ctx: Context, pairs, k: int, descending: bool = True,
+                     lists_major: bool = True):
+    """merge_topk over interleaved (f32 score, i32 id) pairs: `pairs` int32 [n_lists, nq,
+    k, 2] (lists_major, the all-gather of pion_b200.sharded.pack_pairs) or [nq, n_lists,
+    k, 2]; numpy (host) or a CUDA tensor.  Returns (ids [nq, k], scores [nq, k])."""
+    if _is_torch(pairs):
+        if not pairs.is_contiguous() or pairs.dtype != torch.int32:
+            raise TypeError("pairs must be a contiguous int32 tensor")
+        p, mem = pairs.data_ptr(), (MEM_DEVICE if pairs.is_cuda else MEM_HOST)
+        keep = pairs
+    else:
+        keep = np.ascontiguousarray(pairs, dtype=np.int32)
+        p, mem = keep.ctypes.data, MEM_HOST
+    if keep.ndim != 4 or keep.shape[-1] != 2:
+        raise ValueError("pairs must have shape [lists, nq, k, 2] or [nq, lists, k, 2]")
+    if lists_major:
+        n_lists, nq, kk = keep.shape[:3]
+    else:
+        nq, n_lists, kk = keep.shape[:3]
+    if kk != k:
+        raise ValueError("candidate lists must hold exactly k entries")
+    ids, sc, po_i, po_v = _outputs(mem == MEM_DEVICE, nq, k,
+                                   pairs.device if mem == MEM_DEVICE else None)
+    with _TorchStream(ctx, mem):
+        flags = ((_lib.MERGE_DESC if descending else 0) |
+                 (_lib.MERGE_LISTS_MAJOR if lists_major else 0) | _lib.MERGE_PAIRS)
+        ctx.check(ctx.lib.pion_v_b200_merge_topk(ctx.h, p, None, nq, n_lists, k, flags, po_v,
                                                  po_i, mem))
     return ids, sc
 
@@ -840,11 +877,29 @@ def rescore_knn(index, q, ids, scores, ctx: Context | None = None):
     ascending and stable (the reference's insertion sort), ids alongside.  `ids` int32
     [nq, k] and `scores` float32 [nq, k], host arrays, are updated in place; when the index
     has no source for metric scores (a block-quantised graph without FP32 rows) both stay
-    as they are.  Returns (ids, scores)."""
+    as they are.  Returns (ids, scores).
+
+    A stable argsort equals the insertion sort on rows without NaN; a row holding a NaN
+    is sorted by the insertion loop itself (`<` is false against NaN, so a NaN stops the
+    entries behind it where the reference stops them)."""
+    if not isinstance(ids, np.ndarray) or not isinstance(scores, np.ndarray):
+        raise TypeError("rescore_knn: ids and scores must be host numpy arrays")
+    if ids.shape != scores.shape or ids.ndim != 2:
+        raise ValueError("rescore_knn: ids and scores must both be [nq, k]")
     ok = index.metric_scores(q, ids, scores, ctx=ctx)
     if ok is False:
         return ids, scores
+    nan_rows = np.isnan(scores).any(axis=1)
     order = np.argsort(scores, axis=1, kind="stable")
-    ids[...] = np.take_along_axis(ids, order, axis=1)
-    scores[...] = np.take_along_axis(scores, order, axis=1)
+    clean = ~nan_rows
+    ids[clean] = np.take_along_axis(ids[clean], order[clean], axis=1)
+    scores[clean] = np.take_along_axis(scores[clean], order[clean], axis=1)
+    for t in np.nonzero(nan_rows)[0]:
+        si, ss = ids[t], scores[t]
+        for a in range(1, ss.shape[0]):
+            b = a
+            while b > 0 and ss[b] < ss[b - 1]:
+                ss[b], ss[b - 1] = ss[b - 1], ss[b]
+                si[b], si[b - 1] = si[b - 1], si[b]
+                b -= 1
     return ids, scores

@@ -7,6 +7,9 @@ This is the B200 counterpart of the reference's intra-process shard bus
 concatenate up to k per shard, keep the best k), over NCCL instead of shared memory.
 Ids are global (each shard registers its rows with id_base = its first row), and the
 merge orders by (score, id), so the result equals the single-index result.
+
+A shard's k results per query travel as interleaved 8-byte (f32 score, i32 id) pairs,
+so one all-gather of B * k * 8 bytes per rank carries them (not one per array).
 """
 from __future__ import annotations
 
@@ -18,13 +21,26 @@ def shard_bounds(n_rows: int, world: int, rank: int) -> Tuple[int, int]:
     return n_rows * rank // world, n_rows * (rank + 1) // world
 
 
+def pack_pairs(ids, scores):
+    """ids int32 [B, k] and scores float32 [B, k] -> int32 [B, k, 2]: per entry the
+    score's bits, then the id (the 8-byte pair layout of PION_B200_MERGE_PAIRS)."""
+    import torch
+    return torch.stack((scores.contiguous().view(torch.int32), ids.contiguous()), dim=-1)
+
+
+def unpack_pairs(pairs):
+    """int32 [..., k, 2] pairs -> (ids int32 [..., k], scores float32 [..., k])."""
+    import torch
+    return pairs[..., 1].contiguous(), pairs[..., 0].contiguous().view(torch.float32)
+
+
 class ShardedSearch:
     """One step of a row-sharded search.
 
     local_search(inputs) -> (ids int32 [B, k], scores float32 [B, k]) for this shard,
-    global ids, ordered.  merge(scores [W, B, k], ids [W, B, k]) -> (ids, scores): the
-    k best per query of the gathered lists (on the GPU: pion_b200.merge_topk with
-    lists_major=True).  `group` is a torch.distributed process group (None: default).
+    global ids, ordered.  merge(pairs int32 [W, B, k, 2]) -> (ids, scores): the k best
+    per query of the gathered (score, id) pairs (on the GPU: pion_b200.merge_topk_pairs
+    with lists_major=True).  `group` is a torch.distributed process group (None: default).
     """
 
     def __init__(self, local_search: Callable, k: int, merge: Callable, group=None):
@@ -35,7 +51,6 @@ class ShardedSearch:
         self.merge = merge
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self._bufs = None
 
     def _gather(self, t):
         import torch
@@ -53,4 +68,31 @@ class ShardedSearch:
         ids, scores = self.local_search(inputs)
         if self.world == 1:
             return ids, scores
-        return self.merge(self._gather(scores), self._gather(ids))
+        return self.merge(self._gather(pack_pairs(ids, scores)))
+
+    def breakdown(self, inputs, steps: int):
+        """Average device milliseconds per step of each phase -- local scoring and
+        top-k, pack + all-gather, merge -- over `steps` steps timed with CUDA events on
+        the current stream (GPU tensors only)."""
+        import torch
+
+        st = torch.cuda.current_stream()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        for e in ev:
+            e[0].record(st)
+            ids, scores = self.local_search(inputs)
+            e[1].record(st)
+            if self.world > 1:
+                g = self._gather(pack_pairs(ids, scores))
+                e[2].record(st)
+                self.merge(g)
+            else:
+                e[2].record(st)
+            e[3].record(st)
+        torch.cuda.synchronize()
+        parts = [0.0, 0.0, 0.0]
+        for e in ev:
+            for j in range(3):
+                parts[j] += e[j].elapsed_time(e[j + 1])
+        n = max(1, steps)
+        return {"local_ms": parts[0] / n, "allgather_ms": parts[1] / n, "merge_ms": parts[2] / n}

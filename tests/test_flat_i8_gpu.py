@@ -222,3 +222,129 @@ def test_full_size_one_million_rows(ctx, oracle):
     s = sc.cpu().numpy()
     assert (np.diff(s, axis=1) <= 0).all()
     assert ((ids >= 0) & (ids < 1_000_000)).all()
+
+
+@pytest.mark.parametrize("descending,lists_major", [(True, True), (False, True), (True, False)])
+def test_merge_topk_pairs_matches_numpy(ctx, rng, descending, lists_major):
+    """The all-gather layout: one buffer of interleaved (f32 score, i32 id) pairs,
+    ties at every score, padding entries (id -1) at the ends of some lists."""
+    import torch
+
+    import pion_b200
+    from pion_b200.sharded import pack_pairs
+    L, nq, k = 8, 300, 10
+    v = rng.integers(0, 6, (L, nq, k)).astype(np.float32)
+    i = rng.integers(0, 100000, (L, nq, k)).astype(np.int32)
+    sign = -1.0 if descending else 1.0
+    pad = -np.inf if descending else np.inf
+    v[0, :5, 7:] = pad
+    i[0, :5, 7:] = -1
+    for a in range(L):
+        for b in range(nq):
+            o = np.lexsort((np.where(i[a, b] < 0, 1 << 30, i[a, b]), sign * v[a, b]))
+            v[a, b], i[a, b] = v[a, b][o], i[a, b][o]
+    pairs = pack_pairs(torch.from_numpy(i), torch.from_numpy(v))  # [L, nq, k, 2]
+    if not lists_major:
+        pairs = pairs.permute(1, 0, 2, 3).contiguous()
+    for dev in (False, True):
+        p = pairs.cuda() if dev else pairs.numpy()
+        ids, sc = pion_b200.merge_topk_pairs(ctx, p, k, descending=descending,
+                                             lists_major=lists_major)
+        if dev:
+            ids, sc = ids.cpu().numpy(), sc.cpu().numpy()
+        for b in range(nq):
+            fv, fi = v[:, b].ravel(), i[:, b].ravel()
+            o = np.lexsort((np.where(fi < 0, 1 << 30, fi), sign * fv))[:k]
+            assert ids[b].tolist() == fi[o].tolist(), b
+            assert sc[b].tolist() == fv[o].tolist(), b
+
+
+def test_merge_topk_many_lists_unstaged(ctx, rng):
+    """More lists x k than a warp stages in shared memory: the global-memory path."""
+    import pion_b200
+    nq, L, k = 9, 300, 16
+    v = -np.sort(-rng.standard_normal((nq, L, k)).astype(np.float32), axis=2)
+    i = rng.integers(0, 1 << 30, (nq, L, k)).astype(np.int32)
+    ids, sc = pion_b200.merge_topk(ctx, v, i, k, descending=True)
+    for a in range(nq):
+        fv, fi = v[a].ravel(), i[a].ravel()
+        o = np.lexsort((fi, -fv))[:k]
+        assert ids[a].tolist() == fi[o].tolist()
+
+
+def test_timing_phases(ctx, oracle):
+    """The threshold and main passes are timed separately inside the scoring span."""
+    import pion_b200
+    keys, ks, q, qsc = quantized_case(oracle, 120000, 1536, 256, seed=77)
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    ctx.timing(True)
+    try:
+        for _ in range(3):
+            ix.search(q, qsc, 10)
+        tot, n = ctx.timing_read(0)
+        thr, nt = ctx.timing_read(1)
+        main, nm = ctx.timing_read(2)
+    finally:
+        ctx.timing(False)
+    assert n == 3 and nt == 3 and nm == 3
+    assert 0 < thr < tot and 0 < main < tot and thr + main <= tot * 1.001
+    ix.free()
+
+
+def test_second_device_in_one_process(oracle):
+    """The kernels' shared-memory limit is raised on every device a process uses, not
+    only on the first one that launched them."""
+    import torch
+
+    import pion_b200
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one visible GPU")
+    keys, ks, q, qsc = quantized_case(oracle, 20000, 1536, 130, seed=5)
+    got = []
+    for dev in (0, 1):
+        with pion_b200.Context(dev) as c:
+            ix = pion_b200.FlatI8Index(c, keys, ks)
+            got.append(ix.search(q, qsc, 10))
+            got.append(ix.search(q, qsc, 40))
+            ix.free()
+    assert all(np.array_equal(a[0], b[0]) for a, b in zip(got[:2], got[2:]))
+    assert_matches_oracle(oracle, keys, ks, q, qsc, 10, *got[0])
+
+
+def test_wait_that_runs_out(ctx, oracle, monkeypatch):
+    """A device-side wait that runs out (one CTA's MMA warp waits on a barrier nothing
+    arrives on, with a 1 ms budget) ends the kernel with PION_B200_ETIMEOUT: the copies
+    and MMAs in flight drain, the tensor memory is freed, and the next call on the same
+    context is correct.  Host-buffer calls report it themselves; device-buffer calls
+    through pion_v_b200_sync, never as a later call's failure."""
+    import torch
+
+    import pion_b200
+    from pion_b200 import _lib
+    keys, ks, q, qsc = quantized_case(oracle, 20000, 1536, 300, seed=31)
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    want_i, want_v = ix.search(q, qsc, 10)
+    dq, dqs = torch.from_numpy(q).cuda(), torch.from_numpy(qsc).cuda()
+    ctx.set_wait_budget(1_000_000)
+    monkeypatch.setenv("PION_B200_TEST_STALL", "1")
+    try:
+        with pytest.raises(pion_b200.PionError) as e:
+            ix.search(q, qsc, 10)
+        assert e.value.code == _lib.ETIMEOUT
+        ix.search(dq, dqs, 10)            # device buffers: returns once queued
+        monkeypatch.delenv("PION_B200_TEST_STALL")
+        got_i, got_v = ix.search(q, qsc, 10)  # a host call after it is not blamed
+        assert np.array_equal(got_i, want_i)
+        with pytest.raises(pion_b200.PionError) as e:
+            ctx.sync()
+        assert e.value.code == _lib.ETIMEOUT
+    finally:
+        monkeypatch.delenv("PION_B200_TEST_STALL", raising=False)
+        ctx.set_wait_budget(0)
+    ctx.sync()
+    got_i, got_v = ix.search(q, qsc, 10)
+    assert np.array_equal(got_i, want_i) and np.array_equal(got_v, want_v)
+    di, dv = ix.search(dq, dqs, 10)
+    ctx.sync()
+    assert np.array_equal(di.cpu().numpy(), want_i)
+    ix.free()

@@ -157,6 +157,45 @@ def test_reference_beam_symbol(oracle, small):
     assert lib.pion_v_b200_beam_forget(None) == 0
 
 
+def test_beam_symbol_sees_a_new_graph_at_the_same_addresses(oracle, small):
+    """The device copy pion_v_beam_1536 keeps is keyed by the view's host pointers and
+    sizes and by a fingerprint of sampled rows: another graph written into the same
+    buffers is served as itself, without pion_v_b200_beam_forget."""
+    import ctypes
+
+    import pion_b200
+    from pion_b200 import _lib
+    _, A, _, _, qs = small
+    B = _graph(6000, 64, seed=9)[0].arrays()
+    assert B["num_nodes"] == A["num_nodes"] and B["compact_stride"] == A["compact_stride"]
+    lib = pion_b200.load()
+    bufs = {x: np.array(A[x], copy=True) for x in ("l0_compact", "l0_slots", "compact_buffer")}
+    n = A["num_nodes"]
+    for G in (A, B, A):
+        for x in bufs:
+            np.copyto(bufs[x], G[x])
+        qc = np.ascontiguousarray(oracle.hnsw_query_codes(G, qs[:1])[0])
+        start, ef = int(G["entry_point"]), 64
+        v = G["compact_buffer"][G["node_slot"][start], 8:8 + 1536].astype(np.int32)
+        d0 = np.float32(((v - qc.astype(np.int32)) ** 2).sum())
+        qn = np.float32((qc.astype(np.int32) ** 2).sum())
+        entries = np.zeros(ef, dtype=[("d", "<f4"), ("id", "<u4")])
+        entries[0] = (d0, start)
+        pool = _lib.LinearPool(entries.ctypes.data, ef, 1, 0, ef)
+        visited = np.zeros(n, np.uint16)
+        view = _lib.BeamView1536(ctypes.pointer(pool), ef, float(qn), 0.0, qc.ctypes.data,
+                                 bufs["l0_compact"].ctypes.data, bufs["l0_slots"].ctypes.data,
+                                 n, None, visited.ctypes.data, 7,
+                                 bufs["compact_buffer"].ctypes.data, G["compact_stride"],
+                                 G["compact_hdr"], None)
+        assert lib.pion_v_beam_1536(ctypes.byref(view)) == 0
+        od, oi = oracle.hnsw_beam_pool(G, qc, qn, ef, [d0], [start], 0)
+        got = entries[:pool.size]
+        assert np.array_equal(got["id"], oi)
+        assert np.array_equal(got["d"].view(np.uint32), od.view(np.uint32))
+    assert lib.pion_v_b200_beam_forget(None) == 0
+
+
 def test_metric_scores(oracle, small, ctx):
     """metric_scores on the GPU == the restatement, bit for bit (COSINE: 1 - cos from the
     dequantised codes), and close to the exact fp32 cosine distance of the rows."""

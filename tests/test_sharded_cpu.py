@@ -25,7 +25,9 @@ def _merge(descending):
     """Test-side stand-in for the GPU merge kernel: (score, id) order over the lists."""
     import torch
 
-    def merge(scores, ids):  # [W, B, k]
+    def merge(pairs):  # [W, B, k, 2] int32: (score bits, id)
+        from pion_b200.sharded import unpack_pairs
+        ids, scores = unpack_pairs(pairs)
         W, B, k = scores.shape
         s = scores.permute(1, 0, 2).reshape(B, W * k).numpy()
         i = ids.permute(1, 0, 2).reshape(B, W * k).numpy()
