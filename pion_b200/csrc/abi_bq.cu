@@ -15,6 +15,13 @@ using namespace pion;
 
 namespace {
 
+// PION_B200_BQ_PATH: 0 auto (one query: the popcount stream), 1 the stream for every
+// query, 2 the tensor-core stages (tests).
+int forced_bq_path() {
+    const char* e = getenv("PION_B200_BQ_PATH");
+    return e ? atoi(e) : 0;
+}
+
 // PION_B200_BQ_EXACT=1 sends every query through the exact popcount scan (tests).
 int force_fallback() {
     const char* e = getenv("PION_B200_BQ_EXACT");
@@ -148,9 +155,51 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
                                       align_up(out_bytes, 256));
     }
     int rc = 0;
+    const int path = forced_bq_path();
+    const bool scan1 = ix->n_rows > 0 && bq_scan1_supported(words, S) &&
+                       (path == 1 || (path == 0 && nq == 1));
     if (ix->n_rows == 0) {
         rc = launch_fill_results(dv, di, (size_t)nq * kk, INFINITY, st);
         ctx->launches++;
+    } else if (scan1) {
+        // One query: the popcount stream over the packed codes, then the same rerank.
+        const int ctas = bq_scan1_ctas(ix->n_rows, ctx->num_sms);
+        size_t off = 0;
+        auto take = [&](size_t bytes) {
+            size_t o = off;
+            off += align_up(bytes, 256);
+            return o;
+        };
+        const size_t o_qn = take((size_t)nq * dim * 4), o_qnorm = take((size_t)nq * 4),
+                     o_qpm = take((size_t)nq * dim), o_qc = take((size_t)nq * words * 8),
+                     o_slid = take((size_t)nq * S * 4), o_slh = take((size_t)nq * S * 2),
+                     o_sln = take((size_t)nq * 4),
+                     o_work = take(bq_scan1_scratch(ix->n_rows, words));
+        if (ensure(ctx->scratch, off) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "bq_rerank_knn: scratch");
+        char* base = static_cast<char*>(ctx->scratch.ptr);
+        float* qn = reinterpret_cast<float*>(base + o_qn);
+        uint64_t* qc = reinterpret_cast<uint64_t*>(base + o_qc);
+        int32_t* sl_id = reinterpret_cast<int32_t*>(base + o_slid);
+        uint16_t* sl_h = reinterpret_cast<uint16_t*>(base + o_slh);
+        int* sl_n = reinterpret_cast<int*>(base + o_sln);
+        const int t_all = timing_begin(ctx);
+        rc = launch_query_normalize(dq, nqi, dim, qn, reinterpret_cast<float*>(base + o_qnorm),
+                                    st);
+        if (rc == 0) rc = launch_signs(qn, nq, dim, reinterpret_cast<int8_t*>(base + o_qpm), qc, st);
+        ctx->launches += 2;
+        for (int64_t t = 0; t < nq && rc == 0; ++t) {
+            rc = launch_bq_scan1(ix->codes, ix->n_rows, words, qc + (size_t)t * words, S, ctas,
+                                 base + o_work, sl_id + (size_t)t * S, sl_h + (size_t)t * S,
+                                 sl_n + t, st);
+            ctx->launches += 3;
+        }
+        timing_end(ctx, t_all);
+        if (rc == 0) {
+            rc = launch_bq_rerank(ix->rows_f32, dim, qn, sl_id, sl_n, S, nqi, kk, ix->id_base, dv,
+                                  di, st);
+            ctx->launches++;
+        }
     } else {
         const int n_qt = (nqi + bq_query_tile() - 1) / bq_query_tile();
         const int n_tiles = (int)((ix->n_rows + bq_tile_rows() - 1) / bq_tile_rows());

@@ -13,6 +13,13 @@
 using namespace pion;
 
 // PION_B200_F32_EXACT=1 sends every query through the exact CUDA-core scan (tests).
+// Forced path selection for tests: 0 auto (one query: the exact stream), 1 the exact
+// stream for every query, 2 the tensor-core shortlist.
+static int forced_f32_path() {
+    const char* e = getenv("PION_B200_F32_PATH");
+    return e ? atoi(e) : 0;
+}
+
 static int force_exact_f32() {
     const char* e = getenv("PION_B200_F32_EXACT");
     return e && atoi(e) != 0 ? 1 : 0;
@@ -197,9 +204,40 @@ int pion_v_b200_flat_f32_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, cons
                                       align_up(out_bytes, 256));
     }
     int rc = 0;
+    const int path = forced_f32_path();
+    const bool scan1 = ix->n_rows > 0 && ff32_scan1_supported(dim, kk) &&
+                       (path == 1 || (path == 0 && nq == 1));
     if (ix->n_rows == 0) {
         rc = launch_fill_results(dv, di, (size_t)nq * kk, INFINITY, st);
         ctx->launches++;
+    } else if (scan1) {
+        // One query (or forced): an exact HBM stream per query, no tensor-core shortlist.
+        const int ctas = ff32_scan1_ctas(ix->n_rows, ctx->num_sms);
+        const size_t n_qn = (size_t)nq * dim, n_cand = (size_t)nq * ctas * kk;
+        const size_t o_qn = 0, o_qnorm = align_up(n_qn * 4, 256),
+                     o_cv = o_qnorm + align_up((size_t)nq * 4, 256),
+                     o_ci = o_cv + align_up(n_cand * 4, 256), total = o_ci + n_cand * 4;
+        if (ensure(ctx->scratch, total) != 0)
+            return set_error(ctx, PION_B200_ENOMEM, "flat_f32_knn: scratch");
+        char* base = static_cast<char*>(ctx->scratch.ptr);
+        float* qn = reinterpret_cast<float*>(base + o_qn);
+        float* cv = reinterpret_cast<float*>(base + o_cv);
+        int32_t* ci = reinterpret_cast<int32_t*>(base + o_ci);
+        const int t_all = timing_begin(ctx);
+        rc = launch_query_normalize(dq, nqi, dim, qn, reinterpret_cast<float*>(base + o_qnorm),
+                                    st);
+        ctx->launches++;
+        for (int64_t t = 0; t < nq && rc == 0; ++t) {
+            rc = launch_flat_f32_scan1(ix->rows_f32, ix->n_rows, dim, qn + (size_t)t * dim, kk,
+                                       ctas, cv + (size_t)t * ctas * kk,
+                                       ci + (size_t)t * ctas * kk, st);
+            ctx->launches++;
+        }
+        timing_end(ctx, t_all);
+        if (rc == 0) {
+            rc = launch_merge_lists(cv, ci, nqi, ctas, kk, ix->id_base, false, dv, di, st);
+            ctx->launches++;
+        }
     } else {
         const int kc = ff32_kc(kk);
         const int n_qt = (nqi + ff32_query_tile() - 1) / ff32_query_tile();

@@ -531,9 +531,237 @@ __global__ void __launch_bounds__(256) bq_rerank_kernel(
     }
 }
 
+// ------------------------------------------------------- one query: popcount stream
+// The Hamming shortlist of ONE query as an HBM stream over the packed codes (no ±1
+// expansion): 4 lanes per row, each 128-bit load two code words, XOR with the query's
+// words and popcount; every distance is kept (u16, 2 bytes per row) and counted in a
+// histogram.  Then the S-th smallest distance D* comes from the histogram; rows below
+// D* are collected in any order, rows at D* are taken by ascending row id (the
+// (distance, id) order of the batched path), and the shortlist is sorted.
+constexpr int B1_THREADS = 256;
+constexpr int B1_GROUPS = B1_THREADS / 4;
+constexpr int B1_MAX_WORDS = 256;   // dim <= 16384
+constexpr int B1_TIECAP = 8192;     // ties at D* sorted in shared memory; more: ordered scan
+
+__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Pass 1: dist[r] and the global histogram (hist[0..dim], zeroed by the caller).
+__global__ void __launch_bounds__(B1_THREADS)
+    bq_scan1_hist_kernel(const uint64_t* __restrict__ codes, int64_t n_rows, int words,
+                         const uint64_t* __restrict__ qcode, int64_t rows_per_cta,
+                         uint16_t* __restrict__ dist, int* __restrict__ hist) {
+    extern __shared__ int b1_hist[];  // dim + 1 bins
+    __shared__ uint4 qv[B1_MAX_WORDS / 2];
+    const int dim = words * 64;
+    const int chunks = words >> 1;  // 16-byte chunks per row
+    for (int i = threadIdx.x; i <= dim; i += B1_THREADS) b1_hist[i] = 0;
+    for (int c = threadIdx.x; c < chunks; c += B1_THREADS)
+        qv[c] = reinterpret_cast<const uint4*>(qcode)[c];
+    __syncthreads();
+    const int g = threadIdx.x >> 2;
+    const int j = threadIdx.x & 3;
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > n_rows) r1 = n_rows;
+    for (int64_t base = r0; base < r1; base += B1_GROUPS) {
+        const int64_t r = base + g;
+        int h = 0;
+        if (r < r1) {
+            const uint4* rp = reinterpret_cast<const uint4*>(codes + r * words);
+#pragma unroll 4
+            for (int c = j; c < chunks; c += 4) {
+                const uint4 a = ld_stream_u4(rp + c);
+                const uint4 b = qv[c];
+                h += __popc(a.x ^ b.x) + __popc(a.y ^ b.y) + __popc(a.z ^ b.z) +
+                     __popc(a.w ^ b.w);
+            }
+        }
+        h += __shfl_xor_sync(0xffffffffu, h, 1);
+        h += __shfl_xor_sync(0xffffffffu, h, 2);
+        if (r < r1 && j == 0) {
+            dist[r] = (uint16_t)h;
+            atomicAdd(&b1_hist[h], 1);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i <= dim; i += B1_THREADS)
+        if (b1_hist[i]) atomicAdd(&hist[i], b1_hist[i]);
+}
+
+// D* = the smallest d with #(dist <= d) >= want, and #(dist < D*), by one CTA's scan
+// of the histogram (every CTA of pass 2 recomputes it: 6 KB of reads).
+__device__ void b1_threshold(const int* __restrict__ hist, int dim, int want, int* d_out,
+                             int* below_out) {
+    __shared__ int seg[B1_THREADS];
+    const int per = (dim + 1 + B1_THREADS - 1) / B1_THREADS;
+    const int lo = threadIdx.x * per;
+    int sum = 0;
+    for (int i = lo; i < lo + per && i <= dim; ++i) sum += hist[i];
+    seg[threadIdx.x] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0, t = 0;
+        for (; t < B1_THREADS; ++t) {
+            if (acc + seg[t] >= want) break;
+            acc += seg[t];
+        }
+        int d = t * per;
+        for (; d <= dim; ++d) {
+            if (acc + hist[d] >= want) break;
+            acc += hist[d];
+        }
+        *d_out = d;
+        *below_out = acc;
+    }
+    __syncthreads();
+}
+
+// Pass 2: rows below D* as (dist << 32 | row) keys, rows at D* as row ids (unordered,
+// counted; at most B1_TIECAP kept).  meta: [0] keys, [1] ties, [2] D*, [3] below.
+__global__ void __launch_bounds__(B1_THREADS)
+    bq_scan1_collect_kernel(const uint16_t* __restrict__ dist, int64_t n_rows, int dim,
+                            const int* __restrict__ hist, int want, int64_t rows_per_cta,
+                            uint64_t* __restrict__ keys, int32_t* __restrict__ ties,
+                            int* __restrict__ meta) {
+    __shared__ int D, below;
+    b1_threshold(hist, dim, want, &D, &below);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        meta[2] = D;
+        meta[3] = below;
+    }
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > n_rows) r1 = n_rows;
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += B1_THREADS) {
+        const int h = dist[r];
+        if (h < D) {
+            keys[atomicAdd(&meta[0], 1)] = ((uint64_t)h << 32) | (uint32_t)r;
+        } else if (h == D) {
+            const int t = atomicAdd(&meta[1], 1);
+            if (t < B1_TIECAP) ties[t] = (int32_t)r;
+        }
+    }
+}
+
+// Pass 3 (one CTA): the first (want - below) rows at D* by id -- sorted in shared memory,
+// or, when there are more than B1_TIECAP of them, by an ordered scan of dist -- then the
+// shortlist sorted by (distance, id).
+__global__ void __launch_bounds__(1024)
+    bq_scan1_finish_kernel(const uint16_t* __restrict__ dist, int64_t n_rows,
+                           const uint64_t* __restrict__ keys_in, const int32_t* __restrict__ ties,
+                           const int* __restrict__ meta, int want, int S,
+                           int32_t* __restrict__ out_id, uint16_t* __restrict__ out_h,
+                           int* __restrict__ out_n) {
+    extern __shared__ uint64_t b1_keys[];  // B1_TIECAP (ties) then 512 (shortlist)
+    uint64_t* tk = b1_keys;
+    uint64_t* sk = b1_keys + B1_TIECAP;
+    __shared__ int warp_cnt[32];
+    __shared__ int taken;
+    const int D = meta[2], below = meta[3], n_tie = meta[1];
+    const int need = want - below;
+    for (int i = threadIdx.x; i < below; i += blockDim.x) sk[i] = keys_in[i];
+    if (n_tie <= B1_TIECAP) {
+        int p2 = 1;
+        while (p2 < n_tie) p2 <<= 1;
+        for (int i = threadIdx.x; i < p2; i += blockDim.x)
+            tk[i] = i < n_tie ? (uint64_t)(uint32_t)ties[i] : ~0ull;
+        __syncthreads();
+        if (n_tie > 1) bitonic_sort_u64(tk, p2);
+        for (int i = threadIdx.x; i < need; i += blockDim.x)
+            sk[below + i] = ((uint64_t)D << 32) | tk[i];
+    } else {
+        if (threadIdx.x == 0) taken = 0;
+        __syncthreads();
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+        for (int64_t base = 0; base < n_rows && taken < need; base += blockDim.x) {
+            const int64_t r = base + threadIdx.x;
+            const bool tie = r < n_rows && dist[r] == D;
+            const unsigned bal = __ballot_sync(0xffffffffu, tie);
+            if (lane == 0) warp_cnt[w] = __popc(bal);
+            __syncthreads();
+            int before = taken;
+            for (int x = 0; x < w; ++x) before += warp_cnt[x];
+            const int rank = before + __popc(bal & ((1u << lane) - 1u));
+            if (tie && rank < need) sk[below + rank] = ((uint64_t)D << 32) | (uint32_t)r;
+            __syncthreads();
+            if (threadIdx.x == 0)
+                for (int x = 0; x < nw; ++x) taken += warp_cnt[x];
+            __syncthreads();
+        }
+    }
+    __syncthreads();
+    int p2 = 1;
+    while (p2 < want) p2 <<= 1;
+    for (int i = want + threadIdx.x; i < p2; i += blockDim.x) sk[i] = ~0ull;
+    __syncthreads();
+    if (want > 1) bitonic_sort_u64(sk, p2);
+    for (int i = threadIdx.x; i < S; i += blockDim.x) {
+        out_id[i] = i < want ? (int32_t)(uint32_t)sk[i] : -1;
+        out_h[i] = i < want ? (uint16_t)(sk[i] >> 32) : (uint16_t)0xffff;
+    }
+    if (threadIdx.x == 0) *out_n = want;
+}
+
 }  // namespace bq
 
 // =========================================================== host launchers ==
+
+bool bq_scan1_supported(int words, int S) {
+    return words % 2 == 0 && words <= bq::B1_MAX_WORDS && S >= 1 && S <= 512;
+}
+
+int bq_scan1_ctas(int64_t n_rows, int num_sms) {
+    int64_t ctas = (int64_t)num_sms * 4;
+    const int64_t min_rows = 4 * bq::B1_GROUPS;
+    if (ctas * min_rows > n_rows) ctas = (n_rows + min_rows - 1) / min_rows;
+    return (int)(ctas < 1 ? 1 : ctas);
+}
+
+size_t bq_scan1_scratch(int64_t n_rows, int words) {
+    return (size_t)(n_rows * 2 + 255) / 256 * 256 + (size_t)(words * 64 + 1 + 63) / 64 * 256 +
+           512 * 8 + bq::B1_TIECAP * 4 + 256;
+}
+
+int launch_bq_scan1(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcode,
+                    int S, int ctas, void* scratch, int32_t* sl_id, uint16_t* sl_h, int* sl_n,
+                    cudaStream_t st) {
+    if (!bq_scan1_supported(words, S) || n_rows <= 0) return PION_B200_ESHAPE;
+    const int dim = words * 64;
+    char* base = static_cast<char*>(scratch);
+    uint16_t* dist = reinterpret_cast<uint16_t*>(base);
+    size_t off = (size_t)(n_rows * 2 + 255) / 256 * 256;
+    int* hist = reinterpret_cast<int*>(base + off);
+    off += (size_t)(dim + 1 + 63) / 64 * 256;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(base + off);
+    off += 512 * 8;
+    int32_t* ties = reinterpret_cast<int32_t*>(base + off);
+    off += bq::B1_TIECAP * 4;
+    int* meta = reinterpret_cast<int*>(base + off);
+    const int want = n_rows < S ? (int)n_rows : S;
+    if (cudaMemsetAsync(hist, 0, (size_t)(dim + 1) * 4, st) != cudaSuccess ||
+        cudaMemsetAsync(meta, 0, 16, st) != cudaSuccess)
+        return PION_B200_ECUDA;
+    const int64_t per = (n_rows + ctas - 1) / ctas;
+    const size_t hsm = (size_t)(dim + 1) * 4;
+    if (hsm > 48 * 1024 && set_smem_limit((const void*)bq::bq_scan1_hist_kernel, (int)hsm) != 0)
+        return PION_B200_ECUDA;
+    bq::bq_scan1_hist_kernel<<<ctas, bq::B1_THREADS, hsm, st>>>(codes, n_rows, words, qcode,
+                                                                 per, dist, hist);
+    bq::bq_scan1_collect_kernel<<<ctas, bq::B1_THREADS, 0, st>>>(dist, n_rows, dim, hist, want,
+                                                                  per, keys, ties, meta);
+    const size_t fsm = (size_t)(bq::B1_TIECAP + 512) * 8;
+    if (set_smem_limit((const void*)bq::bq_scan1_finish_kernel, (int)fsm) != 0)
+        return PION_B200_ECUDA;
+    bq::bq_scan1_finish_kernel<<<1, 1024, fsm, st>>>(dist, n_rows, keys, ties, meta, want, S,
+                                                     sl_id, sl_h, sl_n);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
 
 int bq_tile_rows() { return bq::BN; }
 int bq_query_tile() { return bq::BM; }

@@ -654,9 +654,172 @@ __global__ void exact_merge_kernel(const float* __restrict__ chunk_d,
     }
 }
 
+// ------------------------------------------------------------- one query scan
+// exact_knn for ONE query as an HBM stream (COSINE: 1 - dot_f32_4chain(q^, row)).  Four
+// lanes per row; lane j owns chain j of the reference's 4 x 4 accumulators (elements
+// 16 i + 4 j .. 16 i + 4 j + 3), so every step is one 128-bit non-allocating load of the
+// row and one shared-memory load of the query.  A 4 x 4 transpose across the group
+// then gives lane l the l-th lane of every chain, t[l] = (c0 + c1) + (c2 + c3), and the
+// lane sum (t0 + t2) + (t1 + t3): src/vector/fp32_scan.mojo:17-38 in order.
+constexpr int S1_THREADS = 128;
+constexpr int S1_GROUPS = S1_THREADS / 4;  // rows in flight per CTA (one list each)
+constexpr int S1_UNROLL = 12;              // 16-element steps in flight per lane
+constexpr int S1_MAX_DIM = 16384;
+
+__device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float sel4(float a0, float a1, float a2, float a3, int i) {
+    return i == 0 ? a0 : (i == 1 ? a1 : (i == 2 ? a2 : a3));
+}
+
+template <int KCAP>
+__global__ void __launch_bounds__(S1_THREADS)
+    flat_f32_scan1_kernel(const float* __restrict__ rows, int64_t n_rows, int dim,
+                          const float* __restrict__ qn, int k, int64_t rows_per_cta,
+                          float* cand_d, int32_t* cand_i) {
+    extern __shared__ __align__(16) float s1_smem[];
+    float4* qv = reinterpret_cast<float4*>(s1_smem);  // dim / 4
+    float* lv = s1_smem + dim;                        // [S1_GROUPS][KCAP] of -distance
+    int32_t* li = reinterpret_cast<int32_t*>(lv + S1_GROUPS * KCAP);
+    const int steps = dim >> 4;
+    for (int c = threadIdx.x; c < (dim >> 2); c += S1_THREADS)
+        qv[c] = reinterpret_cast<const float4*>(qn)[c];
+    __syncthreads();
+    const int g = threadIdx.x >> 2;
+    const int j = threadIdx.x & 3;
+    const int gbase = (threadIdx.x & 31) & ~3;
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > n_rows) r1 = n_rows;
+    TopKDesc<KCAP> top;  // (-distance desc, id asc) == (distance asc, id asc)
+    top.init();
+    float thr = -INFINITY;
+    // Warp-uniform trip count (rows past r1 are masked), so the full-warp shuffles below
+    // always see all 32 lanes.
+    for (int64_t base = r0; base < r1; base += S1_GROUPS) {
+        const int64_t r = base + g;
+        const bool valid = r < r1;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        if (valid) {
+            const float4* rp = reinterpret_cast<const float4*>(rows + r * dim) + j;
+            for (int i0 = 0; i0 < steps; i0 += S1_UNROLL) {
+                float4 v[S1_UNROLL];
+#pragma unroll
+                for (int u = 0; u < S1_UNROLL; ++u)
+                    if (i0 + u < steps) v[u] = ld_stream_f4(rp + (size_t)(i0 + u) * 4);
+#pragma unroll
+                for (int u = 0; u < S1_UNROLL; ++u)
+                    if (i0 + u < steps) {
+                        const float4 q = qv[(i0 + u) * 4 + j];
+                        a0 = __fadd_rn(__fmul_rn(q.x, v[u].x), a0);
+                        a1 = __fadd_rn(__fmul_rn(q.y, v[u].y), a1);
+                        a2 = __fadd_rn(__fmul_rn(q.z, v[u].z), a2);
+                        a3 = __fadd_rn(__fmul_rn(q.w, v[u].w), a3);
+                    }
+            }
+        }
+        // Transpose: in round x lane j receives lane (j ^ x)'s accumulator j, i.e. lane j
+        // of chain j ^ x; R[x] below holds it (R[0] = own lane j of chain j).
+        const float own = sel4(a0, a1, a2, a3, j);
+        const float r1v = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 1), 1);
+        const float r2v = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 2), 2);
+        const float r3v = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 3), 3);
+        // chain m's lane j arrived in round j ^ m
+        const float c0 = sel4(own, r1v, r2v, r3v, j ^ 0);
+        const float c1 = sel4(own, r1v, r2v, r3v, j ^ 1);
+        const float c2 = sel4(own, r1v, r2v, r3v, j ^ 2);
+        const float c3 = sel4(own, r1v, r2v, r3v, j ^ 3);
+        const float t = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+        const float t0 = __shfl_sync(0xffffffffu, t, gbase + 0);
+        const float t1 = __shfl_sync(0xffffffffu, t, gbase + 1);
+        const float t2 = __shfl_sync(0xffffffffu, t, gbase + 2);
+        const float t3 = __shfl_sync(0xffffffffu, t, gbase + 3);
+        if (valid && j == 0) {
+            const float dot = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+            const float neg = -__fsub_rn(1.0f, dot);
+            if (neg > thr) {
+                top.insert(neg, (int32_t)r);
+                thr = top.kth(k);
+            }
+        }
+    }
+    if (j == 0) {
+#pragma unroll
+        for (int e = 0; e < KCAP; ++e) {
+            lv[g * KCAP + e] = top.v[e];
+            li[g * KCAP + e] = top.i[e];
+        }
+    }
+    __syncthreads();
+    // Warp 0 merges the CTA's S1_GROUPS sorted lists (lane = list) into k.
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int cur = 0;
+        for (int e = 0; e < k; ++e) {
+            float bv = cur < KCAP ? lv[lane * KCAP + cur] : -INFINITY;
+            int32_t bi = cur < KCAP ? li[lane * KCAP + cur] : -1;
+            int bl = lane;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+                if (better_desc(ov, oi, bv, bi) || (ov == bv && oi == bi && ol < bl)) {
+                    bv = ov;
+                    bi = oi;
+                    bl = ol;
+                }
+            }
+            if (lane == bl) ++cur;
+            if (lane == 0) {
+                cand_d[(size_t)blockIdx.x * k + e] = -bv;  // padding: +inf
+                cand_i[(size_t)blockIdx.x * k + e] = bi;
+            }
+        }
+    }
+}
+
 }  // namespace ff32
 
 // =========================================================== host launchers ==
+
+bool ff32_scan1_supported(int dim, int k) {
+    return dim % 16 == 0 && dim <= ff32::S1_MAX_DIM && k >= 1 && k <= 64;
+}
+
+int ff32_scan1_ctas(int64_t n_rows, int num_sms) {
+    int64_t ctas = (int64_t)num_sms * 8;
+    const int64_t min_rows = 2 * ff32::S1_GROUPS;
+    if (ctas * min_rows > n_rows) ctas = (n_rows + min_rows - 1) / min_rows;
+    return (int)(ctas < 1 ? 1 : ctas);
+}
+
+template <int KCAP>
+static int launch_scan1_k(const float* rows, int64_t n_rows, int dim, const float* qn, int k,
+                          int ctas, float* cand_d, int32_t* cand_i, cudaStream_t st) {
+    const size_t smem = (size_t)dim * 4 + (size_t)ff32::S1_GROUPS * KCAP * 8;
+    if (smem > 48 * 1024 &&
+        set_smem_limit((const void*)ff32::flat_f32_scan1_kernel<KCAP>, (int)smem) != 0)
+        return PION_B200_ECUDA;
+    const int64_t per = (n_rows + ctas - 1) / ctas;
+    ff32::flat_f32_scan1_kernel<KCAP><<<ctas, ff32::S1_THREADS, smem, st>>>(rows, n_rows, dim, qn,
+                                                                           k, per, cand_d, cand_i);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_flat_f32_scan1(const float* rows, int64_t n_rows, int dim, const float* qn, int k,
+                          int ctas, float* cand_d, int32_t* cand_i, cudaStream_t st) {
+    if (!ff32_scan1_supported(dim, k) || n_rows <= 0) return PION_B200_ESHAPE;
+    if (k <= 16) return launch_scan1_k<16>(rows, n_rows, dim, qn, k, ctas, cand_d, cand_i, st);
+    if (k <= 32) return launch_scan1_k<32>(rows, n_rows, dim, qn, k, ctas, cand_d, cand_i, st);
+    return launch_scan1_k<64>(rows, n_rows, dim, qn, k, ctas, cand_d, cand_i, st);
+}
 
 int ff32_tile_rows() { return ff32::BN; }
 int ff32_query_tile() { return ff32::BM; }

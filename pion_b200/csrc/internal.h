@@ -69,6 +69,13 @@ int launch_rescore_certify(const float* rows, int dim, const float* qn, const fl
                            float row_norm_max, const float* cand_v, const int32_t* cand_i, int nq,
                            int kc, int k, int64_t id_base, float* out_d, int32_t* out_i,
                            int* flagged, int* n_flagged, int force_exact, cudaStream_t st);
+// exact_knn for one query as an HBM stream: per CTA the k best (distance asc, row asc)
+// of its contiguous row range, [ctas][k] into cand_d / cand_i (rows local, +inf / -1
+// padding); merge them with launch_merge_lists (ascending).
+bool ff32_scan1_supported(int dim, int k);
+int ff32_scan1_ctas(int64_t n_rows, int num_sms);
+int launch_flat_f32_scan1(const float* rows, int64_t n_rows, int dim, const float* qn, int k,
+                          int ctas, float* cand_d, int32_t* cand_i, cudaStream_t st);
 int launch_exact_fallback(const float* rows, int64_t n_rows, int dim, const float* qn,
                           const int* flagged, const int* n_flagged, int nq, int k,
                           int64_t id_base, float* chunk_d, int32_t* chunk_i, float* out_d,
@@ -463,6 +470,15 @@ int launch_bq_select(const int32_t* cid, const uint16_t* ch, const int* cn, int 
 int launch_bq_fallback(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcodes,
                        const int* flagged, const int* n_flagged, int S, int32_t* out_id,
                        uint16_t* out_h, int* out_n, int num_sms, cudaStream_t st);
+// One query's Hamming shortlist as an HBM popcount stream over the packed codes: the S
+// smallest distances by (distance, row), sorted, into sl_id / sl_h / sl_n (three
+// kernels; `scratch` holds bq_scan1_scratch bytes).
+bool bq_scan1_supported(int words, int S);
+int bq_scan1_ctas(int64_t n_rows, int num_sms);
+size_t bq_scan1_scratch(int64_t n_rows, int words);
+int launch_bq_scan1(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcode,
+                    int S, int ctas, void* scratch, int32_t* sl_id, uint16_t* sl_h, int* sl_n,
+                    cudaStream_t st);
 int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t* sl_id,
                      const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
                      int32_t* out_i, cudaStream_t st);

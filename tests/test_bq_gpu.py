@@ -54,3 +54,52 @@ def test_bq_exact_fallback_and_duplicates(ctx, oracle):
         os.environ.pop("PION_B200_BQ_EXACT", None)
     assert np.array_equal(ids2, ids) and np.array_equal(sc2, sc)
     assert ids[0, :3].tolist() == [5, 20000, 29999]
+
+
+@pytest.mark.parametrize("n,dim,S,k,centres", [
+    (200000, 1536, 100, 10, 256),
+    (20000, 512, 256, 1, 32),
+    (3000, 1536, 100, 64, 16),
+    (50, 1536, 100, 10, 4),          # fewer rows than the shortlist
+])
+def test_one_query_popcount_stream(ctx, oracle, n, dim, S, k, centres):
+    """nq = 1 takes the popcount stream over the packed codes (histogram threshold,
+    ties at the S-th distance by row id): shortlist and rerank equal the oracle's."""
+    import pion_b200
+    rows, qs = mixture_np(n, dim, centres, seed=n + S + 1, n_queries=3)
+    ix = pion_b200.BQIndex(ctx, rows)
+    for t in range(qs.shape[0]):
+        ids, sc = ix.search(qs[t:t + 1], k, shortlist=S)
+        check(oracle, rows, qs[t:t + 1], S, k, ids, sc)
+    ix.free()
+
+
+def test_one_query_stream_massive_ties(ctx, oracle):
+    """Most rows share one code, so the S-th distance ties across more rows than the
+    shared-memory sort holds: the ordered scan takes the first ones by id."""
+    import pion_b200
+    rows, qs = mixture_np(30000, 1536, 8, seed=12, n_queries=2)
+    rows[5:25000] = rows[3]
+    rows[25000:25010] *= -1.0
+    ix = pion_b200.BQIndex(ctx, rows)
+    for t in range(2):
+        ids, sc = ix.search(qs[t:t + 1], 10, shortlist=100)
+        check(oracle, rows, qs[t:t + 1], 100, 10, ids, sc)
+    ids, sc = ix.search(rows[3:4], 10, shortlist=100)
+    check(oracle, rows, rows[3:4], 100, 10, ids, sc)
+    ix.free()
+
+
+def test_one_query_stream_equals_tensor_path(ctx, oracle):
+    import pion_b200
+    rows, qs = mixture_np(60000, 1536, 64, seed=8, n_queries=70)
+    ix = pion_b200.BQIndex(ctx, rows)
+    want_i, want_s = ix.search(qs, 10)
+    os.environ["PION_B200_BQ_PATH"] = "1"
+    try:
+        got_i, got_s = ix.search(qs, 10)
+    finally:
+        os.environ.pop("PION_B200_BQ_PATH", None)
+    assert np.array_equal(got_i, want_i)
+    assert np.array_equal(got_s.view(np.uint32), want_s.view(np.uint32))
+    ix.free()

@@ -147,3 +147,42 @@ def test_merge_delta_matches_oracle(ctx, oracle, cosine):
     oi2, os2 = ix.merge_delta(qs, n, ids.copy(), scores.copy(), k, cosine=cosine)
     w2 = oracle.merge_delta(stored, n, cosine, qs, ids, scores, k)
     assert np.array_equal(oi2, w2[2]) and np.array_equal(os2, w2[3])
+
+
+@pytest.mark.parametrize("n,dim,k,centres", [
+    (100000, 1536, 10, 256),   # the FLAT FP32 configuration, one query at a time
+    (30011, 1536, 64, 64),     # ragged last CTA, the 64-entry lists
+    (4099, 512, 33, 16),
+    (100, 1536, 10, 4),        # fewer rows than one CTA's rows in flight
+    (7, 1536, 10, 2),          # fewer rows than k
+])
+def test_one_query_stream_matches_oracle(ctx, oracle, n, dim, k, centres):
+    """nq = 1 takes the exact HBM stream (4 lanes per row, the 4-chain order restated
+    across the group): distances bit-identical, ids as exact_knn's."""
+    import pion_b200
+    rows, qs = mixture_np(n, dim, centres, seed=n + 3 * k, n_queries=4)
+    rows[n // 2] = rows[n // 3]        # duplicate rows: ties broken by id
+    qs[1] = rows[n // 3] * 7.0
+    ix = pion_b200.FlatF32Index(ctx, rows)
+    rn = oracle.l2_normalize_rows(rows)
+    for t in range(qs.shape[0]):
+        ids, dist = ix.search(qs[t:t + 1] * 2.0, k)
+        assert_f32_matches(oracle, rn, qs[t:t + 1] * 2.0, k, ids, dist)
+    ix.free()
+
+
+def test_one_query_stream_equals_tensor_path(ctx, oracle):
+    """The stream forced for a whole batch returns what the tensor-core shortlist plus
+    certified rescore returns, bit for bit, ids included (both order by (distance, id))."""
+    import pion_b200
+    rows, qs = mixture_np(60000, 1536, 128, seed=41, n_queries=96)
+    ix = pion_b200.FlatF32Index(ctx, rows)
+    want_i, want_d = ix.search(qs, 10)
+    os.environ["PION_B200_F32_PATH"] = "1"
+    try:
+        got_i, got_d = ix.search(qs, 10)
+    finally:
+        os.environ.pop("PION_B200_F32_PATH", None)
+    assert np.array_equal(got_i, want_i)
+    assert np.array_equal(got_d.view(np.uint32), want_d.view(np.uint32))
+    ix.free()
