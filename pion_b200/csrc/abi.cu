@@ -254,8 +254,9 @@ int pion_v_b200_shutdown(pion_b200_ctx* ctx) {
     if (!ctx) return PION_B200_EINVAL;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    DevBuf* bufs[] = {&ctx->scratch,   &ctx->scratch2,     &ctx->stage_in,
-                      &ctx->stage_out, &ctx->hnsw_visited, &ctx->hnsw_misc};
+    DevBuf* bufs[] = {&ctx->scratch,      &ctx->scratch2,     &ctx->stage_in,
+                      &ctx->stage_out,    &ctx->hnsw_visited, &ctx->hnsw_misc,
+                      &ctx->hnsw_touched};
     for (DevBuf* b : bufs)
         if (b->ptr) cudaFree(b->ptr);
     if (ctx->d_status) cudaFree(ctx->d_status);

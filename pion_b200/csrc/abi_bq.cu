@@ -173,7 +173,7 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
         const size_t o_qn = take((size_t)nq * dim * 4), o_qnorm = take((size_t)nq * 4),
                      o_qpm = take((size_t)nq * dim), o_qc = take((size_t)nq * words * 8),
                      o_slid = take((size_t)nq * S * 4), o_slh = take((size_t)nq * S * 2),
-                     o_sln = take((size_t)nq * 4),
+                     o_sln = take((size_t)nq * 4), o_rd = take((size_t)nq * S * 4),
                      o_work = take(bq_scan1_scratch(ix->n_rows, words));
         if (ensure(ctx->scratch, off) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "bq_rerank_knn: scratch");
@@ -196,9 +196,14 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
         }
         timing_end(ctx, t_all);
         if (rc == 0) {
-            rc = launch_bq_rerank(ix->rows_f32, dim, qn, sl_id, sl_n, S, nqi, kk, ix->id_base, dv,
-                                  di, st);
-            ctx->launches++;
+            if (dim % 16 == 0)
+                rc = launch_bq_rerank_wide(ix->rows_f32, dim, qn, sl_id, sl_n, S, nqi, kk,
+                                           ix->id_base, reinterpret_cast<float*>(base + o_rd),
+                                           dv, di, st);
+            else
+                rc = launch_bq_rerank(ix->rows_f32, dim, qn, sl_id, sl_n, S, nqi, kk, ix->id_base,
+                                      dv, di, st);
+            ctx->launches += 2;
         }
     } else {
         const int n_qt = (nqi + bq_query_tile() - 1) / bq_query_tile();

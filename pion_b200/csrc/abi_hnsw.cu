@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -380,8 +381,8 @@ int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         int64_t ctas = (int64_t)per_sm * ctx->num_sms;
         const int64_t need = (nq + warps - 1) / warps;
         if (ctas > need) ctas = need;
-        const int64_t vis_words = ((ix->n_rows + 31) / 32 + 3) / 4 * 4;
-        if (ensure(ctx->hnsw_visited, (size_t)ctas * warps * vis_words * 4) != 0)
+        HnswLaunch Lc;
+        if (hnsw_visit_buffers(ctx, ctas * warps, ix->n_rows, Lc) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "hnsw_search: visited bitmaps");
         size_t off = 0;
         auto take = [&](size_t bytes) {
@@ -412,7 +413,6 @@ int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         if (!rc) rc = launch_hnsw_quantize(qsrc, (int)nq, h.gmin, scale, codes, blk, st);
         ctx->launches++;
         if (!rc) {
-            HnswLaunch Lc;
             Lc.codes = h.codes;
             Lc.norms = h.norms;
             Lc.l0_compact = h.l0_compact;
@@ -433,8 +433,6 @@ int pion_v_b200_hnsw_search(pion_b200_ctx* ctx, const pion_b200_index* ix, const
             Lc.nq = (int)nq;
             Lc.k = (int)k;
             Lc.ef = (int)ef;
-            Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
-            Lc.vis_words = vis_words;
             Lc.out_ids = di;
             Lc.out_dist = dv;
             Lc.stats = stats;
@@ -531,13 +529,12 @@ int pion_v_b200_hnsw_beam_batch(pion_b200_ctx* ctx, const pion_b200_index* ix,
     int64_t ctas = (int64_t)per_sm * ctx->num_sms;
     const int64_t need = (nq + warps - 1) / warps;
     if (ctas > need) ctas = need;
-    const int64_t vis_words = ((ix->n_rows + 31) / 32 + 3) / 4 * 4;
-    if (ensure(ctx->hnsw_visited, (size_t)ctas * warps * vis_words * 4) != 0)
+    HnswLaunch Lc;
+    if (hnsw_visit_buffers(ctx, ctas * warps, ix->n_rows, Lc) != 0)
         return set_error(ctx, PION_B200_ENOMEM, "hnsw_beam_batch: visited bitmaps");
     unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
     if (cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 32, st) != cudaSuccess)
         return set_error(ctx, PION_B200_ECUDA, "hnsw_beam_batch: memset failed");
-    HnswLaunch Lc;
     Lc.codes = h.codes;
     Lc.norms = h.norms;
     Lc.l0_compact = h.l0_compact;
@@ -558,8 +555,6 @@ int pion_v_b200_hnsw_beam_batch(pion_b200_ctx* ctx, const pion_b200_index* ix,
     Lc.nq = (int)nq;
     Lc.k = 0;
     Lc.ef = (int)ef;
-    Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
-    Lc.vis_words = vis_words;
     Lc.stats = stats;
     Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
     Lc.status = call_status(ctx, mem);
@@ -667,6 +662,44 @@ int pion_v_b200_hnsw_last_stats(pion_b200_ctx* ctx, int64_t* out3) {
     for (int i = 0; i < 3; ++i) out3[i] = (int64_t)v[i];
     return 0;
 }
+
+}  // extern "C"
+
+// ------------------------------------------------------ visited bitmaps
+
+// Per resident warp: the touched-word list of the beam kernel (words a query turned
+// non-zero, zeroed again when it ends).  16,384 entries cover ~500K visited nodes'
+// words; a query past that zeroes its whole bitmap.
+constexpr int kTouchCap = 16384;
+
+int pion::hnsw_visit_buffers(pion_b200_ctx* ctx, int64_t warps, int64_t num_nodes,
+                             HnswLaunch& L) {
+    const int64_t vis_words = ((num_nodes + 31) / 32 + 3) / 4 * 4;
+    void* before = ctx->hnsw_visited.ptr;
+    if (ensure(ctx->hnsw_visited, (size_t)warps * vis_words * 4) != 0 ||
+        ensure(ctx->hnsw_touched, (size_t)warps * kTouchCap * 4) != 0)
+        return PION_B200_ENOMEM;
+    if (ctx->hnsw_visited.ptr != before || !ctx->vis_clean) {
+        // new memory, or left non-zero by another kernel: zero it once; the beam kernel
+        // leaves it zero after every query
+        if (cudaMemsetAsync(ctx->hnsw_visited.ptr, 0, ctx->hnsw_visited.bytes, ctx->stream) !=
+            cudaSuccess)
+            return PION_B200_ECUDA;
+        ctx->vis_clean = true;
+    }
+    L.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+    L.vis_words = vis_words;
+    L.touched = static_cast<uint32_t*>(ctx->hnsw_touched.ptr);
+    L.touch_cap = kTouchCap;
+    // test hook: a smaller list, so that queries overflow it and zero their whole bitmap
+    if (const char* e = getenv("PION_B200_TOUCH_CAP")) {
+        const int c = atoi(e);
+        if (c >= 32 && c < kTouchCap) L.touch_cap = c;
+    }
+    return 0;
+}
+
+extern "C" {
 
 // ------------------------------------------------- pion_v_beam_1536 (compat)
 
@@ -810,12 +843,11 @@ int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
         cudaMemsetAsync(ctx->hnsw_misc.ptr, 0, 32, st) != cudaSuccess)
         return beam_fail("copy to the device failed");
     const int warps = hnsw_warps_per_cta();
-    const int64_t vis_words = ((v->num_nodes + 31) / 32 + 3) / 4 * 4;
-    if (ensure(ctx->hnsw_visited, (size_t)warps * vis_words * 4) != 0)
+    HnswLaunch Lc;
+    if (hnsw_visit_buffers(ctx, warps, v->num_nodes, Lc) != 0)
         return beam_fail("out of device memory");
     if (hnsw_ctas_per_sm((int)ef) <= 0) return beam_fail("ef does not fit");
     unsigned long long* stats = static_cast<unsigned long long*>(ctx->hnsw_misc.ptr);
-    HnswLaunch Lc;
     Lc.codes = g->codes;
     Lc.norms = g->norms;
     Lc.l0_compact = g->l0_compact;
@@ -827,8 +859,6 @@ int64_t pion_v_beam_1536(pion_beam_view_1536* v) {
     Lc.nq = 1;
     Lc.k = 0;
     Lc.ef = (int)ef;
-    Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
-    Lc.vis_words = vis_words;
     Lc.stats = stats;
     Lc.next_query = reinterpret_cast<unsigned*>(stats + 3);
     Lc.status = call_status(ctx, PION_B200_MEM_HOST);

@@ -323,6 +323,7 @@ int64_t pion_v_quant_beam_1536(pion_quant_beam_view_1536* v) {
     Lc.k = 1;
     Lc.ef = (int)ef;
     Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+    ctx->vis_clean = false;  // this kernel leaves its bitmaps set
     Lc.vis_words = vis_words;
     Lc.cand_tail = ctx->scratch2.ptr;
     Lc.cand_cap = cap;
@@ -698,6 +699,7 @@ int pion_v_b200_hnsw_quant_search(pion_b200_ctx* ctx, const pion_b200_index* ix,
         Lc.k = (int)k;
         Lc.ef = (int)ef;
         Lc.visited = static_cast<uint32_t*>(ctx->hnsw_visited.ptr);
+    ctx->vis_clean = false;  // this kernel leaves its bitmaps set
         Lc.vis_words = vis_words;
         Lc.cand_tail = ctx->scratch2.ptr;
         Lc.cand_cap = cap1;

@@ -542,6 +542,8 @@ constexpr int B1_THREADS = 256;
 constexpr int B1_GROUPS = B1_THREADS / 4;
 constexpr int B1_MAX_WORDS = 256;   // dim <= 16384
 constexpr int B1_TIECAP = 8192;     // ties at D* sorted in shared memory; more: ordered scan
+constexpr int B1_RPI = 4;           // rows per group per iteration
+constexpr int B1_CPL = 3;           // 16-byte chunks per lane held in registers (<= 1536 dims)
 
 __device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
     uint4 v;
@@ -569,24 +571,57 @@ __global__ void __launch_bounds__(B1_THREADS)
     const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
     int64_t r1 = r0 + rows_per_cta;
     if (r1 > n_rows) r1 = n_rows;
-    for (int64_t base = r0; base < r1; base += B1_GROUPS) {
-        const int64_t r = base + g;
-        int h = 0;
-        if (r < r1) {
-            const uint4* rp = reinterpret_cast<const uint4*>(codes + r * words);
-#pragma unroll 4
-            for (int c = j; c < chunks; c += 4) {
-                const uint4 a = ld_stream_u4(rp + c);
-                const uint4 b = qv[c];
-                h += __popc(a.x ^ b.x) + __popc(a.y ^ b.y) + __popc(a.z ^ b.z) +
-                     __popc(a.w ^ b.w);
+    // B1_RPI rows per group per iteration, every chunk load of all of them issued before
+    // the first popcount (up to 12 loads in flight per lane at 1536 dims)
+    for (int64_t base = r0; base < r1; base += (int64_t)B1_GROUPS * B1_RPI) {
+        int h[B1_RPI];
+#pragma unroll
+        for (int u = 0; u < B1_RPI; ++u) h[u] = 0;
+        if (chunks <= 4 * B1_CPL) {
+            uint4 a[B1_RPI][B1_CPL];
+#pragma unroll
+            for (int u = 0; u < B1_RPI; ++u) {
+                const int64_t r = base + (int64_t)u * B1_GROUPS + g;
+                const uint4* rp = reinterpret_cast<const uint4*>(codes + r * words);
+#pragma unroll
+                for (int i = 0; i < B1_CPL; ++i)
+                    if (r < r1 && j + 4 * i < chunks) a[u][i] = ld_stream_u4(rp + j + 4 * i);
+            }
+#pragma unroll
+            for (int u = 0; u < B1_RPI; ++u) {
+                const int64_t r = base + (int64_t)u * B1_GROUPS + g;
+#pragma unroll
+                for (int i = 0; i < B1_CPL; ++i)
+                    if (r < r1 && j + 4 * i < chunks) {
+                        const uint4 b = qv[j + 4 * i];
+                        h[u] += __popc(a[u][i].x ^ b.x) + __popc(a[u][i].y ^ b.y) +
+                                __popc(a[u][i].z ^ b.z) + __popc(a[u][i].w ^ b.w);
+                    }
+            }
+        } else {  // long codes: one row at a time
+#pragma unroll 1
+            for (int u = 0; u < B1_RPI; ++u) {
+                const int64_t r = base + (int64_t)u * B1_GROUPS + g;
+                if (r >= r1) continue;
+                const uint4* rp = reinterpret_cast<const uint4*>(codes + r * words);
+                for (int c = j; c < chunks; c += 4) {
+                    const uint4 a = ld_stream_u4(rp + c);
+                    const uint4 b = qv[c];
+                    h[u] += __popc(a.x ^ b.x) + __popc(a.y ^ b.y) + __popc(a.z ^ b.z) +
+                            __popc(a.w ^ b.w);
+                }
             }
         }
-        h += __shfl_xor_sync(0xffffffffu, h, 1);
-        h += __shfl_xor_sync(0xffffffffu, h, 2);
-        if (r < r1 && j == 0) {
-            dist[r] = (uint16_t)h;
-            atomicAdd(&b1_hist[h], 1);
+#pragma unroll
+        for (int u = 0; u < B1_RPI; ++u) {
+            const int64_t r = base + (int64_t)u * B1_GROUPS + g;
+            int hu = h[u];
+            hu += __shfl_xor_sync(0xffffffffu, hu, 1);
+            hu += __shfl_xor_sync(0xffffffffu, hu, 2);
+            if (r < r1 && j == 0) {
+                dist[r] = (uint16_t)hu;
+                atomicAdd(&b1_hist[hu], 1);
+            }
         }
     }
     __syncthreads();
@@ -708,6 +743,68 @@ __global__ void __launch_bounds__(1024)
     if (threadIdx.x == 0) *out_n = want;
 }
 
+// Rerank for few queries: the shortlist rows spread over many CTAs, 4 lanes per row
+// (dot4chain_quad: the 4-chain order with 128-bit loads), distances to `dist`; then a
+// warp per query picks the k best by (distance, shortlist position) exactly as the
+// tail of bq_rerank_kernel does.
+constexpr int RW_THREADS = 128;
+constexpr int RW_ROWS = RW_THREADS / 4;
+
+__global__ void __launch_bounds__(RW_THREADS)
+    bq_rerank_rows_kernel(const float* __restrict__ rows, int dim, const float* __restrict__ qn,
+                          const int32_t* __restrict__ sl_id, const int* __restrict__ sl_n, int S,
+                          float* __restrict__ dist) {
+    extern __shared__ float4 rw_q[];  // dim / 4
+    const int q = blockIdx.y;
+    for (int c = threadIdx.x; c < (dim >> 2); c += RW_THREADS)
+        rw_q[c] = reinterpret_cast<const float4*>(qn + (size_t)q * dim)[c];
+    __syncthreads();
+    const int jj = blockIdx.x * RW_ROWS + (threadIdx.x >> 2);
+    const bool valid = jj < sl_n[q];
+    const float* row = valid ? rows + (size_t)sl_id[(size_t)q * S + jj] * dim : nullptr;
+    const float dot = dot4chain_quad<12>(rw_q, row, dim);
+    if (valid && (threadIdx.x & 3) == 0) dist[(size_t)q * S + jj] = __fsub_rn(1.0f, dot);
+}
+
+__global__ void __launch_bounds__(128)
+    bq_rerank_pick_kernel(const float* __restrict__ dist_in, const int32_t* __restrict__ sl_id,
+                          const int* __restrict__ sl_n, int S, int nq, int k, int64_t id_base,
+                          float* __restrict__ out_d, int32_t* __restrict__ out_i) {
+    __shared__ float dist_all[4][256];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 4 + w;
+    if (q >= nq) return;
+    float* dist = dist_all[w];
+    const int n = sl_n[q];
+    for (int j = lane; j < n; j += 32) dist[j] = dist_in[(size_t)q * S + j];
+    __syncwarp();
+    for (int r = 0; r < k; ++r) {
+        float bd = INFINITY;
+        int bp = -1;
+        for (int j = lane; j < n; j += 32)
+            if (dist[j] == dist[j] && (bp < 0 || dist[j] < bd)) {  // first (lowest j) wins ties
+                bd = dist[j];
+                bp = j;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float od = __shfl_xor_sync(0xffffffffu, bd, o);
+            const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+            if (op >= 0 && (bp < 0 || od < bd || (od == bd && op < bp))) {
+                bd = od;
+                bp = op;
+            }
+        }
+        if (lane == 0) {
+            out_d[(size_t)q * k + r] = bp >= 0 ? bd : INFINITY;
+            out_i[(size_t)q * k + r] =
+                bp >= 0 ? (int32_t)(sl_id[(size_t)q * S + bp] + id_base) : -1;
+        }
+        if (bp >= 0 && lane == (bp & 31)) dist[bp] = __int_as_float(0x7fffffff);  // taken (NaN)
+        __syncwarp();
+    }
+}
+
 }  // namespace bq
 
 // =========================================================== host launchers ==
@@ -820,6 +917,19 @@ int launch_bq_fallback(const uint64_t* codes, int64_t n_rows, int words, const u
                        uint16_t* out_h, int* out_n, int num_sms, cudaStream_t st) {
     bq::bq_fallback_kernel<<<num_sms, bq::SEL_THREADS, (size_t)(words * 64 + 1) * 4, st>>>(
         codes, n_rows, words, qcodes, flagged, n_flagged, S, out_id, out_h, out_n);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_bq_rerank_wide(const float* rows, int dim, const float* qn, const int32_t* sl_id,
+                          const int* sl_n, int S, int nq, int k, int64_t id_base, float* dist,
+                          float* out_d, int32_t* out_i, cudaStream_t st) {
+    if (nq <= 0) return 0;
+    if (dim % 16 != 0 || S > 256 || (size_t)dim * 4 > 48 * 1024) return PION_B200_ESHAPE;
+    dim3 grid((S + bq::RW_ROWS - 1) / bq::RW_ROWS, nq);
+    bq::bq_rerank_rows_kernel<<<grid, bq::RW_THREADS, (size_t)dim * 4, st>>>(rows, dim, qn, sl_id,
+                                                                            sl_n, S, dist);
+    bq::bq_rerank_pick_kernel<<<(nq + 3) / 4, 128, 0, st>>>(dist, sl_id, sl_n, S, nq, k, id_base,
+                                                            out_d, out_i);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

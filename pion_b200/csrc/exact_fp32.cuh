@@ -84,6 +84,69 @@ __device__ __forceinline__ void prefetch_row_f32_l2(const float* row, int dim) {
                  : "memory");
 }
 
+__device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float sel4(float a0, float a1, float a2, float a3, int i) {
+    return i == 0 ? a0 : (i == 1 ? a1 : (i == 2 ? a2 : a3));
+}
+
+// dot_f32_4chain over `dim` (a multiple of 16) floats by a group of 4 consecutive lanes:
+// lane j (= lane & 3) owns chain j of the reference's 4 x 4 accumulators, i.e. elements
+// 16 i + 4 j .. 16 i + 4 j + 3, read with 128-bit non-allocating loads (`row` may be
+// null for a masked group: zero accumulators); q4 holds the query as float4 (shared
+// memory).  A 4 x 4 transpose then gives lane l the l-th lane of every chain,
+// t[l] = (c0 + c1) + (c2 + c3), and the lane sum (t0 + t2) + (t1 + t3) returned to all
+// four lanes: src/vector/fp32_scan.mojo:17-38 in order.  Every lane of the warp must
+// call it (full-warp shuffles).
+template <int UNROLL>
+__device__ __forceinline__ float dot4chain_quad(const float4* __restrict__ q4,
+                                                const float* __restrict__ row, int dim) {
+    const int j = threadIdx.x & 3;
+    const int gbase = (threadIdx.x & 31) & ~3;
+    const int steps = dim >> 4;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    if (row) {
+        const float4* rp = reinterpret_cast<const float4*>(row) + j;
+        for (int i0 = 0; i0 < steps; i0 += UNROLL) {
+            float4 v[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u)
+                if (i0 + u < steps) v[u] = ld_stream_f4(rp + (size_t)(i0 + u) * 4);
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u)
+                if (i0 + u < steps) {
+                    const float4 q = q4[(i0 + u) * 4 + j];
+                    a0 = __fadd_rn(__fmul_rn(q.x, v[u].x), a0);
+                    a1 = __fadd_rn(__fmul_rn(q.y, v[u].y), a1);
+                    a2 = __fadd_rn(__fmul_rn(q.z, v[u].z), a2);
+                    a3 = __fadd_rn(__fmul_rn(q.w, v[u].w), a3);
+                }
+        }
+    }
+    // round x: lane j receives lane (j ^ x)'s accumulator j = lane j of chain j ^ x
+    const float own = sel4(a0, a1, a2, a3, j);
+    const float r1 = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 1), 1);
+    const float r2 = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 2), 2);
+    const float r3 = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 3), 3);
+    // chain m's lane j arrived in round j ^ m
+    const float c0 = sel4(own, r1, r2, r3, j ^ 0);
+    const float c1 = sel4(own, r1, r2, r3, j ^ 1);
+    const float c2 = sel4(own, r1, r2, r3, j ^ 2);
+    const float c3 = sel4(own, r1, r2, r3, j ^ 3);
+    const float t = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+    const float t0 = __shfl_sync(0xffffffffu, t, gbase + 0);
+    const float t1 = __shfl_sync(0xffffffffu, t, gbase + 1);
+    const float t2 = __shfl_sync(0xffffffffu, t, gbase + 2);
+    const float t3 = __shfl_sync(0xffffffffu, t, gbase + 3);
+    return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+}
+
 // (distance asc, id asc)
 __device__ __forceinline__ bool better_asc(float da, int32_t ia, float db, int32_t ib) {
     if (da != db) return da < db;

@@ -336,6 +336,9 @@ __global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int 
     if (threadIdx.x < nr) {
         const float* x = qsm + threadIdx.x * pitch;
         float ss = 0.0f;
+        // unrolled so the shared-memory loads and products run ahead of the (sequential)
+        // addition chain
+#pragma unroll 16
         for (int d = 0; d < dim; ++d) ss = __fadd_rn(ss, __fmul_rn(x[d], x[d]));
         inv_s[threadIdx.x] = ss > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
     }
@@ -666,18 +669,6 @@ constexpr int S1_GROUPS = S1_THREADS / 4;  // rows in flight per CTA (one list e
 constexpr int S1_UNROLL = 12;              // 16-element steps in flight per lane
 constexpr int S1_MAX_DIM = 16384;
 
-__device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
-    float4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ float sel4(float a0, float a1, float a2, float a3, int i) {
-    return i == 0 ? a0 : (i == 1 ? a1 : (i == 2 ? a2 : a3));
-}
-
 template <int KCAP>
 __global__ void __launch_bounds__(S1_THREADS)
     flat_f32_scan1_kernel(const float* __restrict__ rows, int64_t n_rows, int dim,
@@ -687,61 +678,24 @@ __global__ void __launch_bounds__(S1_THREADS)
     float4* qv = reinterpret_cast<float4*>(s1_smem);  // dim / 4
     float* lv = s1_smem + dim;                        // [S1_GROUPS][KCAP] of -distance
     int32_t* li = reinterpret_cast<int32_t*>(lv + S1_GROUPS * KCAP);
-    const int steps = dim >> 4;
     for (int c = threadIdx.x; c < (dim >> 2); c += S1_THREADS)
         qv[c] = reinterpret_cast<const float4*>(qn)[c];
     __syncthreads();
     const int g = threadIdx.x >> 2;
     const int j = threadIdx.x & 3;
-    const int gbase = (threadIdx.x & 31) & ~3;
     const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
     int64_t r1 = r0 + rows_per_cta;
     if (r1 > n_rows) r1 = n_rows;
     TopKDesc<KCAP> top;  // (-distance desc, id asc) == (distance asc, id asc)
     top.init();
     float thr = -INFINITY;
-    // Warp-uniform trip count (rows past r1 are masked), so the full-warp shuffles below
-    // always see all 32 lanes.
+    // Warp-uniform trip count (rows past r1 are masked), so the full-warp shuffles of
+    // dot4chain_quad always see all 32 lanes.
     for (int64_t base = r0; base < r1; base += S1_GROUPS) {
         const int64_t r = base + g;
         const bool valid = r < r1;
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-        if (valid) {
-            const float4* rp = reinterpret_cast<const float4*>(rows + r * dim) + j;
-            for (int i0 = 0; i0 < steps; i0 += S1_UNROLL) {
-                float4 v[S1_UNROLL];
-#pragma unroll
-                for (int u = 0; u < S1_UNROLL; ++u)
-                    if (i0 + u < steps) v[u] = ld_stream_f4(rp + (size_t)(i0 + u) * 4);
-#pragma unroll
-                for (int u = 0; u < S1_UNROLL; ++u)
-                    if (i0 + u < steps) {
-                        const float4 q = qv[(i0 + u) * 4 + j];
-                        a0 = __fadd_rn(__fmul_rn(q.x, v[u].x), a0);
-                        a1 = __fadd_rn(__fmul_rn(q.y, v[u].y), a1);
-                        a2 = __fadd_rn(__fmul_rn(q.z, v[u].z), a2);
-                        a3 = __fadd_rn(__fmul_rn(q.w, v[u].w), a3);
-                    }
-            }
-        }
-        // Transpose: in round x lane j receives lane (j ^ x)'s accumulator j, i.e. lane j
-        // of chain j ^ x; R[x] below holds it (R[0] = own lane j of chain j).
-        const float own = sel4(a0, a1, a2, a3, j);
-        const float r1v = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 1), 1);
-        const float r2v = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 2), 2);
-        const float r3v = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 3), 3);
-        // chain m's lane j arrived in round j ^ m
-        const float c0 = sel4(own, r1v, r2v, r3v, j ^ 0);
-        const float c1 = sel4(own, r1v, r2v, r3v, j ^ 1);
-        const float c2 = sel4(own, r1v, r2v, r3v, j ^ 2);
-        const float c3 = sel4(own, r1v, r2v, r3v, j ^ 3);
-        const float t = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
-        const float t0 = __shfl_sync(0xffffffffu, t, gbase + 0);
-        const float t1 = __shfl_sync(0xffffffffu, t, gbase + 1);
-        const float t2 = __shfl_sync(0xffffffffu, t, gbase + 2);
-        const float t3 = __shfl_sync(0xffffffffu, t, gbase + 3);
+        const float dot = dot4chain_quad<S1_UNROLL>(qv, valid ? rows + r * dim : nullptr, dim);
         if (valid && j == 0) {
-            const float dot = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
             const float neg = -__fsub_rn(1.0f, dot);
             if (neg > thr) {
                 top.insert(neg, (int32_t)r);

@@ -37,8 +37,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
 constexpr uint32_t IDESC = make_idesc_i8(BM, BN);
 constexpr size_t SMEM_PIPE_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
-// per epilogue warp: one 32 x 32 chunk of dots and the 32 row scales of its columns
-constexpr size_t STASH_BYTES = 32 * 32 * 4 + 32 * 4;
+// per epilogue warp: a 32-value row per lane for the candidate path
+constexpr size_t STASH_BYTES = 32 * 32 * 4;
 __host__ __device__ constexpr size_t smem_bytes(int epi_warps) {
     return SMEM_PIPE_BYTES + (size_t)epi_warps * STASH_BYTES;
 }
@@ -109,45 +109,59 @@ struct QueryTop {
 };
 
 // One 32-column chunk of TMEM accumulators: integer pre-filter into a candidate
-// mask, then the exact reference score for the (rare) candidates, ascending columns.
-// When any lane of the warp has a candidate, the warp parks the chunk in its shared
-// `stash` (column-major [32][32], conflict-free) so that candidates are read by index
-// instead of selected out of registers.
+// mask, then the exact reference score for the candidates, ascending columns.
+// Candidates are common on clustered data (a lane has one in a few percent of the
+// chunks, so most chunks have some lane with one), so this path is lane-local: a lane
+// with candidates parks its own 32 values in its own row of `stash` (eight 16-byte
+// stores, slots XOR-swizzled by lane so a quarter-warp's stores hit distinct banks)
+// and reads them back by index; the row scale comes from L1 (the tile's scales were
+// just loaded).  No warp synchronisation: lanes without candidates go on at once.
 template <int KCAP>
 __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], int64_t col0, int64_t valid,
-                                           float rs_lane, float qs, float inv, int k,
-                                           uint32_t* stash, float* stash_rs, int lane,
+                                           const float* __restrict__ row_scale, float qs,
+                                           float inv, int k, uint32_t* stash, int lane,
                                            QueryTop<KCAP>& st) {
     // Common case first: one max-reduction says whether any column can qualify.
     int32_t mx = (int32_t)r[0];
 #pragma unroll
     for (int j = 1; j < 32; ++j) mx = max(mx, (int32_t)r[j]);
-    uint32_t mask = 0;
-    if (mx > st.dmin) {
+    if (!(mx > st.dmin)) return;
+    uint32_t mask;
+    if (st.dmin == INT32_MIN) {
+        mask = 0xffffffffu;
+    } else {
+        // bit j = (r[j] > dmin) = sign of dmin - r[j] (|r| < 2^25 and dmin < 2^31 - 2^25:
+        // no overflow), shifted in by two independent funnel-shift chains
+        uint32_t lo = 0, hi = 0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mask |= ((int32_t)r[j] > st.dmin ? 1u : 0u) << j;
-        if (valid < 32) mask &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+        for (int j = 15; j >= 0; --j) {
+            lo = __funnelshift_l((uint32_t)(st.dmin - (int32_t)r[j]), lo, 1);
+            hi = __funnelshift_l((uint32_t)(st.dmin - (int32_t)r[j + 16]), hi, 1);
+        }
+        mask = lo | (hi << 16);
     }
-    if (!__any_sync(0xffffffffu, mask != 0u)) return;
+    if (valid < 32) mask &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+    if (!mask) return;
+    uint4* row4 = reinterpret_cast<uint4*>(stash + lane * 32);
+    const int sw = lane & 7;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) stash[j * 32 + lane] = r[j];
-    stash_rs[lane] = rs_lane;  // lane j brought the row scale of column j
-    __syncwarp();
+    for (int i = 0; i < 8; ++i)
+        row4[i ^ sw] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+    const uint32_t* row = stash + lane * 32;
 #pragma unroll 1
     while (mask) {
         const int j = __ffs(mask) - 1;
         mask &= mask - 1u;
-        const int32_t dv = (int32_t)stash[j * 32 + lane];
+        const int32_t dv = (int32_t)row[(((j >> 2) ^ sw) << 2) | (j & 3)];
         if (dv <= st.dmin) continue;
         const int64_t col = col0 + j;
-        const float s = i8_score(dv, stash_rs[j], qs);
+        const float s = i8_score(dv, __ldg(&row_scale[col]), qs);
         if (s > st.thr) {
             st.top.insert(s, (int32_t)col);
             st.thr = fmaxf(st.top.kth(k), st.floor_thr);
             st.dmin = dot_bound(st.thr, inv);
         }
     }
-    __syncwarp();  // the stash is rewritten by the next chunk
 }
 
 // Threshold pass: one exact score per 32-column chunk, that of the chunk's largest dot
@@ -183,13 +197,14 @@ __device__ __forceinline__ void bound_chunk(const uint32_t (&r)[32], int64_t col
 
 template <int KCAP>
 __device__ __forceinline__ void process_chunk(bool bound, const uint32_t (&r)[32], int64_t col0,
-                                              int64_t valid, float rs_lane, float qs, float inv,
-                                              int k, uint32_t* stash, float* stash_rs, int lane,
+                                              int64_t valid, float rs_lane,
+                                              const float* __restrict__ row_scale, float qs,
+                                              float inv, int k, uint32_t* stash, int lane,
                                               QueryTop<KCAP>& st) {
     if (bound)
         bound_chunk<KCAP>(r, col0, valid, rs_lane, qs, inv, k, st);
     else
-        scan_chunk<KCAP>(r, col0, valid, rs_lane, qs, inv, k, stash, stash_rs, lane, st);
+        scan_chunk<KCAP>(r, col0, valid, row_scale, qs, inv, k, stash, lane, st);
 }
 
 template <int KCAP, int EPI_WARPS>
@@ -328,7 +343,6 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
         // --------------------------------------------- epilogue: score + top-k
         const int ew = warp - 2;
         uint32_t* stash = stash_all + ew * (STASH_BYTES / 4);
-        float* stash_rs = reinterpret_cast<float*>(stash + 32 * 32);
         const int lg = warp & 3;  // TMEM lane quarter this warp may read
         const int half = ew >> 2; // column slice of each tile
         const int row = lg * 32 + lane;
@@ -378,14 +392,14 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
                     __syncwarp();
                     tmem_ld32(taddr + (uint32_t)((c + 1) * 32), rb);
                     process_chunk<KCAP>(bound, ra, col0 + c * 32, valid - c * 32,
-                                        sel_rs<CHUNKS>(rsv, c), qs, inv, p.k, stash, stash_rs,
-                                        lane, st);
+                                        sel_rs<CHUNKS>(rsv, c), p.row_scale, qs, inv, p.k,
+                                        stash, lane, st);
                     __syncwarp();
                     tmem_ld_wait_regs(rb);
                     if (c + 2 < CHUNKS) tmem_ld32(taddr + (uint32_t)((c + 2) * 32), ra);
                     process_chunk<KCAP>(bound, rb, col0 + (c + 1) * 32, valid - (c + 1) * 32,
-                                        sel_rs<CHUNKS>(rsv, c + 1), qs, inv, p.k, stash,
-                                        stash_rs, lane, st);
+                                        sel_rs<CHUNKS>(rsv, c + 1), p.row_scale, qs, inv,
+                                        p.k, stash, lane, st);
                     __syncwarp();
                     if (c + 2 < CHUNKS) tmem_ld_wait_regs(ra);
                 }
@@ -398,8 +412,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1)
                     tmem_ld32(taddr + (uint32_t)(c * 32), ra);
                     tmem_ld_wait_regs(ra);
                     process_chunk<KCAP>(bound, ra, col0 + c * 32, valid - c * 32,
-                                        sel_rs<CHUNKS>(rsv, c), qs, inv, p.k, stash, stash_rs,
-                                        lane, st);
+                                        sel_rs<CHUNKS>(rsv, c), p.row_scale, qs, inv, p.k,
+                                        stash, lane, st);
                 }
             }
             tc_fence_before();
@@ -676,6 +690,107 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32)
     }
 }
 
+// Many lists per query (a one-query scan's per-CTA lists): one CTA per query.  Each of
+// its MB_WARPS warps merges a contiguous range of the lists (heads read from global
+// memory, each lane keeping the best head of its own lists), the warps' k-lists meet in
+// shared memory, and warp 0 merges those.  Order and padding as merge_lists_kernel.
+constexpr int MB_WARPS = 8;
+constexpr int MB_KMAX = 64;
+
+template <bool DESC>
+__global__ void __launch_bounds__(MB_WARPS * 32)
+    merge_lists_block_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci,
+                             int es, int nq, int n_lists, int k, int64_t id_offset, float* out_v,
+                             int32_t* out_i, int lists_major, int out_stride) {
+    __shared__ float wv[MB_WARPS][MB_KMAX];
+    __shared__ int32_t wi[MB_WARPS][MB_KMAX];
+    __shared__ uint16_t cursor[MERGE_MAX_LISTS];
+    const int q = blockIdx.x;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float pad = DESC ? -INFINITY : INFINITY;
+    const size_t base = lists_major ? (size_t)q * k : (size_t)q * n_lists * k;
+    const size_t lstride = lists_major ? (size_t)nq * k : (size_t)k;
+    for (int l = threadIdx.x; l < n_lists; l += blockDim.x) cursor[l] = 0;
+    __syncthreads();
+    const int l0 = (int)((int64_t)n_lists * w / MB_WARPS);
+    const int l1 = (int)((int64_t)n_lists * (w + 1) / MB_WARPS);
+    auto lane_best = [&](float& bv, int32_t& bi, int& bl) {
+        bv = pad;
+        bi = -1;
+        bl = -1;
+        for (int l = l0 + lane; l < l1; l += 32) {
+            const int c = cursor[l];
+            if (c >= k) continue;
+            const size_t at = (base + (size_t)l * lstride + c) * es;
+            const float v = cv[at];
+            const int32_t id = ci[at];
+            if (bl < 0 || merge_better<DESC>(v, id, bv, bi)) {
+                bv = v;
+                bi = id;
+                bl = l;
+            }
+        }
+    };
+    // phase 1: warp w's lists -> its k best in shared memory
+    float mv;
+    int32_t mi;
+    int ml;
+    lane_best(mv, mi, ml);
+    for (int j = 0; j < k; ++j) {
+        float bv = mv;
+        int32_t bi = mi;
+        int bl = ml;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            if ((ol >= 0) && (bl < 0 || merge_better<DESC>(ov, oi, bv, bi) ||
+                              (ov == bv && oi == bi && ol < bl))) {
+                bv = ov;
+                bi = oi;
+                bl = ol;
+            }
+        }
+        if (lane == 0) {
+            wv[w][j] = bl >= 0 ? bv : pad;
+            wi[w][j] = bl >= 0 ? bi : -1;
+        }
+        if (bl >= 0 && ((bl - l0) & 31) == lane) {
+            cursor[bl] += 1;
+            lane_best(mv, mi, ml);
+        }
+    }
+    __syncthreads();
+    // phase 2: warp 0 merges the MB_WARPS lists (list = lane < MB_WARPS)
+    if (w != 0) return;
+    int cur = 0;
+    for (int j = 0; j < k; ++j) {
+        const bool has = lane < MB_WARPS && cur < k;
+        float bv = has ? wv[lane][cur] : pad;
+        int32_t bi = has ? wi[lane][cur] : -1;
+        int bl = has ? lane : -1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            if ((ol >= 0) && (bl < 0 || merge_better<DESC>(ov, oi, bv, bi) ||
+                              (ov == bv && oi == bi && ol < bl))) {
+                bv = ov;
+                bi = oi;
+                bl = ol;
+            }
+        }
+        if (lane == bl) ++cur;
+        if (lane == 0) {
+            out_v[(size_t)q * out_stride + j] = bl >= 0 ? bv : pad;
+            out_i[(size_t)q * out_stride + j] =
+                (bl >= 0 && bi >= 0) ? (int32_t)(bi + id_offset) : -1;
+        }
+    }
+}
+
 __global__ void fill_results_kernel(float* v, int32_t* i, size_t n, float value) {
     for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < n;
          t += (size_t)gridDim.x * blockDim.x) {
@@ -754,9 +869,18 @@ int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, 
     if (out_stride <= 0) out_stride = k;
     const int es = pairs ? 2 : 1;
     if (pairs) ci = reinterpret_cast<const int32_t*>(cv) + 1;
+    const int lm = lists_major ? 1 : 0;
+    if (n_lists > 128 && k <= MB_KMAX) {  // few queries, many lists: a CTA per query
+        if (descending)
+            merge_lists_block_kernel<true><<<nq, MB_WARPS * 32, 0, st>>>(
+                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride);
+        else
+            merge_lists_block_kernel<false><<<nq, MB_WARPS * 32, 0, st>>>(
+                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride);
+        return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+    }
     const int blocks = (nq + MERGE_WARPS - 1) / MERGE_WARPS;
     const bool staged = (int64_t)n_lists * k <= MERGE_STAGE_ENTRIES;
-    const int lm = lists_major ? 1 : 0;
 #define PION_MERGE_GO(D, S)                                                              \
     merge_lists_kernel<D, S><<<blocks, MERGE_WARPS * 32, 0, st>>>(cv, ci, es, nq, n_lists, k, \
                                                                   id_offset, out_v, out_i, lm, \

@@ -37,9 +37,12 @@
 // CHECKED bit yields.  The pool therefore equals the reference's entry for entry.
 //
 // The visited set is a bitmap of num_nodes bits per resident warp in global memory,
-// cleared by the warp before each query.  Every loop is bounded (the beam by the
-// node count); a malformed graph records an error status instead of reading out of
-// bounds.
+// all zero between queries.  Each warp appends the index of every word it turns from
+// zero to non-zero to its own list (up to touch_cap words) and, when the query ends,
+// zeroes just those words: O(nodes visited), not O(num_nodes), per query.  A query
+// that visits more words than the list holds zeroes its whole bitmap instead.  Every
+// loop is bounded (the beam by the node count); a malformed graph records an error
+// status instead of reading out of bounds.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -81,8 +84,10 @@ struct Params {
     const int8_t* qcodes;  // nq x DIM
     const int32_t* qblk;   // nq x 8: block norms of the query codes
     int nq, k, ef, efr;
-    uint32_t* visited;  // vis_words per resident warp
+    uint32_t* visited;  // vis_words per resident warp, all zero between queries
     int64_t vis_words;
+    uint32_t* touched;  // touch_cap word indices per resident warp
+    int touch_cap;
     int32_t* out_ids;
     float* out_dist;
     unsigned long long* stats;  // level-0 evaluations, expansions, upper evaluations
@@ -231,6 +236,19 @@ __device__ __forceinline__ int upper_bound(const Entry* pool, int size, float d)
     return lo;
 }
 
+// Appends the words that lanes in `mask` turned non-zero (lane L's word `w`) to the
+// warp's touched list; n is the warp-uniform count (it may pass cap: then the list is
+// incomplete and the query zeroes the whole bitmap).
+__device__ __forceinline__ void note_words(uint32_t* list, int cap, int& n, unsigned mask,
+                                           uint32_t w, int lane) {
+    if (!mask) return;
+    if (mask & (1u << lane)) {
+        const int at = n + __popc(mask & ((1u << lane) - 1u));
+        if (at < cap) list[at] = w;
+    }
+    n += __popc(mask);
+}
+
 template <int STAGE>
 __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -246,6 +264,7 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
     int* qq = reinterpret_cast<int*>(g_lane + 32);  // block norms of the query codes
     int* tail_l2 = qq + 8;                          // [tail lane][block]
     uint32_t* vis = p.visited + ((size_t)blockIdx.x * WARPS + warp) * (size_t)p.vis_words;
+    uint32_t* touch = p.touched + ((size_t)blockIdx.x * WARPS + warp) * (size_t)p.touch_cap;
     const uint32_t nn = (uint32_t)p.num_nodes;
     const int ef = p.ef;
     unsigned n_evals = 0, n_expand = 0, n_upper = 0;  // per warp: far below 2^32
@@ -284,12 +303,7 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             if (lane < 8) qq[lane] = p.qblk[(size_t)qi * 8 + lane];
         }
         const float qn = p.from_pool ? p.qn_given[qi] : (float)qn_int;
-        {
-            int4* v4 = reinterpret_cast<int4*>(vis);
-            const int64_t n4 = p.vis_words / 4;
-            for (int64_t w = lane; w < n4; w += 32) v4[w] = make_int4(0, 0, 0, 0);
-        }
-        __syncwarp();
+        int n_touch = 0;  // words of `vis` this query turned non-zero (warp-uniform)
 
         // ---- upper levels: greedy in code space (skipped when starting from a pool)
         uint32_t curr = p.from_pool ? 0u : (uint32_t)p.entry;
@@ -380,16 +394,28 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             // the caller's pool; its nodes are the ones it marked visited
             size = min(p.pool_size[qi], ef);
             hint = min(p.pool_cursor[qi], size);
-            for (int i = lane; i < size; i += 32) {
-                const Entry e = p.pool_io[(size_t)qi * p.pool_stride + i];
-                pool[i] = e;
-                const uint32_t nd = e.id & ~CHECKED;
-                if (nd < nn) atomicOr(&vis[nd >> 5], 1u << (nd & 31));
+            for (int i0 = 0; i0 < size; i0 += 32) {
+                const int i = i0 + lane;
+                bool fresh_word = false;
+                uint32_t nd = 0xffffffffu;
+                if (i < size) {
+                    const Entry e = p.pool_io[(size_t)qi * p.pool_stride + i];
+                    pool[i] = e;
+                    nd = e.id & ~CHECKED;
+                    if (nd < nn) fresh_word = atomicOr(&vis[nd >> 5], 1u << (nd & 31)) == 0u;
+                }
+                note_words(touch, p.touch_cap, n_touch, __ballot_sync(FULL, fresh_word),
+                           nd >> 5, lane);
             }
-        } else if (lane == 0) {
-            atomicOr(&vis[curr >> 5], 1u << (curr & 31));
-            pool[0].d = cd;
-            pool[0].id = curr;
+        } else {
+            bool fresh_word = false;
+            if (lane == 0) {
+                fresh_word = atomicOr(&vis[curr >> 5], 1u << (curr & 31)) == 0u;
+                pool[0].d = cd;
+                pool[0].id = curr;
+            }
+            note_words(touch, p.touch_cap, n_touch, __ballot_sync(FULL, fresh_word), curr >> 5,
+                       lane);
         }
         // Look-ahead: the row of the entry predicted to be popped next (the second
         // unchecked entry at this pop) and the visited words of its neighbours, read
@@ -443,19 +469,24 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             const unsigned key = valid ? nb : (0x80000000u | (unsigned)lane);
             const unsigned peers = __match_any_sync(FULL, key);
             bool fresh = false;
+            bool fresh_word = false;
             if (valid && (__ffs(peers) - 1) == lane) {
                 const uint32_t bit = 1u << (nb & 31);
                 if (hit) {  // the word was read after every earlier mark of this query
                     fresh = (sp_word & bit) == 0;
-                    if (fresh) atomicOr(&vis[nb >> 5], bit);
+                    if (fresh) fresh_word = atomicOr(&vis[nb >> 5], bit) == 0u;
                 } else {
-                    fresh = (atomicOr(&vis[nb >> 5], bit) & bit) == 0;
+                    const uint32_t old = atomicOr(&vis[nb >> 5], bit);
+                    fresh = (old & bit) == 0;
+                    fresh_word = old == 0u;
                 }
                 if (fresh && sl >= nn) {
                     record_error(p.status, PION_B200_EINVAL);
                     fresh = false;
                 }
             }
+            note_words(touch, p.touch_cap, n_touch, __ballot_sync(FULL, fresh_word), nb >> 5,
+                       lane);
             // look-ahead row of the predicted next pop, in flight while this step scores
             sp_node = pred;
             if (pred != 0xffffffffu) {
@@ -621,6 +652,15 @@ __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
             }
         }
 
+        // back to an all-zero bitmap: the listed words, or every word if the list overflowed
+        __syncwarp();
+        if (n_touch <= p.touch_cap) {
+            for (int i = lane; i < n_touch; i += 32) vis[touch[i]] = 0u;
+        } else {
+            int4* v4 = reinterpret_cast<int4*>(vis);
+            const int64_t n4 = p.vis_words / 4;
+            for (int64_t w = lane; w < n4; w += 32) v4[w] = make_int4(0, 0, 0, 0);
+        }
         if (p.from_pool) {  // the whole pool back to the caller
             for (int i = lane; i < size; i += 32) p.pool_io[(size_t)qi * p.pool_stride + i] = pool[i];
             if (lane == 0) p.pool_size_out[qi] = size;
@@ -821,6 +861,9 @@ int launch_hnsw_beam(const HnswLaunch& L, cudaStream_t st) {
     p.efr = (L.ef + 31) / 32 * 32;
     p.visited = L.visited;
     p.vis_words = L.vis_words;
+    p.touched = L.touched;
+    p.touch_cap = L.touch_cap;
+    if (!p.touched || p.touch_cap < 32) return PION_B200_EINVAL;
     p.out_ids = L.out_ids;
     p.out_dist = L.out_dist;
     p.stats = L.stats;

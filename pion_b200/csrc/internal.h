@@ -97,6 +97,8 @@ struct pion_b200_ctx {
     pion::DevBuf stage_in;         // device copies of host inputs
     pion::DevBuf stage_out;        // device outputs copied back to host
     pion::DevBuf hnsw_visited;     // HNSW visited bitmaps, one per resident warp
+    pion::DevBuf hnsw_touched;     // per resident warp: the bitmap words a query touched
+    bool vis_clean = false;        // hnsw_visited is all zero (the beam kernel keeps it so)
     pion::DevBuf hnsw_misc;        // HNSW work counters and query counter
     std::string last_error;
     int64_t launches = 0;
@@ -194,8 +196,10 @@ struct HnswLaunch {
     const int8_t* qcodes = nullptr;
     const int32_t* qblk = nullptr;
     int nq = 0, k = 0, ef = 0;
-    uint32_t* visited = nullptr;
+    uint32_t* visited = nullptr;  // all zero on entry, left all zero (launch_hnsw_beam)
     int64_t vis_words = 0;
+    uint32_t* touched = nullptr;  // touch_cap words per resident warp
+    int touch_cap = 0;
     int32_t* out_ids = nullptr;
     float* out_dist = nullptr;
     unsigned long long* stats = nullptr;
@@ -218,6 +222,9 @@ int hnsw_ctas_per_sm(int ef);
 int launch_hnsw_quantize(const float* q, int nq, float gmin, float scale, int8_t* codes,
                          int32_t* blk, cudaStream_t st);
 int launch_hnsw_beam(const HnswLaunch& launch, cudaStream_t st);
+// Visited bitmaps (all zero) and touched-word lists for `warps` resident warps of the beam
+// kernel in the context's scratch, into L.visited / L.vis_words / L.touched / L.touch_cap.
+int hnsw_visit_buffers(pion_b200_ctx* ctx, int64_t warps, int64_t num_nodes, HnswLaunch& L);
 int launch_hnsw_relayout(const int8_t* src, int64_t n, int64_t stride, int64_t hdr,
                          int8_t* codes, float* norms, cudaStream_t st);
 // rows: the FP32 copy by node (the metric then reads it, unclamped), or null (the codes)
@@ -479,6 +486,11 @@ size_t bq_scan1_scratch(int64_t n_rows, int words);
 int launch_bq_scan1(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcode,
                     int S, int ctas, void* scratch, int32_t* sl_id, uint16_t* sl_h, int* sl_n,
                     cudaStream_t st);
+// The same rerank for few queries: shortlist rows spread over CTAs (dim % 16 == 0,
+// S <= 256), `dist` holds nq * S floats of scratch.
+int launch_bq_rerank_wide(const float* rows, int dim, const float* qn, const int32_t* sl_id,
+                          const int* sl_n, int S, int nq, int k, int64_t id_base, float* dist,
+                          float* out_d, int32_t* out_i, cudaStream_t st);
 int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t* sl_id,
                      const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
                      int32_t* out_i, cudaStream_t st);

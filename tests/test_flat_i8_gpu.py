@@ -348,3 +348,39 @@ def test_wait_that_runs_out(ctx, oracle, monkeypatch):
     ctx.sync()
     assert np.array_equal(di.cpu().numpy(), want_i)
     ix.free()
+
+
+@pytest.mark.parametrize("descending", [True, False])
+def test_merge_many_lists_one_cta_per_query(ctx, rng, descending):
+    """More than 128 lists per query (a one-query scan's per-CTA lists) take the CTA-per-
+    query merge: host and device memory, the pair layout, lists-major."""
+    import torch
+
+    import pion_b200
+    from pion_b200.sharded import pack_pairs
+    L, nq, k = 600, 3, 10
+    sign = -1.0 if descending else 1.0
+    v = rng.integers(0, 40, (L, nq, k)).astype(np.float32)
+    i = rng.integers(0, 1 << 20, (L, nq, k)).astype(np.int32)
+    for a in range(L):
+        for b in range(nq):
+            o = np.lexsort((i[a, b], sign * v[a, b]))
+            v[a, b], i[a, b] = v[a, b][o], i[a, b][o]
+    want = []
+    for b in range(nq):
+        fv, fi = v[:, b].ravel(), i[:, b].ravel()
+        o = np.lexsort((fi, sign * fv))[:k]
+        want.append((fi[o], fv[o]))
+    pairs = pack_pairs(torch.from_numpy(i), torch.from_numpy(v))
+    for p in (pairs.numpy(), pairs.cuda()):
+        ids, sc = pion_b200.merge_topk_pairs(ctx, p, k, descending=descending, lists_major=True)
+        ids = ids if isinstance(ids, np.ndarray) else ids.cpu().numpy()
+        sc = sc if isinstance(sc, np.ndarray) else sc.cpu().numpy()
+        for b in range(nq):
+            assert ids[b].tolist() == want[b][0].tolist()
+            assert sc[b].tolist() == want[b][1].tolist()
+    vq = np.ascontiguousarray(v.transpose(1, 0, 2))
+    iq = np.ascontiguousarray(i.transpose(1, 0, 2))
+    ids, sc = pion_b200.merge_topk(ctx, vq, iq, k, descending=descending)
+    for b in range(nq):
+        assert ids[b].tolist() == want[b][0].tolist()

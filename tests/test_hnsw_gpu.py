@@ -273,3 +273,16 @@ def test_index_file_serves_on_gpu(ctx, oracle, small, tmp_path):
     i1, d1 = gix.search(qs, 10, 64)
     assert np.array_equal(i0, i1) and np.array_equal(d0.view(np.uint32), d1.view(np.uint32))
     _same(oracle, G.arrays(), gix, qs, 10, 32)
+
+
+def test_visited_words_cleared_between_queries(oracle, small, monkeypatch):
+    """Each warp zeroes only the bitmap words its query touched; with a touched-word list
+    too small for the query it zeroes the whole bitmap.  Both leave the bitmaps clean:
+    many queries per warp, either way, give the oracle's pools."""
+    g, A, ix, rows, qs = small
+    many = np.concatenate([qs] * 40)  # more queries than resident warps
+    monkeypatch.setenv("PION_B200_TOUCH_CAP", "32")
+    _same(oracle, A, ix, many, 10, 256)
+    monkeypatch.delenv("PION_B200_TOUCH_CAP")
+    _same(oracle, A, ix, many, 10, 64)
+    _same(oracle, A, ix, qs, 10, 1024)
