@@ -613,7 +613,12 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         // k-th score; the main pass starts from it, so its integer pre-filter rejects
         // almost every row at once.  The main pass then scores every tile.
         const bool pre = use_prepass(n_tiles, kk, "PION_B200_I8_PREPASS");
-        const int pre_tiles = pre ? bound_tiles(n_tiles, kk) : 0;
+        int pre_tiles = pre ? bound_tiles(n_tiles, kk) : 0;
+        if (pre) {  // tuning hook: the sample's size in tiles (the result is exact for any)
+            const char* e = getenv("PION_B200_I8_SAMPLE");
+            const int want = e ? atoi(e) : 0;
+            if (want > 0) pre_tiles = want < n_tiles ? want : n_tiles;
+        }
         const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
         const int n_lists = splits * lps;
         int bnd_splits = pre ? ctx->num_sms / n_qt : 0;

@@ -350,26 +350,54 @@ __global__ void __launch_bounds__(THREADS, 1)
                 int32_t mx = (int32_t)r[0];
 #pragma unroll
                 for (int j = 1; j < 32; ++j) mx = max(mx, (int32_t)r[j]);
-                if (!__any_sync(0xffffffffu, 2 * (int64_t)mx - mcur[c] > (int64_t)ithr)) return;
-                const int vi = vicur[c];
-                uint32_t mask = 0;
+                const bool coarse = 2 * (int64_t)mx - mcur[c] > (int64_t)ithr;
+                if (!__any_sync(0xffffffffu, coarse)) return;
+                // the chunk's 32 floor norms (lane j holds column j's) for every lane
+                int* vrow = reinterpret_cast<int*>(stash_v);
+                vrow[lane] = vicur[c];
+                __syncwarp();
+                if (!coarse) return;
+                // From here on each lane works alone: no warp synchronisation.
+                uint32_t mask;
+                if (ithr == INT_MIN) {
+                    mask = 0xffffffffu;
+                } else {
+                    // bit j = (2 dot_j - v_j > ithr) = sign of ithr - (2 dot_j - v_j), two
+                    // funnel-shift chains (|2 dot - v| < 2^31 - 2^27, |ithr| < 2^27)
+                    uint32_t lo = 0, hi = 0;
+                    const int4* v4 = reinterpret_cast<const int4*>(vrow);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int v = __shfl_sync(0xffffffffu, vi, j);
-                    mask |= (2 * (int32_t)r[j] - v > ithr ? 1u : 0u) << j;
+                    for (int i = 3; i >= 0; --i) {
+                        const int4 a = v4[i], b = v4[i + 4];
+                        const int va[4] = {a.x, a.y, a.z, a.w}, vb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                        for (int e = 3; e >= 0; --e) {
+                            const int j = 4 * i + e;
+                            lo = __funnelshift_l(
+                                (uint32_t)(ithr - (2 * (int32_t)r[j] - va[e])), lo, 1);
+                            hi = __funnelshift_l(
+                                (uint32_t)(ithr - (2 * (int32_t)r[j + 16] - vb[e])), hi, 1);
+                        }
+                    }
+                    mask = lo | (hi << 16);
                 }
                 const int64_t vc = p.n_rows - c0;
                 if (vc < 32) mask &= vc <= 0 ? 0u : ((1u << vc) - 1u);
-                if (!__any_sync(0xffffffffu, mask != 0u)) return;
+                if (!mask) return;
+                // this lane's 32 dots into its own stash row (16-byte slots XOR-swizzled by
+                // lane), read back by index
+                uint4* row4 = reinterpret_cast<uint4*>(stash + lane * 32);
+                const int sw = lane & 7;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) stash[j * 32 + lane] = r[j];
-                stash_v[lane] = vl;
-                __syncwarp();
+                for (int i = 0; i < 8; ++i)
+                    row4[i ^ sw] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+                const uint32_t* row = stash + lane * 32;
 #pragma unroll 1
                 while (mask) {
                     const int j = __ffs(mask) - 1;
                     mask &= mask - 1u;
-                    const float d = l2_dist(qn, stash_v[j], (int32_t)stash[j * 32 + lane]);
+                    const float d = l2_dist(qn, __ldg(&p.vnorm[c0 + j]),
+                                            (int32_t)row[(((j >> 2) ^ sw) << 2) | (j & 3)]);
                     if (!(d < thr)) continue;  // the threshold moved within this chunk
                     if (count < p.cap) {
                         out_d[count] = d;
@@ -381,7 +409,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                         ithr = int_floor(thr);
                     }
                 }
-                __syncwarp();  // the stash is rewritten by the next chunk
             };
             if constexpr (KCAP <= 32) {
                 // chunks in pairs: the next chunk's TMEM load is in flight while the
