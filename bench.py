@@ -91,6 +91,9 @@ def args_parse(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="flat_i8")
     ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--batch-sweep", default=None,
+                    help="FLAT INT8: comma-separated batch sizes measured one after another on "
+                         "the same index, one JSON line each (e.g. 1,64,4096)")
     ap.add_argument("--rows", type=int, default=None,
                     help="override the index size (small cases for profiler captures)")
     ap.add_argument("--e2e-steps", type=int, default=None)
@@ -320,6 +323,9 @@ class I8Workload:
 
     def search(self, inp):
         return self.ix.search(inp[0], inp[1], self.k)
+
+    def search_pairs(self, inp):
+        return self.ix.search_pairs(inp[0], inp[1], self.k)
 
     def host_call(self, hin, out_i, out_v):
         import pion_b200
@@ -1024,6 +1030,8 @@ def run_ours(a, wl):
                                 device_id=dev)
 
     batch = a.batch or wl["batch"]
+    if a.batch_sweep:  # queries for the largest batch, sliced per batch size
+        batch = max(int(x) for x in a.batch_sweep.split(","))
     k = wl["k"]
     n = wl["rows"]
     lo, hi = shard_bounds(n, world, rank)
@@ -1040,7 +1048,8 @@ def run_ours(a, wl):
         return pion_b200.merge_topk_pairs(ctx, pairs, k, descending=W.descending,
                                           lists_major=True)
 
-    step = W.search if getattr(W, "replicas", False) else ShardedSearch(W.search, k, merge)
+    step = W.search if getattr(W, "replicas", False) else ShardedSearch(
+        W.search, k, merge, local_pairs=getattr(W, "search_pairs", None))
     workers = a.workers or (3 if wl["kind"] in ("hnsw", "quant") else 1)
     if workers > 1 and wl["kind"] not in ("hnsw", "slot", "quant"):
         raise SystemExit("--workers > 1 is for the hnsw workloads")
@@ -1068,146 +1077,160 @@ def run_ours(a, wl):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
-    inp = W.inputs()
-    run_steps(max(3, a.warmup), inp)
-    barrier()
+    def measure(batch, local_batch):
+        """Warm-up, the timed region, the e2e region and rank 0's JSON line for one batch
+        size (W's queries already set to it)."""
+        inp = W.inputs()
+        run_steps(max(3, a.warmup), inp)
+        barrier()
 
-    clocks = ClockMonitor(local)
-    clocks.start()
-    for c_ in ctxs:
-        c_.timing(True)
-    launches0 = sum(c_.launches for c_ in ctxs)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    ev0.record(stream)
-    run_steps(a.steps, inp)
-    ev1.record(stream)
-    barrier()
-    elapsed = ev0.elapsed_time(ev1)
-    launches = sum(c_.launches for c_ in ctxs) - launches0
-    kern_ms, kern_n = 0.0, 0
-    phase_ms = {"threshold_ms": 0.0, "main_ms": 0.0}
-    for c_ in ctxs:
-        km, kn = c_.timing_read()
-        for tag, key in ((1, "threshold_ms"), (2, "main_ms")):
-            pm, pn = c_.timing_read(tag)
-            phase_ms[key] += pm / max(1, kn)
-        c_.timing(False)
-        kern_ms, kern_n = kern_ms + km, kern_n + kn
-    if workers > 1:  # overlapping batches: the time per batch of the whole run
-        kern_ms, kern_n = elapsed, a.steps
-    clk = clocks.stop()
-    # per-phase device time of a few more steps: local scoring, all-gather, merge
-    breakdown = None
-    if isinstance(step, ShardedSearch):
-        breakdown = step.breakdown(inp, max(3, min(a.steps, 20)))
+        clocks = ClockMonitor(local)
+        clocks.start()
+        for c_ in ctxs:
+            c_.timing(True)
+        launches0 = sum(c_.launches for c_ in ctxs)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        ev0.record(stream)
+        run_steps(a.steps, inp)
+        ev1.record(stream)
+        barrier()
+        elapsed = ev0.elapsed_time(ev1)
+        launches = sum(c_.launches for c_ in ctxs) - launches0
+        kern_ms, kern_n = 0.0, 0
+        phase_ms = {"threshold_ms": 0.0, "main_ms": 0.0}
+        for c_ in ctxs:
+            km, kn = c_.timing_read()
+            for tag, key in ((1, "threshold_ms"), (2, "main_ms")):
+                pm, pn = c_.timing_read(tag)
+                phase_ms[key] += pm / max(1, kn)
+            c_.timing(False)
+            kern_ms, kern_n = kern_ms + km, kern_n + kn
+        if workers > 1:  # overlapping batches: the time per batch of the whole run
+            kern_ms, kern_n = elapsed, a.steps
+        clk = clocks.stop()
+        # per-phase device time of a few more steps: local scoring, all-gather, merge
+        breakdown = None
+        if isinstance(step, ShardedSearch):
+            breakdown = step.breakdown(inp, max(3, min(a.steps, 20)))
 
-    # ---- e2e: host (pinned) queries in, host results out, through the C ABI
-    e2e_steps = a.e2e_steps or max(10, min(a.steps, 200))
-    hin = [t.cpu().pin_memory() for t in inp]
-    dbuf = [torch.empty_like(t) for t in inp]
-    out_i = torch.empty((local_batch, k), dtype=torch.int32).pin_memory()
-    out_v = torch.empty((local_batch, k), dtype=torch.float32).pin_memory()
+        # ---- e2e: host (pinned) queries in, host results out, through the C ABI
+        e2e_steps = a.e2e_steps or max(10, min(a.steps, 200))
+        hin = [t.cpu().pin_memory() for t in inp]
+        dbuf = [torch.empty_like(t) for t in inp]
+        out_i = torch.empty((local_batch, k), dtype=torch.int32).pin_memory()
+        out_v = torch.empty((local_batch, k), dtype=torch.float32).pin_memory()
 
-    def e2e_step():
-        if world == 1 or getattr(W, "replicas", False):
-            # the C-ABI host-buffer path: copies, kernels, copies, sync
-            W.host_call(hin, out_i, out_v)
-            return
-        for d, h in zip(dbuf, hin):
-            d.copy_(h, non_blocking=True)
-        ids, sc = step(dbuf)
-        out_i.copy_(ids, non_blocking=True)
-        out_v.copy_(sc, non_blocking=True)
-        stream.synchronize()
+        def e2e_step():
+            if world == 1 or getattr(W, "replicas", False):
+                # the C-ABI host-buffer path: copies, kernels, copies, sync
+                W.host_call(hin, out_i, out_v)
+                return
+            for d, h in zip(dbuf, hin):
+                d.copy_(h, non_blocking=True)
+            ids, sc = step(dbuf)
+            out_i.copy_(ids, non_blocking=True)
+            out_v.copy_(sc, non_blocking=True)
+            stream.synchronize()
 
-    def e2e_threads(n):
-        """n batches through the C ABI with host buffers, one host thread per worker
-        context (each call copies in, searches and copies out, synchronously)."""
-        import threading
-        bufs = [([t.clone().pin_memory() for t in hin],
-                 torch.empty_like(out_i).pin_memory(), torch.empty_like(out_v).pin_memory())
-                for _ in range(workers)]
-        errs = []
+        def e2e_threads(n):
+            """n batches through the C ABI with host buffers, one host thread per worker
+            context (each call copies in, searches and copies out, synchronously)."""
+            import threading
+            bufs = [([t.clone().pin_memory() for t in hin],
+                     torch.empty_like(out_i).pin_memory(), torch.empty_like(out_v).pin_memory())
+                    for _ in range(workers)]
+            errs = []
 
-        def work(w):
+            def work(w):
+                try:
+                    for i in range(w, n, workers):
+                        W.host_call(bufs[w][0], bufs[w][1], bufs[w][2], ctx=ctxs[w])
+                except Exception as e:  # pragma: no cover
+                    errs.append(e)
+            ths = [threading.Thread(target=work, args=(w,)) for w in range(workers)]
+            for t_ in ths:
+                t_.start()
+            for t_ in ths:
+                t_.join()
+            if errs:
+                raise errs[0]
+
+        run_e2e = (lambda n: [e2e_step() for _ in range(n)]) if workers == 1 else e2e_threads
+        run_e2e(3)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run_e2e(e2e_steps)
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        h2d = sum(t.numel() * t.element_size() for t in hin)
+        d2h = local_batch * k * 8
+
+        # ---- max over ranks
+        bd = [breakdown[x] for x in ("local_ms", "allgather_ms", "merge_ms")] if breakdown else [0.0] * 3
+        t = torch.tensor([elapsed, e2e_ms, kern_ms / max(1, kern_n), phase_ms["threshold_ms"],
+                          phase_ms["main_ms"], *bd], device=dev, dtype=torch.float64)
+        lt = torch.tensor([launches], device=dev, dtype=torch.int64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dist.all_reduce(lt, op=dist.ReduceOp.SUM)
+        elapsed, e2e_ms, kern_avg_ms, thr_ms, main_ms, bd_local, bd_ag, bd_merge = t.tolist()
+        launches = int(lt.item())
+
+        line = None
+        if rank == 0:
+            per_step = getattr(W, "queries_per_step", batch)
+            qps = per_step * a.steps / (elapsed / 1000.0)
+            e2e_qps = per_step * e2e_steps / (e2e_ms / 1000.0)
+            peaks, peak_kind = measured_peaks()
+            regime, why = choose_regime(elapsed / 1000.0, clk)
+            roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind, regime=regime,
+                              phases={"threshold_ms": thr_ms, "main_ms": main_ms})
+            roof["regime_reason"] = why
+            roof["traffic"] = profiled_traffic(f"{a.workload}_{world}")
+            line = {
+                "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed / a.steps,
+                "higher_is_better": True,
+                "scaling": "weak" if getattr(W, "replicas", False) else "strong",
+                "vs_baseline": None,
+                "dtype": W.dtype, "data": "synthetic (seeded Gaussian mixture on the device)",
+                "config": config_of(wl, batch, world, a),
+                "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "gpu_launches": launches,
+                "workers": workers,
+                "roofline": roof,
+                "clocks": clk,
+            }
+            if breakdown is not None:
+                line["step_breakdown_ms"] = {
+                    "local_search": bd_local, "allgather": bd_ag, "merge": bd_merge,
+                    "note": "max over ranks of the per-step device time of each phase, CUDA events "
+                            "over extra steps after the timed region"}
+        # ---- CPU baseline on rank 0 at N=1 (bounded sample of the same workload)
+        if rank == 0 and hasattr(W, "extra"):
+            line["config"].update(W.extra(dev))
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
             try:
-                for i in range(w, n, workers):
-                    W.host_call(bufs[w][0], bufs[w][1], bufs[w][2], ctx=ctxs[w])
+                line["cpu_baseline"] = cpu_baseline(W, batch, k, a.cpu_seconds)
             except Exception as e:  # pragma: no cover
-                errs.append(e)
-        ths = [threading.Thread(target=work, args=(w,)) for w in range(workers)]
-        for t_ in ths:
-            t_.start()
-        for t_ in ths:
-            t_.join()
-        if errs:
-            raise errs[0]
+                line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
 
-    run_e2e = (lambda n: [e2e_step() for _ in range(n)]) if workers == 1 else e2e_threads
-    run_e2e(3)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    run_e2e(e2e_steps)
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    h2d = sum(t.numel() * t.element_size() for t in hin)
-    d2h = local_batch * k * 8
-
-    # ---- max over ranks
-    bd = [breakdown[x] for x in ("local_ms", "allgather_ms", "merge_ms")] if breakdown else [0.0] * 3
-    t = torch.tensor([elapsed, e2e_ms, kern_ms / max(1, kern_n), phase_ms["threshold_ms"],
-                      phase_ms["main_ms"], *bd], device=dev, dtype=torch.float64)
-    lt = torch.tensor([launches], device=dev, dtype=torch.int64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(lt, op=dist.ReduceOp.SUM)
-    elapsed, e2e_ms, kern_avg_ms, thr_ms, main_ms, bd_local, bd_ag, bd_merge = t.tolist()
-    launches = int(lt.item())
-
-    line = None
-    if rank == 0:
-        per_step = getattr(W, "queries_per_step", batch)
-        qps = per_step * a.steps / (elapsed / 1000.0)
-        e2e_qps = per_step * e2e_steps / (e2e_ms / 1000.0)
-        peaks, peak_kind = measured_peaks()
-        regime, why = choose_regime(elapsed / 1000.0, clk)
-        roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind, regime=regime,
-                          phases={"threshold_ms": thr_ms, "main_ms": main_ms})
-        roof["regime_reason"] = why
-        roof["traffic"] = profiled_traffic(f"{a.workload}_{world}")
-        line = {
-            "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed / a.steps,
-            "higher_is_better": True,
-            "scaling": "weak" if getattr(W, "replicas", False) else "strong",
-            "vs_baseline": None,
-            "dtype": W.dtype, "data": "synthetic (seeded Gaussian mixture on the device)",
-            "config": config_of(wl, batch, world, a),
-            "e2e": {"value": e2e_qps, "unit": "queries/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-            "gpu_launches": launches,
-            "workers": workers,
-            "roofline": roof,
-            "clocks": clk,
-        }
-        if breakdown is not None:
-            line["step_breakdown_ms"] = {
-                "local_search": bd_local, "pack_allgather": bd_ag, "merge": bd_merge,
-                "note": "max over ranks of the per-step device time of each phase, CUDA events "
-                        "over extra steps after the timed region"}
-    # ---- CPU baseline on rank 0 at N=1 (bounded sample of the same workload)
-    if rank == 0 and hasattr(W, "extra"):
-        line["config"].update(W.extra(dev))
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        try:
-            line["cpu_baseline"] = cpu_baseline(W, batch, k, a.cpu_seconds)
-        except Exception as e:  # pragma: no cover
-            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    sweep = [int(x) for x in a.batch_sweep.split(",")] if a.batch_sweep else None
+    if sweep:
+        if wl["kind"] != "i8":
+            raise SystemExit("--batch-sweep is for the FLAT INT8 workloads")
+        q_all, qs_all = W.q, W.qs
+        for b in sweep:
+            W.q, W.qs, W.batch = q_all[:b].contiguous(), qs_all[:b].contiguous(), b
+            measure(b, b)
+    else:
+        measure(batch, local_batch)
     W.ix.free()
     for c_ in ctxs[1:]:
         c_.close()

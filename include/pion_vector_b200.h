@@ -56,6 +56,10 @@ extern "C" {
 #define PION_B200_MEM_DEVICE 1        /* device memory: used in place, no copies      */
 #define PION_B200_MEM_DEVICE_BORROW 2 /* registration only: keep the caller's device
                                          pointer (no copy); caller keeps it alive     */
+/* Or'ed into `mem` of pion_v_b200_flat_i8_knn with PION_B200_MEM_DEVICE: out_scores
+ * receives nq x k interleaved 8-byte (f32 score, i32 id) pairs (8-byte aligned) -- the
+ * layout one row shard exchanges with the others -- and out_ids is ignored. */
+#define PION_B200_OUT_PAIRS 0x100
 
 /* Same value as VECTOR_ABI_VERSION (src/vector/vector_abi.mojo:29). */
 #define PION_B200_ABI_VERSION 1

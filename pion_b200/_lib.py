@@ -24,6 +24,7 @@ EABI = -12
 MEM_HOST = 0
 MEM_DEVICE = 1
 MEM_DEVICE_BORROW = 2
+OUT_PAIRS = 0x100
 
 MERGE_DESC = 1
 MERGE_LISTS_MAJOR = 2

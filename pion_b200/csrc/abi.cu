@@ -536,6 +536,16 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
                             const float* q_scale, int64_t nq, int64_t k, int32_t* out_ids,
                             float* out_scores, int mem) {
     if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    // interleaved (score, id) pairs in out_scores (device memory only)
+    const bool pairs_out = (mem & PION_B200_OUT_PAIRS) != 0;
+    mem &= ~PION_B200_OUT_PAIRS;
+    if (pairs_out) {
+        if (mem != PION_B200_MEM_DEVICE || (reinterpret_cast<uintptr_t>(out_scores) & 7u) != 0)
+            return set_error(ctx, PION_B200_EINVAL,
+                             "flat_i8_knn: pairs out need 8-byte aligned device memory");
+        out_ids = reinterpret_cast<int32_t*>(out_scores) + 1;
+    }
+    const int oes = pairs_out ? 2 : 1;
     if (!ix || ix->kind != kFlatI8)
         return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn: not a FLAT INT8 index");
     if (ix->device != ctx->device)
@@ -580,7 +590,7 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
     int rc = 0;
     if (ix->n_rows == 0) {
         // Empty index: every result slot is padding (id -1, score -inf).
-        rc = launch_fill_results(dv, di, (size_t)nq * kk, -INFINITY, st);
+        rc = launch_fill_results(dv, di, (size_t)nq * kk, -INFINITY, st, oes);
         ctx->launches++;
     }
     const int path = forced_i8_path();
@@ -601,7 +611,8 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
             ctx->launches++;
         }
         if (rc == 0) {
-            rc = launch_merge_lists(cv, ci, nqi, ctas, kk, ix->id_base, true, dv, di, st);
+            rc = launch_merge_lists(cv, ci, nqi, ctas, kk, ix->id_base, true, dv, di, st, false, 0,
+                                    false, oes);
             ctx->launches++;
         }
     } else if (ix->n_rows > 0) {
@@ -689,7 +700,8 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         }
         timing_end(ctx, t_all);
         if (rc == 0) {
-            rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, dv, di, st);
+            rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, dv, di, st, false,
+                                    0, false, oes);
             ctx->launches++;
         }
     }

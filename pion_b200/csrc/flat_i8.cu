@@ -607,7 +607,7 @@ template <bool DESC, bool STAGED>
 __global__ void __launch_bounds__(MERGE_WARPS * 32)
     merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int es,
                        int nq, int n_lists, int k, int64_t id_offset, float* out_v,
-                       int32_t* out_i, int lists_major, int out_stride) {
+                       int32_t* out_i, int lists_major, int out_stride, int out_es) {
     __shared__ uint16_t cursor[MERGE_WARPS][STAGED ? MERGE_STAGE_ENTRIES : MERGE_MAX_LISTS];
     __shared__ float stage_v[STAGED ? MERGE_WARPS : 1][STAGED ? MERGE_STAGE_ENTRIES : 1];
     __shared__ int32_t stage_i[STAGED ? MERGE_WARPS : 1][STAGED ? MERGE_STAGE_ENTRIES : 1];
@@ -621,12 +621,36 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32)
     const size_t base = lists_major ? (size_t)q * k : (size_t)q * n_lists * k;
     const size_t lstride = lists_major ? (size_t)nq * k : (size_t)k;
     if (STAGED) {
+        // eight loads in flight per lane before the first store (a query's lists are
+        // one contiguous run unless lists-major)
         const int total = n_lists * k;
-        for (int e = lane; e < total; e += 32) {
-            const int l = e / k, c = e - l * k;
-            const size_t at = (base + (size_t)l * lstride + c) * es;
-            stage_v[w][e] = cv[at];
-            stage_i[w][e] = ci[at];
+        constexpr int U = 8;
+        for (int e0 = lane; e0 < total; e0 += 32 * U) {
+            float v[U];
+            int32_t id[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int e = e0 + 32 * u;
+                if (e < total) {
+                    size_t at;
+                    if (lists_major) {
+                        const int l = e / k, c = e - l * k;
+                        at = (base + (size_t)l * lstride + c) * es;
+                    } else {
+                        at = (base + (size_t)e) * es;
+                    }
+                    v[u] = cv[at];
+                    id[u] = ci[at];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int e = e0 + 32 * u;
+                if (e < total) {
+                    stage_v[w][e] = v[u];
+                    stage_i[w][e] = id[u];
+                }
+            }
         }
     }
     __syncwarp();
@@ -680,8 +704,9 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32)
             }
         }
         if (lane == 0) {
-            out_v[(size_t)q * out_stride + j] = bl >= 0 ? bv : pad;
-            out_i[(size_t)q * out_stride + j] = (bl >= 0 && bi >= 0) ? (int32_t)(bi + id_offset) : -1;
+            const size_t o = ((size_t)q * out_stride + j) * out_es;
+            out_v[o] = bl >= 0 ? bv : pad;
+            out_i[o] = (bl >= 0 && bi >= 0) ? (int32_t)(bi + id_offset) : -1;
         }
         if (bl >= 0 && (bl & 31) == lane) {
             cursor[w][bl] += 1;
@@ -701,7 +726,7 @@ template <bool DESC>
 __global__ void __launch_bounds__(MB_WARPS * 32)
     merge_lists_block_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci,
                              int es, int nq, int n_lists, int k, int64_t id_offset, float* out_v,
-                             int32_t* out_i, int lists_major, int out_stride) {
+                             int32_t* out_i, int lists_major, int out_stride, int out_es) {
     __shared__ float wv[MB_WARPS][MB_KMAX];
     __shared__ int32_t wi[MB_WARPS][MB_KMAX];
     __shared__ uint16_t cursor[MERGE_MAX_LISTS];
@@ -784,18 +809,18 @@ __global__ void __launch_bounds__(MB_WARPS * 32)
         }
         if (lane == bl) ++cur;
         if (lane == 0) {
-            out_v[(size_t)q * out_stride + j] = bl >= 0 ? bv : pad;
-            out_i[(size_t)q * out_stride + j] =
-                (bl >= 0 && bi >= 0) ? (int32_t)(bi + id_offset) : -1;
+            const size_t o = ((size_t)q * out_stride + j) * out_es;
+            out_v[o] = bl >= 0 ? bv : pad;
+            out_i[o] = (bl >= 0 && bi >= 0) ? (int32_t)(bi + id_offset) : -1;
         }
     }
 }
 
-__global__ void fill_results_kernel(float* v, int32_t* i, size_t n, float value) {
+__global__ void fill_results_kernel(float* v, int32_t* i, size_t n, float value, int es) {
     for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < n;
          t += (size_t)gridDim.x * blockDim.x) {
-        v[t] = value;
-        i[t] = -1;
+        v[t * es] = value;
+        i[t * es] = -1;
     }
 }
 
@@ -854,16 +879,17 @@ int launch_quantize_rows_i8(const float* src, int64_t n_rows, int d, int d_pad, 
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
-int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st) {
+int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st, int es) {
     if (n == 0) return 0;
     const unsigned blocks = (unsigned)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
-    fill_results_kernel<<<blocks, 256, 0, st>>>(v, i, n, value);
+    fill_results_kernel<<<blocks, 256, 0, st>>>(v, i, n, value, es);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
-                       cudaStream_t st, bool lists_major, int out_stride, bool pairs) {
+                       cudaStream_t st, bool lists_major, int out_stride, bool pairs,
+                       int out_es) {
     if (nq <= 0) return 0;
     if (n_lists < 1 || n_lists > MERGE_MAX_LISTS || k < 1 || k > 65535) return PION_B200_ESHAPE;
     if (out_stride <= 0) out_stride = k;
@@ -873,10 +899,10 @@ int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, 
     if (n_lists > 128 && k <= MB_KMAX) {  // few queries, many lists: a CTA per query
         if (descending)
             merge_lists_block_kernel<true><<<nq, MB_WARPS * 32, 0, st>>>(
-                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride);
+                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride, out_es);
         else
             merge_lists_block_kernel<false><<<nq, MB_WARPS * 32, 0, st>>>(
-                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride);
+                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride, out_es);
         return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
     }
     const int blocks = (nq + MERGE_WARPS - 1) / MERGE_WARPS;
@@ -884,7 +910,7 @@ int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, 
 #define PION_MERGE_GO(D, S)                                                              \
     merge_lists_kernel<D, S><<<blocks, MERGE_WARPS * 32, 0, st>>>(cv, ci, es, nq, n_lists, k, \
                                                                   id_offset, out_v, out_i, lm, \
-                                                                  out_stride)
+                                                                  out_stride, out_es)
     if (descending) {
         if (staged) PION_MERGE_GO(true, true); else PION_MERGE_GO(true, false);
     } else {
@@ -894,18 +920,21 @@ int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, 
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
-// Splits of the index across CTAs for a batch of n_qt query tiles: the count whose
-// total CTA number fills whole waves of the SMs best, preferring fewer splits.
+// Splits of the index across CTAs for a batch of n_qt query tiles.  One CTA fills an
+// SM (its shared memory), so the launch runs in waves of num_sms CTAs and an SM pays a
+// CTA's fixed cost (set-up, pipeline fill and drain, about two tiles' worth) once per
+// wave: the modelled time is waves x (2 + the largest CTA's tiles); the smallest wins,
+// fewer splits on ties.
 int fi8_choose_splits(int n_qt, int n_tiles, int num_sms) {
     int best = 1;
-    double best_eff = -1.0;
-    for (int s = 1; s <= 64; ++s) {
+    long best_cost = -1;
+    for (int s = 1; s <= 256; ++s) {
         if (s > 1 && n_tiles / s < 4) break;
         const long total = (long)n_qt * s;
         const long waves = (total + num_sms - 1) / num_sms;
-        const double eff = (double)total / (double)(waves * num_sms);
-        if (eff > best_eff + 1e-9) {
-            best_eff = eff;
+        const long cost = waves * (2 + (n_tiles + s - 1) / s);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
             best = s;
         }
     }

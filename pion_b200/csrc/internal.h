@@ -333,11 +333,14 @@ int fi8_scan1_ctas(int64_t n_rows, int num_sms);
 int launch_tile_max(const float* rs, int64_t n_rows, float* out, cudaStream_t st);
 int launch_quantize_rows_i8(const float* src, int64_t n_rows, int d, int d_pad, int8_t* dst,
                             float* dst_scale, cudaStream_t st);
-int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st);
+// n result slots of (value, id -1); es = 2 for interleaved (score, id) pairs (v = the
+// pairs, i = v + 1 as ints)
+int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_t st,
+                        int es = 1);
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
                        cudaStream_t st, bool lists_major = false, int out_stride = 0,
-                       bool pairs = false);
+                       bool pairs = false, int out_es = 1);
 // Event pair around one scoring-kernel launch (or one phase of it, `tag` =
 // PION_B200_TIMING_*) when timing is enabled.  timing_begin returns the pair's slot
 // (-1 when timing is off); timing_end closes `slot`, or the pair opened last.

@@ -225,6 +225,27 @@ class FlatI8Index(_Index):
         return ids, sc
 
 
+def _search_pairs_i8(ix, q, q_scale, k: int):
+    """FlatI8Index.search into one int32 [nq, k, 2] CUDA tensor of (score bits, id)."""
+    if not (_is_torch(q) and q.is_cuda):
+        raise TypeError("search_pairs needs CUDA tensors")
+    pq, mq, kq = _ptr(q, np.int8, "q")
+    ps, ms, ks = _ptr(q_scale, np.float32, "q_scale")
+    _same_mem(mq, ms)
+    out = torch.empty((q.shape[0], k, 2), dtype=torch.int32, device=q.device)
+    with _TorchStream(ix.ctx, MEM_DEVICE):
+        ix.ctx.check(ix.ctx.lib.pion_v_b200_flat_i8_knn(ix.ctx.h, ix.h, pq, ps, q.shape[0], k,
+                                                        None, out.data_ptr(),
+                                                        MEM_DEVICE | _lib.OUT_PAIRS))
+    return out
+
+
+FlatI8Index.search_pairs = _search_pairs_i8
+FlatI8Index.search_pairs.__doc__ = (
+    "Top-k as interleaved (score, id) pairs, int32 [nq, k, 2] on the GPU: the layout one "
+    "row shard all-gathers (pion_b200.sharded), written by the search's final merge.")
+
+
 class FlatF32Index(_Index):
     """Device-resident FLAT FP32 index for COSINE exact_knn."""
 

@@ -43,14 +43,21 @@ class ShardedSearch:
     with lists_major=True).  `group` is a torch.distributed process group (None: default).
     """
 
-    def __init__(self, local_search: Callable, k: int, merge: Callable, group=None):
+    def __init__(self, local_search: Callable, k: int, merge: Callable, group=None,
+                 local_pairs: Callable | None = None):
         import torch.distributed as dist
 
         self.local_search = local_search
+        self.local_pairs = local_pairs  # inputs -> int32 [B, k, 2] pairs, written directly
         self.k = k
         self.merge = merge
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def _pairs(self, inputs):
+        if self.local_pairs is not None:
+            return self.local_pairs(inputs)
+        return pack_pairs(*self.local_search(inputs))
 
     def _gather(self, t):
         import torch
@@ -65,28 +72,29 @@ class ShardedSearch:
         return out
 
     def __call__(self, inputs):
-        ids, scores = self.local_search(inputs)
         if self.world == 1:
-            return ids, scores
-        return self.merge(self._gather(pack_pairs(ids, scores)))
+            return self.local_search(inputs)
+        return self.merge(self._gather(self._pairs(inputs)))
 
     def breakdown(self, inputs, steps: int):
-        """Average device milliseconds per step of each phase -- local scoring and
-        top-k, pack + all-gather, merge -- over `steps` steps timed with CUDA events on
-        the current stream (GPU tensors only)."""
+        """Average device milliseconds per step of each phase -- local scoring and top-k
+        (as pairs), all-gather, merge -- over `steps` steps timed with CUDA events on the
+        current stream (GPU tensors only)."""
         import torch
 
         st = torch.cuda.current_stream()
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
         for e in ev:
             e[0].record(st)
-            ids, scores = self.local_search(inputs)
-            e[1].record(st)
             if self.world > 1:
-                g = self._gather(pack_pairs(ids, scores))
+                pairs = self._pairs(inputs)
+                e[1].record(st)
+                g = self._gather(pairs)
                 e[2].record(st)
                 self.merge(g)
             else:
+                self.local_search(inputs)
+                e[1].record(st)
                 e[2].record(st)
             e[3].record(st)
         torch.cuda.synchronize()

@@ -384,3 +384,30 @@ def test_merge_many_lists_one_cta_per_query(ctx, rng, descending):
     ids, sc = pion_b200.merge_topk(ctx, vq, iq, k, descending=descending)
     for b in range(nq):
         assert ids[b].tolist() == want[b][0].tolist()
+
+
+def test_search_pairs_equals_search(ctx, oracle):
+    """PION_B200_OUT_PAIRS: the final merge writes interleaved (score, id) pairs, equal to
+    packing the two-array result; for the batched path, the one-query scan and an empty
+    index."""
+    import torch
+
+    import pion_b200
+    from pion_b200.sharded import pack_pairs
+    keys, ks = oracle.pkm_quantize_rows_i8(mixture_np(30000, 1536, 64, 9, 0)[0])
+    q, qsc = oracle.pkm_quantize_rows_i8(mixture_np(10, 1536, 64, 10, 200)[1])
+    dk, dks = torch.from_numpy(keys).cuda(), torch.from_numpy(ks).cuda()
+    dq, dqs = torch.from_numpy(q).cuda(), torch.from_numpy(qsc).cuda()
+    ix = pion_b200.FlatI8Index(ctx, dk, dks, id_base=500)
+    for b in (200, 1):
+        ids, sc = ix.search(dq[:b].contiguous(), dqs[:b].contiguous(), 10)
+        pairs = ix.search_pairs(dq[:b].contiguous(), dqs[:b].contiguous(), 10)
+        torch.cuda.synchronize()
+        assert torch.equal(pairs, pack_pairs(ids, sc))
+    ix.free()
+    empty = pion_b200.FlatI8Index(ctx, dk[:0], dks[:0])
+    pairs = empty.search_pairs(dq[:3].contiguous(), dqs[:3].contiguous(), 4)
+    torch.cuda.synchronize()
+    assert (pairs[..., 1] == -1).all()
+    assert torch.isneginf(pairs[..., 0].contiguous().view(torch.float32)).all()
+    empty.free()
