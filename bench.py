@@ -335,7 +335,11 @@ class I8Workload:
                                               out_v.data_ptr(), pion_b200._lib.MEM_HOST))
 
     def roofline(self, rows_local, kern_ms, peaks, peak_kind, regime="burst", phases=None):
-        if self.batch > 1:
+        ops = 2.0 * self.dim * rows_local * self.batch
+        byts = float(rows_local) * (self.dim + 4)
+        t_ops = ops / (tensor_peak(peaks, regime, 2.0)[0] * 1e12)
+        t_hbm = byts / (peaks["hbm_gbs"] * 1e9)
+        if self.batch > 1 and t_ops >= t_hbm:  # enough queries per row for the tensor cores
             ops = 2.0 * self.dim * rows_local * self.batch
             achieved = ops / (kern_ms / 1000.0) / 1e12
             peak, burst, sus = tensor_peak(peaks, regime, 2.0)
@@ -351,12 +355,16 @@ class I8Workload:
                 r["threshold_pass_ms"] = phases.get("threshold_ms")
                 r["frac_main_pass"] = ops / (phases["main_ms"] / 1000.0) / 1e12 / peak
             return r
-        byts = float(rows_local) * (self.dim + 4)
+        # one query (the scan) or too few for the rows' bytes to be hidden: every row
+        # streams from HBM once per batch
         achieved = byts / (kern_ms / 1000.0) / 1e9
         peak = peaks["hbm_gbs"]
         return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                "algorithmic_per_launch": byts, "kernel_ms": kern_ms}
+                "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs (a copy: read "
+                                                         f"+ write bytes)",
+                "algorithmic_per_launch": byts, "kernel_ms": kern_ms,
+                "tensor_frac": ops / (kern_ms / 1000.0) / 1e12 / tensor_peak(peaks, regime,
+                                                                              2.0)[0]}
 
     def host_data(self):
         return (self.keys.cpu().numpy(), self.ks.cpu().numpy(), self.q.cpu().numpy(),
