@@ -104,6 +104,11 @@ def args_parse(argv=None):
     ap.add_argument("--graph-cache", default=None,
                     help="HNSW workloads: load the graph from this index file (pion.hnsw.0 "
                          "format) when it exists, else build it and save it there")
+    ap.add_argument("--build", choices=["lanes", "batched", "gpu"], default="lanes",
+                    help="HNSW workloads: graph build -- the reference's parallel link lanes "
+                         "(host), batched insertion on the host, or batched insertion with "
+                         "the batches' searches on the GPU (the same graph as 'batched')")
+    ap.add_argument("--build-batch", type=int, default=4096)
     ap.add_argument("--workers", type=int, default=None,
                     help="worker contexts (each its own CUDA stream) taking batches in turn; "
                          "default 3 for hnsw, 1 otherwise")
@@ -559,9 +564,13 @@ class HNSWWorkload:
                     raise SystemExit(f"{cache} holds {self.graph.layout.num_nodes} nodes, not {n}")
             else:
                 t0 = time.perf_counter()
-                self.graph = pion_b200.HNSWGraph(rows.numpy(), M=wl["M"],
-                                                 ef_construction=wl["ef_construction"])
+                how = wl.get("build", "lanes")
+                self.graph = pion_b200.HNSWGraph(
+                    rows.numpy(), M=wl["M"], ef_construction=wl["ef_construction"],
+                    batch=wl.get("build_batch", 4096) if how != "lanes" else 0,
+                    gpu=ctx if how == "gpu" else None)
                 self.build_s = time.perf_counter() - t0
+                self.build_how = how
                 if cache:
                     self.graph.save(cache)
             self.rows_host = rows
@@ -660,6 +669,7 @@ class HNSWWorkload:
         del rows
         torch.cuda.empty_cache()
         return {"recall_at_10": recall, "ef": self.ef, "build_s": self.build_s,
+                "build": getattr(self, "build_how", "cache"),
                 "build_threads": os.cpu_count()}
 
     def host_data(self):
@@ -1272,6 +1282,8 @@ def main(argv=None):
     wl = dict(WORKLOADS[a.workload])
     wl["ef"] = a.ef
     wl["graph_cache"] = a.graph_cache
+    wl["build"] = a.build
+    wl["build_batch"] = a.build_batch
     if a.rows:
         wl["rows"] = a.rows
         wl["desc"] += f" (rows overridden: {a.rows:,})"

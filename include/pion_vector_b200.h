@@ -480,6 +480,18 @@ int pion_v_b200_hnsw_build_batched(const float *rows, int64_t n_rows, int64_t di
                                    int64_t ef_construction, int metric, int64_t id_base,
                                    int n_threads, int64_t max_batch,
                                    pion_b200_hnsw_graph **out_graph);
+/* The batched build with the search half on a GPU: every batch of at least 64 nodes is
+ * planned on ctx's device -- a warp per node does the greedy descent, _search_layer_mt at
+ * efConstruction and _prune_neighbors (src/vector/hnsw.mojo:2032-2240, 3595-3628) against
+ * the graph as it stood before the batch, with the host's heap and distance arithmetic --
+ * and linked on the host in node order, so the graph is array for array the one
+ * pion_v_b200_hnsw_build_batched builds with the same max_batch.  dim 1536,
+ * ef_construction <= 1024.  Host memory in and out; n_threads prepare each batch's rows and
+ * run the repair passes. */
+int pion_v_b200_hnsw_build_gpu(pion_b200_ctx *ctx, const float *rows, int64_t n_rows,
+                               int64_t dim, int64_t M, int64_t ef_construction, int metric,
+                               int64_t id_base, int n_threads, int64_t max_batch,
+                               pion_b200_hnsw_graph **out_graph);
 /* The graph's buffers (host memory owned by the graph). */
 int pion_v_b200_hnsw_graph_layout(const pion_b200_hnsw_graph *graph,
                                   pion_b200_hnsw_layout *out_layout);
@@ -487,6 +499,8 @@ int pion_v_b200_hnsw_graph_layout(const pion_b200_hnsw_graph *graph,
  * link drops, relinked under-linked nodes, nodes re-linked by the exit repair, links added
  * by the reachability repair. */
 int pion_v_b200_hnsw_graph_stats(const pion_b200_hnsw_graph *graph, int64_t *out5);
+/* The same five counters, then the nodes whose insertion a GPU planned. */
+int pion_v_b200_hnsw_graph_stats6(const pion_b200_hnsw_graph *graph, int64_t *out6);
 int pion_v_b200_hnsw_graph_free(pion_b200_hnsw_graph *graph);
 
 /* Copies a graph (every pointer of `layout` in HOST memory) to the GPU.  Checks the

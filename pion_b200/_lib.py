@@ -78,6 +78,9 @@ SIGNATURES = {
                                             _PP]),
     "pion_v_b200_hnsw_graph_layout": (_I, [_P, _P]),
     "pion_v_b200_hnsw_graph_stats": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_graph_stats6": (_I, [_P, _P]),
+    "pion_v_b200_hnsw_build_gpu": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I, _I64, _I, _I64,
+                                        _PP]),
     "pion_v_b200_hnsw_graph_free": (_I, [_P]),
     "pion_v_b200_register_hnsw": (_I, [_P, _P, _PP]),
     "pion_v_b200_hnsw_search": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I]),

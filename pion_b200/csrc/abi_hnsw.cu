@@ -214,6 +214,13 @@ int pion_v_b200_hnsw_graph_stats(const pion_b200_hnsw_graph* graph, int64_t* out
     return 0;
 }
 
+int pion_v_b200_hnsw_graph_stats6(const pion_b200_hnsw_graph* graph, int64_t* out6) {
+    if (!graph || !out6) return PION_B200_EINVAL;
+    pion_v_b200_hnsw_graph_stats(graph, out6);
+    out6[5] = graph->stats.planned_elsewhere;
+    return 0;
+}
+
 int pion_v_b200_hnsw_graph_free(pion_b200_hnsw_graph* graph) {
     if (!graph) return PION_B200_EINVAL;
     delete graph;

@@ -247,6 +247,21 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n) {
            | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// ------------------------------------------------------ visited-word lists --
+// A warp's visited bitmap is kept all zero between searches by listing the words it turns
+// non-zero.  Appends the words that lanes in `mask` turned non-zero (lane L's word `w`) to
+// the warp's list; n is the warp-uniform count (it may pass cap: then the list is
+// incomplete and the search zeroes the whole bitmap).  Call with the whole warp.
+__device__ __forceinline__ void note_words(uint32_t* list, int cap, int& n, unsigned mask,
+                                           uint32_t w, int lane) {
+    if (!mask) return;
+    if (mask & (1u << lane)) {
+        const int at = n + __popc(mask & ((1u << lane) - 1u));
+        if (at < cap) list[at] = w;
+    }
+    n += __popc(mask);
+}
+
 // ------------------------------------------------------- top-k in registers --
 // PTX select: the compiler cannot fold a chain of these back into an indexed
 // access, which would move the whole register array to local memory.

@@ -236,19 +236,6 @@ __device__ __forceinline__ int upper_bound(const Entry* pool, int size, float d)
     return lo;
 }
 
-// Appends the words that lanes in `mask` turned non-zero (lane L's word `w`) to the
-// warp's touched list; n is the warp-uniform count (it may pass cap: then the list is
-// incomplete and the query zeroes the whole bitmap).
-__device__ __forceinline__ void note_words(uint32_t* list, int cap, int& n, unsigned mask,
-                                           uint32_t w, int lane) {
-    if (!mask) return;
-    if (mask & (1u << lane)) {
-        const int at = n + __popc(mask & ((1u << lane) - 1u));
-        if (at < cap) list[at] = w;
-    }
-    n += __popc(mask);
-}
-
 template <int STAGE>
 __global__ void __launch_bounds__(WARPS * 32, 7) hnsw_beam_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem[];

@@ -387,12 +387,8 @@ struct Builder {
     // neighbours kept per level (level l's at [offs[l'], offs[l' + 1]) with l' counted
     // from the top).  link() applies them as insert() would; plan() then link() of one
     // node is insert() (a level's links never change a lower level's search).
-    struct Plan {
-        std::vector<uint32_t> ids;
-        std::vector<float> d;  // their distances to the node
-        std::vector<uint32_t> offs;
-        int top = -1;
-    };
+    using Plan = BuildPlan;
+    std::vector<int64_t>* dirty = nullptr;  // nodes whose lists link() changed
 
     void plan(int64_t id, Scratch& s, Plan& p) {
         const int lvl = g.level[id];
@@ -442,6 +438,7 @@ struct Builder {
     // from the top, in the order insert() makes them (one thread).
     void link(int64_t id, const Plan& p) {
         const int8_t* q = code(id);
+        if (dirty) dirty->push_back(id);
         for (int l = p.top, k = 0; l >= 0; --l, ++k) {
             const int64_t m_limit = cap(l);
             for (uint32_t j = p.offs[k]; j < p.offs[k + 1]; ++j) {
@@ -460,6 +457,10 @@ struct Builder {
                     }
                 }
                 if (evicted >= 0 && evicted < g.n) remove_link(evicted, l, nb);
+                if (dirty) {
+                    dirty->push_back(nb);
+                    if (evicted >= 0 && evicted < g.n) dirty->push_back(evicted);
+                }
                 const uint32_t onc = count(id, l).load(std::memory_order_relaxed);
                 if ((int64_t)onc < m_limit) {
                     add_published(id, l, nb, dnb);
@@ -819,7 +820,8 @@ int level_of(int64_t i, float ml) {
 }  // namespace
 
 int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
-          int64_t id_base, int n_threads, Graph& g, BuildStats* stats, int64_t max_batch) {
+          int64_t id_base, int n_threads, Graph& g, BuildStats* stats, int64_t max_batch,
+          BatchPlanner* planner, int64_t planner_min) {
     g = Graph();
     g.n = n;
     g.dim = dim;
@@ -930,25 +932,65 @@ int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int
         for (int64_t i = 0; i < n; ++i)
             if (i != g.entry) order.push_back(i);
         std::vector<Builder::Plan> plans;
+        // With a planner: every node whose lists changed since its last update.
+        std::vector<int64_t> dirty;
+        std::vector<float> brows;
+        bool use_planner =
+            planner != nullptr &&
+            planner->begin(g, g.codes.data(), b.link_base.data(), b.cnt_base.data(),
+                           (int64_t)b.links.size(), ct, b.scale, b.offset, max_batch) == 0;
+        if (use_planner) b.dirty = &dirty;
         int64_t done = 0, linked = 1;
         while (done < (int64_t)order.size()) {
             int64_t bsz = std::max<int64_t>(1, linked / 4);
             bsz = std::min(bsz, max_batch);
             bsz = std::min(bsz, (int64_t)order.size() - done);
             if ((int64_t)plans.size() < bsz) plans.resize((size_t)bsz);
-            std::atomic<int64_t> next{0};
-            auto work = [&](int t) {
-                for (int64_t j = next.fetch_add(1); j < bsz; j = next.fetch_add(1))
-                    b.plan(order[(size_t)(done + j)], scratch[(size_t)t], plans[(size_t)j]);
-            };
-            const int use = (int)std::min<int64_t>(nt, bsz);
-            if (use <= 1) {
-                work(0);
-            } else {
-                std::vector<std::thread> th;
-                for (int t = 1; t < use; ++t) th.emplace_back(work, t);
-                work(0);
-                for (auto& x : th) x.join();
+            bool planned = false;
+            if (use_planner && bsz >= planner_min) {
+                // the graph's changes since the last batch, then this batch's rows
+                std::sort(dirty.begin(), dirty.end());
+                dirty.erase(std::unique(dirty.begin(), dirty.end()), dirty.end());
+                const uint32_t* cnts = reinterpret_cast<const uint32_t*>(b.cnt.get());
+                static_assert(sizeof(std::atomic<uint32_t>) == sizeof(uint32_t), "counts");
+                if (planner->update(dirty.data(), (int64_t)dirty.size(), b.links.data(), cnts) ==
+                    0) {
+                    dirty.clear();
+                    brows.resize((size_t)(bsz * dim));
+                    const int use = (int)std::min<int64_t>(nt, bsz);
+                    auto rows_of = [&](int t) {
+                        std::vector<float> buf((size_t)dim);
+                        for (int64_t j = t; j < bsz; j += use) {
+                            const float* x = b.row(order[(size_t)(done + j)], buf);
+                            std::memcpy(brows.data() + j * dim, x, (size_t)dim * sizeof(float));
+                        }
+                    };
+                    std::vector<std::thread> th;
+                    for (int t = 1; t < use; ++t) th.emplace_back(rows_of, t);
+                    rows_of(0);
+                    for (auto& x : th) x.join();
+                    planned = planner->plan(order.data() + done, bsz, brows.data(), plans) == 0;
+                    if (planned && stats) stats->planned_elsewhere += bsz;
+                } else {
+                    use_planner = false;  // the planner failed: the host plans the rest
+                    b.dirty = nullptr;
+                }
+            }
+            if (!planned) {
+                std::atomic<int64_t> next{0};
+                auto work = [&](int t) {
+                    for (int64_t j = next.fetch_add(1); j < bsz; j = next.fetch_add(1))
+                        b.plan(order[(size_t)(done + j)], scratch[(size_t)t], plans[(size_t)j]);
+                };
+                const int use = (int)std::min<int64_t>(nt, bsz);
+                if (use <= 1) {
+                    work(0);
+                } else {
+                    std::vector<std::thread> th;
+                    for (int t = 1; t < use; ++t) th.emplace_back(work, t);
+                    work(0);
+                    for (auto& x : th) x.join();
+                }
             }
             for (int64_t j = 0; j < bsz; ++j) b.link(order[(size_t)(done + j)], plans[(size_t)j]);
             done += bsz;

@@ -36,13 +36,49 @@ struct BuildStats {
     int64_t relinked = 0;
     int64_t repaired_exits = 0;
     int64_t repaired_links = 0;
+    int64_t planned_elsewhere = 0;  // nodes a BatchPlanner planned
+};
+
+// The search half of one node's insertion (greedy descent, _search_layer_mt at
+// efConstruction, _prune_neighbors on every level it joins): the pruned neighbours per
+// level, from the top level `top` down to 0, level l's at [offs[k], offs[k + 1]) with k
+// counted from the top, and their distances (exact INT8 L2) to the node.
+struct BuildPlan {
+    std::vector<uint32_t> ids;
+    std::vector<float> d;
+    std::vector<uint32_t> offs;
+    int top = -1;
+};
+
+// Plans whole batches of insertions elsewhere (a GPU), identically to the host's plan.
+// The builder keeps every node's lists in one array: node i's level-l list (capacity 2M at
+// level 0, M above) starts at link_base[i] + (l == 0 ? 0 : 2M + (l - 1) M), its count at
+// cnt_base[i] + l.
+class BatchPlanner {
+  public:
+    virtual ~BatchPlanner() {}
+    // Once, before any batch: codes (n x dim, node order), levels, list layout, the
+    // greedy descent's dequantisation (x = c * scale + offset), the largest batch.
+    virtual int begin(const Graph& g, const int8_t* codes, const int64_t* link_base,
+                      const int64_t* cnt_base, int64_t n_links, int64_t n_counts, float scale,
+                      float offset, int64_t max_batch) = 0;
+    // Node blocks (all its lists and counts) that changed since the last call.
+    virtual int update(const int64_t* nodes, int64_t count, const uint32_t* links,
+                       const uint32_t* counts) = 0;
+    // Plans for nodes ids[0..count) against the graph as last updated; rows[j] is the fp32
+    // row node ids[j] is linked with (normalised under COSINE).  Nonzero: plan on the host.
+    virtual int plan(const int64_t* ids, int64_t count, const float* rows,
+                     std::vector<BuildPlan>& out) = 0;
 };
 
 // Builds the graph of n rows (fp32, n x dim, normalised first under COSINE) with the
 // reference's parameters; node i gets external id id_base + i.  n_threads link lanes, or
-// with max_batch > 0 batched insertion (deterministic; n_threads plan each batch).
+// with max_batch > 0 batched insertion (deterministic; n_threads plan each batch).  With a
+// planner, batches of at least planner_min nodes are planned by it (the graph is the
+// same).
 int build(const float* rows, int64_t n, int64_t dim, int64_t M, int64_t efc, int metric,
-          int64_t id_base, int n_threads, Graph& g, BuildStats* stats, int64_t max_batch = 0);
+          int64_t id_base, int n_threads, Graph& g, BuildStats* stats, int64_t max_batch = 0,
+          BatchPlanner* planner = nullptr, int64_t planner_min = 64);
 
 // Block-quantised slot formats (the reference's PolarQuant / NanoQuant / TurboQuant
 // compact_vectors): kinds, and the buffers quantize() fills from the rows the graph was

@@ -462,12 +462,22 @@ class HNSWGraph:
     time (the same graph for any thread count; batch = 1 is the one-lane build)."""
 
     def __init__(self, rows, M: int = 16, ef_construction: int = 200, metric: str = "cosine",
-                 id_base: int = 0, threads: int = 0, batch: int = 0):
+                 id_base: int = 0, threads: int = 0, batch: int = 0, gpu: "Context" = None):
+        """gpu: a Context whose device plans the batches (needs batch > 0); the graph is
+        the one the host's batched build makes."""
         self.lib = _lib.load()
         a = np.ascontiguousarray(rows, dtype=np.float32)
         h = ctypes.c_void_p()
         mt = 1 if metric == "cosine" else 0
-        if batch > 0:  # batched insertion (deterministic for any thread count)
+        if gpu is not None:
+            if batch <= 0:
+                raise ValueError("the GPU build is a batched build: give batch > 0")
+            gpu.check(self.lib.pion_v_b200_hnsw_build_gpu(gpu.h, a.ctypes.data, a.shape[0],
+                                                          a.shape[1], M, ef_construction, mt,
+                                                          id_base, threads, batch,
+                                                          ctypes.byref(h)))
+            rc = 0
+        elif batch > 0:  # batched insertion (deterministic for any thread count)
             rc = self.lib.pion_v_b200_hnsw_build_batched(a.ctypes.data, a.shape[0], a.shape[1],
                                                          M, ef_construction, mt, id_base,
                                                          threads, batch, ctypes.byref(h))
@@ -526,11 +536,12 @@ class HNSWGraph:
             raise PionError(rc, f"hnsw_save {path} failed")
 
     def stats(self) -> dict:
-        """lanes, link_drops, relinked, repaired_exits, repaired_links."""
-        out = (ctypes.c_int64 * 5)()
-        self.lib.pion_v_b200_hnsw_graph_stats(self.h, out)
+        """lanes, link_drops, relinked, repaired_exits, repaired_links, gpu_planned (nodes
+        whose insertion a GPU planned)."""
+        out = (ctypes.c_int64 * 6)()
+        self.lib.pion_v_b200_hnsw_graph_stats6(self.h, out)
         return dict(zip(("lanes", "link_drops", "relinked", "repaired_exits",
-                         "repaired_links"), list(out)))
+                         "repaired_links", "gpu_planned"), list(out)))
 
     def arrays(self) -> dict:
         """The layout as numpy views of the library's buffers (each view keeps the graph

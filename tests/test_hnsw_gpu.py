@@ -286,3 +286,25 @@ def test_visited_words_cleared_between_queries(oracle, small, monkeypatch):
     monkeypatch.delenv("PION_B200_TOUCH_CAP")
     _same(oracle, A, ix, many, 10, 64)
     _same(oracle, A, ix, qs, 10, 1024)
+
+
+@pytest.mark.parametrize("metric,M,efc,n", [("cosine", 16, 100, 20000), ("l2", 8, 64, 12000),
+                                            ("cosine", 16, 200, 60000)])
+def test_gpu_planned_build_equals_host_batched_build(ctx, metric, M, efc, n):
+    """pion_v_b200_hnsw_build_gpu plans every batch of >= 64 nodes on the GPU (greedy
+    descent, _search_layer_mt, _prune_neighbors) and links on the host: the graph must be
+    the host batched build's, array for array."""
+    import pion_b200
+    rows, _ = mixture_np(n, 1536, 64, seed=n + M, n_queries=0)
+    host = pion_b200.HNSWGraph(rows, M=M, ef_construction=efc, metric=metric, batch=1024,
+                               threads=8)
+    gpu = pion_b200.HNSWGraph(rows, M=M, ef_construction=efc, metric=metric, batch=1024,
+                              threads=8, gpu=ctx)
+    st = gpu.stats()
+    assert st["gpu_planned"] > n // 2, st
+    A, B = host.arrays(), gpu.arrays()
+    for name in ("compact_buffer", "l0_compact", "l0_slots", "node_slot", "node_ids",
+                 "node_level", "upper_offset", "upper_links"):
+        assert np.array_equal(A[name], B[name]), name
+    for name in ("entry_point", "max_level", "global_min", "global_max"):
+        assert A[name] == B[name], name
