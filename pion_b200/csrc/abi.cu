@@ -630,14 +630,8 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
             const int want = e ? atoi(e) : 0;
             if (want > 0) pre_tiles = want < n_tiles ? want : n_tiles;
         }
-        // Staged (PION_B200_I8_STAGED=1): the sampled tiles are scored exactly (no bound) as
-        // the first stage, their k best per query bound the rest, which the second stage
-        // scores; the first stage's k best ride along as one extra list of the final merge.
-        const char* stg = getenv("PION_B200_I8_STAGED");
-        const bool staged = pre && stg && atoi(stg) == 1 && pre_tiles < n_tiles;
-        const int main_begin = staged ? pre_tiles : 0;
-        const int splits = fi8_choose_splits(n_qt, n_tiles - main_begin, ctx->num_sms);
-        const int n_lists = splits * lps + (staged ? 1 : 0);
+        const int splits = fi8_choose_splits(n_qt, n_tiles, ctx->num_sms);
+        const int n_lists = splits * lps;
         int bnd_splits = pre ? ctx->num_sms / n_qt : 0;
         if (pre) bnd_splits = bnd_splits < 1 ? 1 : (bnd_splits > pre_tiles ? pre_tiles : bnd_splits);
         const int bnd_lists = bnd_splits * lps;
@@ -679,16 +673,10 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
             L.cand_val = bv;
             L.cand_idx = bi;
             L.thr0 = nullptr;
-            L.bound_mode = staged ? 0 : 1;
+            L.bound_mode = 1;
             rc = launch_flat_i8_tc(L, st);
             ctx->launches++;
-            if (rc == 0 && staged) {  // stage one's k best: the last list of the final merge
-                rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, 0, true,
-                                        cv + (size_t)(n_lists - 1) * kk,
-                                        ci + (size_t)(n_lists - 1) * kk, st, false,
-                                        n_lists * kk);
-                ctx->launches++;
-            } else if (rc == 0) {  // per query: the k best chunk scores; the k-th is the bound
+            if (rc == 0) {  // per query: the k best chunk scores; the k-th is the bound
                 rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, 0, true, tv, ti, st);
                 ctx->launches++;
             }
@@ -696,15 +684,14 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
         }
         if (rc == 0) {
             const int t_main = timing_begin(ctx, PION_B200_TIMING_MAIN);
-            L.tile_begin = main_begin;
+            L.tile_begin = 0;
             L.tile_end = n_tiles;
             L.n_splits = splits;
             L.n_lists = n_lists;
             L.cand_val = cv;
             L.cand_idx = ci;
-            L.thr0 = staged ? cv + (size_t)(n_lists - 1) * kk + (kk - 1)
-                            : (pre ? tv + (kk - 1) : nullptr);
-            L.thr0_stride = staged ? n_lists * kk : kk;
+            L.thr0 = pre ? tv + (kk - 1) : nullptr;
+            L.thr0_stride = kk;
             L.bound_mode = 0;
             L.test_stall = test_stall();
             rc = launch_flat_i8_tc(L, st);
