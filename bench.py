@@ -109,6 +109,10 @@ def args_parse(argv=None):
                          "(host), batched insertion on the host, or batched insertion with "
                          "the batches' searches on the GPU (the same graph as 'batched')")
     ap.add_argument("--build-batch", type=int, default=4096)
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="FLAT INT8 on N > 1 GPUs: the shards' lists cross NVLink through the "
+                         "library's peer-memory exchange (with the threshold sample shared by "
+                         "the ranks), or through an NCCL all-gather")
     ap.add_argument("--workers", type=int, default=None,
                     help="worker contexts (each its own CUDA stream) taking batches in turn; "
                          "default 3 for hnsw, 1 otherwise")
@@ -272,7 +276,9 @@ def dist_env():
 def config_of(wl, batch, world, a=None):
     c = {"workload": wl["desc"], "rows": wl["rows"], "dim": wl["dim"],
          "centres": wl["centres"], "batch": batch, "k": wl["k"], "seed": wl["seed"],
-         "parallelism": f"row shards x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+         "parallelism": f"row shards x{world}" + (
+             (" + NVLink peer exchange" if (a is None or a.exchange == "peer") and
+              wl["kind"] == "i8" else " + NCCL all-gather") if world > 1 else ""),
          "l2": "index larger than L2 (no flush needed)"}
     if wl["kind"] == "hnsw":
         c.update({"M": wl["M"], "ef_construction": wl["ef_construction"],
@@ -1066,8 +1072,14 @@ def run_ours(a, wl):
         return pion_b200.merge_topk_pairs(ctx, pairs, k, descending=W.descending,
                                           lists_major=True)
 
-    step = W.search if getattr(W, "replicas", False) else ShardedSearch(
-        W.search, k, merge, local_pairs=getattr(W, "search_pairs", None))
+    if getattr(W, "replicas", False):
+        step = W.search
+    elif world > 1 and wl["kind"] == "i8" and a.exchange == "peer":
+        # the library's NVLink peer exchange: shared threshold sample, one call per step
+        from pion_b200.sharded import PeerExchange, PeerShardedSearch
+        step = PeerShardedSearch(W.ix, PeerExchange(ctx, batch, k))
+    else:
+        step = ShardedSearch(W.search, k, merge, local_pairs=getattr(W, "search_pairs", None))
     workers = a.workers or (3 if wl["kind"] in ("hnsw", "quant") else 1)
     if workers > 1 and wl["kind"] not in ("hnsw", "slot", "quant"):
         raise SystemExit("--workers > 1 is for the hnsw workloads")
@@ -1099,6 +1111,7 @@ def run_ours(a, wl):
         """Warm-up, the timed region, the e2e region and rank 0's JSON line for one batch
         size (W's queries already set to it)."""
         inp = W.inputs()
+        barrier()
         run_steps(max(3, a.warmup), inp)
         barrier()
 
@@ -1183,6 +1196,8 @@ def run_ours(a, wl):
         e1.record(stream)
         barrier()
         e2e_ms = e0.elapsed_time(e1)
+        for c_ in ctxs:  # any device-side wait that gave up (e.g. a peer's flag) fails the run
+            c_.sync()
         h2d = sum(t.numel() * t.element_size() for t in hin)
         d2h = local_batch * k * 8
 
@@ -1249,6 +1264,11 @@ def run_ours(a, wl):
             measure(b, b)
     else:
         measure(batch, local_batch)
+    torch.cuda.synchronize()
+    if world > 1:  # no rank frees its exchange buffers while a peer may still write them
+        dist.barrier(device_ids=[local])
+    if getattr(step, "ex", None) is not None:
+        step.ex.close()
     W.ix.free()
     for c_ in ctxs[1:]:
         c_.close()

@@ -406,6 +406,45 @@ int pion_v_b200_merge_topk(pion_b200_ctx *ctx, const float *cand_scores, const i
                            int64_t nq, int64_t n_lists, int64_t k, int flags,
                            float *out_scores, int32_t *out_ids, int mem);
 
+/* ---------------------------------------------------- row-shard exchange -- */
+/* One process per GPU, each holding a row shard (registered with id_base = its first
+ * row): the shards' per-query k (score, id) pairs cross NVLink as peer stores into every
+ * rank's receive buffer (shared through CUDA IPC handles), a flag per rank and step marks
+ * them complete, and every rank merges the world lists itself -- the all-gather + merge
+ * of src/commands/vector.mojo:4394-4436 without a collective call.  Set-up: create on
+ * every rank, exchange the PION_B200_IPC_HANDLE_BYTES handles by any channel (e.g.
+ * torch.distributed), connect with the world's handles (rank order).  Waits are bounded
+ * by the context's wait budget (pion_v_b200_set_wait_budget): a missing peer turns into
+ * PION_B200_ETIMEOUT from pion_v_b200_sync, not a hang.  `regions` independent uses per
+ * step (<= 4), each double-buffered by the step's parity. */
+#define PION_B200_IPC_HANDLE_BYTES 64
+typedef struct pion_b200_exchange pion_b200_exchange;
+int pion_v_b200_exchange_create(pion_b200_ctx *ctx, int world, int rank, int regions,
+                                int64_t max_nq, int64_t k, pion_b200_exchange **out);
+int pion_v_b200_exchange_handle(const pion_b200_exchange *ex, void *out_handle);
+int pion_v_b200_exchange_connect(pion_b200_exchange *ex, const void *handles);
+int pion_v_b200_exchange_free(pion_b200_exchange *ex);
+/* The exchange's world size once connected, else -1. */
+int pion_v_b200_exchange_world(const pion_b200_exchange *ex);
+/* This rank's `pairs` (device, nq x k interleaved (f32 score, i32 id)) to every rank, then
+ * the merged k best per query of all ranks' lists (PION_B200_MERGE_DESC for largest-first)
+ * into out_scores / out_ids, or into out_scores as pairs with PION_B200_OUT_PAIRS.  `epoch`
+ * (>= 1) numbers the step and must advance by one per call on every rank. */
+int pion_v_b200_exchange_merge(pion_b200_ctx *ctx, pion_b200_exchange *ex, const void *pairs,
+                               int64_t nq, int64_t k, uint32_t epoch, int flags,
+                               float *out_scores, int32_t *out_ids);
+/* Row-sharded FLAT INT8 KNN in one call (device memory, the exchange created with 2
+ * regions): this rank scores its share of the threshold sample, the ranks exchange and
+ * merge those k-lists into one bound per query (the k-th best of the union of every
+ * rank's sample: a lower bound of the global k-th score), every rank scores its whole
+ * shard from that bound, and the ranks exchange and merge their k-lists: out_scores /
+ * out_ids (or pairs with PION_B200_OUT_PAIRS) hold the global top k by (score desc, id
+ * asc) on every rank. */
+int pion_v_b200_flat_i8_knn_sharded(pion_b200_ctx *ctx, const pion_b200_index *ix,
+                                    pion_b200_exchange *ex, const int8_t *q, const float *q_scale,
+                                    int64_t nq, int64_t k, uint32_t epoch, int flags,
+                                    int32_t *out_ids, float *out_scores);
+
 /* ------------------------------------------------------------------- HNSW -- */
 
 /* An HNSW INT8 graph in the reference's compact level-0 layout: the buffers that

@@ -29,6 +29,7 @@ OUT_PAIRS = 0x100
 MERGE_DESC = 1
 MERGE_LISTS_MAJOR = 2
 MERGE_PAIRS = 4
+IPC_HANDLE_BYTES = 64
 
 ABI_VERSION = 1
 
@@ -73,6 +74,14 @@ SIGNATURES = {
     "pion_v_b200_quantize_rows_i8": (_I, [_P, _P, _I64, _I64, _I64, _P, _P, _I]),
     "pion_v_b200_l2_normalize_rows": (_I, [_P, _P, _I64, _I64, _P, _I]),
     "pion_v_b200_merge_topk": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P, _P, _I]),
+    "pion_v_b200_exchange_create": (_I, [_P, _I, _I, _I, _I64, _I64, _PP]),
+    "pion_v_b200_exchange_handle": (_I, [_P, _P]),
+    "pion_v_b200_exchange_connect": (_I, [_P, _P]),
+    "pion_v_b200_exchange_world": (_I, [_P]),
+    "pion_v_b200_exchange_free": (_I, [_P]),
+    "pion_v_b200_exchange_merge": (_I, [_P, _P, _P, _I64, _I64, ctypes.c_uint32, _I, _P, _P]),
+    "pion_v_b200_flat_i8_knn_sharded": (_I, [_P, _P, _P, _P, _P, _I64, _I64, ctypes.c_uint32,
+                                             _I, _P, _P]),
     "pion_v_b200_hnsw_build": (_I, [_P, _I64, _I64, _I64, _I64, _I, _I64, _I, _PP]),
     "pion_v_b200_hnsw_build_batched": (_I, [_P, _I64, _I64, _I64, _I64, _I, _I64, _I, _I64,
                                             _PP]),

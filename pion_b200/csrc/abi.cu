@@ -717,6 +717,132 @@ int pion_v_b200_flat_i8_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, const
     return 0;
 }
 
+// ------------------------------------------------------- row-sharded search
+
+int pion_v_b200_flat_i8_knn_sharded(pion_b200_ctx* ctx, const pion_b200_index* ix,
+                                    pion_b200_exchange* ex, const int8_t* q,
+                                    const float* q_scale, int64_t nq, int64_t k, uint32_t epoch,
+                                    int flags, int32_t* out_ids, float* out_scores) {
+    if (!valid_ctx(ctx)) return PION_B200_EINVAL;
+    if (!ix || ix->kind != kFlatI8 || ix->device != ctx->device)
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn_sharded: not a FLAT INT8 index here");
+    const bool pairs_out = (flags & PION_B200_OUT_PAIRS) != 0;
+    if (pairs_out && out_scores) out_ids = reinterpret_cast<int32_t*>(out_scores) + 1;
+    if (!ex || nq < 1 || k < 1 || k > 64 || !q || !q_scale || !out_ids || !out_scores ||
+        epoch == 0 || (reinterpret_cast<uintptr_t>(q) & 15u) != 0)
+        return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn_sharded: bad arguments");
+    if (int rc = use_device(ctx)) return rc;
+    cudaStream_t st = ctx->stream;
+    const int dim = (int)ix->dim;
+    const int kk = (int)k, nqi = (int)nq;
+    const int world = pion_v_b200_exchange_world(ex);
+    if (world < 1) return set_error(ctx, PION_B200_EINVAL, "flat_i8_knn_sharded: no exchange");
+    const int n_qt = (nqi + fi8_query_tile() - 1) / fi8_query_tile();
+    const int n_tiles = (int)((ix->n_rows + fi8_tile_rows() - 1) / fi8_tile_rows());
+    const int lps = fi8_lists_per_split(kk);
+    // this rank's share of the sample one index of the whole would take
+    int sample = 0;
+    if (n_tiles > 0) {
+        sample = (bound_tiles(n_tiles * world, kk) + world - 1) / world;
+        sample = sample < 2 ? 2 : sample;
+        sample = sample > n_tiles ? n_tiles : sample;
+    }
+    const int splits = n_tiles > 0 ? fi8_choose_splits(n_qt, n_tiles, ctx->num_sms) : 1;
+    const int n_lists = splits * lps;
+    int bnd_splits = ctx->num_sms / n_qt;
+    bnd_splits = bnd_splits < 1 ? 1 : (bnd_splits > sample ? (sample > 0 ? sample : 1) : bnd_splits);
+    const int bnd_lists = bnd_splits * lps;
+    const size_t ncand = (size_t)nq * n_lists * kk, nbnd = (size_t)nq * bnd_lists * kk;
+    const size_t npair = (size_t)nq * kk * 2;  // floats / ints of one pair list
+    if (ensure(ctx->scratch, (ncand + nbnd) * 8 + 3 * npair * 4 + 1024) != 0)
+        return set_error(ctx, PION_B200_ENOMEM, "flat_i8_knn_sharded: scratch");
+    float* cv = static_cast<float*>(ctx->scratch.ptr);
+    int32_t* ci = reinterpret_cast<int32_t*>(cv + ncand);
+    float* bv = reinterpret_cast<float*>(ci + ncand);
+    int32_t* bi = reinterpret_cast<int32_t*>(bv + nbnd);
+    float* lbp = reinterpret_cast<float*>(align_up(reinterpret_cast<uintptr_t>(bi + nbnd), 256));
+    float* gbp = lbp + npair;  // the merged bound lists (pairs)
+    float* lfp = gbp + npair;  // this shard's final k per query (pairs)
+    int rc = 0;
+    const int t_all = timing_begin(ctx);
+    CUtensorMap tmap_q;
+    Fi8TcLaunch L;
+    if (n_tiles > 0) {
+        if (make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, (uint64_t)dim, (uint64_t)nq,
+                         (uint64_t)dim, (uint32_t)fi8_k_block(), (uint32_t)fi8_query_tile(),
+                         CU_TENSOR_MAP_SWIZZLE_128B) != 0)
+            return set_error(ctx, PION_B200_ECUDA, "flat_i8_knn_sharded: query tensor map");
+        L.tmap_q = &tmap_q;
+        L.tmap_rows = &ix->tmap_rows;
+        L.row_scale = ix->row_scale;
+        L.tile_rs_max = ix->tile_rs_max;
+        L.q_scale = q_scale;
+        L.n_rows = ix->n_rows;
+        L.nq = nqi;
+        L.dim = dim;
+        L.k = kk;
+        L.status = call_status(ctx, PION_B200_MEM_DEVICE);
+        L.wait_ns = ctx->wait_ns;
+        // 1. this rank's sample in bound mode, its k best chunk scores per query
+        const int t_pre = timing_begin(ctx, PION_B200_TIMING_THRESHOLD);
+        L.tile_begin = 0;
+        L.tile_end = sample;
+        L.n_splits = bnd_splits;
+        L.n_lists = bnd_lists;
+        L.cand_val = bv;
+        L.cand_idx = bi;
+        L.bound_mode = 1;
+        rc = launch_flat_i8_tc(L, st);
+        ctx->launches++;
+        if (rc == 0)
+            rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, ix->id_base, true, lbp,
+                                    reinterpret_cast<int32_t*>(lbp) + 1, st, false, 0, false, 2);
+        ctx->launches++;
+        timing_end(ctx, t_pre);
+    } else {
+        rc = launch_fill_results(lbp, reinterpret_cast<int32_t*>(lbp) + 1, (size_t)nq * kk,
+                                 -INFINITY, st, 2);
+        ctx->launches++;
+    }
+    // 2. every rank's sample lists -> one bound per query (the union's k-th best)
+    if (rc == 0)
+        rc = exchange_merge(ctx, ex, 0, lbp, nq, k, epoch, true, gbp,
+                            reinterpret_cast<int32_t*>(gbp) + 1, 2);
+    // 3. the whole shard from that bound, merged to this shard's k per query
+    if (rc == 0 && n_tiles > 0) {
+        const int t_main = timing_begin(ctx, PION_B200_TIMING_MAIN);
+        L.tile_begin = 0;
+        L.tile_end = n_tiles;
+        L.n_splits = splits;
+        L.n_lists = n_lists;
+        L.cand_val = cv;
+        L.cand_idx = ci;
+        L.thr0 = gbp + 2 * (kk - 1);
+        L.thr0_stride = 2 * kk;
+        L.bound_mode = 0;
+        rc = launch_flat_i8_tc(L, st);
+        ctx->launches++;
+        timing_end(ctx, t_main);
+        if (rc == 0)
+            rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, lfp,
+                                    reinterpret_cast<int32_t*>(lfp) + 1, st, false, 0, false, 2);
+        ctx->launches++;
+    } else if (rc == 0) {
+        rc = launch_fill_results(lfp, reinterpret_cast<int32_t*>(lfp) + 1, (size_t)nq * kk,
+                                 -INFINITY, st, 2);
+        ctx->launches++;
+    }
+    // 4. every shard's k -> the global k
+    if (rc == 0)
+        rc = exchange_merge(ctx, ex, 1, lfp, nq, k, epoch, true, out_scores, out_ids,
+                            pairs_out ? 2 : 1);
+    timing_end(ctx, t_all);
+    if (rc != 0)
+        return set_error(ctx, rc, "flat_i8_knn_sharded: failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+    return 0;
+}
+
 // --------------------------------------------------------------- utilities
 
 int pion_v_b200_quantize_rows_i8(pion_b200_ctx* ctx, const float* src, int64_t n_rows, int64_t d,

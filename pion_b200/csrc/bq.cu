@@ -618,14 +618,10 @@ __global__ void __launch_bounds__(B1_THREADS)
             int hu = h[u];
             hu += __shfl_xor_sync(0xffffffffu, hu, 1);
             hu += __shfl_xor_sync(0xffffffffu, hu, 2);
-            const bool own = r < r1 && j == 0;
-            if (own) dist[r] = (uint16_t)hu;
-            // one shared atomic per distinct distance of the warp's eight rows (nearby
-            // distances repeat: the hot bins would serialise otherwise)
-            const unsigned peers =
-                __match_any_sync(0xffffffffu, own ? (unsigned)hu : (0x40000000u | threadIdx.x));
-            if (own && (__ffs(peers) - 1) == (int)(threadIdx.x & 31))
-                atomicAdd(&b1_hist[hu], __popc(peers));
+            if (r < r1 && j == 0) {
+                dist[r] = (uint16_t)hu;
+                atomicAdd(&b1_hist[hu], 1);
+            }
         }
     }
     __syncthreads();

@@ -607,7 +607,7 @@ template <bool DESC, bool STAGED>
 __global__ void __launch_bounds__(MERGE_WARPS * 32)
     merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int es,
                        int nq, int n_lists, int k, int64_t id_offset, float* out_v,
-                       int32_t* out_i, int lists_major, int out_stride, int out_es) {
+                       int32_t* out_i, int lists_major, int out_stride, int out_es, int lm_nq) {
     __shared__ uint16_t cursor[MERGE_WARPS][STAGED ? MERGE_STAGE_ENTRIES : MERGE_MAX_LISTS];
     __shared__ float stage_v[STAGED ? MERGE_WARPS : 1][STAGED ? MERGE_STAGE_ENTRIES : 1];
     __shared__ int32_t stage_i[STAGED ? MERGE_WARPS : 1][STAGED ? MERGE_STAGE_ENTRIES : 1];
@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32)
     const float pad = DESC ? -INFINITY : INFINITY;
     // entry c of list l of query q sits at element (base + l * lstride + c) * es
     const size_t base = lists_major ? (size_t)q * k : (size_t)q * n_lists * k;
-    const size_t lstride = lists_major ? (size_t)nq * k : (size_t)k;
+    const size_t lstride = lists_major ? (size_t)lm_nq * k : (size_t)k;
     if (STAGED) {
         // eight loads in flight per lane before the first store (a query's lists are
         // one contiguous run unless lists-major)
@@ -726,7 +726,8 @@ template <bool DESC>
 __global__ void __launch_bounds__(MB_WARPS * 32)
     merge_lists_block_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci,
                              int es, int nq, int n_lists, int k, int64_t id_offset, float* out_v,
-                             int32_t* out_i, int lists_major, int out_stride, int out_es) {
+                             int32_t* out_i, int lists_major, int out_stride, int out_es,
+                             int lm_nq) {
     __shared__ float wv[MB_WARPS][MB_KMAX];
     __shared__ int32_t wi[MB_WARPS][MB_KMAX];
     __shared__ uint16_t cursor[MERGE_MAX_LISTS];
@@ -734,7 +735,7 @@ __global__ void __launch_bounds__(MB_WARPS * 32)
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float pad = DESC ? -INFINITY : INFINITY;
     const size_t base = lists_major ? (size_t)q * k : (size_t)q * n_lists * k;
-    const size_t lstride = lists_major ? (size_t)nq * k : (size_t)k;
+    const size_t lstride = lists_major ? (size_t)lm_nq * k : (size_t)k;
     for (int l = threadIdx.x; l < n_lists; l += blockDim.x) cursor[l] = 0;
     __syncthreads();
     const int l0 = (int)((int64_t)n_lists * w / MB_WARPS);
@@ -889,20 +890,22 @@ int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
                        cudaStream_t st, bool lists_major, int out_stride, bool pairs,
-                       int out_es) {
+                       int out_es, int lm_nq) {
     if (nq <= 0) return 0;
     if (n_lists < 1 || n_lists > MERGE_MAX_LISTS || k < 1 || k > 65535) return PION_B200_ESHAPE;
     if (out_stride <= 0) out_stride = k;
     const int es = pairs ? 2 : 1;
     if (pairs) ci = reinterpret_cast<const int32_t*>(cv) + 1;
     const int lm = lists_major ? 1 : 0;
+    if (lm_nq <= 0) lm_nq = nq;  // lists-major: query slots per list
+    if (lm_nq < nq) return PION_B200_ESHAPE;
     if (n_lists > 128 && k <= MB_KMAX) {  // few queries, many lists: a CTA per query
         if (descending)
             merge_lists_block_kernel<true><<<nq, MB_WARPS * 32, 0, st>>>(
-                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride, out_es);
+                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride, out_es, lm_nq);
         else
             merge_lists_block_kernel<false><<<nq, MB_WARPS * 32, 0, st>>>(
-                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride, out_es);
+                cv, ci, es, nq, n_lists, k, id_offset, out_v, out_i, lm, out_stride, out_es, lm_nq);
         return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
     }
     const int blocks = (nq + MERGE_WARPS - 1) / MERGE_WARPS;
@@ -910,7 +913,7 @@ int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, 
 #define PION_MERGE_GO(D, S)                                                              \
     merge_lists_kernel<D, S><<<blocks, MERGE_WARPS * 32, 0, st>>>(cv, ci, es, nq, n_lists, k, \
                                                                   id_offset, out_v, out_i, lm, \
-                                                                  out_stride, out_es)
+                                                                  out_stride, out_es, lm_nq)
     if (descending) {
         if (staged) PION_MERGE_GO(true, true); else PION_MERGE_GO(true, false);
     } else {

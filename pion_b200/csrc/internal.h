@@ -340,7 +340,11 @@ int launch_fill_results(float* v, int32_t* i, size_t n, float value, cudaStream_
 int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, int k,
                        int64_t id_offset, bool descending, float* out_v, int32_t* out_i,
                        cudaStream_t st, bool lists_major = false, int out_stride = 0,
-                       bool pairs = false, int out_es = 1);
+                       bool pairs = false, int out_es = 1, int lm_nq = 0);
+// ---- exchange.cu: publish this rank's pairs to every rank, wait for theirs, merge
+int exchange_merge(pion_b200_ctx* ctx, pion_b200_exchange* e, int region, const void* pairs,
+                   int64_t nq, int64_t k, uint32_t epoch, bool descending, float* out_v,
+                   int32_t* out_i, int out_es);
 // Event pair around one scoring-kernel launch (or one phase of it, `tag` =
 // PION_B200_TIMING_*) when timing is enabled.  timing_begin returns the pair's slot
 // (-1 when timing is off); timing_end closes `slot`, or the pair opened last.

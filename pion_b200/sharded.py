@@ -104,3 +104,79 @@ class ShardedSearch:
                 parts[j] += e[j].elapsed_time(e[j + 1])
         n = max(1, steps)
         return {"local_ms": parts[0] / n, "allgather_ms": parts[1] / n, "merge_ms": parts[2] / n}
+
+
+class PeerExchange:
+    """The library's NVLink peer-memory shard exchange (pion_v_b200_exchange_*): every rank
+    creates it on its own GPU, the ranks swap its IPC handles over `group` (any
+    torch.distributed backend), and each rank maps the others' receive buffers.  After
+    that no collective call is needed per step: pion_v_b200_flat_i8_knn_sharded and
+    pion_v_b200_exchange_merge move the pairs with peer stores and bounded flag waits."""
+
+    def __init__(self, ctx, max_nq: int, k: int, regions: int = 2, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        self.ctx = ctx
+        self.k = k
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.pion_v_b200_exchange_create(ctx.h, self.world, self.rank, regions,
+                                                      max_nq, k, ctypes.byref(h)))
+        self.h = h
+        mine = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        ctx.check(ctx.lib.pion_v_b200_exchange_handle(self.h, mine))
+        t = torch.tensor(list(mine), dtype=torch.uint8)
+        if self.world > 1:
+            backend = dist.get_backend(group)
+            dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else None
+            t = t.to(dev) if dev is not None else t
+            out = torch.empty(self.world * _lib.IPC_HANDLE_BYTES, dtype=torch.uint8,
+                              device=t.device)
+            dist.all_gather_into_tensor(out, t, group=group)
+            allh = bytes(out.cpu().tolist())
+        else:
+            allh = bytes(mine)
+        buf = (ctypes.c_uint8 * len(allh)).from_buffer_copy(allh)
+        ctx.check(ctx.lib.pion_v_b200_exchange_connect(self.h, buf))
+        self.epoch = 0
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.pion_v_b200_exchange_free(self.h)
+            self.h = None
+
+
+class PeerShardedSearch:
+    """One step of the row-sharded FLAT INT8 search through PeerExchange: the threshold
+    sample shared by all ranks, every shard scored, the shard lists exchanged and merged
+    (pion_v_b200_flat_i8_knn_sharded).  index: this rank's FlatI8Index (id_base = its first
+    row); inputs: [q int8 [B, dim], q_scale float32 [B]] CUDA tensors."""
+
+    def __init__(self, index, ex: PeerExchange):
+        self.ix = index
+        self.ex = ex
+        self.world = ex.world
+
+    def __call__(self, inputs):
+        import torch
+
+        from . import _lib
+        from .search import _TorchStream
+        q, qs = inputs
+        ctx = self.ix.ctx
+        nq, k = q.shape[0], self.ex.k
+        out = torch.empty((nq, k, 2), dtype=torch.int32, device=q.device)
+        with _TorchStream(ctx, _lib.MEM_DEVICE):
+            ctx.check(ctx.lib.pion_v_b200_flat_i8_knn_sharded(
+                ctx.h, self.ix.h, self.ex.h, q.data_ptr(), qs.data_ptr(), nq, k,
+                self.ex.next_epoch(), _lib.OUT_PAIRS, None, out.data_ptr()))
+        return unpack_pairs(out)
