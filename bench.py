@@ -109,10 +109,11 @@ def args_parse(argv=None):
                          "(host), batched insertion on the host, or batched insertion with "
                          "the batches' searches on the GPU (the same graph as 'batched')")
     ap.add_argument("--build-batch", type=int, default=4096)
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--exchange", choices=["peer", "peer-local", "nccl"], default="peer",
                     help="FLAT INT8 on N > 1 GPUs: the shards' lists cross NVLink through the "
                          "library's peer-memory exchange (with the threshold sample shared by "
-                         "the ranks), or through an NCCL all-gather")
+                         "the ranks, or each rank's own sample share: peer-local), or through "
+                         "an NCCL all-gather")
     ap.add_argument("--workers", type=int, default=None,
                     help="worker contexts (each its own CUDA stream) taking batches in turn; "
                          "default 3 for hnsw, 1 otherwise")
@@ -277,7 +278,9 @@ def config_of(wl, batch, world, a=None):
     c = {"workload": wl["desc"], "rows": wl["rows"], "dim": wl["dim"],
          "centres": wl["centres"], "batch": batch, "k": wl["k"], "seed": wl["seed"],
          "parallelism": f"row shards x{world}" + (
-             (" + NVLink peer exchange" if (a is None or a.exchange == "peer") and
+             ((" + NVLink peer exchange" + (" (local bounds)" if a is not None and
+                                              a.exchange == "peer-local" else ""))
+              if (a is None or a.exchange.startswith("peer")) and
               wl["kind"] == "i8" else " + NCCL all-gather") if world > 1 else ""),
          "l2": "index larger than L2 (no flush needed)"}
     if wl["kind"] == "hnsw":
@@ -360,11 +363,16 @@ class I8Workload:
                  "peak_source": f"2 x {peak_kind} dense bf16 {regime} (int8 rate = 2 x bf16 "
                                 f"on B200); int8 tera-ops counted as TFLOP",
                  "algorithmic_per_launch": ops, "kernel_ms": kern_ms,
-                 "kernel_ms_covers": "threshold pass + its merge + main pass, per search"}
+                 "kernel_ms_covers": "threshold pass + its merge + main pass, per search"
+                                    + (" + the shard exchanges" if phases and
+                                       phases.get("exchange_ms") else "")}
             if phases and phases.get("main_ms"):
                 r["main_pass_ms"] = phases["main_ms"]
                 r["threshold_pass_ms"] = phases.get("threshold_ms")
                 r["frac_main_pass"] = ops / (phases["main_ms"] / 1000.0) / 1e12 / peak
+            if phases and phases.get("exchange_ms"):
+                r["exchange_ms"] = phases["exchange_ms"]  # both exchanges, per search
+                r["exchange_wait_ms"] = phases.get("exchange_wait_ms")
             return r
         # one query (the scan) or too few for the rows' bytes to be hidden: every row
         # streams from HBM once per batch
@@ -1074,10 +1082,11 @@ def run_ours(a, wl):
 
     if getattr(W, "replicas", False):
         step = W.search
-    elif world > 1 and wl["kind"] == "i8" and a.exchange == "peer":
+    elif world > 1 and wl["kind"] == "i8" and a.exchange.startswith("peer"):
         # the library's NVLink peer exchange: shared threshold sample, one call per step
         from pion_b200.sharded import PeerExchange, PeerShardedSearch
-        step = PeerShardedSearch(W.ix, PeerExchange(ctx, batch, k))
+        step = PeerShardedSearch(W.ix, PeerExchange(ctx, batch, k),
+                                 local_bound=a.exchange == "peer-local")
     else:
         step = ShardedSearch(W.search, k, merge, local_pairs=getattr(W, "search_pairs", None))
     workers = a.workers or (3 if wl["kind"] in ("hnsw", "quant") else 1)
@@ -1129,10 +1138,12 @@ def run_ours(a, wl):
         elapsed = ev0.elapsed_time(ev1)
         launches = sum(c_.launches for c_ in ctxs) - launches0
         kern_ms, kern_n = 0.0, 0
-        phase_ms = {"threshold_ms": 0.0, "main_ms": 0.0}
+        phase_ms = {"threshold_ms": 0.0, "main_ms": 0.0, "exchange_ms": 0.0,
+                    "exchange_wait_ms": 0.0}
         for c_ in ctxs:
             km, kn = c_.timing_read()
-            for tag, key in ((1, "threshold_ms"), (2, "main_ms")):
+            for tag, key in ((1, "threshold_ms"), (2, "main_ms"), (3, "exchange_ms"),
+                             (4, "exchange_wait_ms")):
                 pm, pn = c_.timing_read(tag)
                 phase_ms[key] += pm / max(1, kn)
             c_.timing(False)
@@ -1204,12 +1215,14 @@ def run_ours(a, wl):
         # ---- max over ranks
         bd = [breakdown[x] for x in ("local_ms", "allgather_ms", "merge_ms")] if breakdown else [0.0] * 3
         t = torch.tensor([elapsed, e2e_ms, kern_ms / max(1, kern_n), phase_ms["threshold_ms"],
-                          phase_ms["main_ms"], *bd], device=dev, dtype=torch.float64)
+                          phase_ms["main_ms"], phase_ms["exchange_ms"],
+                          phase_ms["exchange_wait_ms"], *bd], device=dev, dtype=torch.float64)
         lt = torch.tensor([launches], device=dev, dtype=torch.int64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             dist.all_reduce(lt, op=dist.ReduceOp.SUM)
-        elapsed, e2e_ms, kern_avg_ms, thr_ms, main_ms, bd_local, bd_ag, bd_merge = t.tolist()
+        (elapsed, e2e_ms, kern_avg_ms, thr_ms, main_ms, ex_ms, exw_ms, bd_local, bd_ag,
+         bd_merge) = t.tolist()
         launches = int(lt.item())
 
         line = None
@@ -1220,7 +1233,8 @@ def run_ours(a, wl):
             peaks, peak_kind = measured_peaks()
             regime, why = choose_regime(elapsed / 1000.0, clk)
             roof = W.roofline(hi - lo, kern_avg_ms, peaks, peak_kind, regime=regime,
-                              phases={"threshold_ms": thr_ms, "main_ms": main_ms})
+                              phases={"threshold_ms": thr_ms, "main_ms": main_ms,
+                                      "exchange_ms": ex_ms, "exchange_wait_ms": exw_ms})
             roof["regime_reason"] = why
             roof["traffic"] = profiled_traffic(f"{a.workload}_{world}")
             line = {

@@ -269,6 +269,10 @@ int pion_v_b200_timing_read(pion_b200_ctx *ctx, double *total_ms, int64_t *count
 #define PION_B200_TIMING_SCORING 0
 #define PION_B200_TIMING_THRESHOLD 1
 #define PION_B200_TIMING_MAIN 2
+/* pion_v_b200_flat_i8_knn_sharded: each exchange (publish, wait, merge), and within it the
+ * wait-and-merge kernel alone (which holds the time spent waiting for the other ranks). */
+#define PION_B200_TIMING_EXCHANGE 3
+#define PION_B200_TIMING_EXCHANGE_WAIT 4
 int pion_v_b200_timing_read_tag(pion_b200_ctx *ctx, int tag, double *total_ms, int64_t *count);
 
 /* ------------------------------------------------------------ any index kind -- */
@@ -439,7 +443,10 @@ int pion_v_b200_exchange_merge(pion_b200_ctx *ctx, pion_b200_exchange *ex, const
  * rank's sample: a lower bound of the global k-th score), every rank scores its whole
  * shard from that bound, and the ranks exchange and merge their k-lists: out_scores /
  * out_ids (or pairs with PION_B200_OUT_PAIRS) hold the global top k by (score desc, id
- * asc) on every rank. */
+ * asc) on every rank.  With PION_B200_SHARD_LOCAL_BOUND each rank starts its shard from
+ * the k-th best of its own sample share instead (no exchange before the main pass: one
+ * exchange per call; the same results). */
+#define PION_B200_SHARD_LOCAL_BOUND 0x200
 int pion_v_b200_flat_i8_knn_sharded(pion_b200_ctx *ctx, const pion_b200_index *ix,
                                     pion_b200_exchange *ex, const int8_t *q, const float *q_scale,
                                     int64_t nq, int64_t k, uint32_t epoch, int flags,

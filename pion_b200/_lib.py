@@ -25,6 +25,7 @@ MEM_HOST = 0
 MEM_DEVICE = 1
 MEM_DEVICE_BORROW = 2
 OUT_PAIRS = 0x100
+SHARD_LOCAL_BOUND = 0x200
 
 MERGE_DESC = 1
 MERGE_LISTS_MAJOR = 2

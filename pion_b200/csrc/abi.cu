@@ -501,12 +501,12 @@ static int forced_i8_path() {
     return e ? atoi(e) : 0;
 }
 
+}  // extern "C"
+
 // Index tiles scored by the threshold pre-pass: 8 tiles (2048 rows) per result
 // slot, at least 64 tiles (16384 rows) -- enough that the sample's k-th score is
 // close to the final one on clustered data, where a query's neighbours are a small
 // fraction of the rows.
-}  // extern "C"
-
 int pion::prepass_tiles(int k) { return k * 8 > 64 ? k * 8 : 64; }
 
 // Tiles sampled by the threshold pass: about 1/6 of the index (the main pass scores
@@ -743,7 +743,10 @@ int pion_v_b200_flat_i8_knn_sharded(pion_b200_ctx* ctx, const pion_b200_index* i
     // this rank's share of the sample one index of the whole would take
     int sample = 0;
     if (n_tiles > 0) {
-        sample = (bound_tiles(n_tiles * world, kk) + world - 1) / world;
+        int total = bound_tiles(n_tiles * world, kk);
+        const char* e = getenv("PION_B200_I8_SAMPLE");  // tuning hook, as in flat_i8_knn
+        if (e && atoi(e) > 0) total = atoi(e);
+        sample = (total + world - 1) / world;
         sample = sample < 2 ? 2 : sample;
         sample = sample > n_tiles ? n_tiles : sample;
     }
@@ -794,18 +797,27 @@ int pion_v_b200_flat_i8_knn_sharded(pion_b200_ctx* ctx, const pion_b200_index* i
         L.bound_mode = 1;
         rc = launch_flat_i8_tc(L, st);
         ctx->launches++;
-        if (rc == 0)
-            rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, ix->id_base, true, lbp,
-                                    reinterpret_cast<int32_t*>(lbp) + 1, st, false, 0, false, 2);
-        ctx->launches++;
         timing_end(ctx, t_pre);
     } else {
         rc = launch_fill_results(lbp, reinterpret_cast<int32_t*>(lbp) + 1, (size_t)nq * kk,
                                  -INFINITY, st, 2);
         ctx->launches++;
     }
-    // 2. every rank's sample lists -> one bound per query (the union's k-th best)
-    if (rc == 0)
+    // 2. every rank's sample lists -> one bound per query (the union's k-th best); the
+    // local merge publishes its result straight into every rank's receive buffer
+    const bool local_bound = (flags & PION_B200_SHARD_LOCAL_BOUND) != 0;
+    const bool fused_bnd = n_tiles > 0 && bnd_lists <= exchange_max_lists() && !local_bound;
+    if (rc == 0 && n_tiles > 0 && !fused_bnd) {
+        rc = launch_merge_lists(bv, bi, nqi, bnd_lists, kk, ix->id_base, true, lbp,
+                                reinterpret_cast<int32_t*>(lbp) + 1, st, false, 0, false, 2);
+        ctx->launches++;
+    }
+    if (rc == 0 && local_bound)
+        gbp = lbp;  // this rank's own sample bound
+    else if (rc == 0 && fused_bnd)
+        rc = exchange_lists_merge(ctx, ex, 0, bv, bi, bnd_lists, ix->id_base, nq, k, epoch, true,
+                                  gbp, reinterpret_cast<int32_t*>(gbp) + 1, 2);
+    else if (rc == 0)
         rc = exchange_merge(ctx, ex, 0, lbp, nq, k, epoch, true, gbp,
                             reinterpret_cast<int32_t*>(gbp) + 1, 2);
     // 3. the whole shard from that bound, merged to this shard's k per query
@@ -823,17 +835,22 @@ int pion_v_b200_flat_i8_knn_sharded(pion_b200_ctx* ctx, const pion_b200_index* i
         rc = launch_flat_i8_tc(L, st);
         ctx->launches++;
         timing_end(ctx, t_main);
-        if (rc == 0)
-            rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, lfp,
-                                    reinterpret_cast<int32_t*>(lfp) + 1, st, false, 0, false, 2);
+    }
+    // 4. every shard's k -> the global k
+    const bool fused_fin = n_tiles > 0 && n_lists <= exchange_max_lists();
+    if (rc == 0 && n_tiles > 0 && !fused_fin) {
+        rc = launch_merge_lists(cv, ci, nqi, n_lists, kk, ix->id_base, true, lfp,
+                                reinterpret_cast<int32_t*>(lfp) + 1, st, false, 0, false, 2);
         ctx->launches++;
-    } else if (rc == 0) {
+    } else if (rc == 0 && n_tiles == 0) {
         rc = launch_fill_results(lfp, reinterpret_cast<int32_t*>(lfp) + 1, (size_t)nq * kk,
                                  -INFINITY, st, 2);
         ctx->launches++;
     }
-    // 4. every shard's k -> the global k
-    if (rc == 0)
+    if (rc == 0 && fused_fin)
+        rc = exchange_lists_merge(ctx, ex, 1, cv, ci, n_lists, ix->id_base, nq, k, epoch, true,
+                                  out_scores, out_ids, pairs_out ? 2 : 1);
+    else if (rc == 0)
         rc = exchange_merge(ctx, ex, 1, lfp, nq, k, epoch, true, out_scores, out_ids,
                             pairs_out ? 2 : 1);
     timing_end(ctx, t_all);

@@ -335,4 +335,14 @@ __device__ __forceinline__ bool better_desc(float sa, int32_t ia, float sb, int3
     return ia < ib;
 }
 
+// (score desc, id asc) when DESC, else (score asc, id asc); a padding id (< 0) last.
+template <bool DESC>
+__device__ __forceinline__ bool merge_better(float sa, int32_t ia, float sb, int32_t ib) {
+    if (DESC) return better_desc(sa, ia, sb, ib);
+    if (sa != sb) return sa < sb;
+    if (ia < 0) return false;
+    if (ib < 0) return true;
+    return ia < ib;
+}
+
 }  // namespace pion

@@ -594,15 +594,6 @@ constexpr int MERGE_WARPS = 4;
 constexpr int MERGE_MAX_LISTS = 2048;
 constexpr int MERGE_STAGE_ENTRIES = 1024;  // per warp: 8 KB of staged pairs
 
-template <bool DESC>
-__device__ __forceinline__ bool merge_better(float sa, int32_t ia, float sb, int32_t ib) {
-    if (DESC) return better_desc(sa, ia, sb, ib);
-    if (sa != sb) return sa < sb;
-    if (ia < 0) return false;
-    if (ib < 0) return true;
-    return ia < ib;
-}
-
 template <bool DESC, bool STAGED>
 __global__ void __launch_bounds__(MERGE_WARPS * 32)
     merge_lists_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci, int es,

@@ -345,6 +345,14 @@ int launch_merge_lists(const float* cv, const int32_t* ci, int nq, int n_lists, 
 int exchange_merge(pion_b200_ctx* ctx, pion_b200_exchange* e, int region, const void* pairs,
                    int64_t nq, int64_t k, uint32_t epoch, bool descending, float* out_v,
                    int32_t* out_i, int out_es);
+// The largest n_lists exchange_lists_merge takes.
+int exchange_max_lists();
+// The same from this shard's candidate lists [nq][n_lists][k]: merged, offset by
+// id_offset and published by one kernel, then waited for and merged by another.
+int exchange_lists_merge(pion_b200_ctx* ctx, pion_b200_exchange* e, int region,
+                         const float* cv, const int32_t* ci, int n_lists, int64_t id_offset,
+                         int64_t nq, int64_t k, uint32_t epoch, bool descending, float* out_v,
+                         int32_t* out_i, int out_es);
 // Event pair around one scoring-kernel launch (or one phase of it, `tag` =
 // PION_B200_TIMING_*) when timing is enabled.  timing_begin returns the pair's slot
 // (-1 when timing is off); timing_end closes `slot`, or the pair opened last.

@@ -159,12 +159,15 @@ class PeerShardedSearch:
     """One step of the row-sharded FLAT INT8 search through PeerExchange: the threshold
     sample shared by all ranks, every shard scored, the shard lists exchanged and merged
     (pion_v_b200_flat_i8_knn_sharded).  index: this rank's FlatI8Index (id_base = its first
-    row); inputs: [q int8 [B, dim], q_scale float32 [B]] CUDA tensors."""
+    row); inputs: [q int8 [B, dim], q_scale float32 [B]] CUDA tensors.  local_bound: each
+    rank starts from its own sample share's bound (one exchange per step instead of two)."""
 
-    def __init__(self, index, ex: PeerExchange):
+    def __init__(self, index, ex: PeerExchange, local_bound: bool = False):
+        from . import _lib
         self.ix = index
         self.ex = ex
         self.world = ex.world
+        self.flags = _lib.OUT_PAIRS | (_lib.SHARD_LOCAL_BOUND if local_bound else 0)
 
     def __call__(self, inputs):
         import torch
@@ -178,5 +181,5 @@ class PeerShardedSearch:
         with _TorchStream(ctx, _lib.MEM_DEVICE):
             ctx.check(ctx.lib.pion_v_b200_flat_i8_knn_sharded(
                 ctx.h, self.ix.h, self.ex.h, q.data_ptr(), qs.data_ptr(), nq, k,
-                self.ex.next_epoch(), _lib.OUT_PAIRS, None, out.data_ptr()))
+                self.ex.next_epoch(), self.flags, None, out.data_ptr()))
         return unpack_pairs(out)

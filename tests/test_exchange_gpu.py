@@ -1,7 +1,8 @@
 """The NVLink peer-memory shard exchange on two GPUs (skipped with fewer): each rank holds
 a row shard, pion_v_b200_flat_i8_knn_sharded shares the threshold sample, scores the shard
-and exchanges the k-lists; every rank must return the single index's answer, step after
-step (the receive buffers alternate by the step's parity).  The ranks are processes, one
+and exchanges the k-lists (or starts from its own sample share's bound and exchanges once);
+every rank must return the single index's answer, step after step (the receive buffers
+alternate by the step's parity).  The ranks are processes, one
 per GPU, swapping the IPC handles over gloo."""
 import os
 import socket
@@ -14,6 +15,8 @@ from pion_b200.workloads import mixture_np
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# (batch, local bound) per step: the exchange's parities and regions in every order
+CASES = ((300, 0), (1, 0), (130, 0), (300, 1), (7, 1), (130, 0), (64, 1))
 
 
 def _free_port():
@@ -46,11 +49,10 @@ def _rank(rank, world, port, out_dir):
         ix = pion_b200.FlatI8Index(ctx, torch.from_numpy(keys[lo:hi]).cuda(),
                                    torch.from_numpy(ks[lo:hi]).cuda(), id_base=lo)
         ex = PeerExchange(ctx, 512, 10)
-        step = PeerShardedSearch(ix, ex)
+        steps = (PeerShardedSearch(ix, ex), PeerShardedSearch(ix, ex, local_bound=True))
         dq, dqs = torch.from_numpy(q).cuda(), torch.from_numpy(qs).cuda()
-        for s in range(3):  # both parities, twice
-            b = (300, 1, 130)[s]
-            ids, sc = step([dq[:b].contiguous(), dqs[:b].contiguous()])
+        for s, (b, local) in enumerate(CASES):  # both parities, both bounds
+            ids, sc = steps[local]([dq[:b].contiguous(), dqs[:b].contiguous()])
             torch.cuda.synchronize()
             ctx.sync()
             np.save(os.path.join(out_dir, f"r{rank}_s{s}_ids.npy"), ids.cpu().numpy())
@@ -73,7 +75,7 @@ def test_two_gpu_peer_exchange_equals_single_index(oracle, tmp_path):
     keys, ks = oracle.pkm_quantize_rows_i8(rows)
     q, qs = oracle.pkm_quantize_rows_i8(qf)
     oi, ov = oracle.flat_i8_knn(keys, ks, q, qs, 10)
-    for s, b in enumerate((300, 1, 130)):
+    for s, (b, _) in enumerate(CASES):
         for r in range(2):
             ids = np.load(tmp_path / f"r{r}_s{s}_ids.npy")
             sc = np.load(tmp_path / f"r{r}_s{s}_sc.npy")
