@@ -22,6 +22,20 @@ int forced_bq_path() {
     return e ? atoi(e) : 0;
 }
 
+// PION_B200_BQ_RERANK=1 keeps the one-query rerank on the spread-rows kernel pair
+// (tests compare it with the staged kernel).
+int forced_rerank_path() {
+    const char* e = getenv("PION_B200_BQ_RERANK");
+    return e ? atoi(e) : 0;
+}
+
+// PION_B200_BQ_STREAM=1 keeps the one-query first pass on the register kernel (tests
+// compare it with the shared-memory staged one).
+int forced_stream_path() {
+    const char* e = getenv("PION_B200_BQ_STREAM");
+    return e ? atoi(e) : 0;
+}
+
 // PION_B200_BQ_EXACT=1 sends every query through the exact popcount scan (tests).
 int force_fallback() {
     const char* e = getenv("PION_B200_BQ_EXACT");
@@ -156,6 +170,8 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
     }
     int rc = 0;
     const int path = forced_bq_path();
+    const int rerank_path = forced_rerank_path();
+    const int stream_path = forced_stream_path();
     const bool scan1 = ix->n_rows > 0 && bq_scan1_supported(words, S) &&
                        (path == 1 || (path == 0 && nq == 1));
     if (ix->n_rows == 0) {
@@ -163,7 +179,7 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
         ctx->launches++;
     } else if (scan1) {
         // One query: the popcount stream over the packed codes, then the same rerank.
-        const int ctas = bq_scan1_ctas(ix->n_rows, ctx->num_sms);
+        const int ctas = bq_scan1_ctas(ix->n_rows, words, ctx->num_sms, stream_path);
         size_t off = 0;
         auto take = [&](size_t bytes) {
             size_t o = off;
@@ -171,9 +187,10 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
             return o;
         };
         const size_t o_qn = take((size_t)nq * dim * 4), o_qnorm = take((size_t)nq * 4),
-                     o_qpm = take((size_t)nq * dim), o_qc = take((size_t)nq * words * 8),
+                     o_qc = take((size_t)nq * words * 8),
                      o_slid = take((size_t)nq * S * 4), o_slh = take((size_t)nq * S * 2),
                      o_sln = take((size_t)nq * 4), o_rd = take((size_t)nq * S * 4),
+                     o_done = take((size_t)nq * 4),
                      o_work = take(bq_scan1_scratch(ix->n_rows, words));
         if (ensure(ctx->scratch, off) != 0)
             return set_error(ctx, PION_B200_ENOMEM, "bq_rerank_knn: scratch");
@@ -185,18 +202,23 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
         int* sl_n = reinterpret_cast<int*>(base + o_sln);
         const int t_all = timing_begin(ctx);
         rc = launch_query_normalize(dq, nqi, dim, qn, reinterpret_cast<float*>(base + o_qnorm),
-                                    st);
-        if (rc == 0) rc = launch_signs(qn, nq, dim, reinterpret_cast<int8_t*>(base + o_qpm), qc, st);
-        ctx->launches += 2;
+                                    st, nullptr, qc);
+        ctx->launches++;
         for (int64_t t = 0; t < nq && rc == 0; ++t) {
             rc = launch_bq_scan1(ix->codes, ix->n_rows, words, qc + (size_t)t * words, S, ctas,
                                  base + o_work, sl_id + (size_t)t * S, sl_h + (size_t)t * S,
-                                 sl_n + t, st);
+                                 sl_n + t, call_status(ctx, mem), ctx->wait_ns, stream_path,
+                                 st);
             ctx->launches += 3;
         }
         timing_end(ctx, t_all);
         if (rc == 0) {
-            if (dim % 16 == 0)
+            if (dim % 16 == 0 && rerank_path != 1)
+                rc = launch_bq_rerank_staged(ix->rows_f32, dim, qn, sl_id, sl_n, S, nqi, kk,
+                                             ix->id_base, reinterpret_cast<float*>(base + o_rd),
+                                             reinterpret_cast<unsigned*>(base + o_done),
+                                             call_status(ctx, mem), ctx->wait_ns, dv, di, st);
+            else if (dim % 16 == 0)
                 rc = launch_bq_rerank_wide(ix->rows_f32, dim, qn, sl_id, sl_n, S, nqi, kk,
                                            ix->id_base, reinterpret_cast<float*>(base + o_rd),
                                            dv, di, st);
@@ -250,9 +272,8 @@ int pion_v_b200_bq_rerank_knn(pion_b200_ctx* ctx, const pion_b200_index* ix, con
         int* sl_n = reinterpret_cast<int*>(base + o_sln);
         int* flags = reinterpret_cast<int*>(base + o_flag);  // [0] count, then query ids
         timing_begin(ctx);
-        rc = launch_query_normalize(dq, nqi, dim, qn, qnorm, st);
-        if (rc == 0) rc = launch_signs(qn, nq, dim, qpm, qc, st);
-        ctx->launches += 2;
+        rc = launch_query_normalize(dq, nqi, dim, qn, qnorm, st, qpm, qc);
+        ctx->launches++;
         CUtensorMap tmap_q;
         if (rc == 0 && make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qpm, (uint64_t)dim,
                                     (uint64_t)nq, (uint64_t)dim, (uint32_t)bq_k_block(),

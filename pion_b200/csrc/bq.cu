@@ -553,10 +553,47 @@ __device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
     return v;
 }
 
+// Adds this CTA's shared histogram into the global one, bins 0..this CTA's own want-th
+// smallest distance only: the global want-th smallest D* is at most every CTA's, so every
+// bin <= D* still gets every CTA's count, and the bins above D* are never read.  (Adding
+// every nonzero bin made the CTAs queue on the same few L2 lines at the end.)  Called by
+// all B1_THREADS threads after a barrier.
+__device__ void flush_hist_truncated(const int* b1_hist, int dim, int want, int* hist) {
+    __shared__ int warp_tot[B1_THREADS / 32];
+    __shared__ int cut;
+    const int per = (dim + 1 + B1_THREADS - 1) / B1_THREADS;
+    const int lo = threadIdx.x * per;
+    int sum = 0;
+    for (int i = lo; i < lo + per && i <= dim; ++i) sum += b1_hist[i];
+    int incl = sum;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[w] = incl;
+    if (threadIdx.x == 0) cut = dim;
+    __syncthreads();
+    for (int v = 0; v < w; ++v) incl += warp_tot[v];
+    const int excl = incl - sum;
+    if (excl < want && incl >= want) {  // the crossing is in this thread's bins
+        int acc = excl, d = lo;
+        for (; d < lo + per && d <= dim; ++d) {
+            acc += b1_hist[d];
+            if (acc >= want) break;
+        }
+        cut = d;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i <= cut; i += B1_THREADS)
+        if (b1_hist[i]) atomicAdd(&hist[i], b1_hist[i]);
+}
+
 // Pass 1: dist[r] and the global histogram (hist[0..dim], zeroed by the caller).
 __global__ void __launch_bounds__(B1_THREADS)
     bq_scan1_hist_kernel(const uint64_t* __restrict__ codes, int64_t n_rows, int words,
-                         const uint64_t* __restrict__ qcode, int64_t rows_per_cta,
+                         const uint64_t* __restrict__ qcode, int64_t rows_per_cta, int want,
                          uint16_t* __restrict__ dist, int* __restrict__ hist) {
     extern __shared__ int b1_hist[];  // dim + 1 bins
     __shared__ uint4 qv[B1_MAX_WORDS / 2];
@@ -625,8 +662,107 @@ __global__ void __launch_bounds__(B1_THREADS)
         }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i <= dim; i += B1_THREADS)
-        if (b1_hist[i]) atomicAdd(&hist[i], b1_hist[i]);
+    flush_hist_truncated(b1_hist, dim, want, hist);
+}
+
+// Pass 1 through shared memory, for rows of at most B1S_MAX_ROW_BYTES: each CTA streams
+// its contiguous row range in stages of B1S_ROWS rows, one bulk copy per stage
+// (cp.async.bulk, completing on the stage's mbarrier) and B1S_STAGES stages in flight, so
+// the bytes in flight do not depend on registers; 4 lanes per row then popcount from
+// shared memory.  Same outputs as bq_scan1_hist_kernel.
+constexpr int B1S_ROWS = 128;
+constexpr int B1S_STAGES = 4;
+constexpr int B1S_MAX_ROW_BYTES = 384;  // dim <= 3072
+
+__global__ void __launch_bounds__(B1_THREADS)
+    bq_scan1_stream_kernel(const uint64_t* __restrict__ codes, int64_t n_rows, int words,
+                           const uint64_t* __restrict__ qcode, int64_t rows_per_cta, int want,
+                           uint16_t* __restrict__ dist, int* __restrict__ hist, int* status,
+                           uint64_t wait_ns) {
+    extern __shared__ __align__(128) uint8_t b1s_smem[];
+    const int dim = words * 64;
+    const int row_bytes = words * 8;
+    const int chunks = words >> 1;
+    uint8_t* ring = b1s_smem;
+    int* b1_hist = reinterpret_cast<int*>(ring + (size_t)B1S_STAGES * B1S_ROWS * row_bytes);
+    uint4* qv = reinterpret_cast<uint4*>(b1_hist + ((dim + 1 + 3) & ~3));
+    uint64_t* full = reinterpret_cast<uint64_t*>(qv + chunks);
+    __shared__ int abort_flag;
+    for (int i = threadIdx.x; i <= dim; i += B1_THREADS) b1_hist[i] = 0;
+    for (int c = threadIdx.x; c < chunks; c += B1_THREADS)
+        qv[c] = reinterpret_cast<const uint4*>(qcode)[c];
+    const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > n_rows) r1 = n_rows;
+    const int n_stages = r1 > r0 ? (int)((r1 - r0 + B1S_ROWS - 1) / B1S_ROWS) : 0;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < B1S_STAGES; ++s) mbar_init(&full[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    auto issue = [&](int it) {  // thread 0: stage `it` of this CTA's range into its slot
+        const int64_t a = r0 + (int64_t)it * B1S_ROWS;
+        const int64_t b = a + B1S_ROWS < r1 ? a + B1S_ROWS : r1;
+        const uint32_t bytes = (uint32_t)((b - a) * row_bytes);
+        uint64_t* bar = &full[it % B1S_STAGES];
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_load(ring + (size_t)(it % B1S_STAGES) * B1S_ROWS * row_bytes,
+                  reinterpret_cast<const uint8_t*>(codes) + a * row_bytes, bytes, bar);
+    };
+    if (threadIdx.x == 0)
+        for (int it = 0; it < B1S_STAGES && it < n_stages; ++it) issue(it);
+    const int g = threadIdx.x >> 2, j = threadIdx.x & 3;
+    int it = 0;
+    for (; it < n_stages; ++it) {
+        const int slot = it % B1S_STAGES;
+        if (!mbar_wait(&full[slot], (uint32_t)((it / B1S_STAGES) & 1), status, &abort_flag,
+                       wait_ns))
+            break;
+        const uint8_t* st = ring + (size_t)slot * B1S_ROWS * row_bytes;
+        const int64_t base = r0 + (int64_t)it * B1S_ROWS;
+#pragma unroll
+        for (int u = 0; u < B1S_ROWS / B1_GROUPS; ++u) {
+            const int rr = u * B1_GROUPS + g;
+            const int64_t r = base + rr;
+            const uint4* rp = reinterpret_cast<const uint4*>(st + (size_t)rr * row_bytes);
+            int h = 0;
+            if (r < r1)
+                for (int c = j; c < chunks; c += 4) {
+                    const uint4 a = rp[c];
+                    const uint4 b = qv[c];
+                    h += __popc(a.x ^ b.x) + __popc(a.y ^ b.y) + __popc(a.z ^ b.z) +
+                         __popc(a.w ^ b.w);
+                }
+            h += __shfl_xor_sync(0xffffffffu, h, 1);
+            h += __shfl_xor_sync(0xffffffffu, h, 2);
+            if (r < r1 && j == 0) {
+                dist[r] = (uint16_t)h;
+                atomicAdd(&b1_hist[h], 1);
+            }
+        }
+        __syncthreads();  // every thread is done with the slot: refill it
+        if (threadIdx.x == 0 && it + B1S_STAGES < n_stages) issue(it + B1S_STAGES);
+    }
+    if (it < n_stages) {
+        // a wait ran out: let the copies already issued land before the CTA exits
+        if (threadIdx.x == 0) {
+            const int last = n_stages < it + B1S_STAGES ? n_stages : it + B1S_STAGES;
+            for (int t = it; t < last; ++t)
+                mbar_wait(&full[t % B1S_STAGES], (uint32_t)((t / B1S_STAGES) & 1), nullptr,
+                          nullptr, wait_ns);
+        }
+        __syncthreads();
+        return;
+    }
+    __syncthreads();
+    flush_hist_truncated(b1_hist, dim, want, hist);
+}
+
+size_t b1s_smem_bytes(int words) {
+    const int dim = words * 64;
+    return (size_t)B1S_STAGES * B1S_ROWS * words * 8 + (size_t)((dim + 1 + 3) & ~3) * 4 +
+           (size_t)(words >> 1) * 16 + B1S_STAGES * 8;
 }
 
 // D* = the smallest d with #(dist <= d) >= want, and #(dist < D*), by one CTA's scan
@@ -805,6 +941,116 @@ __global__ void __launch_bounds__(128)
     }
 }
 
+// Rerank for few queries with the shortlist rows staged in shared memory: a one-warp CTA
+// per 8 shortlist rows pulls them in with one bulk copy each (all in flight at once, one
+// DRAM round trip), then 4 lanes per row run the reference's 4-chain dot from shared
+// memory (lane j = chain j, the same transpose and sums as dot4chain_quad); the last CTA
+// of a query to finish picks the k best by (distance, shortlist position).
+constexpr int RS_ROWS = 8;
+constexpr int RS_PAD = 16;  // floats between staged rows (rows 64 B apart in the banks)
+
+__global__ void __launch_bounds__(32)
+    bq_rerank_staged_kernel(const float* __restrict__ rows, int dim, const float* __restrict__ qn,
+                            const int32_t* __restrict__ sl_id, const int* __restrict__ sl_n,
+                            int S, int k, int64_t id_base, float* dist, unsigned* done,
+                            int* status, uint64_t wait_ns, float* __restrict__ out_d,
+                            int32_t* __restrict__ out_i) {
+    extern __shared__ __align__(16) uint8_t rs_smem[];
+    const int pitch = dim + RS_PAD;
+    float4* qs = reinterpret_cast<float4*>(rs_smem);
+    float* rsm = reinterpret_cast<float*>(rs_smem + (size_t)dim * 4);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(rs_smem + (size_t)dim * 4 +
+                                                (size_t)RS_ROWS * pitch * 4);
+    const int q = blockIdx.y, lane = threadIdx.x;
+    const int n = sl_n[q];
+    const int j0 = blockIdx.x * RS_ROWS;
+    const int nr = n - j0 < 0 ? 0 : (n - j0 > RS_ROWS ? RS_ROWS : n - j0);
+    if (nr > 0) {
+        if (lane == 0) {
+            mbar_init(bar, 1);
+            fence_barrier_init();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(nr * dim * 4));
+        __syncwarp();
+        if (lane < nr)
+            bulk_load(rsm + (size_t)lane * pitch,
+                      rows + (size_t)sl_id[(size_t)q * S + j0 + lane] * dim, (uint32_t)dim * 4,
+                      bar);
+        for (int c = lane; c < (dim >> 2); c += 32)
+            qs[c] = reinterpret_cast<const float4*>(qn + (size_t)q * dim)[c];
+        __syncwarp();
+        bool ok = mbar_wait(bar, 0, status, nullptr, wait_ns);
+        if (!ok) mbar_wait(bar, 0, nullptr, nullptr, wait_ns);  // let the copies land
+        ok = __all_sync(0xffffffffu, ok);
+        const int r = lane >> 2, j = lane & 3;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        if (ok && r < nr) {
+            const float4* rp = reinterpret_cast<const float4*>(rsm + (size_t)r * pitch) + j;
+            const int steps = dim >> 4;
+#pragma unroll 8
+            for (int i = 0; i < steps; ++i) {
+                const float4 v = rp[i * 4];
+                const float4 qv = qs[i * 4 + j];
+                a0 = __fadd_rn(__fmul_rn(qv.x, v.x), a0);
+                a1 = __fadd_rn(__fmul_rn(qv.y, v.y), a1);
+                a2 = __fadd_rn(__fmul_rn(qv.z, v.z), a2);
+                a3 = __fadd_rn(__fmul_rn(qv.w, v.w), a3);
+            }
+        }
+        const int gbase = lane & ~3;
+        const float own = sel4(a0, a1, a2, a3, j);
+        const float r1 = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 1), 1);
+        const float r2 = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 2), 2);
+        const float r3 = __shfl_xor_sync(0xffffffffu, sel4(a0, a1, a2, a3, j ^ 3), 3);
+        const float c0 = sel4(own, r1, r2, r3, j ^ 0);
+        const float c1 = sel4(own, r1, r2, r3, j ^ 1);
+        const float c2 = sel4(own, r1, r2, r3, j ^ 2);
+        const float c3 = sel4(own, r1, r2, r3, j ^ 3);
+        const float t = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+        const float t0 = __shfl_sync(0xffffffffu, t, gbase + 0);
+        const float t1 = __shfl_sync(0xffffffffu, t, gbase + 1);
+        const float t2 = __shfl_sync(0xffffffffu, t, gbase + 2);
+        const float t3 = __shfl_sync(0xffffffffu, t, gbase + 3);
+        const float dot = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+        if (r < nr && j == 0) dist[(size_t)q * S + j0 + r] = __fsub_rn(1.0f, dot);
+        __threadfence();
+    }
+    unsigned last = 0;
+    if (lane == 0) last = atomicAdd(&done[q], 1u) == gridDim.x - 1 ? 1u : 0u;
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    __threadfence();
+    if (lane == 0) done[q] = 0;  // ready for the next call (stream-ordered)
+    float* dl = rsm;             // n <= 256 distances fit in the staged rows' room
+    for (int j = lane; j < n; j += 32) dl[j] = __ldcg(dist + (size_t)q * S + j);
+    __syncwarp();
+    for (int rr = 0; rr < k; ++rr) {
+        float bd = INFINITY;
+        int bp = -1;
+        for (int j = lane; j < n; j += 32)
+            if (dl[j] == dl[j] && (bp < 0 || dl[j] < bd)) {  // first (lowest j) wins ties
+                bd = dl[j];
+                bp = j;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float od = __shfl_xor_sync(0xffffffffu, bd, o);
+            const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+            if (op >= 0 && (bp < 0 || od < bd || (od == bd && op < bp))) {
+                bd = od;
+                bp = op;
+            }
+        }
+        if (lane == 0) {
+            out_d[(size_t)q * k + rr] = bp >= 0 ? bd : INFINITY;
+            out_i[(size_t)q * k + rr] =
+                bp >= 0 ? (int32_t)(sl_id[(size_t)q * S + bp] + id_base) : -1;
+        }
+        if (bp >= 0 && lane == (bp & 31)) dl[bp] = __int_as_float(0x7fffffff);  // taken (NaN)
+        __syncwarp();
+    }
+}
+
 }  // namespace bq
 
 // =========================================================== host launchers ==
@@ -813,8 +1059,28 @@ bool bq_scan1_supported(int words, int S) {
     return words % 2 == 0 && words <= bq::B1_MAX_WORDS && S >= 1 && S <= 512;
 }
 
-int bq_scan1_ctas(int64_t n_rows, int num_sms) {
-    int64_t ctas = (int64_t)num_sms * 4;
+// One full wave of the first pass: as many CTAs as fit on the SMs at once (the register
+// pass's 84 registers a thread allow 2 CTAs of 256 threads per SM; the staged pass's
+// ~105 KB of shared memory also 2).
+int bq_scan1_ctas(int64_t n_rows, int words, int num_sms, int stream_path) {
+    int per_sm = 0;
+    cudaError_t e;
+    if (words * 8 <= bq::B1S_MAX_ROW_BYTES && stream_path != 1) {
+        const size_t ssm = bq::b1s_smem_bytes(words);
+        e = set_smem_limit((const void*)bq::bq_scan1_stream_kernel, (int)ssm) == 0
+                ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                      &per_sm, bq::bq_scan1_stream_kernel, bq::B1_THREADS, ssm)
+                : cudaErrorInvalidValue;
+    } else {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bq::bq_scan1_hist_kernel,
+                                                          bq::B1_THREADS,
+                                                          (size_t)(words * 64 + 1) * 4);
+    }
+    if (e != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 2;
+    }
+    int64_t ctas = (int64_t)num_sms * per_sm;
     const int64_t min_rows = 4 * bq::B1_GROUPS;
     if (ctas * min_rows > n_rows) ctas = (n_rows + min_rows - 1) / min_rows;
     return (int)(ctas < 1 ? 1 : ctas);
@@ -827,7 +1093,7 @@ size_t bq_scan1_scratch(int64_t n_rows, int words) {
 
 int launch_bq_scan1(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcode,
                     int S, int ctas, void* scratch, int32_t* sl_id, uint16_t* sl_h, int* sl_n,
-                    cudaStream_t st) {
+                    int* status, uint64_t wait_ns, int stream_path, cudaStream_t st) {
     if (!bq_scan1_supported(words, S) || n_rows <= 0) return PION_B200_ESHAPE;
     const int dim = words * 64;
     char* base = static_cast<char*>(scratch);
@@ -845,11 +1111,20 @@ int launch_bq_scan1(const uint64_t* codes, int64_t n_rows, int words, const uint
         cudaMemsetAsync(meta, 0, 16, st) != cudaSuccess)
         return PION_B200_ECUDA;
     const int64_t per = (n_rows + ctas - 1) / ctas;
-    const size_t hsm = (size_t)(dim + 1) * 4;
-    if (hsm > 48 * 1024 && set_smem_limit((const void*)bq::bq_scan1_hist_kernel, (int)hsm) != 0)
-        return PION_B200_ECUDA;
-    bq::bq_scan1_hist_kernel<<<ctas, bq::B1_THREADS, hsm, st>>>(codes, n_rows, words, qcode,
-                                                                 per, dist, hist);
+    if (words * 8 <= bq::B1S_MAX_ROW_BYTES && stream_path != 1) {
+        const size_t ssm = bq::b1s_smem_bytes(words);
+        if (set_smem_limit((const void*)bq::bq_scan1_stream_kernel, (int)ssm) != 0)
+            return PION_B200_ECUDA;
+        bq::bq_scan1_stream_kernel<<<ctas, bq::B1_THREADS, ssm, st>>>(
+            codes, n_rows, words, qcode, per, want, dist, hist, status, wait_ns);
+    } else {
+        const size_t hsm = (size_t)(dim + 1) * 4;
+        if (hsm > 48 * 1024 &&
+            set_smem_limit((const void*)bq::bq_scan1_hist_kernel, (int)hsm) != 0)
+            return PION_B200_ECUDA;
+        bq::bq_scan1_hist_kernel<<<ctas, bq::B1_THREADS, hsm, st>>>(codes, n_rows, words, qcode,
+                                                                     per, want, dist, hist);
+    }
     bq::bq_scan1_collect_kernel<<<ctas, bq::B1_THREADS, 0, st>>>(dist, n_rows, dim, hist, want,
                                                                   per, keys, ties, meta);
     const size_t fsm = (size_t)(bq::B1_TIECAP + 512) * 8;
@@ -930,6 +1205,23 @@ int launch_bq_rerank_wide(const float* rows, int dim, const float* qn, const int
                                                                             sl_n, S, dist);
     bq::bq_rerank_pick_kernel<<<(nq + 3) / 4, 128, 0, st>>>(dist, sl_id, sl_n, S, nq, k, id_base,
                                                             out_d, out_i);
+    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
+}
+
+int launch_bq_rerank_staged(const float* rows, int dim, const float* qn, const int32_t* sl_id,
+                            const int* sl_n, int S, int nq, int k, int64_t id_base, float* dist,
+                            unsigned* done, int* status, uint64_t wait_ns, float* out_d,
+                            int32_t* out_i, cudaStream_t st) {
+    if (nq <= 0) return 0;
+    const size_t smem = (size_t)dim * 4 + (size_t)bq::RS_ROWS * (dim + bq::RS_PAD) * 4 + 16;
+    if (dim % 16 != 0 || S > 256 || smem > 200 * 1024) return PION_B200_ESHAPE;
+    if (smem > 48 * 1024 &&
+        set_smem_limit((const void*)bq::bq_rerank_staged_kernel, (int)smem) != 0)
+        return PION_B200_ECUDA;
+    if (cudaMemsetAsync(done, 0, (size_t)nq * 4, st) != cudaSuccess) return PION_B200_ECUDA;
+    dim3 grid((S + bq::RS_ROWS - 1) / bq::RS_ROWS, nq);
+    bq::bq_rerank_staged_kernel<<<grid, 32, smem, st>>>(rows, dim, qn, sl_id, sl_n, S, k, id_base,
+                                                        dist, done, status, wait_ns, out_d, out_i);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

@@ -317,18 +317,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// Staged row pitch in floats: 16-byte aligned rows for dim % 4 == 0 (and rows 4 banks
+// apart), else one float of padding.
+__host__ __device__ inline int normalize_pitch(int dim) {
+    return (dim & 3) == 0 ? dim + 4 : dim + 1;
+}
+
 // exact_knn's query normalisation (src/commands/vector.mojo:1254-1260): a sequential
 // sum of squares, inv = 1/sqrt(ss) (1 if ss == 0), y = x * inv.  A CTA stages ROWS
-// queries in shared memory with coalesced loads; one thread per query runs the
-// sequential sum; all threads write the result.  qnorm (|y|, which only feeds the
-// certification bound, whose 1 % slack covers its rounding) is a warp reduction.
+// queries in shared memory with coalesced loads (rows 16-byte aligned when dim % 4 == 0);
+// one thread per query runs the sequential sum, reading four elements per shared load so
+// that only the addition chain is serial; all threads write the result.  qnorm (|y|,
+// which only feeds the certification bound, whose 1 % slack covers its rounding) is a
+// warp reduction.  With `codes` (dim % 64 == 0) it also writes the normalised query's
+// sign code (bit b of word w = y[64w + b] > 0) and, with `pm`, its +-1 bytes: the BQ
+// query encoding.
 __global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int dim, int rows,
-                                       float* __restrict__ out, float* __restrict__ qnorm) {
-    extern __shared__ float qsm[];  // [rows][dim + 1]
+                                       float* __restrict__ out, float* __restrict__ qnorm,
+                                       int8_t* __restrict__ pm, uint64_t* __restrict__ codes) {
+    extern __shared__ __align__(16) float qsm[];  // [rows][pitch]
     __shared__ float inv_s[32];
     const int q0 = blockIdx.x * rows;
     const int nr = min(rows, nq - q0);
-    const int pitch = dim + 1;
+    const int pitch = normalize_pitch(dim);
     for (int r = 0; r < nr; ++r)
         for (int d = threadIdx.x; d < dim; d += blockDim.x)
             qsm[r * pitch + d] = q[(size_t)(q0 + r) * dim + d];
@@ -336,31 +347,57 @@ __global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int 
     if (threadIdx.x < nr) {
         const float* x = qsm + threadIdx.x * pitch;
         float ss = 0.0f;
-        // unrolled so the shared-memory loads and products run ahead of the (sequential)
-        // addition chain
+        if ((dim & 3) == 0) {
+            const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 8
+            for (int d4 = 0; d4 < (dim >> 2); ++d4) {
+                const float4 v = x4[d4];
+                ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+                ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+                ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+                ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+            }
+        } else {
 #pragma unroll 16
-        for (int d = 0; d < dim; ++d) ss = __fadd_rn(ss, __fmul_rn(x[d], x[d]));
+            for (int d = 0; d < dim; ++d) ss = __fadd_rn(ss, __fmul_rn(x[d], x[d]));
+        }
         inv_s[threadIdx.x] = ss > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
     }
     __syncthreads();
+    for (int i = threadIdx.x; i < nr * dim; i += blockDim.x) {
+        const int r = i / dim, d = i - r * dim;
+        out[(size_t)(q0 + r) * dim + d] = __fmul_rn(qsm[r * pitch + d], inv_s[r]);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int r = warp; r < nr; r += nw) {
         const float inv = inv_s[r];
         float n2 = 0.0f;
         for (int d = lane; d < dim; d += 32) {
             const float y = __fmul_rn(qsm[r * pitch + d], inv);
-            out[(size_t)(q0 + r) * dim + d] = y;
             n2 = fmaf(y, y, n2);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, o);
         if (lane == 0) qnorm[q0 + r] = sqrtf(n2);
     }
+    if (codes) {  // a warp per (row, 64-element word)
+        const int words = dim / 64;
+        for (int t = warp; t < nr * words; t += nw) {
+            const int r = t / words, wd = t - r * words;
+            const float inv = inv_s[r];
+            const float a = __fmul_rn(qsm[r * pitch + wd * 64 + lane], inv);
+            const float b = __fmul_rn(qsm[r * pitch + wd * 64 + 32 + lane], inv);
+            const unsigned lo = __ballot_sync(0xffffffffu, a > 0.0f);
+            const unsigned hi = __ballot_sync(0xffffffffu, b > 0.0f);
+            if (pm) {
+                pm[(size_t)(q0 + r) * dim + wd * 64 + lane] = a > 0.0f ? 1 : -1;
+                pm[(size_t)(q0 + r) * dim + wd * 64 + 32 + lane] = b > 0.0f ? 1 : -1;
+            }
+            if (lane == 0) codes[(size_t)(q0 + r) * words + wd] = ((uint64_t)hi << 32) | lo;
+        }
+    }
 }
 
-// l2_normalize_fp32 (src/vector/kernels.mojo:318-357), 4 lanes per row: lane l sums
-// elements l, l+4, ... (the 4-lane SSE accumulator), then (s0 + s2) + (s1 + s3), the
-// scalar tail, inv = 1/sqrt.  Also records each row's resulting L2 norm.
 // l2_normalize_fp32 (src/vector/kernels.mojo:318-357) of whole rows: four lanes of
 // sequential sums (lane l takes the elements l, l+4, ...), combined (s0 + s2) + (s1 + s3),
 // the scalar tail added in order, inv = 1/sqrt; a zero row passes through.  A CTA stages
@@ -783,7 +820,7 @@ int ff32_kc(int k) { return k <= 16 ? 32 : 64; }
 // Rows staged per CTA by the normalisation kernels: up to 8, within 96 KB of shared
 // memory (one row of the largest supported dim, 16384, takes 64 KB).
 static int staged_rows(int dim) {
-    const int per = (int)((96 * 1024) / ((size_t)(dim + 1) * 4));
+    const int per = (int)((96 * 1024) / ((size_t)ff32::normalize_pitch(dim) * 4));
     return per < 1 ? 1 : per > 8 ? 8 : per;
 }
 
@@ -793,13 +830,14 @@ static bool allow_big_smem(K kernel) {
 }
 
 int launch_query_normalize(const float* q, int nq, int dim, float* out, float* qnorm,
-                           cudaStream_t st) {
+                           cudaStream_t st, int8_t* pm, uint64_t* codes) {
     if (nq <= 0) return 0;
+    if (codes && dim % 64 != 0) return PION_B200_ESHAPE;
     if (!allow_big_smem(ff32::query_normalize_kernel)) return PION_B200_ECUDA;
     const int rows = staged_rows(dim);
-    const size_t smem = (size_t)rows * (dim + 1) * 4;
-    ff32::query_normalize_kernel<<<(nq + rows - 1) / rows, 256, smem, st>>>(q, nq, dim, rows,
-                                                                          out, qnorm);
+    const size_t smem = (size_t)rows * ff32::normalize_pitch(dim) * 4;
+    ff32::query_normalize_kernel<<<(nq + rows - 1) / rows, 256, smem, st>>>(
+        q, nq, dim, rows, out, qnorm, pm, codes);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

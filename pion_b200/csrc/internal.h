@@ -59,8 +59,10 @@ struct Ff32TcLaunch {
 };
 int launch_flat_bf16x3_tc(const Ff32TcLaunch& launch, cudaStream_t st);
 int launch_split_bf16(const float* x, size_t n, void* hi, void* lo, cudaStream_t st);
+// exact_knn's query normalisation; with `codes` also the BQ sign code (and +-1 bytes
+// into `pm` when given) of the normalised query.
 int launch_query_normalize(const float* q, int nq, int dim, float* out, float* qnorm,
-                           cudaStream_t st);
+                           cudaStream_t st, int8_t* pm = nullptr, uint64_t* codes = nullptr);
 int launch_l2_normalize_rows(const float* src, int64_t n_rows, int dim, float* dst, float* norms,
                              cudaStream_t st);
 int launch_row_norms(const float* rows, int64_t n_rows, int dim, float* norms, cudaStream_t st);
@@ -496,16 +498,25 @@ int launch_bq_fallback(const uint64_t* codes, int64_t n_rows, int words, const u
 // smallest distances by (distance, row), sorted, into sl_id / sl_h / sl_n (three
 // kernels; `scratch` holds bq_scan1_scratch bytes).
 bool bq_scan1_supported(int words, int S);
-int bq_scan1_ctas(int64_t n_rows, int num_sms);
+int bq_scan1_ctas(int64_t n_rows, int words, int num_sms, int stream_path = 0);
 size_t bq_scan1_scratch(int64_t n_rows, int words);
+// The first pass streams the codes through shared memory by bulk copies (rows of at most
+// 384 bytes, unless stream_path == 1) or through registers; `status` / `wait_ns` bound its
+// waits.  bq_scan1_ctas sizes the grid to one full wave of the pass that runs.
 int launch_bq_scan1(const uint64_t* codes, int64_t n_rows, int words, const uint64_t* qcode,
                     int S, int ctas, void* scratch, int32_t* sl_id, uint16_t* sl_h, int* sl_n,
-                    cudaStream_t st);
+                    int* status, uint64_t wait_ns, int stream_path, cudaStream_t st);
 // The same rerank for few queries: shortlist rows spread over CTAs (dim % 16 == 0,
 // S <= 256), `dist` holds nq * S floats of scratch.
 int launch_bq_rerank_wide(const float* rows, int dim, const float* qn, const int32_t* sl_id,
                           const int* sl_n, int S, int nq, int k, int64_t id_base, float* dist,
                           float* out_d, int32_t* out_i, cudaStream_t st);
+// The same with the shortlist rows bulk-copied into shared memory (8 per one-warp CTA)
+// and the pick done by each query's last CTA; `done` holds nq counters of scratch.
+int launch_bq_rerank_staged(const float* rows, int dim, const float* qn, const int32_t* sl_id,
+                            const int* sl_n, int S, int nq, int k, int64_t id_base, float* dist,
+                            unsigned* done, int* status, uint64_t wait_ns, float* out_d,
+                            int32_t* out_i, cudaStream_t st);
 int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t* sl_id,
                      const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
                      int32_t* out_i, cudaStream_t st);

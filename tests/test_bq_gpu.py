@@ -103,3 +103,48 @@ def test_one_query_stream_equals_tensor_path(ctx, oracle):
     assert np.array_equal(got_i, want_i)
     assert np.array_equal(got_s.view(np.uint32), want_s.view(np.uint32))
     ix.free()
+
+
+def test_one_query_staged_rerank_equals_spread_rerank(ctx, oracle):
+    """The one-query rerank with the shortlist rows bulk-copied into shared memory (and the
+    pick by each query's last CTA) equals the spread-rows kernel pair, for one query and
+    for many (PION_B200_BQ_PATH=1 sends a batch down the popcount stream too)."""
+    import pion_b200
+    rows, qs = mixture_np(40000, 1536, 32, seed=31, n_queries=9)
+    ix = pion_b200.BQIndex(ctx, rows)
+    os.environ["PION_B200_BQ_PATH"] = "1"
+    try:
+        for S, k in ((100, 10), (256, 64), (7, 7)):
+            a = ix.search(qs, k, shortlist=S)
+            os.environ["PION_B200_BQ_RERANK"] = "1"
+            try:
+                b = ix.search(qs, k, shortlist=S)
+            finally:
+                os.environ.pop("PION_B200_BQ_RERANK", None)
+            assert np.array_equal(a[0], b[0])
+            assert np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+            check(oracle, rows, qs, S, k, a[0], a[1])
+    finally:
+        os.environ.pop("PION_B200_BQ_PATH", None)
+    ix.free()
+
+
+@pytest.mark.parametrize("n,dim", [(300000, 1536), (5000, 3072), (70001, 128)])
+def test_one_query_staged_stream_equals_register_stream(ctx, oracle, n, dim):
+    """The one-query first pass through shared memory (bulk copies of 128-row stages,
+    ragged last stages) equals the register pass (PION_B200_BQ_STREAM=1) and the oracle."""
+    import pion_b200
+    rows, qs = mixture_np(n, dim, 64, seed=n + dim, n_queries=3)
+    ix = pion_b200.BQIndex(ctx, rows)
+    for t in range(qs.shape[0]):
+        a = ix.search(qs[t:t + 1], 10, shortlist=100)
+        os.environ["PION_B200_BQ_STREAM"] = "1"
+        try:
+            b = ix.search(qs[t:t + 1], 10, shortlist=100)
+        finally:
+            os.environ.pop("PION_B200_BQ_STREAM", None)
+        assert np.array_equal(a[0], b[0])
+        assert np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+        if n <= 100000:
+            check(oracle, rows, qs[t:t + 1], 100, 10, a[0], a[1])
+    ix.free()
