@@ -109,11 +109,11 @@ def args_parse(argv=None):
                          "(host), batched insertion on the host, or batched insertion with "
                          "the batches' searches on the GPU (the same graph as 'batched')")
     ap.add_argument("--build-batch", type=int, default=4096)
-    ap.add_argument("--exchange", choices=["peer", "peer-local", "nccl"], default="peer",
-                    help="FLAT INT8 on N > 1 GPUs: the shards' lists cross NVLink through the "
+    ap.add_argument("--exchange", choices=["nccl", "peer", "peer-local"], default="nccl",
+                    help="FLAT INT8 on N > 1 GPUs: the shards' lists cross NVLink through an "
+                         "NCCL all-gather (each rank's own threshold sample), or through the "
                          "library's peer-memory exchange (with the threshold sample shared by "
-                         "the ranks, or each rank's own sample share: peer-local), or through "
-                         "an NCCL all-gather")
+                         "the ranks, or each rank's own sample share: peer-local)")
     ap.add_argument("--workers", type=int, default=None,
                     help="worker contexts (each its own CUDA stream) taking batches in turn; "
                          "default 3 for hnsw, 1 otherwise")
@@ -280,7 +280,7 @@ def config_of(wl, batch, world, a=None):
          "parallelism": f"row shards x{world}" + (
              ((" + NVLink peer exchange" + (" (local bounds)" if a is not None and
                                               a.exchange == "peer-local" else ""))
-              if (a is None or a.exchange.startswith("peer")) and
+              if (a is not None and a.exchange.startswith("peer")) and
               wl["kind"] == "i8" else " + NCCL all-gather") if world > 1 else ""),
          "l2": "index larger than L2 (no flush needed)"}
     if wl["kind"] == "hnsw":
