@@ -670,8 +670,8 @@ __global__ void __launch_bounds__(B1_THREADS)
 // (cp.async.bulk, completing on the stage's mbarrier) and B1S_STAGES stages in flight, so
 // the bytes in flight do not depend on registers; 4 lanes per row then popcount from
 // shared memory.  Same outputs as bq_scan1_hist_kernel.
-constexpr int B1S_ROWS = 128;
-constexpr int B1S_STAGES = 4;
+constexpr int B1S_ROWS = 64;    // 12 KB stages at 1536 dims: four CTAs per SM (measured:
+constexpr int B1S_STAGES = 4;   // 128-row stages at two per SM and one-CTA rings were slower)
 constexpr int B1S_MAX_ROW_BYTES = 384;  // dim <= 3072
 
 __global__ void __launch_bounds__(B1_THREADS)
@@ -688,19 +688,10 @@ __global__ void __launch_bounds__(B1_THREADS)
     uint4* qv = reinterpret_cast<uint4*>(b1_hist + ((dim + 1 + 3) & ~3));
     uint64_t* full = reinterpret_cast<uint64_t*>(qv + chunks);
     __shared__ int abort_flag;
-    for (int i = threadIdx.x; i <= dim; i += B1_THREADS) b1_hist[i] = 0;
-    for (int c = threadIdx.x; c < chunks; c += B1_THREADS)
-        qv[c] = reinterpret_cast<const uint4*>(qcode)[c];
     const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
     int64_t r1 = r0 + rows_per_cta;
     if (r1 > n_rows) r1 = n_rows;
     const int n_stages = r1 > r0 ? (int)((r1 - r0 + B1S_ROWS - 1) / B1S_ROWS) : 0;
-    if (threadIdx.x == 0) {
-        abort_flag = 0;
-        for (int s = 0; s < B1S_STAGES; ++s) mbar_init(&full[s], 1);
-        fence_barrier_init();
-    }
-    __syncthreads();
     auto issue = [&](int it) {  // thread 0: stage `it` of this CTA's range into its slot
         const int64_t a = r0 + (int64_t)it * B1S_ROWS;
         const int64_t b = a + B1S_ROWS < r1 ? a + B1S_ROWS : r1;
@@ -710,8 +701,16 @@ __global__ void __launch_bounds__(B1_THREADS)
         bulk_load(ring + (size_t)(it % B1S_STAGES) * B1S_ROWS * row_bytes,
                   reinterpret_cast<const uint8_t*>(codes) + a * row_bytes, bytes, bar);
     };
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {  // the first stages are in flight while the CTA sets up
+        abort_flag = 0;
+        for (int s = 0; s < B1S_STAGES; ++s) mbar_init(&full[s], 1);
+        fence_barrier_init();
         for (int it = 0; it < B1S_STAGES && it < n_stages; ++it) issue(it);
+    }
+    for (int i = threadIdx.x; i <= dim; i += B1_THREADS) b1_hist[i] = 0;
+    for (int c = threadIdx.x; c < chunks; c += B1_THREADS)
+        qv[c] = reinterpret_cast<const uint4*>(qcode)[c];
+    __syncthreads();
     const int g = threadIdx.x >> 2, j = threadIdx.x & 3;
     int it = 0;
     for (; it < n_stages; ++it) {
@@ -1061,7 +1060,7 @@ bool bq_scan1_supported(int words, int S) {
 
 // One full wave of the first pass: as many CTAs as fit on the SMs at once (the register
 // pass's 84 registers a thread allow 2 CTAs of 256 threads per SM; the staged pass's
-// ~105 KB of shared memory also 2).
+// ~55 KB of shared memory 4).
 int bq_scan1_ctas(int64_t n_rows, int words, int num_sms, int stream_path) {
     int per_sm = 0;
     cudaError_t e;
