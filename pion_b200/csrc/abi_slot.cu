@@ -30,17 +30,6 @@ struct Stage {
     int begin, end, splits;
 };
 
-// Tiles of the sampled bound pass at the start of a one-stage list scan of `tiles` tiles:
-// 256 (64K slots; their chunk bests' k-th smallest, with the prefix's entries, bounds
-// every split after them), at most a quarter of the stage, none below 8.
-// PION_B200_SLOT_SAMPLE=<tiles> overrides (0: no sample).
-int sample_tiles(int tiles) {
-    int t = 256;
-    if (const char* e = getenv("PION_B200_SLOT_SAMPLE")) t = atoi(e);
-    if (t > tiles / 4) t = tiles / 4;
-    return t >= 8 ? t : 0;
-}
-
 // The first slots go through the exact loop from dense distance rows (no lists); their
 // k-th smallest bounds everything after.  4096 slots: longer prefixes cut the candidate
 // lists but cost more than they save (measured on 512K slots, 1024 queries, k 10 / 20).
@@ -98,7 +87,6 @@ struct ScanState {
     int32_t* cand_i;
     int* cand_n;
     float* pub;
-    float* bound2;          // per query: the sampled bound
     int* status = nullptr;  // the call's status word (call_status)
 };
 
@@ -115,7 +103,7 @@ size_t scan_layout(size_t off, int64_t nq, int keff, int max_splits, ScanState* 
                  o_sx = take((size_t)nq * 4), o_qf = take((size_t)nq * 4),
                  o_fl = take((size_t)(nq + 1) * 4), o_cd = take(cand_e * 4),
                  o_ci = take(cand_e * 4), o_cn = take((size_t)nq * max_splits * 2 * 4),
-                 o_pb = take((size_t)nq * max_splits * 2 * 4), o_b2 = take((size_t)nq * 4);
+                 o_pb = take((size_t)nq * max_splits * 2 * 4);
     if (base) {
         S->qnorm = reinterpret_cast<float*>(base + o_qn);
         S->st_d = reinterpret_cast<float*>(base + o_sd);
@@ -128,7 +116,6 @@ size_t scan_layout(size_t off, int64_t nq, int keff, int max_splits, ScanState* 
         S->cand_i = reinterpret_cast<int32_t*>(base + o_ci);
         S->cand_n = reinterpret_cast<int*>(base + o_cn);
         S->pub = reinterpret_cast<float*>(base + o_pb);
-        S->bound2 = reinterpret_cast<float*>(base + o_b2);
     }
     return off;
 }
@@ -269,43 +256,6 @@ int run_scan(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes,
                                           st);
         ctx->launches++;
     }
-    // the sampled bound (one-stage scans): the bound pass over the first tiles of the
-    // stage, then the k-th smallest of its chunk bests and the prefix's entries
-    int b2_tile = 0;
-    const int smp = ns == 1 && keff <= kLocalKMax ? sample_tiles(stages[0].end - stages[0].begin) : 0;
-    if (rc == 0 && smp > 0) {
-        const int n_qt = (nq + slot_query_tile() - 1) / slot_query_tile();
-        int bs = ctx->num_sms / n_qt;
-        bs = bs < 1 ? 1 : bs;
-        bs = bs > smp ? smp : bs;
-        bs = bs > stages[0].splits ? stages[0].splits : bs;  // the candidate buffers' size
-        SlotTcLaunch L;
-        L.tmap_q = &tmap_q;
-        L.tmap_rows = &ix->tmap_rows;
-        L.chunk_vmin = h.chunk_vmin;
-        L.k = keff;
-        L.bound = S.st_worst;
-        L.qnorm = S.qnorm;
-        L.vnorm = h.norms;
-        L.n_rows = n_scan;
-        L.nq = nq;
-        L.tile_begin = stages[0].begin;
-        L.tile_end = stages[0].begin + smp;
-        L.n_splits = bs;
-        L.cap = cap_for(keff);
-        L.cand_d = S.cand_d;
-        L.cand_i = S.cand_i;
-        L.cand_n = S.cand_n;
-        L.status = S.status;
-        L.bound_pass = true;
-        rc = launch_slot_tc(L, st);
-        ctx->launches++;
-        if (rc == 0)
-            rc = launch_slot_bound_select(S.cand_d, bs * 2, cap_for(keff), S.st_d, nq, keff,
-                                          S.bound2, st);
-        ctx->launches++;
-        b2_tile = stages[0].begin + smp;
-    }
     for (int s = 0; s < ns && rc == 0; ++s) {
         SlotTcLaunch L;
         L.tmap_q = &tmap_q;
@@ -313,10 +263,6 @@ int run_scan(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes,
         L.chunk_vmin = h.chunk_vmin;
         L.k = keff;
         L.bound = S.st_worst;
-        if (smp > 0) {
-            L.bound2 = S.bound2;
-            L.bound2_tile = b2_tile;
-        }
         L.qnorm = S.qnorm;
         L.vnorm = h.norms;
         L.n_rows = n_scan;

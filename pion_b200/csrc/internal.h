@@ -436,19 +436,12 @@ struct SlotTcLaunch {
     const int* n_dense = nullptr;  // queries in the dense rows (null: nq)
     float* pub = nullptr;          // [nq][n_splits][2] published list thresholds, or null
     const int* chunk_vmin = nullptr;  // per 32-slot chunk min floor(norm), whole tiles
-    const float* bound2 = nullptr;    // per query: the sampled bound, for splits whose
-    int bound2_tile = 0;              // first tile is >= bound2_tile
-    bool bound_pass = false;          // the sampled bound pass (k values per list)
 };
 int launch_slot_chunk_vmin(const float* vnorm, int64_t n, int* out, cudaStream_t st);
 int launch_slot_prep(const int8_t* codes, const float* qnorm_in, int nq, int k, float* qnorm,
                      float* st_d, int32_t* st_i, float* st_worst, int* st_widx, int* qflag,
                      int* flags, int force_exact, cudaStream_t st);
 int launch_slot_tc(const SlotTcLaunch& launch, cudaStream_t st);
-// The k-th smallest of the bound pass's n_lists lists (k values each, list stride cap)
-// and the prefix loop's k entries per query, into out[q].
-int launch_slot_bound_select(const float* lists, int n_lists, int cap, const float* st_d, int nq,
-                             int k, float* out, cudaStream_t st);
 int launch_slot_replay(const float* cand_d, const int32_t* cand_i, const int* cand_n, int n_lists,
                        int cap, int nq, int k, float* st_d, int32_t* st_i, float* st_worst,
                        int* st_widx, int* qflag, int* flags, unsigned long long* counters,

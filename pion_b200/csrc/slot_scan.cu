@@ -78,10 +78,6 @@ struct TcParams {
     // list of split s + 1 may use split s's values, which already fold in those of
     // split s - 1: the chain carries the tightest earlier threshold forward.
     float* pub;
-    // lists mode: per query a second bound (the sampled bound) for the splits whose first
-    // tile is at or after bound2_tile (every slot they scan comes after the sample)
-    const float* bound2;
-    int bound2_tile;
 };
 
 // The k smallest candidates of a list so far, unsorted in registers (entries past k hold
@@ -132,11 +128,7 @@ struct LocalTopK {
 // DENSE: the exact path for queries whose lists overflowed; the epilogue writes every
 // distance (transposed through shared memory so that each store is one 128-byte row
 // segment) and collects nothing.
-// BOUND (the sampled bound pass): per 32-slot chunk the slot with the smallest
-// floor(vn) - 2 dot gets its exact distance, and each list keeps the k smallest of those
-// (distinct slots: their k-th smallest bounds the loop's worst after them).  The lists
-// written hold exactly k values each (+inf where fewer chunks passed).
-template <int KCAP, bool DENSE, bool BOUND = false>
+template <int KCAP, bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
     slot_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                    const __grid_constant__ CUtensorMap tmap_rows, TcParams p) {
@@ -264,9 +256,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         float* stash_v = reinterpret_cast<float*>(stash + 32 * 32);
         const int q = qt * BM + lg * 32 + lane;
         const bool q_ok = q < p.nq;
-        float bound = q_ok && !DENSE ? p.bound[q] : -INFINITY;
-        if (!DENSE && !BOUND && q_ok && p.bound2 && t_begin >= p.bound2_tile)
-            bound = fminf(bound, p.bound2[q]);
+        const float bound = q_ok && !DENSE ? p.bound[q] : -INFINITY;
         const float qn = q_ok ? p.qnorm[q] : 0.0f;
         const size_t list = ((size_t)(q_ok ? q : 0) * p.n_splits + split) * 2 + half;
         float* out_d = p.cand_d + list * p.cap;
@@ -367,29 +357,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 vrow[lane] = vicur[c];
                 __syncwarp();
                 if (!coarse) return;
-                if constexpr (BOUND) {
-                    // the chunk's likeliest nearest slot by floor(vn) - 2 dot (first on
-                    // ties), then its exact distance
-                    const int64_t vcb = p.n_rows - c0;
-                    int best = INT_MAX, bj = -1;
-                    int32_t bdot = 0;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int key = vrow[j] - 2 * (int32_t)r[j];
-                        const bool take = j < vcb && key < best;
-                        best = take ? key : best;
-                        bj = take ? j : bj;
-                        bdot = take ? (int32_t)r[j] : bdot;
-                    }
-                    if (bj >= 0) {
-                        const float d = l2_dist(qn, __ldg(&p.vnorm[c0 + bj]), bdot);
-                        if (d < thr) {
-                            thr = fminf(thr, top.insert(d));
-                            ithr = int_floor(thr);
-                        }
-                    }
-                    return;
-                }
                 // From here on each lane works alone: no warp synchronisation.
                 uint32_t mask;
                 if (ithr == INT_MIN) {
@@ -476,71 +443,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_arrive(&tempty[buf]);
             if (my_pub) __stcg(my_pub, thr);
         }
-        if constexpr (BOUND) {
-            if (q_ok) {
-#pragma unroll
-                for (int m = 0; m < KT; ++m)
-                    if (m < p.k) out_d[m] = top.v[m];
-                p.cand_n[list] = p.k;
-            }
-        } else if (!DENSE && q_ok) {
-            p.cand_n[list] = count;
-        }
+        if (!DENSE && q_ok) p.cand_n[list] = count;
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
-    }
-}
-
-// The sampled bound of a query: the k-th smallest of the bound pass's lists (k values
-// each) and the prefix loop's k entries -- exact distances of distinct slots that all
-// come before the splits it bounds.  A warp per query: each lane keeps the k smallest of
-// its share, then a radix select over the lanes' values (bit by bit, counts summed by
-// shuffles) finds the k-th smallest; +inf if there are fewer than k finite values.
-template <int KT>
-__global__ void __launch_bounds__(128)
-    slot_bound_select_kernel(const float* __restrict__ lists, int n_lists, int cap,
-                             const float* __restrict__ st_d, int nq, int k,
-                             float* __restrict__ out) {
-    const int q = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (q >= nq) return;  // warp-uniform
-    LocalTopK<KT> top;
-    top.init(k);
-    float kth = INFINITY;
-    const int total = n_lists * k + k;
-    for (int e = lane; e < total; e += 32) {
-        const float v = e < n_lists * k
-                            ? lists[((size_t)q * n_lists + e / k) * cap + e % k]
-                            : st_d[(size_t)q * k + (e - n_lists * k)];
-        if (v < kth) kth = top.insert(v);
-    }
-    auto key_of = [](float v) {
-        const uint32_t b = __float_as_uint(v);
-        return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    };
-    uint32_t prefix = 0;
-    int rem = k;
-    for (int bit = 31; bit >= 0; --bit) {
-        int cnt = 0;
-#pragma unroll
-        for (int m = 0; m < KT; ++m) {
-            const uint32_t key = key_of(top.v[m]);
-            const bool hi_match = bit == 31 || ((key ^ prefix) >> (bit + 1)) == 0;
-            cnt += (m < k && hi_match && ((key >> bit) & 1u) == 0) ? 1 : 0;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-        if (cnt < rem) {
-            rem -= cnt;
-            prefix |= 1u << bit;
-        }
-    }
-    if (lane == 0) {
-        const uint32_t b = (prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix;
-        out[q] = __uint_as_float(b);
     }
 }
 
@@ -952,13 +861,12 @@ int launch_slot_prep(const int8_t* codes, const float* qnorm_in, int nq, int k, 
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
-template <int KCAP, bool DENSE, bool BOUND = false>
+template <int KCAP, bool DENSE>
 static int slot_tc_go(dim3 grid, const SlotTcLaunch& L, const slot::TcParams& p,
                       cudaStream_t st) {
-    if (set_smem_limit((const void*)slot::slot_tc_kernel<KCAP, DENSE, BOUND>,
-                       (int)slot::SMEM_BYTES) != 0)
+    if (set_smem_limit((const void*)slot::slot_tc_kernel<KCAP, DENSE>, (int)slot::SMEM_BYTES) != 0)
         return PION_B200_ECUDA;
-    slot::slot_tc_kernel<KCAP, DENSE, BOUND><<<grid, slot::THREADS, slot::SMEM_BYTES, st>>>(
+    slot::slot_tc_kernel<KCAP, DENSE><<<grid, slot::THREADS, slot::SMEM_BYTES, st>>>(
         *L.tmap_q, *L.tmap_rows, p);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
@@ -986,8 +894,6 @@ int launch_slot_tc(const SlotTcLaunch& L, cudaStream_t st) {
     p.n_dense = L.n_dense;
     p.pub = L.pub;
     p.chunk_vmin = L.chunk_vmin;
-    p.bound2 = L.bound2;
-    p.bound2_tile = L.bound2_tile;
     if (p.tile_end <= p.tile_begin || p.n_splits < 1 || p.n_splits > p.tile_end - p.tile_begin)
         return PION_B200_ESHAPE;
     if (p.k < 1 || p.k > slot::KMAX) return PION_B200_ESHAPE;
@@ -998,34 +904,11 @@ int launch_slot_tc(const SlotTcLaunch& L, cudaStream_t st) {
             return PION_B200_ESHAPE;
         return slot_tc_go<0, true>(grid, L, p, st);
     }
-    if (L.bound_pass) {  // lists of exactly k values: k <= 64, no chain
-        if (p.k > 64 || p.cap < p.k || p.pub) return PION_B200_ESHAPE;
-        if (p.k <= 16) return slot_tc_go<16, false, true>(grid, L, p, st);
-        if (p.k <= 32) return slot_tc_go<32, false, true>(grid, L, p, st);
-        return slot_tc_go<64, false, true>(grid, L, p, st);
-    }
     if (p.cap < slot::HALF) return PION_B200_ESHAPE;
     if (p.k <= 16) return slot_tc_go<16, false>(grid, L, p, st);
     if (p.k <= 32) return slot_tc_go<32, false>(grid, L, p, st);
     if (p.k <= 64) return slot_tc_go<64, false>(grid, L, p, st);
     return slot_tc_go<0, false>(grid, L, p, st);
-}
-
-int launch_slot_bound_select(const float* lists, int n_lists, int cap, const float* st_d, int nq,
-                             int k, float* out, cudaStream_t st) {
-    if (nq <= 0) return 0;
-    if (k < 1 || k > 64 || cap < k || n_lists < 1) return PION_B200_ESHAPE;
-    const int blocks = (nq + 3) / 4;
-    if (k <= 16)
-        slot::slot_bound_select_kernel<16><<<blocks, 128, 0, st>>>(lists, n_lists, cap, st_d, nq,
-                                                                   k, out);
-    else if (k <= 32)
-        slot::slot_bound_select_kernel<32><<<blocks, 128, 0, st>>>(lists, n_lists, cap, st_d, nq,
-                                                                   k, out);
-    else
-        slot::slot_bound_select_kernel<64><<<blocks, 128, 0, st>>>(lists, n_lists, cap, st_d, nq,
-                                                                   k, out);
-    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
 int launch_slot_replay(const float* cand_d, const int32_t* cand_i, const int* cand_n, int n_lists,

@@ -181,32 +181,3 @@ def test_brute_force_recall(ctx, oracle, small):
     truth = np.argsort(-(qn @ rn.T), axis=1, kind="stable")[:, :10]
     recall = np.mean([len(set(ids[i]) & set(truth[i])) / 10 for i in range(len(qs))])
     assert recall >= 0.97
-
-
-@pytest.mark.parametrize("sample", [None, "0", "8", "64"])
-def test_slot_scan_sampled_bound(ctx, oracle, large, sample, monkeypatch):
-    """The sampled bound pass (the chunk bests of the first tiles of the list stage, whose
-    k-th smallest with the prefix's entries bounds every later split) only drops slots the
-    loop cannot admit: entries equal the oracle's with the sample off, short or long, and
-    on ties everywhere (codes in {-1, 0, 1})."""
-    import pion_b200
-    if sample is not None:
-        monkeypatch.setenv("PION_B200_SLOT_SAMPLE", sample)
-    g, A, ix, rows, qs = large
-    c, qn = _codes(oracle, A, qs[:100])
-    for k in (10, 40):
-        _same(ix.slot_scan_topk(c, k, qn), oracle.slot_scan_topk(A, c, qn, A["num_nodes"], k))
-    A = dict(A)
-    n, stride, hdr = A["num_nodes"], A["compact_stride"], A["compact_hdr"]
-    rng = np.random.Generator(np.random.PCG64(9))
-    buf = A["compact_buffer"].reshape(n, stride).copy()
-    cc = rng.integers(-1, 2, size=(n, 1536)).astype(np.int8)
-    buf[:, hdr:hdr + 1536] = cc
-    buf[:, :4] = (cc.astype(np.int32) ** 2).sum(1).astype(np.float32)[:, None].view(np.uint8)
-    A["compact_buffer"] = buf.reshape(-1)
-    tix = pion_b200.HNSWIndex(ctx, A)
-    qc = rng.integers(-1, 2, size=(20, 1536)).astype(np.int8)
-    tqn = (qc.astype(np.int32) ** 2).sum(1).astype(np.float32)
-    for k in (7, 64):
-        _same(tix.slot_scan_topk(qc, k, tqn), oracle.slot_scan_topk(A, qc, tqn, n, k))
-    tix.free()
