@@ -30,13 +30,6 @@ struct Stage {
     int begin, end, splits;
 };
 
-// PION_B200_SLOT_SET=0 keeps the brute-force search with rerank rows on the replayed loop
-// (tests compare the two).
-int set_mode_allowed() {
-    const char* e = getenv("PION_B200_SLOT_SET");
-    return e ? atoi(e) != 0 : 1;
-}
-
 // The first slots go through the exact loop from dense distance rows (no lists); their
 // k-th smallest bounds everything after.  4096 slots: longer prefixes cut the candidate
 // lists but cost more than they save (measured on 512K slots, 1024 queries, k 10 / 20).
@@ -204,101 +197,6 @@ int run_dense(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes
             ctx->launches++;
         }
     }
-    return rc;
-}
-
-// The loop's final entries as a set, for callers that order them by another key (the
-// brute-force search reranks them): the k smallest (distance, slot) pairs per query,
-// sorted, into S.st_d / S.st_i.  The prefix runs the exact loop as in run_scan; the one
-// list stage runs the set-mode kernel (each list's k best, one shared bound per query);
-// a merge by (distance, slot) of the prefix's entries and every list gives the set.
-int run_scan_set(pion_b200_ctx* ctx, const pion_b200_index* ix, const int8_t* codes, int nq,
-                 int64_t n_scan, int keff, const Stage& stg, const ScanState& S) {
-    cudaStream_t st = ctx->stream;
-    const auto& h = ix->hnsw;
-    if (ensure(ctx->hnsw_misc, 64) != 0) return PION_B200_ENOMEM;
-    unsigned long long* counters =
-        reinterpret_cast<unsigned long long*>(static_cast<char*>(ctx->hnsw_misc.ptr) + 32);
-    if (cudaMemsetAsync(counters, 0, 16, st) != cudaSuccess) return PION_B200_ECUDA;
-    int rc = launch_slot_prep(codes, nullptr, nq, keff, S.qnorm, S.st_d, S.st_i, S.st_worst,
-                              S.st_widx, S.qflag, S.flags, 0, st);
-    ctx->launches++;
-    CUtensorMap tmap_q;
-    if (rc == 0 && make_tmap_2d(&tmap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, codes,
-                                (uint64_t)hnsw_dim(), (uint64_t)nq, (uint64_t)hnsw_dim(),
-                                (uint32_t)slot_k_block(), (uint32_t)slot_query_tile(),
-                                CU_TENSOR_MAP_SWIZZLE_128B) != 0)
-        rc = PION_B200_ECUDA;
-    timing_begin(ctx);
-    const int64_t pre = prefix_rows(nq, n_scan);
-    if (rc == 0) {
-        const int64_t tr = slot_tile_rows();
-        if (ensure(ctx->scratch2, (size_t)nq * pre * 4) != 0) rc = PION_B200_ENOMEM;
-        float* dense = static_cast<float*>(ctx->scratch2.ptr);
-        SlotTcLaunch L;
-        L.tmap_q = &tmap_q;
-        L.tmap_rows = &ix->tmap_rows;
-        L.chunk_vmin = h.chunk_vmin;
-        L.k = keff;
-        L.qnorm = S.qnorm;
-        L.vnorm = h.norms;
-        L.n_rows = n_scan;
-        L.nq = nq;
-        L.tile_begin = 0;
-        L.tile_end = (int)(pre / tr);
-        const int n_qt = (nq + slot_query_tile() - 1) / slot_query_tile();
-        int sp = (ctx->num_sms + n_qt - 1) / n_qt;
-        L.n_splits = sp < L.tile_end ? sp : L.tile_end;
-        L.status = S.status;
-        L.dense = dense;
-        L.dense_base = 0;
-        L.dense_ld = pre;
-        if (rc == 0) rc = launch_slot_tc(L, st);
-        ctx->launches++;
-        if (rc == 0)
-            rc = launch_slot_dense_replay(dense, pre, 0, pre < n_scan ? pre : n_scan, nullptr, nq,
-                                          keff, S.st_d, S.st_i, S.st_worst, S.st_widx, 0,
-                                          nullptr, 0, nullptr, nullptr, nullptr, nullptr, S.qflag,
-                                          st);
-        ctx->launches++;
-    }
-    const int set_lists = 1 + 2 * stg.splits;
-    if (rc == 0)
-        rc = launch_slot_set_prefix(S.st_d, S.st_i, nq, keff, set_lists, S.cand_d, S.cand_i, st);
-    ctx->launches++;
-    uint32_t* set_pub = reinterpret_cast<uint32_t*>(S.pub);
-    if (rc == 0 && cudaMemsetAsync(set_pub, 0xff, (size_t)nq * 4, st) != cudaSuccess)
-        rc = PION_B200_ECUDA;
-    if (rc == 0) {
-        SlotTcLaunch L;
-        L.tmap_q = &tmap_q;
-        L.tmap_rows = &ix->tmap_rows;
-        L.chunk_vmin = h.chunk_vmin;
-        L.k = keff;
-        L.bound = S.st_worst;
-        L.qnorm = S.qnorm;
-        L.vnorm = h.norms;
-        L.n_rows = n_scan;
-        L.nq = nq;
-        L.tile_begin = stg.begin;
-        L.tile_end = stg.end;
-        L.n_splits = stg.splits;
-        L.cap = cap_for(keff);
-        L.cand_d = S.cand_d;
-        L.cand_i = S.cand_i;
-        L.cand_n = S.cand_n;
-        L.status = S.status;
-        L.set_pub = set_pub;
-        L.set_lists = set_lists;
-        rc = launch_slot_tc(L, st);
-        ctx->launches++;
-    }
-    if (rc == 0)
-        rc = launch_merge_lists(S.cand_d, S.cand_i, nq, set_lists, keff, 0, false, S.st_d,
-                                S.st_i, st);
-    ctx->launches++;
-    timing_end(ctx);
-    ctx->slot_exact = 0;
     return rc;
 }
 
@@ -614,28 +512,8 @@ int pion_v_b200_hnsw_brute_force(pion_b200_ctx* ctx, const pion_b200_index* ix, 
             rc = launch_hnsw_quantize(qsrc, (int)nq, h.gmin, 254.0f / range, codes,
                                       reinterpret_cast<int32_t*>(base + o_blk), st);
         ctx->launches++;
-        // with rerank rows only the loop's final set matters (unless reranked distances
-        // tie): the set-mode scan, redone through the replayed loop when they do
-        const bool set_mode = h.rerank && keff <= 32 && ns == 1 && set_mode_allowed() &&
-                              (1 + 2 * stages[0].splits) * keff <=
-                                  (int64_t)ms * 2 * cap_for(keff);
-        bool done = false;
-        if (rc == 0 && set_mode) {
-            rc = run_scan_set(ctx, ix, codes, (int)nq, n, keff, stages[0], S);
-            if (rc == 0) {
-                rc = launch_slot_finish(S.st_d, S.st_i, (int)nq, keff, dq, h.rerank, h.slot_ext,
-                                        n, (int)final_k, (int)k, di, dv, df, st, S.flags);
-                ctx->launches++;
-            }
-            int tie = 0;
-            if (rc == 0 &&
-                (cudaMemcpyAsync(&tie, S.flags, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-                 cudaStreamSynchronize(st) != cudaSuccess))
-                rc = PION_B200_ECUDA;
-            done = rc == 0 && tie == 0;
-        }
-        if (rc == 0 && !done) rc = run_scan(ctx, ix, codes, nullptr, (int)nq, n, keff, stages, ns, S);
-        if (rc == 0 && !done) {
+        if (rc == 0) rc = run_scan(ctx, ix, codes, nullptr, (int)nq, n, keff, stages, ns, S);
+        if (rc == 0) {
             rc = launch_slot_finish(S.st_d, S.st_i, (int)nq, keff, dq, h.rerank, h.slot_ext, n,
                                     (int)final_k, (int)k, di, dv, df, st);
             ctx->launches++;

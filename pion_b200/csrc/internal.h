@@ -436,17 +436,12 @@ struct SlotTcLaunch {
     const int* n_dense = nullptr;  // queries in the dense rows (null: nq)
     float* pub = nullptr;          // [nq][n_splits][2] published list thresholds, or null
     const int* chunk_vmin = nullptr;  // per 32-slot chunk min floor(norm), whole tiles
-    uint32_t* set_pub = nullptr;      // set mode: per query the shared bound (see slot_scan.cu)
-    int set_lists = 0;                // set mode: lists per query, 1 + 2 * n_splits
 };
 int launch_slot_chunk_vmin(const float* vnorm, int64_t n, int* out, cudaStream_t st);
 int launch_slot_prep(const int8_t* codes, const float* qnorm_in, int nq, int k, float* qnorm,
                      float* st_d, int32_t* st_i, float* st_worst, int* st_widx, int* qflag,
                      int* flags, int force_exact, cudaStream_t st);
 int launch_slot_tc(const SlotTcLaunch& launch, cudaStream_t st);
-// Set mode: the prefix loop's k entries sorted by (distance, slot) into list 0 of each query.
-int launch_slot_set_prefix(const float* st_d, const int32_t* st_i, int nq, int k, int set_lists,
-                           float* cand_d, int32_t* cand_i, cudaStream_t st);
 int launch_slot_replay(const float* cand_d, const int32_t* cand_i, const int* cand_n, int n_lists,
                        int cap, int nq, int k, float* st_d, int32_t* st_i, float* st_worst,
                        int* st_widx, int* qflag, int* flags, unsigned long long* counters,
@@ -464,7 +459,7 @@ int launch_slot_emit(const float* st_d, const int32_t* st_i, int nq, int k, int 
 int launch_slot_finish(const float* st_d, const int32_t* st_i, int nq, int k, const float* q_raw,
                        const float* rerank, const int32_t* slot_ext, int64_t n, int final_k,
                        int k_out, int32_t* out_ids, float* out_scores, int32_t* out_found,
-                       cudaStream_t st, int* tie_flag = nullptr);
+                       cudaStream_t st);
 
 // ---- bq.cu
 int bq_tile_rows();

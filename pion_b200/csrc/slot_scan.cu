@@ -78,10 +78,6 @@ struct TcParams {
     // list of split s + 1 may use split s's values, which already fold in those of
     // split s - 1: the chain carries the tightest earlier threshold forward.
     float* pub;
-    // SET: per query the published bound (fkey; 0xffffffff: none), and the lists' layout
-    // [nq][set_lists][k] (list 0 holds the prefix's entries)
-    uint32_t* set_pub;
-    int set_lists;
 };
 
 // The k smallest candidates of a list so far, unsorted in registers (entries past k hold
@@ -122,56 +118,6 @@ struct LocalTopK {
     }
 };
 
-// The k smallest (distance, slot) pairs of a list so far (the set the worst-replace loop
-// ends with: its final entries are the k smallest by (distance, slot), since a slot is
-// admitted only strictly below the current worst).  Unsorted in registers like
-// LocalTopK; the max tree orders by (distance, slot).
-template <int KCAP>
-struct LocalTopKI {
-    float v[KCAP];
-    int32_t id[KCAP];
-    int mpos;
-    __device__ __forceinline__ void init(int k) {
-#pragma unroll
-        for (int m = 0; m < KCAP; ++m) {
-            v[m] = m < k ? INFINITY : -INFINITY;
-            id[m] = INT_MAX;
-        }
-        mpos = 0;
-    }
-    __device__ __forceinline__ float insert(float d, int32_t i) {
-#pragma unroll
-        for (int m = 0; m < KCAP; ++m) {
-            v[m] = __uint_as_float(selp_u32(__float_as_uint(d), __float_as_uint(v[m]), m == mpos));
-            id[m] = (int32_t)selp_u32((uint32_t)i, (uint32_t)id[m], m == mpos);
-        }
-        // the new largest by a running scan (no tree temporaries: the epilogue's registers
-        // are nearly all taken)
-        float mv = v[0];
-        int32_t mi = id[0];
-        int mp = 0;
-#pragma unroll
-        for (int m = 1; m < KCAP; ++m) {
-            const bool up = v[m] > mv || (v[m] == mv && id[m] > mi);
-            mv = up ? v[m] : mv;
-            mi = up ? id[m] : mi;
-            mp = up ? m : mp;
-        }
-        mpos = mp;
-        return mv;
-    }
-};
-
-// Order-preserving unsigned key of a float (for atomicMin on distances).
-__device__ __forceinline__ uint32_t fkey(float v) {
-    const uint32_t b = __float_as_uint(v);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float fkey_inv(uint32_t k) {
-    if (k == 0xffffffffu) return INFINITY;  // nothing published yet
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
-}
-
 // KCAP > 0 (k <= KCAP): a lane also drops slots that are not below the k-th smallest
 // candidate of its own list so far.  Those slots come earlier in the scan, so the loop's
 // worst at a slot is at most that k-th distance and such a slot cannot enter the loop;
@@ -182,13 +128,7 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 // DENSE: the exact path for queries whose lists overflowed; the epilogue writes every
 // distance (transposed through shared memory so that each store is one 128-byte row
 // segment) and collects nothing.
-// SET (the brute-force search with rerank rows, which needs only the loop's final set):
-// each list keeps its k smallest (distance, slot) pairs; a slot is a candidate if it is
-// below the prefix's worst and the list's own k-th strictly and not above the smallest
-// k-th any list of the query has published (set_pub, an atomicMin per tile: any k slots
-// bound the final k-th, and a slot equal to it may still win on its slot index); at the
-// end the list is written sorted by (distance, slot) for a merge.
-template <int KCAP, bool DENSE, bool SET = false>
+template <int KCAP, bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
     slot_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                    const __grid_constant__ CUtensorMap tmap_rows, TcParams p) {
@@ -325,11 +265,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         constexpr int KT = KCAP > 0 ? KCAP : 1;
         LocalTopK<KT> top;
         top.init(KCAP > 0 ? p.k : 0);
-        float thr = bound;  // min(bound, this list's k-th candidate) [SET: and the shared bound]
-        LocalTopKI<SET ? KT : 1> topi;
-        float thr_own = bound;  // SET: min(bound, this list's own k-th)
-        float tsh = INFINITY;   // SET: the query's shared bound
-        if constexpr (SET) topi.init(p.k);
+        float thr = bound;  // min(bound, this list's k-th candidate)
         // Integer pre-test of d < thr: 2 dot - floor(vn) > floor(qn - thr) - 64.  The
         // float rounding of d stays below 64 at these magnitudes (|qn|, |vn| < 2^26), so
         // the test passes every slot that can pass the exact one.
@@ -365,14 +301,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int buf = t & 1;
             const uint32_t use = (uint32_t)(t >> 1);
             const int64_t col0 = (int64_t)(t_begin + t) * BN + half * HALF;
-            if constexpr (SET) {
-                if (q_ok) tsh = fkey_inv(__ldcg(p.set_pub + q));
-                const float t2 = fminf(thr_own, tsh);
-                if (t2 < thr) {
-                    thr = t2;
-                    ithr = int_floor(thr);
-                }
-            }
             if (ext < thr) {
                 thr = ext;
                 ithr = int_floor(thr);
@@ -470,13 +398,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mask &= mask - 1u;
                     const float d = l2_dist(qn, __ldg(&p.vnorm[c0 + j]),
                                             (int32_t)row[(((j >> 2) ^ sw) << 2) | (j & 3)]);
-                    if constexpr (SET) {
-                        if (!(d < thr_own && d <= tsh)) continue;
-                        thr_own = fminf(thr_own, topi.insert(d, (int32_t)(c0 + j)));
-                        thr = fminf(thr_own, tsh);
-                        ithr = int_floor(thr);
-                        continue;
-                    }
                     if (!(d < thr)) continue;  // the threshold moved within this chunk
                     if (count < p.cap) {
                         out_d[count] = d;
@@ -521,34 +442,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
             if (my_pub) __stcg(my_pub, thr);
-            if constexpr (SET) {
-                if (q_ok && thr_own < INFINITY) atomicMin(p.set_pub + q, fkey(thr_own));
-            }
         }
-        if constexpr (SET) {
-            if (q_ok) {  // the list sorted by (distance, slot): rank of each entry
-                const size_t lo = ((size_t)q * p.set_lists + 1 + split * 2 + half) * p.k;
-#pragma unroll
-                for (int m = 0; m < KT; ++m) {
-                    int rank = 0;
-#pragma unroll
-                    for (int x = 0; x < KT; ++x)
-                        rank += (x < p.k &&
-                                 (topi.v[x] < topi.v[m] ||
-                                  (topi.v[x] == topi.v[m] &&
-                                   (topi.id[x] < topi.id[m] || (topi.id[x] == topi.id[m] && x < m)))))
-                                    ? 1
-                                    : 0;
-                    if (m < p.k) {
-                        const bool real = topi.v[m] < INFINITY;
-                        p.cand_d[lo + rank] = real ? topi.v[m] : INFINITY;
-                        p.cand_i[lo + rank] = real ? topi.id[m] : -1;
-                    }
-                }
-            }
-        } else if (!DENSE && q_ok) {
-            p.cand_n[list] = count;
-        }
+        if (!DENSE && q_ok) p.cand_n[list] = count;
     }
     tc_fence_before();
     __syncthreads();
@@ -892,7 +787,7 @@ __global__ void __launch_bounds__(256)
                        const float* __restrict__ q_raw, const float* __restrict__ rerank,
                        const int32_t* __restrict__ slot_ext, int64_t n, int final_k, int k_out,
                        int32_t* __restrict__ out_ids, float* __restrict__ out_scores,
-                       int32_t* __restrict__ out_found, int* tie_flag) {
+                       int32_t* __restrict__ out_found) {
     __shared__ float sdist[KMAX];
     __shared__ int32_t sslot[KMAX];
     __shared__ float qs[DIM];
@@ -928,16 +823,6 @@ __global__ void __launch_bounds__(256)
         __syncthreads();
     }
     const int found = k < final_k ? k : final_k;
-    if (tie_flag) {
-        // entries in (distance, slot) order rather than the loop's: the order below is the
-        // same unless two ranked distances are equal (or NaN), which the caller redoes
-        for (int p = threadIdx.x; p < k; p += blockDim.x) {
-            const float d = sdist[p];
-            bool tie = d != d;
-            for (int j = 0; j < k; ++j) tie = tie || (j != p && sdist[j] == d);
-            if (tie) atomicOr(tie_flag, 1);
-        }
-    }
     for (int p = threadIdx.x; p < k; p += blockDim.x) {
         const float d = sdist[p];
         int rank = 0;
@@ -958,30 +843,6 @@ __global__ void __launch_bounds__(256)
     if (threadIdx.x == 0) out_found[q] = found;
 }
 
-// SET: the prefix loop's k entries, sorted by (distance, slot), as list 0 of each query.
-__global__ void __launch_bounds__(128)
-    slot_set_prefix_kernel(const float* __restrict__ st_d, const int32_t* __restrict__ st_i,
-                           int nq, int k, int set_lists, float* __restrict__ cand_d,
-                           int32_t* __restrict__ cand_i) {
-    const int q = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (q >= nq) return;
-    const float* d = st_d + (size_t)q * k;
-    const int32_t* id = st_i + (size_t)q * k;
-    for (int m = lane; m < k; m += 32) {
-        const float dm = d[m];
-        const int32_t im = id[m] < 0 ? INT_MAX : id[m];
-        int rank = 0;
-        for (int x = 0; x < k; ++x) {
-            const int32_t ix = id[x] < 0 ? INT_MAX : id[x];
-            rank += (d[x] < dm || (d[x] == dm && (ix < im || (ix == im && x < m)))) ? 1 : 0;
-        }
-        const size_t o = (size_t)q * set_lists * k + rank;
-        const bool real = dm < INFINITY && id[m] >= 0;
-        cand_d[o] = real ? dm : INFINITY;
-        cand_i[o] = real ? id[m] : -1;
-    }
-}
-
 }  // namespace slot
 
 int slot_tile_rows() { return slot::BN; }
@@ -1000,13 +861,12 @@ int launch_slot_prep(const int8_t* codes, const float* qnorm_in, int nq, int k, 
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
-template <int KCAP, bool DENSE, bool SET = false>
+template <int KCAP, bool DENSE>
 static int slot_tc_go(dim3 grid, const SlotTcLaunch& L, const slot::TcParams& p,
                       cudaStream_t st) {
-    if (set_smem_limit((const void*)slot::slot_tc_kernel<KCAP, DENSE, SET>,
-                       (int)slot::SMEM_BYTES) != 0)
+    if (set_smem_limit((const void*)slot::slot_tc_kernel<KCAP, DENSE>, (int)slot::SMEM_BYTES) != 0)
         return PION_B200_ECUDA;
-    slot::slot_tc_kernel<KCAP, DENSE, SET><<<grid, slot::THREADS, slot::SMEM_BYTES, st>>>(
+    slot::slot_tc_kernel<KCAP, DENSE><<<grid, slot::THREADS, slot::SMEM_BYTES, st>>>(
         *L.tmap_q, *L.tmap_rows, p);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
@@ -1034,8 +894,6 @@ int launch_slot_tc(const SlotTcLaunch& L, cudaStream_t st) {
     p.n_dense = L.n_dense;
     p.pub = L.pub;
     p.chunk_vmin = L.chunk_vmin;
-    p.set_pub = L.set_pub;
-    p.set_lists = L.set_lists;
     if (p.tile_end <= p.tile_begin || p.n_splits < 1 || p.n_splits > p.tile_end - p.tile_begin)
         return PION_B200_ESHAPE;
     if (p.k < 1 || p.k > slot::KMAX) return PION_B200_ESHAPE;
@@ -1046,24 +904,11 @@ int launch_slot_tc(const SlotTcLaunch& L, cudaStream_t st) {
             return PION_B200_ESHAPE;
         return slot_tc_go<0, true>(grid, L, p, st);
     }
-    if (L.set_pub) {  // SET: k <= 32, lists [nq][set_lists][k], no chain
-        if (p.k > 32 || p.pub || L.set_lists != 1 + 2 * p.n_splits) return PION_B200_ESHAPE;
-        if (p.k <= 16) return slot_tc_go<16, false, true>(grid, L, p, st);
-        return slot_tc_go<32, false, true>(grid, L, p, st);
-    }
     if (p.cap < slot::HALF) return PION_B200_ESHAPE;
     if (p.k <= 16) return slot_tc_go<16, false>(grid, L, p, st);
     if (p.k <= 32) return slot_tc_go<32, false>(grid, L, p, st);
     if (p.k <= 64) return slot_tc_go<64, false>(grid, L, p, st);
     return slot_tc_go<0, false>(grid, L, p, st);
-}
-
-int launch_slot_set_prefix(const float* st_d, const int32_t* st_i, int nq, int k, int set_lists,
-                           float* cand_d, int32_t* cand_i, cudaStream_t st) {
-    if (nq <= 0) return 0;
-    slot::slot_set_prefix_kernel<<<(nq + 3) / 4, 128, 0, st>>>(st_d, st_i, nq, k, set_lists,
-                                                               cand_d, cand_i);
-    return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
 int launch_slot_replay(const float* cand_d, const int32_t* cand_i, const int* cand_n, int n_lists,
@@ -1120,12 +965,11 @@ int launch_slot_emit(const float* st_d, const int32_t* st_i, int nq, int k, int 
 int launch_slot_finish(const float* st_d, const int32_t* st_i, int nq, int k, const float* q_raw,
                        const float* rerank, const int32_t* slot_ext, int64_t n, int final_k,
                        int k_out, int32_t* out_ids, float* out_scores, int32_t* out_found,
-                       cudaStream_t st, int* tie_flag) {
+                       cudaStream_t st) {
     if (nq <= 0) return 0;
     if (k < 1 || k > slot::KMAX) return PION_B200_ESHAPE;
     slot::slot_finish_kernel<<<nq, 256, 0, st>>>(st_d, st_i, k, q_raw, rerank, slot_ext, n,
-                                                  final_k, k_out, out_ids, out_scores, out_found,
-                                                  tie_flag);
+                                                  final_k, k_out, out_ids, out_scores, out_found);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 

@@ -181,39 +181,3 @@ def test_brute_force_recall(ctx, oracle, small):
     truth = np.argsort(-(qn @ rn.T), axis=1, kind="stable")[:, :10]
     recall = np.mean([len(set(ids[i]) & set(truth[i])) / 10 for i in range(len(qs))])
     assert recall >= 0.97
-
-
-@pytest.mark.parametrize("metric", ["cosine", "l2"])
-def test_brute_force_set_mode(ctx, oracle, large, metric, monkeypatch):
-    """With rerank rows the search needs only the loop's final set (the 2k smallest
-    (distance, slot) pairs) unless reranked distances tie: the set-mode scan (each list's
-    k best, one shared bound per query, a (distance, slot) merge) equals the replayed loop
-    (PION_B200_SLOT_SET=0) and the oracle; with rerank rows repeated across slots the
-    reranked distances tie and the call redoes the batch through the replayed loop."""
-    import pion_b200
-    g, A, ix0, rows, qs = large
-    if metric == "l2":
-        g, rows, qs = _graph(40000, 256, seed=43, metric="l2", nq=300)
-        A = g.arrays()
-        qs = qs * 2.5
-    ix = pion_b200.HNSWIndex(ctx, g)
-    rr = np.empty_like(rows)
-    rr[A["node_slot"]] = rows
-    ix.set_rerank_rows(rr)
-    for k in (1, 5, 10, 16):
-        got = ix.brute_force(qs, k)
-        monkeypatch.setenv("PION_B200_SLOT_SET", "0")
-        ref = ix.brute_force(qs, k)
-        monkeypatch.delenv("PION_B200_SLOT_SET")
-        for a, b in zip(got, ref):
-            assert np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
-        wi, ws, wf = oracle.hnsw_brute_force(A, qs[:60], k, rr)
-        assert np.array_equal(got[0][:60], wi) and np.array_equal(got[2][:60], wf)
-        assert np.array_equal(got[1][:60].view(np.uint32), ws.view(np.uint32))
-    tied = rr[np.arange(rr.shape[0]) % 97]  # every reranked distance repeats
-    ix.set_rerank_rows(tied)
-    ids, sc, found = ix.brute_force(qs[:40], 10)
-    wi, ws, wf = oracle.hnsw_brute_force(A, qs[:40], 10, tied)
-    assert np.array_equal(ids, wi) and np.array_equal(found, wf)
-    assert np.array_equal(sc.view(np.uint32), ws.view(np.uint32))
-    ix.free()
