@@ -670,8 +670,8 @@ __global__ void __launch_bounds__(B1_THREADS)
 // (cp.async.bulk, completing on the stage's mbarrier) and B1S_STAGES stages in flight, so
 // the bytes in flight do not depend on registers; 4 lanes per row then popcount from
 // shared memory.  Same outputs as bq_scan1_hist_kernel.
-constexpr int B1S_ROWS = 64;    // 12 KB stages at 1536 dims: four CTAs per SM (measured:
-constexpr int B1S_STAGES = 4;   // 128-row stages at two per SM and one-CTA rings were slower)
+constexpr int B1S_ROWS = 64;    // 12 KB stages at 1536 dims, two per CTA: seven CTAs per SM
+constexpr int B1S_STAGES = 2;   // (measured: deeper rings at fewer CTAs per SM were slower)
 constexpr int B1S_MAX_ROW_BYTES = 384;  // dim <= 3072
 
 __global__ void __launch_bounds__(B1_THREADS)
@@ -1060,7 +1060,7 @@ bool bq_scan1_supported(int words, int S) {
 
 // One full wave of the first pass: as many CTAs as fit on the SMs at once (the register
 // pass's 84 registers a thread allow 2 CTAs of 256 threads per SM; the staged pass's
-// ~55 KB of shared memory 4).
+// ~31 KB of shared memory 7).
 int bq_scan1_ctas(int64_t n_rows, int words, int num_sms, int stream_path) {
     int per_sm = 0;
     cudaError_t e;

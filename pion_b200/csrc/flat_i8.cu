@@ -994,8 +994,10 @@ int launch_flat_i8_tc(const Fi8TcLaunch& L, cudaStream_t st) {
 int fi8_query_tile() { return fi8::BM; }
 int fi8_k_block() { return fi8::BK; }
 
+// One wave at k <= 32: two 256-thread CTAs per SM (two waves measured 278 us per search at
+// 1M rows against 261 us for one).
 int fi8_scan1_ctas(int64_t n_rows, int num_sms) {
-    int64_t ctas = (int64_t)num_sms * 4;
+    int64_t ctas = (int64_t)num_sms * 2;
     const int64_t min_rows = 256;
     if (ctas * min_rows > n_rows) ctas = (n_rows + min_rows - 1) / min_rows;
     return (int)(ctas < 1 ? 1 : ctas);
