@@ -340,9 +340,19 @@ __global__ void query_normalize_kernel(const float* __restrict__ q, int nq, int 
     const int q0 = blockIdx.x * rows;
     const int nr = min(rows, nq - q0);
     const int pitch = normalize_pitch(dim);
-    for (int r = 0; r < nr; ++r)
-        for (int d = threadIdx.x; d < dim; d += blockDim.x)
-            qsm[r * pitch + d] = q[(size_t)(q0 + r) * dim + d];
+    if ((dim & 3) == 0) {  // 128-bit loads, all of a thread's in flight together
+        const int d4 = dim >> 2;
+#pragma unroll 4
+        for (int i = threadIdx.x; i < nr * d4; i += blockDim.x) {
+            const int r = i / d4, c = i - r * d4;
+            reinterpret_cast<float4*>(qsm + r * pitch)[c] =
+                reinterpret_cast<const float4*>(q + (size_t)(q0 + r) * dim)[c];
+        }
+    } else {
+        for (int r = 0; r < nr; ++r)
+            for (int d = threadIdx.x; d < dim; d += blockDim.x)
+                qsm[r * pitch + d] = q[(size_t)(q0 + r) * dim + d];
+    }
     __syncthreads();
     if (threadIdx.x < nr) {
         const float* x = qsm + threadIdx.x * pitch;
@@ -467,21 +477,23 @@ __global__ void max_reduce_kernel(const float* __restrict__ x, int64_t n, float*
     if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(out), __float_as_int(m));
 }
 
-// One warp per query: exact distances of the kc candidates (two per warp step, one
-// per half-warp), the k best by (distance, id), and the certificate.
-// One CTA per query: its 16 half-warps take the candidates 16 at a time (exact 4-chain
-// dots, candidate rows prefetched into L2 first), then warp 0 selects and certifies.
+// One CTA per query: exact 4-chain dots of the kc candidates (rows prefetched into L2
+// first), then warp 0 selects the k best by (distance, id) and certifies.  dim % 16 == 0:
+// 128 threads, four lanes per candidate (dot4chain_quad: 128-bit loads, twelve in
+// flight, the query in shared memory); otherwise 256 threads, a half-warp per candidate
+// (dot4chain_half).
 __global__ void __launch_bounds__(256) rescore_certify_kernel(
     const float* __restrict__ rows, int dim, const float* __restrict__ qn,
     const float* __restrict__ qnorm, float row_norm_max, const float* __restrict__ cand_v,
     const int32_t* __restrict__ cand_i, int nq, int kc, int k, int64_t id_base,
     float* __restrict__ out_d, int32_t* __restrict__ out_i, int* __restrict__ flagged,
     int* __restrict__ n_flagged, int force_exact) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     const int q = blockIdx.x;
     if (q >= nq) return;
     const int lane = threadIdx.x & 31;
-    float* dist = sm;
+    const bool quad = (dim & 15) == 0;
+    float* dist = quad ? sm + dim : sm;
     int32_t* ids = reinterpret_cast<int32_t*>(dist + kc);
     const float* qv = qn + (size_t)q * dim;
     const int hw = threadIdx.x >> 4;  // half-warp of the CTA
@@ -492,18 +504,36 @@ __global__ void __launch_bounds__(256) rescore_certify_kernel(
             const int32_t id = cand_i[(size_t)q * kc + j];
             if (id >= 0) prefetch_row_f32_l2(rows + (size_t)id * dim, dim);
         }
-    const int halves = blockDim.x >> 4;
-    for (int j0 = 0; j0 < kc; j0 += halves) {
-        const int j = j0 + hw;
-        const int32_t id = j < kc ? cand_i[(size_t)q * kc + j] : -1;
-        float d = INFINITY;
-        if (id >= 0) {
-            const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
-            d = __fsub_rn(1.0f, s);
+    if (quad) {
+        float4* qs4 = reinterpret_cast<float4*>(sm);
+        for (int c = threadIdx.x; c < (dim >> 2); c += blockDim.x)
+            qs4[c] = reinterpret_cast<const float4*>(qv)[c];
+        __syncthreads();
+        const int quads = blockDim.x >> 2;
+        for (int j0 = 0; j0 < kc; j0 += quads) {  // every lane of the warp takes part
+            const int j = j0 + (threadIdx.x >> 2);
+            const int32_t id = j < kc ? cand_i[(size_t)q * kc + j] : -1;
+            const float s = dot4chain_quad<12>(qs4, id >= 0 ? rows + (size_t)id * dim : nullptr,
+                                               dim);
+            if ((threadIdx.x & 3) == 0 && j < kc) {
+                dist[j] = id >= 0 ? __fsub_rn(1.0f, s) : INFINITY;
+                ids[j] = id;
+            }
         }
-        if (hl == 0 && j < kc) {
-            dist[j] = d;
-            ids[j] = id;
+    } else {
+        const int halves = blockDim.x >> 4;
+        for (int j0 = 0; j0 < kc; j0 += halves) {
+            const int j = j0 + hw;
+            const int32_t id = j < kc ? cand_i[(size_t)q * kc + j] : -1;
+            float d = INFINITY;
+            if (id >= 0) {
+                const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
+                d = __fsub_rn(1.0f, s);
+            }
+            if (hl == 0 && j < kc) {
+                dist[j] = d;
+                ids[j] = id;
+            }
         }
     }
     __syncthreads();
@@ -931,8 +961,12 @@ int launch_rescore_certify(const float* rows, int dim, const float* qn, const fl
                            int kc, int k, int64_t id_base, float* out_d, int32_t* out_i,
                            int* flagged, int* n_flagged, int force_exact, cudaStream_t st) {
     if (nq <= 0) return 0;
-    const size_t smem = (size_t)kc * 8;
-    ff32::rescore_certify_kernel<<<nq, 256, smem, st>>>(rows, dim, qn, qnorm, row_norm_max,
+    const bool quad = dim % 16 == 0;
+    const size_t smem = (size_t)kc * 8 + (quad ? (size_t)dim * 4 : 0);
+    if (smem > 48 * 1024 &&
+        set_smem_limit((const void*)ff32::rescore_certify_kernel, (int)smem) != 0)
+        return PION_B200_ECUDA;
+    ff32::rescore_certify_kernel<<<nq, quad ? 128 : 256, smem, st>>>(rows, dim, qn, qnorm, row_norm_max,
                                                         cand_v, cand_i, nq, kc, k, id_base, out_d,
                                                         out_i, flagged, n_flagged, force_exact);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
