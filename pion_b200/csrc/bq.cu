@@ -481,25 +481,40 @@ __global__ void __launch_bounds__(256) bq_rerank_kernel(
     const float* __restrict__ rows, int dim, const float* __restrict__ qn,
     const int32_t* __restrict__ sl_id, const int* __restrict__ sl_n, int S, int nq, int k,
     int64_t id_base, float* __restrict__ out_d, int32_t* __restrict__ out_i) {
-    extern __shared__ float rr[];
+    extern __shared__ __align__(16) float rr[];
     const int q = blockIdx.x;
     if (q >= nq) return;
     const int lane = threadIdx.x & 31;
-    float* dist = rr;
+    const bool quad = (dim & 15) == 0;  // four lanes per row, the query in shared memory
+    float* dist = quad ? rr + dim : rr;
     const float* qv = qn + (size_t)q * dim;
     const int n = sl_n[q];
     for (int j = threadIdx.x; j < n; j += blockDim.x)
         prefetch_row_f32_l2(rows + (size_t)sl_id[(size_t)q * S + j] * dim, dim);
-    const int hw = threadIdx.x >> 4;  // 16 half-warps, one shortlisted row each
-    const int hl = lane & 15;
-    const unsigned hmask = (lane >> 4) ? 0xffff0000u : 0x0000ffffu;
-    const int halves = blockDim.x >> 4;
-    for (int j0 = 0; j0 < n; j0 += halves) {
-        const int j = j0 + hw;
-        if (j < n) {
-            const int32_t id = sl_id[(size_t)q * S + j];
-            const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
-            if (hl == 0) dist[j] = __fsub_rn(1.0f, s);
+    if (quad) {
+        float4* qs4 = reinterpret_cast<float4*>(rr);
+        for (int c = threadIdx.x; c < (dim >> 2); c += blockDim.x)
+            qs4[c] = reinterpret_cast<const float4*>(qv)[c];
+        __syncthreads();
+        const int quads = blockDim.x >> 2;
+        for (int j0 = 0; j0 < n; j0 += quads) {  // every lane of the warp takes part
+            const int j = j0 + (threadIdx.x >> 2);
+            const float* row = j < n ? rows + (size_t)sl_id[(size_t)q * S + j] * dim : nullptr;
+            const float s = dot4chain_quad<12>(qs4, row, dim);
+            if ((threadIdx.x & 3) == 0 && j < n) dist[j] = __fsub_rn(1.0f, s);
+        }
+    } else {
+        const int hw = threadIdx.x >> 4;  // 16 half-warps, one shortlisted row each
+        const int hl = lane & 15;
+        const unsigned hmask = (lane >> 4) ? 0xffff0000u : 0x0000ffffu;
+        const int halves = blockDim.x >> 4;
+        for (int j0 = 0; j0 < n; j0 += halves) {
+            const int j = j0 + hw;
+            if (j < n) {
+                const int32_t id = sl_id[(size_t)q * S + j];
+                const float s = dot4chain_half(qv, rows + (size_t)id * dim, dim, hl, hmask);
+                if (hl == 0) dist[j] = __fsub_rn(1.0f, s);
+            }
         }
     }
     __syncthreads();
@@ -1228,8 +1243,11 @@ int launch_bq_rerank(const float* rows, int dim, const float* qn, const int32_t*
                      const int* sl_n, int S, int nq, int k, int64_t id_base, float* out_d,
                      int32_t* out_i, cudaStream_t st) {
     if (nq <= 0) return 0;
-    bq::bq_rerank_kernel<<<nq, 256, (size_t)S * 4, st>>>(rows, dim, qn, sl_id, sl_n, S, nq, k,
-                                                         id_base, out_d, out_i);
+    const size_t smem = (size_t)S * 4 + (dim % 16 == 0 ? (size_t)dim * 4 : 0);
+    if (smem > 48 * 1024 && set_smem_limit((const void*)bq::bq_rerank_kernel, (int)smem) != 0)
+        return PION_B200_ECUDA;
+    bq::bq_rerank_kernel<<<nq, 256, smem, st>>>(rows, dim, qn, sl_id, sl_n, S, nq, k, id_base,
+                                                out_d, out_i);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
 }
 
