@@ -80,11 +80,34 @@ struct TcParams {
     float* pub;
 };
 
+// Max of bv[0, N) into bv[0] / bp[0] by halving (any N): entry i meets entry i + ceil(N/2),
+// the later one winning only when strictly larger.  Unrolled at compile time, so the
+// arrays stay in registers.
+template <int N>
+struct MaxTree {
+    __device__ __forceinline__ static void run(float* bv, int* bp) {
+        constexpr int H = (N + 1) / 2;
+#pragma unroll
+        for (int i = 0; i < N - H; ++i) {
+            const bool up = bv[i + H] > bv[i];
+            bv[i] = up ? bv[i + H] : bv[i];
+            bp[i] = up ? bp[i + H] : bp[i];
+        }
+        MaxTree<H>::run(bv, bp);
+    }
+};
+template <>
+struct MaxTree<1> {
+    __device__ __forceinline__ static void run(float*, int*) {}
+};
+
 // The k smallest candidates of a list so far, unsorted in registers (entries past k hold
 // -inf and never count), and where the largest sits.  insert() overwrites the largest
 // with d and returns the new largest, i.e. the k-th smallest candidate: independent
-// selects and a depth-log2(KCAP) max tree.  selp keeps the runtime position from being
-// folded back into an indexed access (which would move the array to local memory).
+// selects and a depth-ceil(log2 KCAP) max tree (KCAP need not be a power of two: the
+// 20-entry lists of the brute-force search's top-20 cost 19 comparisons, not 31).  selp
+// keeps the runtime position from being folded back into an indexed access (which would
+// move the array to local memory).
 template <int KCAP>
 struct LocalTopK {
     float v[KCAP];
@@ -105,14 +128,7 @@ struct LocalTopK {
             bv[m] = v[m];
             bp[m] = m;
         }
-#pragma unroll
-        for (int w = KCAP / 2; w >= 1; w /= 2)
-#pragma unroll
-            for (int i = 0; i < w; ++i) {
-                const bool up = bv[i + w] > bv[i];
-                bv[i] = up ? bv[i + w] : bv[i];
-                bp[i] = up ? bp[i + w] : bp[i];
-            }
+        MaxTree<KCAP>::run(bv, bp);
         mpos = bp[0];
         return bv[0];
     }
@@ -906,6 +922,7 @@ int launch_slot_tc(const SlotTcLaunch& L, cudaStream_t st) {
     }
     if (p.cap < slot::HALF) return PION_B200_ESHAPE;
     if (p.k <= 16) return slot_tc_go<16, false>(grid, L, p, st);
+    if (p.k <= 20) return slot_tc_go<20, false>(grid, L, p, st);
     if (p.k <= 32) return slot_tc_go<32, false>(grid, L, p, st);
     if (p.k <= 64) return slot_tc_go<64, false>(grid, L, p, st);
     return slot_tc_go<0, false>(grid, L, p, st);
