@@ -297,58 +297,85 @@ __global__ void __launch_bounds__(SEL_THREADS)
                      int* __restrict__ out_n, int out_qstride, int n_qstride,
                      int* __restrict__ next_dot_min, int* __restrict__ flagged,
                      int* __restrict__ n_flagged, int force_flag) {
-    extern __shared__ int sm_hist[];  // dim + 1 bins
+    extern __shared__ int sm_hist[];  // dim + 1 bins, then the lists' counts
+    int* scnt = sm_hist + ((dim + 1 + 3) & ~3);
     __shared__ uint64_t keys[512];
     __shared__ int32_t ties[SEL_TIES];
+    __shared__ int warp_tot[SEL_THREADS / 32];
     __shared__ int n_keys, n_ties, overflow, dstar, below, total_s;
     const int q = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     for (int i = threadIdx.x; i <= dim; i += SEL_THREADS) sm_hist[i] = 0;
     if (threadIdx.x == 0) {
         n_keys = n_ties = overflow = 0;
         total_s = 0;
     }
     __syncthreads();
+    // the lists' counts in one pass (every load in flight at once), then the candidates
+    // of all lists as one flat range: a query's lists are contiguous, [n_lists][CAP]
     const size_t qbase = (size_t)q * n_lists;
-    for (int l = 0; l < n_lists; ++l) {
+    int my_total = 0;
+    for (int l = threadIdx.x; l < n_lists; l += SEL_THREADS) {
         const int c = cn[qbase + l];
-        if (c > CAP && threadIdx.x == 0) overflow = 1;
+        if (c > CAP) overflow = 1;
         const int m = c < CAP ? c : CAP;
-        for (int j = threadIdx.x; j < m; j += SEL_THREADS)
-            atomicAdd(&sm_hist[ch[(qbase + l) * CAP + j]], 1);
-        if (threadIdx.x == 0) total_s += m;
+        scnt[l] = m;
+        my_total += m;
     }
+    if (my_total) atomicAdd(&total_s, my_total);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        // smallest d with count(h <= d) >= S (all candidates when fewer than S)
-        int acc = 0, d = 0;
-        const int want = total_s < S ? total_s : S;
-        if (want == 0) {
+    const int flat = n_lists * CAP;
+    const uint16_t* chq = ch + qbase * CAP;
+    const int32_t* cidq = cid + qbase * CAP;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < flat; e += SEL_THREADS)
+        if ((e % CAP) < scnt[e / CAP]) atomicAdd(&sm_hist[chq[e]], 1);
+    __syncthreads();
+    // smallest d with count(h <= d) >= want (all candidates when fewer than S): per-thread
+    // runs of bins, a block scan of their sums, the run that crosses scanned by its thread
+    const int want = total_s < S ? total_s : S;
+    {
+        const int per = (dim + 1 + SEL_THREADS - 1) / SEL_THREADS;
+        const int lo = threadIdx.x * per;
+        int sum = 0;
+        for (int i = lo; i < lo + per && i <= dim; ++i) sum += sm_hist[i];
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) warp_tot[w] = incl;
+        if (threadIdx.x == 0) {
             dstar = -1;
             below = 0;
-        } else {
-            for (d = 0; d <= dim; ++d) {
+        }
+        __syncthreads();
+        for (int v = 0; v < w; ++v) incl += warp_tot[v];
+        const int excl = incl - sum;
+        if (want > 0 && excl < want && incl >= want) {
+            int acc = excl, d = lo;
+            for (; d < lo + per && d <= dim; ++d) {
                 if (acc + sm_hist[d] >= want) break;
                 acc += sm_hist[d];
             }
             dstar = d;
             below = acc;
         }
+        __syncthreads();
     }
-    __syncthreads();
     const int D = dstar;
-    const int want = total_s < S ? total_s : S;
-    for (int l = 0; l < n_lists && D >= 0; ++l) {
-        const int c = cn[qbase + l];
-        const int m = c < CAP ? c : CAP;
-        for (int j = threadIdx.x; j < m; j += SEL_THREADS) {
-            const int h = ch[(qbase + l) * CAP + j];
-            const int32_t id = cid[(qbase + l) * CAP + j];
+    if (D >= 0) {
+#pragma unroll 4
+        for (int e = threadIdx.x; e < flat; e += SEL_THREADS) {
+            if ((e % CAP) >= scnt[e / CAP]) continue;
+            const int h = chq[e];
             if (h < D) {
                 const int pos = atomicAdd(&n_keys, 1);
-                if (pos < 512) keys[pos] = ((uint64_t)h << 32) | (uint32_t)id;
+                if (pos < 512) keys[pos] = ((uint64_t)h << 32) | (uint32_t)cidq[e];
             } else if (h == D) {
                 const int pos = atomicAdd(&n_ties, 1);
-                if (pos < SEL_TIES) ties[pos] = id;
+                if (pos < SEL_TIES) ties[pos] = cidq[e];
             }
         }
     }
@@ -1195,7 +1222,10 @@ int launch_bq_select(const int32_t* cid, const uint16_t* ch, const int* cn, int 
                      int* n_flagged, int force_flag, cudaStream_t st) {
     if (nq <= 0) return 0;
     if (S > 256) return PION_B200_ESHAPE;
-    bq::bq_select_kernel<<<nq, bq::SEL_THREADS, (size_t)(dim + 1) * 4, st>>>(
+    const size_t smem = (size_t)((dim + 1 + 3) & ~3) * 4 + (size_t)n_lists * 4;
+    if (smem > 48 * 1024 && set_smem_limit((const void*)bq::bq_select_kernel, (int)smem) != 0)
+        return PION_B200_ECUDA;
+    bq::bq_select_kernel<<<nq, bq::SEL_THREADS, smem, st>>>(
         cid, ch, cn, n_lists, dim, S, out_id, out_h, out_n, out_qstride, n_qstride, next_dot_min,
         flagged, n_flagged, force_flag);
     return cudaGetLastError() == cudaSuccess ? 0 : PION_B200_ECUDA;
