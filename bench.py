@@ -156,7 +156,7 @@ class ClockMonitor:
     REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
                ("hw_thermal_slowdown", 0x40), ("sw_power_cap", 0x4))
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.dev = device_index
         self.period = period_s
         self.samples = []
