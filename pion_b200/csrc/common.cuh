@@ -311,8 +311,10 @@ struct TopKDesc {
         }
     }
     // The k-th best score (1 <= k <= KCAP) by a log-depth select tree over the bits
-    // of k - 1.
+    // of k - 1.  A capacity that is not a power of two is only used with k == KCAP: the
+    // last entry.
     __device__ __forceinline__ float kth(int k) const {
+        if constexpr ((KCAP & (KCAP - 1)) != 0) return v[KCAP - 1];
         uint32_t t[KCAP];
 #pragma unroll
         for (int j = 0; j < KCAP; ++j) t[j] = __float_as_uint(v[j]);

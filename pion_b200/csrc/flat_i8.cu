@@ -18,6 +18,7 @@
 //   quantize_rows_i8_kernel, tile_max_kernel  index preparation.
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -982,6 +983,10 @@ int launch_flat_i8_tc(const Fi8TcLaunch& L, cudaStream_t st) {
     if (p.list_base + p.n_splits * fi8_lists_per_split(p.k) > p.n_lists) return PION_B200_ESHAPE;
     const int n_qt = (L.nq + fi8::BM - 1) / fi8::BM;
     const int ew = fi8_epi_warps(L.k);
+    // k = 10 (the FT.SEARCH default): a list of exactly ten entries, whose k-th is its last
+    // one, instead of 16 with a select tree (PION_B200_I8_KCAP16=1 keeps 16, for tests)
+    if (L.k == 10 && !getenv("PION_B200_I8_KCAP16"))
+        return launch_tc_k<10, 8>(*L.tmap_q, *L.tmap_rows, p, n_qt, st);
     switch (fi8_kcap(L.k)) {
         case 16: return ew == 8 ? launch_tc_k<16, 8>(*L.tmap_q, *L.tmap_rows, p, n_qt, st)
                                 : PION_B200_ESHAPE;

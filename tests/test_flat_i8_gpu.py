@@ -411,3 +411,29 @@ def test_search_pairs_equals_search(ctx, oracle):
     assert (pairs[..., 1] == -1).all()
     assert torch.isneginf(pairs[..., 0].contiguous().view(torch.float32)).all()
     empty.free()
+
+
+def test_ten_entry_lists_equal_sixteen_entry_lists(ctx, oracle, monkeypatch):
+    """k = 10 runs the tensor-core kernel with ten-entry register lists (the k-th is the
+    last entry); the sixteen-entry kernel (PION_B200_I8_KCAP16=1) gives the same scores
+    and ids, and both equal the oracle -- with planted duplicate rows so that scores tie
+    at the tenth place."""
+    import pion_b200
+    rows, qf = mixture_np(70000, 1536, 64, seed=14, n_queries=300)
+    rows[1000:1040] = rows[5]          # forty copies of one row: ties at every rank
+    keys, ks = oracle.pkm_quantize_rows_i8(rows)
+    q, qs = oracle.pkm_quantize_rows_i8(qf)
+    q[:3] = keys[5]
+    qs[:3] = ks[5]
+    ix = pion_b200.FlatI8Index(ctx, keys, ks)
+    a = ix.search(q, qs, 10)
+    monkeypatch.setenv("PION_B200_I8_KCAP16", "1")
+    b = ix.search(q, qs, 10)
+    monkeypatch.delenv("PION_B200_I8_KCAP16")
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+    oi, ov = oracle.flat_i8_knn(keys, ks, q, qs, 10)
+    for t in range(q.shape[0]):
+        o = np.lexsort((oi[t], -ov[t]))
+        assert a[0][t].tolist() == oi[t][o].tolist(), t
+        assert np.array_equal(a[1][t].view(np.uint32), ov[t][o].view(np.uint32)), t
+    ix.free()
